@@ -1,0 +1,241 @@
+/* fusion_b200.h -- C ABI of the B200 (sm_100a) compute backend for Fusion.
+ *
+ * Every entry point is `extern "C"`, takes plain pointers, sizes and POD plans,
+ * and returns an int status (FZ_OK == 0). On failure the thread-local message
+ * from fz_last_error() says what went wrong. No torch or C++ types cross this
+ * boundary. Device pointers are CUDA device addresses; streams are cudaStream_t
+ * passed as void*. NULL stream means the calling thread's library stream on the
+ * current device (fz_default_stream()).
+ *
+ * Each function names the reference interface it replaces (paths relative to the
+ * pytergeist/Nova repository). In the reference those interfaces are C++ templates
+ * inside fusion/src/Fusion; the C++ host layer of this project (nova_b200/host)
+ * keeps their callers and routes them here.
+ */
+#ifndef FUSION_B200_H
+#define FUSION_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FZ_MAX_DIMS 8     /* loop dims of an elementwise plan (after collapsing) */
+#define FZ_MAX_LEAVES 12  /* input tensors of one fused elementwise program */
+#define FZ_MAX_NODES 48   /* ops of one fused elementwise program */
+#define FZ_MAX_OUTPUTS 4  /* outputs of one fused elementwise program */
+
+enum fz_status {
+  FZ_OK = 0,
+  FZ_ERR_INVALID = 1,     /* bad argument: shape, pointer, op code, size */
+  FZ_ERR_CUDA = 2,        /* a CUDA runtime/driver call failed */
+  FZ_ERR_OOM = 3,         /* device allocation failed */
+  FZ_ERR_NCCL = 4,        /* an NCCL call failed */
+  FZ_ERR_UNSUPPORTED = 5, /* no sm_100 device, or a feature this build lacks */
+  FZ_ERR_TIMEOUT = 6,     /* a bounded wait ran out (collective watchdog) */
+  FZ_ERR_JIT = 7          /* runtime compilation of a fused program failed */
+};
+
+/* Binary ops: the tags of fusion/src/Fusion/cpu/simd/SimdTags.hpp:7-53. */
+enum fz_binop {
+  FZ_ADD = 0, FZ_SUB = 1, FZ_MUL = 2, FZ_DIV = 3, FZ_POW = 4,
+  FZ_MAXIMUM = 5, /* a > b ? a : b (MaximumSIMD) */
+  FZ_GT = 6,      /* (a > b) as 1.0f/0.0f (GreaterThanSIMD) */
+  FZ_GE = 7       /* (a >= b) as 1.0f/0.0f (GreaterThanEqualSIMD) */
+};
+
+/* Unary ops: SimdTags.hpp:55-71 (exp/log/sqrt) plus identity (copy). */
+enum fz_unop { FZ_EXP = 0, FZ_LOG = 1, FZ_SQRT = 2, FZ_COPY = 3 };
+
+/* Reductions: SumSIMD via reduction_tag (fusion/src/Fusion/core/TensorIter.hpp:251-297);
+ * mean = sum / (float)len (fusion/src/Fusion/ops/Reduce.hpp:27-36); max has no
+ * reference counterpart (NaN-propagating, +0 ranks above -0). */
+enum fz_redop { FZ_RSUM = 0, FZ_RMEAN = 1, FZ_RMAX = 2 };
+
+/* ---- runtime ------------------------------------------------------------ */
+
+/* Thread-local text of the last failure on this thread ("" if none). */
+const char *fz_last_error(void);
+int fz_version(void);
+
+/* Number of visible CUDA devices of compute capability 10.x. */
+int fz_device_count(int *count);
+/* Make `device` current for this thread and set up its stream and memory pool.
+ * Replaces Device::validate_device (fusion/src/Fusion/device/Device.h:31-33),
+ * which only admitted CPU index <= 0. */
+int fz_set_device(int device);
+int fz_get_device(int *device);
+/* The calling thread's stream on the current device (created on first use). */
+void *fz_default_stream(void);
+int fz_stream_sync(void *stream);
+int fz_device_sync(void);
+
+/* Stream-ordered device memory from the device's pool (cudaMallocAsync with the
+ * release threshold raised so freed blocks are reused, not returned).
+ * Replaces PoolAllocator::allocate/deallocate
+ * (fusion/src/Fusion/alloc/BFCPoolAllocator.cpp:59-111) for tensor storage. */
+int fz_malloc(void **ptr, size_t bytes, void *stream);
+int fz_free(void *ptr, void *stream);
+/* Bytes currently held by this device's pool (used and cached). */
+int fz_pool_stats(size_t *reserved, size_t *used);
+
+/* Copies. d2h waits for the stream so the host buffer is valid on return.
+ * Replaces the host std::copy of tensor_to_numpy / set_values
+ * (fusion/src/Fusion/python/tensor/Helpers.hpp:14-44, BindTensor.hpp:58-70). */
+int fz_memcpy_h2d(void *dst, const void *src, size_t bytes, void *stream);
+int fz_memcpy_d2h(void *dst, const void *src, size_t bytes, void *stream);
+int fz_memcpy_d2d(void *dst, const void *src, size_t bytes, void *stream);
+/* dst[i] = value for i < n. Replaces fill/zeros/ones
+ * (fusion/src/Fusion/TensorFactory.hpp:12-36) and RawTensor::clear
+ * (fusion/src/Fusion/core/RawTensor.hpp:140-149). */
+int fz_fill_f32(float *dst, float value, int64_t n, void *stream);
+/* Pinned host memory for staging (H2D/D2H at full PCIe/C2C rate). */
+int fz_host_alloc(void **ptr, size_t bytes);
+int fz_host_free(void *ptr);
+
+/* Device-side timing of work on a stream: record a start/stop pair around
+ * launches and read milliseconds (waits for the stop event). */
+int fz_timer_create(void **timer);
+int fz_timer_start(void *timer, void *stream);
+int fz_timer_stop(void *timer, void *stream);
+int fz_timer_elapsed_ms(void *timer, float *ms);
+int fz_timer_destroy(void *timer);
+/* Number of kernels this library has launched in this process. */
+int64_t fz_launch_count(void);
+/* Synchronise the current device and report whether any kernel with bounded
+ * waits (the GEMM's mbarrier pipeline) gave up since the last call: FZ_OK, or
+ * FZ_ERR_TIMEOUT with the kernel's code in fz_last_error(). Clears the record. */
+int fz_kernel_status(void);
+
+/* ---- elementwise --------------------------------------------------------- */
+
+/* Loop plan of one elementwise launch: the output index space (outermost dim
+ * first) and, per operand, the BYTE stride of each loop dim (0 = broadcast).
+ * Operand 0 is the output. Same meaning as LoopDim::size / LoopDim::stride_bytes
+ * of BroadcastPlan (fusion/src/Fusion/core/TensorPlan.h:42-68), with the dims
+ * stored column-wise. ndim may be 0 (one element). */
+typedef struct fz_ewise_plan {
+  int32_t ndim;
+  int32_t num_operands;
+  int64_t size[FZ_MAX_DIMS];
+  int64_t stride_bytes[FZ_MAX_LEAVES + FZ_MAX_OUTPUTS][FZ_MAX_DIMS];
+} fz_ewise_plan;
+
+/* out = op(a, b) over `plan` (operands: 0 = out, 1 = a, 2 = b), fp32 IEEE,
+ * round-to-nearest, no contraction. Operand order is taken as given: the
+ * exchange that the reference's scalar-LHS path performs
+ * (fusion/src/Fusion/cpu/simd/SimdTraits.hpp:44-47) is decided by the caller.
+ * Replaces binary_ewise_tag (fusion/src/Fusion/core/TensorIter.hpp:96-178) and
+ * simd_traits<Tag,float>::execute_contiguous (SimdTraits.hpp:26-148). */
+int fz_ewise_binary(int op, const fz_ewise_plan *plan, float *out, const float *a,
+                    const float *b, void *stream);
+
+/* Contiguous fast path of the above: out[i] = op(a[i], b[i]) for i < n
+ * (PlanMeta.hpp:103-107 fastpath; VecFallback.hpp:76-102). */
+int fz_ewise_binary_contig(int op, int64_t n, float *out, const float *a,
+                           const float *b, void *stream);
+
+/* out = op(a) over `plan` (operands: 0 = out, 1 = a). Replaces unary_ewise_tag
+ * (fusion/src/Fusion/core/TensorIter.hpp:180-249) and simd::{exp,log,sqrt}_contiguous
+ * (fusion/src/Fusion/cpu/simd/VecFallback.hpp:41-60). exp/log call CUDA's expf/logf,
+ * sqrt is the IEEE square root. */
+int fz_ewise_unary(int op, const fz_ewise_plan *plan, float *out, const float *a,
+                   void *stream);
+
+/* x[i] -= y[i] for i < n, in place: fusion::math::sub_inplace
+ * (fusion/src/Fusion/ops/Ewise.hpp:69-83), which forces the contiguous path over
+ * x's element count whatever y's shape. */
+int fz_sub_inplace(float *x, const float *y, int64_t n, void *stream);
+
+/* ---- fused elementwise programs (fusion IR) ------------------------------ */
+
+/* One node of a fused program. Operand references: values >= 0 name an earlier
+ * node; -1-k names leaf k (an input tensor). FZ_NODE_CONST nodes carry their
+ * value in `imm`. Binary nodes compute op(src0, src1) with the operand order
+ * given (any reference operand exchange is already applied by the caller). */
+enum fz_node_kind { FZ_NODE_BINARY = 0, FZ_NODE_UNARY = 1, FZ_NODE_CONST = 2 };
+typedef struct fz_node {
+  int32_t kind;
+  int32_t op;
+  int32_t src0, src1;
+  float imm;
+} fz_node;
+
+/* A fused elementwise program: nodes in topological order, leaves bound to the
+ * plan's operands num_outputs..num_outputs+num_leaves-1 and outputs bound to plan
+ * operands 0..num_outputs-1 (output k stores node out_node[k]). The program is
+ * lowered to CUDA C, compiled for sm_100a by NVRTC once per distinct structure,
+ * cached, and launched as a single pass over the plan's index space. There is no
+ * reference counterpart: the reference runs each op as its own pass
+ * (fusion/src/Fusion/core/TensorIter.hpp:96-249). */
+typedef struct fz_program {
+  int32_t num_nodes;
+  int32_t num_leaves;
+  int32_t num_outputs;
+  int32_t out_node[FZ_MAX_OUTPUTS];
+  fz_node nodes[FZ_MAX_NODES];
+} fz_program;
+
+int fz_fused_launch(const fz_program *prog, const fz_ewise_plan *plan,
+                    float *const *outputs, const float *const *leaves, void *stream);
+/* Number of distinct fused kernels compiled so far in this process. */
+int fz_fused_cache_size(void);
+
+/* ---- reductions ---------------------------------------------------------- */
+
+/* Reduce the middle dim of a contiguous [outer, len, inner] view:
+ * out[o, i] = red_{r < len} in[o, r, i]. Replaces reduction_tag
+ * (fusion/src/Fusion/core/TensorIter.hpp:251-297) driven by make_reduction_meta
+ * (fusion/src/Fusion/core/PlanMeta.hpp:148-182); the global reduction is
+ * outer = inner = 1. Long reductions are split over CTAs; the partials live in
+ * stream-ordered scratch taken from the device pool and released after the launch. */
+int fz_reduce(int op, float *out, const float *in, int64_t outer, int64_t len,
+              int64_t inner, void *stream);
+
+/* ---- layout -------------------------------------------------------------- */
+
+/* Materialised swapaxes of a contiguous tensor: out = in with axes a1, a2
+ * exchanged. Replaces serial::swapaxes (fusion/src/Fusion/kernels/Serial.hpp:90-123)
+ * behind fusion::math::linalg::swapaxes (fusion/src/Fusion/ops/Linalg.hpp:109-128). */
+int fz_swapaxes(float *out, const float *in, const int64_t *shape, int ndim, int a1,
+                int a2, void *stream);
+
+/* ---- GEMM ---------------------------------------------------------------- */
+
+enum fz_epilogue { FZ_EPI_NONE = 0, FZ_EPI_BIAS = 1, FZ_EPI_BIAS_RELU = 2 };
+
+/* Batched fp32 GEMM in 3xTF32 on the tcgen05 tensor cores (TMEM accumulators,
+ * TMA-fed shared-memory tiles): C[b] = op(A[b]) @ op(B[b]) for b < batch, with
+ * op(X) = X or X^T (trans flags), element leading dimensions and batch strides.
+ * Each fp32 operand is split into a TF32-exact high part and a low remainder
+ * and C = Ah*Bh + Ah*Bl + Al*Bh, accumulated in fp32. Row-major throughout.
+ * Replaces contraction_tag's BLAS path (fusion/src/Fusion/core/TensorIter.hpp:299-323)
+ * and batched_gemm_rowmajor_nn -> cblas_sgemm
+ * (fusion/src/Fusion/cpu/blas/backend/BlasCblas.hpp:19-39). */
+int fz_gemm_f32(int64_t batch, int64_t M, int64_t N, int64_t K,
+                const float *A, int64_t lda, int64_t strideA, int transA,
+                const float *B, int64_t ldb, int64_t strideB, int transB,
+                float *C, int64_t ldc, int64_t strideC, void *stream);
+
+/* ---- collectives (data-parallel MLP step) -------------------------------- */
+
+#define FZ_UNIQUE_ID_BYTES 128
+/* NCCL unique id for rank 0 to share with the other ranks. */
+int fz_comm_unique_id(unsigned char id[FZ_UNIQUE_ID_BYTES]);
+/* Join a communicator of `world` ranks on the current device. */
+int fz_comm_init(void **comm, int world, int rank,
+                 const unsigned char id[FZ_UNIQUE_ID_BYTES]);
+/* In-place fp32 all-reduce: sum, then multiply by `scale` (1/world for a mean). */
+int fz_comm_allreduce(void *comm, float *buf, int64_t count, float scale, void *stream);
+int fz_comm_broadcast(void *comm, float *buf, int64_t count, int root, void *stream);
+/* Wait for `stream` with a host-side deadline; on expiry abort the communicator
+ * and return FZ_ERR_TIMEOUT instead of blocking for ever. */
+int fz_comm_wait(void *comm, void *stream, double timeout_s);
+int fz_comm_destroy(void *comm);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* FUSION_B200_H */

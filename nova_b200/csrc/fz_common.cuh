@@ -1,0 +1,107 @@
+// Shared definitions of the sm_100a backend: status plumbing, the launch counter,
+// op functors with IEEE round-to-nearest fp32 semantics, and grid sizing.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstdio>
+#include <string>
+
+#include "fusion_b200.h"
+
+namespace fz {
+
+// Thread-local last error message (fz_last_error).
+void set_error(const std::string &msg);
+void clear_error();
+int fail(int code, const std::string &msg);
+int cuda_fail(cudaError_t e, const char *what, const char *file, int line);
+
+// Kernel launch accounting (fz_launch_count).
+void note_launch(int n = 1);
+
+cudaStream_t resolve(void *stream);
+// Per-device int in global memory where kernels with bounded waits record a
+// nonzero code when a wait expires; read and cleared by fz_kernel_status.
+int device_error_word(int **word);
+int num_sms();
+
+// Grid size for a streaming kernel: enough CTAs to cover `work_items` at
+// `per_cta` items each, capped at `waves` full waves of resident CTAs (148 SMs).
+inline unsigned grid_for(int64_t work_items, int64_t per_cta, int ctas_per_sm, int waves = 1) {
+  int64_t need = (work_items + per_cta - 1) / per_cta;
+  int64_t cap = (int64_t)num_sms() * ctas_per_sm * waves;
+  if (need > cap) need = cap;
+  if (need < 1) need = 1;
+  return (unsigned)need;
+}
+
+}  // namespace fz
+
+#define FZ_CUDA(call)                                                        \
+  do {                                                                       \
+    cudaError_t fz_e_ = (call);                                              \
+    if (fz_e_ != cudaSuccess) return fz::cuda_fail(fz_e_, #call, __FILE__, __LINE__); \
+  } while (0)
+
+#define FZ_CHECK_LAUNCH()                                                    \
+  do {                                                                       \
+    cudaError_t fz_e_ = cudaGetLastError();                                  \
+    if (fz_e_ != cudaSuccess) return fz::cuda_fail(fz_e_, "kernel launch", __FILE__, __LINE__); \
+    fz::note_launch();                                                       \
+  } while (0)
+
+#define FZ_REQUIRE(cond, msg)                                                \
+  do {                                                                       \
+    if (!(cond)) return fz::fail(FZ_ERR_INVALID, msg);                       \
+  } while (0)
+
+// ---- device-side op functors (SimdTags.hpp:7-71 semantics) -----------------
+// __f*_rn intrinsics pin round-to-nearest and forbid FMA contraction, so each op
+// rounds exactly once as the reference's scalar loops do.
+namespace fzd {
+
+__device__ __forceinline__ float pow_f(float a, float b) {
+  // std::pow on floats (glibc powf) is correctly rounded; a*a is the correctly
+  // rounded square, so the common exponent 2 is bit-exact. Other exponents use
+  // CUDA's powf.
+  if (b == 2.0f) return __fmul_rn(a, a);
+  return powf(a, b);
+}
+
+__device__ __forceinline__ float binop(int op, float a, float b) {
+  switch (op) {
+    case FZ_ADD: return __fadd_rn(a, b);
+    case FZ_SUB: return __fsub_rn(a, b);
+    case FZ_MUL: return __fmul_rn(a, b);
+    case FZ_DIV: return __fdiv_rn(a, b);
+    case FZ_POW: return pow_f(a, b);
+    case FZ_MAXIMUM: return a > b ? a : b;
+    case FZ_GT: return a > b ? 1.0f : 0.0f;
+    case FZ_GE: return a >= b ? 1.0f : 0.0f;
+  }
+  return 0.0f;
+}
+
+template <int OP>
+__device__ __forceinline__ float binop_t(float a, float b) {
+  if constexpr (OP == FZ_ADD) return __fadd_rn(a, b);
+  else if constexpr (OP == FZ_SUB) return __fsub_rn(a, b);
+  else if constexpr (OP == FZ_MUL) return __fmul_rn(a, b);
+  else if constexpr (OP == FZ_DIV) return __fdiv_rn(a, b);
+  else if constexpr (OP == FZ_POW) return pow_f(a, b);
+  else if constexpr (OP == FZ_MAXIMUM) return a > b ? a : b;
+  else if constexpr (OP == FZ_GT) return a > b ? 1.0f : 0.0f;
+  else return a >= b ? 1.0f : 0.0f;
+}
+
+template <int OP>
+__device__ __forceinline__ float unop_t(float a) {
+  if constexpr (OP == FZ_EXP) return expf(a);
+  else if constexpr (OP == FZ_LOG) return logf(a);
+  else if constexpr (OP == FZ_SQRT) return __fsqrt_rn(a);
+  else return a;
+}
+
+}  // namespace fzd

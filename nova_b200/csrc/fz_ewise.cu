@@ -1,0 +1,195 @@
+// Elementwise binary and unary kernels for sm_100a.
+//
+// A launch walks the output index space of an fz_ewise_plan. The host side first
+// converts byte strides to element strides, drops size-1 dims and merges adjacent
+// dims whose strides chain for every operand, so the usual cases reduce to:
+//   * 1 dim, all strides 1            -> plain contiguous stream (fast path)
+//   * 1 dim, one operand stride 0     -> scalar operand
+//   * 2 dims [rows, cols], a [cols]   -> row broadcast (bias add)
+// The kernel maps each thread to groups of VEC=4 consecutive elements of the
+// innermost dim (128-bit loads/stores when every operand with inner stride 1 is
+// 16-byte aligned at each row start), with a grid-stride loop over groups.
+// Operands with inner stride 0 are loaded once per group and replicated.
+#include "fz_common.cuh"
+#include "fz_ewise_plan.hpp"
+
+namespace {
+
+using fz::EwPlan;
+
+template <typename IDX>
+struct RowMap {
+  // offsets of row `r` (index over all dims but the innermost) for NOPS operands
+  __device__ __forceinline__ static void offsets(const EwPlan &p, IDX r, int64_t *off) {
+    for (int k = 0; k < p.nops; ++k) off[k] = 0;
+    for (int d = p.ndim - 2; d >= 0; --d) {
+      IDX sz = (IDX)p.size[d];
+      IDX q = r / sz;
+      IDX i = r - q * sz;
+      r = q;
+      for (int k = 0; k < p.nops; ++k) off[k] += (int64_t)i * p.stride[k][d];
+    }
+  }
+};
+
+template <int VEC>
+struct Vec;
+template <>
+struct Vec<4> {
+  using T = float4;
+};
+
+__device__ __forceinline__ float4 ld4(const float *p) { return *reinterpret_cast<const float4 *>(p); }
+__device__ __forceinline__ void st4(float *p, float4 v) { *reinterpret_cast<float4 *>(p) = v; }
+
+// Generic kernel: NIN inputs (1 or 2), OP is a binop (NIN=2) or unop (NIN=1).
+template <int NIN, int OP, int VEC, typename IDX>
+__global__ void __launch_bounds__(256) ewise_kernel(EwPlan p, float *__restrict__ out,
+                                                    const float *__restrict__ a,
+                                                    const float *__restrict__ b) {
+  const int64_t inner = p.ndim ? p.size[p.ndim - 1] : 1;
+  const IDX groups_per_row = (IDX)((inner + VEC - 1) / VEC);
+  const IDX total = (IDX)p.rows * groups_per_row;
+  const int64_t so = p.ndim ? p.stride[0][p.ndim - 1] : 0;
+  const int64_t sa = p.ndim ? p.stride[1][p.ndim - 1] : 0;
+  const int64_t sb = (NIN == 2 && p.ndim) ? p.stride[2][p.ndim - 1] : 0;
+  const IDX step = (IDX)gridDim.x * blockDim.x;
+  IDX last_row = (IDX)-1;
+  int64_t off[3] = {0, 0, 0};
+  for (IDX g = (IDX)blockIdx.x * blockDim.x + threadIdx.x; g < total; g += step) {
+    IDX row = g / groups_per_row;
+    IDX col = (g - row * groups_per_row) * VEC;
+    if (row != last_row) {
+      if (p.ndim > 1) RowMap<IDX>::offsets(p, row, off);
+      last_row = row;
+    }
+    if constexpr (VEC == 4) {
+      if ((int64_t)col + 4 <= inner) {
+        float4 x, y = make_float4(0.f, 0.f, 0.f, 0.f);
+        const float *pa = a + off[1] + (int64_t)col * sa;
+        if (sa) x = ld4(pa);
+        else x = make_float4(*pa, *pa, *pa, *pa);
+        if constexpr (NIN == 2) {
+          const float *pb = b + off[2] + (int64_t)col * sb;
+          if (sb) y = ld4(pb);
+          else y = make_float4(*pb, *pb, *pb, *pb);
+        }
+        float4 r;
+        if constexpr (NIN == 2) {
+          r.x = fzd::binop_t<OP>(x.x, y.x);
+          r.y = fzd::binop_t<OP>(x.y, y.y);
+          r.z = fzd::binop_t<OP>(x.z, y.z);
+          r.w = fzd::binop_t<OP>(x.w, y.w);
+        } else {
+          r.x = fzd::unop_t<OP>(x.x);
+          r.y = fzd::unop_t<OP>(x.y);
+          r.z = fzd::unop_t<OP>(x.z);
+          r.w = fzd::unop_t<OP>(x.w);
+        }
+        st4(out + off[0] + (int64_t)col * so, r);
+        continue;
+      }
+    }
+    for (int v = 0; v < VEC && (int64_t)col + v < inner; ++v) {
+      int64_t c = (int64_t)col + v;
+      float x = a[off[1] + c * sa];
+      float r;
+      if constexpr (NIN == 2) r = fzd::binop_t<OP>(x, b[off[2] + c * sb]);
+      else r = fzd::unop_t<OP>(x);
+      out[off[0] + c * so] = r;
+    }
+  }
+}
+
+template <int NIN, int OP>
+int launch_op(const EwPlan &p, float *out, const float *a, const float *b, cudaStream_t s) {
+  int64_t inner = p.ndim ? p.size[p.ndim - 1] : 1;
+  int64_t total = p.rows * inner;
+  if (total == 0) return FZ_OK;
+  // 128-bit path: every operand walking the inner dim with stride 1 must start
+  // each row on a 16-byte boundary; broadcast (stride 0) operands are free.
+  bool vec = p.ndim >= 1;
+  const float *base[3] = {out, a, b};
+  for (int k = 0; vec && k < p.nops; ++k) {
+    int64_t si = p.stride[k][p.ndim - 1];
+    if (si == 0) continue;
+    if (si != 1 || ((uintptr_t)base[k] & 15)) vec = false;
+    for (int d = 0; vec && d + 1 < p.ndim; ++d)
+      if (p.stride[k][d] % 4) vec = false;
+  }
+  int V = vec ? 4 : 1;
+  int64_t groups = p.rows * ((inner + V - 1) / V);
+  bool i64 = groups > (int64_t)0x7fffffff - (int64_t)fz::num_sms() * 2048;
+  unsigned grid = fz::grid_for(groups, 256 * 2, 8);
+  if (vec) {
+    if (i64) ewise_kernel<NIN, OP, 4, int64_t><<<grid, 256, 0, s>>>(p, out, a, b);
+    else ewise_kernel<NIN, OP, 4, int32_t><<<grid, 256, 0, s>>>(p, out, a, b);
+  } else {
+    if (i64) ewise_kernel<NIN, OP, 1, int64_t><<<grid, 256, 0, s>>>(p, out, a, b);
+    else ewise_kernel<NIN, OP, 1, int32_t><<<grid, 256, 0, s>>>(p, out, a, b);
+  }
+  FZ_CHECK_LAUNCH();
+  return FZ_OK;
+}
+
+int dispatch_binary(int op, const EwPlan &p, float *out, const float *a, const float *b,
+                    cudaStream_t s) {
+  switch (op) {
+    case FZ_ADD: return launch_op<2, FZ_ADD>(p, out, a, b, s);
+    case FZ_SUB: return launch_op<2, FZ_SUB>(p, out, a, b, s);
+    case FZ_MUL: return launch_op<2, FZ_MUL>(p, out, a, b, s);
+    case FZ_DIV: return launch_op<2, FZ_DIV>(p, out, a, b, s);
+    case FZ_POW: return launch_op<2, FZ_POW>(p, out, a, b, s);
+    case FZ_MAXIMUM: return launch_op<2, FZ_MAXIMUM>(p, out, a, b, s);
+    case FZ_GT: return launch_op<2, FZ_GT>(p, out, a, b, s);
+    case FZ_GE: return launch_op<2, FZ_GE>(p, out, a, b, s);
+  }
+  return fz::fail(FZ_ERR_INVALID, "fz_ewise_binary: unknown op " + std::to_string(op));
+}
+
+int dispatch_unary(int op, const EwPlan &p, float *out, const float *a, cudaStream_t s) {
+  switch (op) {
+    case FZ_EXP: return launch_op<1, FZ_EXP>(p, out, a, nullptr, s);
+    case FZ_LOG: return launch_op<1, FZ_LOG>(p, out, a, nullptr, s);
+    case FZ_SQRT: return launch_op<1, FZ_SQRT>(p, out, a, nullptr, s);
+    case FZ_COPY: return launch_op<1, FZ_COPY>(p, out, a, nullptr, s);
+  }
+  return fz::fail(FZ_ERR_INVALID, "fz_ewise_unary: unknown op " + std::to_string(op));
+}
+
+}  // namespace
+
+extern "C" {
+
+int fz_ewise_binary(int op, const fz_ewise_plan *plan, float *out, const float *a,
+                    const float *b, void *stream) {
+  FZ_REQUIRE(plan, "fz_ewise_binary: null plan");
+  EwPlan p;
+  int rc = fz::normalize_plan(*plan, 3, p);
+  if (rc) return rc;
+  if (p.rows == 0) return FZ_OK;
+  FZ_REQUIRE(out && a && b, "fz_ewise_binary: null argument");
+  return dispatch_binary(op, p, out, a, b, fz::resolve(stream));
+}
+
+int fz_ewise_binary_contig(int op, int64_t n, float *out, const float *a, const float *b,
+                           void *stream) {
+  FZ_REQUIRE(n >= 0, "fz_ewise_binary_contig: negative length");
+  if (n == 0) return FZ_OK;
+  FZ_REQUIRE(out && a && b, "fz_ewise_binary_contig: null argument");
+  EwPlan p = fz::contiguous_plan(n, 3);
+  return dispatch_binary(op, p, out, a, b, fz::resolve(stream));
+}
+
+int fz_ewise_unary(int op, const fz_ewise_plan *plan, float *out, const float *a,
+                   void *stream) {
+  FZ_REQUIRE(plan, "fz_ewise_unary: null plan");
+  EwPlan p;
+  int rc = fz::normalize_plan(*plan, 2, p);
+  if (rc) return rc;
+  if (p.rows == 0) return FZ_OK;
+  FZ_REQUIRE(out && a, "fz_ewise_unary: null argument");
+  return dispatch_unary(op, p, out, a, fz::resolve(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,500 @@
+// fp32 GEMM in 3xTF32 on the sm_100a tensor cores (tcgen05 + TMEM + TMA).
+//
+// C[b] = op(A[b]) @ op(B[b]), row-major fp32 in and out.
+//
+// 1. Split pass (split_kernel / split_t_kernel): every operand is rewritten as two
+//    K-major planes, hi = x with the low 13 mantissa bits cleared (exactly
+//    representable in TF32) and lo = x - hi (exact in fp32). A is stored [M, K],
+//    B as [N, K] (transposed through shared memory when given as [K, N]). Planes
+//    have a 16-byte-multiple row pitch so TMA can address them.
+// 2. Main kernel, one 128 x 256 output tile per CTA, warp-specialised:
+//      warp 0      TMA producer: per k-tile loads A_hi, A_lo (128 x 32) and
+//                  B_hi, B_lo (256 x 32) into a 2-stage ring (128-byte swizzle)
+//      warp 1      allocates 256 TMEM columns; one lane issues per 8-wide k-step
+//                  three tcgen05.mma.kind::tf32 (hi*hi + hi*lo + lo*hi) into the
+//                  fp32 TMEM accumulator, then tcgen05.commit frees the stage
+//      warps 2-5   epilogue: tcgen05.ld 32 lanes x 32 columns at a time, store C
+//    Every mbarrier wait is bounded by a %globaltimer deadline; on expiry the
+//    kernel records an error code in the device's error word (read by
+//    fz_kernel_status), drains its own TMA loads (bounded), frees TMEM and
+//    returns, so a bad launch surfaces as an error instead of a hang.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "fz_common.cuh"
+
+namespace {
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int BK = 32;  // fp32 elements per k-tile = 128 bytes = one swizzle row
+constexpr int STAGES = 2;
+constexpr int UMMA_K = 8;  // K of one kind::tf32 MMA
+constexpr int TILE_A_BYTES = BM * BK * 4;  // 16 KB
+constexpr int TILE_B_BYTES = BN * BK * 4;  // 32 KB
+constexpr int STAGE_BYTES = 2 * TILE_A_BYTES + 2 * TILE_B_BYTES;  // 96 KB
+constexpr int TMEM_COLS = 256;
+constexpr int NUM_THREADS = 192;
+constexpr unsigned long long kWaitNs = 4000000000ull;  // 4 s per wait
+
+enum : int { kErrNone = 0, kErrTimeoutFull = 1, kErrTimeoutEmpty = 2, kErrTimeoutAcc = 3 };
+
+// ---------------------------------------------------------------- split pass
+__device__ __forceinline__ void split1(float x, float &hi, float &lo) {
+  hi = __uint_as_float(__float_as_uint(x) & 0xffffe000u);
+  lo = __fsub_rn(x, hi);
+}
+
+// src rows are K-major already: src[b][r][k] at b*sb + r*ld + k -> hi/lo[b][r][k] (pitch kp)
+__global__ void __launch_bounds__(256) split_kernel(const float *__restrict__ src, int64_t ld,
+                                                    int64_t sb, int64_t rows, int64_t K,
+                                                    int64_t kp, int64_t batch,
+                                                    float *__restrict__ hi,
+                                                    float *__restrict__ lo) {
+  const int64_t total = batch * rows * kp;
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total;
+       t += (int64_t)gridDim.x * blockDim.x) {
+    int64_t k = t % kp;
+    int64_t rest = t / kp;
+    int64_t r = rest % rows, b = rest / rows;
+    float x = k < K ? src[b * sb + r * ld + k] : 0.0f;
+    float h, l;
+    split1(x, h, l);
+    hi[t] = h;
+    lo[t] = l;
+  }
+}
+
+// src is [b][k][r] (r contiguous, pitch ld): transpose to [b][r][k] while splitting.
+__global__ void __launch_bounds__(256) split_t_kernel(const float *__restrict__ src, int64_t ld,
+                                                      int64_t sb, int64_t rows, int64_t K,
+                                                      int64_t kp, int64_t batch,
+                                                      float *__restrict__ hi,
+                                                      float *__restrict__ lo) {
+  __shared__ float tile[32][33];
+  const int64_t tr = (rows + 31) / 32, tk = (kp + 31) / 32;
+  const int64_t total = batch * tr * tk;
+  const int tx = threadIdx.x % 32, ty = threadIdx.x / 32;
+  for (int64_t t = blockIdx.x; t < total; t += gridDim.x) {
+    int64_t jr = t % tr;
+    int64_t rest = t / tr;
+    int64_t jk = rest % tk, b = rest / tk;
+    const float *s = src + b * sb;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      int64_t k = jk * 32 + ty + 8 * i, r = jr * 32 + tx;
+      tile[ty + 8 * i][tx] = (k < K && r < rows) ? s[k * ld + r] : 0.0f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      int64_t r = jr * 32 + ty + 8 * i, k = jk * 32 + tx;
+      if (r < rows && k < kp) {
+        float h, l;
+        split1(tile[tx][ty + 8 * i], h, l);
+        int64_t o = (b * rows + r) * kp + k;
+        hi[o] = h;
+        lo[o] = l;
+      }
+    }
+    __syncthreads();
+  }
+}
+
+// ---------------------------------------------------------------- PTX helpers
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.b32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait: true on success, false when the deadline passed or another role
+// already reported an error.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (globaltimer() - t0 > kWaitNs) return false;
+  }
+}
+
+__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, uint64_t *bar,
+                                            int c0, int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
+__device__ __forceinline__ void prefetch_map(const CUtensorMap *map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// K-major, 128-byte swizzle: 8-row groups 1024 B apart (SBO), LBO unused (1),
+// descriptor version 1 (bit 46), layout type 2 = SWIZZLE_128B (bits 61-63).
+__device__ __forceinline__ uint64_t smem_desc_k_sw128(uint32_t addr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((addr >> 4) & 0x3fff);
+  d |= (uint64_t)1 << 16;
+  d |= (uint64_t)(1024 >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
+// kind::tf32 instruction descriptor: D = F32 (bits 4-5 = 1), A = B = TF32 (2),
+// both K-major, N >> 3 at bits 17-22, M >> 4 at bits 24-28.
+constexpr uint32_t make_idesc(int m, int n) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(n >> 3) << 17) |
+         ((uint32_t)(m >> 4) << 24);
+}
+constexpr uint32_t kIdesc = make_idesc(BM, BN);
+
+__device__ __forceinline__ void umma_tf32(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t accum) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(a), "l"(b), "r"(kIdesc), "r"(accum)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t *bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+struct GemmArgs {
+  float *C;
+  int64_t ldc, strideC;
+  int M, N, K, batch;
+  int *err;
+};
+
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap mapAh,
+                       const __grid_constant__ CUtensorMap mapAl,
+                       const __grid_constant__ CUtensorMap mapBh,
+                       const __grid_constant__ CUtensorMap mapBl, GemmArgs args) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // 1024-byte alignment for the 128-byte swizzle atoms
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  __shared__ __align__(8) uint64_t full_bar[STAGES];
+  __shared__ __align__(8) uint64_t empty_bar[STAGES];
+  __shared__ __align__(8) uint64_t acc_bar;
+  __shared__ uint32_t tmem_base_slot;
+  __shared__ volatile int abort_flag;
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int tile_n = blockIdx.x, tile_m = blockIdx.y, bz = blockIdx.z;
+  const int num_k = (args.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    mbar_init(&acc_bar, 1);
+    abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    prefetch_map(&mapAh);
+    prefetch_map(&mapAl);
+    prefetch_map(&mapBh);
+    prefetch_map(&mapBl);
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(&tmem_base_slot)),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem_base = tmem_base_slot;
+
+  auto stage_ptr = [&](int s, int which) -> uint8_t * {
+    // which: 0 A_hi, 1 A_lo, 2 B_hi, 3 B_lo
+    uint8_t *base = smem + (size_t)s * STAGE_BYTES;
+    switch (which) {
+      case 0: return base;
+      case 1: return base + TILE_A_BYTES;
+      case 2: return base + 2 * TILE_A_BYTES;
+      default: return base + 2 * TILE_A_BYTES + TILE_B_BYTES;
+    }
+  };
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------ TMA producer
+      int issued = 0;
+      bool ok = true;
+      for (int kt = 0; kt < num_k; ++kt) {
+        const int s = kt % STAGES;
+        const uint32_t round = kt / STAGES;
+        if (kt >= STAGES && !mbar_wait(&empty_bar[s], (round - 1) & 1, &abort_flag)) {
+          ok = false;
+          break;
+        }
+        mbar_expect_tx(&full_bar[s], STAGE_BYTES);
+        const int k0 = kt * BK;
+        tma_load_3d(stage_ptr(s, 0), &mapAh, &full_bar[s], k0, tile_m * BM, bz);
+        tma_load_3d(stage_ptr(s, 1), &mapAl, &full_bar[s], k0, tile_m * BM, bz);
+        tma_load_3d(stage_ptr(s, 2), &mapBh, &full_bar[s], k0, tile_n * BN, bz);
+        tma_load_3d(stage_ptr(s, 3), &mapBl, &full_bar[s], k0, tile_n * BN, bz);
+        ++issued;
+      }
+      if (!ok) {
+        atomicCAS(args.err, kErrNone, kErrTimeoutEmpty);
+        abort_flag = 1;
+        // drain: wait (bounded) for every load this thread issued to land
+        for (int kt = (issued > STAGES ? issued - STAGES : 0); kt < issued; ++kt) {
+          int s = kt % STAGES;
+          const uint64_t t0 = globaltimer();
+          while (!mbar_try_wait(&full_bar[s], (kt / STAGES) & 1) &&
+                 globaltimer() - t0 < kWaitNs) {
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------------------------------ MMA issuer
+      bool ok = true;
+      for (int kt = 0; kt < num_k; ++kt) {
+        const int s = kt % STAGES;
+        if (!mbar_wait(&full_bar[s], (kt / STAGES) & 1, &abort_flag)) {
+          ok = false;
+          break;
+        }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t a_hi = smem_u32(stage_ptr(s, 0)), a_lo = smem_u32(stage_ptr(s, 1));
+        const uint32_t b_hi = smem_u32(stage_ptr(s, 2)), b_lo = smem_u32(stage_ptr(s, 3));
+#pragma unroll
+        for (int kk = 0; kk < BK / UMMA_K; ++kk) {
+          const uint32_t off = kk * UMMA_K * 4;  // 32 bytes per k-step inside the swizzle row
+          const uint64_t dah = smem_desc_k_sw128(a_hi + off), dal = smem_desc_k_sw128(a_lo + off);
+          const uint64_t dbh = smem_desc_k_sw128(b_hi + off), dbl = smem_desc_k_sw128(b_lo + off);
+          const uint32_t first = (kt == 0 && kk == 0) ? 0u : 1u;
+          umma_tf32(tmem_base, dal, dbh, first);  // lo * hi
+          umma_tf32(tmem_base, dah, dbl, 1u);     // hi * lo
+          umma_tf32(tmem_base, dah, dbh, 1u);     // hi * hi (largest term last)
+        }
+        umma_commit(&empty_bar[s]);
+      }
+      if (ok) {
+        umma_commit(&acc_bar);
+      } else {
+        atomicCAS(args.err, kErrNone, kErrTimeoutFull);
+        abort_flag = 1;
+      }
+    }
+  } else {
+    // ------------------------------------------------------ epilogue (warps 2..5)
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    bool ok = mbar_wait(&acc_bar, 0, &abort_flag);
+    if (!ok) {
+      if (lane == 0) atomicCAS(args.err, kErrNone, kErrTimeoutAcc);
+      abort_flag = 1;
+    } else {
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const int row = tile_m * BM + q * 32 + lane;
+      float *crow = args.C + (int64_t)bz * args.strideC + (int64_t)row * args.ldc;
+      const bool vec = ((args.ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(args.C) & 15) == 0) &&
+                       ((args.strideC & 3) == 0);
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, r);
+        const int col0 = tile_n * BN + c0;
+        if (row < args.M && col0 < args.N) {
+          if (vec && col0 + 32 <= args.N) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4) {
+              float4 v = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
+                                     __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
+              *reinterpret_cast<float4 *>(crow + col0 + j) = v;
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (col0 + j < args.N) crow[col0 + j] = __uint_as_float(r[j]);
+          }
+        }
+      }
+    }
+  }
+
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 1) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                 "r"(TMEM_COLS)
+                 : "memory");
+  }
+}
+
+// ---------------------------------------------------------------- host side
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+int get_encoder() {
+  static std::once_flag once;
+  static int rc = FZ_OK;
+  std::call_once(once, []() {
+    cudaDriverEntryPointQueryResult q;
+    void *fn = nullptr;
+    cudaError_t e = cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000,
+                                                     cudaEnableDefault, &q);
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn) {
+      rc = fz::fail(FZ_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+      return;
+    }
+    g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  });
+  return rc;
+}
+
+// 3D map over a [batch, rows, kp] plane (K innermost), box {BK, box_rows, 1}.
+int make_map(CUtensorMap *map, const float *base, int64_t rows, int64_t K, int64_t kp,
+             int64_t batch, int box_rows) {
+  cuuint64_t dims[3] = {(cuuint64_t)K, (cuuint64_t)rows, (cuuint64_t)batch};
+  cuuint64_t strides[2] = {(cuuint64_t)(kp * 4), (cuuint64_t)(kp * rows * 4)};
+  cuuint32_t box[3] = {(cuuint32_t)BK, (cuuint32_t)box_rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, (void *)base, dims, strides, box,
+                        estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fz::fail(FZ_ERR_CUDA, "cuTensorMapEncodeTiled failed with code " + std::to_string((int)r));
+  return FZ_OK;
+}
+
+int split(const float *src, int64_t ld, int64_t sb, bool trans, int64_t rows, int64_t K,
+          int64_t kp, int64_t batch, float *hi, float *lo, cudaStream_t s) {
+  if (!trans) {
+    unsigned grid = fz::grid_for(batch * rows * kp, 256, 8, 4);
+    split_kernel<<<grid, 256, 0, s>>>(src, ld, sb, rows, K, kp, batch, hi, lo);
+  } else {
+    int64_t tiles = batch * ((rows + 31) / 32) * ((kp + 31) / 32);
+    unsigned grid = fz::grid_for(tiles, 1, 8, 4);
+    split_t_kernel<<<grid, 256, 0, s>>>(src, ld, sb, rows, K, kp, batch, hi, lo);
+  }
+  FZ_CHECK_LAUNCH();
+  return FZ_OK;
+}
+
+}  // namespace
+
+extern "C" int fz_gemm_f32(int64_t batch, int64_t M, int64_t N, int64_t K, const float *A,
+                           int64_t lda, int64_t strideA, int transA, const float *B, int64_t ldb,
+                           int64_t strideB, int transB, float *C, int64_t ldc, int64_t strideC,
+                           void *stream) {
+  FZ_REQUIRE(batch >= 0 && M >= 0 && N >= 0 && K >= 0, "fz_gemm_f32: negative extent");
+  if (batch == 0 || M == 0 || N == 0) return FZ_OK;
+  FZ_REQUIRE(C, "fz_gemm_f32: null C");
+  FZ_REQUIRE(M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31) && batch < 65536,
+             "fz_gemm_f32: extent too large");
+  FZ_REQUIRE(ldc >= N, "fz_gemm_f32: ldc < N");
+  cudaStream_t s = fz::resolve(stream);
+  if (K == 0) {
+    for (int64_t b = 0; b < batch; ++b)
+      for (int64_t r = 0; r < M; ++r) {
+        int rc = fz_fill_f32(C + b * strideC + r * ldc, 0.0f, N, s);
+        if (rc) return rc;
+      }
+    return FZ_OK;
+  }
+  FZ_REQUIRE(A && B, "fz_gemm_f32: null operand");
+  FZ_REQUIRE(lda >= (transA ? M : K) && ldb >= (transB ? K : N), "fz_gemm_f32: bad leading dim");
+  int rc = get_encoder();
+  if (rc) return rc;
+
+  const int64_t kp = (K + 3) & ~(int64_t)3;  // 16-byte row pitch for TMA
+  const int64_t a_elems = batch * M * kp, b_elems = batch * N * kp;
+  float *ws = nullptr;
+  rc = fz_malloc((void **)&ws, sizeof(float) * 2 * (a_elems + b_elems), s);
+  if (rc) return rc;
+  float *a_hi = ws, *a_lo = ws + a_elems, *b_hi = ws + 2 * a_elems, *b_lo = b_hi + b_elems;
+  // A as [M, K] K-major: transpose when A is given as [K, M]
+  rc = split(A, lda, strideA, transA != 0, M, K, kp, batch, a_hi, a_lo, s);
+  // B as [N, K] K-major: transpose when B is given as [K, N]
+  if (!rc) rc = split(B, ldb, strideB, transB == 0, N, K, kp, batch, b_hi, b_lo, s);
+
+  CUtensorMap mAh, mAl, mBh, mBl;
+  if (!rc) rc = make_map(&mAh, a_hi, M, K, kp, batch, BM);
+  if (!rc) rc = make_map(&mAl, a_lo, M, K, kp, batch, BM);
+  if (!rc) rc = make_map(&mBh, b_hi, N, K, kp, batch, BN);
+  if (!rc) rc = make_map(&mBl, b_lo, N, K, kp, batch, BN);
+
+  int *err = nullptr;
+  if (!rc) rc = fz::device_error_word(&err);
+  if (!rc) {
+    const size_t smem = (size_t)STAGES * STAGE_BYTES + 1024;
+    static bool attr_done[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 64 && !attr_done[dev]) {
+      cudaFuncSetAttribute(gemm_3xtf32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)smem);
+      attr_done[dev] = true;
+    }
+    GemmArgs ga{C, ldc, strideC, (int)M, (int)N, (int)K, (int)batch, err};
+    dim3 grid((unsigned)((N + BN - 1) / BN), (unsigned)((M + BM - 1) / BM), (unsigned)batch);
+    gemm_3xtf32_kernel<<<grid, NUM_THREADS, smem, s>>>(mAh, mAl, mBh, mBl, ga);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) rc = fz::cuda_fail(e, "gemm_3xtf32_kernel launch", __FILE__, __LINE__);
+    else fz::note_launch();
+  }
+  fz_free(ws, s);
+  return rc;
+}

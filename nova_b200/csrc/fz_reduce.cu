@@ -1,0 +1,310 @@
+// Single-axis reductions (sum / mean / max) for sm_100a.
+//
+// The input is viewed as a contiguous [outer, len, inner] array and reduced over
+// `len`. Two shapes of work:
+//   * inner == 1 (reducing the last axis, or everything): rows of `len`
+//     contiguous floats. Short rows are reduced by groups of G lanes of a warp
+//     (G = 1..32, shuffles within the group); long rows by whole CTAs with
+//     128-bit loads, warp shuffles and a shared-memory tree, and when there are
+//     too few rows to fill 148 SMs a row is split over several CTAs.
+//   * inner > 1 (reducing a leading axis): each thread owns 4 adjacent columns
+//     (one float4 per row read, fully coalesced across the warp) and walks `len`;
+//     when outer*inner/4 threads cannot fill the GPU, `len` is split into chunks.
+// Split work writes fp32 partials to stream-ordered scratch and a second pass
+// reduces them, so results do not depend on scheduling (no atomics).
+// mean = sum / (float)len with an IEEE division, as fusion::math::mean does
+// (fusion/src/Fusion/ops/Reduce.hpp:27-36).
+#include "fz_common.cuh"
+
+namespace {
+
+__device__ __forceinline__ float max_nan(float a, float b) {
+  // NaN propagates; otherwise the larger value, +0 ranking above -0. Order
+  // independent, so a tree and a sequential scan agree bit for bit.
+  if (a != a) return a;
+  if (b != b) return b;
+  if (a > b) return a;
+  if (b > a) return b;
+  return signbit(a) ? b : a;
+}
+
+template <int OP>
+struct Red {
+  __device__ __forceinline__ static float init() { return OP == FZ_RMAX ? -INFINITY : 0.0f; }
+  __device__ __forceinline__ static float op(float a, float b) {
+    return OP == FZ_RMAX ? max_nan(a, b) : __fadd_rn(a, b);
+  }
+};
+
+template <int OP>
+__device__ __forceinline__ float finish(float v, int64_t len, bool final) {
+  if (OP == FZ_RMEAN && final) return __fdiv_rn(v, (float)len);
+  return v;
+}
+
+template <int OP, int G>
+__device__ __forceinline__ float group_reduce(float v) {
+#pragma unroll
+  for (int o = G / 2; o > 0; o >>= 1) v = Red<OP>::op(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Rows of `len` floats (row stride `ld`), G lanes per row. Each lane strides the row
+// by G (vectorised by 4 when the row is 16-byte aligned).
+template <int OP, int G>
+__global__ void __launch_bounds__(256) rows_group_kernel(const float *__restrict__ in,
+                                                         float *__restrict__ out, int64_t rows,
+                                                         int64_t len, int64_t ld,
+                                                         int64_t div_len, int final, int vec) {
+  const int lane = threadIdx.x % G;
+  const int64_t groups_total = (int64_t)gridDim.x * (blockDim.x / G);
+  for (int64_t r = (int64_t)blockIdx.x * (blockDim.x / G) + threadIdx.x / G; r < rows;
+       r += groups_total) {
+    const float *p = in + r * ld;
+    float acc = Red<OP>::init();
+    if (vec) {
+      int64_t nv = len >> 2;
+      const float4 *p4 = reinterpret_cast<const float4 *>(p);
+      for (int64_t j = lane; j < nv; j += G) {
+        float4 q = p4[j];
+        acc = Red<OP>::op(acc, Red<OP>::op(Red<OP>::op(q.x, q.y), Red<OP>::op(q.z, q.w)));
+      }
+      for (int64_t j = (nv << 2) + lane; j < len; j += G) acc = Red<OP>::op(acc, p[j]);
+    } else {
+      for (int64_t j = lane; j < len; j += G) acc = Red<OP>::op(acc, p[j]);
+    }
+    acc = group_reduce<OP, G>(acc);
+    if (lane == 0) out[r] = finish<OP>(acc, div_len, final);
+  }
+}
+
+// Long rows: one CTA per (row, split). Split s covers [s*chunk, min(len, (s+1)*chunk)).
+// out has `splits` entries per row.
+template <int OP>
+__global__ void __launch_bounds__(512) rows_block_kernel(const float *__restrict__ in,
+                                                         float *__restrict__ out, int64_t rows,
+                                                         int64_t len, int64_t ld, int64_t splits,
+                                                         int64_t chunk, int64_t div_len,
+                                                         int final, int vec) {
+  __shared__ float warp_part[32];
+  const int64_t items = rows * splits;
+  for (int64_t it = blockIdx.x; it < items; it += gridDim.x) {
+    const int64_t r = it / splits, s = it - r * splits;
+    const int64_t beg = s * chunk;
+    const int64_t end = beg + chunk < len ? beg + chunk : len;
+    const float *p = in + r * ld;
+    float acc = Red<OP>::init();
+    if (vec) {  // chunk is a multiple of 4 and rows are 16-byte aligned
+      const float4 *p4 = reinterpret_cast<const float4 *>(p + beg);
+      int64_t nv = (end - beg) >> 2;
+      int64_t j = threadIdx.x;
+      for (; j + 3 * (int64_t)blockDim.x < nv; j += 4 * (int64_t)blockDim.x) {
+        float4 q0 = p4[j], q1 = p4[j + blockDim.x], q2 = p4[j + 2 * blockDim.x],
+               q3 = p4[j + 3 * blockDim.x];
+        float t0 = Red<OP>::op(Red<OP>::op(q0.x, q0.y), Red<OP>::op(q0.z, q0.w));
+        float t1 = Red<OP>::op(Red<OP>::op(q1.x, q1.y), Red<OP>::op(q1.z, q1.w));
+        float t2 = Red<OP>::op(Red<OP>::op(q2.x, q2.y), Red<OP>::op(q2.z, q2.w));
+        float t3 = Red<OP>::op(Red<OP>::op(q3.x, q3.y), Red<OP>::op(q3.z, q3.w));
+        acc = Red<OP>::op(acc, Red<OP>::op(Red<OP>::op(t0, t1), Red<OP>::op(t2, t3)));
+      }
+      for (; j < nv; j += blockDim.x) {
+        float4 q = p4[j];
+        acc = Red<OP>::op(acc, Red<OP>::op(Red<OP>::op(q.x, q.y), Red<OP>::op(q.z, q.w)));
+      }
+      for (int64_t k = beg + (nv << 2) + threadIdx.x; k < end; k += blockDim.x)
+        acc = Red<OP>::op(acc, p[k]);
+    } else {
+      for (int64_t k = beg + threadIdx.x; k < end; k += blockDim.x) acc = Red<OP>::op(acc, p[k]);
+    }
+    acc = group_reduce<OP, 32>(acc);
+    const int w = threadIdx.x / 32, nw = blockDim.x / 32;
+    if ((threadIdx.x & 31) == 0) warp_part[w] = acc;
+    __syncthreads();
+    if (w == 0) {
+      float v = (int)threadIdx.x < nw ? warp_part[threadIdx.x] : Red<OP>::init();
+      v = group_reduce<OP, 32>(v);
+      if (threadIdx.x == 0) out[it] = finish<OP>(v, div_len, final);
+    }
+    __syncthreads();
+  }
+}
+
+// Columns: in is [outer, len, inner]; each thread owns V adjacent columns of one
+// outer slice and a chunk of len. out is [splits, outer, inner] (split-major).
+template <int OP, int V>
+__global__ void __launch_bounds__(256) cols_kernel(const float *__restrict__ in,
+                                                   float *__restrict__ out, int64_t outer,
+                                                   int64_t len, int64_t inner, int64_t splits,
+                                                   int64_t chunk, int64_t div_len, int final) {
+  const int64_t cgroups = (inner + V - 1) / V;
+  const int64_t items = splits * outer * cgroups;
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < items;
+       t += (int64_t)gridDim.x * blockDim.x) {
+    int64_t cg = t % cgroups;
+    int64_t rest = t / cgroups;
+    int64_t o = rest % outer;
+    int64_t s = rest / outer;
+    int64_t c = cg * V;
+    int64_t beg = s * chunk, end = beg + chunk < len ? beg + chunk : len;
+    const float *p = in + (o * len) * inner + c;
+    float *q = out + (s * outer + o) * inner + c;
+    if (V == 4 && c + 4 <= inner) {
+      float a0 = Red<OP>::init(), a1 = a0, a2 = a0, a3 = a0;
+      int64_t r = beg;
+      for (; r + 1 < end; r += 2) {
+        float4 x = *reinterpret_cast<const float4 *>(p + r * inner);
+        float4 y = *reinterpret_cast<const float4 *>(p + (r + 1) * inner);
+        a0 = Red<OP>::op(a0, Red<OP>::op(x.x, y.x));
+        a1 = Red<OP>::op(a1, Red<OP>::op(x.y, y.y));
+        a2 = Red<OP>::op(a2, Red<OP>::op(x.z, y.z));
+        a3 = Red<OP>::op(a3, Red<OP>::op(x.w, y.w));
+      }
+      if (r < end) {
+        float4 x = *reinterpret_cast<const float4 *>(p + r * inner);
+        a0 = Red<OP>::op(a0, x.x);
+        a1 = Red<OP>::op(a1, x.y);
+        a2 = Red<OP>::op(a2, x.z);
+        a3 = Red<OP>::op(a3, x.w);
+      }
+      float4 res = make_float4(finish<OP>(a0, div_len, final), finish<OP>(a1, div_len, final),
+                               finish<OP>(a2, div_len, final), finish<OP>(a3, div_len, final));
+      *reinterpret_cast<float4 *>(q) = res;
+    } else {
+      for (int v = 0; v < V && c + v < inner; ++v) {
+        float a = Red<OP>::init();
+        for (int64_t r = beg; r < end; ++r) a = Red<OP>::op(a, p[r * inner + v]);
+        q[v] = finish<OP>(a, div_len, final);
+      }
+    }
+  }
+}
+
+template <int OP>
+int launch_rows(const float *in, float *out, int64_t rows, int64_t len, int64_t ld,
+                int64_t div_len, bool final, cudaStream_t s);
+
+template <int OP>
+int launch_rows_group(const float *in, float *out, int64_t rows, int64_t len, int64_t ld,
+                      int64_t div_len, bool final, cudaStream_t s) {
+  int vec = (ld % 4 == 0) && (((uintptr_t)in & 15) == 0);
+  int G = 1;
+  while (G < 32 && (int64_t)G * 4 * 2 < len) G *= 2;
+  int64_t per_cta = 256 / G;
+  unsigned grid = fz::grid_for(rows, per_cta, 8, 4);
+#define FZ_RG(g)                                                                          \
+  case g:                                                                                 \
+    rows_group_kernel<OP, g><<<grid, 256, 0, s>>>(in, out, rows, len, ld, div_len, final, \
+                                                   vec);                                  \
+    break;
+  switch (G) { FZ_RG(1) FZ_RG(2) FZ_RG(4) FZ_RG(8) FZ_RG(16) FZ_RG(32) }
+#undef FZ_RG
+  FZ_CHECK_LAUNCH();
+  return FZ_OK;
+}
+
+template <int OP>
+int launch_rows(const float *in, float *out, int64_t rows, int64_t len, int64_t ld,
+                int64_t div_len, bool final, cudaStream_t s) {
+  if (len <= 2048) return launch_rows_group<OP>(in, out, rows, len, ld, div_len, final, s);
+  const int threads = 512;
+  const int64_t target_ctas = (int64_t)fz::num_sms() * 4;
+  int64_t splits = 1;
+  if (rows < target_ctas) {
+    splits = (target_ctas + rows - 1) / rows;
+    int64_t max_splits = len / 8192;  // keep >= 8K floats per CTA
+    if (splits > max_splits) splits = max_splits;
+    if (splits < 1) splits = 1;
+  }
+  int64_t chunk = (len + splits - 1) / splits;
+  chunk = (chunk + 3) & ~(int64_t)3;
+  splits = (len + chunk - 1) / chunk;
+  int vec = (ld % 4 == 0) && (((uintptr_t)in & 15) == 0);
+  int64_t items = rows * splits;
+  unsigned grid = (unsigned)(items < target_ctas * 2 ? items : target_ctas * 2);
+  if (splits == 1) {
+    rows_block_kernel<OP><<<grid, threads, 0, s>>>(in, out, rows, len, ld, 1, chunk, div_len,
+                                                   final, vec);
+    FZ_CHECK_LAUNCH();
+    return FZ_OK;
+  }
+  float *part = nullptr;
+  int rc = fz_malloc((void **)&part, sizeof(float) * items, s);
+  if (rc) return rc;
+  rows_block_kernel<OP><<<grid, threads, 0, s>>>(in, part, rows, len, ld, splits, chunk, 0,
+                                                 false, vec);
+  FZ_CHECK_LAUNCH();
+  rc = launch_rows<OP>(part, out, rows, splits, splits, div_len, final, s);
+  fz_free(part, s);
+  return rc;
+}
+
+template <int OP>
+int launch_cols(const float *in, float *out, int64_t outer, int64_t len, int64_t inner,
+                cudaStream_t s) {
+  const bool v4 = (inner % 4 == 0) && (((uintptr_t)in & 15) == 0) && (((uintptr_t)out & 15) == 0);
+  const int V = v4 ? 4 : 1;
+  const int64_t base = outer * ((inner + V - 1) / V);
+  const int64_t target = (int64_t)fz::num_sms() * 2048;
+  int64_t splits = 1;
+  if (base < target) {
+    splits = (target + base - 1) / base;
+    int64_t max_splits = len / 16;  // keep >= 16 rows per thread
+    if (splits > max_splits) splits = max_splits;
+    if (splits < 1) splits = 1;
+  }
+  int64_t chunk = (len + splits - 1) / splits;
+  splits = (len + chunk - 1) / chunk;
+  int64_t items = splits * base;
+  unsigned grid = fz::grid_for(items, 256, 8, 4);
+  float *dst = out;
+  if (splits > 1) {
+    int rc = fz_malloc((void **)&dst, sizeof(float) * splits * outer * inner, s);
+    if (rc) return rc;
+  }
+  if (V == 4)
+    cols_kernel<OP, 4><<<grid, 256, 0, s>>>(in, dst, outer, len, inner, splits, chunk, len,
+                                            splits == 1);
+  else
+    cols_kernel<OP, 1><<<grid, 256, 0, s>>>(in, dst, outer, len, inner, splits, chunk, len,
+                                            splits == 1);
+  FZ_CHECK_LAUNCH();
+  if (splits == 1) return FZ_OK;
+  // second pass: [splits, outer*inner] reduced over splits, finishing with len
+  const int64_t cols = outer * inner;
+  const bool w4 = (cols % 4 == 0) && (((uintptr_t)out & 15) == 0);
+  unsigned g2 = fz::grid_for(cols / (w4 ? 4 : 1) + 1, 256, 8, 4);
+  if (w4)
+    cols_kernel<OP, 4><<<g2, 256, 0, s>>>(dst, out, 1, splits, cols, 1, splits, len, 1);
+  else
+    cols_kernel<OP, 1><<<g2, 256, 0, s>>>(dst, out, 1, splits, cols, 1, splits, len, 1);
+  FZ_CHECK_LAUNCH();
+  fz_free(dst, s);
+  return FZ_OK;
+}
+
+template <int OP>
+int reduce_op(float *out, const float *in, int64_t outer, int64_t len, int64_t inner,
+              cudaStream_t s) {
+  if (inner == 1) return launch_rows<OP>(in, out, outer, len, len, len, true, s);
+  return launch_cols<OP>(in, out, outer, len, inner, s);
+}
+
+}  // namespace
+
+extern "C" int fz_reduce(int op, float *out, const float *in, int64_t outer, int64_t len,
+                         int64_t inner, void *stream) {
+  FZ_REQUIRE(outer >= 0 && len >= 0 && inner >= 0, "fz_reduce: negative extent");
+  if (outer == 0 || inner == 0) return FZ_OK;
+  FZ_REQUIRE(out && (in || len == 0), "fz_reduce: null pointer");
+  cudaStream_t s = fz::resolve(stream);
+  if (len == 0) {
+    float v = op == FZ_RMAX ? -INFINITY : op == FZ_RMEAN ? NAN : 0.0f;
+    return fz_fill_f32(out, v, outer * inner, s);
+  }
+  switch (op) {
+    case FZ_RSUM: return reduce_op<FZ_RSUM>(out, in, outer, len, inner, s);
+    case FZ_RMEAN: return reduce_op<FZ_RMEAN>(out, in, outer, len, inner, s);
+    case FZ_RMAX: return reduce_op<FZ_RMAX>(out, in, outer, len, inner, s);
+  }
+  return fz::fail(FZ_ERR_INVALID, "fz_reduce: unknown op " + std::to_string(op));
+}

@@ -1,0 +1,346 @@
+// Runtime plumbing of the sm_100a backend: errors, devices, per-thread streams,
+// the stream-ordered memory pool, copies, fills and device timers.
+#include <atomic>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "fz_common.cuh"
+
+namespace fz {
+
+static thread_local std::string g_err;
+static std::atomic<int64_t> g_launches{0};
+
+void set_error(const std::string &msg) { g_err = msg; }
+void clear_error() { g_err.clear(); }
+
+int fail(int code, const std::string &msg) {
+  g_err = msg;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char *what, const char *file, int line) {
+  char buf[512];
+  snprintf(buf, sizeof(buf), "CUDA error %d (%s) in %s at %s:%d", (int)e,
+           cudaGetErrorString(e), what, file, line);
+  g_err = buf;
+  return e == cudaErrorMemoryAllocation ? FZ_ERR_OOM : FZ_ERR_CUDA;
+}
+
+void note_launch(int n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+
+constexpr int kMaxDevices = 16;
+
+struct DeviceState {
+  std::once_flag once;
+  int sms = 0;
+  int ok = 0;
+};
+static DeviceState g_dev[kMaxDevices];
+static thread_local cudaStream_t t_stream[kMaxDevices] = {};
+
+static int current_device() {
+  int d = 0;
+  cudaGetDevice(&d);
+  return d;
+}
+
+// One-time per-device setup: check the architecture and keep freed pool blocks
+// cached (release threshold = max) so steady-state allocation never calls the driver.
+static int setup_device(int d) {
+  DeviceState &st = g_dev[d];
+  int rc = FZ_OK;
+  std::call_once(st.once, [&]() {
+    cudaDeviceProp p;
+    if (cudaGetDeviceProperties(&p, d) != cudaSuccess) {
+      rc = fail(FZ_ERR_CUDA, "cudaGetDeviceProperties failed");
+      return;
+    }
+    if (p.major != 10) {
+      rc = fail(FZ_ERR_UNSUPPORTED,
+                "fusion_b200 needs a compute capability 10.x (B200, sm_100a) device; got " +
+                    std::to_string(p.major) + "." + std::to_string(p.minor));
+      return;
+    }
+    st.sms = p.multiProcessorCount;
+    cudaMemPool_t pool;
+    if (cudaDeviceGetDefaultMemPool(&pool, d) == cudaSuccess) {
+      uint64_t thr = UINT64_MAX;
+      cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &thr);
+    }
+    st.ok = 1;
+  });
+  if (rc != FZ_OK) return rc;
+  if (!st.ok) return fail(FZ_ERR_UNSUPPORTED, "device setup failed earlier");
+  return FZ_OK;
+}
+
+cudaStream_t resolve(void *stream) {
+  if (stream) return (cudaStream_t)stream;
+  int d = current_device();
+  if (!t_stream[d]) {
+    setup_device(d);
+    cudaStreamCreateWithFlags(&t_stream[d], cudaStreamNonBlocking);
+  }
+  return t_stream[d];
+}
+
+static int *g_err_word[kMaxDevices] = {};
+static std::mutex g_err_mu;
+
+int device_error_word(int **word) {
+  int d = current_device();
+  std::lock_guard<std::mutex> lk(g_err_mu);
+  if (!g_err_word[d]) {
+    int *p = nullptr;
+    cudaError_t e = cudaMalloc(&p, sizeof(int));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(error word)", __FILE__, __LINE__);
+    e = cudaMemset(p, 0, sizeof(int));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemset(error word)", __FILE__, __LINE__);
+    g_err_word[d] = p;
+  }
+  *word = g_err_word[d];
+  return FZ_OK;
+}
+
+int num_sms() {
+  int d = current_device();
+  if (!g_dev[d].sms) setup_device(d);
+  return g_dev[d].sms ? g_dev[d].sms : 148;
+}
+
+}  // namespace fz
+
+using namespace fz;
+
+namespace {
+__global__ void fill_kernel(float *__restrict__ dst, float v, int64_t n) {
+  int64_t nv = n >> 2;
+  float4 q = make_float4(v, v, v, v);
+  int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  float4 *d4 = reinterpret_cast<float4 *>(dst);
+  for (int64_t j = i; j < nv; j += stride) __stcs(d4 + j, q);
+  for (int64_t j = (nv << 2) + i; j < n; j += stride) dst[j] = v;
+}
+
+__global__ void sub_inplace_kernel(float *__restrict__ x, const float *__restrict__ y, int64_t n) {
+  int64_t nv = n >> 2;
+  int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  float4 *x4 = reinterpret_cast<float4 *>(x);
+  const float4 *y4 = reinterpret_cast<const float4 *>(y);
+  for (int64_t j = i; j < nv; j += stride) {
+    float4 a = x4[j], b = __ldcs(y4 + j);
+    a.x = __fsub_rn(a.x, b.x);
+    a.y = __fsub_rn(a.y, b.y);
+    a.z = __fsub_rn(a.z, b.z);
+    a.w = __fsub_rn(a.w, b.w);
+    x4[j] = a;
+  }
+  for (int64_t j = (nv << 2) + i; j < n; j += stride) x[j] = __fsub_rn(x[j], y[j]);
+}
+
+struct Timer {
+  cudaEvent_t a = nullptr, b = nullptr;
+};
+}  // namespace
+
+extern "C" {
+
+const char *fz_last_error(void) { return g_err.c_str(); }
+int fz_version(void) { return 1; }
+
+int fz_device_count(int *count) {
+  FZ_REQUIRE(count, "fz_device_count: null pointer");
+  int n = 0;
+  cudaError_t e = cudaGetDeviceCount(&n);
+  if (e != cudaSuccess) {
+    *count = 0;
+    cudaGetLastError();
+    return cuda_fail(e, "cudaGetDeviceCount", __FILE__, __LINE__);
+  }
+  int good = 0;
+  for (int d = 0; d < n; ++d) {
+    int major = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, d);
+    if (major == 10) ++good;
+  }
+  *count = good;
+  return FZ_OK;
+}
+
+int fz_set_device(int device) {
+  int n = 0;
+  FZ_CUDA(cudaGetDeviceCount(&n));
+  FZ_REQUIRE(device >= 0 && device < n && device < kMaxDevices, "Invalid device index");
+  FZ_CUDA(cudaSetDevice(device));
+  int rc = setup_device(device);
+  if (rc) return rc;
+  resolve(nullptr);
+  return FZ_OK;
+}
+
+int fz_get_device(int *device) {
+  FZ_REQUIRE(device, "fz_get_device: null pointer");
+  FZ_CUDA(cudaGetDevice(device));
+  return FZ_OK;
+}
+
+void *fz_default_stream(void) { return (void *)resolve(nullptr); }
+
+int fz_stream_sync(void *stream) {
+  FZ_CUDA(cudaStreamSynchronize(resolve(stream)));
+  return FZ_OK;
+}
+
+int fz_device_sync(void) {
+  FZ_CUDA(cudaDeviceSynchronize());
+  return FZ_OK;
+}
+
+int fz_malloc(void **ptr, size_t bytes, void *stream) {
+  FZ_REQUIRE(ptr, "fz_malloc: null pointer");
+  *ptr = nullptr;
+  if (bytes == 0) return FZ_OK;
+  // round to 256 B so every allocation can feed 128-bit and TMA accesses
+  size_t rounded = (bytes + 255) & ~(size_t)255;
+  cudaError_t e = cudaMallocAsync(ptr, rounded, resolve(stream));
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(FZ_ERR_OOM, "device allocation of " + std::to_string(bytes) +
+                                " bytes failed: " + cudaGetErrorString(e));
+  }
+  return FZ_OK;
+}
+
+int fz_free(void *ptr, void *stream) {
+  if (!ptr) return FZ_OK;
+  FZ_CUDA(cudaFreeAsync(ptr, resolve(stream)));
+  return FZ_OK;
+}
+
+int fz_pool_stats(size_t *reserved, size_t *used) {
+  int d = 0;
+  FZ_CUDA(cudaGetDevice(&d));
+  cudaMemPool_t pool;
+  FZ_CUDA(cudaDeviceGetDefaultMemPool(&pool, d));
+  uint64_t r = 0, u = 0;
+  FZ_CUDA(cudaMemPoolGetAttribute(pool, cudaMemPoolAttrReservedMemCurrent, &r));
+  FZ_CUDA(cudaMemPoolGetAttribute(pool, cudaMemPoolAttrUsedMemCurrent, &u));
+  if (reserved) *reserved = r;
+  if (used) *used = u;
+  return FZ_OK;
+}
+
+int fz_memcpy_h2d(void *dst, const void *src, size_t bytes, void *stream) {
+  if (!bytes) return FZ_OK;
+  FZ_REQUIRE(dst && src, "fz_memcpy_h2d: null pointer");
+  FZ_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, resolve(stream)));
+  return FZ_OK;
+}
+
+int fz_memcpy_d2h(void *dst, const void *src, size_t bytes, void *stream) {
+  if (!bytes) return FZ_OK;
+  FZ_REQUIRE(dst && src, "fz_memcpy_d2h: null pointer");
+  cudaStream_t s = resolve(stream);
+  FZ_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, s));
+  FZ_CUDA(cudaStreamSynchronize(s));
+  return FZ_OK;
+}
+
+int fz_memcpy_d2d(void *dst, const void *src, size_t bytes, void *stream) {
+  if (!bytes) return FZ_OK;
+  FZ_REQUIRE(dst && src, "fz_memcpy_d2d: null pointer");
+  FZ_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, resolve(stream)));
+  return FZ_OK;
+}
+
+int fz_fill_f32(float *dst, float value, int64_t n, void *stream) {
+  if (n <= 0) return FZ_OK;
+  FZ_REQUIRE(dst, "fz_fill_f32: null pointer");
+  FZ_REQUIRE(((uintptr_t)dst & 15) == 0, "fz_fill_f32: destination must be 16-byte aligned");
+  unsigned grid = grid_for((n + 3) / 4, 256 * 4, 8);
+  fill_kernel<<<grid, 256, 0, resolve(stream)>>>(dst, value, n);
+  FZ_CHECK_LAUNCH();
+  return FZ_OK;
+}
+
+int fz_sub_inplace(float *x, const float *y, int64_t n, void *stream) {
+  if (n <= 0) return FZ_OK;
+  FZ_REQUIRE(x && y, "fz_sub_inplace: null pointer");
+  FZ_REQUIRE((((uintptr_t)x | (uintptr_t)y) & 15) == 0,
+             "fz_sub_inplace: operands must be 16-byte aligned");
+  unsigned grid = grid_for((n + 3) / 4, 256 * 2, 8);
+  sub_inplace_kernel<<<grid, 256, 0, resolve(stream)>>>(x, y, n);
+  FZ_CHECK_LAUNCH();
+  return FZ_OK;
+}
+
+int fz_host_alloc(void **ptr, size_t bytes) {
+  FZ_REQUIRE(ptr, "fz_host_alloc: null pointer");
+  FZ_CUDA(cudaMallocHost(ptr, bytes ? bytes : 1));
+  return FZ_OK;
+}
+
+int fz_host_free(void *ptr) {
+  if (ptr) FZ_CUDA(cudaFreeHost(ptr));
+  return FZ_OK;
+}
+
+int fz_timer_create(void **timer) {
+  FZ_REQUIRE(timer, "fz_timer_create: null pointer");
+  Timer *t = new Timer;
+  FZ_CUDA(cudaEventCreate(&t->a));
+  FZ_CUDA(cudaEventCreate(&t->b));
+  *timer = t;
+  return FZ_OK;
+}
+
+int fz_timer_start(void *timer, void *stream) {
+  FZ_REQUIRE(timer, "fz_timer_start: null timer");
+  FZ_CUDA(cudaEventRecord(static_cast<Timer *>(timer)->a, resolve(stream)));
+  return FZ_OK;
+}
+
+int fz_timer_stop(void *timer, void *stream) {
+  FZ_REQUIRE(timer, "fz_timer_stop: null timer");
+  FZ_CUDA(cudaEventRecord(static_cast<Timer *>(timer)->b, resolve(stream)));
+  return FZ_OK;
+}
+
+int fz_timer_elapsed_ms(void *timer, float *ms) {
+  FZ_REQUIRE(timer && ms, "fz_timer_elapsed_ms: null pointer");
+  Timer *t = static_cast<Timer *>(timer);
+  FZ_CUDA(cudaEventSynchronize(t->b));
+  FZ_CUDA(cudaEventElapsedTime(ms, t->a, t->b));
+  return FZ_OK;
+}
+
+int fz_timer_destroy(void *timer) {
+  if (!timer) return FZ_OK;
+  Timer *t = static_cast<Timer *>(timer);
+  cudaEventDestroy(t->a);
+  cudaEventDestroy(t->b);
+  delete t;
+  return FZ_OK;
+}
+
+int64_t fz_launch_count(void) { return g_launches.load(); }
+
+int fz_kernel_status(void) {
+  int *w = nullptr;
+  int rc = device_error_word(&w);
+  if (rc) return rc;
+  int v = 0;
+  FZ_CUDA(cudaDeviceSynchronize());
+  FZ_CUDA(cudaMemcpy(&v, w, sizeof(int), cudaMemcpyDeviceToHost));
+  if (v) {
+    FZ_CUDA(cudaMemset(w, 0, sizeof(int)));
+    return fail(FZ_ERR_TIMEOUT, "a kernel's bounded wait expired (code " + std::to_string(v) + ")");
+  }
+  return FZ_OK;
+}
+
+}  // extern "C"

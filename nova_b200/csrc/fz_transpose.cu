@@ -1,0 +1,117 @@
+// Materialised swapaxes for sm_100a.
+//
+// A contiguous tensor with axes a1 < a2 exchanged is viewed as
+//   in  [P, A, Q, B, R]  ->  out [P, B, Q, A, R]
+// with A = shape[a1], B = shape[a2]. When R == 1 (the last axis takes part, as in
+// the W.T / x.T of a Linear layer) each of the P*Q [A, B] planes is transposed
+// through a 32x33 shared-memory tile, so both the reads and the writes are
+// coalesced 128-byte rows. When R > 1 whole R-runs move together and a
+// vectorised gather copy is used.
+#include "fz_common.cuh"
+
+namespace {
+
+constexpr int kTile = 32;
+constexpr int kRows = 8;
+
+__global__ void __launch_bounds__(kTile *kRows) transpose_tiles(const float *__restrict__ in,
+                                                               float *__restrict__ out, int64_t P,
+                                                               int64_t Q, int64_t A, int64_t B) {
+  __shared__ float tile[kTile][kTile + 1];
+  const int64_t ta = (A + kTile - 1) / kTile, tb = (B + kTile - 1) / kTile;
+  const int64_t total = P * Q * ta * tb;
+  const int tx = threadIdx.x % kTile, ty = threadIdx.x / kTile;
+  for (int64_t t = blockIdx.x; t < total; t += gridDim.x) {
+    int64_t jb = t % tb;
+    int64_t rest = t / tb;
+    int64_t ib = rest % ta;
+    rest /= ta;
+    int64_t q = rest % Q, p = rest / Q;
+    const float *src = in + p * A * Q * B + q * B;  // element (i, j) at i*Q*B + j
+    float *dst = out + p * B * Q * A + q * A;       // element (j, i) at j*Q*A + i
+    const int64_t i0 = ib * kTile, j0 = jb * kTile;
+#pragma unroll
+    for (int k = 0; k < kTile / kRows; ++k) {
+      int64_t i = i0 + ty + k * kRows, j = j0 + tx;
+      if (i < A && j < B) tile[ty + k * kRows][tx] = src[i * Q * B + j];
+    }
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < kTile / kRows; ++k) {
+      int64_t j = j0 + ty + k * kRows, i = i0 + tx;
+      if (j < B && i < A) dst[j * Q * A + i] = tile[tx][ty + k * kRows];
+    }
+    __syncthreads();
+  }
+}
+
+// R > 1: out[p, j, q, i, r] = in[p, i, q, j, r]; each thread copies V floats of a run.
+template <int V>
+__global__ void __launch_bounds__(256) transpose_runs(const float *__restrict__ in,
+                                                     float *__restrict__ out, int64_t P, int64_t A,
+                                                     int64_t Q, int64_t B, int64_t R) {
+  const int64_t rv = R / V;
+  const int64_t total = P * B * Q * A * rv;
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total;
+       t += (int64_t)gridDim.x * blockDim.x) {
+    int64_t r = (t % rv) * V;
+    int64_t rest = t / rv;
+    int64_t i = rest % A;
+    rest /= A;
+    int64_t q = rest % Q;
+    rest /= Q;
+    int64_t j = rest % B;
+    int64_t p = rest / B;
+    const float *s = in + (((p * A + i) * Q + q) * B + j) * R + r;
+    float *d = out + (((p * B + j) * Q + q) * A + i) * R + r;
+    if constexpr (V == 4)
+      *reinterpret_cast<float4 *>(d) = *reinterpret_cast<const float4 *>(s);
+    else
+      *d = *s;
+  }
+}
+
+}  // namespace
+
+extern "C" int fz_swapaxes(float *out, const float *in, const int64_t *shape, int ndim, int a1,
+                           int a2, void *stream) {
+  FZ_REQUIRE(shape && ndim >= 0 && ndim <= 32, "fz_swapaxes: bad shape");
+  int64_t total = 1;
+  for (int d = 0; d < ndim; ++d) {
+    FZ_REQUIRE(shape[d] >= 0, "fz_swapaxes: negative extent");
+    total *= shape[d];
+  }
+  if (total == 0) return FZ_OK;
+  FZ_REQUIRE(out && in, "fz_swapaxes: null pointer");
+  cudaStream_t s = fz::resolve(stream);
+  if (ndim < 2) return fz_memcpy_d2d(out, in, total * sizeof(float), s);
+  if (a1 < 0) a1 += ndim;
+  if (a2 < 0) a2 += ndim;
+  FZ_REQUIRE(a1 >= 0 && a1 < ndim && a2 >= 0 && a2 < ndim, "fz_swapaxes: axis out of range");
+  if (a1 == a2) return fz_memcpy_d2d(out, in, total * sizeof(float), s);
+  if (a1 > a2) {
+    int t = a1;
+    a1 = a2;
+    a2 = t;
+  }
+  int64_t P = 1, Q = 1, R = 1, A = shape[a1], B = shape[a2];
+  for (int d = 0; d < a1; ++d) P *= shape[d];
+  for (int d = a1 + 1; d < a2; ++d) Q *= shape[d];
+  for (int d = a2 + 1; d < ndim; ++d) R *= shape[d];
+  if (A == 1 || B == 1) {
+    if (Q == 1 || (A == 1 && B == 1)) return fz_memcpy_d2d(out, in, total * sizeof(float), s);
+  }
+  if (R == 1) {
+    int64_t tiles = P * Q * ((A + kTile - 1) / kTile) * ((B + kTile - 1) / kTile);
+    unsigned grid = fz::grid_for(tiles, 1, 8, 4);
+    transpose_tiles<<<grid, kTile * kRows, 0, s>>>(in, out, P, Q, A, B);
+  } else {
+    bool v4 = R % 4 == 0 && (((uintptr_t)in | (uintptr_t)out) & 15) == 0;
+    int64_t items = total / (v4 ? 4 : 1);
+    unsigned grid = fz::grid_for(items, 256, 8, 4);
+    if (v4) transpose_runs<4><<<grid, 256, 0, s>>>(in, out, P, A, Q, B, R);
+    else transpose_runs<1><<<grid, 256, 0, s>>>(in, out, P, A, Q, B, R);
+  }
+  FZ_CHECK_LAUNCH();
+  return FZ_OK;
+}

@@ -1,0 +1,254 @@
+// pybind11 module `fusion`: the Python API that Nova imports
+// (nova/src/backend/core/clib/__init__.py:1-3), with the names, argument meaning
+// and error behaviour of the reference module (fusion/src/Fusion/python/Bindings.cpp,
+// tensor/BindTensor.hpp, factory/BindFactory.hpp, random/BindRandom.hpp), backed by
+// the B200 tensor of this project.
+#include <pybind11/numpy.h>
+#include <pybind11/operators.h>
+#include <pybind11/pybind11.h>
+#include <pybind11/stl.h>
+
+#include <numeric>
+#include <random>
+#include <sstream>
+
+#include "autodiff.hpp"
+
+namespace py = pybind11;
+using namespace fusion_b200;
+
+namespace {
+
+size_t prod(const std::vector<size_t> &s) {
+  return std::accumulate(s.begin(), s.end(), (size_t)1, std::multiplies<size_t>());
+}
+
+// Random<T>::uniform_base (fusion/src/Fusion/Random.hpp:20-36): mt19937 with
+// uniform_real_distribution<float>, generated on the host, then uploaded.
+struct Random {
+  std::mt19937 engine;
+  explicit Random(uint32_t seed) : engine(seed) {}
+  ADTensor uniform(const std::vector<size_t> &shape, float lo, float hi, Device dev) {
+    std::vector<float> data;
+    size_t n = prod(shape);
+    data.reserve(n);
+    std::uniform_real_distribution<float> dist(lo, hi);
+    for (size_t i = 0; i < n; ++i) data.push_back(dist(engine));
+    return ADTensor(RawTensor(shape, data, DType::FLOAT32, dev), false);
+  }
+};
+
+py::array_t<float> to_numpy(const ADTensor &t) {
+  const auto &shape = t.shape();
+  std::vector<ssize_t> sh(shape.begin(), shape.end());
+  py::array_t<float> arr(sh);
+  t.raw().to_host(static_cast<float *>(arr.request().ptr));
+  return arr;
+}
+
+RawTensor raw_from_array(const std::vector<size_t> &shape, py::array_t<float, py::array::c_style | py::array::forcecast> a,
+                         DType dt, Device dev) {
+  size_t total = prod(shape);
+  if ((size_t)a.size() != total) throw std::invalid_argument("shape* must equal data.size()");
+  return RawTensor(shape, a.data(), dt, dev);
+}
+
+struct GradTape {
+  EngineScope scope;
+};
+
+}  // namespace
+
+PYBIND11_MODULE(fusion, m) {
+  m.doc() = "Fusion Tensor module exposing Tensor<float> (for composition) on the B200 backend";
+
+  py::class_<Device>(m, "CppDevice")
+      .def(py::init([](DeviceType t, int idx) { return Device(t, idx); }), py::arg("type"),
+           py::arg("index") = -1)
+      .def_property_readonly("type", [](const Device &d) { return d.type; })
+      .def_property_readonly("index", [](const Device &d) { return d.idx; });
+
+  py::enum_<DeviceType>(m, "CppDeviceType")
+      .value("CPU", DeviceType::CPU)
+      .value("CUDA", DeviceType::CUDA)
+      .value("METAL", DeviceType::METAL);
+
+  py::enum_<DType>(m, "CppDType")
+      .value("FLOAT32", DType::FLOAT32)
+      .value("FLOAT64", DType::FLOAT64)
+      .value("INT32", DType::INT32)
+      .value("INT64", DType::INT64)
+      .value("BOOL", DType::BOOL);
+
+  using T = ADTensor;
+  py::class_<T>(m, "Tensor")
+      .def(py::init([](const std::vector<size_t> &shape, DType dt, Device dev, bool rg) {
+             return T(RawTensor(shape, dt, dev), rg);
+           }),
+           py::arg("shape"), py::arg("dtype"), py::arg("device"), py::arg("requires_grad"),
+           "Construct a Tensor of given shape, zero-initialized. Optionally set requires_grad.")
+      .def(py::init([](const std::vector<size_t> &shape,
+                       py::array_t<float, py::array::c_style | py::array::forcecast> data, DType dt,
+                       Device dev, bool rg) { return T(raw_from_array(shape, data, dt, dev), rg); }),
+           py::arg("shape"), py::arg("data"), py::arg("dtype"), py::arg("device"),
+           py::arg("requires_grad"),
+           "Construct a Tensor from a shape list and flat data (list or array).")
+      .def(
+          "set_values",
+          [](T &t, py::array_t<float, py::array::c_style | py::array::forcecast> vals) {
+            size_t expected = t.flat_size();
+            if ((size_t)vals.size() != expected)
+              throw std::invalid_argument("set_values: expected " + std::to_string(expected) +
+                                          " elements, got " + std::to_string(vals.size()));
+            t.raw().set_values(vals.data(), expected);
+          },
+          py::arg("values"), "Fill the Tensor with a flat list of length prod(shape).")
+      .def_property_readonly("shape", [](const T &t) { return t.shape(); })
+      .def_property_readonly("ndim", [](const T &t) { return t.rank(); })
+      .def_property_readonly("dtype", [](const T &) { return py::dtype::of<float>(); })
+      .def_property_readonly("size", &T::flat_size)
+      .def_property_readonly("name", [](const T &) { return std::string("ADTensor"); })
+      .def_property_readonly("device", [](const T &t) { return t.device(); })
+      .def_property("requires_grad", &T::requires_grad, &T::set_requires_grad)
+      .def("to_numpy", &to_numpy, "Return a NumPy copy of the Tensor's contents.")
+      .def("__repr__", [](const T &t) { return t.raw().repr(); })
+      .def("__add__", [](const T &a, const T &b) { return a.binary_op(OpKind::Add, b); }, py::is_operator())
+      .def("__add__", [](const T &a, float b) { return a.binary_scalar(OpKind::Add, b); }, py::is_operator())
+      .def("__sub__", [](const T &a, const T &b) { return a.binary_op(OpKind::Subtract, b); }, py::is_operator())
+      .def("__sub__", [](const T &a, float b) { return a.binary_scalar(OpKind::Subtract, b); }, py::is_operator())
+      .def("__mul__", [](const T &a, const T &b) { return a.binary_op(OpKind::Multiply, b); }, py::is_operator())
+      .def("__mul__", [](const T &a, float b) { return a.binary_scalar(OpKind::Multiply, b); }, py::is_operator())
+      .def("__truediv__", [](const T &a, const T &b) { return a.binary_op(OpKind::Divide, b); }, py::is_operator())
+      .def("__truediv__", [](const T &a, float b) { return a.binary_scalar(OpKind::Divide, b); }, py::is_operator())
+      .def("__pow__", [](const T &a, const T &b) { return a.binary_op(OpKind::Pow, b); }, py::is_operator())
+      .def("__pow__", [](const T &a, float b) { return a.binary_scalar(OpKind::Pow, b); }, py::is_operator())
+      .def("__ge__", [](const T &a, const T &b) { return a.binary_op(OpKind::GreaterThanEqual, b); }, py::is_operator())
+      .def("__ge__", [](const T &a, float b) { return a.binary_scalar(OpKind::GreaterThanEqual, b); }, py::is_operator())
+      .def("__gt__", [](const T &a, const T &b) { return a.binary_op(OpKind::GreaterThan, b); }, py::is_operator())
+      .def(
+          "__neg__",
+          // BindTensor.hpp:120-126 computes zeros_like(raw) - raw (an untracked result)
+          [](const T &t) { return T(zeros_like(t.raw()) - t.raw(), false); }, py::is_operator())
+      .def(
+          "__isub__",
+          [](T &a, const T &b) -> T & {
+            a.raw() -= b.raw();
+            return a;
+          },
+          py::is_operator())
+      .def("sqrt", [](const T &t) { return t.unary_op(OpKind::Sqrt); })
+      .def("exp", [](const T &t) { return t.unary_op(OpKind::Exp); })
+      .def("log", [](const T &t) { return t.unary_op(OpKind::Log); })
+      .def("sum", [](const T &t) { return t.unary_op(OpKind::Sum, OpParam{kGlobalReduceAxis, false}); })
+      .def(
+          "sum",
+          [](const T &t, size_t axis, bool keepdim) { return t.unary_op(OpKind::Sum, OpParam{axis, keepdim}); },
+          py::arg("axis"), py::arg("keepdim") = false)
+      .def("mean", [](const T &t) { return t.unary_op(OpKind::Mean, OpParam{kGlobalReduceAxis, false}); })
+      .def(
+          "mean",
+          [](const T &t, size_t axis, bool keepdim) { return t.unary_op(OpKind::Mean, OpParam{axis, keepdim}); },
+          py::arg("axis"), py::arg("keepdim") = false)
+      .def(
+          "max",
+          // New reduction (no reference counterpart); untracked, like comparisons' values.
+          [](const T &t, py::object axis, bool keepdim) {
+            size_t ax = axis.is_none() ? kGlobalReduceAxis : axis.cast<size_t>();
+            return T(t.raw().max(ax, keepdim), false);
+          },
+          py::arg("axis") = py::none(), py::arg("keepdim") = false)
+      .def("__matmul__", [](const T &a, const T &b) { return a.binary_op(OpKind::MatMul, b); })
+      .def("maximum", [](const T &a, const T &b) { return a.binary_op(OpKind::Maximum, b); }, py::is_operator())
+      .def("maximum", [](const T &a, float b) { return a.binary_scalar(OpKind::Maximum, b); }, py::is_operator())
+      .def(
+          "swapaxes",
+          [](const T &t, int a1, int a2) {
+            OpParam p;
+            p.axis1 = a1;
+            p.axis2 = a2;
+            return t.unary_op(OpKind::SwapAxes, p);
+          },
+          py::arg("axis1"), py::arg("axis2"))
+      .def("backward", &T::backward)
+      .def("get_grad", &T::grad)
+      .def("rank", &T::rank)
+      .def("is_pending", [](const T &t) { return t.raw().pending(); },
+           "True while the value is an unlowered node of the fusion IR.");
+
+  auto fac = m.def_submodule("factory", "factory functions for Tensor<float>");
+  fac.def("fill", [](const std::vector<size_t> &s, float v, Device d) {
+    return T(RawTensor::full(s, v, DType::FLOAT32, d), false);
+  }, py::arg("shape"), py::arg("value"), py::arg("device"));
+  fac.def("zeros", [](const std::vector<size_t> &s, Device d) {
+    return T(RawTensor::full(s, 0.0f, DType::FLOAT32, d), false);
+  }, py::arg("shape"), py::arg("device"));
+  fac.def("ones", [](const std::vector<size_t> &s, Device d) {
+    return T(RawTensor::full(s, 1.0f, DType::FLOAT32, d), false);
+  }, py::arg("shape"), py::arg("device"));
+  fac.def("zeros_like", [](const T &t) { return T(zeros_like(t.raw()), t.requires_grad()); },
+          py::arg("other"));
+  fac.def("ones_like", [](const T &t) { return T(ones_like(t.raw()), t.requires_grad()); },
+          py::arg("other"));
+
+  py::class_<Random>(m, "Random")
+      .def(py::init<uint32_t>(), py::arg("seed") = std::random_device{}())
+      .def("uniform_cpp", &Random::uniform, py::arg("shape"), py::arg("min"), py::arg("max"),
+           py::arg("device"));
+
+  py::class_<GradTape>(m, "grad_tape")
+      .def(py::init<>())
+      .def(
+          "__enter__",
+          [](GradTape &self) -> GradTape & {
+            self.scope.enter();
+            return self;
+          },
+          py::return_value_policy::reference)
+      .def("__exit__", [](GradTape &self, const py::object &, const py::object &, const py::object &) {
+        self.scope.exit();
+        return false;
+      });
+
+  auto ad = m.def_submodule("autodiff", "Autodiff control");
+  ad.def(
+      "enabled",
+      [](py::object state) {
+        if (!state.is_none()) set_autodiff_enabled(state.cast<bool>());
+        return grad_enabled();
+      },
+      py::arg("state") = py::none(),
+      "Get or set whether autodiff is enabled for this thread. When enabled, a default "
+      "Engine is installed in the EngineContext.");
+
+  // ---- backend controls (no reference counterpart) ------------------------
+  m.def("set_device", [](int d) { fz_check(fz_set_device(d), "fz_set_device"); }, py::arg("index"),
+        "Make CUDA device `index` current for this thread.");
+  m.def("device_count", []() {
+    int n = 0;
+    fz_device_count(&n);
+    return n;
+  });
+  m.def("synchronize", []() {
+    fz_check(fz_stream_sync(nullptr), "fz_stream_sync");
+    fz_check(fz_kernel_status(), "fz_kernel_status");
+  }, "Wait for this thread's stream and surface any kernel-side bounded-wait error.");
+  m.def("set_fusion", &set_fusion_enabled, py::arg("enabled"),
+        "Enable (default) or disable lazy elementwise fusion.");
+  m.def("fusion_enabled", &fusion_enabled);
+  m.def("flush", [](const T &t) { t.raw().data(); }, py::arg("tensor"),
+        "Lower a pending tensor to device memory now.");
+  m.def("stats", []() {
+    py::dict d;
+    d["kernel_launches"] = fz_launch_count();
+    d["fused_launches"] = fused_launches();
+    d["fused_kernels_compiled"] = fz_fused_cache_size();
+    size_t r = 0, u = 0;
+    if (fz_pool_stats(&r, &u) == FZ_OK) {
+      d["pool_reserved_bytes"] = r;
+      d["pool_used_bytes"] = u;
+    }
+    return d;
+  });
+  m.def("device_ptr", [](const T &t) { return reinterpret_cast<uintptr_t>(t.raw().data()); },
+        py::arg("tensor"), "Device address of the tensor's data (lowers it if pending).");
+}

@@ -1,0 +1,625 @@
+// RawTensor, device storage and the fusion IR lowering (see tensor.hpp).
+#include "tensor.hpp"
+
+#include <algorithm>
+#include <cstring>
+#include <numeric>
+#include <sstream>
+#include <unordered_map>
+
+namespace fusion_b200 {
+
+// ---------------------------------------------------------------- errors
+void throw_check(const char *file, int line, const std::string &msg) {
+  // Same text shape as FUSION_CHECK (fusion/src/Fusion/common/Checks.hpp:14-29).
+  std::ostringstream os;
+  os << "FUSION_CHECK failed @ " << file << ":" << line << ": " << msg;
+  throw std::runtime_error(os.str());
+}
+
+void fz_check(int rc, const char *what) {
+  if (rc == FZ_OK) return;
+  std::string msg = std::string(what) + ": " + fz_last_error();
+  if (rc == FZ_ERR_OOM) throw std::bad_alloc();
+  if (rc == FZ_ERR_INVALID) throw std::invalid_argument(msg);
+  throw std::runtime_error(msg);
+}
+
+// ---------------------------------------------------------------- device
+static int device_count_cached() {
+  static int n = -1;
+  if (n < 0) {
+    int c = 0;
+    n = fz_device_count(&c) == FZ_OK ? c : 0;
+  }
+  return n;
+}
+
+Device::Device(DeviceType t, int i) : type(t), idx(i) {
+  if (t == DeviceType::CPU) FB_CHECK(i <= 0, "Invalid device index");
+  else if (t == DeviceType::CUDA) FB_CHECK(i >= -1, "Invalid device index");
+  else throw std::runtime_error("Unsupported device");
+}
+
+int Device::cuda_index() const {
+  if (type == DeviceType::CUDA && idx >= 0) return idx;
+  int d = 0;
+  fz_check(fz_get_device(&d), "fz_get_device");
+  return d;
+}
+
+int bind_device(const Device &d) {
+  int want = d.cuda_index();
+  int cur = -1;
+  fz_get_device(&cur);
+  if (cur != want || fz_default_stream() == nullptr) {
+    FB_CHECK(want < device_count_cached(), "Invalid device index");
+    fz_check(fz_set_device(want), "fz_set_device");
+  }
+  return want;
+}
+
+size_t dtype_size(DType d) {
+  switch (d) {
+    case DType::FLOAT32: return 4;
+    case DType::FLOAT64: return 8;
+    case DType::INT32: return 4;
+    case DType::INT64: return 8;
+    case DType::BOOL: return 1;
+  }
+  throw std::runtime_error("Unknown DType");
+}
+
+// ---------------------------------------------------------------- memory
+DeviceBuffer::DeviceBuffer(size_t n) : numel(n) {
+  fz_get_device(&device);
+  void *p = nullptr;
+  fz_check(fz_malloc(&p, n * sizeof(float), nullptr), "fz_malloc");
+  ptr = static_cast<float *>(p);
+}
+
+DeviceBuffer::~DeviceBuffer() {
+  if (ptr) fz_free(ptr, nullptr);
+}
+
+size_t Expr::numel() const {
+  size_t n = 1;
+  for (auto s : shape) n *= s;
+  return n;
+}
+
+// ---------------------------------------------------------------- fusion IR
+static bool g_fusion = true;
+static int64_t g_fused_launches = 0;
+constexpr int kNodeLimit = 40;   // below FZ_MAX_NODES, leaving room for dedupe slack
+constexpr int kLeafLimit = 10;   // below FZ_MAX_LEAVES
+
+void set_fusion_enabled(bool on) { g_fusion = on; }
+bool fusion_enabled() { return g_fusion; }
+int64_t fused_launches() { return g_fused_launches; }
+
+static ExprPtr make_leaf(std::shared_ptr<DeviceBuffer> buf, std::vector<size_t> shape) {
+  auto e = std::make_shared<Expr>();
+  e->kind = Expr::Leaf;
+  e->shape = std::move(shape);
+  e->buf = std::move(buf);
+  e->nodes_ub = 0;
+  e->leaves_ub = 1;
+  return e;
+}
+
+static ExprPtr make_const(float v, std::vector<size_t> shape) {
+  auto e = std::make_shared<Expr>();
+  e->kind = Expr::Const;
+  e->shape = std::move(shape);
+  e->imm = v;
+  e->nodes_ub = 1;
+  e->leaves_ub = 0;
+  return e;
+}
+
+float *Storage::data() {
+  if (expr->kind != Expr::Leaf) materialize(expr);
+  return expr->buf ? expr->buf->ptr : nullptr;
+}
+
+// Right-aligned broadcast of two shapes (TensorPlan.cpp:40-48, 67-126 rules).
+static std::vector<size_t> broadcast_shape(const std::vector<size_t> &a, const std::vector<size_t> &b) {
+  size_t n = std::max(a.size(), b.size());
+  std::vector<size_t> out(n);
+  for (size_t d = 0; d < n; ++d) {
+    long ia = (long)d - (long)(n - a.size()), ib = (long)d - (long)(n - b.size());
+    size_t da = ia >= 0 ? a[ia] : 1, db = ib >= 0 ? b[ib] : 1;
+    if (da == db || db == 1) out[d] = da;
+    else if (da == 1) out[d] = db;
+    else throw std::runtime_error("broadcast: dimension mismatch");
+  }
+  return out;
+}
+
+// Element strides of a contiguous operand of shape `s` seen from output shape
+// `out`: 0 on broadcast dims (TensorPlan.cpp:50-65).
+static void operand_strides(const std::vector<size_t> &s, const std::vector<size_t> &out,
+                            int64_t *st) {
+  size_t nd = out.size(), pad = nd - s.size();
+  int64_t r = 1;
+  for (long d = (long)nd - 1; d >= 0; --d) {
+    long i = d - (long)pad;
+    if (i < 0) {
+      st[d] = 0;
+      continue;
+    }
+    st[d] = (s[i] == 1 && out[d] > 1) ? 0 : r;
+    r *= (int64_t)s[i];
+  }
+}
+
+namespace {
+struct Lowering {
+  fz_program prog{};
+  std::unordered_map<const Expr *, int> node_of;
+  std::vector<const Expr *> leaves;
+  std::unordered_map<const float *, int> leaf_of_buf;  // dedupe equal buffers of equal shape
+  bool overflow = false;
+
+  int leaf_index(const Expr *e) {
+    auto it = leaf_of_buf.find(e->buf->ptr);
+    if (it != leaf_of_buf.end() && leaves[it->second]->shape == e->shape) return it->second;
+    if ((int)leaves.size() >= FZ_MAX_LEAVES) {
+      overflow = true;
+      return 0;
+    }
+    leaves.push_back(e);
+    leaf_of_buf[e->buf->ptr] = (int)leaves.size() - 1;
+    return (int)leaves.size() - 1;
+  }
+
+  // Returns an operand reference (>= 0 node, < 0 leaf).
+  int visit(const Expr *e) {
+    if (overflow) return 0;
+    if (e->kind == Expr::Leaf) return -1 - leaf_index(e);
+    auto it = node_of.find(e);
+    if (it != node_of.end()) return it->second;
+    int s0 = 0, s1 = 0;
+    if (e->kind == Expr::Unary || e->kind == Expr::Binary) s0 = visit(e->a.get());
+    if (e->kind == Expr::Binary) s1 = visit(e->b.get());
+    if (overflow) return 0;
+    if (prog.num_nodes >= FZ_MAX_NODES) {
+      overflow = true;
+      return 0;
+    }
+    fz_node &n = prog.nodes[prog.num_nodes];
+    n.kind = e->kind == Expr::Binary ? FZ_NODE_BINARY : e->kind == Expr::Unary ? FZ_NODE_UNARY : FZ_NODE_CONST;
+    n.op = e->op;
+    n.src0 = s0;
+    n.src1 = s1;
+    n.imm = e->imm;
+    node_of[e] = prog.num_nodes;
+    return prog.num_nodes++;
+  }
+};
+
+// Merge chained dims on the host (for ranks above FZ_MAX_DIMS), operands share `size`.
+int collapse(std::vector<int64_t> &size, std::vector<std::vector<int64_t>> &st) {
+  std::vector<int64_t> s2;
+  std::vector<std::vector<int64_t>> st2(st.size());
+  for (size_t d = 0; d < size.size(); ++d) {
+    if (size[d] == 1) continue;
+    if (!s2.empty()) {
+      bool chain = true;
+      for (size_t k = 0; k < st.size() && chain; ++k) chain = st2[k].back() == st[k][d] * size[d];
+      if (chain) {
+        s2.back() *= size[d];
+        for (size_t k = 0; k < st.size(); ++k) st2[k].back() = st[k][d];
+        continue;
+      }
+    }
+    s2.push_back(size[d]);
+    for (size_t k = 0; k < st.size(); ++k) st2[k].push_back(st[k][d]);
+  }
+  size.swap(s2);
+  st.swap(st2);
+  return (int)size.size();
+}
+}  // namespace
+
+static void launch_program(const Lowering &L, const std::vector<size_t> &out_shape,
+                           float *out_ptr) {
+  const int nops = 1 + (int)L.leaves.size();
+  std::vector<int64_t> size(out_shape.begin(), out_shape.end());
+  std::vector<std::vector<int64_t>> st(nops, std::vector<int64_t>(out_shape.size()));
+  operand_strides(out_shape, out_shape, st[0].data());
+  for (size_t k = 0; k < L.leaves.size(); ++k) operand_strides(L.leaves[k]->shape, out_shape, st[k + 1].data());
+  if ((int)size.size() > FZ_MAX_DIMS) collapse(size, st);
+  FB_CHECK((int)size.size() <= FZ_MAX_DIMS, "fused elementwise: too many non-mergeable dims");
+  fz_ewise_plan plan{};
+  plan.ndim = (int32_t)size.size();
+  plan.num_operands = nops;
+  for (int d = 0; d < plan.ndim; ++d) {
+    plan.size[d] = size[d];
+    for (int k = 0; k < nops; ++k) plan.stride_bytes[k][d] = st[k][d] * 4;
+  }
+  std::vector<const float *> leaf_ptrs;
+  for (auto *l : L.leaves) leaf_ptrs.push_back(l->buf->ptr);
+  float *outs[1] = {out_ptr};
+  fz_check(fz_fused_launch(&L.prog, &plan, outs, leaf_ptrs.data(), nullptr), "fz_fused_launch");
+  ++g_fused_launches;
+}
+
+// A single binary op over two leaves runs on the ahead-of-time kernels.
+static bool try_single_op(Expr *e, float *out_ptr) {
+  if (e->kind == Expr::Binary && e->a->kind == Expr::Leaf && e->b->kind == Expr::Leaf) {
+    const auto &os = e->shape;
+    if (e->a->shape == os && e->b->shape == os) {
+      fz_check(fz_ewise_binary_contig(e->op, (int64_t)e->numel(), out_ptr, e->a->buf->ptr,
+                                      e->b->buf->ptr, nullptr), "fz_ewise_binary_contig");
+      return true;
+    }
+    if (os.size() <= FZ_MAX_DIMS) {
+      fz_ewise_plan plan{};
+      plan.ndim = (int32_t)os.size();
+      plan.num_operands = 3;
+      int64_t st[3][FZ_MAX_DIMS];
+      operand_strides(os, os, st[0]);
+      operand_strides(e->a->shape, os, st[1]);
+      operand_strides(e->b->shape, os, st[2]);
+      for (int d = 0; d < plan.ndim; ++d) {
+        plan.size[d] = os[d];
+        for (int k = 0; k < 3; ++k) plan.stride_bytes[k][d] = st[k][d] * 4;
+      }
+      fz_check(fz_ewise_binary(e->op, &plan, out_ptr, e->a->buf->ptr, e->b->buf->ptr, nullptr),
+               "fz_ewise_binary");
+      return true;
+    }
+  }
+  if (e->kind == Expr::Unary && e->a->kind == Expr::Leaf && e->a->shape == e->shape) {
+    fz_ewise_plan plan{};
+    plan.ndim = 1;
+    plan.num_operands = 2;
+    plan.size[0] = (int64_t)e->numel();
+    plan.stride_bytes[0][0] = plan.stride_bytes[1][0] = 4;
+    fz_check(fz_ewise_unary(e->op, &plan, out_ptr, e->a->buf->ptr, nullptr), "fz_ewise_unary");
+    return true;
+  }
+  if (e->kind == Expr::Const) {
+    fz_check(fz_fill_f32(out_ptr, e->imm, (int64_t)e->numel(), nullptr), "fz_fill_f32");
+    return true;
+  }
+  return false;
+}
+
+void materialize(const ExprPtr &ep) {
+  Expr *e = ep.get();
+  if (e->kind == Expr::Leaf) return;
+  auto out = std::make_shared<DeviceBuffer>(e->numel());
+  if (e->numel() > 0 && !try_single_op(e, out->ptr)) {
+    Lowering L;
+    int root = L.visit(e);
+    if (L.overflow) {
+      // too large for one program: materialise the operands first, then retry
+      if (e->a) materialize(e->a);
+      if (e->b) materialize(e->b);
+      materialize(ep);
+      return;
+    }
+    L.prog.num_leaves = (int32_t)L.leaves.size();
+    L.prog.num_outputs = 1;
+    L.prog.out_node[0] = root;
+    launch_program(L, e->shape, out->ptr);
+  }
+  e->kind = Expr::Leaf;
+  e->buf = std::move(out);
+  e->a.reset();
+  e->b.reset();
+  e->nodes_ub = 0;
+  e->leaves_ub = 1;
+}
+
+static ExprPtr make_op(Expr::Kind kind, int op, ExprPtr a, ExprPtr b, std::vector<size_t> shape) {
+  // size policy: keep every pending program within the fused-kernel limits
+  auto nodes = [&]() { return 1 + a->nodes_ub + (b ? b->nodes_ub : 0); };
+  auto leaves = [&]() { return a->leaves_ub + (b ? b->leaves_ub : 0); };
+  while (nodes() > kNodeLimit || leaves() > kLeafLimit) {
+    ExprPtr &big = (!b || a->nodes_ub + a->leaves_ub >= b->nodes_ub + b->leaves_ub) ? a : b;
+    FB_CHECK(big->kind != Expr::Leaf, "fusion policy: cannot shrink program");
+    materialize(big);
+  }
+  auto e = std::make_shared<Expr>();
+  e->kind = kind;
+  e->op = op;
+  e->a = std::move(a);
+  e->b = std::move(b);
+  e->shape = std::move(shape);
+  e->nodes_ub = nodes();
+  e->leaves_ub = leaves();
+  if (!g_fusion) materialize(e);
+  return e;
+}
+
+// ---------------------------------------------------------------- RawTensor
+void RawTensor::set_contiguous_strides() {
+  strides_.assign(shape_.size(), 0);
+  int64_t r = 1;
+  for (long i = (long)shape_.size() - 1; i >= 0; --i) {
+    strides_[i] = r;
+    r *= (int64_t)shape_[i];
+  }
+}
+
+RawTensor::RawTensor(std::vector<size_t> shape, const float *data, DType dtype, Device device)
+    : shape_(std::move(shape)), dtype_(dtype), device_(device) {
+  FB_CHECK(!shape_.empty(), "Tensor: empty shape");
+  bind_device(device_);
+  set_contiguous_strides();
+  size_t n = 1;
+  for (auto s : shape_) n *= s;
+  auto buf = std::make_shared<DeviceBuffer>(n);
+  if (n) fz_check(fz_memcpy_h2d(buf->ptr, data, n * sizeof(float), nullptr), "fz_memcpy_h2d");
+  storage_ = std::make_shared<Storage>(make_leaf(std::move(buf), shape_));
+}
+
+RawTensor::RawTensor(std::vector<size_t> shape, const std::vector<float> &data, DType dtype,
+                     Device device)
+    : RawTensor(shape, data.data(), dtype, device) {
+  size_t n = 1;
+  for (auto s : shape_) n *= s;
+  FB_CHECK(data.size() == n, "Tensor: data size != product(shape)");
+}
+
+RawTensor::RawTensor(std::vector<size_t> shape, DType dtype, Device device)
+    : shape_(std::move(shape)), dtype_(dtype), device_(device) {
+  FB_CHECK(!shape_.empty(), "Tensor: empty shape");
+  bind_device(device_);
+  set_contiguous_strides();
+  storage_ = std::make_shared<Storage>(make_const(0.0f, shape_));
+}
+
+RawTensor::RawTensor(ExprPtr e, DType dtype, Device device)
+    : shape_(e->shape), dtype_(dtype), device_(device) {
+  set_contiguous_strides();
+  storage_ = std::make_shared<Storage>(std::move(e));
+}
+
+RawTensor RawTensor::full(const std::vector<size_t> &shape, float value, DType dtype, Device device) {
+  FB_CHECK(!shape.empty(), "Tensor: empty shape");
+  bind_device(device);
+  return RawTensor(make_const(value, shape), dtype, device);
+}
+
+float *RawTensor::data() const {
+  FB_CHECK(storage_, "uninitialised tensor");
+  return storage_->data();
+}
+
+void RawTensor::to_host(float *dst) const {
+  size_t n = size();
+  if (!n) return;
+  float *p = data();
+  fz_check(fz_memcpy_d2h(dst, p, n * sizeof(float), nullptr), "fz_memcpy_d2h");
+}
+
+std::vector<float> RawTensor::to_host() const {
+  std::vector<float> v(size());
+  to_host(v.data());
+  return v;
+}
+
+void RawTensor::set_values(const float *src, size_t n) {
+  FB_CHECK(storage_, "uninitialised tensor");
+  auto buf = std::make_shared<DeviceBuffer>(n);
+  if (n) fz_check(fz_memcpy_h2d(buf->ptr, src, n * sizeof(float), nullptr), "fz_memcpy_h2d");
+  storage_->expr = make_leaf(std::move(buf), shape_);
+}
+
+void RawTensor::clear() {
+  if (!storage_ || storage_->numel() == 0) return;
+  storage_->expr = make_const(0.0f, storage_->expr->shape);
+}
+
+void RawTensor::assign(const RawTensor &other) {
+  if (!storage_) {
+    *this = other;
+    return;
+  }
+  storage_->expr = other.storage_->expr;
+}
+
+RawTensor &RawTensor::operator-=(const RawTensor &other) {
+  math::sub_inplace(*this, other);
+  return *this;
+}
+
+RawTensor RawTensor::operator+(const RawTensor &o) const { return math::binary(FZ_ADD, *this, o); }
+RawTensor RawTensor::operator-(const RawTensor &o) const { return math::binary(FZ_SUB, *this, o); }
+RawTensor RawTensor::operator*(const RawTensor &o) const { return math::binary(FZ_MUL, *this, o); }
+RawTensor RawTensor::operator/(const RawTensor &o) const { return math::binary(FZ_DIV, *this, o); }
+RawTensor RawTensor::operator>(const RawTensor &o) const { return math::binary(FZ_GT, *this, o); }
+RawTensor RawTensor::operator>=(const RawTensor &o) const { return math::binary(FZ_GT, *this, o); }
+RawTensor RawTensor::maximum(const RawTensor &o) const { return math::binary(FZ_MAXIMUM, *this, o); }
+RawTensor RawTensor::pow(const RawTensor &o) const { return math::binary(FZ_POW, *this, o); }
+// Scalar overloads build a [1] tensor (RawTensor.hpp:30-34, 159-185).
+RawTensor RawTensor::operator+(float s) const { return *this + scalar(s, dtype_, device_); }
+RawTensor RawTensor::operator-(float s) const { return *this - scalar(s, dtype_, device_); }
+RawTensor RawTensor::operator*(float s) const { return *this * scalar(s, dtype_, device_); }
+RawTensor RawTensor::operator/(float s) const { return *this / scalar(s, dtype_, device_); }
+RawTensor RawTensor::operator>=(float s) const { return *this >= scalar(s, dtype_, device_); }
+RawTensor RawTensor::maximum(float s) const { return maximum(scalar(s, dtype_, device_)); }
+RawTensor RawTensor::pow(float s) const { return pow(scalar(s, dtype_, device_)); }
+RawTensor RawTensor::sqrt() const { return math::unary(FZ_SQRT, *this); }
+RawTensor RawTensor::log() const { return math::unary(FZ_LOG, *this); }
+RawTensor RawTensor::exp() const { return math::unary(FZ_EXP, *this); }
+RawTensor RawTensor::sum(size_t axis, bool keepdim) const { return math::reduce(FZ_RSUM, *this, axis, keepdim); }
+RawTensor RawTensor::mean(size_t axis, bool keepdim) const { return math::reduce(FZ_RMEAN, *this, axis, keepdim); }
+RawTensor RawTensor::max(size_t axis, bool keepdim) const { return math::reduce(FZ_RMAX, *this, axis, keepdim); }
+RawTensor RawTensor::matmul(const RawTensor &o) const { return math::matmul(*this, o); }
+RawTensor RawTensor::swapaxes(int a1, int a2) const { return math::swapaxes(*this, a1, a2); }
+
+std::string RawTensor::shape_str() const {
+  std::ostringstream os;
+  os << '(';
+  for (size_t i = 0; i < shape_.size(); ++i) os << shape_[i] << (i + 1 < shape_.size() ? "," : "");
+  os << ')';
+  return os.str();
+}
+
+// operator<< format of the reference (RawTensor.hpp:243-262).
+std::string RawTensor::repr() const {
+  std::ostringstream os;
+  if (!storage_) return "Tensor(unsupported storage type)";
+  auto v = to_host();
+  os << "Tensor(";
+  for (size_t i = 0; i < v.size(); ++i) {
+    os << v[i];
+    if (i + 1 < v.size()) os << ", ";
+  }
+  os << ")" << std::endl;
+  return os.str();
+}
+
+RawTensor zeros_like(const RawTensor &t) { return RawTensor::full(t.shape(), 0.0f, DType::FLOAT32, t.device()); }
+RawTensor ones_like(const RawTensor &t) { return RawTensor::full(t.shape(), 1.0f, DType::FLOAT32, t.device()); }
+
+// ---------------------------------------------------------------- ops
+namespace math {
+
+static void check_pair(const RawTensor &x, const RawTensor &y) {
+  FB_CHECK(x.is_initialised(), "binary ewise: LHS uninitialised");
+  FB_CHECK(y.is_initialised(), "binary ewise: RHS uninitialised");
+  FB_CHECK(x.dtype() == y.dtype(), "dtypes do not match!");
+  FB_CHECK(x.device() == y.device(), "devices do not match!");
+}
+
+// fusion::math::{add,sub,mul,div,pow,maximum,greater} (ops/Ewise.hpp:17-55,
+// ops/Comparison.hpp:17-40). Equal shapes take the contiguous fast path
+// (PlanMeta.hpp:100-108); otherwise the broadcast walk, whose innermost loop
+// hands the operands to the scalar kernel exchanged when only the left operand
+// has stride 0 in the last dim (SimdTraits.hpp:30-31 and peers), so op(b, a).
+RawTensor binary(int op, const RawTensor &x, const RawTensor &y) {
+  check_pair(x, y);
+  const bool same = x.shape() == y.shape();
+  std::vector<size_t> out = same ? x.shape() : broadcast_shape(x.shape(), y.shape());
+  const bool swap = !same && x.shape().back() == 1 && out.back() > 1;
+  ExprPtr a = x.expr(), b = y.expr();
+  if (swap) std::swap(a, b);
+  return RawTensor(make_op(Expr::Binary, op, std::move(a), std::move(b), out), x.dtype(), x.device());
+}
+
+RawTensor unary(int op, const RawTensor &x) {
+  FB_CHECK(x.is_initialised(), "unary ewise: uninitialised tensor");
+  return RawTensor(make_op(Expr::Unary, op, x.expr(), nullptr, x.shape()), x.dtype(), x.device());
+}
+
+// fusion::math::sum/mean (ops/Reduce.hpp:18-36) via make_reduction_meta
+// (PlanMeta.hpp:148-182): axis == (size_t)-1 with keepdim == false is the global
+// reduction to shape [1]; otherwise one axis, removed or kept as 1.
+RawTensor reduce(int op, const RawTensor &x, size_t axis, bool keepdim) {
+  FB_CHECK(x.is_initialised(), "reduction: uninitialised tensor");
+  const auto &s = x.shape();
+  std::vector<size_t> oshape;
+  int64_t outer = 1, len, inner = 1;
+  if (axis == kGlobalReduceAxis && !keepdim) {
+    oshape = {1};
+    len = (int64_t)x.size();
+  } else {
+    if (axis >= s.size()) throw std::runtime_error("axis out of range");
+    for (size_t d = 0; d < axis; ++d) outer *= (int64_t)s[d];
+    len = (int64_t)s[axis];
+    for (size_t d = axis + 1; d < s.size(); ++d) inner *= (int64_t)s[d];
+    for (size_t d = 0; d < s.size(); ++d) {
+      if (d == axis) {
+        if (keepdim) oshape.push_back(1);
+      } else {
+        oshape.push_back(s[d]);
+      }
+    }
+    if (oshape.empty()) oshape = {1};
+  }
+  const float *in = x.data();
+  size_t n = 1;
+  for (auto v : oshape) n *= v;
+  auto buf = std::make_shared<DeviceBuffer>(n);
+  fz_check(fz_reduce(op, buf->ptr, in, outer, len, inner, nullptr), "fz_reduce");
+  return RawTensor(make_leaf(std::move(buf), oshape), x.dtype(), x.device());
+}
+
+RawTensor matmul(const RawTensor &A, const RawTensor &B, bool transA, bool transB) {
+  FB_CHECK(A.is_initialised(), "matmul: A uninitialised");
+  FB_CHECK(B.is_initialised(), "matmul: B uninitialised");
+  FB_CHECK(A.dtype() == B.dtype(), "matmul: dtype mismatch");
+  FB_CHECK(A.device() == B.device(), "matmul: device mismatch");
+  const auto &as = A.shape(), &bs = B.shape();
+  if (as.size() < 2 || bs.size() < 2) throw std::runtime_error("matmul: expected rank >= 2");
+  const size_t ar = as.size(), br = bs.size();
+  const size_t M = transA ? as[ar - 1] : as[ar - 2], Ka = transA ? as[ar - 2] : as[ar - 1];
+  const size_t Kb = transB ? bs[br - 1] : bs[br - 2], N = transB ? bs[br - 2] : bs[br - 1];
+  if (Ka != Kb) throw std::runtime_error("matmul: inner dimension mismatch");
+  if (ar != br) throw std::runtime_error("matmul: batch rank mismatch (implement broadcasting/padding)");
+  std::vector<size_t> oshape;
+  size_t batch = 1, ba = 1, bb = 1;
+  for (size_t d = 0; d + 2 < ar; ++d) {
+    size_t o = as[d] == bs[d] ? as[d] : (as[d] == 1 ? bs[d] : (bs[d] == 1 ? as[d] : 0));
+    if (o == 0) throw std::runtime_error("broadcast: dimension mismatch");
+    oshape.push_back(o);
+    batch *= o;
+    ba *= as[d];
+    bb *= bs[d];
+  }
+  FB_CHECK((ba == batch || ba == 1) && (bb == batch || bb == 1),
+           "matmul: batch dims broadcast only as a whole");
+  oshape.push_back(M);
+  oshape.push_back(N);
+  const float *pa = A.data(), *pb = B.data();
+  size_t n = batch * M * N;
+  auto buf = std::make_shared<DeviceBuffer>(n);
+  const int64_t lda = (int64_t)as[ar - 1], ldb = (int64_t)bs[br - 1];
+  const int64_t sA = ba == 1 ? 0 : (int64_t)(as[ar - 1] * as[ar - 2]);
+  const int64_t sB = bb == 1 ? 0 : (int64_t)(bs[br - 1] * bs[br - 2]);
+  fz_check(fz_gemm_f32((int64_t)batch, (int64_t)M, (int64_t)N, (int64_t)Ka, pa, lda, sA, transA,
+                       pb, ldb, sB, transB, buf->ptr, (int64_t)N, (int64_t)(M * N), nullptr),
+           "fz_gemm_f32");
+  return RawTensor(make_leaf(std::move(buf), oshape), A.dtype(), A.device());
+}
+
+// fusion::math::linalg::swapaxes (ops/Linalg.hpp:109-128): a materialised copy;
+// rank < 2 or equal axes give an unchanged copy.
+RawTensor swapaxes(const RawTensor &x, int a1, int a2) {
+  FB_CHECK(x.is_initialised(), "swapaxes: uninitialised tensor");
+  const int nd = (int)x.rank();
+  if (nd < 2) return RawTensor(x.expr(), x.dtype(), x.device());
+  auto norm = [&](int a) {
+    int r = a < 0 ? a + nd : a;
+    if (r < 0 || r >= nd) throw std::out_of_range("axis out of range");
+    return r;
+  };
+  const int n1 = norm(a1), n2 = norm(a2);
+  if (n1 == n2) return RawTensor(x.expr(), x.dtype(), x.device());
+  std::vector<size_t> oshape = x.shape();
+  std::swap(oshape[n1], oshape[n2]);
+  std::vector<int64_t> shp(x.shape().begin(), x.shape().end());
+  const float *in = x.data();
+  auto buf = std::make_shared<DeviceBuffer>(x.size());
+  fz_check(fz_swapaxes(buf->ptr, in, shp.data(), nd, n1, n2, nullptr), "fz_swapaxes");
+  return RawTensor(make_leaf(std::move(buf), oshape), x.dtype(), x.device());
+}
+
+// fusion::math::sub_inplace (ops/Ewise.hpp:69-83): x[i] -= y[i] for i < x.size,
+// reading y flat whatever its shape. Implemented by rebinding x's storage to the
+// new value, so pending readers of the old value are unaffected.
+void sub_inplace(RawTensor &x, const RawTensor &y) {
+  FB_CHECK(x.is_initialised() && y.is_initialised(), "sub_inplace: uninitialised tensor");
+  if (x.shape() == y.shape()) {
+    x.storage()->expr = make_op(Expr::Binary, FZ_SUB, x.expr(), y.expr(), x.shape());
+    return;
+  }
+  const size_t n = x.size();
+  FB_CHECK(y.size() >= n, "sub_inplace: right-hand side has fewer elements than the tensor");
+  const float *px = x.data();
+  const float *py = y.data();
+  auto buf = std::make_shared<DeviceBuffer>(n);
+  fz_check(fz_ewise_binary_contig(FZ_SUB, (int64_t)n, buf->ptr, px, py, nullptr),
+           "fz_ewise_binary_contig");
+  x.storage()->expr = make_leaf(std::move(buf), x.shape());
+}
+
+}  // namespace math
+}  // namespace fusion_b200

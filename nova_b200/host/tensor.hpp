@@ -1,0 +1,196 @@
+// Fusion's tensor value type and op API over B200 device storage.
+//
+// RawTensor keeps the reference's shape/strides/dtype/device value semantics
+// (fusion/src/Fusion/core/RawTensor.hpp:36-318): copies are shallow and share one
+// Storage, so in-place writes through any copy are seen by all of them.
+//
+// Storage holds an Expr, the node of the fusion IR:
+//   * Leaf  -- a materialised device buffer (HBM, from the stream-ordered pool)
+//   * Const -- a value broadcast over a shape (zeros_like, ones_like, scalars)
+//   * Unary / Binary -- a pending elementwise op over other Exprs
+// Elementwise ops build pending nodes instead of running; a node is lowered to one
+// fused sm_100a kernel when its value is first needed (a GEMM, reduction, transpose,
+// host read-back, or the size limit of a fused program). Lowering turns the node
+// into a Leaf in place, so every holder sees the result and nothing is computed
+// twice. In-place writes (`-=`, set_values, clear) rebind the Storage to a new Expr
+// and leave the old one to pending readers, which keeps program order without
+// copies.
+#pragma once
+
+#include <cstdint>
+#include <memory>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "fusion_b200.h"
+
+namespace fusion_b200 {
+
+// ---- error convention: FUSION_CHECK-style std::runtime_error ---------------
+[[noreturn]] void throw_check(const char *file, int line, const std::string &msg);
+void fz_check(int rc, const char *what);
+
+#define FB_CHECK(cond, msg)                                                          \
+  do {                                                                                \
+    if (!(cond)) ::fusion_b200::throw_check(__FILE__, __LINE__, (msg));               \
+  } while (0)
+
+// ---- device / dtype (fusion/src/Fusion/device/Device.h, core/Dtype.h) -------
+enum class DeviceType : int { CPU = 0, CUDA = 1, METAL = 2 };
+enum class DType : int { FLOAT32 = 0, FLOAT64 = 1, INT32 = 2, INT64 = 3, BOOL = 4 };
+
+// Device tag. Every tensor of this backend lives in HBM of a CUDA device; a CPU
+// tag (Nova's default) places it on the calling thread's current CUDA device.
+// Index rules: CPU admits idx <= 0 as the reference does; CUDA admits -1 (the
+// current device) or 0 .. device_count-1.
+struct Device {
+  DeviceType type{DeviceType::CPU};
+  int idx{-1};
+  Device() = default;
+  Device(DeviceType t, int i = -1);
+  bool operator==(const Device &o) const { return type == o.type && idx == o.idx; }
+  bool is_cpu() const { return type == DeviceType::CPU; }
+  bool is_cuda() const { return type == DeviceType::CUDA; }
+  int cuda_index() const;  // the CUDA ordinal the data lives on
+};
+
+size_t dtype_size(DType d);
+
+// ---- device memory -----------------------------------------------------------
+struct DeviceBuffer {
+  float *ptr = nullptr;
+  size_t numel = 0;
+  int device = 0;
+  explicit DeviceBuffer(size_t n);
+  ~DeviceBuffer();
+  DeviceBuffer(const DeviceBuffer &) = delete;
+  DeviceBuffer &operator=(const DeviceBuffer &) = delete;
+};
+
+// ---- fusion IR node --------------------------------------------------------------
+struct Expr {
+  enum Kind { Leaf, Const, Unary, Binary } kind;
+  int op = 0;  // fz_binop / fz_unop
+  std::vector<size_t> shape;
+  std::shared_ptr<Expr> a, b;
+  std::shared_ptr<DeviceBuffer> buf;  // Leaf
+  float imm = 0.0f;                   // Const
+  int nodes_ub = 1;                   // upper bounds used by the fusion size policy
+  int leaves_ub = 0;
+  size_t numel() const;
+};
+using ExprPtr = std::shared_ptr<Expr>;
+
+struct Storage {
+  ExprPtr expr;
+  explicit Storage(ExprPtr e) : expr(std::move(e)) {}
+  // Materialise (if pending) and return the device pointer.
+  float *data();
+  size_t numel() const { return expr->numel(); }
+};
+
+// Fusion policy switches (fusion enabled by default).
+void set_fusion_enabled(bool on);
+bool fusion_enabled();
+// Lower a pending node to one fused kernel (no-op for a Leaf).
+void materialize(const ExprPtr &e);
+int64_t fused_launches();
+
+class RawTensor {
+ public:
+  RawTensor() = default;
+  // From host data (copied to the device).
+  RawTensor(std::vector<size_t> shape, const float *data, DType dtype, Device device);
+  RawTensor(std::vector<size_t> shape, const std::vector<float> &data, DType dtype, Device device);
+  // Zero-initialised.
+  RawTensor(std::vector<size_t> shape, DType dtype, Device device);
+  // From an Expr (internal).
+  RawTensor(ExprPtr e, DType dtype, Device device);
+
+  static RawTensor full(const std::vector<size_t> &shape, float value, DType dtype, Device device);
+  static RawTensor scalar(float v, DType dtype, Device device) { return full({1}, v, dtype, device); }
+
+  DType dtype() const { return dtype_; }
+  size_t dtype_size() const { return fusion_b200::dtype_size(dtype_); }
+  size_t rank() const { return shape_.size(); }
+  size_t ndims() const { return shape_.size(); }
+  const std::vector<size_t> &shape() const { return shape_; }
+  std::vector<int64_t> strides() const { return strides_; }
+  Device device() const { return device_; }
+  bool is_contiguous() const { return true; }
+  bool is_initialised() const { return storage_ != nullptr; }
+  bool empty() const { return !storage_ || storage_->numel() == 0; }
+  size_t size() const { return storage_ ? storage_->numel() : 0; }
+  size_t flat_size() const { return size(); }
+  const std::shared_ptr<Storage> &storage() const { return storage_; }
+  ExprPtr expr() const { return storage_ ? storage_->expr : nullptr; }
+  bool pending() const { return storage_ && storage_->expr->kind != Expr::Leaf; }
+
+  // Device pointer (materialises a pending value).
+  float *data() const;
+  // Host copy of the values.
+  std::vector<float> to_host() const;
+  void to_host(float *dst) const;
+
+  // In-place writes, visible to every shallow copy.
+  void set_values(const float *src, size_t n);
+  void clear();                           // zero (RawTensor.hpp:140-149)
+  void assign(const RawTensor &other);    // RawTensor.hpp:151-157
+  RawTensor &operator-=(const RawTensor &other);  // sub_inplace (ops/Ewise.hpp:69-83)
+
+  RawTensor operator+(const RawTensor &o) const;
+  RawTensor operator-(const RawTensor &o) const;
+  RawTensor operator*(const RawTensor &o) const;
+  RawTensor operator/(const RawTensor &o) const;
+  RawTensor operator>(const RawTensor &o) const;
+  RawTensor operator>=(const RawTensor &o) const;  // the reference calls greater (RawTensor.hpp:207-209)
+  RawTensor maximum(const RawTensor &o) const;
+  RawTensor pow(const RawTensor &o) const;
+  RawTensor operator+(float s) const;
+  RawTensor operator-(float s) const;
+  RawTensor operator*(float s) const;
+  RawTensor operator/(float s) const;
+  RawTensor operator>=(float s) const;
+  RawTensor maximum(float s) const;
+  RawTensor pow(float s) const;
+  RawTensor sqrt() const;
+  RawTensor log() const;
+  RawTensor exp() const;
+  RawTensor sum(size_t axis, bool keepdim) const;
+  RawTensor mean(size_t axis, bool keepdim) const;
+  RawTensor max(size_t axis, bool keepdim) const;
+  RawTensor matmul(const RawTensor &o) const;
+  RawTensor swapaxes(int a1, int a2) const;
+
+  std::string repr() const;
+  std::string shape_str() const;
+
+ private:
+  std::shared_ptr<Storage> storage_;
+  std::vector<size_t> shape_;
+  std::vector<int64_t> strides_;
+  DType dtype_{DType::FLOAT32};
+  Device device_{};
+  void set_contiguous_strides();
+};
+
+constexpr size_t kGlobalReduceAxis = static_cast<size_t>(-1);
+
+namespace math {
+RawTensor binary(int op, const RawTensor &x, const RawTensor &y);
+RawTensor unary(int op, const RawTensor &x);
+RawTensor reduce(int op, const RawTensor &x, size_t axis, bool keepdim);
+// C = op(A) @ op(B) over the last two dims, batch dims equal (ops/Linalg.hpp:76-107).
+RawTensor matmul(const RawTensor &A, const RawTensor &B, bool transA = false, bool transB = false);
+RawTensor swapaxes(const RawTensor &x, int a1, int a2);
+void sub_inplace(RawTensor &x, const RawTensor &y);
+}  // namespace math
+
+RawTensor zeros_like(const RawTensor &t);
+RawTensor ones_like(const RawTensor &t);
+
+// Make the calling thread's CUDA device current for `d` and return its ordinal.
+int bind_device(const Device &d);
+
+}  // namespace fusion_b200
