@@ -227,8 +227,13 @@ int fz_comm_unique_id(unsigned char id[FZ_UNIQUE_ID_BYTES]);
 /* Join a communicator of `world` ranks on the current device. */
 int fz_comm_init(void **comm, int world, int rank,
                  const unsigned char id[FZ_UNIQUE_ID_BYTES]);
-/* In-place fp32 all-reduce: sum, then multiply by `scale` (1/world for a mean). */
-int fz_comm_allreduce(void *comm, float *buf, int64_t count, float scale, void *stream);
+/* fp32 all-reduce of `count` floats from `send` into `recv` (may be the same
+ * buffer): sum over ranks, then multiply by `scale` (1/world for a mean). */
+int fz_comm_allreduce(void *comm, const float *send, float *recv, int64_t count, float scale,
+                      void *stream);
+/* Start / end a group of collectives issued back to back (one NCCL launch). */
+int fz_comm_group_start(void);
+int fz_comm_group_end(void);
 int fz_comm_broadcast(void *comm, float *buf, int64_t count, int root, void *stream);
 /* Wait for `stream` with a host-side deadline; on expiry abort the communicator
  * and return FZ_ERR_TIMEOUT instead of blocking for ever. */

@@ -99,7 +99,7 @@ def lib() -> C.CDLL:
         L.fz_host_alloc.argtypes = [C.POINTER(C.c_void_p), C.c_size_t]
         L.fz_host_free.argtypes = [vp]
         L.fz_comm_init.argtypes = [C.POINTER(C.c_void_p), C.c_int, C.c_int, C.c_char_p]
-        L.fz_comm_allreduce.argtypes = [vp, vp, i64, f, vp]
+        L.fz_comm_allreduce.argtypes = [vp, vp, vp, i64, f, vp]
         L.fz_comm_broadcast.argtypes = [vp, vp, i64, C.c_int, vp]
         L.fz_comm_wait.argtypes = [vp, vp, C.c_double]
         L.fz_comm_destroy.argtypes = [vp]

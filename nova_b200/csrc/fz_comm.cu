@@ -72,22 +72,33 @@ int fz_comm_init(void **comm, int world, int rank, const unsigned char id[FZ_UNI
   return FZ_OK;
 }
 
-int fz_comm_allreduce(void *comm, float *buf, int64_t count, float scale, void *stream) {
+int fz_comm_allreduce(void *comm, const float *send, float *recv, int64_t count, float scale,
+                      void *stream) {
   FZ_REQUIRE(comm, "fz_comm_allreduce: null communicator");
   if (count == 0) return FZ_OK;
-  FZ_REQUIRE(buf && count > 0, "fz_comm_allreduce: bad buffer");
+  FZ_REQUIRE(send && recv && count > 0, "fz_comm_allreduce: bad buffer");
   Comm *c = static_cast<Comm *>(comm);
   FZ_REQUIRE(!c->aborted, "fz_comm_allreduce: communicator was aborted");
   cudaStream_t s = fz::resolve(stream);
-  ncclResult_t r = ncclAllReduce(buf, buf, (size_t)count, ncclFloat, ncclSum, c->comm, s);
+  ncclResult_t r = ncclAllReduce(send, recv, (size_t)count, ncclFloat, ncclSum, c->comm, s);
   if (r != ncclSuccess) return nccl_fail(r, "ncclAllReduce");
   if (scale != 1.0f) {
-    FZ_REQUIRE(((uintptr_t)buf & 15) == 0, "fz_comm_allreduce: buffer must be 16-byte aligned");
+    FZ_REQUIRE(((uintptr_t)recv & 15) == 0, "fz_comm_allreduce: buffer must be 16-byte aligned");
     unsigned grid = fz::grid_for((count + 3) / 4, 256 * 2, 8);
-    scale_kernel<<<grid, 256, 0, s>>>(buf, scale, count);
+    scale_kernel<<<grid, 256, 0, s>>>(recv, scale, count);
     FZ_CHECK_LAUNCH();
   }
   return FZ_OK;
+}
+
+int fz_comm_group_start(void) {
+  ncclResult_t r = ncclGroupStart();
+  return r == ncclSuccess ? FZ_OK : nccl_fail(r, "ncclGroupStart");
+}
+
+int fz_comm_group_end(void) {
+  ncclResult_t r = ncclGroupEnd();
+  return r == ncclSuccess ? FZ_OK : nccl_fail(r, "ncclGroupEnd");
 }
 
 int fz_comm_broadcast(void *comm, float *buf, int64_t count, int root, void *stream) {

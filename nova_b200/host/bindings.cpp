@@ -62,18 +62,18 @@ struct GradTape {
 PYBIND11_MODULE(fusion, m) {
   m.doc() = "Fusion Tensor module exposing Tensor<float> (for composition) on the B200 backend";
 
-  py::class_<Device>(m, "CppDevice")
+  py::class_<Device>(m, "CppDevice", py::module_local())
       .def(py::init([](DeviceType t, int idx) { return Device(t, idx); }), py::arg("type"),
            py::arg("index") = -1)
       .def_property_readonly("type", [](const Device &d) { return d.type; })
       .def_property_readonly("index", [](const Device &d) { return d.idx; });
 
-  py::enum_<DeviceType>(m, "CppDeviceType")
+  py::enum_<DeviceType>(m, "CppDeviceType", py::module_local())
       .value("CPU", DeviceType::CPU)
       .value("CUDA", DeviceType::CUDA)
       .value("METAL", DeviceType::METAL);
 
-  py::enum_<DType>(m, "CppDType")
+  py::enum_<DType>(m, "CppDType", py::module_local())
       .value("FLOAT32", DType::FLOAT32)
       .value("FLOAT64", DType::FLOAT64)
       .value("INT32", DType::INT32)
@@ -81,7 +81,7 @@ PYBIND11_MODULE(fusion, m) {
       .value("BOOL", DType::BOOL);
 
   using T = ADTensor;
-  py::class_<T>(m, "Tensor")
+  py::class_<T>(m, "Tensor", py::module_local())
       .def(py::init([](const std::vector<size_t> &shape, DType dt, Device dev, bool rg) {
              return T(RawTensor(shape, dt, dev), rg);
            }),
@@ -190,12 +190,12 @@ PYBIND11_MODULE(fusion, m) {
   fac.def("ones_like", [](const T &t) { return T(ones_like(t.raw()), t.requires_grad()); },
           py::arg("other"));
 
-  py::class_<Random>(m, "Random")
+  py::class_<Random>(m, "Random", py::module_local())
       .def(py::init<uint32_t>(), py::arg("seed") = std::random_device{}())
       .def("uniform_cpp", &Random::uniform, py::arg("shape"), py::arg("min"), py::arg("max"),
            py::arg("device"));
 
-  py::class_<GradTape>(m, "grad_tape")
+  py::class_<GradTape>(m, "grad_tape", py::module_local())
       .def(py::init<>())
       .def(
           "__enter__",

@@ -327,11 +327,11 @@ static ExprPtr make_op(Expr::Kind kind, int op, ExprPtr a, ExprPtr b, std::vecto
   auto e = std::make_shared<Expr>();
   e->kind = kind;
   e->op = op;
+  e->nodes_ub = nodes();
+  e->leaves_ub = leaves();
   e->a = std::move(a);
   e->b = std::move(b);
   e->shape = std::move(shape);
-  e->nodes_ub = nodes();
-  e->leaves_ub = leaves();
   if (!g_fusion) materialize(e);
   return e;
 }

@@ -1,0 +1,229 @@
+// Host-memory test double of the C ABI in include/fusion_b200.h.
+//
+// TEST INFRASTRUCTURE ONLY. It lets the CPU test suite run the C++ host layer
+// (nova_b200/host: the fusion-IR lowering, the autodiff engine, Fusion's op
+// semantics and quirks) without a GPU: tests/hostfake/build_fake.py links a copy
+// of the pybind module against this library in tests/hostfake/_build/. The
+// product library nova_b200/libfusion_b200.so never contains or loads it, and it
+// is never a fallback: it exists so host-logic bugs surface on CPU before a GPU
+// run. "Device" pointers here are host pointers; every op is a scalar loop with
+// the IEEE fp32 semantics the sm_100a kernels implement.
+#include <cmath>
+#include <cstdlib>
+#include <cstring>
+#include <set>
+#include <string>
+#include <vector>
+
+#include "fusion_b200.h"
+
+namespace {
+thread_local std::string g_err;
+int64_t g_launches = 0;
+std::set<std::string> g_programs;
+
+int fail(int code, const std::string &m) {
+  g_err = m;
+  return code;
+}
+
+float binop(int op, float a, float b) {
+  switch (op) {
+    case FZ_ADD: return a + b;
+    case FZ_SUB: return a - b;
+    case FZ_MUL: return a * b;
+    case FZ_DIV: return a / b;
+    case FZ_POW: return b == 2.0f ? a * a : std::pow(a, b);
+    case FZ_MAXIMUM: return a > b ? a : b;
+    case FZ_GT: return a > b ? 1.0f : 0.0f;
+    case FZ_GE: return a >= b ? 1.0f : 0.0f;
+  }
+  return 0.0f;
+}
+
+float unop(int op, float a) {
+  switch (op) {
+    case FZ_EXP: return std::exp(a);
+    case FZ_LOG: return std::log(a);
+    case FZ_SQRT: return std::sqrt(a);
+    default: return a;
+  }
+}
+
+// Visit every index of a plan; fn(offsets in elements of each operand).
+template <class Fn>
+void walk(const fz_ewise_plan &p, Fn fn) {
+  int64_t total = 1;
+  for (int d = 0; d < p.ndim; ++d) total *= p.size[d];
+  std::vector<int64_t> idx(p.ndim > 0 ? p.ndim : 1, 0);
+  std::vector<int64_t> off(p.num_operands);
+  for (int64_t i = 0; i < total; ++i) {
+    for (int k = 0; k < p.num_operands; ++k) {
+      int64_t o = 0;
+      for (int d = 0; d < p.ndim; ++d) o += idx[d] * p.stride_bytes[k][d] / 4;
+      off[k] = o;
+    }
+    fn(off.data());
+    for (int d = p.ndim - 1; d >= 0; --d) {
+      if (++idx[d] < p.size[d]) break;
+      idx[d] = 0;
+    }
+  }
+}
+}  // namespace
+
+extern "C" {
+
+const char *fz_last_error(void) { return g_err.c_str(); }
+int fz_version(void) { return 1; }
+int fz_device_count(int *c) { *c = 1; return FZ_OK; }
+int fz_set_device(int d) { return d == 0 ? FZ_OK : fail(FZ_ERR_INVALID, "Invalid device index"); }
+int fz_get_device(int *d) { *d = 0; return FZ_OK; }
+void *fz_default_stream(void) { static int s; return &s; }
+int fz_stream_sync(void *) { return FZ_OK; }
+int fz_device_sync(void) { return FZ_OK; }
+int fz_malloc(void **p, size_t bytes, void *) {
+  *p = nullptr;
+  if (!bytes) return FZ_OK;
+  *p = std::aligned_alloc(256, (bytes + 255) & ~(size_t)255);
+  return *p ? FZ_OK : fail(FZ_ERR_OOM, "host allocation failed");
+}
+int fz_free(void *p, void *) { std::free(p); return FZ_OK; }
+int fz_pool_stats(size_t *r, size_t *u) { if (r) *r = 0; if (u) *u = 0; return FZ_OK; }
+int fz_memcpy_h2d(void *d, const void *s, size_t n, void *) { if (n) std::memcpy(d, s, n); return FZ_OK; }
+int fz_memcpy_d2h(void *d, const void *s, size_t n, void *) { if (n) std::memcpy(d, s, n); return FZ_OK; }
+int fz_memcpy_d2d(void *d, const void *s, size_t n, void *) { if (n) std::memmove(d, s, n); return FZ_OK; }
+int fz_fill_f32(float *d, float v, int64_t n, void *) { for (int64_t i = 0; i < n; ++i) d[i] = v; ++g_launches; return FZ_OK; }
+int fz_host_alloc(void **p, size_t b) { return fz_malloc(p, b ? b : 1, nullptr); }
+int fz_host_free(void *p) { std::free(p); return FZ_OK; }
+int fz_timer_create(void **t) { *t = std::malloc(1); return FZ_OK; }
+int fz_timer_start(void *, void *) { return FZ_OK; }
+int fz_timer_stop(void *, void *) { return FZ_OK; }
+int fz_timer_elapsed_ms(void *, float *ms) { *ms = 0.0f; return FZ_OK; }
+int fz_timer_destroy(void *t) { std::free(t); return FZ_OK; }
+int64_t fz_launch_count(void) { return g_launches; }
+int fz_kernel_status(void) { return FZ_OK; }
+
+int fz_ewise_binary(int op, const fz_ewise_plan *p, float *out, const float *a, const float *b, void *) {
+  if (p->num_operands != 3) return fail(FZ_ERR_INVALID, "elementwise plan: wrong operand count");
+  walk(*p, [&](const int64_t *o) { out[o[0]] = binop(op, a[o[1]], b[o[2]]); });
+  ++g_launches;
+  return FZ_OK;
+}
+int fz_ewise_binary_contig(int op, int64_t n, float *out, const float *a, const float *b, void *) {
+  for (int64_t i = 0; i < n; ++i) out[i] = binop(op, a[i], b[i]);
+  ++g_launches;
+  return FZ_OK;
+}
+int fz_ewise_unary(int op, const fz_ewise_plan *p, float *out, const float *a, void *) {
+  walk(*p, [&](const int64_t *o) { out[o[0]] = unop(op, a[o[1]]); });
+  ++g_launches;
+  return FZ_OK;
+}
+int fz_sub_inplace(float *x, const float *y, int64_t n, void *) {
+  for (int64_t i = 0; i < n; ++i) x[i] = x[i] - y[i];
+  ++g_launches;
+  return FZ_OK;
+}
+
+int fz_fused_launch(const fz_program *pg, const fz_ewise_plan *p, float *const *outs,
+                    const float *const *leaves, void *) {
+  if (p->num_operands != pg->num_outputs + pg->num_leaves)
+    return fail(FZ_ERR_INVALID, "fz_fused_launch: plan operand count != outputs + leaves");
+  g_programs.insert(std::string(reinterpret_cast<const char *>(pg->nodes),
+                                sizeof(fz_node) * pg->num_nodes));
+  std::vector<float> t(pg->num_nodes);
+  walk(*p, [&](const int64_t *o) {
+    auto val = [&](int s) { return s >= 0 ? t[s] : leaves[-1 - s][o[pg->num_outputs + (-1 - s)]]; };
+    for (int i = 0; i < pg->num_nodes; ++i) {
+      const fz_node &n = pg->nodes[i];
+      t[i] = n.kind == FZ_NODE_BINARY ? binop(n.op, val(n.src0), val(n.src1))
+             : n.kind == FZ_NODE_UNARY ? unop(n.op, val(n.src0)) : n.imm;
+    }
+    for (int k = 0; k < pg->num_outputs; ++k) outs[k][o[k]] = t[pg->out_node[k]];
+  });
+  ++g_launches;
+  return FZ_OK;
+}
+int fz_fused_cache_size(void) { return (int)g_programs.size(); }
+
+int fz_reduce(int op, float *out, const float *in, int64_t outer, int64_t len, int64_t inner, void *) {
+  for (int64_t o = 0; o < outer; ++o)
+    for (int64_t j = 0; j < inner; ++j) {
+      const float *q = in + o * len * inner + j;
+      float acc = op == FZ_RMAX ? -INFINITY : 0.0f;
+      for (int64_t r = 0; r < len; ++r) {
+        float v = q[r * inner];
+        if (op == FZ_RMAX) {
+          if (acc != acc) continue;
+          if (v != v || v > acc || (v == 0.0f && acc == 0.0f && !std::signbit(v))) acc = v;
+        } else {
+          acc += v;
+        }
+      }
+      if (op == FZ_RMEAN) acc = acc / (float)len;
+      out[o * inner + j] = acc;
+    }
+  ++g_launches;
+  return FZ_OK;
+}
+
+int fz_swapaxes(float *out, const float *in, const int64_t *shape, int nd, int a1, int a2, void *) {
+  if (a1 < 0) a1 += nd;
+  if (a2 < 0) a2 += nd;
+  std::vector<int64_t> os(shape, shape + nd), ist(nd), ost(nd), idx(nd, 0);
+  std::swap(os[a1], os[a2]);
+  int64_t r = 1, q = 1, total = 1;
+  for (int d = nd - 1; d >= 0; --d) {
+    ist[d] = r; r *= shape[d];
+    ost[d] = q; q *= os[d];
+    total *= shape[d];
+  }
+  for (int64_t i = 0; i < total; ++i) {
+    int64_t o = 0;
+    for (int d = 0; d < nd; ++d) o += idx[d] * ost[d == a1 ? a2 : d == a2 ? a1 : d];
+    out[o] = in[i];
+    for (int d = nd - 1; d >= 0; --d) {
+      if (++idx[d] < shape[d]) break;
+      idx[d] = 0;
+    }
+  }
+  ++g_launches;
+  return FZ_OK;
+}
+
+int fz_gemm_f32(int64_t batch, int64_t M, int64_t N, int64_t K, const float *A, int64_t lda,
+                int64_t sA, int tA, const float *B, int64_t ldb, int64_t sB, int tB, float *C,
+                int64_t ldc, int64_t sC, void *) {
+  for (int64_t b = 0; b < batch; ++b)
+    for (int64_t i = 0; i < M; ++i)
+      for (int64_t j = 0; j < N; ++j) {
+        double s = 0;
+        for (int64_t k = 0; k < K; ++k) {
+          float x = tA ? A[b * sA + k * lda + i] : A[b * sA + i * lda + k];
+          float y = tB ? B[b * sB + j * ldb + k] : B[b * sB + k * ldb + j];
+          s += (double)x * (double)y;
+        }
+        C[b * sC + i * ldc + j] = (float)s;
+      }
+  ++g_launches;
+  return FZ_OK;
+}
+
+int fz_comm_unique_id(unsigned char id[FZ_UNIQUE_ID_BYTES]) { std::memset(id, 0, FZ_UNIQUE_ID_BYTES); return FZ_OK; }
+int fz_comm_init(void **c, int world, int, const unsigned char *) {
+  if (world != 1) return fail(FZ_ERR_UNSUPPORTED, "host test double: world must be 1");
+  *c = std::malloc(1);
+  return FZ_OK;
+}
+int fz_comm_allreduce(void *, const float *s, float *r, int64_t n, float scale, void *) {
+  for (int64_t i = 0; i < n; ++i) r[i] = s[i] * scale;
+  return FZ_OK;
+}
+int fz_comm_group_start(void) { return FZ_OK; }
+int fz_comm_group_end(void) { return FZ_OK; }
+int fz_comm_broadcast(void *, float *, int64_t, int, void *) { return FZ_OK; }
+int fz_comm_wait(void *, void *, double) { return FZ_OK; }
+int fz_comm_destroy(void *c) { std::free(c); return FZ_OK; }
+
+}  // extern "C"
