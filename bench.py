@@ -1,0 +1,460 @@
+#!/usr/bin/env python
+"""Benchmark of the Fusion hot path on B200: the MLP training step through Fusion's
+autodiff (4 Linear layers 1024-4096-4096-4096-16, ReLU, elementwise MSE, SGD
+lr 1e-3, Kaiming-uniform init, global batch 65536), batch-sharded over N GPUs with an
+NCCL all-reduce of the gradients.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Prints one JSON line. `value` is whole-job samples/s with inputs already in HBM,
+timed on the device with CUDA events over exactly K steps (max over ranks); `e2e`
+is the same metric through the public API with the step's inputs copied from
+pinned host memory and the loss read back every step. At N=1 the line also carries
+the roofline of the dominant kernel (the 3xTF32 GEMM at the step's largest shape),
+per-kernel bandwidth figures for the elementwise / reduction workloads, and the
+reference CPU path timed on this host as a baseline.
+
+`--impl reference` times the reference's own CPU implementation of the same step
+(the Fusion C++ sources built into oracle/_ref) on a bounded sample of the batch.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import os
+import pathlib
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = pathlib.Path(__file__).resolve().parent
+DIMS = [1024, 4096, 4096, 4096, 16]
+GLOBAL_BATCH = 65536
+LR = 1e-3
+SEED = 1234
+METRIC = ("MLP training step throughput (4x Linear 1024-4096-4096-4096-16 + ReLU, "
+          "elementwise MSE, SGD lr 1e-3, fp32 with 3xTF32 GEMMs)")
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--batch", type=int, default=GLOBAL_BATCH, help="global batch")
+    ap.add_argument("--no-kernels", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "basis": "measured"}
+    return dict(PEAKS_FALLBACK, basis="fallback")
+
+
+def flops_per_sample():
+    fwd = sum(2 * DIMS[i] * DIMS[i + 1] for i in range(len(DIMS) - 1))
+    return 3 * fwd  # forward + input-grad and weight-grad GEMMs (layer-1 input grad included)
+
+
+# ---------------------------------------------------------------- clocks
+class Clocks:
+    """Samples nvidia-smi during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index, self.rows, self.proc = index, [], None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(self.index)], stdout=subprocess.PIPE,
+                stderr=subprocess.DEVNULL, text=True)
+            threading.Thread(target=self._read, daemon=True).start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([c.strip() for c in line.split(",")])
+
+    def stop(self):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        rows = [r for r in self.rows if len(r) >= 9]
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": float(rows[0][2]) if rows[0][2].replace(".", "").isdigit() else None,
+                "samples": len(rows), "reasons": reasons}
+
+
+# ---------------------------------------------------------------- distributed plumbing
+class Dist:
+    def __init__(self):
+        self.rank = int(os.environ.get("RANK", 0))
+        self.world = int(os.environ.get("WORLD_SIZE", 1))
+        self.local = int(os.environ.get("LOCAL_RANK", 0))
+        self.pg = None
+        if self.world > 1:
+            import datetime
+
+            import torch.distributed as dist
+
+            dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
+            self.pg = dist
+
+    def barrier(self):
+        if self.pg:
+            self.pg.barrier()
+
+    def bcast_bytes(self, b):
+        if not self.pg:
+            return b
+        obj = [b]
+        self.pg.broadcast_object_list(obj, src=0)
+        return obj[0]
+
+    def max(self, v: float) -> float:
+        if not self.pg:
+            return v
+        import torch
+
+        t = torch.tensor([v], dtype=torch.float64)
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.pg:
+            self.pg.barrier()
+            self.pg.destroy_process_group()
+
+
+# ---------------------------------------------------------------- device timing helpers
+class Timer:
+    def __init__(self, capi):
+        self.A, self.L = capi, capi.lib()
+        self.h = C.c_void_p()
+        capi.check(self.L.fz_timer_create(C.byref(self.h)))
+
+    def start(self):
+        self.A.check(self.L.fz_timer_start(self.h, None))
+
+    def stop_ms(self):
+        self.A.check(self.L.fz_timer_stop(self.h, None))
+        ms = C.c_float()
+        self.A.check(self.L.fz_timer_elapsed_ms(self.h, C.byref(ms)))
+        return float(ms.value)
+
+
+def time_launch(capi, fn, reps=10, warm=3):
+    t = Timer(capi)
+    for _ in range(warm):
+        fn()
+    capi.check(capi.lib().fz_stream_sync(None))
+    t.start()
+    for _ in range(reps):
+        fn()
+    return t.stop_ms() / reps
+
+
+def kernel_suite(capi, pk):
+    """Elementwise / reduction / GEMM workloads of the hot-path sweep, one line each."""
+    L, A = capi.lib(), capi
+    hbm = pk["hbm_gbs"]
+    out = {}
+    n = 1 << 28
+    a, b, o = A.DeviceArray((n,)), A.DeviceArray((n,)), A.DeviceArray((n,))
+    A.check(L.fz_fill_f32(a.ptr, C.c_float(0.5), n, None))
+    A.check(L.fz_fill_f32(b.ptr, C.c_float(1.5), n, None))
+
+    def rec(name, ms, nbytes):
+        gbs = nbytes / ms / 1e6
+        out[name] = {"ms": round(ms, 4), "GB/s": round(gbs, 1), "frac_of_hbm": round(gbs / hbm, 3)}
+
+    for op in ("add", "mul", "div"):
+        rec(f"{op}_2^28", time_launch(A, lambda: A.check(L.fz_ewise_binary_contig(
+            A.BINOPS[op], n, o.ptr, a.ptr, b.ptr, None))), 12 * n)
+    plan = A.make_plan((n,), [(n,), (n,)])
+    for op in ("exp", "log", "sqrt"):
+        rec(f"{op}_2^28", time_launch(A, lambda: A.check(L.fz_ewise_unary(
+            A.UNOPS[op], C.byref(plan), o.ptr, a.ptr, None))), 8 * n)
+    r = 16384
+    bplan = A.make_plan((r, r), [(r, r), (r, r), (1, r)])
+    rec("bcast_add_16384^2+[1,16384]", time_launch(A, lambda: A.check(L.fz_ewise_binary(
+        0, C.byref(bplan), o.ptr, a.ptr, b.ptr, None))), 8 * r * r + 4 * r)
+    s = 8192
+    for name, (outer, ln, inner) in (("sum_ax1_8192^2", (s, s, 1)), ("sum_ax0_8192^2", (1, s, s)),
+                                     ("max_ax0_8192^2", (1, s, s))):
+        op = 2 if name.startswith("max") else 0
+        rec(name, time_launch(A, lambda: A.check(L.fz_reduce(op, o.ptr, a.ptr, outer, ln, inner, None))),
+            4 * s * s + 4 * (outer * inner))
+    # [64,256,64,64] over (0,2,3), keepdims: the reference reduces one axis per call
+    def chain4d():
+        A.check(L.fz_reduce(0, o.ptr, a.ptr, 64 * 256 * 64, 64, 1, None))
+        A.check(L.fz_reduce(0, b.ptr, o.ptr, 64 * 256, 64, 1, None))
+        A.check(L.fz_reduce(0, o.ptr, b.ptr, 1, 64, 256, None))
+    rec("sum_4d_axes023_chained", time_launch(A, chain4d), 4 * 64 * 256 * 64 * 64)
+    shp = (C.c_int64 * 2)(r, r)
+    rec("swapaxes_16384^2", time_launch(A, lambda: A.check(L.fz_swapaxes(o.ptr, a.ptr, shp, 2, 0, 1, None))),
+        8 * r * r)
+    g = 8192
+    x, y, c = A.DeviceArray((g, g)), A.DeviceArray((g, g)), A.DeviceArray((g, g))
+    A.check(L.fz_fill_f32(x.ptr, C.c_float(0.01), g * g, None))
+    A.check(L.fz_fill_f32(y.ptr, C.c_float(0.02), g * g, None))
+    ms = time_launch(A, lambda: A.check(L.fz_gemm_f32(1, g, g, g, x.ptr, g, 0, 0, y.ptr, g, 0, 0,
+                                                      c.ptr, g, 0, None)), reps=5, warm=2)
+    tf = 2 * g ** 3 / ms / 1e9
+    out["gemm_3xtf32_8192^3"] = {"ms": round(ms, 3), "TFLOP/s": round(tf, 1),
+                                 "tensor_pipe_TFLOP/s": round(3 * tf, 1)}
+    for arr in (a, b, o, x, y, c):
+        arr.free()
+    return out
+
+
+def gemm_roofline(capi, pk, m):
+    """Dominant kernel of the step: the [m,4096] x [4096,4096] GEMM (layers 2-3 and their
+    backward), timed live on the library stream with CUDA events."""
+    A, L = capi, capi.lib()
+    k = n = 4096
+    x, w, c = A.DeviceArray((m, k)), A.DeviceArray((n, k)), A.DeviceArray((m, n))
+    A.check(L.fz_fill_f32(x.ptr, C.c_float(0.01), m * k, None))
+    A.check(L.fz_fill_f32(w.ptr, C.c_float(0.02), n * k, None))
+    ms = time_launch(A, lambda: A.check(L.fz_gemm_f32(1, m, n, k, x.ptr, k, 0, 0, w.ptr, k, 0, 1,
+                                                      c.ptr, n, 0, None)), reps=10, warm=3)
+    A.check(L.fz_kernel_status())
+    for arr in (x, w, c):
+        arr.free()
+    achieved = 2.0 * m * n * k / ms / 1e9
+    tf32_peak = pk["bf16_tflops"] / 2.0  # TF32 runs at half the bf16 tensor rate
+    peak = tf32_peak / 3.0  # 3xTF32 issues three TF32 MMAs per product
+    traffic = None
+    summary = ROOT / "profiles" / "gemm_3xtf32_mlp_layer.md"
+    if summary.exists():
+        for line in summary.read_text().splitlines():
+            if line.startswith("dram_bytes_per_launch_full_size:"):
+                traffic = float(line.split(":", 1)[1])
+    return {"kernel": f"fz_gemm_f32 3xTF32 [{m},{k}]x[{k},{n}]^T (split pass + tcgen05 main loop)",
+            "bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak, 1),
+            "unit": "TFLOP/s", "frac": round(achieved / peak, 3), "traffic": traffic,
+            "peak_basis": f"{pk['basis']} bf16 {pk['bf16_tflops']} TFLOP/s / 2 (TF32 rate) / 3 (3xTF32)",
+            "tensor_pipe_achieved": round(3 * achieved, 1),
+            "tensor_pipe_frac_of_tf32": round(3 * achieved / tf32_peak, 3),
+            "ms_per_launch": round(ms, 3)}
+
+
+def cpu_baseline_ref(batch=1024, steps=1):
+    """The reference CPU path (oracle/_ref: Fusion's C++ sources + OpenBLAS) on a bounded
+    sample of the workload: `steps` MLP steps on `batch` rows, wall clock."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle
+
+    from nova_b200.mlp import init_params
+
+    R = oracle.Ref()
+    rng = np.random.default_rng(SEED + 7)
+    X = rng.standard_normal((batch, DIMS[0])).astype(np.float32)
+    Y = rng.standard_normal((batch, DIMS[-1])).astype(np.float32)
+    Ws, bs = init_params(DIMS, SEED)
+    Ws, bs, _ = R.mlp_step(X, Y, Ws, bs, LR)  # warm-up
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        Ws, bs, _ = R.mlp_step(X, Y, Ws, bs, LR)
+    dt = (time.perf_counter() - t0) / steps
+    return {"value": round(batch / dt, 2), "unit": "samples/s", "cores": os.cpu_count(),
+            "kind": "reference",
+            "sample": f"{steps} steps of the same MLP step on {batch} rows (reference Fusion C++ "
+                      f"autodiff + OpenBLAS sgemm with all host threads; elementwise ops "
+                      f"single-threaded as in the reference), {dt * 1e3:.0f} ms/step"}
+
+
+# ---------------------------------------------------------------- our arm
+def run_ours(args):
+    d = Dist()
+    import nova_b200
+    from nova_b200 import capi
+    from nova_b200.mlp import MLP, init_params
+
+    F = nova_b200.fusion
+    F.set_device(d.local)
+    comm = None
+    if d.world > 1:
+        uid = d.bcast_bytes(F.comm_unique_id() if d.rank == 0 else None)
+        comm = F.Comm(d.world, d.rank, uid)
+    assert args.batch % d.world == 0, "global batch must divide by the number of GPUs"
+    local = args.batch // d.world
+    Ws, bs = init_params(DIMS, SEED)
+    model = MLP(F, Ws, bs)
+    rng = np.random.default_rng(SEED + 1 + d.rank)
+    Xh = rng.standard_normal((local, DIMS[0]), dtype=np.float32)
+    Yh = rng.standard_normal((local, DIMS[-1]), dtype=np.float32)
+    # pinned host copies for the end-to-end leg
+    L = capi.lib()
+    pin = []
+    for src in (Xh, Yh):
+        p = C.c_void_p()
+        capi.check(L.fz_host_alloc(C.byref(p), src.nbytes))
+        arr = np.ctypeslib.as_array((C.c_float * src.size).from_address(p.value)).reshape(src.shape)
+        arr[...] = src
+        pin.append((p, arr))
+    Xp, Yp = pin[0][1], pin[1][1]
+    X = model.tensor(Xh, True)  # nova's Tensor defaults to requires_grad=True
+    Y = model.tensor(Yh, True)
+
+    for _ in range(args.warmup):
+        model.step(X, Y, LR, comm)
+    F.synchronize()
+
+    clocks = Clocks(d.local)
+    timer = Timer(capi)
+    d.barrier()
+    F.synchronize()
+    clocks.start()
+    launches0 = L.fz_launch_count()
+    timer.start()
+    for _ in range(args.steps):
+        loss = model.step(X, Y, LR, comm)
+    ms_local = timer.stop_ms()
+    F.synchronize()
+    if comm:
+        comm.wait(120.0)
+    launches = L.fz_launch_count() - launches0
+    d.barrier()
+    ms = d.max(ms_local) / args.steps
+
+    # end to end: host inputs copied in each step, loss read back each step
+    h2d = Xp.nbytes + Yp.nbytes
+    d.barrier()
+    F.synchronize()
+    timer.start()
+    for _ in range(args.steps):
+        x = model.tensor(Xp, True)
+        y = model.tensor(Yp, True)
+        loss = model.step(x, y, LR, comm)
+        loss.mean().to_numpy()
+    e2e_local = timer.stop_ms()
+    F.synchronize()
+    clk = clocks.stop()
+    d.barrier()
+    e2e_ms = d.max(e2e_local) / args.steps
+
+    value = args.batch / (ms / 1e3)
+    res = {
+        "metric": METRIC, "value": round(value, 1), "unit": "samples/s", "n_gpus": d.world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded N(0,1) inputs/targets, Kaiming-uniform weights, zero biases)",
+        "config": {"workload": "mlp_train_step", "dims": DIMS, "global_batch": args.batch,
+                   "per_gpu_batch": local, "parallelism": f"dp{d.world}", "lr": LR,
+                   "optimizer": "SGD momentum 0", "loss": "elementwise MSE (x/size)",
+                   "l2": "inputs and activations larger than L2 (1 GiB per [65536,4096] tensor)"},
+        "e2e": {"value": round(args.batch / (e2e_ms / 1e3), 1), "unit": "samples/s",
+                "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": 4,
+                "path": "nova_b200.fusion Python API (Tensor from pinned host arrays, "
+                        "loss.mean().to_numpy())"},
+        "gpu_launches": int(launches),
+        "gpu_launches_per_step": round(launches / args.steps, 1),
+        "model_tflops_per_step": round(flops_per_sample() * args.batch / 1e12, 2),
+        "clocks": clk,
+    }
+    if d.world == 1 and d.rank == 0:
+        pk = peaks()
+        res["roofline"] = gemm_roofline(capi, pk, local)
+        if not args.no_kernels:
+            res["kernels"] = kernel_suite(capi, pk)
+        if not args.no_cpu_baseline:
+            try:
+                res["cpu_baseline"] = cpu_baseline_ref()
+            except Exception as e:  # oracle not built on this host
+                res["cpu_baseline"] = {"value": None, "unavailable": str(e)}
+    if comm:
+        comm.destroy()
+    for p, _ in pin:
+        L.fz_host_free(p)
+    if d.rank == 0:
+        print(json.dumps(res), flush=True)
+    d.close()
+
+
+# ---------------------------------------------------------------- reference arm
+def run_reference(args):
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    if rank != 0:
+        return
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle
+
+    from nova_b200.mlp import init_params
+
+    if not oracle.have_ref():
+        print(json.dumps({"impl": "reference", "unavailable":
+                          "oracle/_ref/libfusion_ref.so not built (make -C oracle ref)"}))
+        return
+    R = oracle.Ref()
+    sample = 1024  # rows per step: a bounded sample of the 65536-row batch
+    rng = np.random.default_rng(SEED + 7)
+    X = rng.standard_normal((sample, DIMS[0])).astype(np.float32)
+    Y = rng.standard_normal((sample, DIMS[-1])).astype(np.float32)
+    Ws, bs = init_params(DIMS, SEED)
+    # A reference step costs ~10-20 s on 8 host cores whatever the row count (its
+    # serial swapaxes of the 4096x4096 weights dominates), so warm-up and timed steps
+    # stop early once their time budget is spent; `steps` reports the steps timed.
+    t0 = time.perf_counter()
+    for _ in range(args.warmup):
+        Ws, bs, _ = R.mlp_step(X, Y, Ws, bs, LR)
+        if time.perf_counter() - t0 > 30:
+            break
+    done = 0
+    t0 = time.perf_counter()
+    while done < args.steps:
+        Ws, bs, _ = R.mlp_step(X, Y, Ws, bs, LR)
+        done += 1
+        if time.perf_counter() - t0 > 120:
+            break
+    dt = (time.perf_counter() - t0) / done
+    v = round(sample / dt, 2)
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "samples/s",
+        "n_gpus": world, "steps": done, "steps_requested": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(dt * 1e3, 1), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "mlp_train_step", "dims": DIMS, "global_batch": args.batch,
+                   "sample_rows_per_step": sample, "parallelism": "none (reference is single-process CPU)"},
+        "cpu_baseline": {"value": v, "unit": "samples/s", "cores": os.cpu_count(), "kind": "reference",
+                         "sample": f"{sample} of {args.batch} rows per step"},
+        "e2e": {"value": v, "unit": "samples/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

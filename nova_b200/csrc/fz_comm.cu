@@ -8,6 +8,7 @@
 #include <nccl.h>
 
 #include <chrono>
+#include <cmath>
 #include <cstring>
 #include <thread>
 
@@ -80,9 +81,14 @@ int fz_comm_allreduce(void *comm, const float *send, float *recv, int64_t count,
   Comm *c = static_cast<Comm *>(comm);
   FZ_REQUIRE(!c->aborted, "fz_comm_allreduce: communicator was aborted");
   cudaStream_t s = fz::resolve(stream);
-  ncclResult_t r = ncclAllReduce(send, recv, (size_t)count, ncclFloat, ncclSum, c->comm, s);
+  // scale 1 -> sum; scale 1/world -> NCCL's average (no extra kernel, so the call
+  // is safe inside an fz_comm_group_start/end group); any other scale -> sum then
+  // a scaling pass (not allowed inside a group).
+  const bool avg = scale != 1.0f && std::fabs(scale * (float)c->world - 1.0f) < 1e-6f;
+  ncclResult_t r = ncclAllReduce(send, recv, (size_t)count, ncclFloat, avg ? ncclAvg : ncclSum,
+                                 c->comm, s);
   if (r != ncclSuccess) return nccl_fail(r, "ncclAllReduce");
-  if (scale != 1.0f) {
+  if (scale != 1.0f && !avg) {
     FZ_REQUIRE(((uintptr_t)recv & 15) == 0, "fz_comm_allreduce: buffer must be 16-byte aligned");
     unsigned grid = fz::grid_for((count + 3) / 4, 256 * 2, 8);
     scale_kernel<<<grid, 256, 0, s>>>(recv, scale, count);

@@ -57,6 +57,54 @@ struct GradTape {
   EngineScope scope;
 };
 
+// NCCL communicator over the GPUs of one data-parallel job (one process per GPU).
+struct Comm {
+  void *c = nullptr;
+  int world = 1, rank = 0;
+  Comm(int w, int r, py::bytes uid) : world(w), rank(r) {
+    std::string id = uid;
+    if (id.size() != FZ_UNIQUE_ID_BYTES) throw std::invalid_argument("Comm: unique id must be 128 bytes");
+    fz_check(fz_comm_init(&c, w, r, reinterpret_cast<const unsigned char *>(id.data())), "fz_comm_init");
+  }
+  ~Comm() { destroy(); }
+  void destroy() {
+    if (c) fz_comm_destroy(c);
+    c = nullptr;
+  }
+  // Average each tensor over ranks, out of place, then rebind the tensor's storage
+  // to the result so pending readers of the old value keep it. All reductions are
+  // issued as one NCCL group.
+  void allreduce_mean(const std::vector<ADTensor *> &ts) {
+    if (!c) throw std::runtime_error("Comm: destroyed");
+    std::vector<std::shared_ptr<DeviceBuffer>> outs;
+    std::vector<const float *> ins;
+    for (ADTensor *t : ts) {
+      ins.push_back(t->raw().data());
+      outs.push_back(std::make_shared<DeviceBuffer>(t->raw().size()));
+    }
+    fz_check(fz_comm_group_start(), "fz_comm_group_start");
+    for (size_t i = 0; i < ts.size(); ++i)
+      fz_check(fz_comm_allreduce(c, ins[i], outs[i]->ptr, (int64_t)ts[i]->raw().size(),
+                                 1.0f / (float)world, nullptr),
+               "fz_comm_allreduce");
+    fz_check(fz_comm_group_end(), "fz_comm_group_end");
+    for (size_t i = 0; i < ts.size(); ++i) ts[i]->raw().rebind_buffer(outs[i]);
+  }
+  void broadcast(const std::vector<ADTensor *> &ts, int root) {
+    if (!c) throw std::runtime_error("Comm: destroyed");
+    for (ADTensor *t : ts) {
+      auto buf = std::make_shared<DeviceBuffer>(t->raw().size());
+      fz_check(fz_memcpy_d2d(buf->ptr, t->raw().data(), t->raw().size() * 4, nullptr), "fz_memcpy_d2d");
+      fz_check(fz_comm_broadcast(c, buf->ptr, (int64_t)t->raw().size(), root, nullptr), "fz_comm_broadcast");
+      t->raw().rebind_buffer(buf);
+    }
+  }
+  void wait(double timeout_s) {
+    if (!c) throw std::runtime_error("Comm: destroyed");
+    fz_check(fz_comm_wait(c, nullptr, timeout_s), "fz_comm_wait");
+  }
+};
+
 }  // namespace
 
 PYBIND11_MODULE(fusion, m) {
@@ -251,4 +299,21 @@ PYBIND11_MODULE(fusion, m) {
   });
   m.def("device_ptr", [](const T &t) { return reinterpret_cast<uintptr_t>(t.raw().data()); },
         py::arg("tensor"), "Device address of the tensor's data (lowers it if pending).");
+
+  m.def("comm_unique_id", []() {
+    unsigned char id[FZ_UNIQUE_ID_BYTES];
+    fz_check(fz_comm_unique_id(id), "fz_comm_unique_id");
+    return py::bytes(reinterpret_cast<const char *>(id), FZ_UNIQUE_ID_BYTES);
+  }, "NCCL unique id (128 bytes) for rank 0 to share with the other ranks.");
+  py::class_<Comm>(m, "Comm", py::module_local())
+      .def(py::init<int, int, py::bytes>(), py::arg("world"), py::arg("rank"), py::arg("unique_id"))
+      .def_readonly("world", &Comm::world)
+      .def_readonly("rank", &Comm::rank)
+      .def("allreduce_mean", &Comm::allreduce_mean, py::arg("tensors"),
+           "Average tensors over all ranks (one NCCL group, out of place).")
+      .def("broadcast", &Comm::broadcast, py::arg("tensors"), py::arg("root") = 0)
+      .def("wait", &Comm::wait, py::arg("timeout_s"),
+           "Wait for this rank's stream with a deadline; on expiry abort the communicator "
+           "and raise.")
+      .def("destroy", &Comm::destroy);
 }

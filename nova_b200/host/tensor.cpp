@@ -411,6 +411,12 @@ void RawTensor::set_values(const float *src, size_t n) {
   storage_->expr = make_leaf(std::move(buf), shape_);
 }
 
+void RawTensor::rebind_buffer(std::shared_ptr<DeviceBuffer> buf) {
+  FB_CHECK(storage_, "uninitialised tensor");
+  FB_CHECK(buf && buf->numel == size(), "rebind_buffer: size mismatch");
+  storage_->expr = make_leaf(std::move(buf), shape_);
+}
+
 void RawTensor::clear() {
   if (!storage_ || storage_->numel() == 0) return;
   storage_->expr = make_const(0.0f, storage_->expr->shape);

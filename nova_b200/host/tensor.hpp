@@ -135,6 +135,8 @@ class RawTensor {
 
   // In-place writes, visible to every shallow copy.
   void set_values(const float *src, size_t n);
+  // Point the storage at an already computed device buffer of the same size.
+  void rebind_buffer(std::shared_ptr<DeviceBuffer> buf);
   void clear();                           // zero (RawTensor.hpp:140-149)
   void assign(const RawTensor &other);    // RawTensor.hpp:151-157
   RawTensor &operator-=(const RawTensor &other);  // sub_inplace (ops/Ewise.hpp:69-83)

@@ -53,7 +53,8 @@ def ulp_diff(a, b):
     ib = np.where(ib < 0, np.int64(-2**31) - ib, ib)
     d = np.abs(ia - ib)
     both_nan = np.isnan(a) & np.isnan(b)
-    return np.where(both_nan, 0, d)
+    d = np.where(both_nan, 0, d)
+    return d if d.size else np.zeros(1, np.int64)
 
 
 def assert_bits_equal(got, want, what=""):
