@@ -194,6 +194,19 @@ int fz_fused_cache_size(void);
 int fz_reduce(int op, float *out, const float *in, int64_t outer, int64_t len,
               int64_t inner, void *stream);
 
+/* fz_reduce without any device allocation, for callers that must not allocate
+ * while they run (a runtime that reserves and accounts for all device memory
+ * itself, or a latency-critical loop that must not grow the pool). It has no
+ * counterpart in the reference. Split partials go to a fixed 8 MiB array
+ * compiled into the library (held on every GPU that loads it until exit) instead
+ * of the pool; the kernels and split plan are fz_reduce's, so results are
+ * bit-identical. Returns FZ_ERR_INVALID when a reduction's plan needs more
+ * partials than the array holds. The first call on a device looks up the array's
+ * address (make it before any stream capture). Calls share the array: calls that
+ * overlap on the GPU race and must be serialised by the caller. */
+int fz_reduce_noalloc(int op, float *out, const float *in, int64_t outer, int64_t len,
+                      int64_t inner, void *stream);
+
 /* ---- layout -------------------------------------------------------------- */
 
 /* Materialised swapaxes of a contiguous tensor: out = in with axes a1, a2

@@ -14,6 +14,8 @@
 // reduces them, so results do not depend on scheduling (no atomics).
 // mean = sum / (float)len with an IEEE division, as fusion::math::mean does
 // (fusion/src/Fusion/ops/Reduce.hpp:27-36).
+#include <mutex>
+
 #include "fz_common.cuh"
 
 namespace {
@@ -307,4 +309,162 @@ extern "C" int fz_reduce(int op, float *out, const float *in, int64_t outer, int
     case FZ_RMAX: return reduce_op<FZ_RMAX>(out, in, outer, len, inner, s);
   }
   return fz::fail(FZ_ERR_INVALID, "fz_reduce: unknown op " + std::to_string(op));
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of fz_reduce.
+//
+// Some callers must not allocate device memory while they run: a host runtime
+// that reserves the GPU's memory up front and accounts for every byte itself
+// (a serving process that pre-partitions HBM between models, for instance), or
+// a latency-critical loop where growing the allocator's pool would call into the
+// driver. fz_reduce takes its split partials from the stream-ordered pool, so
+// this variant takes them from a fixed array compiled into the library instead:
+// kNoAllocScratchFloats floats (8 MiB) of device memory that every GPU which
+// loads the library holds until the process exits.
+//
+// It launches exactly the kernels fz_reduce launches, with the same split plan,
+// so its results are bit-identical. It rejects (FZ_ERR_INVALID) any reduction
+// whose split plan needs more partials than the array holds. The array's device
+// address is looked up with cudaGetSymbolAddress the first time the entry point
+// runs on a device, so that first call should come before any stream capture.
+// All calls share the array and it keeps the last call's contents; every partial
+// is written before it is read, so nothing needs clearing, but calls whose work
+// overlaps on the GPU (different streams, or different host threads on one
+// device) race on it and must be serialised by the caller.
+namespace {
+
+constexpr int64_t kNoAllocScratchFloats = int64_t(1) << 21;
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchFloats];
+
+std::mutex g_noalloc_mu;
+float *g_noalloc_ptr[64] = {};
+
+int noalloc_scratch(float **p) {
+  int dev = 0;
+  FZ_CUDA(cudaGetDevice(&dev));
+  FZ_REQUIRE(dev >= 0 && dev < 64, "fz_reduce_noalloc: device ordinal out of range");
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void *q = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&q, g_noalloc_scratch);
+    if (e != cudaSuccess) return fz::cuda_fail(e, "cudaGetSymbolAddress(scratch)", __FILE__, __LINE__);
+    g_noalloc_ptr[dev] = static_cast<float *>(q);
+  }
+  *p = g_noalloc_ptr[dev];
+  return FZ_OK;
+}
+
+int too_big(int64_t need) {
+  return fz::fail(FZ_ERR_INVALID,
+                  "fz_reduce_noalloc: this reduction needs " + std::to_string(need) +
+                      " partial sums but the library's fixed scratch holds " +
+                      std::to_string(kNoAllocScratchFloats) + "; use fz_reduce");
+}
+
+// Same plan as launch_rows, partials in the fixed scratch.
+template <int OP>
+int noalloc_rows(const float *in, float *out, int64_t rows, int64_t len, float *scratch,
+                 cudaStream_t s) {
+  if (len <= 2048) return launch_rows_group<OP>(in, out, rows, len, len, len, true, s);
+  const int threads = 512;
+  const int64_t target_ctas = (int64_t)fz::num_sms() * 4;
+  int64_t splits = 1;
+  if (rows < target_ctas) {
+    splits = (target_ctas + rows - 1) / rows;
+    int64_t max_splits = len / 8192;
+    if (splits > max_splits) splits = max_splits;
+    if (splits < 1) splits = 1;
+  }
+  int64_t chunk = (len + splits - 1) / splits;
+  chunk = (chunk + 3) & ~(int64_t)3;
+  splits = (len + chunk - 1) / chunk;
+  int vec = (len % 4 == 0) && (((uintptr_t)in & 15) == 0);
+  int64_t items = rows * splits;
+  unsigned grid = (unsigned)(items < target_ctas * 2 ? items : target_ctas * 2);
+  if (splits == 1) {
+    rows_block_kernel<OP><<<grid, threads, 0, s>>>(in, out, rows, len, len, 1, chunk, len, true,
+                                                   vec);
+    FZ_CHECK_LAUNCH();
+    return FZ_OK;
+  }
+  if (items > kNoAllocScratchFloats || splits > 2048) return too_big(items);
+  rows_block_kernel<OP><<<grid, threads, 0, s>>>(in, scratch, rows, len, len, splits, chunk, 0,
+                                                 false, vec);
+  FZ_CHECK_LAUNCH();
+  return launch_rows_group<OP>(scratch, out, rows, splits, splits, len, true, s);
+}
+
+// Same plan as launch_cols, partials in the fixed scratch.
+template <int OP>
+int noalloc_cols(const float *in, float *out, int64_t outer, int64_t len, int64_t inner,
+                 float *scratch, cudaStream_t s) {
+  const bool v4 = (inner % 4 == 0) && (((uintptr_t)in & 15) == 0) && (((uintptr_t)out & 15) == 0);
+  const int V = v4 ? 4 : 1;
+  const int64_t base = outer * ((inner + V - 1) / V);
+  const int64_t target = (int64_t)fz::num_sms() * 2048;
+  int64_t splits = 1;
+  if (base < target) {
+    splits = (target + base - 1) / base;
+    int64_t max_splits = len / 16;
+    if (splits > max_splits) splits = max_splits;
+    if (splits < 1) splits = 1;
+  }
+  int64_t chunk = (len + splits - 1) / splits;
+  splits = (len + chunk - 1) / chunk;
+  int64_t items = splits * base;
+  unsigned grid = fz::grid_for(items, 256, 8, 4);
+  float *dst = out;
+  if (splits > 1) {
+    if (splits * outer * inner > kNoAllocScratchFloats) return too_big(splits * outer * inner);
+    dst = scratch;
+  }
+  if (V == 4)
+    cols_kernel<OP, 4><<<grid, 256, 0, s>>>(in, dst, outer, len, inner, splits, chunk, len,
+                                            splits == 1);
+  else
+    cols_kernel<OP, 1><<<grid, 256, 0, s>>>(in, dst, outer, len, inner, splits, chunk, len,
+                                            splits == 1);
+  FZ_CHECK_LAUNCH();
+  if (splits == 1) return FZ_OK;
+  const int64_t cols = outer * inner;
+  const bool w4 = (cols % 4 == 0) && (((uintptr_t)out & 15) == 0);
+  unsigned g2 = fz::grid_for(cols / (w4 ? 4 : 1) + 1, 256, 8, 4);
+  if (w4)
+    cols_kernel<OP, 4><<<g2, 256, 0, s>>>(dst, out, 1, splits, cols, 1, splits, len, 1);
+  else
+    cols_kernel<OP, 1><<<g2, 256, 0, s>>>(dst, out, 1, splits, cols, 1, splits, len, 1);
+  FZ_CHECK_LAUNCH();
+  return FZ_OK;
+}
+
+template <int OP>
+int noalloc_op(float *out, const float *in, int64_t outer, int64_t len, int64_t inner,
+               float *scratch, cudaStream_t s) {
+  if (inner == 1) return noalloc_rows<OP>(in, out, outer, len, scratch, s);
+  return noalloc_cols<OP>(in, out, outer, len, inner, scratch, s);
+}
+
+}  // namespace
+
+extern "C" int fz_reduce_noalloc(int op, float *out, const float *in, int64_t outer, int64_t len,
+                                 int64_t inner, void *stream) {
+  FZ_REQUIRE(outer >= 0 && len >= 0 && inner >= 0, "fz_reduce_noalloc: negative extent");
+  if (outer == 0 || inner == 0) return FZ_OK;
+  FZ_REQUIRE(out && (in || len == 0), "fz_reduce_noalloc: null pointer");
+  FZ_REQUIRE(op == FZ_RSUM || op == FZ_RMEAN || op == FZ_RMAX,
+             "fz_reduce_noalloc: unknown op " + std::to_string(op));
+  float *scratch = nullptr;
+  int rc = noalloc_scratch(&scratch);
+  if (rc) return rc;
+  cudaStream_t s = fz::resolve(stream);
+  if (len == 0) {
+    float v = op == FZ_RMAX ? -INFINITY : op == FZ_RMEAN ? NAN : 0.0f;
+    return fz_fill_f32(out, v, outer * inner, s);
+  }
+  switch (op) {
+    case FZ_RSUM: return noalloc_op<FZ_RSUM>(out, in, outer, len, inner, scratch, s);
+    case FZ_RMEAN: return noalloc_op<FZ_RMEAN>(out, in, outer, len, inner, scratch, s);
+    default: return noalloc_op<FZ_RMAX>(out, in, outer, len, inner, scratch, s);
+  }
 }
