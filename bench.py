@@ -51,6 +51,10 @@ def parse():
     ap.add_argument("--batch", type=int, default=GLOBAL_BATCH, help="global batch")
     ap.add_argument("--no-kernels", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--kernel", default=None,
+                    help="run one hot-path kernel on a profiling-sized case instead of the step "
+                         "(gemm, add, bcast_add, exp, sum_ax0, sum_ax1, swapaxes, bias_relu)")
+    ap.add_argument("--reps", type=int, default=3)
     return ap.parse_args()
 
 
@@ -448,9 +452,62 @@ def run_reference(args):
     }), flush=True)
 
 
+def run_kernel(args):
+    """One kernel in a loop, sized for an ncu capture (inputs above L2, a few GB)."""
+    import nova_b200
+    from nova_b200 import capi
+
+    F = nova_b200.fusion
+    F.set_device(0)
+    A, L = capi, capi.lib()
+    k = args.kernel
+    if k == "gemm":  # the MLP's dominant GEMM shape at 1/8 of the batch
+        m, n, kk = 8192, 4096, 4096
+        x, w, c = A.DeviceArray((m, kk)), A.DeviceArray((n, kk)), A.DeviceArray((m, n))
+        A.check(L.fz_fill_f32(x.ptr, C.c_float(0.01), m * kk, None))
+        A.check(L.fz_fill_f32(w.ptr, C.c_float(0.02), n * kk, None))
+        fn = lambda: A.check(L.fz_gemm_f32(1, m, n, kk, x.ptr, kk, 0, 0, w.ptr, kk, 0, 1, c.ptr,
+                                            n, 0, None))
+        work = 2.0 * m * n * kk
+    elif k == "bias_relu":  # fused relu(x + b) of the MLP forward through the fusion IR
+        rows, cols = 16384, 4096
+        dev = F.CppDevice(F.CppDeviceType.CPU, 0)
+        xt = F.Tensor([rows, cols], np.zeros(rows * cols, np.float32), F.CppDType.FLOAT32, dev, False)
+        bt = F.Tensor([cols], np.zeros(cols, np.float32), F.CppDType.FLOAT32, dev, False)
+
+        def fn():
+            F.flush((xt + bt).maximum(0.0))
+        work = 8.0 * rows * cols
+    else:
+        n = 1 << 26
+        a, b, o = A.DeviceArray((n,)), A.DeviceArray((n,)), A.DeviceArray((n,))
+        A.check(L.fz_fill_f32(a.ptr, C.c_float(0.5), n, None))
+        A.check(L.fz_fill_f32(b.ptr, C.c_float(1.5), n, None))
+        r = 8192
+        plan1 = A.make_plan((n,), [(n,), (n,)])
+        bplan = A.make_plan((r, r), [(r, r), (r, r), (1, r)])
+        shp = (C.c_int64 * 2)(r, r)
+        fn, work = {
+            "add": (lambda: A.check(L.fz_ewise_binary_contig(0, n, o.ptr, a.ptr, b.ptr, None)), 12.0 * n),
+            "exp": (lambda: A.check(L.fz_ewise_unary(0, C.byref(plan1), o.ptr, a.ptr, None)), 8.0 * n),
+            "bcast_add": (lambda: A.check(L.fz_ewise_binary(0, C.byref(bplan), o.ptr, a.ptr, b.ptr, None)),
+                          8.0 * r * r + 4 * r),
+            "sum_ax1": (lambda: A.check(L.fz_reduce(0, o.ptr, a.ptr, r, r, 1, None)), 4.0 * r * r),
+            "sum_ax0": (lambda: A.check(L.fz_reduce(0, o.ptr, a.ptr, 1, r, r, None)), 4.0 * r * r),
+            "swapaxes": (lambda: A.check(L.fz_swapaxes(o.ptr, a.ptr, shp, 2, 0, 1, None)), 8.0 * r * r),
+        }[k]
+    ms = time_launch(A, fn, reps=args.reps, warm=1)
+    F.synchronize()
+    unit = "TFLOP/s" if k == "gemm" else "GB/s"
+    print(json.dumps({"kernel": k, "ms": round(ms, 4),
+                      unit: round(work / ms / (1e9 if k == "gemm" else 1e6), 1)}), flush=True)
+
+
 def main():
     args = parse()
-    if args.impl == "reference":
+    if args.kernel:
+        run_kernel(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)
