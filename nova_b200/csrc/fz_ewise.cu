@@ -17,20 +17,21 @@ namespace {
 
 using fz::EwPlan;
 
-template <typename IDX>
-struct RowMap {
-  // offsets of row `r` (index over all dims but the innermost) for NOPS operands
-  __device__ __forceinline__ static void offsets(const EwPlan &p, IDX r, int64_t *off) {
-    for (int k = 0; k < p.nops; ++k) off[k] = 0;
-    for (int d = p.ndim - 2; d >= 0; --d) {
-      IDX sz = (IDX)p.size[d];
-      IDX q = r / sz;
-      IDX i = r - q * sz;
-      r = q;
-      for (int k = 0; k < p.nops; ++k) off[k] += (int64_t)i * p.stride[k][d];
-    }
+// Offsets of row `r` (the index over every dim but the innermost) for NOPS
+// operands; NOPS is a template parameter so the offsets stay in registers.
+template <int NOPS, typename IDX>
+__device__ __forceinline__ void row_offsets(const EwPlan &p, IDX r, int64_t (&off)[NOPS]) {
+#pragma unroll
+  for (int k = 0; k < NOPS; ++k) off[k] = 0;
+  for (int d = p.ndim - 2; d >= 0; --d) {
+    const IDX sz = (IDX)p.size[d];
+    const IDX q = r / sz;
+    const int64_t i = (int64_t)(r - q * sz);
+    r = q;
+#pragma unroll
+    for (int k = 0; k < NOPS; ++k) off[k] += i * p.stride[k][d];
   }
-};
+}
 
 template <int VEC>
 struct Vec;
@@ -54,15 +55,14 @@ __global__ void __launch_bounds__(256) ewise_kernel(EwPlan p, float *__restrict_
   const int64_t sa = p.ndim ? p.stride[1][p.ndim - 1] : 0;
   const int64_t sb = (NIN == 2 && p.ndim) ? p.stride[2][p.ndim - 1] : 0;
   const IDX step = (IDX)gridDim.x * blockDim.x;
-  IDX last_row = (IDX)-1;
-  int64_t off[3] = {0, 0, 0};
+  constexpr int NOPS = NIN + 1;
+  int64_t off[NOPS];
+#pragma unroll
+  for (int k = 0; k < NOPS; ++k) off[k] = 0;
   for (IDX g = (IDX)blockIdx.x * blockDim.x + threadIdx.x; g < total; g += step) {
     IDX row = g / groups_per_row;
     IDX col = (g - row * groups_per_row) * VEC;
-    if (row != last_row) {
-      if (p.ndim > 1) RowMap<IDX>::offsets(p, row, off);
-      last_row = row;
-    }
+    if (p.ndim > 1) row_offsets<NOPS, IDX>(p, row, off);
     if constexpr (VEC == 4) {
       if ((int64_t)col + 4 <= inner) {
         float4 x, y = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -70,7 +70,7 @@ __global__ void __launch_bounds__(256) ewise_kernel(EwPlan p, float *__restrict_
         if (sa) x = ld4(pa);
         else x = make_float4(*pa, *pa, *pa, *pa);
         if constexpr (NIN == 2) {
-          const float *pb = b + off[2] + (int64_t)col * sb;
+          const float *pb = b + off[NIN] + (int64_t)col * sb;
           if (sb) y = ld4(pb);
           else y = make_float4(*pb, *pb, *pb, *pb);
         }
@@ -94,7 +94,7 @@ __global__ void __launch_bounds__(256) ewise_kernel(EwPlan p, float *__restrict_
       int64_t c = (int64_t)col + v;
       float x = a[off[1] + c * sa];
       float r;
-      if constexpr (NIN == 2) r = fzd::binop_t<OP>(x, b[off[2] + c * sb]);
+      if constexpr (NIN == 2) r = fzd::binop_t<OP>(x, b[off[NIN] + c * sb]);
       else r = fzd::unop_t<OP>(x);
       out[off[0] + c * so] = r;
     }

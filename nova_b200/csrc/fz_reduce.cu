@@ -132,58 +132,67 @@ __global__ void __launch_bounds__(512) rows_block_kernel(const float *__restrict
 }
 
 // Columns: in is [outer, len, inner]; each thread owns V adjacent columns of one
-// outer slice and a chunk of len. out is [splits, outer, inner] (split-major).
+// outer slice and a chunk of len, with 4 rows in flight. Unsplit it writes
+// out[o*inner + c]; split, it writes partials column-major,
+// out[(o*inner + c) * splits + s], so the second pass is a row reduction.
 template <int OP, int V>
 __global__ void __launch_bounds__(256) cols_kernel(const float *__restrict__ in,
                                                    float *__restrict__ out, int64_t outer,
                                                    int64_t len, int64_t inner, int64_t splits,
-                                                   int64_t chunk, int64_t div_len, int final) {
+                                                   int64_t chunk, int64_t div_len) {
   const int64_t cgroups = (inner + V - 1) / V;
   const int64_t items = splits * outer * cgroups;
+  const bool split = splits > 1;
   for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < items;
        t += (int64_t)gridDim.x * blockDim.x) {
     int64_t cg = t % cgroups;
     int64_t rest = t / cgroups;
     int64_t o = rest % outer;
-    int64_t s = rest / outer;
+    int64_t sp = rest / outer;
     int64_t c = cg * V;
-    int64_t beg = s * chunk, end = beg + chunk < len ? beg + chunk : len;
+    int64_t beg = sp * chunk, end = beg + chunk < len ? beg + chunk : len;
     const float *p = in + (o * len) * inner + c;
-    float *q = out + (s * outer + o) * inner + c;
+    const int64_t col = o * inner + c;
     if (V == 4 && c + 4 <= inner) {
       float a0 = Red<OP>::init(), a1 = a0, a2 = a0, a3 = a0;
       int64_t r = beg;
-      for (; r + 1 < end; r += 2) {
-        float4 x = *reinterpret_cast<const float4 *>(p + r * inner);
-        float4 y = *reinterpret_cast<const float4 *>(p + (r + 1) * inner);
-        a0 = Red<OP>::op(a0, Red<OP>::op(x.x, y.x));
-        a1 = Red<OP>::op(a1, Red<OP>::op(x.y, y.y));
-        a2 = Red<OP>::op(a2, Red<OP>::op(x.z, y.z));
-        a3 = Red<OP>::op(a3, Red<OP>::op(x.w, y.w));
+      for (; r + 3 < end; r += 4) {
+        float4 x0 = *reinterpret_cast<const float4 *>(p + r * inner);
+        float4 x1 = *reinterpret_cast<const float4 *>(p + (r + 1) * inner);
+        float4 x2 = *reinterpret_cast<const float4 *>(p + (r + 2) * inner);
+        float4 x3 = *reinterpret_cast<const float4 *>(p + (r + 3) * inner);
+        a0 = Red<OP>::op(a0, Red<OP>::op(Red<OP>::op(x0.x, x1.x), Red<OP>::op(x2.x, x3.x)));
+        a1 = Red<OP>::op(a1, Red<OP>::op(Red<OP>::op(x0.y, x1.y), Red<OP>::op(x2.y, x3.y)));
+        a2 = Red<OP>::op(a2, Red<OP>::op(Red<OP>::op(x0.z, x1.z), Red<OP>::op(x2.z, x3.z)));
+        a3 = Red<OP>::op(a3, Red<OP>::op(Red<OP>::op(x0.w, x1.w), Red<OP>::op(x2.w, x3.w)));
       }
-      if (r < end) {
+      for (; r < end; ++r) {
         float4 x = *reinterpret_cast<const float4 *>(p + r * inner);
         a0 = Red<OP>::op(a0, x.x);
         a1 = Red<OP>::op(a1, x.y);
         a2 = Red<OP>::op(a2, x.z);
         a3 = Red<OP>::op(a3, x.w);
       }
-      float4 res = make_float4(finish<OP>(a0, div_len, final), finish<OP>(a1, div_len, final),
-                               finish<OP>(a2, div_len, final), finish<OP>(a3, div_len, final));
-      *reinterpret_cast<float4 *>(q) = res;
+      if (!split) {
+        *reinterpret_cast<float4 *>(out + col) =
+            make_float4(finish<OP>(a0, div_len, true), finish<OP>(a1, div_len, true),
+                        finish<OP>(a2, div_len, true), finish<OP>(a3, div_len, true));
+      } else {
+        out[(col + 0) * splits + sp] = a0;
+        out[(col + 1) * splits + sp] = a1;
+        out[(col + 2) * splits + sp] = a2;
+        out[(col + 3) * splits + sp] = a3;
+      }
     } else {
       for (int v = 0; v < V && c + v < inner; ++v) {
         float a = Red<OP>::init();
         for (int64_t r = beg; r < end; ++r) a = Red<OP>::op(a, p[r * inner + v]);
-        q[v] = finish<OP>(a, div_len, final);
+        if (!split) out[col + v] = finish<OP>(a, div_len, true);
+        else out[(col + v) * splits + sp] = a;
       }
     }
   }
 }
-
-template <int OP>
-int launch_rows(const float *in, float *out, int64_t rows, int64_t len, int64_t ld,
-                int64_t div_len, bool final, cudaStream_t s);
 
 template <int OP>
 int launch_rows_group(const float *in, float *out, int64_t rows, int64_t len, int64_t ld,
@@ -204,10 +213,35 @@ int launch_rows_group(const float *in, float *out, int64_t rows, int64_t len, in
   return FZ_OK;
 }
 
+// Where split partials go: `ptr` null means stream-ordered memory from the pool
+// (fz_reduce); otherwise a caller-owned buffer of `cap` floats (fz_reduce_noalloc).
+struct Scratch {
+  float *ptr;
+  int64_t cap;
+};
+
+int scratch_too_small(int64_t need, int64_t cap) {
+  return fz::fail(FZ_ERR_INVALID,
+                  "fz_reduce_noalloc: this reduction needs " + std::to_string(need) +
+                      " partial sums but the library's fixed scratch holds " + std::to_string(cap) +
+                      "; use fz_reduce");
+}
+
+int take_scratch(const Scratch &sc, int64_t need, float **part, bool *own, cudaStream_t s) {
+  *own = false;
+  if (sc.ptr) {
+    if (need > sc.cap) return scratch_too_small(need, sc.cap);
+    *part = sc.ptr;
+    return FZ_OK;
+  }
+  *own = true;
+  return fz_malloc((void **)part, sizeof(float) * need, s);
+}
+
 template <int OP>
-int launch_rows(const float *in, float *out, int64_t rows, int64_t len, int64_t ld,
-                int64_t div_len, bool final, cudaStream_t s) {
-  if (len <= 2048) return launch_rows_group<OP>(in, out, rows, len, ld, div_len, final, s);
+int launch_rows(const float *in, float *out, int64_t rows, int64_t len, int64_t div_len,
+                const Scratch &sc, cudaStream_t s) {
+  if (len <= 2048) return launch_rows_group<OP>(in, out, rows, len, len, div_len, true, s);
   const int threads = 512;
   const int64_t target_ctas = (int64_t)fz::num_sms() * 4;
   int64_t splits = 1;
@@ -220,37 +254,39 @@ int launch_rows(const float *in, float *out, int64_t rows, int64_t len, int64_t 
   int64_t chunk = (len + splits - 1) / splits;
   chunk = (chunk + 3) & ~(int64_t)3;
   splits = (len + chunk - 1) / chunk;
-  int vec = (ld % 4 == 0) && (((uintptr_t)in & 15) == 0);
+  int vec = (len % 4 == 0) && (((uintptr_t)in & 15) == 0);
   int64_t items = rows * splits;
   unsigned grid = (unsigned)(items < target_ctas * 2 ? items : target_ctas * 2);
   if (splits == 1) {
-    rows_block_kernel<OP><<<grid, threads, 0, s>>>(in, out, rows, len, ld, 1, chunk, div_len,
-                                                   final, vec);
+    rows_block_kernel<OP><<<grid, threads, 0, s>>>(in, out, rows, len, len, 1, chunk, div_len,
+                                                   true, vec);
     FZ_CHECK_LAUNCH();
     return FZ_OK;
   }
   float *part = nullptr;
-  int rc = fz_malloc((void **)&part, sizeof(float) * items, s);
+  bool own = false;
+  int rc = take_scratch(sc, items, &part, &own, s);
   if (rc) return rc;
-  rows_block_kernel<OP><<<grid, threads, 0, s>>>(in, part, rows, len, ld, splits, chunk, 0,
+  rows_block_kernel<OP><<<grid, threads, 0, s>>>(in, part, rows, len, len, splits, chunk, 0,
                                                  false, vec);
   FZ_CHECK_LAUNCH();
-  rc = launch_rows<OP>(part, out, rows, splits, splits, div_len, final, s);
-  fz_free(part, s);
+  // splits <= 4 * SMs, so the second pass is a short-row group reduction
+  rc = launch_rows_group<OP>(part, out, rows, splits, splits, div_len, true, s);
+  if (own) fz_free(part, s);
   return rc;
 }
 
 template <int OP>
 int launch_cols(const float *in, float *out, int64_t outer, int64_t len, int64_t inner,
-                cudaStream_t s) {
+                const Scratch &sc, cudaStream_t s) {
   const bool v4 = (inner % 4 == 0) && (((uintptr_t)in & 15) == 0) && (((uintptr_t)out & 15) == 0);
   const int V = v4 ? 4 : 1;
   const int64_t base = outer * ((inner + V - 1) / V);
-  const int64_t target = (int64_t)fz::num_sms() * 2048;
+  const int64_t target = (int64_t)fz::num_sms() * 1024;  // 4 rows in flight per thread
   int64_t splits = 1;
   if (base < target) {
     splits = (target + base - 1) / base;
-    int64_t max_splits = len / 16;  // keep >= 16 rows per thread
+    int64_t max_splits = len / 32;  // keep >= 32 rows per thread
     if (splits > max_splits) splits = max_splits;
     if (splits < 1) splits = 1;
   }
@@ -259,36 +295,42 @@ int launch_cols(const float *in, float *out, int64_t outer, int64_t len, int64_t
   int64_t items = splits * base;
   unsigned grid = fz::grid_for(items, 256, 8, 4);
   float *dst = out;
+  bool own = false;
   if (splits > 1) {
-    int rc = fz_malloc((void **)&dst, sizeof(float) * splits * outer * inner, s);
+    int rc = take_scratch(sc, splits * outer * inner, &dst, &own, s);
     if (rc) return rc;
   }
   if (V == 4)
-    cols_kernel<OP, 4><<<grid, 256, 0, s>>>(in, dst, outer, len, inner, splits, chunk, len,
-                                            splits == 1);
+    cols_kernel<OP, 4><<<grid, 256, 0, s>>>(in, dst, outer, len, inner, splits, chunk, len);
   else
-    cols_kernel<OP, 1><<<grid, 256, 0, s>>>(in, dst, outer, len, inner, splits, chunk, len,
-                                            splits == 1);
+    cols_kernel<OP, 1><<<grid, 256, 0, s>>>(in, dst, outer, len, inner, splits, chunk, len);
   FZ_CHECK_LAUNCH();
   if (splits == 1) return FZ_OK;
-  // second pass: [splits, outer*inner] reduced over splits, finishing with len
-  const int64_t cols = outer * inner;
-  const bool w4 = (cols % 4 == 0) && (((uintptr_t)out & 15) == 0);
-  unsigned g2 = fz::grid_for(cols / (w4 ? 4 : 1) + 1, 256, 8, 4);
-  if (w4)
-    cols_kernel<OP, 4><<<g2, 256, 0, s>>>(dst, out, 1, splits, cols, 1, splits, len, 1);
-  else
-    cols_kernel<OP, 1><<<g2, 256, 0, s>>>(dst, out, 1, splits, cols, 1, splits, len, 1);
-  FZ_CHECK_LAUNCH();
-  fz_free(dst, s);
-  return FZ_OK;
+  // second pass: every output column's `splits` partials are contiguous
+  int rc = launch_rows_group<OP>(dst, out, outer * inner, splits, splits, len, true, s);
+  if (own) fz_free(dst, s);
+  return rc;
 }
 
 template <int OP>
 int reduce_op(float *out, const float *in, int64_t outer, int64_t len, int64_t inner,
-              cudaStream_t s) {
-  if (inner == 1) return launch_rows<OP>(in, out, outer, len, len, len, true, s);
-  return launch_cols<OP>(in, out, outer, len, inner, s);
+              const Scratch &sc, cudaStream_t s) {
+  if (inner == 1) return launch_rows<OP>(in, out, outer, len, len, sc, s);
+  return launch_cols<OP>(in, out, outer, len, inner, sc, s);
+}
+
+int reduce_entry(int op, float *out, const float *in, int64_t outer, int64_t len, int64_t inner,
+                 const Scratch &sc, cudaStream_t s) {
+  if (len == 0) {
+    float v = op == FZ_RMAX ? -INFINITY : op == FZ_RMEAN ? NAN : 0.0f;
+    return fz_fill_f32(out, v, outer * inner, s);
+  }
+  switch (op) {
+    case FZ_RSUM: return reduce_op<FZ_RSUM>(out, in, outer, len, inner, sc, s);
+    case FZ_RMEAN: return reduce_op<FZ_RMEAN>(out, in, outer, len, inner, sc, s);
+    case FZ_RMAX: return reduce_op<FZ_RMAX>(out, in, outer, len, inner, sc, s);
+  }
+  return fz::fail(FZ_ERR_INVALID, "fz_reduce: unknown op " + std::to_string(op));
 }
 
 }  // namespace
@@ -298,17 +340,7 @@ extern "C" int fz_reduce(int op, float *out, const float *in, int64_t outer, int
   FZ_REQUIRE(outer >= 0 && len >= 0 && inner >= 0, "fz_reduce: negative extent");
   if (outer == 0 || inner == 0) return FZ_OK;
   FZ_REQUIRE(out && (in || len == 0), "fz_reduce: null pointer");
-  cudaStream_t s = fz::resolve(stream);
-  if (len == 0) {
-    float v = op == FZ_RMAX ? -INFINITY : op == FZ_RMEAN ? NAN : 0.0f;
-    return fz_fill_f32(out, v, outer * inner, s);
-  }
-  switch (op) {
-    case FZ_RSUM: return reduce_op<FZ_RSUM>(out, in, outer, len, inner, s);
-    case FZ_RMEAN: return reduce_op<FZ_RMEAN>(out, in, outer, len, inner, s);
-    case FZ_RMAX: return reduce_op<FZ_RMAX>(out, in, outer, len, inner, s);
-  }
-  return fz::fail(FZ_ERR_INVALID, "fz_reduce: unknown op " + std::to_string(op));
+  return reduce_entry(op, out, in, outer, len, inner, Scratch{nullptr, 0}, fz::resolve(stream));
 }
 
 // ---------------------------------------------------------------------------
@@ -323,8 +355,9 @@ extern "C" int fz_reduce(int op, float *out, const float *in, int64_t outer, int
 // kNoAllocScratchFloats floats (8 MiB) of device memory that every GPU which
 // loads the library holds until the process exits.
 //
-// It launches exactly the kernels fz_reduce launches, with the same split plan,
-// so its results are bit-identical. It rejects (FZ_ERR_INVALID) any reduction
+// It runs fz_reduce's own launcher with the partials pointed at the fixed array,
+// so it launches the same kernels with the same split plan and its results are
+// bit-identical. It rejects (FZ_ERR_INVALID) any reduction
 // whose split plan needs more partials than the array holds. The array's device
 // address is looked up with cudaGetSymbolAddress the first time the entry point
 // runs on a device, so that first call should come before any stream capture.
@@ -355,96 +388,6 @@ int noalloc_scratch(float **p) {
   return FZ_OK;
 }
 
-int too_big(int64_t need) {
-  return fz::fail(FZ_ERR_INVALID,
-                  "fz_reduce_noalloc: this reduction needs " + std::to_string(need) +
-                      " partial sums but the library's fixed scratch holds " +
-                      std::to_string(kNoAllocScratchFloats) + "; use fz_reduce");
-}
-
-// Same plan as launch_rows, partials in the fixed scratch.
-template <int OP>
-int noalloc_rows(const float *in, float *out, int64_t rows, int64_t len, float *scratch,
-                 cudaStream_t s) {
-  if (len <= 2048) return launch_rows_group<OP>(in, out, rows, len, len, len, true, s);
-  const int threads = 512;
-  const int64_t target_ctas = (int64_t)fz::num_sms() * 4;
-  int64_t splits = 1;
-  if (rows < target_ctas) {
-    splits = (target_ctas + rows - 1) / rows;
-    int64_t max_splits = len / 8192;
-    if (splits > max_splits) splits = max_splits;
-    if (splits < 1) splits = 1;
-  }
-  int64_t chunk = (len + splits - 1) / splits;
-  chunk = (chunk + 3) & ~(int64_t)3;
-  splits = (len + chunk - 1) / chunk;
-  int vec = (len % 4 == 0) && (((uintptr_t)in & 15) == 0);
-  int64_t items = rows * splits;
-  unsigned grid = (unsigned)(items < target_ctas * 2 ? items : target_ctas * 2);
-  if (splits == 1) {
-    rows_block_kernel<OP><<<grid, threads, 0, s>>>(in, out, rows, len, len, 1, chunk, len, true,
-                                                   vec);
-    FZ_CHECK_LAUNCH();
-    return FZ_OK;
-  }
-  if (items > kNoAllocScratchFloats || splits > 2048) return too_big(items);
-  rows_block_kernel<OP><<<grid, threads, 0, s>>>(in, scratch, rows, len, len, splits, chunk, 0,
-                                                 false, vec);
-  FZ_CHECK_LAUNCH();
-  return launch_rows_group<OP>(scratch, out, rows, splits, splits, len, true, s);
-}
-
-// Same plan as launch_cols, partials in the fixed scratch.
-template <int OP>
-int noalloc_cols(const float *in, float *out, int64_t outer, int64_t len, int64_t inner,
-                 float *scratch, cudaStream_t s) {
-  const bool v4 = (inner % 4 == 0) && (((uintptr_t)in & 15) == 0) && (((uintptr_t)out & 15) == 0);
-  const int V = v4 ? 4 : 1;
-  const int64_t base = outer * ((inner + V - 1) / V);
-  const int64_t target = (int64_t)fz::num_sms() * 2048;
-  int64_t splits = 1;
-  if (base < target) {
-    splits = (target + base - 1) / base;
-    int64_t max_splits = len / 16;
-    if (splits > max_splits) splits = max_splits;
-    if (splits < 1) splits = 1;
-  }
-  int64_t chunk = (len + splits - 1) / splits;
-  splits = (len + chunk - 1) / chunk;
-  int64_t items = splits * base;
-  unsigned grid = fz::grid_for(items, 256, 8, 4);
-  float *dst = out;
-  if (splits > 1) {
-    if (splits * outer * inner > kNoAllocScratchFloats) return too_big(splits * outer * inner);
-    dst = scratch;
-  }
-  if (V == 4)
-    cols_kernel<OP, 4><<<grid, 256, 0, s>>>(in, dst, outer, len, inner, splits, chunk, len,
-                                            splits == 1);
-  else
-    cols_kernel<OP, 1><<<grid, 256, 0, s>>>(in, dst, outer, len, inner, splits, chunk, len,
-                                            splits == 1);
-  FZ_CHECK_LAUNCH();
-  if (splits == 1) return FZ_OK;
-  const int64_t cols = outer * inner;
-  const bool w4 = (cols % 4 == 0) && (((uintptr_t)out & 15) == 0);
-  unsigned g2 = fz::grid_for(cols / (w4 ? 4 : 1) + 1, 256, 8, 4);
-  if (w4)
-    cols_kernel<OP, 4><<<g2, 256, 0, s>>>(dst, out, 1, splits, cols, 1, splits, len, 1);
-  else
-    cols_kernel<OP, 1><<<g2, 256, 0, s>>>(dst, out, 1, splits, cols, 1, splits, len, 1);
-  FZ_CHECK_LAUNCH();
-  return FZ_OK;
-}
-
-template <int OP>
-int noalloc_op(float *out, const float *in, int64_t outer, int64_t len, int64_t inner,
-               float *scratch, cudaStream_t s) {
-  if (inner == 1) return noalloc_rows<OP>(in, out, outer, len, scratch, s);
-  return noalloc_cols<OP>(in, out, outer, len, inner, scratch, s);
-}
-
 }  // namespace
 
 extern "C" int fz_reduce_noalloc(int op, float *out, const float *in, int64_t outer, int64_t len,
@@ -457,14 +400,6 @@ extern "C" int fz_reduce_noalloc(int op, float *out, const float *in, int64_t ou
   float *scratch = nullptr;
   int rc = noalloc_scratch(&scratch);
   if (rc) return rc;
-  cudaStream_t s = fz::resolve(stream);
-  if (len == 0) {
-    float v = op == FZ_RMAX ? -INFINITY : op == FZ_RMEAN ? NAN : 0.0f;
-    return fz_fill_f32(out, v, outer * inner, s);
-  }
-  switch (op) {
-    case FZ_RSUM: return noalloc_op<FZ_RSUM>(out, in, outer, len, inner, scratch, s);
-    case FZ_RMEAN: return noalloc_op<FZ_RMEAN>(out, in, outer, len, inner, scratch, s);
-    default: return noalloc_op<FZ_RMAX>(out, in, outer, len, inner, scratch, s);
-  }
+  return reduce_entry(op, out, in, outer, len, inner, Scratch{scratch, kNoAllocScratchFloats},
+                      fz::resolve(stream));
 }

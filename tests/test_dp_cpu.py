@@ -1,0 +1,110 @@
+"""Data-parallel MLP step, world size 2 over gloo on CPU.
+
+Each rank runs nova_b200.mlp.MLP.step on its half of the batch through the C++ host
+layer (host test double of the C ABI), with a gloo-backed stand-in for the NCCL
+Comm that averages the gradient tensors over ranks. The updated weights must equal
+the reference's single-process step on the whole batch (oracle/_ref), because each
+shard's loss is divided by its own size and the average over ranks undoes that.
+The bias follows the reference quirk (SGD applies row 0 of the unreduced [B, U]
+gradient): under data parallelism it moves by the average of the shards' row 0,
+which is what the reference gives when run on each shard and averaged.
+"""
+import os
+import pathlib
+import socket
+import sys
+
+import numpy as np
+import pytest
+
+HERE = pathlib.Path(__file__).resolve().parent
+ROOT = HERE.parent
+DIMS = [16, 32, 32, 4]
+BATCH = 24
+LR = 1e-2
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+class GlooComm:
+    """Stand-in for fusion.Comm: average tensors over ranks with gloo, then rebind."""
+
+    def __init__(self, F, dist):
+        self.F, self.dist = F, dist
+
+    def allreduce_mean(self, tensors):
+        import torch
+
+        for t in tensors:
+            a = torch.from_numpy(t.to_numpy().copy())
+            self.dist.all_reduce(a)
+            t.set_values((a / self.dist.get_world_size()).numpy().ravel())
+
+
+def _worker(rank, world, port, out_dir, ext_path):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import importlib.util
+
+    import torch.distributed as dist
+
+    sys.path[:0] = [str(ROOT), str(HERE)]
+    import api_cases
+    from nova_b200.mlp import MLP
+
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    spec = importlib.util.spec_from_file_location("hostfake.fusion", ext_path)
+    F = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(F)
+    X, Y, Ws, bs = api_cases.mlp_inputs(31, DIMS, BATCH)
+    lo, hi = rank * BATCH // world, (rank + 1) * BATCH // world
+    model = MLP(F, Ws, bs)
+    x = model.tensor(X[lo:hi], True)
+    y = model.tensor(Y[lo:hi], True)
+    model.step(x, y, LR, GlooComm(F, dist))
+    for i, (W, b) in enumerate(model.numpy_params()):
+        np.save(out_dir / f"r{rank}_W{i}.npy", W)
+        np.save(out_dir / f"r{rank}_b{i}.npy", b)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.fixture(scope="module")
+def fake_ext():
+    sys.path.insert(0, str(HERE / "hostfake"))
+    import build_fake
+
+    return build_fake.build()
+
+
+def test_dp2_step_matches_reference_full_batch(tmp_path, fake_ext, ref):
+    import torch.multiprocessing as mp
+
+    import api_cases
+
+    mp.spawn(_worker, args=(2, _free_port(), tmp_path, str(fake_ext)), nprocs=2, join=True)
+    X, Y, Ws, bs = api_cases.mlp_inputs(31, DIMS, BATCH)
+    W_full, _, _ = ref.mlp_step(X, Y, Ws, bs, LR)
+    shard_b = []
+    for r in range(2):
+        lo, hi = r * BATCH // 2, (r + 1) * BATCH // 2
+        _, b_r, _ = ref.mlp_step(X[lo:hi], Y[lo:hi], Ws, bs, LR)
+        shard_b.append(b_r)
+    for i in range(len(DIMS) - 1):
+        w0, w1 = np.load(tmp_path / f"r0_W{i}.npy"), np.load(tmp_path / f"r1_W{i}.npy")
+        np.testing.assert_array_equal(w0, w1)  # replicas stay identical
+        err = np.linalg.norm(w0 - W_full[i]) / np.linalg.norm(W_full[i])
+        assert err <= 1e-5, (i, err)
+        b0 = np.load(tmp_path / f"r0_b{i}.npy")
+        want_b = (shard_b[0][i] + shard_b[1][i]) / 2
+        np.testing.assert_allclose(b0, want_b, rtol=1e-5, atol=1e-7)
+
+
+def test_shards_cover_batch_once():
+    world, batch = 8, 65536
+    rows = [range(r * batch // world, (r + 1) * batch // world) for r in range(world)]
+    flat = [i for r in rows for i in r]
+    assert flat == list(range(batch))
