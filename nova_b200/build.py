@@ -37,10 +37,16 @@ NVCC_FLAGS = ARCH + [
 
 
 def _nccl_dirs():
-    """NCCL header and library used by the collective entry points."""
-    inc = pathlib.Path("/usr/include")
-    lib = pathlib.Path("/usr/lib/x86_64-linux-gnu")
-    return inc, lib
+    """NCCL header and library used by the collective entry points.
+
+    Prefer the NCCL wheel in the Python environment: it is the copy torch loads, and
+    two NCCL builds cannot coexist in one process (they share the soname
+    libnccl.so.2), so linking the same one keeps `import torch` working in either
+    import order."""
+    site = pathlib.Path(sysconfig.get_paths()["purelib"]) / "nvidia" / "nccl"
+    if (site / "include" / "nccl.h").exists() and (site / "lib" / "libnccl.so.2").exists():
+        return site / "include", site / "lib"
+    return pathlib.Path("/usr/include"), pathlib.Path("/usr/lib/x86_64-linux-gnu")
 
 
 def _stale(out: pathlib.Path, deps) -> bool:
@@ -76,9 +82,11 @@ def build_lib(verbose: bool = False, jobs: int = 8) -> pathlib.Path:
     with ThreadPoolExecutor(max_workers=jobs) as ex:
         list(ex.map(lambda c: _run(c, verbose), jobs_list))
     if jobs_list or _stale(LIB, objs):
-        _run([NVCC, *ARCH, "-shared", "-o", str(LIB), *map(str, objs),
-              "-L" + str(nccl_lib), "-lnccl", "-lnvrtc",
-              "-Xlinker", "-rpath," + str(CUDA_HOME / "lib64")], verbose)
+        nccl_so = nccl_lib / "libnccl.so"
+        nccl_link = ["-L" + str(nccl_lib), "-lnccl"] if nccl_so.exists() else [
+            "-L" + str(nccl_lib), "-Xlinker", "-l:libnccl.so.2"]
+        _run([NVCC, *ARCH, "-shared", "-o", str(LIB), *map(str, objs), *nccl_link, "-lnvrtc",
+              "-Xlinker", "-rpath," + str(nccl_lib) + ":" + str(CUDA_HOME / "lib64")], verbose)
     return LIB
 
 

@@ -2,22 +2,34 @@
 //
 // C[b] = op(A[b]) @ op(B[b]), row-major fp32 in and out.
 //
-// 1. Split pass (split_kernel / split_t_kernel): every operand is rewritten as two
-//    K-major planes, hi = x with the low 13 mantissa bits cleared (exactly
-//    representable in TF32) and lo = x - hi (exact in fp32). A is stored [M, K],
-//    B as [N, K] (transposed through shared memory when given as [K, N]). Planes
-//    have a 16-byte-multiple row pitch so TMA can address them.
-// 2. Main kernel, one 128 x 256 output tile per CTA, warp-specialised:
-//      warp 0      TMA producer: per k-tile loads A_hi, A_lo (128 x 32) and
-//                  B_hi, B_lo (256 x 32) into a 2-stage ring (128-byte swizzle)
-//      warp 1      allocates 256 TMEM columns; one lane issues per 8-wide k-step
-//                  three tcgen05.mma.kind::tf32 (hi*hi + hi*lo + lo*hi) into the
-//                  fp32 TMEM accumulator, then tcgen05.commit frees the stage
-//      warps 2-5   epilogue: tcgen05.ld 32 lanes x 32 columns at a time, store C
-//    Every mbarrier wait is bounded by a %globaltimer deadline; on expiry the
-//    kernel records an error code in the device's error word (read by
-//    fz_kernel_status), drains its own TMA loads (bounded), frees TMEM and
-//    returns, so a bad launch surfaces as an error instead of a hang.
+// 3xTF32: x = hi + lo with hi = x with its 13 low mantissa bits cleared (exact in
+// TF32) and lo = x - hi (exact in fp32); C = Ah*Bh + Ah*Bl + Al*Bh. The kind::tf32
+// MMA ignores the 13 low mantissa bits of its fp32 inputs, so an operand already
+// stored K-major ([M, K] for A, [N, K] for B) is its own hi plane and only its lo
+// plane is written (lo_kernel); an operand given the other way round is transposed
+// into K-major hi and lo planes through shared memory (split_t_kernel).
+//
+// Main kernel, persistent (one CTA per SM walking 128 x 256 output tiles in grouped
+// order), warp-specialised, 320 threads:
+//   warp 0     TMA producer: per k-tile of BK = 16 loads A_hi, A_lo (128 x 16) and
+//              B_hi, B_lo (256 x 16) into a 4-stage ring of 48 KB (64-byte swizzle)
+//   warp 1     allocates 2 x 256 TMEM columns; one lane issues, per 8-wide k-step,
+//              tcgen05.mma.kind::tf32 lo*hi, hi*lo, hi*hi, and tcgen05.commit frees
+//              each stage. The K range is cut into chunks of 256; each chunk
+//              accumulates from zero into one of the two TMEM buffers.
+//   warps 2-9  promotion and epilogue: two warps per TMEM lane quarter, each owning
+//              128 of the 256 columns, tcgen05.ld every finished chunk and add it
+//              into an fp32 register accumulator (IEEE adds), then store C.
+// The tensor core's own fp32 accumulation is truncating, so its error grows with
+// the number of MMAs folded into one accumulator (about 3e-5 relative at K = 4096
+// when a whole tile accumulates in TMEM); promoting every 256 of K bounds it to the
+// error of a 256-long chunk and keeps long-K products (weight gradients, K = batch)
+// within 1e-5. Double-buffered chunks let the MMAs run on while a chunk is promoted.
+//
+// Every mbarrier wait is bounded by a %globaltimer deadline; on expiry the kernel
+// records an error code in the device's error word (read by fz_kernel_status),
+// drains its own TMA loads (bounded), frees TMEM and returns, so a bad launch
+// surfaces as an error instead of a hang.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -29,14 +41,23 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BN = 256;
-constexpr int BK = 32;  // fp32 elements per k-tile = 128 bytes = one swizzle row
-constexpr int STAGES = 2;
+// k-tile: BK fp32 = one swizzle row (BK = 16 -> 64-byte swizzle, 4 stages of 48 KB;
+// BK = 32 -> 128-byte swizzle, 2 stages of 96 KB)
+#ifndef FZ_GEMM_BK
+#define FZ_GEMM_BK 16
+#endif
+constexpr int BK = FZ_GEMM_BK;
+constexpr int STAGES = BK == 16 ? 4 : 2;
+constexpr int SWIZZLE_BYTES = BK * 4;
+static_assert(BK == 16 || BK == 32, "BK must be 16 or 32");
 constexpr int UMMA_K = 8;  // K of one kind::tf32 MMA
 constexpr int TILE_A_BYTES = BM * BK * 4;  // 16 KB
 constexpr int TILE_B_BYTES = BN * BK * 4;  // 32 KB
 constexpr int STAGE_BYTES = 2 * TILE_A_BYTES + 2 * TILE_B_BYTES;  // 96 KB
-constexpr int TMEM_COLS = 256;
-constexpr int NUM_THREADS = 192;
+constexpr int TMEM_COLS = 256;          // one accumulator buffer (BN fp32 columns)
+constexpr int KCHUNK = 16;              // k-tiles per promotion chunk (K = 256)
+constexpr int NUM_EPI_WARPS = 8;        // 2 per TMEM lane quarter
+constexpr int NUM_THREADS = 64 + 32 * NUM_EPI_WARPS;
 constexpr unsigned long long kWaitNs = 4000000000ull;  // 4 s per wait
 
 enum : int { kErrNone = 0, kErrTimeoutFull = 1, kErrTimeoutEmpty = 2, kErrTimeoutAcc = 3 };
@@ -47,23 +68,42 @@ __device__ __forceinline__ void split1(float x, float &hi, float &lo) {
   lo = __fsub_rn(x, hi);
 }
 
-// src rows are K-major already: src[b][r][k] at b*sb + r*ld + k -> hi/lo[b][r][k] (pitch kp)
-__global__ void __launch_bounds__(256) split_kernel(const float *__restrict__ src, int64_t ld,
-                                                    int64_t sb, int64_t rows, int64_t K,
-                                                    int64_t kp, int64_t batch,
-                                                    float *__restrict__ hi,
-                                                    float *__restrict__ lo) {
+// src rows are K-major already: src[b][r][k] at b*sb + r*ld + k. Writes the lo
+// plane lo[b][r][k] (pitch kp, zero beyond K); the MMA reads src itself as hi. When
+// src cannot be addressed by TMA (row pitch not a multiple of 16 bytes, or a
+// broadcast batch), `hi` is non-null and receives a copy of src at pitch kp.
+__global__ void __launch_bounds__(256) lo_kernel(const float *__restrict__ src, int64_t ld,
+                                                 int64_t sb, int64_t rows, int64_t K, int64_t kp,
+                                                 int64_t batch, float *__restrict__ lo,
+                                                 float *__restrict__ hi) {
+  const int64_t step = (int64_t)gridDim.x * blockDim.x;
+  const int64_t t0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (!hi && ld == kp && K == kp && (batch == 1 || sb == rows * kp) && (((uintptr_t)src | (uintptr_t)lo) & 15) == 0) {
+    const int64_t n4 = batch * rows * kp / 4;  // dense rows: one flat float4 stream
+    const float4 *s4 = reinterpret_cast<const float4 *>(src);
+    float4 *l4 = reinterpret_cast<float4 *>(lo);
+    for (int64_t t = t0; t < n4; t += step) {
+      float4 x = s4[t];
+      float h;
+      float4 r;
+      split1(x.x, h, r.x);
+      split1(x.y, h, r.y);
+      split1(x.z, h, r.z);
+      split1(x.w, h, r.w);
+      l4[t] = r;
+    }
+    return;
+  }
   const int64_t total = batch * rows * kp;
-  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total;
-       t += (int64_t)gridDim.x * blockDim.x) {
+  for (int64_t t = t0; t < total; t += step) {
     int64_t k = t % kp;
     int64_t rest = t / kp;
-    int64_t r = rest % rows, b = rest / rows;
-    float x = k < K ? src[b * sb + r * ld + k] : 0.0f;
+    int64_t r = rest % rows, bb = rest / rows;
+    float x = k < K ? src[bb * sb + r * ld + k] : 0.0f;
     float h, l;
     split1(x, h, l);
-    hi[t] = h;
     lo[t] = l;
+    if (hi) hi[t] = x;
   }
 }
 
@@ -161,15 +201,17 @@ __device__ __forceinline__ void prefetch_map(const CUtensorMap *map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
-// K-major, 128-byte swizzle: 8-row groups 1024 B apart (SBO), LBO unused (1),
-// descriptor version 1 (bit 46), layout type 2 = SWIZZLE_128B (bits 61-63).
-__device__ __forceinline__ uint64_t smem_desc_k_sw128(uint32_t addr) {
+// K-major shared-memory descriptor for rows of SWIZZLE_BYTES (one swizzle atom
+// row per tile row): 8-row groups 8*SWIZZLE_BYTES apart (SBO), LBO unused (1),
+// descriptor version 1 (bit 46), layout type at bits 61-63: 2 = SWIZZLE_128B,
+// 4 = SWIZZLE_64B.
+__device__ __forceinline__ uint64_t smem_desc_k(uint32_t addr) {
   uint64_t d = 0;
   d |= (uint64_t)((addr >> 4) & 0x3fff);
   d |= (uint64_t)1 << 16;
-  d |= (uint64_t)(1024 >> 4) << 32;
+  d |= (uint64_t)((8 * SWIZZLE_BYTES) >> 4) << 32;
   d |= (uint64_t)1 << 46;
-  d |= (uint64_t)2 << 61;
+  d |= (uint64_t)(SWIZZLE_BYTES == 128 ? 2 : 4) << 61;
   return d;
 }
 
@@ -215,26 +257,48 @@ struct GemmArgs {
   float *C;
   int64_t ldc, strideC;
   int M, N, K, batch;
+  int tiles_m, tiles_n, num_tiles, group_m;
   int *err;
 };
 
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Tile t -> (m block, n block, batch) in grouped order: within a batch, bands of
+// group_m row blocks are walked column by column, so the tiles in flight on the
+// 148 SMs share A rows and B columns in L2.
+__device__ __forceinline__ void decode_tile(int t, const GemmArgs &a, int &mb, int &nb, int &bz) {
+  const int per_batch = a.tiles_m * a.tiles_n;
+  bz = t / per_batch;
+  const int r = t - bz * per_batch;
+  const int band = r / (a.group_m * a.tiles_n);
+  const int first_m = band * a.group_m;
+  const int rows = min(a.group_m, a.tiles_m - first_m);
+  const int in_band = r - band * a.group_m * a.tiles_n;
+  mb = first_m + in_band % rows;
+  nb = in_band / rows;
+}
+
+// Persistent kernel: one CTA per SM walks tiles blockIdx.x, +gridDim.x, ...
+// K is cut into chunks of KCHUNK k-tiles accumulated alternately in two TMEM
+// buffers; warps 2-9 fold each finished chunk into fp32 registers.
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap mapAh,
                        const __grid_constant__ CUtensorMap mapAl,
                        const __grid_constant__ CUtensorMap mapBh,
                        const __grid_constant__ CUtensorMap mapBl, GemmArgs args) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  // 1024-byte alignment for the 128-byte swizzle atoms
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   __shared__ __align__(8) uint64_t full_bar[STAGES];
   __shared__ __align__(8) uint64_t empty_bar[STAGES];
-  __shared__ __align__(8) uint64_t acc_bar;
+  __shared__ __align__(8) uint64_t acc_full[2];
+  __shared__ __align__(8) uint64_t acc_empty[2];
   __shared__ uint32_t tmem_base_slot;
   __shared__ volatile int abort_flag;
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int tile_n = blockIdx.x, tile_m = blockIdx.y, bz = blockIdx.z;
   const int num_k = (args.K + BK - 1) / BK;
 
   if (threadIdx.x == 0) {
@@ -242,7 +306,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 1);
     }
-    mbar_init(&acc_bar, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 32 * NUM_EPI_WARPS);  // every epilogue thread arrives
+    }
     abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     prefetch_map(&mapAh);
@@ -253,7 +320,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(&tmem_base_slot)),
-                 "r"(TMEM_COLS)
+                 "r"(2 * TMEM_COLS)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -263,7 +330,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const uint32_t tmem_base = tmem_base_slot;
 
   auto stage_ptr = [&](int s, int which) -> uint8_t * {
-    // which: 0 A_hi, 1 A_lo, 2 B_hi, 3 B_lo
     uint8_t *base = smem + (size_t)s * STAGE_BYTES;
     switch (which) {
       case 0: return base;
@@ -276,32 +342,34 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (warp == 0) {
     if (lane == 0) {
       // ------------------------------------------------------ TMA producer
-      int issued = 0;
+      int it = 0;
       bool ok = true;
-      for (int kt = 0; kt < num_k; ++kt) {
-        const int s = kt % STAGES;
-        const uint32_t round = kt / STAGES;
-        if (kt >= STAGES && !mbar_wait(&empty_bar[s], (round - 1) & 1, &abort_flag)) {
-          ok = false;
-          break;
+      for (int t = blockIdx.x; ok && t < args.num_tiles; t += gridDim.x) {
+        int mb, nb, bz;
+        decode_tile(t, args, mb, nb, bz);
+        for (int kt = 0; kt < num_k; ++kt, ++it) {
+          const int s = it % STAGES;
+          const uint32_t round = it / STAGES;
+          if (it >= STAGES && !mbar_wait(&empty_bar[s], (round - 1) & 1, &abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(&full_bar[s], STAGE_BYTES);
+          const int k0 = kt * BK;
+          tma_load_3d(stage_ptr(s, 0), &mapAh, &full_bar[s], k0, mb * BM, bz);
+          tma_load_3d(stage_ptr(s, 1), &mapAl, &full_bar[s], k0, mb * BM, bz);
+          tma_load_3d(stage_ptr(s, 2), &mapBh, &full_bar[s], k0, nb * BN, bz);
+          tma_load_3d(stage_ptr(s, 3), &mapBl, &full_bar[s], k0, nb * BN, bz);
         }
-        mbar_expect_tx(&full_bar[s], STAGE_BYTES);
-        const int k0 = kt * BK;
-        tma_load_3d(stage_ptr(s, 0), &mapAh, &full_bar[s], k0, tile_m * BM, bz);
-        tma_load_3d(stage_ptr(s, 1), &mapAl, &full_bar[s], k0, tile_m * BM, bz);
-        tma_load_3d(stage_ptr(s, 2), &mapBh, &full_bar[s], k0, tile_n * BN, bz);
-        tma_load_3d(stage_ptr(s, 3), &mapBl, &full_bar[s], k0, tile_n * BN, bz);
-        ++issued;
       }
       if (!ok) {
         atomicCAS(args.err, kErrNone, kErrTimeoutEmpty);
         abort_flag = 1;
-        // drain: wait (bounded) for every load this thread issued to land
-        for (int kt = (issued > STAGES ? issued - STAGES : 0); kt < issued; ++kt) {
-          int s = kt % STAGES;
+        // drain: wait (bounded) for the loads of the last STAGES issued k-tiles
+        for (int i = (it > STAGES ? it - STAGES : 0); i < it; ++i) {
+          const int s = i % STAGES;
           const uint64_t t0 = globaltimer();
-          while (!mbar_try_wait(&full_bar[s], (kt / STAGES) & 1) &&
-                 globaltimer() - t0 < kWaitNs) {
+          while (!mbar_try_wait(&full_bar[s], (i / STAGES) & 1) && globaltimer() - t0 < kWaitNs) {
           }
         }
       }
@@ -309,66 +377,95 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       // ------------------------------------------------------ MMA issuer
+      int it = 0, cc = 0;  // k-tile and chunk counters, running across tiles
       bool ok = true;
-      for (int kt = 0; kt < num_k; ++kt) {
-        const int s = kt % STAGES;
-        if (!mbar_wait(&full_bar[s], (kt / STAGES) & 1, &abort_flag)) {
-          ok = false;
-          break;
-        }
-        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint32_t a_hi = smem_u32(stage_ptr(s, 0)), a_lo = smem_u32(stage_ptr(s, 1));
-        const uint32_t b_hi = smem_u32(stage_ptr(s, 2)), b_lo = smem_u32(stage_ptr(s, 3));
+      for (int t = blockIdx.x; ok && t < args.num_tiles; t += gridDim.x) {
+        for (int kt0 = 0; ok && kt0 < num_k; kt0 += KCHUNK, ++cc) {
+          const int b = cc & 1;
+          if (cc >= 2 && !mbar_wait(&acc_empty[b], ((cc >> 1) - 1) & 1, &abort_flag)) {
+            ok = false;
+            break;
+          }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const uint32_t d_tmem = tmem_base + (uint32_t)(b * TMEM_COLS);
+          const int kend = kt0 + KCHUNK < num_k ? kt0 + KCHUNK : num_k;
+          for (int kt = kt0; kt < kend; ++kt, ++it) {
+            const int s = it % STAGES;
+            if (!mbar_wait(&full_bar[s], (it / STAGES) & 1, &abort_flag)) {
+              ok = false;
+              break;
+            }
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const uint32_t a_hi = smem_u32(stage_ptr(s, 0)), a_lo = smem_u32(stage_ptr(s, 1));
+            const uint32_t b_hi = smem_u32(stage_ptr(s, 2)), b_lo = smem_u32(stage_ptr(s, 3));
 #pragma unroll
-        for (int kk = 0; kk < BK / UMMA_K; ++kk) {
-          const uint32_t off = kk * UMMA_K * 4;  // 32 bytes per k-step inside the swizzle row
-          const uint64_t dah = smem_desc_k_sw128(a_hi + off), dal = smem_desc_k_sw128(a_lo + off);
-          const uint64_t dbh = smem_desc_k_sw128(b_hi + off), dbl = smem_desc_k_sw128(b_lo + off);
-          const uint32_t first = (kt == 0 && kk == 0) ? 0u : 1u;
-          umma_tf32(tmem_base, dal, dbh, first);  // lo * hi
-          umma_tf32(tmem_base, dah, dbl, 1u);     // hi * lo
-          umma_tf32(tmem_base, dah, dbh, 1u);     // hi * hi (largest term last)
+            for (int kk = 0; kk < BK / UMMA_K; ++kk) {
+              const uint32_t off = kk * UMMA_K * 4;  // 32 bytes per k-step in the swizzle row
+              const uint64_t dah = smem_desc_k(a_hi + off), dal = smem_desc_k(a_lo + off);
+              const uint64_t dbh = smem_desc_k(b_hi + off), dbl = smem_desc_k(b_lo + off);
+              const uint32_t first = (kt == kt0 && kk == 0) ? 0u : 1u;
+              umma_tf32(d_tmem, dal, dbh, first);  // lo * hi
+              umma_tf32(d_tmem, dah, dbl, 1u);     // hi * lo
+              umma_tf32(d_tmem, dah, dbh, 1u);     // hi * hi (largest term last)
+            }
+            umma_commit(&empty_bar[s]);
+          }
+          if (ok) umma_commit(&acc_full[b]);
         }
-        umma_commit(&empty_bar[s]);
       }
-      if (ok) {
-        umma_commit(&acc_bar);
-      } else {
+      if (!ok) {
         atomicCAS(args.err, kErrNone, kErrTimeoutFull);
         abort_flag = 1;
       }
     }
   } else {
-    // ------------------------------------------------------ epilogue (warps 2..5)
-    const int q = warp & 3;  // TMEM lane quarter this warp may access
-    bool ok = mbar_wait(&acc_bar, 0, &abort_flag);
-    if (!ok) {
-      if (lane == 0) atomicCAS(args.err, kErrNone, kErrTimeoutAcc);
-      abort_flag = 1;
-    } else {
-      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const int row = tile_m * BM + q * 32 + lane;
-      float *crow = args.C + (int64_t)bz * args.strideC + (int64_t)row * args.ldc;
-      const bool vec = ((args.ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(args.C) & 15) == 0) &&
-                       ((args.strideC & 3) == 0);
-#pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 32) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, r);
-        const int col0 = tile_n * BN + c0;
-        if (row < args.M && col0 < args.N) {
-          if (vec && col0 + 32 <= args.N) {
+    // ------------------------------------------------------ promotion + epilogue (warps 2..9)
+    const int q = warp & 3;             // TMEM lane quarter this warp may access
+    const int half = (warp - 2) >> 2;   // which 128 of the 256 columns
+    const bool vec = ((args.ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(args.C) & 15) == 0) &&
+                     ((args.strideC & 3) == 0);
+    int cc = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; ok && t < args.num_tiles; t += gridDim.x) {
+      float acc[128];
 #pragma unroll
-            for (int j = 0; j < 32; j += 4) {
-              float4 v = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
-                                     __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
-              *reinterpret_cast<float4 *>(crow + col0 + j) = v;
-            }
-          } else {
+      for (int i = 0; i < 128; ++i) acc[i] = 0.0f;
+      for (int kt0 = 0; kt0 < num_k; kt0 += KCHUNK, ++cc) {
+        const int b = cc & 1;
+        if (!mbar_wait(&acc_full[b], (cc >> 1) & 1, &abort_flag)) {
+          if (lane == 0) atomicCAS(args.err, kErrNone, kErrTimeoutAcc);
+          abort_flag = 1;
+          ok = false;
+          break;
+        }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t taddr = tmem_base + (uint32_t)(b * TMEM_COLS + half * 128) +
+                               ((uint32_t)(q * 32) << 16);
 #pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (col0 + j < args.N) crow[col0 + j] = __uint_as_float(r[j]);
-          }
+        for (int c0 = 0; c0 < 128; c0 += 32) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(taddr + (uint32_t)c0, r);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) acc[c0 + i] = __fadd_rn(acc[c0 + i], __uint_as_float(r[i]));
+        }
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        mbar_arrive(&acc_empty[b]);
+      }
+      if (!ok) break;
+      int mb, nb, bz;
+      decode_tile(t, args, mb, nb, bz);
+      const int row = mb * BM + q * 32 + lane;
+      const int col0 = nb * BN + half * 128;
+      if (row < args.M && col0 < args.N) {
+        float *crow = args.C + (int64_t)bz * args.strideC + (int64_t)row * args.ldc + col0;
+        if (vec && col0 + 128 <= args.N) {
+#pragma unroll
+          for (int i = 0; i < 128; i += 4)
+            *reinterpret_cast<float4 *>(crow + i) = make_float4(acc[i], acc[i + 1], acc[i + 2], acc[i + 3]);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 128; ++i)
+            if (col0 + i < args.N) crow[i] = acc[i];
         }
       }
     }
@@ -379,7 +476,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (warp == 1) {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
-                 "r"(TMEM_COLS)
+                 "r"(2 * TMEM_COLS)
                  : "memory");
   }
 }
@@ -404,32 +501,67 @@ int get_encoder() {
   return rc;
 }
 
-// 3D map over a [batch, rows, kp] plane (K innermost), box {BK, box_rows, 1}.
-int make_map(CUtensorMap *map, const float *base, int64_t rows, int64_t K, int64_t kp,
+// 3D map over a [batch, rows, K] operand (K innermost, row pitch ld floats, batch
+// pitch sb floats), box {BK, box_rows, 1}. TMA needs ld*4 and sb*4 to be multiples
+// of 16 bytes and the base 16-byte aligned.
+int make_map(CUtensorMap *map, const float *base, int64_t rows, int64_t K, int64_t ld, int64_t sb,
              int64_t batch, int box_rows) {
+  if (batch == 1) sb = ld * rows;
   cuuint64_t dims[3] = {(cuuint64_t)K, (cuuint64_t)rows, (cuuint64_t)batch};
-  cuuint64_t strides[2] = {(cuuint64_t)(kp * 4), (cuuint64_t)(kp * rows * 4)};
+  cuuint64_t strides[2] = {(cuuint64_t)(ld * 4), (cuuint64_t)(sb * 4)};
   cuuint32_t box[3] = {(cuuint32_t)BK, (cuuint32_t)box_rows, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, (void *)base, dims, strides, box,
-                        estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        SWIZZLE_BYTES == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return fz::fail(FZ_ERR_CUDA, "cuTensorMapEncodeTiled failed with code " + std::to_string((int)r));
   return FZ_OK;
 }
 
-int split(const float *src, int64_t ld, int64_t sb, bool trans, int64_t rows, int64_t K,
-          int64_t kp, int64_t batch, float *hi, float *lo, cudaStream_t s) {
-  if (!trans) {
-    unsigned grid = fz::grid_for(batch * rows * kp, 256, 8, 4);
-    split_kernel<<<grid, 256, 0, s>>>(src, ld, sb, rows, K, kp, batch, hi, lo);
-  } else {
-    int64_t tiles = batch * ((rows + 31) / 32) * ((kp + 31) / 32);
-    unsigned grid = fz::grid_for(tiles, 1, 8, 4);
-    split_t_kernel<<<grid, 256, 0, s>>>(src, ld, sb, rows, K, kp, batch, hi, lo);
+// One operand as the (hi, lo) pair the kernel reads, both [batch, rows, K] K-major.
+struct Operand {
+  const float *hi;
+  int64_t hi_ld, hi_sb;
+  float *lo;  // plane at pitch kp
+};
+
+// Plane floats an operand needs in the workspace (lo always; hi unless the source
+// is K-major and TMA-addressable).
+bool direct_hi(const float *src, int64_t ld, int64_t sb, bool kmajor, int64_t batch) {
+  return kmajor && ld % 4 == 0 && ((uintptr_t)src & 15) == 0 && (batch == 1 || (sb > 0 && sb % 4 == 0));
+}
+
+int prepare(const float *src, int64_t ld, int64_t sb, bool kmajor, int64_t rows, int64_t K,
+            int64_t kp, int64_t batch, float *ws, Operand *op, cudaStream_t s) {
+  const int64_t plane = batch * rows * kp;
+  op->lo = ws;
+  if (kmajor) {
+    const bool direct = direct_hi(src, ld, sb, kmajor, batch);
+    float *hi = direct ? nullptr : ws + plane;
+    unsigned grid = fz::grid_for(plane / 4 + 1, 256, 8, 4);
+    lo_kernel<<<grid, 256, 0, s>>>(src, ld, sb, rows, K, kp, batch, op->lo, hi);
+    FZ_CHECK_LAUNCH();
+    if (direct) {
+      op->hi = src;
+      op->hi_ld = ld;
+      op->hi_sb = sb;
+    } else {
+      op->hi = hi;
+      op->hi_ld = kp;
+      op->hi_sb = rows * kp;
+    }
+    return FZ_OK;
   }
+  float *hi = ws + plane;
+  int64_t tiles = batch * ((rows + 31) / 32) * ((kp + 31) / 32);
+  unsigned grid = fz::grid_for(tiles, 1, 8, 4);
+  split_t_kernel<<<grid, 256, 0, s>>>(src, ld, sb, rows, K, kp, batch, hi, op->lo);
   FZ_CHECK_LAUNCH();
+  op->hi = hi;
+  op->hi_ld = kp;
+  op->hi_sb = rows * kp;
   return FZ_OK;
 }
 
@@ -460,21 +592,25 @@ extern "C" int fz_gemm_f32(int64_t batch, int64_t M, int64_t N, int64_t K, const
   if (rc) return rc;
 
   const int64_t kp = (K + 3) & ~(int64_t)3;  // 16-byte row pitch for TMA
-  const int64_t a_elems = batch * M * kp, b_elems = batch * N * kp;
+  const bool a_km = transA == 0, b_km = transB != 0;  // A as [M,K], B as [N,K]
+  const int64_t a_plane = batch * M * kp, b_plane = batch * N * kp;
+  const int64_t a_need = a_plane * (direct_hi(A, lda, strideA, a_km, batch) ? 1 : 2);
+  const int64_t b_need = b_plane * (direct_hi(B, ldb, strideB, b_km, batch) ? 1 : 2);
   float *ws = nullptr;
-  rc = fz_malloc((void **)&ws, sizeof(float) * 2 * (a_elems + b_elems), s);
+  rc = fz_malloc((void **)&ws, sizeof(float) * (a_need + b_need), s);
   if (rc) return rc;
-  float *a_hi = ws, *a_lo = ws + a_elems, *b_hi = ws + 2 * a_elems, *b_lo = b_hi + b_elems;
-  // A as [M, K] K-major: transpose when A is given as [K, M]
-  rc = split(A, lda, strideA, transA != 0, M, K, kp, batch, a_hi, a_lo, s);
-  // B as [N, K] K-major: transpose when B is given as [K, N]
-  if (!rc) rc = split(B, ldb, strideB, transB == 0, N, K, kp, batch, b_hi, b_lo, s);
+  Operand oa{}, ob{};
+  rc = prepare(A, lda, strideA, a_km, M, K, kp, batch, ws, &oa, s);
+  if (!rc) rc = prepare(B, ldb, strideB, b_km, N, K, kp, batch, ws + a_need, &ob, s);
 
   CUtensorMap mAh, mAl, mBh, mBl;
-  if (!rc) rc = make_map(&mAh, a_hi, M, K, kp, batch, BM);
-  if (!rc) rc = make_map(&mAl, a_lo, M, K, kp, batch, BM);
-  if (!rc) rc = make_map(&mBh, b_hi, N, K, kp, batch, BN);
-  if (!rc) rc = make_map(&mBl, b_lo, N, K, kp, batch, BN);
+  if (!rc) rc = make_map(&mAh, oa.hi, M, K, oa.hi_ld, oa.hi_sb, batch, BM);
+  if (!rc) rc = make_map(&mAl, oa.lo, M, K, kp, M * kp, batch, BM);
+  if (!rc) rc = make_map(&mBh, ob.hi, N, K, ob.hi_ld, ob.hi_sb, batch, BN);
+  if (!rc) rc = make_map(&mBl, ob.lo, N, K, kp, N * kp, batch, BN);
+  const int tiles_m = (int)((M + BM - 1) / BM), tiles_n = (int)((N + BN - 1) / BN);
+  const int64_t num_tiles = (int64_t)tiles_m * tiles_n * batch;
+  if (!rc && num_tiles >= (1ll << 31)) rc = fz::fail(FZ_ERR_INVALID, "fz_gemm_f32: too many tiles");
 
   int *err = nullptr;
   if (!rc) rc = fz::device_error_word(&err);
@@ -488,8 +624,9 @@ extern "C" int fz_gemm_f32(int64_t batch, int64_t M, int64_t N, int64_t K, const
                            (int)smem);
       attr_done[dev] = true;
     }
-    GemmArgs ga{C, ldc, strideC, (int)M, (int)N, (int)K, (int)batch, err};
-    dim3 grid((unsigned)((N + BN - 1) / BN), (unsigned)((M + BM - 1) / BM), (unsigned)batch);
+    GemmArgs ga{C, ldc, strideC, (int)M, (int)N, (int)K, (int)batch,
+                tiles_m, tiles_n, (int)num_tiles, tiles_m < 16 ? tiles_m : 16, err};
+    const unsigned grid = (unsigned)(num_tiles < fz::num_sms() ? num_tiles : fz::num_sms());
     gemm_3xtf32_kernel<<<grid, NUM_THREADS, smem, s>>>(mAh, mAl, mBh, mBl, ga);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) rc = fz::cuda_fail(e, "gemm_3xtf32_kernel launch", __FILE__, __LINE__);

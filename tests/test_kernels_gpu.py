@@ -173,7 +173,8 @@ def _gemm(capi, a, b, transA=False, transB=False):
 
 @pytest.mark.parametrize("batch,M,N,K", [(1, 128, 256, 32), (1, 256, 512, 256), (1, 200, 300, 70),
                                          (1, 1, 5, 3), (3, 65, 33, 17), (1, 512, 512, 1024),
-                                         (2, 1000, 129, 257)])
+                                         (2, 1000, 129, 257), (1, 256, 512, 4096),
+                                         (1, 160, 300, 16384)])
 @pytest.mark.parametrize("tA,tB", [(False, False), (False, True), (True, False), (True, True)])
 def test_gemm_3xtf32(capi, port, batch, M, N, K, tA, tB):
     s = 1.0 / np.sqrt(K)
@@ -187,6 +188,19 @@ def test_gemm_3xtf32(capi, port, batch, M, N, K, tA, tB):
     assert err <= 1e-5, err
     bound = np.einsum("bmk,bkn->bmn", np.abs(A.astype(np.float64)), np.abs(B.astype(np.float64)))
     assert np.all(np.abs(got - want) <= 1e-5 * bound + 1e-30)
+
+
+@pytest.mark.parametrize("M,N,K", [(256, 256, 65536), (4096, 16, 8192)])
+def test_gemm_3xtf32_long_k(capi, port, M, N, K):
+    """The weight-gradient shapes of the MLP step (K = batch rows) hold 1e-5 too."""
+    s = 1.0 / np.sqrt(K)
+    A = (RNG.standard_normal((1, K, M)) * s).astype(np.float32)  # given transposed, as x^T
+    B = (RNG.standard_normal((1, K, N)) * s).astype(np.float32)
+    got = _gemm(capi, A, B, True, False)
+    # the oracle's double-accumulation product, via float64 BLAS for speed at this K
+    want = (A[0].astype(np.float64).T @ B[0].astype(np.float64))[None]
+    err = np.linalg.norm((got - want).ravel()) / np.linalg.norm(want.ravel())
+    assert err <= 1e-5, err
 
 
 def _program(nodes, nleaves, outs):
