@@ -347,8 +347,13 @@ def run_ours(args):
     d.barrier()
     ms = d.max(ms_local) / args.steps
 
+    clk = clocks.stop()  # sampled over the device-timed steps (the e2e leg syncs every step)
+
     # end to end: host inputs copied in each step, loss read back each step
     h2d = Xp.nbytes + Yp.nbytes
+    x = model.tensor(Xp, True)  # one untimed end-to-end step compiles the read-back program
+    y = model.tensor(Yp, True)
+    model.step(x, y, LR, comm).mean().to_numpy()
     d.barrier()
     F.synchronize()
     timer.start()
@@ -359,7 +364,6 @@ def run_ours(args):
         loss.mean().to_numpy()
     e2e_local = timer.stop_ms()
     F.synchronize()
-    clk = clocks.stop()
     d.barrier()
     e2e_ms = d.max(e2e_local) / args.steps
 

@@ -256,8 +256,10 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)
 struct GemmArgs {
   float *C;
   int64_t ldc, strideC;
+  int64_t split_stride;  // floats between the partial outputs of consecutive K splits
   int M, N, K, batch;
-  int tiles_m, tiles_n, num_tiles, group_m;
+  int tiles_m, tiles_n, num_tiles, group_m;  // num_tiles counts work units (tiles x K splits)
+  int splits, k_per_split;  // K is cut into `splits` ranges of k_per_split (multiple of BK)
   int *err;
 };
 
@@ -265,11 +267,15 @@ __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
-// Tile t -> (m block, n block, batch) in grouped order: within a batch, bands of
-// group_m row blocks are walked column by column, so the tiles in flight on the
-// 148 SMs share A rows and B columns in L2.
-__device__ __forceinline__ void decode_tile(int t, const GemmArgs &a, int &mb, int &nb, int &bz) {
+// Work unit t -> (K split, batch, m block, n block). Units of one K split are
+// consecutive; within a batch, bands of group_m row blocks are walked column by
+// column, so the units in flight on the 148 SMs share A rows and B columns in L2.
+__device__ __forceinline__ void decode_tile(int t, const GemmArgs &a, int &mb, int &nb, int &bz,
+                                            int &ks) {
   const int per_batch = a.tiles_m * a.tiles_n;
+  const int per_split = per_batch * a.batch;  // units of one K split
+  ks = t / per_split;
+  t -= ks * per_split;
   bz = t / per_batch;
   const int r = t - bz * per_batch;
   const int band = r / (a.group_m * a.tiles_n);
@@ -278,6 +284,13 @@ __device__ __forceinline__ void decode_tile(int t, const GemmArgs &a, int &mb, i
   const int in_band = r - band * a.group_m * a.tiles_n;
   mb = first_m + in_band % rows;
   nb = in_band / rows;
+}
+
+// k-tiles of unit `ks`: [ks * k_per_split, min(K, (ks + 1) * k_per_split)).
+__device__ __forceinline__ int unit_k_tiles(const GemmArgs &a, int ks, int &k_begin) {
+  k_begin = ks * a.k_per_split;
+  const int k_end = min(a.K, k_begin + a.k_per_split);
+  return (k_end - k_begin + BK - 1) / BK;
 }
 
 // Persistent kernel: one CTA per SM walks tiles blockIdx.x, +gridDim.x, ...
@@ -299,7 +312,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   __shared__ volatile int abort_flag;
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int num_k = (args.K + BK - 1) / BK;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -345,9 +357,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       int it = 0;
       bool ok = true;
       for (int t = blockIdx.x; ok && t < args.num_tiles; t += gridDim.x) {
-        int mb, nb, bz;
-        decode_tile(t, args, mb, nb, bz);
-        for (int kt = 0; kt < num_k; ++kt, ++it) {
+        int mb, nb, bz, ks, kb;
+        decode_tile(t, args, mb, nb, bz, ks);
+        const int nk = unit_k_tiles(args, ks, kb);
+        for (int kt = 0; kt < nk; ++kt, ++it) {
           const int s = it % STAGES;
           const uint32_t round = it / STAGES;
           if (it >= STAGES && !mbar_wait(&empty_bar[s], (round - 1) & 1, &abort_flag)) {
@@ -355,7 +368,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             break;
           }
           mbar_expect_tx(&full_bar[s], STAGE_BYTES);
-          const int k0 = kt * BK;
+          const int k0 = kb + kt * BK;
           tma_load_3d(stage_ptr(s, 0), &mapAh, &full_bar[s], k0, mb * BM, bz);
           tma_load_3d(stage_ptr(s, 1), &mapAl, &full_bar[s], k0, mb * BM, bz);
           tma_load_3d(stage_ptr(s, 2), &mapBh, &full_bar[s], k0, nb * BN, bz);
@@ -380,6 +393,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       int it = 0, cc = 0;  // k-tile and chunk counters, running across tiles
       bool ok = true;
       for (int t = blockIdx.x; ok && t < args.num_tiles; t += gridDim.x) {
+        int mb, nb, bz, ks, kb;
+        decode_tile(t, args, mb, nb, bz, ks);
+        const int num_k = unit_k_tiles(args, ks, kb);
         for (int kt0 = 0; ok && kt0 < num_k; kt0 += KCHUNK, ++cc) {
           const int b = cc & 1;
           if (cc >= 2 && !mbar_wait(&acc_empty[b], ((cc >> 1) - 1) & 1, &abort_flag)) {
@@ -427,6 +443,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     int cc = 0;
     bool ok = true;
     for (int t = blockIdx.x; ok && t < args.num_tiles; t += gridDim.x) {
+      int mb, nb, bz, ks, kb;
+      decode_tile(t, args, mb, nb, bz, ks);
+      const int num_k = unit_k_tiles(args, ks, kb);
       float acc[128];
 #pragma unroll
       for (int i = 0; i < 128; ++i) acc[i] = 0.0f;
@@ -452,12 +471,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         mbar_arrive(&acc_empty[b]);
       }
       if (!ok) break;
-      int mb, nb, bz;
-      decode_tile(t, args, mb, nb, bz);
       const int row = mb * BM + q * 32 + lane;
       const int col0 = nb * BN + half * 128;
       if (row < args.M && col0 < args.N) {
-        float *crow = args.C + (int64_t)bz * args.strideC + (int64_t)row * args.ldc + col0;
+        float *crow = args.C + (int64_t)ks * args.split_stride + (int64_t)bz * args.strideC +
+                      (int64_t)row * args.ldc + col0;
         if (vec && col0 + 128 <= args.N) {
 #pragma unroll
           for (int i = 0; i < 128; i += 4)
@@ -518,6 +536,35 @@ int make_map(CUtensorMap *map, const float *base, int64_t rows, int64_t K, int64
   if (r != CUDA_SUCCESS)
     return fz::fail(FZ_ERR_CUDA, "cuTensorMapEncodeTiled failed with code " + std::to_string((int)r));
   return FZ_OK;
+}
+
+int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
+
+// Number of K splits for a GEMM of `tiles` output tiles. A split turns one tile
+// into several units over K ranges (multiples of the 256-wide promotion chunk, at
+// least 1024 long) whose fp32 partials are summed afterwards; it pays when the
+// tiles fill the 148 SMs poorly (weight gradients: few tiles, K = batch rows).
+// Cost model in units of one tile's time per k: waves * K_per_unit, plus the
+// partials' write and read at HBM speed.
+int choose_splits(int64_t tiles, int64_t M, int64_t N, int64_t K, int64_t batch) {
+  const int64_t sms = fz::num_sms();
+  const double k_time = 2.65e-8;  // s per k of one 128x256 tile (3 TF32 MMAs at ~1.1 PFLOP/s per GPU)
+  int best = 1;
+  double best_t = 1e300;
+  const int cand[] = {1, 2, 3, 4, 6, 8, 12, 16, 24, 32};
+  for (int sp : cand) {
+    const int64_t kps = sp == 1 ? K : round_up((K + sp - 1) / sp, (int64_t)BK * KCHUNK);
+    if (sp > 1 && kps < 1024) break;
+    const int64_t real = (K + kps - 1) / kps;
+    const int64_t waves = (tiles * real + sms - 1) / sms;
+    double t = (double)waves * (double)kps;
+    if (real > 1) t += (double)(real * batch * M * N) * 8.0 / 6.0e12 / k_time;
+    if (t < best_t * 0.97) {
+      best_t = t;
+      best = (int)real;
+    }
+  }
+  return best;
 }
 
 // One operand as the (hi, lo) pair the kernel reads, both [batch, rows, K] K-major.
@@ -609,8 +656,16 @@ extern "C" int fz_gemm_f32(int64_t batch, int64_t M, int64_t N, int64_t K, const
   if (!rc) rc = make_map(&mBh, ob.hi, N, K, ob.hi_ld, ob.hi_sb, batch, BN);
   if (!rc) rc = make_map(&mBl, ob.lo, N, K, kp, N * kp, batch, BN);
   const int tiles_m = (int)((M + BM - 1) / BM), tiles_n = (int)((N + BN - 1) / BN);
-  const int64_t num_tiles = (int64_t)tiles_m * tiles_n * batch;
-  if (!rc && num_tiles >= (1ll << 31)) rc = fz::fail(FZ_ERR_INVALID, "fz_gemm_f32: too many tiles");
+  const int64_t tiles = (int64_t)tiles_m * tiles_n * batch;
+  const bool dense_c = ldc == N && (batch == 1 || strideC == M * N);
+  const int splits = dense_c ? choose_splits(tiles, M, N, K, batch) : 1;
+  const int64_t kps = splits > 1 ? round_up((K + splits - 1) / splits, (int64_t)BK * KCHUNK) : K;
+  const int real_splits = (int)((K + kps - 1) / kps);
+  const int64_t num_units = tiles * real_splits;
+  if (!rc && num_units >= (1ll << 31)) rc = fz::fail(FZ_ERR_INVALID, "fz_gemm_f32: too many tiles");
+  float *partial = nullptr;
+  if (!rc && real_splits > 1)
+    rc = fz_malloc((void **)&partial, sizeof(float) * real_splits * batch * M * N, s);
 
   int *err = nullptr;
   if (!rc) rc = fz::device_error_word(&err);
@@ -624,14 +679,19 @@ extern "C" int fz_gemm_f32(int64_t batch, int64_t M, int64_t N, int64_t K, const
                            (int)smem);
       attr_done[dev] = true;
     }
-    GemmArgs ga{C, ldc, strideC, (int)M, (int)N, (int)K, (int)batch,
-                tiles_m, tiles_n, (int)num_tiles, tiles_m < 16 ? tiles_m : 16, err};
-    const unsigned grid = (unsigned)(num_tiles < fz::num_sms() ? num_tiles : fz::num_sms());
+    GemmArgs ga{partial ? partial : C, partial ? N : ldc, partial ? M * N : strideC,
+                batch * M * N, (int)M, (int)N, (int)K, (int)batch,
+                tiles_m, tiles_n, (int)num_units, tiles_m < 16 ? tiles_m : 16,
+                real_splits, (int)kps, err};
+    const unsigned grid = (unsigned)(num_units < fz::num_sms() ? num_units : fz::num_sms());
     gemm_3xtf32_kernel<<<grid, NUM_THREADS, smem, s>>>(mAh, mAl, mBh, mBl, ga);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) rc = fz::cuda_fail(e, "gemm_3xtf32_kernel launch", __FILE__, __LINE__);
     else fz::note_launch();
+    // K-split partials: summed over the splits in a fixed order (deterministic)
+    if (!rc && partial) rc = fz_reduce(FZ_RSUM, C, partial, 1, real_splits, batch * M * N, s);
   }
+  if (partial) fz_free(partial, s);
   fz_free(ws, s);
   return rc;
 }

@@ -139,12 +139,14 @@ static std::vector<size_t> broadcast_shape(const std::vector<size_t> &a, const s
 
 // Element strides of a contiguous operand of shape `s` seen from output shape
 // `out`: 0 on broadcast dims (TensorPlan.cpp:50-65).
+// An operand with more dims than `out` (a flat-prefix evaluation, below) sits at
+// index 0 along its extra leading dims.
 static void operand_strides(const std::vector<size_t> &s, const std::vector<size_t> &out,
                             int64_t *st) {
-  size_t nd = out.size(), pad = nd - s.size();
+  const long nd = (long)out.size(), pad = nd - (long)s.size();
   int64_t r = 1;
   for (long d = (long)nd - 1; d >= 0; --d) {
-    long i = d - (long)pad;
+    long i = d - pad;
     if (i < 0) {
       st[d] = 0;
       continue;
@@ -286,6 +288,24 @@ static bool try_single_op(Expr *e, float *out_ptr) {
     return true;
   }
   return false;
+}
+
+// Values at flat indices [0, prod(shape[k:])) of a pending node, i.e. the slice
+// at index 0 of its first k dims, lowered into a fresh buffer.
+static std::shared_ptr<DeviceBuffer> materialize_prefix(const ExprPtr &ep, size_t k) {
+  std::vector<size_t> sub(ep->shape.begin() + (long)k, ep->shape.end());
+  size_t n = 1;
+  for (auto v : sub) n *= v;
+  auto out = std::make_shared<DeviceBuffer>(n);
+  if (n == 0) return out;
+  Lowering L;
+  int root = L.visit(ep.get());
+  if (L.overflow) return nullptr;
+  L.prog.num_leaves = (int32_t)L.leaves.size();
+  L.prog.num_outputs = 1;
+  L.prog.out_node[0] = root;
+  launch_program(L, sub, out->ptr);
+  return out;
 }
 
 void materialize(const ExprPtr &ep) {
@@ -620,7 +640,23 @@ void sub_inplace(RawTensor &x, const RawTensor &y) {
   const size_t n = x.size();
   FB_CHECK(y.size() >= n, "sub_inplace: right-hand side has fewer elements than the tensor");
   const float *px = x.data();
-  const float *py = y.data();
+  // Only y's first n values are read. When y is pending and those values are the
+  // slice at index 0 of its leading dims (the [U] bias minus row 0 of a [B, U]
+  // gradient), lower just that slice instead of all of y.
+  std::shared_ptr<DeviceBuffer> prefix;
+  if (y.pending() && y.size() > n) {
+    const auto &ys = y.shape();
+    size_t tail = 1;
+    for (size_t k = ys.size(); k-- > 0;) {
+      tail *= ys[k];
+      if (tail == n) {
+        prefix = materialize_prefix(y.expr(), k);
+        break;
+      }
+      if (tail > n) break;
+    }
+  }
+  const float *py = prefix ? prefix->ptr : y.data();
   auto buf = std::make_shared<DeviceBuffer>(n);
   fz_check(fz_ewise_binary_contig(FZ_SUB, (int64_t)n, buf->ptr, px, py, nullptr),
            "fz_ewise_binary_contig");
