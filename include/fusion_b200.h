@@ -72,13 +72,20 @@ void *fz_default_stream(void);
 int fz_stream_sync(void *stream);
 int fz_device_sync(void);
 
-/* Stream-ordered device memory from the device's pool (cudaMallocAsync with the
- * release threshold raised so freed blocks are reused, not returned).
+/* Stream-ordered device memory. fz_free puts the block on a free list of `stream`
+ * (the block may be reused by work ordered after that point on `stream`); the next
+ * fz_malloc of the same size class on that stream takes it back without a driver
+ * call. Misses go to the device's pool (cudaMallocAsync, release threshold raised).
  * Replaces PoolAllocator::allocate/deallocate
- * (fusion/src/Fusion/alloc/BFCPoolAllocator.cpp:59-111) for tensor storage. */
+ * (fusion/src/Fusion/alloc/BFCPoolAllocator.cpp:59-111) for tensor storage.
+ * fz_free of a pointer fz_malloc did not return fails with FZ_ERR_INVALID. */
 int fz_malloc(void **ptr, size_t bytes, void *stream);
 int fz_free(void *ptr, void *stream);
-/* Bytes currently held by this device's pool (used and cached). */
+/* Return the current device's cached blocks to the driver and trim its pool
+ * (synchronises the device). fz_malloc does this by itself before it reports OOM. */
+int fz_pool_release(void);
+/* reserved: bytes the current device's pool holds (in use, cached or pool-internal);
+ * used: bytes handed out by fz_malloc and not freed yet. */
 int fz_pool_stats(size_t *reserved, size_t *used);
 
 /* Copies. d2h waits for the stream so the host buffer is valid on return.

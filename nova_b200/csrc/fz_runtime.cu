@@ -4,6 +4,8 @@
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <unordered_map>
+#include <vector>
 
 #include "fz_common.cuh"
 
@@ -200,25 +202,137 @@ int fz_device_sync(void) {
   return FZ_OK;
 }
 
+// Block cache in front of the stream-ordered pool, in the role of Fusion's
+// PoolAllocator (fusion/src/Fusion/alloc/BFCPoolAllocator.cpp:59-111). A freed
+// block goes onto a free list keyed by (stream, size class); the next allocation
+// of that class on the same stream takes it back without calling the driver. Work
+// on one stream runs in order, so a block reused on the stream it was freed on
+// needs no event. A training step allocates the same sizes every step, so in the
+// steady state no allocation reaches cudaMallocAsync; that call can block the host
+// for tens to hundreds of milliseconds in the driver while it maps pool pages,
+// long enough to leave the GPU idle behind it.
+namespace {
+struct FreeLists {
+  int device = 0;
+  std::unordered_map<size_t, std::vector<void *>> by_size;
+};
+struct LiveBlock {
+  size_t size;
+  int device;
+};
+std::mutex g_cache_mu;
+std::unordered_map<void *, LiveBlock> g_live;
+std::unordered_map<cudaStream_t, FreeLists> g_free;
+size_t g_live_bytes[fz::kMaxDevices] = {};
+size_t g_cached_bytes[fz::kMaxDevices] = {};
+
+// Size classes: 512 B granules below 1 MiB, 2 MiB granules above (the driver
+// pool maps in 2 MiB pages, so a larger granule wastes nothing there).
+size_t size_class(size_t bytes) {
+  const size_t small = 512, large = (size_t)2 << 20;
+  return bytes < ((size_t)1 << 20) ? (bytes + small - 1) / small * small
+                                   : (bytes + large - 1) / large * large;
+}
+
+// Give every cached block of `device` back to the driver pool and trim the pool.
+// The device is synchronised first, so the blocks can be freed on any stream.
+int release_cached(int device) {
+  std::vector<void *> blocks;
+  {
+    std::lock_guard<std::mutex> lk(g_cache_mu);
+    for (auto it = g_free.begin(); it != g_free.end();) {
+      if (it->second.device != device) {
+        ++it;
+        continue;
+      }
+      for (auto &kv : it->second.by_size)
+        for (void *p : kv.second) blocks.push_back(p);
+      it = g_free.erase(it);
+    }
+    g_cached_bytes[device] = 0;
+  }
+  int prev = 0;
+  FZ_CUDA(cudaGetDevice(&prev));
+  FZ_CUDA(cudaSetDevice(device));
+  cudaStream_t s = fz::resolve(nullptr);
+  cudaError_t e = cudaDeviceSynchronize();
+  for (void *p : blocks)
+    if (e == cudaSuccess) e = cudaFreeAsync(p, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  cudaMemPool_t pool;
+  if (e == cudaSuccess) e = cudaDeviceGetDefaultMemPool(&pool, device);
+  if (e == cudaSuccess) e = cudaMemPoolTrimTo(pool, 0);
+  cudaSetDevice(prev);
+  if (e != cudaSuccess) return fz::cuda_fail(e, "releasing cached device blocks", __FILE__, __LINE__);
+  return FZ_OK;
+}
+}  // namespace
+
 int fz_malloc(void **ptr, size_t bytes, void *stream) {
   FZ_REQUIRE(ptr, "fz_malloc: null pointer");
   *ptr = nullptr;
   if (bytes == 0) return FZ_OK;
-  // round to 256 B so every allocation can feed 128-bit and TMA accesses
-  size_t rounded = (bytes + 255) & ~(size_t)255;
-  cudaError_t e = cudaMallocAsync(ptr, rounded, resolve(stream));
+  // size classes are multiples of 512 B, so every block can feed 128-bit and TMA accesses
+  const size_t sz = size_class(bytes);
+  cudaStream_t s = resolve(stream);
+  int d = current_device();
+  {
+    std::lock_guard<std::mutex> lk(g_cache_mu);
+    auto it = g_free.find(s);
+    if (it != g_free.end()) {
+      auto jt = it->second.by_size.find(sz);
+      if (jt != it->second.by_size.end() && !jt->second.empty()) {
+        void *p = jt->second.back();
+        jt->second.pop_back();
+        g_cached_bytes[d] -= sz;
+        g_live.emplace(p, LiveBlock{sz, d});
+        g_live_bytes[d] += sz;
+        *ptr = p;
+        return FZ_OK;
+      }
+    }
+  }
+  cudaError_t e = cudaMallocAsync(ptr, sz, s);
+  if (e == cudaErrorMemoryAllocation) {
+    // the pool is full: hand the cached blocks back and try once more
+    cudaGetLastError();
+    int rc = release_cached(d);
+    if (rc) return rc;
+    e = cudaMallocAsync(ptr, sz, s);
+  }
   if (e != cudaSuccess) {
     cudaGetLastError();
+    *ptr = nullptr;
     return fail(FZ_ERR_OOM, "device allocation of " + std::to_string(bytes) +
                                 " bytes failed: " + cudaGetErrorString(e));
   }
+  std::lock_guard<std::mutex> lk(g_cache_mu);
+  g_live.emplace(*ptr, LiveBlock{sz, d});
+  g_live_bytes[d] += sz;
   return FZ_OK;
 }
 
 int fz_free(void *ptr, void *stream) {
   if (!ptr) return FZ_OK;
-  FZ_CUDA(cudaFreeAsync(ptr, resolve(stream)));
+  cudaStream_t s = resolve(stream);
+  std::lock_guard<std::mutex> lk(g_cache_mu);
+  auto it = g_live.find(ptr);
+  FZ_REQUIRE(it != g_live.end(), "fz_free: pointer was not returned by fz_malloc or was freed already");
+  const LiveBlock b = it->second;
+  g_live.erase(it);
+  g_live_bytes[b.device] -= b.size;
+  FreeLists &fl = g_free[s];
+  fl.device = b.device;
+  fl.by_size[b.size].push_back(ptr);
+  g_cached_bytes[b.device] += b.size;
   return FZ_OK;
+}
+
+int fz_pool_release(void) {
+  int d = 0;
+  FZ_CUDA(cudaGetDevice(&d));
+  FZ_REQUIRE(d < kMaxDevices, "fz_pool_release: device index out of range");
+  return release_cached(d);
 }
 
 int fz_pool_stats(size_t *reserved, size_t *used) {
@@ -226,11 +340,13 @@ int fz_pool_stats(size_t *reserved, size_t *used) {
   FZ_CUDA(cudaGetDevice(&d));
   cudaMemPool_t pool;
   FZ_CUDA(cudaDeviceGetDefaultMemPool(&pool, d));
-  uint64_t r = 0, u = 0;
+  uint64_t r = 0;
   FZ_CUDA(cudaMemPoolGetAttribute(pool, cudaMemPoolAttrReservedMemCurrent, &r));
-  FZ_CUDA(cudaMemPoolGetAttribute(pool, cudaMemPoolAttrUsedMemCurrent, &u));
   if (reserved) *reserved = r;
-  if (used) *used = u;
+  if (used) {
+    std::lock_guard<std::mutex> lk(g_cache_mu);
+    *used = d < kMaxDevices ? g_live_bytes[d] : 0;
+  }
   return FZ_OK;
 }
 

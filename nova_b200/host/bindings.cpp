@@ -283,6 +283,8 @@ PYBIND11_MODULE(fusion, m) {
   m.def("set_fusion", &set_fusion_enabled, py::arg("enabled"),
         "Enable (default) or disable lazy elementwise fusion.");
   m.def("fusion_enabled", &fusion_enabled);
+  m.def("empty_cache", []() { fz_check(fz_pool_release(), "fz_pool_release"); },
+        "Return this device's cached blocks to the driver (synchronises the device).");
   m.def("flush", [](const T &t) { t.raw().data(); }, py::arg("tensor"),
         "Lower a pending tensor to device memory now.");
   m.def("stats", []() {

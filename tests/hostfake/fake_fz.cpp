@@ -89,6 +89,7 @@ int fz_malloc(void **p, size_t bytes, void *) {
   return *p ? FZ_OK : fail(FZ_ERR_OOM, "host allocation failed");
 }
 int fz_free(void *p, void *) { std::free(p); return FZ_OK; }
+int fz_pool_release(void) { return FZ_OK; }
 int fz_pool_stats(size_t *r, size_t *u) { if (r) *r = 0; if (u) *u = 0; return FZ_OK; }
 int fz_memcpy_h2d(void *d, const void *s, size_t n, void *) { if (n) std::memcpy(d, s, n); return FZ_OK; }
 int fz_memcpy_d2h(void *d, const void *s, size_t n, void *) { if (n) std::memcpy(d, s, n); return FZ_OK; }
