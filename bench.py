@@ -53,7 +53,7 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--kernel", default=None,
                     help="run one hot-path kernel on a profiling-sized case instead of the step "
-                         "(gemm, add, bcast_add, exp, sum_ax0, sum_ax1, swapaxes, bias_relu)")
+                         "(gemm, gemm_wgrad, add, bcast_add, exp, sum_ax0, sum_ax1, swapaxes, bias_relu)")
     ap.add_argument("--reps", type=int, default=3)
     return ap.parse_args()
 
@@ -223,32 +223,47 @@ def kernel_suite(capi, pk):
     shp = (C.c_int64 * 2)(r, r)
     rec("swapaxes_16384^2", time_launch(A, lambda: A.check(L.fz_swapaxes(o.ptr, a.ptr, shp, 2, 0, 1, None))),
         8 * r * r)
-    g = 8192
-    x, y, c = A.DeviceArray((g, g)), A.DeviceArray((g, g)), A.DeviceArray((g, g))
-    A.check(L.fz_fill_f32(x.ptr, C.c_float(0.01), g * g, None))
-    A.check(L.fz_fill_f32(y.ptr, C.c_float(0.02), g * g, None))
-    ms = time_launch(A, lambda: A.check(L.fz_gemm_f32(1, g, g, g, x.ptr, g, 0, 0, y.ptr, g, 0, 0,
-                                                      c.ptr, g, 0, None)), reps=5, warm=2)
-    tf = 2 * g ** 3 / ms / 1e9
-    out["gemm_3xtf32_8192^3"] = {"ms": round(ms, 3), "TFLOP/s": round(tf, 1),
-                                 "tensor_pipe_TFLOP/s": round(3 * tf, 1)}
-    for arr in (a, b, o, x, y, c):
+    for arr in (a, b, o):
         arr.free()
+    # GEMMs (N(0,1) operands), whole fz_gemm_f32 call including the remainder split:
+    # square 8192^3 (A [M,K], B [K,N]) and the weight-gradient shape x^T @ g
+    # (K = 65536 batch rows, both operands MN-major)
+    for name, (M, N, K, tA, tB) in (("gemm_3xtf32_8192^3", (8192, 8192, 8192, 0, 0)),
+                                    ("gemm_3xtf32_wgrad_4096x4096x65536", (4096, 4096, 65536, 1, 0))):
+        x = _random_device(A, (K, M) if tA else (M, K), 21)
+        y = _random_device(A, (N, K) if tB else (K, N), 22)
+        c = A.DeviceArray((M, N))
+        lda, ldb = (M if tA else K), (K if tB else N)
+        ms = time_launch(A, lambda: A.check(L.fz_gemm_f32(1, M, N, K, x.ptr, lda, 0, tA, y.ptr, ldb,
+                                                          0, tB, c.ptr, N, 0, None)), reps=5, warm=2)
+        tf = 2.0 * M * N * K / ms / 1e9
+        out[name] = {"ms": round(ms, 3), "TFLOP/s": round(tf, 1), "tensor_pipe_TFLOP/s": round(3 * tf, 1)}
+        for arr in (x, y, c):
+            arr.free()
     return out
 
 
+def _random_device(capi, shape, seed):
+    a = np.random.default_rng(seed).standard_normal(shape, dtype=np.float32)
+    return capi.DeviceArray.from_numpy(a)
+
+
 def gemm_roofline(capi, pk, m):
-    """Dominant kernel of the step: the [m,4096] x [4096,4096] GEMM (layers 2-3 and their
-    backward), timed live on the library stream with CUDA events."""
+    """Dominant kernel of the step: gemm_3xtf32_kernel on the [m,4096] x [4096,4096]^T
+    product of layers 2-3, timed live on the library stream with CUDA events. The
+    operands' TF32 remainder planes are split before the timed region (as the step's
+    split cache does), so the timed launches are the GEMM kernel alone."""
     A, L = capi, capi.lib()
     k = n = 4096
-    x, w, c = A.DeviceArray((m, k)), A.DeviceArray((n, k)), A.DeviceArray((m, n))
-    A.check(L.fz_fill_f32(x.ptr, C.c_float(0.01), m * k, None))
-    A.check(L.fz_fill_f32(w.ptr, C.c_float(0.02), n * k, None))
-    ms = time_launch(A, lambda: A.check(L.fz_gemm_f32(1, m, n, k, x.ptr, k, 0, 0, w.ptr, k, 0, 1,
-                                                      c.ptr, n, 0, None)), reps=10, warm=3)
+    x, w, c = _random_device(A, (m, k), 11), _random_device(A, (n, k), 12), A.DeviceArray((m, n))
+    xl, wl = A.DeviceArray((m, k)), A.DeviceArray((n, k))
+    A.check(L.fz_tf32_lo(xl.ptr, x.ptr, m * k, None))
+    A.check(L.fz_tf32_lo(wl.ptr, w.ptr, n * k, None))
+    ms = time_launch(A, lambda: A.check(L.fz_gemm_f32_split(1, m, n, k, x.ptr, xl.ptr, k, 0, 0,
+                                                            w.ptr, wl.ptr, k, 0, 1, c.ptr, n, 0,
+                                                            None)), reps=10, warm=3)
     A.check(L.fz_kernel_status())
-    for arr in (x, w, c):
+    for arr in (x, w, c, xl, wl):
         arr.free()
     achieved = 2.0 * m * n * k / ms / 1e9
     tf32_peak = pk["bf16_tflops"] / 2.0  # TF32 runs at half the bf16 tensor rate
@@ -259,7 +274,8 @@ def gemm_roofline(capi, pk, m):
         for line in summary.read_text().splitlines():
             if line.startswith("dram_bytes_per_launch_full_size:"):
                 traffic = float(line.split(":", 1)[1])
-    return {"kernel": f"fz_gemm_f32 3xTF32 [{m},{k}]x[{k},{n}]^T (split pass + tcgen05 main loop)",
+    return {"kernel": f"gemm_3xtf32_kernel [{m},{k}]x[{n},{k}]^T, N(0,1) operands, "
+                      f"remainder planes split beforehand",
             "bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak, 1),
             "unit": "TFLOP/s", "frac": round(achieved / peak, 3), "traffic": traffic,
             "peak_basis": f"{pk['basis']} bf16 {pk['bf16_tflops']} TFLOP/s / 2 (TF32 rate) / 3 (3xTF32)",
@@ -465,13 +481,18 @@ def run_kernel(args):
     F.set_device(0)
     A, L = capi, capi.lib()
     k = args.kernel
-    if k == "gemm":  # the MLP's dominant GEMM shape at 1/8 of the batch
-        m, n, kk = 8192, 4096, 4096
-        x, w, c = A.DeviceArray((m, kk)), A.DeviceArray((n, kk)), A.DeviceArray((m, n))
-        A.check(L.fz_fill_f32(x.ptr, C.c_float(0.01), m * kk, None))
-        A.check(L.fz_fill_f32(w.ptr, C.c_float(0.02), n * kk, None))
-        fn = lambda: A.check(L.fz_gemm_f32(1, m, n, kk, x.ptr, kk, 0, 0, w.ptr, kk, 0, 1, c.ptr,
-                                            n, 0, None))
+    if k in ("gemm", "gemm_wgrad"):
+        # gemm: the MLP's dominant forward shape x @ W^T at 1/8 of the batch (both operands
+        # K-major); gemm_wgrad: the weight gradient x^T @ g at 1/4 of the batch (both
+        # MN-major). Remainder planes split beforehand: the loop is the GEMM kernel alone.
+        m, n, kk, tA, tB = (8192, 4096, 4096, 0, 1) if k == "gemm" else (4096, 4096, 16384, 1, 0)
+        ash, bsh = ((kk, m) if tA else (m, kk)), ((n, kk) if tB else (kk, n))
+        x, w, c = _random_device(A, ash, 1), _random_device(A, bsh, 2), A.DeviceArray((m, n))
+        xl, wl = A.DeviceArray(ash), A.DeviceArray(bsh)
+        A.check(L.fz_tf32_lo(xl.ptr, x.ptr, m * kk, None))
+        A.check(L.fz_tf32_lo(wl.ptr, w.ptr, n * kk, None))
+        fn = lambda: A.check(L.fz_gemm_f32_split(1, m, n, kk, x.ptr, xl.ptr, ash[1], 0, tA, w.ptr,
+                                                  wl.ptr, bsh[1], 0, tB, c.ptr, n, 0, None))
         work = 2.0 * m * n * kk
     elif k == "bias_relu":  # fused relu(x + b) of the MLP forward through the fusion IR
         rows, cols = 16384, 4096
@@ -502,9 +523,10 @@ def run_kernel(args):
         }[k]
     ms = time_launch(A, fn, reps=args.reps, warm=1)
     F.synchronize()
-    unit = "TFLOP/s" if k == "gemm" else "GB/s"
+    gemm = k.startswith("gemm")
+    unit = "TFLOP/s" if gemm else "GB/s"
     print(json.dumps({"kernel": k, "ms": round(ms, 4),
-                      unit: round(work / ms / (1e9 if k == "gemm" else 1e6), 1)}), flush=True)
+                      unit: round(work / ms / (1e9 if gemm else 1e6), 1)}), flush=True)
 
 
 def main():

@@ -239,6 +239,20 @@ int fz_gemm_f32(int64_t batch, int64_t M, int64_t N, int64_t K,
                 const float *B, int64_t ldb, int64_t strideB, int transB,
                 float *C, int64_t ldc, int64_t strideC, void *stream);
 
+/* fz_gemm_f32 with the low TF32 remainders of the operands supplied by the caller:
+ * A_lo[i] = fz_tf32_lo(A)[i] at A's own leading dimension and batch stride (same for
+ * B_lo), so an operand read by several GEMMs (an activation in the forward and the
+ * weight-gradient GEMM) is split once. A NULL plane, or an operand TMA cannot
+ * address (leading dimension or batch stride not a multiple of 4 floats, base not
+ * 16-byte aligned, broadcast batch), is split here as in fz_gemm_f32. */
+int fz_gemm_f32_split(int64_t batch, int64_t M, int64_t N, int64_t K,
+                      const float *A, const float *A_lo, int64_t lda, int64_t strideA, int transA,
+                      const float *B, const float *B_lo, int64_t ldb, int64_t strideB, int transB,
+                      float *C, int64_t ldc, int64_t strideC, void *stream);
+/* lo[i] = x[i] - tf32_hi(x[i]) for i < n, tf32_hi clearing the 13 low mantissa bits
+ * (the plane fz_gemm_f32_split takes). */
+int fz_tf32_lo(float *lo, const float *x, int64_t n, void *stream);
+
 /* ---- collectives (data-parallel MLP step) -------------------------------- */
 
 #define FZ_UNIQUE_ID_BYTES 128

@@ -91,6 +91,9 @@ def lib() -> C.CDLL:
         L.fz_swapaxes.argtypes = [vp, vp, C.POINTER(C.c_int64), C.c_int, C.c_int, C.c_int, vp]
         L.fz_gemm_f32.argtypes = [i64, i64, i64, i64, vp, i64, i64, C.c_int, vp, i64, i64,
                                   C.c_int, vp, i64, i64, vp]
+        L.fz_gemm_f32_split.argtypes = [i64, i64, i64, i64, vp, vp, i64, i64, C.c_int, vp, vp,
+                                        i64, i64, C.c_int, vp, i64, i64, vp]
+        L.fz_tf32_lo.argtypes = [vp, vp, i64, vp]
         L.fz_timer_create.argtypes = [C.POINTER(C.c_void_p)]
         L.fz_timer_start.argtypes = [vp, vp]
         L.fz_timer_stop.argtypes = [vp, vp]

@@ -4,15 +4,17 @@
 //
 // 3xTF32: x = hi + lo with hi = x with its 13 low mantissa bits cleared (exact in
 // TF32) and lo = x - hi (exact in fp32); C = Ah*Bh + Ah*Bl + Al*Bh. The kind::tf32
-// MMA ignores the 13 low mantissa bits of its fp32 inputs, so an operand already
-// stored K-major ([M, K] for A, [N, K] for B) is its own hi plane and only its lo
-// plane is written (lo_kernel); an operand given the other way round is transposed
-// into K-major hi and lo planes through shared memory (split_t_kernel).
+// MMA ignores the 13 low mantissa bits of its fp32 inputs, so every operand is its
+// own hi plane and only its lo plane is written (lo_kernel, same layout as the
+// operand). Operands are read in the layout they are stored in: K-major ([M, K] for
+// A, [N, K] for B; 64-byte swizzled boxes of 16 k) or MN-major ([K, M] / [K, N], the
+// weight-gradient case where K is the batch; boxes of 32 rows x 16 k in the 128-byte
+// swizzle with 32-byte atoms), selected per operand by template and the MMA's major bits.
 //
 // Main kernel, persistent (one CTA per SM walking 128 x 256 output tiles in grouped
 // order), warp-specialised, 320 threads:
 //   warp 0     TMA producer: per k-tile of BK = 16 loads A_hi, A_lo (128 x 16) and
-//              B_hi, B_lo (256 x 16) into a 4-stage ring of 48 KB (64-byte swizzle)
+//              B_hi, B_lo (256 x 16) into a 4-stage ring of 48 KB
 //   warp 1     allocates 2 x 256 TMEM columns; one lane issues, per 8-wide k-step,
 //              tcgen05.mma.kind::tf32 lo*hi, hi*lo, hi*hi, and tcgen05.commit frees
 //              each stage. The K range is cut into chunks of 256; each chunk
@@ -51,6 +53,8 @@ constexpr int STAGES = BK == 16 ? 4 : 2;
 constexpr int SWIZZLE_BYTES = BK * 4;
 static_assert(BK == 16 || BK == 32, "BK must be 16 or 32");
 constexpr int UMMA_K = 8;  // K of one kind::tf32 MMA
+constexpr int MN_CHUNK = 32;              // MN-major tiles: M/N rows per 128-byte swizzle row
+constexpr int MN_CHUNK_BYTES = BK * 128;  // one such chunk of a stage tile (BK k-rows)
 constexpr int TILE_A_BYTES = BM * BK * 4;  // 16 KB
 constexpr int TILE_B_BYTES = BN * BK * 4;  // 32 KB
 constexpr int STAGE_BYTES = 2 * TILE_A_BYTES + 2 * TILE_B_BYTES;  // 96 KB
@@ -68,17 +72,19 @@ __device__ __forceinline__ void split1(float x, float &hi, float &lo) {
   lo = __fsub_rn(x, hi);
 }
 
-// src rows are K-major already: src[b][r][k] at b*sb + r*ld + k. Writes the lo
-// plane lo[b][r][k] (pitch kp, zero beyond K); the MMA reads src itself as hi. When
-// src cannot be addressed by TMA (row pitch not a multiple of 16 bytes, or a
-// broadcast batch), `hi` is non-null and receives a copy of src at pitch kp.
+// src[b][r][k] at b*sb + r*ld + k (k the contiguous index: K for a K-major operand,
+// M or N for an MN-major one). Writes the lo plane lo[b][r][k] (pitch kp, zero
+// beyond K); the MMA reads src itself as hi. When src cannot be addressed by TMA
+// (row pitch not a multiple of 16 bytes, or a broadcast batch), `hi` is non-null and
+// receives a copy of src at pitch kp.
 __global__ void __launch_bounds__(256) lo_kernel(const float *__restrict__ src, int64_t ld,
                                                  int64_t sb, int64_t rows, int64_t K, int64_t kp,
                                                  int64_t batch, float *__restrict__ lo,
                                                  float *__restrict__ hi) {
   const int64_t step = (int64_t)gridDim.x * blockDim.x;
   const int64_t t0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (!hi && ld == kp && K == kp && (batch == 1 || sb == rows * kp) && (((uintptr_t)src | (uintptr_t)lo) & 15) == 0) {
+  if (!hi && ld == kp && K == kp && kp % 4 == 0 && (batch == 1 || sb == rows * kp) &&
+      (((uintptr_t)src | (uintptr_t)lo) & 15) == 0) {
     const int64_t n4 = batch * rows * kp / 4;  // dense rows: one flat float4 stream
     const float4 *s4 = reinterpret_cast<const float4 *>(src);
     float4 *l4 = reinterpret_cast<float4 *>(lo);
@@ -104,42 +110,6 @@ __global__ void __launch_bounds__(256) lo_kernel(const float *__restrict__ src, 
     split1(x, h, l);
     lo[t] = l;
     if (hi) hi[t] = x;
-  }
-}
-
-// src is [b][k][r] (r contiguous, pitch ld): transpose to [b][r][k] while splitting.
-__global__ void __launch_bounds__(256) split_t_kernel(const float *__restrict__ src, int64_t ld,
-                                                      int64_t sb, int64_t rows, int64_t K,
-                                                      int64_t kp, int64_t batch,
-                                                      float *__restrict__ hi,
-                                                      float *__restrict__ lo) {
-  __shared__ float tile[32][33];
-  const int64_t tr = (rows + 31) / 32, tk = (kp + 31) / 32;
-  const int64_t total = batch * tr * tk;
-  const int tx = threadIdx.x % 32, ty = threadIdx.x / 32;
-  for (int64_t t = blockIdx.x; t < total; t += gridDim.x) {
-    int64_t jr = t % tr;
-    int64_t rest = t / tr;
-    int64_t jk = rest % tk, b = rest / tk;
-    const float *s = src + b * sb;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      int64_t k = jk * 32 + ty + 8 * i, r = jr * 32 + tx;
-      tile[ty + 8 * i][tx] = (k < K && r < rows) ? s[k * ld + r] : 0.0f;
-    }
-    __syncthreads();
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      int64_t r = jr * 32 + ty + 8 * i, k = jk * 32 + tx;
-      if (r < rows && k < kp) {
-        float h, l;
-        split1(tile[tx][ty + 8 * i], h, l);
-        int64_t o = (b * rows + r) * kp + k;
-        hi[o] = h;
-        lo[o] = l;
-      }
-    }
-    __syncthreads();
   }
 }
 
@@ -201,6 +171,21 @@ __device__ __forceinline__ void prefetch_map(const CUtensorMap *map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
+// One operand's k-tile [row0, row0 + ROWS) x [k0, k0 + BK) into a stage tile.
+// K-major: one box {BK, ROWS}. MN-major: ROWS / 32 boxes {32, BK}, each a chunk of
+// MN_CHUNK_BYTES; rows past the operand's extent are zero-filled by the TMA unit.
+template <bool MN, int ROWS>
+__device__ __forceinline__ void load_operand(uint8_t *dst, const CUtensorMap *map, uint64_t *bar,
+                                             int k0, int row0, int bz) {
+  if constexpr (MN) {
+#pragma unroll
+    for (int j = 0; j < ROWS / MN_CHUNK; ++j)
+      tma_load_3d(dst + j * MN_CHUNK_BYTES, map, bar, row0 + j * MN_CHUNK, k0, bz);
+  } else {
+    tma_load_3d(dst, map, bar, k0, row0, bz);
+  }
+}
+
 // K-major shared-memory descriptor for rows of SWIZZLE_BYTES (one swizzle atom
 // row per tile row): 8-row groups 8*SWIZZLE_BYTES apart (SBO), LBO unused (1),
 // descriptor version 1 (bit 46), layout type at bits 61-63: 2 = SWIZZLE_128B,
@@ -215,20 +200,45 @@ __device__ __forceinline__ uint64_t smem_desc_k(uint32_t addr) {
   return d;
 }
 
-// kind::tf32 instruction descriptor: D = F32 (bits 4-5 = 1), A = B = TF32 (2),
-// both K-major, N >> 3 at bits 17-22, M >> 4 at bits 24-28.
-constexpr uint32_t make_idesc(int m, int n) {
-  return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(n >> 3) << 17) |
-         ((uint32_t)(m >> 4) << 24);
+// MN-major shared-memory descriptor. For 32-bit (TF32) operands the MN-major layout
+// is the 128-byte swizzle with 32-byte atomicity (layout type 1): 32-byte units of a
+// 128-byte row are permuted by the row index mod 4, in atoms of 4 k-rows x 128 bytes
+// (512 B). The tile is stored as chunks of 32 M/N rows, each BK k-rows of 128 bytes;
+// LBO = distance between the 32-wide M/N chunks (BK * 128 bytes), SBO = distance
+// between 4-row k atoms (512 bytes). The TMA writes this image with
+// CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B.
+__device__ __forceinline__ uint64_t smem_desc_mn(uint32_t addr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((addr >> 4) & 0x3fff);
+  d |= (uint64_t)(MN_CHUNK_BYTES >> 4) << 16;
+  d |= (uint64_t)(512 >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)1 << 61;
+  return d;
 }
-constexpr uint32_t kIdesc = make_idesc(BM, BN);
 
-__device__ __forceinline__ void umma_tf32(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t accum) {
+// Descriptor of k-step kk (UMMA_K wide) of a stage tile at `base`.
+template <bool MN>
+__device__ __forceinline__ uint64_t operand_desc(uint32_t base, int kk) {
+  if constexpr (MN) return smem_desc_mn(base + (uint32_t)kk * (UMMA_K * 128));  // 8 k-rows
+  else return smem_desc_k(base + (uint32_t)kk * (UMMA_K * 4));                  // 32 bytes
+}
+
+// kind::tf32 instruction descriptor: D = F32 (bits 4-5 = 1), A = B = TF32 (2),
+// A major at bit 15 and B major at bit 16 (0 = K-major, 1 = MN-major), N >> 3 at
+// bits 17-22, M >> 4 at bits 24-28.
+__host__ __device__ constexpr uint32_t make_idesc(int m, int n, bool a_mn, bool b_mn) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)a_mn << 15) | ((uint32_t)b_mn << 16) |
+         ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_tf32(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc,
+                                          uint32_t accum) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-      "l"(a), "l"(b), "r"(kIdesc), "r"(accum)
+      "l"(a), "l"(b), "r"(idesc), "r"(accum)
       : "memory");
 }
 
@@ -296,6 +306,8 @@ __device__ __forceinline__ int unit_k_tiles(const GemmArgs &a, int ks, int &k_be
 // Persistent kernel: one CTA per SM walks tiles blockIdx.x, +gridDim.x, ...
 // K is cut into chunks of KCHUNK k-tiles accumulated alternately in two TMEM
 // buffers; warps 2-9 fold each finished chunk into fp32 registers.
+// A_MN / B_MN: the operand is MN-major in global and shared memory.
+template <bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap mapAh,
                        const __grid_constant__ CUtensorMap mapAl,
@@ -312,6 +324,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   __shared__ volatile int abort_flag;
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  constexpr uint32_t kIdesc = make_idesc(BM, BN, A_MN, B_MN);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -369,10 +382,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           }
           mbar_expect_tx(&full_bar[s], STAGE_BYTES);
           const int k0 = kb + kt * BK;
-          tma_load_3d(stage_ptr(s, 0), &mapAh, &full_bar[s], k0, mb * BM, bz);
-          tma_load_3d(stage_ptr(s, 1), &mapAl, &full_bar[s], k0, mb * BM, bz);
-          tma_load_3d(stage_ptr(s, 2), &mapBh, &full_bar[s], k0, nb * BN, bz);
-          tma_load_3d(stage_ptr(s, 3), &mapBl, &full_bar[s], k0, nb * BN, bz);
+          load_operand<A_MN, BM>(stage_ptr(s, 0), &mapAh, &full_bar[s], k0, mb * BM, bz);
+          load_operand<A_MN, BM>(stage_ptr(s, 1), &mapAl, &full_bar[s], k0, mb * BM, bz);
+          load_operand<B_MN, BN>(stage_ptr(s, 2), &mapBh, &full_bar[s], k0, nb * BN, bz);
+          load_operand<B_MN, BN>(stage_ptr(s, 3), &mapBl, &full_bar[s], k0, nb * BN, bz);
         }
       }
       if (!ok) {
@@ -416,13 +429,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             const uint32_t b_hi = smem_u32(stage_ptr(s, 2)), b_lo = smem_u32(stage_ptr(s, 3));
 #pragma unroll
             for (int kk = 0; kk < BK / UMMA_K; ++kk) {
-              const uint32_t off = kk * UMMA_K * 4;  // 32 bytes per k-step in the swizzle row
-              const uint64_t dah = smem_desc_k(a_hi + off), dal = smem_desc_k(a_lo + off);
-              const uint64_t dbh = smem_desc_k(b_hi + off), dbl = smem_desc_k(b_lo + off);
+              const uint64_t dah = operand_desc<A_MN>(a_hi, kk), dal = operand_desc<A_MN>(a_lo, kk);
+              const uint64_t dbh = operand_desc<B_MN>(b_hi, kk), dbl = operand_desc<B_MN>(b_lo, kk);
               const uint32_t first = (kt == kt0 && kk == 0) ? 0u : 1u;
-              umma_tf32(d_tmem, dal, dbh, first);  // lo * hi
-              umma_tf32(d_tmem, dah, dbl, 1u);     // hi * lo
-              umma_tf32(d_tmem, dah, dbh, 1u);     // hi * hi (largest term last)
+              umma_tf32(d_tmem, dal, dbh, kIdesc, first);  // lo * hi
+              umma_tf32(d_tmem, dah, dbl, kIdesc, 1u);     // hi * lo
+              umma_tf32(d_tmem, dah, dbh, kIdesc, 1u);     // hi * hi (largest term last)
             }
             umma_commit(&empty_bar[s]);
           }
@@ -519,19 +531,25 @@ int get_encoder() {
   return rc;
 }
 
-// 3D map over a [batch, rows, K] operand (K innermost, row pitch ld floats, batch
-// pitch sb floats), box {BK, box_rows, 1}. TMA needs ld*4 and sb*4 to be multiples
-// of 16 bytes and the base 16-byte aligned.
-int make_map(CUtensorMap *map, const float *base, int64_t rows, int64_t K, int64_t ld, int64_t sb,
-             int64_t batch, int box_rows) {
-  if (batch == 1) sb = ld * rows;
-  cuuint64_t dims[3] = {(cuuint64_t)K, (cuuint64_t)rows, (cuuint64_t)batch};
+// 3D map over one operand plane. K-major ([batch, rows, K], K innermost): box
+// {BK, box_rows, 1}, 64-byte swizzle (128-byte for BK = 32). MN-major ([batch, K,
+// rows], rows innermost): box {32, BK, 1}, 128-byte swizzle with 32-byte atoms,
+// fetched box_rows / 32 times per k-tile. TMA needs ld*4 and sb*4 to be multiples of 16 bytes and the
+// base 16-byte aligned; every box starts at an inner coordinate that is a multiple
+// of 16 (K-major) or 32 (MN-major) elements.
+int make_map(CUtensorMap *map, const float *base, bool mn, int64_t rows, int64_t K, int64_t ld,
+             int64_t sb, int64_t batch, int box_rows) {
+  if (batch == 1) sb = ld * (mn ? K : rows);
+  cuuint64_t dims[3] = {(cuuint64_t)(mn ? rows : K), (cuuint64_t)(mn ? K : rows), (cuuint64_t)batch};
   cuuint64_t strides[2] = {(cuuint64_t)(ld * 4), (cuuint64_t)(sb * 4)};
-  cuuint32_t box[3] = {(cuuint32_t)BK, (cuuint32_t)box_rows, 1};
+  cuuint32_t box[3] = {mn ? (cuuint32_t)MN_CHUNK : (cuuint32_t)BK,
+                       mn ? (cuuint32_t)BK : (cuuint32_t)box_rows, 1};
   cuuint32_t estr[3] = {1, 1, 1};
+  const CUtensorMapSwizzle sw = mn ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B
+                               : SWIZZLE_BYTES == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                                      : CU_TENSOR_MAP_SWIZZLE_64B;
   CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, (void *)base, dims, strides, box,
-                        estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                        SWIZZLE_BYTES == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                        estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return fz::fail(FZ_ERR_CUDA, "cuTensorMapEncodeTiled failed with code " + std::to_string((int)r));
@@ -567,57 +585,90 @@ int choose_splits(int64_t tiles, int64_t M, int64_t N, int64_t K, int64_t batch)
   return best;
 }
 
-// One operand as the (hi, lo) pair the kernel reads, both [batch, rows, K] K-major.
+// One operand as the (hi, lo) planes the kernel reads, in the operand's own layout:
+// outer rows of `inner` contiguous floats (K-major: rows = M or N, inner = K;
+// MN-major: rows = K, inner = M or N).
 struct Operand {
+  bool mn;
+  int64_t rows, inner;
   const float *hi;
   int64_t hi_ld, hi_sb;
-  float *lo;  // plane at pitch kp
+  const float *lo;
+  int64_t lo_ld, lo_sb;
 };
 
-// Plane floats an operand needs in the workspace (lo always; hi unless the source
-// is K-major and TMA-addressable).
-bool direct_hi(const float *src, int64_t ld, int64_t sb, bool kmajor, int64_t batch) {
-  return kmajor && ld % 4 == 0 && ((uintptr_t)src & 15) == 0 && (batch == 1 || (sb > 0 && sb % 4 == 0));
+// The raw operand can serve as the hi plane when TMA can address it.
+bool direct_hi(const float *src, int64_t ld, int64_t sb, int64_t batch) {
+  return ld % 4 == 0 && ((uintptr_t)src & 15) == 0 && (batch == 1 || (sb > 0 && sb % 4 == 0));
 }
 
-int prepare(const float *src, int64_t ld, int64_t sb, bool kmajor, int64_t rows, int64_t K,
-            int64_t kp, int64_t batch, float *ws, Operand *op, cudaStream_t s) {
-  const int64_t plane = batch * rows * kp;
-  op->lo = ws;
-  if (kmajor) {
-    const bool direct = direct_hi(src, ld, sb, kmajor, batch);
-    float *hi = direct ? nullptr : ws + plane;
-    unsigned grid = fz::grid_for(plane / 4 + 1, 256, 8, 4);
-    lo_kernel<<<grid, 256, 0, s>>>(src, ld, sb, rows, K, kp, batch, op->lo, hi);
-    FZ_CHECK_LAUNCH();
-    if (direct) {
-      op->hi = src;
-      op->hi_ld = ld;
-      op->hi_sb = sb;
-    } else {
-      op->hi = hi;
-      op->hi_ld = kp;
-      op->hi_sb = rows * kp;
-    }
+// Workspace floats the operand needs: none when the caller supplied its lo plane
+// and the operand is TMA-addressable; else a lo plane at a 16-byte pitch, plus a
+// hi copy when the operand itself is not TMA-addressable.
+int64_t workspace_floats(const Operand &o, const float *src, int64_t ld, int64_t sb,
+                         const float *lo_given, int64_t batch) {
+  const bool direct = direct_hi(src, ld, sb, batch);
+  if (direct && lo_given) return 0;
+  const int64_t plane = batch * o.rows * ((o.inner + 3) & ~(int64_t)3);
+  return plane * (direct ? 1 : 2);
+}
+
+// Point op at its hi and lo planes, writing into ws what the caller did not supply.
+int prepare(const float *src, int64_t ld, int64_t sb, const float *lo_given, int64_t batch,
+            float *ws, Operand *op, cudaStream_t s) {
+  const bool direct = direct_hi(src, ld, sb, batch);
+  if (batch == 1) sb = ld * op->rows;
+  if (direct && lo_given) {
+    op->hi = src;
+    op->lo = lo_given;
+    op->hi_ld = op->lo_ld = ld;
+    op->hi_sb = op->lo_sb = sb;
     return FZ_OK;
   }
-  float *hi = ws + plane;
-  int64_t tiles = batch * ((rows + 31) / 32) * ((kp + 31) / 32);
-  unsigned grid = fz::grid_for(tiles, 1, 8, 4);
-  split_t_kernel<<<grid, 256, 0, s>>>(src, ld, sb, rows, K, kp, batch, hi, op->lo);
+  const int64_t pitch = (op->inner + 3) & ~(int64_t)3;  // 16-byte row pitch for TMA
+  const int64_t plane = batch * op->rows * pitch;
+  float *lo = ws, *hi = direct ? nullptr : ws + plane;
+  unsigned grid = fz::grid_for(plane / 4 + 1, 256, 8, 4);
+  lo_kernel<<<grid, 256, 0, s>>>(src, ld, sb, op->rows, op->inner, pitch, batch, lo, hi);
   FZ_CHECK_LAUNCH();
-  op->hi = hi;
-  op->hi_ld = kp;
-  op->hi_sb = rows * kp;
+  op->lo = lo;
+  op->lo_ld = pitch;
+  op->lo_sb = op->rows * pitch;
+  if (direct) {
+    op->hi = src;
+    op->hi_ld = ld;
+    op->hi_sb = sb;
+  } else {
+    op->hi = hi;
+    op->hi_ld = pitch;
+    op->hi_sb = op->rows * pitch;
+  }
   return FZ_OK;
 }
 
-}  // namespace
+template <bool A_MN, bool B_MN>
+int launch_gemm(const CUtensorMap &mAh, const CUtensorMap &mAl, const CUtensorMap &mBh,
+                const CUtensorMap &mBl, const GemmArgs &ga, unsigned grid, size_t smem,
+                cudaStream_t s) {
+  static bool attr_done[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !attr_done[dev]) {
+    cudaFuncSetAttribute(gemm_3xtf32_kernel<A_MN, B_MN>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    attr_done[dev] = true;
+  }
+  gemm_3xtf32_kernel<A_MN, B_MN><<<grid, NUM_THREADS, smem, s>>>(mAh, mAl, mBh, mBl, ga);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fz::cuda_fail(e, "gemm_3xtf32_kernel launch", __FILE__, __LINE__);
+  fz::note_launch();
+  return FZ_OK;
+}
 
-extern "C" int fz_gemm_f32(int64_t batch, int64_t M, int64_t N, int64_t K, const float *A,
-                           int64_t lda, int64_t strideA, int transA, const float *B, int64_t ldb,
-                           int64_t strideB, int transB, float *C, int64_t ldc, int64_t strideC,
-                           void *stream) {
+int gemm_impl(int64_t batch, int64_t M, int64_t N, int64_t K, const float *A, const float *A_lo,
+              int64_t lda, int64_t strideA, int transA, const float *B, const float *B_lo,
+              int64_t ldb, int64_t strideB, int transB, float *C, int64_t ldc, int64_t strideC,
+              void *stream) {
   FZ_REQUIRE(batch >= 0 && M >= 0 && N >= 0 && K >= 0, "fz_gemm_f32: negative extent");
   if (batch == 0 || M == 0 || N == 0) return FZ_OK;
   FZ_REQUIRE(C, "fz_gemm_f32: null C");
@@ -638,23 +689,25 @@ extern "C" int fz_gemm_f32(int64_t batch, int64_t M, int64_t N, int64_t K, const
   int rc = get_encoder();
   if (rc) return rc;
 
-  const int64_t kp = (K + 3) & ~(int64_t)3;  // 16-byte row pitch for TMA
-  const bool a_km = transA == 0, b_km = transB != 0;  // A as [M,K], B as [N,K]
-  const int64_t a_plane = batch * M * kp, b_plane = batch * N * kp;
-  const int64_t a_need = a_plane * (direct_hi(A, lda, strideA, a_km, batch) ? 1 : 2);
-  const int64_t b_need = b_plane * (direct_hi(B, ldb, strideB, b_km, batch) ? 1 : 2);
+  // A as stored: [M, K] (transA = 0, K-major) or [K, M] (MN-major); B: [N, K]
+  // (transB != 0, K-major) or [K, N] (MN-major).
+  Operand oa{transA != 0, transA ? K : M, transA ? M : K};
+  Operand ob{transB == 0, transB ? N : K, transB ? K : N};
+  const int64_t a_need = workspace_floats(oa, A, lda, strideA, A_lo, batch);
+  const int64_t b_need = workspace_floats(ob, B, ldb, strideB, B_lo, batch);
   float *ws = nullptr;
-  rc = fz_malloc((void **)&ws, sizeof(float) * (a_need + b_need), s);
-  if (rc) return rc;
-  Operand oa{}, ob{};
-  rc = prepare(A, lda, strideA, a_km, M, K, kp, batch, ws, &oa, s);
-  if (!rc) rc = prepare(B, ldb, strideB, b_km, N, K, kp, batch, ws + a_need, &ob, s);
+  if (a_need + b_need) {
+    rc = fz_malloc((void **)&ws, sizeof(float) * (a_need + b_need), s);
+    if (rc) return rc;
+  }
+  rc = prepare(A, lda, strideA, A_lo, batch, ws, &oa, s);
+  if (!rc) rc = prepare(B, ldb, strideB, B_lo, batch, ws + a_need, &ob, s);
 
   CUtensorMap mAh, mAl, mBh, mBl;
-  if (!rc) rc = make_map(&mAh, oa.hi, M, K, oa.hi_ld, oa.hi_sb, batch, BM);
-  if (!rc) rc = make_map(&mAl, oa.lo, M, K, kp, M * kp, batch, BM);
-  if (!rc) rc = make_map(&mBh, ob.hi, N, K, ob.hi_ld, ob.hi_sb, batch, BN);
-  if (!rc) rc = make_map(&mBl, ob.lo, N, K, kp, N * kp, batch, BN);
+  if (!rc) rc = make_map(&mAh, oa.hi, oa.mn, M, K, oa.hi_ld, oa.hi_sb, batch, BM);
+  if (!rc) rc = make_map(&mAl, oa.lo, oa.mn, M, K, oa.lo_ld, oa.lo_sb, batch, BM);
+  if (!rc) rc = make_map(&mBh, ob.hi, ob.mn, N, K, ob.hi_ld, ob.hi_sb, batch, BN);
+  if (!rc) rc = make_map(&mBl, ob.lo, ob.mn, N, K, ob.lo_ld, ob.lo_sb, batch, BN);
   const int tiles_m = (int)((M + BM - 1) / BM), tiles_n = (int)((N + BN - 1) / BN);
   const int64_t tiles = (int64_t)tiles_m * tiles_n * batch;
   const bool dense_c = ldc == N && (batch == 1 || strideC == M * N);
@@ -671,27 +724,48 @@ extern "C" int fz_gemm_f32(int64_t batch, int64_t M, int64_t N, int64_t K, const
   if (!rc) rc = fz::device_error_word(&err);
   if (!rc) {
     const size_t smem = (size_t)STAGES * STAGE_BYTES + 1024;
-    static bool attr_done[64] = {};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev < 64 && !attr_done[dev]) {
-      cudaFuncSetAttribute(gemm_3xtf32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           (int)smem);
-      attr_done[dev] = true;
-    }
     GemmArgs ga{partial ? partial : C, partial ? N : ldc, partial ? M * N : strideC,
                 batch * M * N, (int)M, (int)N, (int)K, (int)batch,
                 tiles_m, tiles_n, (int)num_units, tiles_m < 16 ? tiles_m : 16,
                 real_splits, (int)kps, err};
     const unsigned grid = (unsigned)(num_units < fz::num_sms() ? num_units : fz::num_sms());
-    gemm_3xtf32_kernel<<<grid, NUM_THREADS, smem, s>>>(mAh, mAl, mBh, mBl, ga);
-    cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) rc = fz::cuda_fail(e, "gemm_3xtf32_kernel launch", __FILE__, __LINE__);
-    else fz::note_launch();
+    if (!oa.mn && !ob.mn) rc = launch_gemm<false, false>(mAh, mAl, mBh, mBl, ga, grid, smem, s);
+    else if (!oa.mn && ob.mn) rc = launch_gemm<false, true>(mAh, mAl, mBh, mBl, ga, grid, smem, s);
+    else if (oa.mn && !ob.mn) rc = launch_gemm<true, false>(mAh, mAl, mBh, mBl, ga, grid, smem, s);
+    else rc = launch_gemm<true, true>(mAh, mAl, mBh, mBl, ga, grid, smem, s);
     // K-split partials: summed over the splits in a fixed order (deterministic)
     if (!rc && partial) rc = fz_reduce(FZ_RSUM, C, partial, 1, real_splits, batch * M * N, s);
   }
   if (partial) fz_free(partial, s);
   fz_free(ws, s);
   return rc;
+}
+
+}  // namespace
+
+extern "C" int fz_gemm_f32(int64_t batch, int64_t M, int64_t N, int64_t K, const float *A,
+                           int64_t lda, int64_t strideA, int transA, const float *B, int64_t ldb,
+                           int64_t strideB, int transB, float *C, int64_t ldc, int64_t strideC,
+                           void *stream) {
+  return gemm_impl(batch, M, N, K, A, nullptr, lda, strideA, transA, B, nullptr, ldb, strideB,
+                   transB, C, ldc, strideC, stream);
+}
+
+extern "C" int fz_gemm_f32_split(int64_t batch, int64_t M, int64_t N, int64_t K, const float *A,
+                                 const float *A_lo, int64_t lda, int64_t strideA, int transA,
+                                 const float *B, const float *B_lo, int64_t ldb, int64_t strideB,
+                                 int transB, float *C, int64_t ldc, int64_t strideC, void *stream) {
+  return gemm_impl(batch, M, N, K, A, A_lo, lda, strideA, transA, B, B_lo, ldb, strideB, transB,
+                   C, ldc, strideC, stream);
+}
+
+extern "C" int fz_tf32_lo(float *lo, const float *x, int64_t n, void *stream) {
+  FZ_REQUIRE(n >= 0, "fz_tf32_lo: negative size");
+  if (n == 0) return FZ_OK;
+  FZ_REQUIRE(lo && x, "fz_tf32_lo: null pointer");
+  cudaStream_t s = fz::resolve(stream);
+  unsigned grid = fz::grid_for(n / 4 + 1, 256, 8, 4);
+  lo_kernel<<<grid, 256, 0, s>>>(x, n, n, 1, n, n, 1, lo, nullptr);
+  FZ_CHECK_LAUNCH();
+  return FZ_OK;
 }

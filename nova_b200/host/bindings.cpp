@@ -283,6 +283,9 @@ PYBIND11_MODULE(fusion, m) {
   m.def("set_fusion", &set_fusion_enabled, py::arg("enabled"),
         "Enable (default) or disable lazy elementwise fusion.");
   m.def("fusion_enabled", &fusion_enabled);
+  m.def("set_split_cache", &set_split_cache_enabled, py::arg("enabled"),
+        "Keep GEMM operands' TF32 remainder planes with their buffers (default on).");
+  m.def("split_cache_enabled", &split_cache_enabled);
   m.def("empty_cache", []() { fz_check(fz_pool_release(), "fz_pool_release"); },
         "Return this device's cached blocks to the driver (synchronises the device).");
   m.def("flush", [](const T &t) { t.raw().data(); }, py::arg("tensor"),

@@ -90,6 +90,9 @@ size_t Expr::numel() const {
 
 // ---------------------------------------------------------------- fusion IR
 static bool g_fusion = true;
+static bool g_split_cache = true;
+void set_split_cache_enabled(bool on) { g_split_cache = on; }
+bool split_cache_enabled() { return g_split_cache; }
 static int64_t g_fused_launches = 0;
 constexpr int kNodeLimit = 40;   // below FZ_MAX_NODES, leaving room for dedupe slack
 constexpr int kLeafLimit = 10;   // below FZ_MAX_LEAVES
@@ -568,6 +571,24 @@ RawTensor reduce(int op, const RawTensor &x, size_t axis, bool keepdim) {
   return RawTensor(make_leaf(std::move(buf), oshape), x.dtype(), x.device());
 }
 
+// The TF32 remainder plane of a materialised GEMM operand, split on first use and
+// kept with its buffer; null (the GEMM splits it itself) when caching is off or the
+// GEMM could not read it directly (pitch or batch stride not a multiple of 4 floats,
+// broadcast batch).
+static const float *tf32_lo_plane(const RawTensor &t, int64_t ld, int64_t stride, size_t batch) {
+  if (!split_cache_enabled() || ld % 4 != 0 || stride % 4 != 0 || (batch > 1 && stride == 0))
+    return nullptr;
+  ExprPtr e = t.expr();
+  if (!e || e->kind != Expr::Leaf || !e->buf) return nullptr;
+  DeviceBuffer &b = *e->buf;
+  if (!b.tf32_lo) {
+    auto lo = std::make_shared<DeviceBuffer>(b.numel);
+    fz_check(fz_tf32_lo(lo->ptr, b.ptr, (int64_t)b.numel, nullptr), "fz_tf32_lo");
+    b.tf32_lo = std::move(lo);
+  }
+  return b.tf32_lo->ptr;
+}
+
 RawTensor matmul(const RawTensor &A, const RawTensor &B, bool transA, bool transB) {
   FB_CHECK(A.is_initialised(), "matmul: A uninitialised");
   FB_CHECK(B.is_initialised(), "matmul: B uninitialised");
@@ -600,9 +621,11 @@ RawTensor matmul(const RawTensor &A, const RawTensor &B, bool transA, bool trans
   const int64_t lda = (int64_t)as[ar - 1], ldb = (int64_t)bs[br - 1];
   const int64_t sA = ba == 1 ? 0 : (int64_t)(as[ar - 1] * as[ar - 2]);
   const int64_t sB = bb == 1 ? 0 : (int64_t)(bs[br - 1] * bs[br - 2]);
-  fz_check(fz_gemm_f32((int64_t)batch, (int64_t)M, (int64_t)N, (int64_t)Ka, pa, lda, sA, transA,
-                       pb, ldb, sB, transB, buf->ptr, (int64_t)N, (int64_t)(M * N), nullptr),
-           "fz_gemm_f32");
+  const float *la = tf32_lo_plane(A, lda, sA, batch), *lb = tf32_lo_plane(B, ldb, sB, batch);
+  fz_check(fz_gemm_f32_split((int64_t)batch, (int64_t)M, (int64_t)N, (int64_t)Ka, pa, la, lda, sA,
+                             transA, pb, lb, ldb, sB, transB, buf->ptr, (int64_t)N,
+                             (int64_t)(M * N), nullptr),
+           "fz_gemm_f32_split");
   return RawTensor(make_leaf(std::move(buf), oshape), A.dtype(), A.device());
 }
 

@@ -58,10 +58,15 @@ struct Device {
 size_t dtype_size(DType d);
 
 // ---- device memory -----------------------------------------------------------
+// Device storage of one value. A buffer is written once, by the kernel or copy that
+// produces it, before anything reads it; later values (in-place ops, set_values,
+// all-reduce results) go to new buffers. So data derived from the values, like the
+// TF32 remainder plane a GEMM reads, can be kept with the buffer.
 struct DeviceBuffer {
   float *ptr = nullptr;
   size_t numel = 0;
   int device = 0;
+  std::shared_ptr<DeviceBuffer> tf32_lo;  // fz_tf32_lo(ptr), made by the first GEMM reading it
   explicit DeviceBuffer(size_t n);
   ~DeviceBuffer();
   DeviceBuffer(const DeviceBuffer &) = delete;
@@ -93,6 +98,11 @@ struct Storage {
 // Fusion policy switches (fusion enabled by default).
 void set_fusion_enabled(bool on);
 bool fusion_enabled();
+// Keep each GEMM operand's TF32 remainder plane with its buffer, so an operand read
+// by several GEMMs is split once (on by default; off frees the memory it holds on to
+// for buffers made later).
+void set_split_cache_enabled(bool on);
+bool split_cache_enabled();
 // Lower a pending node to one fused kernel (no-op for a Leaf).
 void materialize(const ExprPtr &e);
 int64_t fused_launches();

@@ -211,6 +211,47 @@ int fz_gemm_f32(int64_t batch, int64_t M, int64_t N, int64_t K, const float *A, 
   return FZ_OK;
 }
 
+static float tf32_lo1(float x) {
+  uint32_t u;
+  std::memcpy(&u, &x, 4);
+  u &= 0xffffe000u;
+  float h;
+  std::memcpy(&h, &u, 4);
+  return x - h;
+}
+
+int fz_tf32_lo(float *lo, const float *x, int64_t n, void *) {
+  for (int64_t i = 0; i < n; ++i) lo[i] = tf32_lo1(x[i]);
+  ++g_launches;
+  return FZ_OK;
+}
+
+// A supplied lo plane must hold the remainders of the operand's current values:
+// a stale plane (the host reusing one after the operand changed) is an error here.
+static int check_lo(const float *X, const float *X_lo, int64_t rows, int64_t cols, int64_t ld,
+                    int64_t sb, int64_t batch, const char *name) {
+  if (!X_lo) return FZ_OK;
+  for (int64_t b = 0; b < batch; ++b)
+    for (int64_t r = 0; r < rows; ++r)
+      for (int64_t c = 0; c < cols; ++c) {
+        const int64_t o = b * sb + r * ld + c;
+        const float want = tf32_lo1(X[o]);
+        if (std::memcmp(&want, &X_lo[o], 4) != 0)
+          return fail(FZ_ERR_INVALID, std::string("fz_gemm_f32_split: stale lo plane for ") + name);
+      }
+  return FZ_OK;
+}
+
+int fz_gemm_f32_split(int64_t batch, int64_t M, int64_t N, int64_t K, const float *A,
+                      const float *A_lo, int64_t lda, int64_t sA, int tA, const float *B,
+                      const float *B_lo, int64_t ldb, int64_t sB, int tB, float *C, int64_t ldc,
+                      int64_t sC, void *st) {
+  int rc = check_lo(A, A_lo, tA ? K : M, tA ? M : K, lda, sA, sA ? batch : 1, "A");
+  if (!rc) rc = check_lo(B, B_lo, tB ? N : K, tB ? K : N, ldb, sB, sB ? batch : 1, "B");
+  if (rc) return rc;
+  return fz_gemm_f32(batch, M, N, K, A, lda, sA, tA, B, ldb, sB, tB, C, ldc, sC, st);
+}
+
 int fz_comm_unique_id(unsigned char id[FZ_UNIQUE_ID_BYTES]) { std::memset(id, 0, FZ_UNIQUE_ID_BYTES); return FZ_OK; }
 int fz_comm_init(void **c, int world, int, const unsigned char *) {
   if (world != 1) return fail(FZ_ERR_UNSUPPORTED, "host test double: world must be 1");

@@ -94,3 +94,30 @@ def test_second_backward_zeroes_shared_grads(fake_fusion):
         g1 = a.get_grad()
         first = g1.to_numpy().copy()
         np.testing.assert_array_equal(first, [3.0, 3.0])
+
+
+def test_split_planes_follow_values(fake_fusion):
+    """A GEMM operand's TF32 remainder plane is split once per buffer and never
+    outlives the value: after `-=` or set_values the operand is a new buffer and gets
+    a new plane (the test double refuses a plane that does not match its operand)."""
+    F = fake_fusion
+    rng = np.random.default_rng(5)
+    a = rng.standard_normal((8, 12)).astype(np.float32)
+    w = rng.standard_normal((12, 4)).astype(np.float32)
+    x, W = api_cases.T(F, a), api_cases.T(F, w)
+    assert F.split_cache_enabled()
+    y1 = (x @ W).to_numpy()
+    launches = F.stats()["kernel_launches"]
+    y2 = (x @ W).to_numpy()  # both planes cached: one GEMM launch, no splits
+    assert F.stats()["kernel_launches"] == launches + 1
+    np.testing.assert_array_equal(y1, y2)
+    d = rng.standard_normal((12, 4)).astype(np.float32)
+    W -= api_cases.T(F, d)
+    np.testing.assert_allclose((x @ W).to_numpy(), a.astype(np.float64) @ (w - d), rtol=1e-5, atol=1e-5)
+    x.set_values(np.ones(96, np.float32))
+    np.testing.assert_allclose((x @ W).to_numpy(), np.ones((8, 12)) @ (w - d), rtol=1e-5, atol=1e-5)
+    F.set_split_cache(False)
+    try:
+        np.testing.assert_allclose((x @ W).to_numpy(), np.ones((8, 12)) @ (w - d), rtol=1e-5, atol=1e-5)
+    finally:
+        F.set_split_cache(True)

@@ -203,6 +203,35 @@ def test_gemm_3xtf32_long_k(capi, port, M, N, K):
     assert err <= 1e-5, err
 
 
+def test_tf32_lo_plane_bits(capi):
+    """fz_tf32_lo: x - (x with its 13 low mantissa bits cleared), exact, any length."""
+    for n in [1, 3, 4, 1027, (1 << 20) + 5]:
+        x = (RNG.standard_normal(n) * 10.0 ** RNG.integers(-30, 30, n)).astype(np.float32)
+        hi = (x.view(np.uint32) & np.uint32(0xFFFFE000)).view(np.float32)
+        dx, dl = capi.DeviceArray.from_numpy(x), capi.DeviceArray((n,))
+        capi.check(capi.lib().fz_tf32_lo(dl.ptr, dx.ptr, n, None))
+        assert_bits_equal(dl.numpy(), x - hi, f"tf32 lo n={n}")
+
+
+@pytest.mark.parametrize("tA,tB", [(False, False), (False, True), (True, False), (True, True)])
+@pytest.mark.parametrize("batch,M,N,K", [(1, 300, 520, 260), (2, 128, 256, 1024)])
+def test_gemm_split_planes_match_internal_split(capi, batch, M, N, K, tA, tB):
+    """fz_gemm_f32_split with caller-supplied lo planes gives fz_gemm_f32's bits."""
+    L = capi.lib()
+    A = RNG.standard_normal((batch, K, M) if tA else (batch, M, K)).astype(np.float32)
+    B = RNG.standard_normal((batch, N, K) if tB else (batch, K, N)).astype(np.float32)
+    want = _gemm(capi, A, B, tA, tB)
+    da, db, dc = capi.DeviceArray.from_numpy(A), capi.DeviceArray.from_numpy(B), capi.DeviceArray((batch, M, N))
+    la, lb = capi.DeviceArray(A.shape), capi.DeviceArray(B.shape)
+    capi.check(L.fz_tf32_lo(la.ptr, da.ptr, A.size, None))
+    capi.check(L.fz_tf32_lo(lb.ptr, db.ptr, B.size, None))
+    capi.check(L.fz_gemm_f32_split(batch, M, N, K, da.ptr, la.ptr, A.shape[2], A.shape[1] * A.shape[2],
+                                   int(tA), db.ptr, lb.ptr, B.shape[2], B.shape[1] * B.shape[2], int(tB),
+                                   dc.ptr, N, M * N, None))
+    capi.check(L.fz_kernel_status())
+    assert_bits_equal(dc.numpy(), want, "split planes")
+
+
 def _program(nodes, nleaves, outs):
     pg = C.pointer(C.c_char())  # placeholder to keep ctypes import used
     del pg
