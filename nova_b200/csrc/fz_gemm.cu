@@ -171,16 +171,31 @@ __device__ __forceinline__ void prefetch_map(const CUtensorMap *map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
+__device__ __forceinline__ void tma_load_4d(void *dst, const CUtensorMap *map, uint64_t *bar,
+                                            int c0, int c1, int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+
 // One operand's k-tile [row0, row0 + ROWS) x [k0, k0 + BK) into a stage tile.
-// K-major: one box {BK, ROWS}. MN-major: ROWS / 32 boxes {32, BK}, each a chunk of
-// MN_CHUNK_BYTES; rows past the operand's extent are zero-filled by the TMA unit.
+// K-major: one box {BK, ROWS}. MN-major: the tile is ROWS / 32 chunks of
+// MN_CHUNK_BYTES; a "wide" map (4D: 32 rows, K, chunk, batch) fetches all chunks in
+// one box, a narrow one (3D) one chunk per box. Rows past the operand's extent are
+// zero-filled by the TMA unit.
 template <bool MN, int ROWS>
 __device__ __forceinline__ void load_operand(uint8_t *dst, const CUtensorMap *map, uint64_t *bar,
-                                             int k0, int row0, int bz) {
+                                             int k0, int row0, int bz, bool wide) {
   if constexpr (MN) {
+    if (wide) {
+      tma_load_4d(dst, map, bar, 0, k0, row0 / MN_CHUNK, bz);
+    } else {
 #pragma unroll
-    for (int j = 0; j < ROWS / MN_CHUNK; ++j)
-      tma_load_3d(dst + j * MN_CHUNK_BYTES, map, bar, row0 + j * MN_CHUNK, k0, bz);
+      for (int j = 0; j < ROWS / MN_CHUNK; ++j)
+        tma_load_3d(dst + j * MN_CHUNK_BYTES, map, bar, row0 + j * MN_CHUNK, k0, bz);
+    }
   } else {
     tma_load_3d(dst, map, bar, k0, row0, bz);
   }
@@ -270,6 +285,7 @@ struct GemmArgs {
   int M, N, K, batch;
   int tiles_m, tiles_n, num_tiles, group_m;  // num_tiles counts work units (tiles x K splits)
   int splits, k_per_split;  // K is cut into `splits` ranges of k_per_split (multiple of BK)
+  int wide;                 // bits 0-3: map Ah, Al, Bh, Bl is a wide (4D) MN-major map
   int *err;
 };
 
@@ -382,10 +398,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           }
           mbar_expect_tx(&full_bar[s], STAGE_BYTES);
           const int k0 = kb + kt * BK;
-          load_operand<A_MN, BM>(stage_ptr(s, 0), &mapAh, &full_bar[s], k0, mb * BM, bz);
-          load_operand<A_MN, BM>(stage_ptr(s, 1), &mapAl, &full_bar[s], k0, mb * BM, bz);
-          load_operand<B_MN, BN>(stage_ptr(s, 2), &mapBh, &full_bar[s], k0, nb * BN, bz);
-          load_operand<B_MN, BN>(stage_ptr(s, 3), &mapBl, &full_bar[s], k0, nb * BN, bz);
+          load_operand<A_MN, BM>(stage_ptr(s, 0), &mapAh, &full_bar[s], k0, mb * BM, bz, args.wide & 1);
+          load_operand<A_MN, BM>(stage_ptr(s, 1), &mapAl, &full_bar[s], k0, mb * BM, bz, args.wide & 2);
+          load_operand<B_MN, BN>(stage_ptr(s, 2), &mapBh, &full_bar[s], k0, nb * BN, bz, args.wide & 4);
+          load_operand<B_MN, BN>(stage_ptr(s, 3), &mapBl, &full_bar[s], k0, nb * BN, bz, args.wide & 8);
         }
       }
       if (!ok) {
@@ -531,26 +547,44 @@ int get_encoder() {
   return rc;
 }
 
-// 3D map over one operand plane. K-major ([batch, rows, K], K innermost): box
-// {BK, box_rows, 1}, 64-byte swizzle (128-byte for BK = 32). MN-major ([batch, K,
-// rows], rows innermost): box {32, BK, 1}, 128-byte swizzle with 32-byte atoms,
-// fetched box_rows / 32 times per k-tile. TMA needs ld*4 and sb*4 to be multiples of 16 bytes and the
-// base 16-byte aligned; every box starts at an inner coordinate that is a multiple
-// of 16 (K-major) or 32 (MN-major) elements.
+// Map over one operand plane, K-major ([batch, rows, K], K innermost) or MN-major
+// ([batch, K, rows], rows innermost). TMA needs ld*4 and sb*4 to be multiples of 16
+// bytes and the base 16-byte aligned; every box starts at an inner coordinate that
+// is a multiple of 16 (K-major) or 32 (MN-major) elements, or at 0 (wide).
+// K-major: 3D, box {BK, box_rows, 1}, 64-byte swizzle (128-byte for BK = 32).
+// MN-major: 128-byte swizzle with 32-byte atoms. When ld is a multiple of 32 floats
+// and the rows fill whole 32-row chunks (or the plane is one of ours, padded with
+// zeros to its 32-float pitch), the map is "wide": 4D {32 rows, K, rows / 32
+// chunks, batch} with a chunk stride of 128 bytes, so one box {32, BK, box_rows /
+// 32, 1} lands the whole k-tile in the chunked layout and no read leaves a row's
+// pitch. Otherwise 3D {rows, K, batch} with one box {32, BK, 1} per chunk, the TMA
+// unit zero-filling past the rows. *wide reports which was made.
 int make_map(CUtensorMap *map, const float *base, bool mn, int64_t rows, int64_t K, int64_t ld,
-             int64_t sb, int64_t batch, int box_rows) {
+             int64_t sb, int64_t batch, int box_rows, bool padded, bool *wide) {
   if (batch == 1) sb = ld * (mn ? K : rows);
-  cuuint64_t dims[3] = {(cuuint64_t)(mn ? rows : K), (cuuint64_t)(mn ? K : rows), (cuuint64_t)batch};
-  cuuint64_t strides[2] = {(cuuint64_t)(ld * 4), (cuuint64_t)(sb * 4)};
-  cuuint32_t box[3] = {mn ? (cuuint32_t)MN_CHUNK : (cuuint32_t)BK,
-                       mn ? (cuuint32_t)BK : (cuuint32_t)box_rows, 1};
-  cuuint32_t estr[3] = {1, 1, 1};
-  const CUtensorMapSwizzle sw = mn ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B
-                               : SWIZZLE_BYTES == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
-                                                      : CU_TENSOR_MAP_SWIZZLE_64B;
-  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, (void *)base, dims, strides, box,
-                        estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
-                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  *wide = mn && ld % MN_CHUNK == 0 && (rows % MN_CHUNK == 0 || padded);
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r;
+  if (*wide) {
+    cuuint64_t dims[4] = {(cuuint64_t)MN_CHUNK, (cuuint64_t)K,
+                          (cuuint64_t)((rows + MN_CHUNK - 1) / MN_CHUNK), (cuuint64_t)batch};
+    cuuint64_t strides[3] = {(cuuint64_t)(ld * 4), (cuuint64_t)(MN_CHUNK * 4), (cuuint64_t)(sb * 4)};
+    cuuint32_t box[4] = {(cuuint32_t)MN_CHUNK, (cuuint32_t)BK, (cuuint32_t)(box_rows / MN_CHUNK), 1};
+    r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (void *)base, dims, strides, box, estr,
+                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B,
+                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  } else {
+    cuuint64_t dims[3] = {(cuuint64_t)(mn ? rows : K), (cuuint64_t)(mn ? K : rows), (cuuint64_t)batch};
+    cuuint64_t strides[2] = {(cuuint64_t)(ld * 4), (cuuint64_t)(sb * 4)};
+    cuuint32_t box[3] = {mn ? (cuuint32_t)MN_CHUNK : (cuuint32_t)BK,
+                         mn ? (cuuint32_t)BK : (cuuint32_t)box_rows, 1};
+    const CUtensorMapSwizzle sw = mn ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B
+                                 : SWIZZLE_BYTES == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                                        : CU_TENSOR_MAP_SWIZZLE_64B;
+    r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, (void *)base, dims, strides, box, estr,
+                 CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  }
   if (r != CUDA_SUCCESS)
     return fz::fail(FZ_ERR_CUDA, "cuTensorMapEncodeTiled failed with code " + std::to_string((int)r));
   return FZ_OK;
@@ -595,6 +629,7 @@ struct Operand {
   int64_t hi_ld, hi_sb;
   const float *lo;
   int64_t lo_ld, lo_sb;
+  bool hi_padded = false, lo_padded = false;  // planes written here, zero-padded to their pitch
 };
 
 // The raw operand can serve as the hi plane when TMA can address it.
@@ -609,7 +644,7 @@ int64_t workspace_floats(const Operand &o, const float *src, int64_t ld, int64_t
                          const float *lo_given, int64_t batch) {
   const bool direct = direct_hi(src, ld, sb, batch);
   if (direct && lo_given) return 0;
-  const int64_t plane = batch * o.rows * ((o.inner + 3) & ~(int64_t)3);
+  const int64_t plane = batch * o.rows * (o.mn ? round_up(o.inner, MN_CHUNK) : round_up(o.inner, 4));
   return plane * (direct ? 1 : 2);
 }
 
@@ -625,7 +660,8 @@ int prepare(const float *src, int64_t ld, int64_t sb, const float *lo_given, int
     op->hi_sb = op->lo_sb = sb;
     return FZ_OK;
   }
-  const int64_t pitch = (op->inner + 3) & ~(int64_t)3;  // 16-byte row pitch for TMA
+  // row pitch: 16 bytes for TMA; MN-major planes a multiple of 32 floats (wide map)
+  const int64_t pitch = op->mn ? round_up(op->inner, MN_CHUNK) : round_up(op->inner, 4);
   const int64_t plane = batch * op->rows * pitch;
   float *lo = ws, *hi = direct ? nullptr : ws + plane;
   unsigned grid = fz::grid_for(plane / 4 + 1, 256, 8, 4);
@@ -634,6 +670,7 @@ int prepare(const float *src, int64_t ld, int64_t sb, const float *lo_given, int
   op->lo = lo;
   op->lo_ld = pitch;
   op->lo_sb = op->rows * pitch;
+  op->lo_padded = true;
   if (direct) {
     op->hi = src;
     op->hi_ld = ld;
@@ -642,6 +679,7 @@ int prepare(const float *src, int64_t ld, int64_t sb, const float *lo_given, int
     op->hi = hi;
     op->hi_ld = pitch;
     op->hi_sb = op->rows * pitch;
+    op->hi_padded = true;
   }
   return FZ_OK;
 }
@@ -704,10 +742,12 @@ int gemm_impl(int64_t batch, int64_t M, int64_t N, int64_t K, const float *A, co
   if (!rc) rc = prepare(B, ldb, strideB, B_lo, batch, ws + a_need, &ob, s);
 
   CUtensorMap mAh, mAl, mBh, mBl;
-  if (!rc) rc = make_map(&mAh, oa.hi, oa.mn, M, K, oa.hi_ld, oa.hi_sb, batch, BM);
-  if (!rc) rc = make_map(&mAl, oa.lo, oa.mn, M, K, oa.lo_ld, oa.lo_sb, batch, BM);
-  if (!rc) rc = make_map(&mBh, ob.hi, ob.mn, N, K, ob.hi_ld, ob.hi_sb, batch, BN);
-  if (!rc) rc = make_map(&mBl, ob.lo, ob.mn, N, K, ob.lo_ld, ob.lo_sb, batch, BN);
+  bool wide[4] = {false, false, false, false};
+  if (!rc) rc = make_map(&mAh, oa.hi, oa.mn, M, K, oa.hi_ld, oa.hi_sb, batch, BM, oa.hi_padded, &wide[0]);
+  if (!rc) rc = make_map(&mAl, oa.lo, oa.mn, M, K, oa.lo_ld, oa.lo_sb, batch, BM, oa.lo_padded, &wide[1]);
+  if (!rc) rc = make_map(&mBh, ob.hi, ob.mn, N, K, ob.hi_ld, ob.hi_sb, batch, BN, ob.hi_padded, &wide[2]);
+  if (!rc) rc = make_map(&mBl, ob.lo, ob.mn, N, K, ob.lo_ld, ob.lo_sb, batch, BN, ob.lo_padded, &wide[3]);
+  const int wide_mask = (int)wide[0] | (int)wide[1] << 1 | (int)wide[2] << 2 | (int)wide[3] << 3;
   const int tiles_m = (int)((M + BM - 1) / BM), tiles_n = (int)((N + BN - 1) / BN);
   const int64_t tiles = (int64_t)tiles_m * tiles_n * batch;
   const bool dense_c = ldc == N && (batch == 1 || strideC == M * N);
@@ -727,7 +767,7 @@ int gemm_impl(int64_t batch, int64_t M, int64_t N, int64_t K, const float *A, co
     GemmArgs ga{partial ? partial : C, partial ? N : ldc, partial ? M * N : strideC,
                 batch * M * N, (int)M, (int)N, (int)K, (int)batch,
                 tiles_m, tiles_n, (int)num_units, tiles_m < 16 ? tiles_m : 16,
-                real_splits, (int)kps, err};
+                real_splits, (int)kps, wide_mask, err};
     const unsigned grid = (unsigned)(num_units < fz::num_sms() ? num_units : fz::num_sms());
     if (!oa.mn && !ob.mn) rc = launch_gemm<false, false>(mAh, mAl, mBh, mBl, ga, grid, smem, s);
     else if (!oa.mn && ob.mn) rc = launch_gemm<false, true>(mAh, mAl, mBh, mBl, ga, grid, smem, s);
