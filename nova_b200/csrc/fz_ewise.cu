@@ -6,10 +6,13 @@
 //   * 1 dim, all strides 1            -> plain contiguous stream (fast path)
 //   * 1 dim, one operand stride 0     -> scalar operand
 //   * 2 dims [rows, cols], a [cols]   -> row broadcast (bias add)
-// The kernel maps each thread to groups of VEC=4 consecutive elements of the
-// innermost dim (128-bit loads/stores when every operand with inner stride 1 is
-// 16-byte aligned at each row start), with a grid-stride loop over groups.
-// Operands with inner stride 0 are loaded once per group and replicated.
+// Plans of 1 or 2 dims with a long inner dim (>= 1024) on the 128-bit path run the
+// tiled kernel (no per-element index arithmetic, U loads per thread in flight);
+// the rest run the generic kernel, which maps each thread to groups of VEC=4
+// consecutive elements of the innermost dim (128-bit loads/stores when every
+// operand with inner stride 1 is 16-byte aligned at each row start), with a
+// grid-stride loop over groups. Operands with inner stride 0 are loaded once per
+// group and replicated.
 #include "fz_common.cuh"
 #include "fz_ewise_plan.hpp"
 
@@ -101,6 +104,67 @@ __global__ void __launch_bounds__(256) ewise_kernel(EwPlan p, float *__restrict_
   }
 }
 
+// Plans of at most 2 dims ([rows, inner], inner >= 1024) on the 128-bit path: the
+// index space is cut into tiles of one row x 1024*U columns and a CTA walks tiles
+// blockIdx.x, +gridDim.x, ... (one division per tile, none per element). Each thread
+// loads its U float4 groups of a tile (256 groups apart, so every warp access is
+// one contiguous 512-byte run) before computing and storing any, keeping U loads
+// per operand in flight. Inner strides are 0 (broadcast) or 1.
+template <int NIN, int OP, int U>
+__global__ void __launch_bounds__(256) ewise_tiles_kernel(EwPlan p, float *__restrict__ out,
+                                                          const float *__restrict__ a,
+                                                          const float *__restrict__ b) {
+  constexpr int64_t TW = 1024 * U;
+  const int64_t inner = p.size[p.ndim - 1];
+  const int64_t ctiles = (inner + TW - 1) / TW;
+  const int64_t total = p.rows * ctiles;
+  const bool va = p.stride[1][p.ndim - 1] != 0;
+  const bool vb = NIN == 2 && p.stride[2][p.ndim - 1] != 0;
+  const int64_t ro = p.ndim > 1 ? p.stride[0][0] : 0, ra = p.ndim > 1 ? p.stride[1][0] : 0;
+  const int64_t rb = (NIN == 2 && p.ndim > 1) ? p.stride[2][0] : 0;
+  for (int64_t t = blockIdx.x; t < total; t += gridDim.x) {
+    const int64_t row = t / ctiles;
+    const int64_t c0 = (t - row * ctiles) * TW + threadIdx.x * 4;
+    const float *pa = a + row * ra;
+    const float *pb = NIN == 2 ? b + row * rb : nullptr;
+    float *po = out + row * ro;
+    float4 x[U], y[U];
+#pragma unroll
+    for (int j = 0; j < U; ++j) {
+      const int64_t c = c0 + j * 1024;
+      if (c + 4 <= inner) {
+        x[j] = va ? ld4(pa + c) : make_float4(*pa, *pa, *pa, *pa);
+        if constexpr (NIN == 2) y[j] = vb ? ld4(pb + c) : make_float4(*pb, *pb, *pb, *pb);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < U; ++j) {
+      const int64_t c = c0 + j * 1024;
+      if (c + 4 <= inner) {
+        float4 r;
+        if constexpr (NIN == 2) {
+          r.x = fzd::binop_t<OP>(x[j].x, y[j].x);
+          r.y = fzd::binop_t<OP>(x[j].y, y[j].y);
+          r.z = fzd::binop_t<OP>(x[j].z, y[j].z);
+          r.w = fzd::binop_t<OP>(x[j].w, y[j].w);
+        } else {
+          r.x = fzd::unop_t<OP>(x[j].x);
+          r.y = fzd::unop_t<OP>(x[j].y);
+          r.z = fzd::unop_t<OP>(x[j].z);
+          r.w = fzd::unop_t<OP>(x[j].w);
+        }
+        st4(po + c, r);
+      } else {
+        for (int64_t e = c; e < inner; ++e) {
+          const float xa = pa[va ? e : 0];
+          if constexpr (NIN == 2) po[e] = fzd::binop_t<OP>(xa, pb[vb ? e : 0]);
+          else po[e] = fzd::unop_t<OP>(xa);
+        }
+      }
+    }
+  }
+}
+
 template <int NIN, int OP>
 int launch_op(const EwPlan &p, float *out, const float *a, const float *b, cudaStream_t s) {
   int64_t inner = p.ndim ? p.size[p.ndim - 1] : 1;
@@ -116,6 +180,16 @@ int launch_op(const EwPlan &p, float *out, const float *a, const float *b, cudaS
     if (si != 1 || ((uintptr_t)base[k] & 15)) vec = false;
     for (int d = 0; vec && d + 1 < p.ndim; ++d)
       if (p.stride[k][d] % 4) vec = false;
+  }
+  if (vec && p.ndim <= 2 && inner >= 1024 && p.stride[0][p.ndim - 1] == 1) {
+    const int U = inner >= 4096 ? 4 : inner >= 2048 ? 2 : 1;
+    const int64_t tiles = p.rows * ((inner + 1024 * U - 1) / (1024 * U));
+    const unsigned grid = (unsigned)(tiles < (int64_t)fz::num_sms() * 8 ? tiles : fz::num_sms() * 8);
+    if (U == 4) ewise_tiles_kernel<NIN, OP, 4><<<grid, 256, 0, s>>>(p, out, a, b);
+    else if (U == 2) ewise_tiles_kernel<NIN, OP, 2><<<grid, 256, 0, s>>>(p, out, a, b);
+    else ewise_tiles_kernel<NIN, OP, 1><<<grid, 256, 0, s>>>(p, out, a, b);
+    FZ_CHECK_LAUNCH();
+    return FZ_OK;
   }
   int V = vec ? 4 : 1;
   int64_t groups = p.rows * ((inner + V - 1) / V);

@@ -10,8 +10,9 @@
 //
 // The generated source is specialised on the program, the per-operand class of
 // the innermost stride (0 = broadcast, 1 = unit, other = general), the vector
-// width (4 when every unit-stride operand is 16-byte aligned at each row) and the
-// index width. Shapes and strides stay runtime parameters, so one compiled kernel
+// width (4 when every unit-stride operand is 16-byte aligned at each row), the
+// index width and the loop form (tiled over rows x 1024*U columns for plans of at
+// most 2 dims with a long inner dim, else a generic ND grid-stride loop). Shapes and strides stay runtime parameters, so one compiled kernel
 // serves every shape with the same structure.
 #include <cuda.h>
 #include <nvrtc.h>
@@ -116,7 +117,62 @@ int validate(const fz_program &pg) {
 std::string ref_name(int s) { return s >= 0 ? "t" + std::to_string(s) : "l" + std::to_string(-1 - s); }
 
 // cls[k]: inner-stride class of operand k (0 broadcast, 1 unit, 2 general)
-std::string generate(const fz_program &pg, const int *cls, int vec, bool i64) {
+// Tiled form for plans of at most 2 dims on the 128-bit path with inner >= 1024:
+// tiles of one row x 1024*U columns walked by whole CTAs, one division per tile,
+// each thread loading its U float4 groups of every leaf before evaluating.
+void generate_tiles(std::ostringstream &o, const fz_program &pg, const int *cls, int U) {
+  const int nout = pg.num_outputs, nleaf = pg.num_leaves, nops = nout + nleaf;
+  o << "extern \"C\" __global__ void __launch_bounds__(256) fz_fused(const FusedParams p) {\n"
+    << "  const long long inner = p.size[p.ndim - 1];\n"
+    << "  const long long TW = " << 1024 * U << ";\n"
+    << "  const long long ctiles = (inner + TW - 1) / TW;\n"
+    << "  const long long total = p.rows * ctiles;\n";
+  for (int k = 0; k < nops; ++k)
+    o << "  const long long r" << k << " = p.ndim > 1 ? p.stride[" << k << "][0] : 0;\n";
+  o << "  for (long long t = blockIdx.x; t < total; t += gridDim.x) {\n"
+    << "    const long long row = t / ctiles;\n"
+    << "    const long long c0 = (t - row * ctiles) * TW + threadIdx.x * 4;\n";
+  for (int k = 0; k < nops; ++k)
+    o << "    float *b" << k << " = p.ptr[" << k << "] + row * r" << k << ";\n";
+  for (int lk = 0; lk < nleaf; ++lk) o << "    float4 v" << lk << "[" << U << "];\n";
+  o << "#pragma unroll\n    for (int j = 0; j < " << U << "; ++j) {\n"
+    << "      const long long c = c0 + j * 1024;\n"
+    << "      if (c + 4 <= inner) {\n";
+  for (int k = nout; k < nops; ++k) {
+    const int lk = k - nout;
+    if (cls[k] == 1)
+      o << "        v" << lk << "[j] = *reinterpret_cast<const float4 *>(b" << k << " + c);\n";
+    else
+      o << "        { const float s = b" << k << "[0]; v" << lk << "[j] = make_float4(s, s, s, s); }\n";
+  }
+  o << "      }\n    }\n";
+  o << "#pragma unroll\n    for (int j = 0; j < " << U << "; ++j) {\n"
+    << "      const long long c = c0 + j * 1024;\n"
+    << "      if (c + 4 <= inner) {\n";
+  for (int k = 0; k < nout; ++k) o << "        float4 q" << k << ";\n";
+  const char *lanes[4] = {"x", "y", "z", "w"};
+  for (int ln = 0; ln < 4; ++ln) {
+    o << "        fz_eval(";
+    for (int lk = 0; lk < nleaf; ++lk) o << "v" << lk << "[j]." << lanes[ln] << ", ";
+    for (int k = 0; k < nout; ++k) o << "q" << k << "." << lanes[ln] << (k + 1 < nout ? ", " : "");
+    o << ");\n";
+  }
+  for (int k = 0; k < nout; ++k)
+    o << "        *reinterpret_cast<float4 *>(b" << k << " + c) = q" << k << ";\n";
+  o << "      } else {\n"
+    << "        for (long long e = c; e < inner; ++e) {\n";
+  for (int k = nout; k < nops; ++k)
+    o << "          const float e" << (k - nout) << " = b" << k << "[" << (cls[k] == 1 ? "e" : "0") << "];\n";
+  for (int k = 0; k < nout; ++k) o << "          float s" << k << ";\n";
+  o << "          fz_eval(";
+  for (int lk = 0; lk < nleaf; ++lk) o << "e" << lk << ", ";
+  for (int k = 0; k < nout; ++k) o << "s" << k << (k + 1 < nout ? ", " : "");
+  o << ");\n";
+  for (int k = 0; k < nout; ++k) o << "          b" << k << "[e] = s" << k << ";\n";
+  o << "        }\n      }\n    }\n  }\n}\n";
+}
+
+std::string generate(const fz_program &pg, const int *cls, int vec, bool i64, int tiles_u) {
   std::ostringstream o;
   o << kPrelude;
   const int nout = pg.num_outputs, nleaf = pg.num_leaves, nops = nout + nleaf;
@@ -139,6 +195,10 @@ std::string generate(const fz_program &pg, const int *cls, int vec, bool i64) {
   }
   for (int k = 0; k < nout; ++k) o << "  o" << k << " = t" << pg.out_node[k] << ";\n";
   o << "}\n";
+  if (tiles_u) {
+    generate_tiles(o, pg, cls, tiles_u);
+    return o.str();
+  }
   const char *IDX = i64 ? "long long" : "int";
   o << "extern \"C\" __global__ void __launch_bounds__(256) fz_fused(const FusedParams p) {\n"
     << "  typedef " << IDX << " IDX;\n"
@@ -281,12 +341,14 @@ int fz_fused_launch(const fz_program *prog, const fz_ewise_plan *plan, float *co
   const int V = vec ? 4 : 1;
   const int64_t groups = p.rows * ((inner + V - 1) / V);
   const bool i64 = groups > (int64_t)0x7fffffff - (int64_t)fz::num_sms() * 2048;
+  const int U = (vec && p.ndim <= 2 && inner >= 1024) ? (inner >= 4096 ? 4 : inner >= 2048 ? 2 : 1) : 0;
   // cache key: program bytes + specialisation
   std::string key(reinterpret_cast<const char *>(prog), offsetof(fz_program, nodes) +
                                                             sizeof(fz_node) * prog->num_nodes);
   for (int k = 0; k < nops; ++k) key.push_back((char)('0' + cls[k]));
   key.push_back((char)V);
   key.push_back(i64 ? 'L' : 'I');
+  key.push_back((char)('0' + U));
   cudaKernel_t kern = nullptr;
   {
     Cache &c = cache();
@@ -295,7 +357,7 @@ int fz_fused_launch(const fz_program *prog, const fz_ewise_plan *plan, float *co
     if (it != c.kernels.end()) {
       kern = it->second;
     } else {
-      rc = compile(generate(*prog, cls, V, i64), &kern);
+      rc = compile(generate(*prog, cls, V, i64, U), &kern);
       if (rc) return rc;
       c.kernels.emplace(key, kern);
     }
@@ -309,7 +371,13 @@ int fz_fused_launch(const fz_program *prog, const fz_ewise_plan *plan, float *co
     for (int d = 0; d < p.ndim; ++d) fp.stride[k][d] = p.stride[k][d];
     fp.ptr[k] = ptrs[k];
   }
-  unsigned grid = fz::grid_for(groups, 256 * 2, 8);
+  unsigned grid;
+  if (U) {
+    const int64_t tiles = p.rows * ((inner + 1024 * U - 1) / (1024 * U));
+    grid = (unsigned)(tiles < (int64_t)fz::num_sms() * 8 ? tiles : fz::num_sms() * 8);
+  } else {
+    grid = fz::grid_for(groups, 256 * 2, 8);
+  }
   void *args[] = {&fp};
   FZ_CUDA(cudaLaunchKernel((const void *)kern, dim3(grid), dim3(256), args, 0, fz::resolve(stream)));
   fz::note_launch();
