@@ -53,7 +53,8 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--kernel", default=None,
                     help="run one hot-path kernel on a profiling-sized case instead of the step "
-                         "(gemm, gemm_wgrad, add, bcast_add, exp, sum_ax0, sum_ax1, swapaxes, bias_relu)")
+                         "(gemm, gemm_wgrad, add, bcast_add, exp, log, sqrt, sum_ax0, sum_ax1, max_ax0, "
+                         "sum_rows64, swapaxes, bias_relu)")
     ap.add_argument("--reps", type=int, default=3)
     return ap.parse_args()
 
@@ -342,6 +343,10 @@ def run_ours(args):
     X = model.tensor(Xh, True)  # nova's Tensor defaults to requires_grad=True
     Y = model.tensor(Yh, True)
 
+    kernels = None
+    if d.world == 1 and not args.no_kernels:
+        # per-kernel sweep first, on a GPU not yet heated by the GEMM-bound step
+        kernels = kernel_suite(capi, peaks())
     for _ in range(args.warmup):
         model.step(X, Y, LR, comm)
     F.synchronize()
@@ -405,8 +410,8 @@ def run_ours(args):
     if d.world == 1 and d.rank == 0:
         pk = peaks()
         res["roofline"] = gemm_roofline(capi, pk, local)
-        if not args.no_kernels:
-            res["kernels"] = kernel_suite(capi, pk)
+        if kernels is not None:
+            res["kernels"] = kernels
         if not args.no_cpu_baseline:
             try:
                 res["cpu_baseline"] = cpu_baseline_ref()
@@ -512,9 +517,14 @@ def run_kernel(args):
         plan1 = A.make_plan((n,), [(n,), (n,)])
         bplan = A.make_plan((r, r), [(r, r), (r, r), (1, r)])
         shp = (C.c_int64 * 2)(r, r)
+        q = 1 << 20  # [64,256,64,64] as 2^20 rows of 64 (first call of the axes-(0,2,3) chain)
         fn, work = {
             "add": (lambda: A.check(L.fz_ewise_binary_contig(0, n, o.ptr, a.ptr, b.ptr, None)), 12.0 * n),
             "exp": (lambda: A.check(L.fz_ewise_unary(0, C.byref(plan1), o.ptr, a.ptr, None)), 8.0 * n),
+            "log": (lambda: A.check(L.fz_ewise_unary(1, C.byref(plan1), o.ptr, a.ptr, None)), 8.0 * n),
+            "sqrt": (lambda: A.check(L.fz_ewise_unary(2, C.byref(plan1), o.ptr, a.ptr, None)), 8.0 * n),
+            "max_ax0": (lambda: A.check(L.fz_reduce(2, o.ptr, a.ptr, 1, r, r, None)), 4.0 * r * r),
+            "sum_rows64": (lambda: A.check(L.fz_reduce(0, o.ptr, a.ptr, q, 64, 1, None)), 4.0 * q * 64),
             "bcast_add": (lambda: A.check(L.fz_ewise_binary(0, C.byref(bplan), o.ptr, a.ptr, b.ptr, None)),
                           8.0 * r * r + 4 * r),
             "sum_ax1": (lambda: A.check(L.fz_reduce(0, o.ptr, a.ptr, r, r, 1, None)), 4.0 * r * r),

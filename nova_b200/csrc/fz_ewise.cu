@@ -182,10 +182,12 @@ int launch_op(const EwPlan &p, float *out, const float *a, const float *b, cudaS
       if (p.stride[k][d] % 4) vec = false;
   }
   if (vec && p.ndim <= 2 && inner >= 1024 && p.stride[0][p.ndim - 1] == 1) {
-    const int U = inner >= 4096 ? 4 : inner >= 2048 ? 2 : 1;
+    // one input: 8 float4 per thread in flight; two inputs: 4 of each
+    const int U = (NIN == 1 && inner >= 8192) ? 8 : inner >= 4096 ? 4 : inner >= 2048 ? 2 : 1;
     const int64_t tiles = p.rows * ((inner + 1024 * U - 1) / (1024 * U));
     const unsigned grid = (unsigned)(tiles < (int64_t)fz::num_sms() * 8 ? tiles : fz::num_sms() * 8);
-    if (U == 4) ewise_tiles_kernel<NIN, OP, 4><<<grid, 256, 0, s>>>(p, out, a, b);
+    if (U == 8) ewise_tiles_kernel<NIN, OP, (NIN == 1 ? 8 : 4)><<<grid, 256, 0, s>>>(p, out, a, b);
+    else if (U == 4) ewise_tiles_kernel<NIN, OP, 4><<<grid, 256, 0, s>>>(p, out, a, b);
     else if (U == 2) ewise_tiles_kernel<NIN, OP, 2><<<grid, 256, 0, s>>>(p, out, a, b);
     else ewise_tiles_kernel<NIN, OP, 1><<<grid, 256, 0, s>>>(p, out, a, b);
     FZ_CHECK_LAUNCH();

@@ -341,7 +341,10 @@ int fz_fused_launch(const fz_program *prog, const fz_ewise_plan *plan, float *co
   const int V = vec ? 4 : 1;
   const int64_t groups = p.rows * ((inner + V - 1) / V);
   const bool i64 = groups > (int64_t)0x7fffffff - (int64_t)fz::num_sms() * 2048;
-  const int U = (vec && p.ndim <= 2 && inner >= 1024) ? (inner >= 4096 ? 4 : inner >= 2048 ? 2 : 1) : 0;
+  // tiled form: one leaf keeps 8 float4 per thread in flight, more leaves 4 each
+  const int U = (vec && p.ndim <= 2 && inner >= 1024)
+                    ? ((nleaf <= 1 && inner >= 8192) ? 8 : inner >= 4096 ? 4 : inner >= 2048 ? 2 : 1)
+                    : 0;
   // cache key: program bytes + specialisation
   std::string key(reinterpret_cast<const char *>(prog), offsetof(fz_program, nodes) +
                                                             sizeof(fz_node) * prog->num_nodes);

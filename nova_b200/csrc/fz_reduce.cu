@@ -9,11 +9,16 @@
 //     too few rows to fill 148 SMs a row is split over several CTAs.
 //   * inner > 1 (reducing a leading axis): each thread owns 4 adjacent columns
 //     (one float4 per row read, fully coalesced across the warp) and walks `len`;
-//     when outer*inner/4 threads cannot fill the GPU, `len` is split into chunks.
-// Split work writes fp32 partials to stream-ordered scratch and a second pass
-// reduces them, so results do not depend on scheduling (no atomics).
+//     when outer*inner/4 threads cannot fill the GPU, `len` is split: over the 8
+//     warps of a CTA and the up to 8 CTAs of a thread-block cluster, folded in a
+//     fixed order through shared and distributed shared memory in the same launch
+//     (enough columns), or into chunks whose partials a second pass reduces.
+// Split row work writes fp32 partials to stream-ordered scratch and a second pass
+// reduces them. No atomics: results do not depend on scheduling.
 // mean = sum / (float)len with an IEEE division, as fusion::math::mean does
 // (fusion/src/Fusion/ops/Reduce.hpp:27-36).
+#include <cooperative_groups.h>
+
 #include <mutex>
 
 #include "fz_common.cuh"
@@ -21,13 +26,12 @@
 namespace {
 
 __device__ __forceinline__ float max_nan(float a, float b) {
-  // NaN propagates; otherwise the larger value, +0 ranking above -0. Order
-  // independent, so a tree and a sequential scan agree bit for bit.
-  if (a != a) return a;
-  if (b != b) return b;
-  if (a > b) return a;
-  if (b > a) return b;
-  return signbit(a) ? b : a;
+  // NaN propagates (as the canonical NaN); otherwise the larger value, +0 ranking
+  // above -0: one max.NaN.f32. Order independent, so a tree and a sequential scan
+  // agree bit for bit.
+  float r;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
 }
 
 template <int OP>
@@ -51,32 +55,47 @@ __device__ __forceinline__ float group_reduce(float v) {
   return v;
 }
 
-// Rows of `len` floats (row stride `ld`), G lanes per row. Each lane strides the row
-// by G (vectorised by 4 when the row is 16-byte aligned).
-template <int OP, int G>
+// Rows of `len` floats (row stride `ld`), G lanes per row, R consecutive rows per
+// group at a time: each lane strides its rows by G (vectorised by 4 when the rows
+// are 16-byte aligned) and issues the loads of all R rows before reducing any, so
+// short rows still keep R loads per lane in flight.
+template <int OP, int G, int R>
 __global__ void __launch_bounds__(256) rows_group_kernel(const float *__restrict__ in,
                                                          float *__restrict__ out, int64_t rows,
                                                          int64_t len, int64_t ld,
                                                          int64_t div_len, int final, int vec) {
   const int lane = threadIdx.x % G;
   const int64_t groups_total = (int64_t)gridDim.x * (blockDim.x / G);
-  for (int64_t r = (int64_t)blockIdx.x * (blockDim.x / G) + threadIdx.x / G; r < rows;
-       r += groups_total) {
-    const float *p = in + r * ld;
-    float acc = Red<OP>::init();
-    if (vec) {
-      int64_t nv = len >> 2;
-      const float4 *p4 = reinterpret_cast<const float4 *>(p);
-      for (int64_t j = lane; j < nv; j += G) {
-        float4 q = p4[j];
-        acc = Red<OP>::op(acc, Red<OP>::op(Red<OP>::op(q.x, q.y), Red<OP>::op(q.z, q.w)));
-      }
-      for (int64_t j = (nv << 2) + lane; j < len; j += G) acc = Red<OP>::op(acc, p[j]);
-    } else {
-      for (int64_t j = lane; j < len; j += G) acc = Red<OP>::op(acc, p[j]);
+  const int64_t nv = vec ? len >> 2 : 0;
+  for (int64_t r0 = ((int64_t)blockIdx.x * (blockDim.x / G) + threadIdx.x / G) * R; r0 < rows;
+       r0 += groups_total * R) {
+    float acc[R];
+#pragma unroll
+    for (int i = 0; i < R; ++i) acc[i] = Red<OP>::init();
+    for (int64_t j = lane; j < nv; j += G) {
+      float4 q[R];
+#pragma unroll
+      for (int i = 0; i < R; ++i)
+        if (r0 + i < rows) q[i] = reinterpret_cast<const float4 *>(in + (r0 + i) * ld)[j];
+#pragma unroll
+      for (int i = 0; i < R; ++i)
+        if (r0 + i < rows)
+          acc[i] = Red<OP>::op(acc[i], Red<OP>::op(Red<OP>::op(q[i].x, q[i].y),
+                                                   Red<OP>::op(q[i].z, q[i].w)));
     }
-    acc = group_reduce<OP, G>(acc);
-    if (lane == 0) out[r] = finish<OP>(acc, div_len, final);
+#pragma unroll
+    for (int i = 0; i < R; ++i) {
+      if (r0 + i >= rows) break;
+      const float *p = in + (r0 + i) * ld;
+      for (int64_t j = (nv << 2) + lane; j < len; j += G) acc[i] = Red<OP>::op(acc[i], p[j]);
+    }
+#pragma unroll
+    for (int i = 0; i < R; ++i) acc[i] = group_reduce<OP, G>(acc[i]);
+    if (lane == 0) {
+#pragma unroll
+      for (int i = 0; i < R; ++i)
+        if (r0 + i < rows) out[r0 + i] = finish<OP>(acc[i], div_len, final);
+    }
   }
 }
 
@@ -194,20 +213,109 @@ __global__ void __launch_bounds__(256) cols_kernel(const float *__restrict__ in,
   }
 }
 
+// Columns in one pass, with a thread-block cluster along `len`. The CS CTAs of a
+// cluster (blockIdx.y = rank) reduce the same 128 columns of one outer slice over
+// consecutive row ranges; inside a CTA the 8 warps split the range (rows ty,
+// ty + 8, ...; 4 rows in flight per thread) and fold their partials through shared
+// memory in warp order, then CTA 0 folds the CTAs' partials through distributed
+// shared memory in rank order. The order is fixed, so the result does not depend
+// on scheduling, and no scratch memory or second launch is needed.
+template <int OP>
+__global__ void __launch_bounds__(256, 4) cols_cluster_kernel(const float *__restrict__ in,
+                                                           float *__restrict__ out, int64_t outer,
+                                                           int64_t len, int64_t inner,
+                                                           int64_t rows_per_cta, int64_t div_len) {
+  namespace cg = cooperative_groups;
+  cg::cluster_group cluster = cg::this_cluster();
+  __shared__ float4 warp_part[8][32];
+  __shared__ float4 cta_part[32];
+  const int tx = threadIdx.x % 32, ty = threadIdx.x / 32;
+  const int64_t cblocks = (inner + 127) / 128;
+  const int64_t o = (int64_t)blockIdx.x / cblocks, cb = (int64_t)blockIdx.x - o * cblocks;
+  const unsigned rank = cluster.block_rank();
+  const unsigned cs = cluster.num_blocks();
+  const int64_t c = cb * 128 + tx * 4;
+  const int64_t beg = (int64_t)rank * rows_per_cta;
+  const int64_t end = beg + rows_per_cta < len ? beg + rows_per_cta : len;
+  const float z = Red<OP>::init();
+  float4 acc = make_float4(z, z, z, z);
+  auto fold = [](float4 a, float4 b) {
+    return make_float4(Red<OP>::op(a.x, b.x), Red<OP>::op(a.y, b.y), Red<OP>::op(a.z, b.z),
+                       Red<OP>::op(a.w, b.w));
+  };
+  if (c < inner) {
+    const float *p = in + o * len * inner + c;
+    int64_t r = beg + ty;
+    for (; r + 24 < end; r += 32) {
+      const float4 x0 = *reinterpret_cast<const float4 *>(p + r * inner);
+      const float4 x1 = *reinterpret_cast<const float4 *>(p + (r + 8) * inner);
+      const float4 x2 = *reinterpret_cast<const float4 *>(p + (r + 16) * inner);
+      const float4 x3 = *reinterpret_cast<const float4 *>(p + (r + 24) * inner);
+      acc = fold(acc, fold(fold(x0, x1), fold(x2, x3)));
+    }
+    for (; r < end; r += 8) acc = fold(acc, *reinterpret_cast<const float4 *>(p + r * inner));
+  }
+  warp_part[ty][tx] = acc;
+  __syncthreads();
+  if (ty == 0) {
+    float4 v = warp_part[0][tx];
+#pragma unroll
+    for (int w = 1; w < 8; ++w) v = fold(v, warp_part[w][tx]);
+    cta_part[tx] = v;
+  }
+  cluster.sync();  // every CTA's partial is in its shared memory
+  if (rank == 0 && ty == 0) {
+    float4 v = cta_part[tx];
+    for (unsigned k = 1; k < cs; ++k) v = fold(v, *cluster.map_shared_rank(&cta_part[tx], k));
+    if (c < inner)
+      *reinterpret_cast<float4 *>(out + o * inner + c) =
+          make_float4(finish<OP>(v.x, div_len, true), finish<OP>(v.y, div_len, true),
+                      finish<OP>(v.z, div_len, true), finish<OP>(v.w, div_len, true));
+  }
+  cluster.sync();  // keep every CTA's shared memory alive until CTA 0 has read it
+}
+
+template <int OP>
+int launch_cols_cluster(const float *in, float *out, int64_t outer, int64_t len, int64_t inner,
+                        int cs, cudaStream_t s) {
+  const int64_t cblocks = (inner + 127) / 128;
+  const int64_t rows_per_cta = (len + cs - 1) / cs;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3((unsigned)(outer * cblocks), (unsigned)cs, 1);
+  cfg.blockDim = dim3(256, 1, 1);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = (unsigned)cs;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  FZ_CUDA(cudaLaunchKernelEx(&cfg, cols_cluster_kernel<OP>, in, out, outer, len, inner,
+                             rows_per_cta, len));
+  fz::note_launch();
+  return FZ_OK;
+}
+
 template <int OP>
 int launch_rows_group(const float *in, float *out, int64_t rows, int64_t len, int64_t ld,
                       int64_t div_len, bool final, cudaStream_t s) {
   int vec = (ld % 4 == 0) && (((uintptr_t)in & 15) == 0);
   int G = 1;
   while (G < 32 && (int64_t)G * 4 * 2 < len) G *= 2;
-  int64_t per_cta = 256 / G;
+  // rows in flight per group: short rows take several, long ones fill the lanes alone
+  const int R = len <= 256 ? 4 : len <= 1024 ? 2 : 1;
+  int64_t per_cta = 256 / G * R;
   unsigned grid = fz::grid_for(rows, per_cta, 8, 4);
-#define FZ_RG(g)                                                                          \
-  case g:                                                                                 \
-    rows_group_kernel<OP, g><<<grid, 256, 0, s>>>(in, out, rows, len, ld, div_len, final, \
-                                                   vec);                                  \
-    break;
-  switch (G) { FZ_RG(1) FZ_RG(2) FZ_RG(4) FZ_RG(8) FZ_RG(16) FZ_RG(32) }
+#define FZ_RG(g, r)                                                                          \
+  if (G == g && R == r) {                                                                    \
+    rows_group_kernel<OP, g, r><<<grid, 256, 0, s>>>(in, out, rows, len, ld, div_len, final, \
+                                                      vec);                                  \
+  } else
+  FZ_RG(1, 4) FZ_RG(2, 4) FZ_RG(4, 4) FZ_RG(8, 4) FZ_RG(16, 4) FZ_RG(32, 4)
+  FZ_RG(32, 2) FZ_RG(32, 1) {
+    return fz::fail(FZ_ERR_INVALID, "fz_reduce: no row-group kernel for this row length");
+  }
 #undef FZ_RG
   FZ_CHECK_LAUNCH();
   return FZ_OK;
@@ -292,6 +400,15 @@ int launch_cols(const float *in, float *out, int64_t outer, int64_t len, int64_t
   }
   int64_t chunk = (len + splits - 1) / splits;
   splits = (len + chunk - 1) / chunk;
+  if (splits > 1 && v4) {
+    // one pass through a cluster of up to 8 CTAs per 128 columns, when that fills
+    // the GPU (or the whole reduction is small enough that one launch is best)
+    const int64_t cblocks = outer * ((inner + 127) / 128);
+    const int cs = (int)(len >= 8 * 64 ? 8 : (len + 63) / 64 > 1 ? (len + 63) / 64 : 1);
+    if (cblocks < 65536 * 32768LL &&
+        (cblocks * cs >= 2 * (int64_t)fz::num_sms() || outer * len * inner <= ((int64_t)1 << 22)))
+      return launch_cols_cluster<OP>(in, out, outer, len, inner, cs, s);
+  }
   int64_t items = splits * base;
   unsigned grid = fz::grid_for(items, 256, 8, 4);
   float *dst = out;

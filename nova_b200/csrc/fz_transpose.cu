@@ -5,7 +5,8 @@
 // with A = shape[a1], B = shape[a2]. When R == 1 (the last axis takes part, as in
 // the W.T / x.T of a Linear layer) each of the P*Q [A, B] planes is transposed
 // through a 32x33 shared-memory tile, so both the reads and the writes are
-// coalesced 128-byte rows. When R > 1 whole R-runs move together and a
+// coalesced 128-byte rows; a 3D grid addresses the tiles, so the kernel divides
+// no index. When R > 1 whole R-runs move together and a
 // vectorised gather copy is used.
 #include "fz_common.cuh"
 
@@ -14,34 +15,36 @@ namespace {
 constexpr int kTile = 32;
 constexpr int kRows = 8;
 
+// One 32 x 32 tile of one [A, B] plane per CTA: blockIdx.x walks the tiles along B,
+// blockIdx.y those along A and blockIdx.z the P*Q planes, each dimension grid-
+// striding when it exceeds the launch limits, so no index is ever divided.
 __global__ void __launch_bounds__(kTile *kRows) transpose_tiles(const float *__restrict__ in,
                                                                float *__restrict__ out, int64_t P,
                                                                int64_t Q, int64_t A, int64_t B) {
   __shared__ float tile[kTile][kTile + 1];
   const int64_t ta = (A + kTile - 1) / kTile, tb = (B + kTile - 1) / kTile;
-  const int64_t total = P * Q * ta * tb;
   const int tx = threadIdx.x % kTile, ty = threadIdx.x / kTile;
-  for (int64_t t = blockIdx.x; t < total; t += gridDim.x) {
-    int64_t jb = t % tb;
-    int64_t rest = t / tb;
-    int64_t ib = rest % ta;
-    rest /= ta;
-    int64_t q = rest % Q, p = rest / Q;
+  for (int64_t pq = blockIdx.z; pq < P * Q; pq += gridDim.z) {
+    const int64_t p = pq / Q, q = pq - p * Q;  // once per plane
     const float *src = in + p * A * Q * B + q * B;  // element (i, j) at i*Q*B + j
     float *dst = out + p * B * Q * A + q * A;       // element (j, i) at j*Q*A + i
-    const int64_t i0 = ib * kTile, j0 = jb * kTile;
+    for (int64_t ib = blockIdx.y; ib < ta; ib += gridDim.y) {
+      for (int64_t jb = blockIdx.x; jb < tb; jb += gridDim.x) {
+        const int64_t i0 = ib * kTile, j0 = jb * kTile;
 #pragma unroll
-    for (int k = 0; k < kTile / kRows; ++k) {
-      int64_t i = i0 + ty + k * kRows, j = j0 + tx;
-      if (i < A && j < B) tile[ty + k * kRows][tx] = src[i * Q * B + j];
-    }
-    __syncthreads();
+        for (int k = 0; k < kTile / kRows; ++k) {
+          const int64_t i = i0 + ty + k * kRows, j = j0 + tx;
+          if (i < A && j < B) tile[ty + k * kRows][tx] = src[i * Q * B + j];
+        }
+        __syncthreads();
 #pragma unroll
-    for (int k = 0; k < kTile / kRows; ++k) {
-      int64_t j = j0 + ty + k * kRows, i = i0 + tx;
-      if (j < B && i < A) dst[j * Q * A + i] = tile[tx][ty + k * kRows];
+        for (int k = 0; k < kTile / kRows; ++k) {
+          const int64_t j = j0 + ty + k * kRows, i = i0 + tx;
+          if (j < B && i < A) dst[j * Q * A + i] = tile[tx][ty + k * kRows];
+        }
+        __syncthreads();
+      }
     }
-    __syncthreads();
   }
 }
 
@@ -102,8 +105,9 @@ extern "C" int fz_swapaxes(float *out, const float *in, const int64_t *shape, in
     if (Q == 1 || (A == 1 && B == 1)) return fz_memcpy_d2d(out, in, total * sizeof(float), s);
   }
   if (R == 1) {
-    int64_t tiles = P * Q * ((A + kTile - 1) / kTile) * ((B + kTile - 1) / kTile);
-    unsigned grid = fz::grid_for(tiles, 1, 8, 4);
+    const int64_t ta = (A + kTile - 1) / kTile, tb = (B + kTile - 1) / kTile;
+    dim3 grid((unsigned)(tb < 0x7fffffff ? tb : 0x7fffffff), (unsigned)(ta < 65535 ? ta : 65535),
+              (unsigned)(P * Q < 65535 ? P * Q : 65535));
     transpose_tiles<<<grid, kTile * kRows, 0, s>>>(in, out, P, Q, A, B);
   } else {
     bool v4 = R % 4 == 0 && (((uintptr_t)in | (uintptr_t)out) & 15) == 0;

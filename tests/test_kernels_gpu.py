@@ -120,7 +120,9 @@ def _reduce_gpu(capi, op, x, axis):
 @pytest.mark.parametrize("shape,axis", [((1024, 1024), 1), ((1024, 1024), 0), ((513, 1031), 1),
                                         ((513, 1031), 0), ((3, 5, 7), 1), ((7, 9, 64), 2),
                                         ((16, 256, 64, 64), 0), ((1 << 22,), None), ((5,), None),
-                                        ((2, 70000), 1), ((70000, 3), 0)])
+                                        ((2, 70000), 1), ((70000, 3), 0), ((4096, 8192), 0),
+                                        ((3, 2000, 512), 1), ((100, 260), 0), ((1 << 16, 64), 1),
+                                        ((999, 200), 1)])
 @pytest.mark.parametrize("op", ["sum", "mean", "max"])
 def test_reduce(capi, port, shape, axis, op):
     x = RNG.standard_normal(shape).astype(np.float32)
@@ -142,6 +144,22 @@ def test_reduce_max_nan_and_zero_sign(capi, port):
     x = np.array([[-0.0, 0.0, -1.0], [1.0, np.nan, 2.0], [-0.0, -0.0, -3.0]], np.float32)
     for axis in (0, 1):
         assert_bits_equal(_reduce_gpu(capi, "max", x, axis), port.reduce("max", x, axis))
+
+
+@pytest.mark.parametrize("shape", [(4096, 1024), (3000, 64)])
+def test_reduce_max_nan_and_zero_sign_split(capi, port, shape):
+    """The same rules when a column's rows are split over warps and cluster CTAs (or
+    chunks) and when rows are reduced several at a time: NaN anywhere wins, +0 ranks
+    above -0, wherever they sit."""
+    x = -np.abs(RNG.standard_normal(shape)).astype(np.float32)
+    x[:, 0] = -0.0
+    x[shape[0] // 2, 1] = 0.0  # one +0 among -0s in a column of negatives
+    x[:, 1] = np.where(np.arange(shape[0]) == shape[0] // 2, 0.0, -0.0)
+    x[shape[0] - 1, 2] = np.nan
+    x[7, shape[1] - 1] = np.nan
+    x[3, 5] = np.nan
+    for axis in (0, 1):
+        assert_bits_equal(_reduce_gpu(capi, "max", x, axis), port.reduce("max", x, axis), f"axis {axis}")
 
 
 @pytest.mark.parametrize("shape,a1,a2", [((33, 65), 0, 1), ((4096, 1024), 1, 0), ((3, 40, 50), 1, 2),
