@@ -164,7 +164,9 @@ def test_reduce_max_nan_and_zero_sign_split(capi, port, shape):
 
 @pytest.mark.parametrize("shape,a1,a2", [((33, 65), 0, 1), ((4096, 1024), 1, 0), ((3, 40, 50), 1, 2),
                                          ((3, 40, 50), 0, 2), ((2, 3, 4, 5), 0, 2),
-                                         ((6, 7, 8), 0, 1), ((1, 5), 0, 1), ((5, 1, 3), 0, 1)])
+                                         ((6, 7, 8), 0, 1), ((1, 5), 0, 1), ((5, 1, 3), 0, 1),
+                                         ((68, 100), 0, 1), ((8, 12, 20, 36), 1, 3),
+                                         ((5, 64, 132), 1, 2), ((4, 4), 0, 1), ((1000, 4), 0, 1)])
 def test_swapaxes(capi, port, shape, a1, a2):
     x = RNG.standard_normal(shape).astype(np.float32)
     want = port.swapaxes(x, a1, a2)
