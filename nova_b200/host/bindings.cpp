@@ -283,6 +283,11 @@ PYBIND11_MODULE(fusion, m) {
   m.def("set_fusion", &set_fusion_enabled, py::arg("enabled"),
         "Enable (default) or disable lazy elementwise fusion.");
   m.def("fusion_enabled", &fusion_enabled);
+  m.def("flat_prefix", [](const T &t, const T &like) {
+          return T(math::flat_prefix(t.raw(), like.raw().size(), like.raw().shape()), false);
+        }, py::arg("tensor"), py::arg("like"),
+        "The first like.size values of tensor (flat order) as a new tensor shaped like `like`: "
+        "what `like -= tensor` reads.");
   m.def("set_split_cache", &set_split_cache_enabled, py::arg("enabled"),
         "Keep GEMM operands' TF32 remainder planes with their buffers (default on).");
   m.def("split_cache_enabled", &split_cache_enabled);

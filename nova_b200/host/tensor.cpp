@@ -651,39 +651,59 @@ RawTensor swapaxes(const RawTensor &x, int a1, int a2) {
   return RawTensor(make_leaf(std::move(buf), oshape), x.dtype(), x.device());
 }
 
+// When y is pending and its first n values are the slice at index 0 of its leading
+// dims (the [U] bias minus row 0 of a [B, U] gradient), lower just that slice into
+// a buffer instead of all of y; null otherwise (read y itself).
+static std::shared_ptr<DeviceBuffer> prefix_values(const RawTensor &y, size_t n) {
+  if (!y.pending() || y.size() <= n) return nullptr;
+  const auto &ys = y.shape();
+  size_t tail = 1;
+  for (size_t k = ys.size(); k-- > 0;) {
+    tail *= ys[k];
+    if (tail == n) return materialize_prefix(y.expr(), k);
+    if (tail > n) break;
+  }
+  return nullptr;
+}
+
 // fusion::math::sub_inplace (ops/Ewise.hpp:69-83): x[i] -= y[i] for i < x.size,
 // reading y flat whatever its shape. Implemented by rebinding x's storage to the
 // new value, so pending readers of the old value are unaffected.
 void sub_inplace(RawTensor &x, const RawTensor &y) {
   FB_CHECK(x.is_initialised() && y.is_initialised(), "sub_inplace: uninitialised tensor");
   if (x.shape() == y.shape()) {
+    // lowered now, as one fused program with y's pending ops: an updated value (a
+    // parameter) is read again and again, and left pending it would be inlined into
+    // every reader, growing by one term with every update
     x.storage()->expr = make_op(Expr::Binary, FZ_SUB, x.expr(), y.expr(), x.shape());
+    materialize(x.storage()->expr);
     return;
   }
   const size_t n = x.size();
   FB_CHECK(y.size() >= n, "sub_inplace: right-hand side has fewer elements than the tensor");
   const float *px = x.data();
-  // Only y's first n values are read. When y is pending and those values are the
-  // slice at index 0 of its leading dims (the [U] bias minus row 0 of a [B, U]
-  // gradient), lower just that slice instead of all of y.
-  std::shared_ptr<DeviceBuffer> prefix;
-  if (y.pending() && y.size() > n) {
-    const auto &ys = y.shape();
-    size_t tail = 1;
-    for (size_t k = ys.size(); k-- > 0;) {
-      tail *= ys[k];
-      if (tail == n) {
-        prefix = materialize_prefix(y.expr(), k);
-        break;
-      }
-      if (tail > n) break;
-    }
-  }
+  // Only y's first n values are read.
+  std::shared_ptr<DeviceBuffer> prefix = prefix_values(y, n);
   const float *py = prefix ? prefix->ptr : y.data();
   auto buf = std::make_shared<DeviceBuffer>(n);
   fz_check(fz_ewise_binary_contig(FZ_SUB, (int64_t)n, buf->ptr, px, py, nullptr),
            "fz_ewise_binary_contig");
   x.storage()->expr = make_leaf(std::move(buf), x.shape());
+}
+
+// The first n values of x (flat order) as a tensor of `shape` (n elements).
+RawTensor flat_prefix(const RawTensor &x, size_t n, const std::vector<size_t> &shape) {
+  FB_CHECK(x.is_initialised(), "flat_prefix: uninitialised tensor");
+  FB_CHECK(x.size() >= n, "flat_prefix: the tensor has fewer than n elements");
+  size_t m = 1;
+  for (size_t d : shape) m *= d;
+  FB_CHECK(m == n, "flat_prefix: shape does not hold n elements");
+  std::shared_ptr<DeviceBuffer> buf = prefix_values(x, n);
+  if (!buf) {
+    buf = std::make_shared<DeviceBuffer>(n);
+    if (n) fz_check(fz_memcpy_d2d(buf->ptr, x.data(), n * sizeof(float), nullptr), "fz_memcpy_d2d");
+  }
+  return RawTensor(make_leaf(std::move(buf), shape), x.dtype(), x.device());
 }
 
 }  // namespace math

@@ -197,6 +197,7 @@ RawTensor reduce(int op, const RawTensor &x, size_t axis, bool keepdim);
 RawTensor matmul(const RawTensor &A, const RawTensor &B, bool transA = false, bool transB = false);
 RawTensor swapaxes(const RawTensor &x, int a1, int a2);
 void sub_inplace(RawTensor &x, const RawTensor &y);
+RawTensor flat_prefix(const RawTensor &x, size_t n, const std::vector<size_t> &shape);
 }  // namespace math
 
 RawTensor zeros_like(const RawTensor &t);

@@ -11,6 +11,11 @@ autodiff exactly as a Nova model does:
     examples/simple_network/mlp.py:65);
   * SGD (momentum 0): ``p -= grad * lr`` (nova/src/optim/sgd.py:29-44).
 With data parallelism the gradients are averaged over ranks before the update.
+Fusion's in-place subtract reads only the parameter's count of values from the
+gradient (fusion/src/Fusion/ops/Ewise.hpp:69-83), so a bias, whose gradient keeps
+the batch dimension ([B, U]), moves by row 0 of it; the ranks average just those
+values (``flat_prefix``), which is what the update reads, instead of shipping the
+whole [B, U] gradient.
 """
 from __future__ import annotations
 
@@ -62,14 +67,21 @@ class MLP:
             loss = loss / loss.size
             loss.backward()
         flat = [p for pair in self.params for p in pair]
+        grads = [p.get_grad() for p in flat]
         if comm is not None:
-            comm.allreduce_mean([p.get_grad() for p in flat])
-        for p in flat:
-            g = p.get_grad()
+            grads = [g if g is None or g.size == p.size else self._prefix(g, p)
+                     for p, g in zip(flat, grads)]
+            comm.allreduce_mean([g for g in grads if g is not None])
+        for p, g in zip(flat, grads):
             if g is None:
                 continue
             p -= g * lr
         return loss
+
+    def _prefix(self, g, p):
+        # the values `p -= g * lr` reads from a gradient larger than p
+        fp = getattr(self.F, "flat_prefix", None)
+        return fp(g, p) if fp is not None else g
 
     def numpy_params(self):
         return [(W.to_numpy(), b.to_numpy()) for W, b in self.params]

@@ -121,3 +121,20 @@ def test_split_planes_follow_values(fake_fusion):
         np.testing.assert_allclose((x @ W).to_numpy(), np.ones((8, 12)) @ (w - d), rtol=1e-5, atol=1e-5)
     finally:
         F.set_split_cache(True)
+
+
+def test_inplace_update_does_not_grow_readers(fake_fusion):
+    """`b -= g` leaves b materialised: a parameter updated every step and read by a
+    fused consumer must not be re-evaluated from its whole update history."""
+    F = fake_fusion
+    x = api_cases.T(F, np.ones((4, 3)))
+    b = api_cases.T(F, [0.5, -0.5, 1.0])
+    g = api_cases.T(F, [0.25, 0.25, 0.25])
+    want = np.array([0.5, -0.5, 1.0], np.float32)
+    for _ in range(6):
+        y = (x + b).maximum(0.0)
+        np.testing.assert_array_equal(y.to_numpy(), np.maximum(1.0 + want, 0.0)[None].repeat(4, 0))
+        b -= g * 2.0
+        want = want - np.float32(0.5)
+        assert not b.is_pending()
+    np.testing.assert_array_equal(b.to_numpy(), want)
