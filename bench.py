@@ -53,8 +53,8 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--kernel", default=None,
                     help="run one hot-path kernel on a profiling-sized case instead of the step "
-                         "(gemm, gemm_wgrad, add, bcast_add, exp, log, sqrt, sum_ax0, sum_ax1, max_ax0, "
-                         "sum_rows64, swapaxes, bias_relu)")
+                         "(step, gemm, gemm_wgrad, tf32_lo, add, bcast_add, exp, log, sqrt, sum_ax0, "
+                         "sum_ax1, max_ax0, sum_rows64, swapaxes, bias_relu)")
     ap.add_argument("--reps", type=int, default=3)
     return ap.parse_args()
 
@@ -499,6 +499,23 @@ def run_kernel(args):
         fn = lambda: A.check(L.fz_gemm_f32_split(1, m, n, kk, x.ptr, xl.ptr, ash[1], 0, tA, w.ptr,
                                                   wl.ptr, bsh[1], 0, tB, c.ptr, n, 0, None))
         work = 2.0 * m * n * kk
+    elif k == "step":  # the MLP training step alone (reps steps), for a launch list
+        from nova_b200.mlp import MLP, init_params
+
+        Ws, bs = init_params(DIMS, SEED)
+        model = MLP(F, Ws, bs)
+        rng = np.random.default_rng(SEED + 1)
+        X = model.tensor(rng.standard_normal((args.batch, DIMS[0]), dtype=np.float32), True)
+        Y = model.tensor(rng.standard_normal((args.batch, DIMS[-1]), dtype=np.float32), True)
+
+        def fn():
+            model.step(X, Y, LR)
+        work = float(args.batch)
+    elif k == "tf32_lo":  # remainder plane of a [65536,4096] activation (GEMM operand split)
+        n = 1 << 28
+        a, o = _random_device(A, (n,), 3), A.DeviceArray((n,))
+        fn = lambda: A.check(L.fz_tf32_lo(o.ptr, a.ptr, n, None))
+        work = 8.0 * n
     elif k == "bias_relu":  # fused relu(x + b) of the MLP forward through the fusion IR
         rows, cols = 16384, 4096
         dev = F.CppDevice(F.CppDeviceType.CPU, 0)
@@ -534,9 +551,10 @@ def run_kernel(args):
     ms = time_launch(A, fn, reps=args.reps, warm=1)
     F.synchronize()
     gemm = k.startswith("gemm")
-    unit = "TFLOP/s" if gemm else "GB/s"
-    print(json.dumps({"kernel": k, "ms": round(ms, 4),
-                      unit: round(work / ms / (1e9 if gemm else 1e6), 1)}), flush=True)
+    unit = "TFLOP/s" if gemm else "samples/s" if k == "step" else "GB/s"
+    scale = 1e9 if gemm else 1e-3 if k == "step" else 1e6
+    print(json.dumps({"kernel": k, "ms": round(ms, 4), unit: round(work / ms / scale, 1)}),
+          flush=True)
 
 
 def main():
