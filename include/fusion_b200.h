@@ -224,8 +224,6 @@ int fz_swapaxes(float *out, const float *in, const int64_t *shape, int ndim, int
 
 /* ---- GEMM ---------------------------------------------------------------- */
 
-enum fz_epilogue { FZ_EPI_NONE = 0, FZ_EPI_BIAS = 1, FZ_EPI_BIAS_RELU = 2 };
-
 /* Batched fp32 GEMM in 3xTF32 on the tcgen05 tensor cores (TMEM accumulators,
  * TMA-fed shared-memory tiles): C[b] = op(A[b]) @ op(B[b]) for b < batch, with
  * op(X) = X or X^T (trans flags), element leading dimensions and batch strides.
@@ -252,6 +250,14 @@ int fz_gemm_f32_split(int64_t batch, int64_t M, int64_t N, int64_t K,
 /* lo[i] = x[i] - tf32_hi(x[i]) for i < n, tf32_hi clearing the 13 low mantissa bits
  * (the plane fz_gemm_f32_split takes). */
 int fz_tf32_lo(float *lo, const float *x, int64_t n, void *stream);
+/* GEMM tile schedule for the calls that follow (process-wide): FZ_GEMM_TILES_AUTO picks
+ * CTA pairs (256 x 256 tiles, tcgen05 cta_group::2) for products with at least 256 rows
+ * and enough tiles to occupy every SM pair, single CTAs (128 x 256 tiles) otherwise;
+ * SINGLE and PAIR force one schedule (a pair schedule on fewer rows computes zero rows).
+ * Both meet the same error bounds; with the same K split (none, or the same count) an
+ * output element is accumulated from the same K chunks in the same order. */
+enum fz_gemm_tiles { FZ_GEMM_TILES_AUTO = 0, FZ_GEMM_TILES_SINGLE = 1, FZ_GEMM_TILES_PAIR = 2 };
+int fz_gemm_set_tiles(int mode);
 
 /* ---- collectives (data-parallel MLP step) -------------------------------- */
 

@@ -94,6 +94,7 @@ def lib() -> C.CDLL:
         L.fz_gemm_f32_split.argtypes = [i64, i64, i64, i64, vp, vp, i64, i64, C.c_int, vp, vp,
                                         i64, i64, C.c_int, vp, i64, i64, vp]
         L.fz_tf32_lo.argtypes = [vp, vp, i64, vp]
+        L.fz_gemm_set_tiles.argtypes = [C.c_int]
         L.fz_timer_create.argtypes = [C.POINTER(C.c_void_p)]
         L.fz_timer_start.argtypes = [vp, vp]
         L.fz_timer_stop.argtypes = [vp, vp]

@@ -35,6 +35,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <mutex>
 
 #include "fz_common.cuh"
@@ -527,6 +528,311 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   }
 }
 
+// ---------------------------------------------------------------- 2-SM (CTA pair) variant
+//
+// A cluster of two CTAs computes a 256 x 256 output tile with
+// tcgen05.mma.cta_group::2: each CTA holds 128 rows of A and 128 rows (N) of B per
+// stage, the leader CTA (rank 0) issues the MMAs, the tensor cores read the peer's
+// half of each operand from its shared memory, and each CTA's TMEM receives its 128
+// rows x 256 columns. Per MMA a CTA reads half of B from its own shared memory
+// instead of all of it, and loads a third fewer bytes per k-tile: less shared-memory
+// and L2 traffic, and energy, per product. Protocol: both CTAs' TMA loads complete
+// their bytes on the leader's full barrier (which the leader's producer armed for the
+// pair's bytes); the leader's commits multicast to both CTAs' empty and acc_full
+// barriers; the peer's epilogue threads arrive on the leader's acc_empty barriers.
+// TMEM is allocated and freed with cta_group::2 by warp 1 of both CTAs. Every wait is
+// bounded as in the single-CTA kernel, and both CTAs meet at a cluster barrier before
+// freeing TMEM and exiting.
+constexpr int PAIR_STAGES = 6;
+constexpr int PAIR_TILE_BYTES = BM * BK * 4;             // 128 rows of A or B: 8 KB
+constexpr int PAIR_STAGE_BYTES = 4 * PAIR_TILE_BYTES;    // A_hi, A_lo, B_hi, B_lo: 32 KB
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                   : "memory");
+}
+
+// Shared-memory address of the same variable in the cluster's CTA 0.
+__device__ __forceinline__ uint32_t in_leader(const void *p) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, 0;" : "=r"(r) : "r"(smem_u32(p)));
+  return r;
+}
+
+__device__ __forceinline__ void tma_load_3d_pair(void *dst, const CUtensorMap *map, uint32_t bar,
+                                                 int c0, int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_4d_pair(void *dst, const CUtensorMap *map, uint32_t bar,
+                                                 int c0, int c1, int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+
+// load_operand for a CTA of a pair: 128 rows, bytes completed on the leader's barrier.
+template <bool MN>
+__device__ __forceinline__ void load_operand_pair(uint8_t *dst, const CUtensorMap *map, uint32_t bar,
+                                                  int k0, int row0, int bz, bool wide) {
+  if constexpr (MN) {
+    if (wide) {
+      tma_load_4d_pair(dst, map, bar, 0, k0, row0 / MN_CHUNK, bz);
+    } else {
+#pragma unroll
+      for (int j = 0; j < BM / MN_CHUNK; ++j)
+        tma_load_3d_pair(dst + j * MN_CHUNK_BYTES, map, bar, row0 + j * MN_CHUNK, k0, bz);
+    }
+  } else {
+    tma_load_3d_pair(dst, map, bar, k0, row0, bz);
+  }
+}
+
+__device__ __forceinline__ void umma_tf32_pair(uint32_t tmem_d, uint64_t a, uint64_t b,
+                                               uint32_t idesc, uint32_t accum) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(a), "l"(b), "r"(idesc), "r"(accum)
+      : "memory");
+}
+
+// Arrive on the barrier at this offset in both CTAs of the pair when the MMAs issued
+// so far have completed.
+__device__ __forceinline__ void umma_commit_pair(uint64_t *bar) {
+  asm volatile(
+      "{\n\t.reg .b16 m;\n\tmov.b16 m, 3;\n\t"
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], m;\n\t}" ::"r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+               : "memory");
+}
+
+template <bool A_MN, bool B_MN>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap mapAh,
+                     const __grid_constant__ CUtensorMap mapAl,
+                     const __grid_constant__ CUtensorMap mapBh,
+                     const __grid_constant__ CUtensorMap mapBl, GemmArgs args) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  __shared__ __align__(8) uint64_t full_bar[PAIR_STAGES];
+  __shared__ __align__(8) uint64_t empty_bar[PAIR_STAGES];
+  __shared__ __align__(8) uint64_t acc_full[2];
+  __shared__ __align__(8) uint64_t acc_empty[2];
+  __shared__ uint32_t tmem_base_slot;
+  __shared__ volatile int abort_flag;
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  constexpr uint32_t kIdesc = make_idesc(2 * BM, BN, A_MN, B_MN);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < PAIR_STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 2 * 32 * NUM_EPI_WARPS);  // both CTAs' epilogue threads
+    }
+    abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    prefetch_map(&mapAh);
+    prefetch_map(&mapAl);
+    prefetch_map(&mapBh);
+    prefetch_map(&mapBl);
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(&tmem_base_slot)),
+                 "r"(2 * TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  cluster_sync_all();  // both CTAs' barriers initialised and TMEM allocated
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem_base = tmem_base_slot;
+
+  auto stage_ptr = [&](int s, int which) -> uint8_t * {
+    return smem + (size_t)s * PAIR_STAGE_BYTES + (size_t)which * PAIR_TILE_BYTES;
+  };
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------ TMA producer (both CTAs)
+      int it = 0;
+      bool ok = true;
+      for (int t = pair; ok && t < args.num_tiles; t += npairs) {
+        int mb, nb, bz, ks, kb;
+        decode_tile(t, args, mb, nb, bz, ks);
+        const int nk = unit_k_tiles(args, ks, kb);
+        const int row_a = mb * 2 * BM + (int)rank * BM, row_b = nb * BN + (int)rank * BM;
+        for (int kt = 0; kt < nk; ++kt, ++it) {
+          const int s = it % PAIR_STAGES;
+          const uint32_t round = it / PAIR_STAGES;
+          if (it >= PAIR_STAGES && !mbar_wait(&empty_bar[s], (round - 1) & 1, &abort_flag)) {
+            ok = false;
+            break;
+          }
+          if (leader) mbar_expect_tx(&full_bar[s], 2 * PAIR_STAGE_BYTES);
+          const uint32_t fb = in_leader(&full_bar[s]);
+          const int k0 = kb + kt * BK;
+          load_operand_pair<A_MN>(stage_ptr(s, 0), &mapAh, fb, k0, row_a, bz, args.wide & 1);
+          load_operand_pair<A_MN>(stage_ptr(s, 1), &mapAl, fb, k0, row_a, bz, args.wide & 2);
+          load_operand_pair<B_MN>(stage_ptr(s, 2), &mapBh, fb, k0, row_b, bz, args.wide & 4);
+          load_operand_pair<B_MN>(stage_ptr(s, 3), &mapBl, fb, k0, row_b, bz, args.wide & 8);
+        }
+      }
+      if (!ok) {
+        atomicCAS(args.err, kErrNone, kErrTimeoutEmpty);
+        abort_flag = 1;
+        if (leader) {  // drain (bounded): the last PAIR_STAGES k-tiles' loads of the pair
+          for (int i = (it > PAIR_STAGES ? it - PAIR_STAGES : 0); i < it; ++i) {
+            const int s = i % PAIR_STAGES;
+            const uint64_t t0 = globaltimer();
+            while (!mbar_try_wait(&full_bar[s], (i / PAIR_STAGES) & 1) && globaltimer() - t0 < kWaitNs) {
+            }
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      // ------------------------------------------------------ MMA issuer (leader only)
+      int it = 0, cc = 0;
+      bool ok = true;
+      for (int t = pair; ok && t < args.num_tiles; t += npairs) {
+        int mb, nb, bz, ks, kb;
+        decode_tile(t, args, mb, nb, bz, ks);
+        const int num_k = unit_k_tiles(args, ks, kb);
+        for (int kt0 = 0; ok && kt0 < num_k; kt0 += KCHUNK, ++cc) {
+          const int b = cc & 1;
+          if (cc >= 2 && !mbar_wait(&acc_empty[b], ((cc >> 1) - 1) & 1, &abort_flag)) {
+            ok = false;
+            break;
+          }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const uint32_t d_tmem = tmem_base + (uint32_t)(b * TMEM_COLS);
+          const int kend = kt0 + KCHUNK < num_k ? kt0 + KCHUNK : num_k;
+          for (int kt = kt0; kt < kend; ++kt, ++it) {
+            const int s = it % PAIR_STAGES;
+            if (!mbar_wait(&full_bar[s], (it / PAIR_STAGES) & 1, &abort_flag)) {
+              ok = false;
+              break;
+            }
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const uint32_t a_hi = smem_u32(stage_ptr(s, 0)), a_lo = smem_u32(stage_ptr(s, 1));
+            const uint32_t b_hi = smem_u32(stage_ptr(s, 2)), b_lo = smem_u32(stage_ptr(s, 3));
+#pragma unroll
+            for (int kk = 0; kk < BK / UMMA_K; ++kk) {
+              const uint64_t dah = operand_desc<A_MN>(a_hi, kk), dal = operand_desc<A_MN>(a_lo, kk);
+              const uint64_t dbh = operand_desc<B_MN>(b_hi, kk), dbl = operand_desc<B_MN>(b_lo, kk);
+              const uint32_t first = (kt == kt0 && kk == 0) ? 0u : 1u;
+              umma_tf32_pair(d_tmem, dal, dbh, kIdesc, first);  // lo * hi
+              umma_tf32_pair(d_tmem, dah, dbl, kIdesc, 1u);     // hi * lo
+              umma_tf32_pair(d_tmem, dah, dbh, kIdesc, 1u);     // hi * hi
+            }
+            umma_commit_pair(&empty_bar[s]);
+          }
+          if (ok) umma_commit_pair(&acc_full[b]);
+        }
+      }
+      if (!ok) {
+        atomicCAS(args.err, kErrNone, kErrTimeoutFull);
+        abort_flag = 1;
+      }
+    }
+  } else {
+    // ------------------------------------------------------ promotion + epilogue (warps 2..9)
+    const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const bool vec = ((args.ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(args.C) & 15) == 0) &&
+                     ((args.strideC & 3) == 0);
+    const uint32_t acc_empty_leader[2] = {in_leader(&acc_empty[0]), in_leader(&acc_empty[1])};
+    int cc = 0;
+    bool ok = true;
+    for (int t = pair; ok && t < args.num_tiles; t += npairs) {
+      int mb, nb, bz, ks, kb;
+      decode_tile(t, args, mb, nb, bz, ks);
+      const int num_k = unit_k_tiles(args, ks, kb);
+      float acc[128];
+#pragma unroll
+      for (int i = 0; i < 128; ++i) acc[i] = 0.0f;
+      for (int kt0 = 0; kt0 < num_k; kt0 += KCHUNK, ++cc) {
+        const int b = cc & 1;
+        if (!mbar_wait(&acc_full[b], (cc >> 1) & 1, &abort_flag)) {
+          if (lane == 0) atomicCAS(args.err, kErrNone, kErrTimeoutAcc);
+          abort_flag = 1;
+          ok = false;
+          break;
+        }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t taddr = tmem_base + (uint32_t)(b * TMEM_COLS + half * 128) +
+                               ((uint32_t)(q * 32) << 16);
+#pragma unroll
+        for (int c0 = 0; c0 < 128; c0 += 32) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(taddr + (uint32_t)c0, r);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) acc[c0 + i] = __fadd_rn(acc[c0 + i], __uint_as_float(r[i]));
+        }
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        if (leader) mbar_arrive(&acc_empty[b]);
+        else mbar_arrive_remote(acc_empty_leader[b]);
+      }
+      if (!ok) break;
+      const int row = mb * 2 * BM + (int)rank * BM + q * 32 + lane;
+      const int col0 = nb * BN + half * 128;
+      if (row < args.M && col0 < args.N) {
+        float *crow = args.C + (int64_t)ks * args.split_stride + (int64_t)bz * args.strideC +
+                      (int64_t)row * args.ldc + col0;
+        if (vec && col0 + 128 <= args.N) {
+#pragma unroll
+          for (int i = 0; i < 128; i += 4)
+            *reinterpret_cast<float4 *>(crow + i) = make_float4(acc[i], acc[i + 1], acc[i + 2], acc[i + 3]);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 128; ++i)
+            if (col0 + i < args.N) crow[i] = acc[i];
+        }
+      }
+    }
+  }
+
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  cluster_sync_all();  // neither CTA frees TMEM or exits while the pair may still use it
+  if (warp == 1) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                 "r"(2 * TMEM_COLS)
+                 : "memory");
+  }
+}
+
 // ---------------------------------------------------------------- host side
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 
@@ -592,14 +898,16 @@ int make_map(CUtensorMap *map, const float *base, bool mn, int64_t rows, int64_t
 
 int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
 
+std::atomic<int> g_tile_mode{FZ_GEMM_TILES_AUTO};
+
 // Number of K splits for a GEMM of `tiles` output tiles. A split turns one tile
 // into several units over K ranges (multiples of the 256-wide promotion chunk, at
 // least 1024 long) whose fp32 partials are summed afterwards; it pays when the
 // tiles fill the 148 SMs poorly (weight gradients: few tiles, K = batch rows).
 // Cost model in units of one tile's time per k: waves * K_per_unit, plus the
 // partials' write and read at HBM speed.
-int choose_splits(int64_t tiles, int64_t M, int64_t N, int64_t K, int64_t batch) {
-  const int64_t sms = fz::num_sms();
+int choose_splits(int64_t tiles, int64_t M, int64_t N, int64_t K, int64_t batch, int64_t workers) {
+  const int64_t sms = workers;
   const double k_time = 2.65e-8;  // s per k of one 128x256 tile (3 TF32 MMAs at ~1.1 PFLOP/s per GPU)
   int best = 1;
   double best_t = 1e300;
@@ -686,17 +994,26 @@ int prepare(const float *src, int64_t ld, int64_t sb, const float *lo_given, int
 
 template <bool A_MN, bool B_MN>
 int launch_gemm(const CUtensorMap &mAh, const CUtensorMap &mAl, const CUtensorMap &mBh,
-                const CUtensorMap &mBl, const GemmArgs &ga, unsigned grid, size_t smem,
+                const CUtensorMap &mBl, const GemmArgs &ga, unsigned grid, bool pair,
                 cudaStream_t s) {
-  static bool attr_done[64] = {};
+  static bool attr_done[2][64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 64 && !attr_done[dev]) {
-    cudaFuncSetAttribute(gemm_3xtf32_kernel<A_MN, B_MN>,
-                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    attr_done[dev] = true;
+  const size_t smem = pair ? (size_t)PAIR_STAGES * PAIR_STAGE_BYTES + 1024
+                           : (size_t)STAGES * STAGE_BYTES + 1024;
+  if (dev < 64 && !attr_done[pair][dev]) {
+    if (pair)
+      cudaFuncSetAttribute(gemm_pair_kernel<A_MN, B_MN>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    else
+      cudaFuncSetAttribute(gemm_3xtf32_kernel<A_MN, B_MN>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    attr_done[pair][dev] = true;
   }
-  gemm_3xtf32_kernel<A_MN, B_MN><<<grid, NUM_THREADS, smem, s>>>(mAh, mAl, mBh, mBl, ga);
+  if (pair)
+    gemm_pair_kernel<A_MN, B_MN><<<2 * grid, NUM_THREADS, smem, s>>>(mAh, mAl, mBh, mBl, ga);
+  else
+    gemm_3xtf32_kernel<A_MN, B_MN><<<grid, NUM_THREADS, smem, s>>>(mAh, mAl, mBh, mBl, ga);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fz::cuda_fail(e, "gemm_3xtf32_kernel launch", __FILE__, __LINE__);
   fz::note_launch();
@@ -741,17 +1058,25 @@ int gemm_impl(int64_t batch, int64_t M, int64_t N, int64_t K, const float *A, co
   rc = prepare(A, lda, strideA, A_lo, batch, ws, &oa, s);
   if (!rc) rc = prepare(B, ldb, strideB, B_lo, batch, ws + a_need, &ob, s);
 
+  // CTA pairs (256 x 256 tiles, cta_group::2) when there are rows for both halves
+  // and enough tiles to keep the pairs busy; single CTAs (128 x 256) otherwise
+  const int64_t pair_tiles = ((M + 2 * BM - 1) / (2 * BM)) * ((N + BN - 1) / BN) * batch;
+  const int mode = g_tile_mode.load(std::memory_order_relaxed);
+  const bool pair = mode == FZ_GEMM_TILES_PAIR ||
+                    (mode == FZ_GEMM_TILES_AUTO && M >= 2 * BM && pair_tiles * 2 >= fz::num_sms());
+  const int tile_m = pair ? 2 * BM : BM, box_b = pair ? BM : BN;
+  const int64_t workers = pair ? fz::num_sms() / 2 : fz::num_sms();
   CUtensorMap mAh, mAl, mBh, mBl;
   bool wide[4] = {false, false, false, false};
   if (!rc) rc = make_map(&mAh, oa.hi, oa.mn, M, K, oa.hi_ld, oa.hi_sb, batch, BM, oa.hi_padded, &wide[0]);
   if (!rc) rc = make_map(&mAl, oa.lo, oa.mn, M, K, oa.lo_ld, oa.lo_sb, batch, BM, oa.lo_padded, &wide[1]);
-  if (!rc) rc = make_map(&mBh, ob.hi, ob.mn, N, K, ob.hi_ld, ob.hi_sb, batch, BN, ob.hi_padded, &wide[2]);
-  if (!rc) rc = make_map(&mBl, ob.lo, ob.mn, N, K, ob.lo_ld, ob.lo_sb, batch, BN, ob.lo_padded, &wide[3]);
+  if (!rc) rc = make_map(&mBh, ob.hi, ob.mn, N, K, ob.hi_ld, ob.hi_sb, batch, box_b, ob.hi_padded, &wide[2]);
+  if (!rc) rc = make_map(&mBl, ob.lo, ob.mn, N, K, ob.lo_ld, ob.lo_sb, batch, box_b, ob.lo_padded, &wide[3]);
   const int wide_mask = (int)wide[0] | (int)wide[1] << 1 | (int)wide[2] << 2 | (int)wide[3] << 3;
-  const int tiles_m = (int)((M + BM - 1) / BM), tiles_n = (int)((N + BN - 1) / BN);
+  const int tiles_m = (int)((M + tile_m - 1) / tile_m), tiles_n = (int)((N + BN - 1) / BN);
   const int64_t tiles = (int64_t)tiles_m * tiles_n * batch;
   const bool dense_c = ldc == N && (batch == 1 || strideC == M * N);
-  const int splits = dense_c ? choose_splits(tiles, M, N, K, batch) : 1;
+  const int splits = dense_c ? choose_splits(tiles, M, N, K, batch, workers) : 1;
   const int64_t kps = splits > 1 ? round_up((K + splits - 1) / splits, (int64_t)BK * KCHUNK) : K;
   const int real_splits = (int)((K + kps - 1) / kps);
   const int64_t num_units = tiles * real_splits;
@@ -763,16 +1088,16 @@ int gemm_impl(int64_t batch, int64_t M, int64_t N, int64_t K, const float *A, co
   int *err = nullptr;
   if (!rc) rc = fz::device_error_word(&err);
   if (!rc) {
-    const size_t smem = (size_t)STAGES * STAGE_BYTES + 1024;
     GemmArgs ga{partial ? partial : C, partial ? N : ldc, partial ? M * N : strideC,
                 batch * M * N, (int)M, (int)N, (int)K, (int)batch,
                 tiles_m, tiles_n, (int)num_units, tiles_m < 16 ? tiles_m : 16,
                 real_splits, (int)kps, wide_mask, err};
-    const unsigned grid = (unsigned)(num_units < fz::num_sms() ? num_units : fz::num_sms());
-    if (!oa.mn && !ob.mn) rc = launch_gemm<false, false>(mAh, mAl, mBh, mBl, ga, grid, smem, s);
-    else if (!oa.mn && ob.mn) rc = launch_gemm<false, true>(mAh, mAl, mBh, mBl, ga, grid, smem, s);
-    else if (oa.mn && !ob.mn) rc = launch_gemm<true, false>(mAh, mAl, mBh, mBl, ga, grid, smem, s);
-    else rc = launch_gemm<true, true>(mAh, mAl, mBh, mBl, ga, grid, smem, s);
+    // persistent grid: one CTA (or CTA pair) per SM (pair of SMs)
+    const unsigned grid = (unsigned)(num_units < workers ? num_units : workers);
+    if (!oa.mn && !ob.mn) rc = launch_gemm<false, false>(mAh, mAl, mBh, mBl, ga, grid, pair, s);
+    else if (!oa.mn && ob.mn) rc = launch_gemm<false, true>(mAh, mAl, mBh, mBl, ga, grid, pair, s);
+    else if (oa.mn && !ob.mn) rc = launch_gemm<true, false>(mAh, mAl, mBh, mBl, ga, grid, pair, s);
+    else rc = launch_gemm<true, true>(mAh, mAl, mBh, mBl, ga, grid, pair, s);
     // K-split partials: summed over the splits in a fixed order (deterministic)
     if (!rc && partial) rc = fz_reduce(FZ_RSUM, C, partial, 1, real_splits, batch * M * N, s);
   }
@@ -807,5 +1132,12 @@ extern "C" int fz_tf32_lo(float *lo, const float *x, int64_t n, void *stream) {
   unsigned grid = fz::grid_for(n / 4 + 1, 256, 8, 4);
   lo_kernel<<<grid, 256, 0, s>>>(x, n, n, 1, n, n, 1, lo, nullptr);
   FZ_CHECK_LAUNCH();
+  return FZ_OK;
+}
+
+extern "C" int fz_gemm_set_tiles(int mode) {
+  FZ_REQUIRE(mode == FZ_GEMM_TILES_AUTO || mode == FZ_GEMM_TILES_SINGLE || mode == FZ_GEMM_TILES_PAIR,
+             "fz_gemm_set_tiles: unknown mode " + std::to_string(mode));
+  g_tile_mode.store(mode, std::memory_order_relaxed);
   return FZ_OK;
 }

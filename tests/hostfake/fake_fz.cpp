@@ -220,6 +220,8 @@ static float tf32_lo1(float x) {
   return x - h;
 }
 
+int fz_gemm_set_tiles(int mode) { return mode >= 0 && mode <= 2 ? FZ_OK : fail(FZ_ERR_INVALID, "fz_gemm_set_tiles: unknown mode"); }
+
 int fz_tf32_lo(float *lo, const float *x, int64_t n, void *) {
   for (int64_t i = 0; i < n; ++i) lo[i] = tf32_lo1(x[i]);
   ++g_launches;

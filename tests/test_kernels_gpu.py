@@ -210,6 +210,46 @@ def test_gemm_3xtf32(capi, port, batch, M, N, K, tA, tB):
     assert np.all(np.abs(got - want) <= 1e-5 * bound + 1e-30)
 
 
+@pytest.mark.parametrize("tA,tB", [(False, False), (False, True), (True, False), (True, True)])
+@pytest.mark.parametrize("batch,M,N,K", [(1, 2560, 2048, 256), (1, 2600, 2100, 200),
+                                         (2, 1536, 1792, 64), (1, 2560, 2048, 8192)])
+def test_gemm_3xtf32_cta_pairs(capi, batch, M, N, K, tA, tB):
+    """Shapes with enough 256 x 256 tiles for the CTA-pair kernel (cta_group::2): ragged
+    M and N, K not a multiple of the k-tile, batches, and a K long enough to be split."""
+    rng = np.random.default_rng(M + N + K + batch)
+    s = 1.0 / np.sqrt(K)
+    A = (rng.standard_normal((batch, M, K)) * s).astype(np.float32)
+    B = (rng.standard_normal((batch, K, N)) * s).astype(np.float32)
+    a_in = np.ascontiguousarray(A.transpose(0, 2, 1)) if tA else A
+    b_in = np.ascontiguousarray(B.transpose(0, 2, 1)) if tB else B
+    got = _gemm(capi, a_in, b_in, tA, tB)
+    want = np.matmul(A.astype(np.float64), B.astype(np.float64))
+    err = np.linalg.norm((got - want).ravel()) / np.linalg.norm(want.ravel())
+    assert err <= 1e-5, err
+    bound = np.matmul(np.abs(A).astype(np.float64), np.abs(B).astype(np.float64))
+    assert np.all(np.abs(got - want) <= 1e-5 * bound + 1e-30)
+
+
+@pytest.mark.parametrize("tA,tB", [(False, True), (True, False)])
+def test_gemm_tile_schedules_agree(capi, tA, tB):
+    """The single-CTA and CTA-pair schedules, forced through fz_gemm_set_tiles, give the
+    same product (bit for bit here: no K split, same chunk order)."""
+    L = capi.lib()
+    rng = np.random.default_rng(77)
+    M, N, K = 1024, 768, 600
+    A = rng.standard_normal((1, K, M) if tA else (1, M, K)).astype(np.float32)
+    B = rng.standard_normal((1, N, K) if tB else (1, K, N)).astype(np.float32)
+    outs = []
+    try:
+        for mode in (1, 2):  # FZ_GEMM_TILES_SINGLE, FZ_GEMM_TILES_PAIR
+            capi.check(L.fz_gemm_set_tiles(mode))
+            outs.append(_gemm(capi, A, B, tA, tB))
+    finally:
+        capi.check(L.fz_gemm_set_tiles(0))
+    assert_bits_equal(outs[1], outs[0], "pair vs single")
+    assert L.fz_gemm_set_tiles(7) == 1
+
+
 @pytest.mark.parametrize("M,N,K", [(256, 256, 65536), (4096, 16, 8192)])
 def test_gemm_3xtf32_long_k(capi, port, M, N, K):
     """The weight-gradient shapes of the MLP step (K = batch rows) hold 1e-5 too."""
