@@ -47,7 +47,9 @@ enum fz_binop {
 };
 
 /* Unary ops: SimdTags.hpp:55-71 (exp/log/sqrt) plus identity (copy). */
-enum fz_unop { FZ_EXP = 0, FZ_LOG = 1, FZ_SQRT = 2, FZ_COPY = 3 };
+/* FZ_TF32_LO: x minus x with its 13 low mantissa bits cleared (the remainder plane a
+ * 3xTF32 GEMM reads; fz_tf32_lo); not an op of Fusion's API. */
+enum fz_unop { FZ_EXP = 0, FZ_LOG = 1, FZ_SQRT = 2, FZ_COPY = 3, FZ_TF32_LO = 4 };
 
 /* Reductions: SumSIMD via reduction_tag (fusion/src/Fusion/core/TensorIter.hpp:251-297);
  * mean = sum / (float)len (fusion/src/Fusion/ops/Reduce.hpp:27-36); max has no

@@ -22,7 +22,7 @@ FZ_MAX_NODES = 48
 FZ_MAX_OUTPUTS = 4
 
 BINOPS = {"add": 0, "sub": 1, "mul": 2, "div": 3, "pow": 4, "maximum": 5, "gt": 6, "ge": 7}
-UNOPS = {"exp": 0, "log": 1, "sqrt": 2, "copy": 3}
+UNOPS = {"exp": 0, "log": 1, "sqrt": 2, "copy": 3, "tf32_lo": 4}
 REDOPS = {"sum": 0, "mean": 1, "max": 2}
 NODE_BINARY, NODE_UNARY, NODE_CONST = 0, 1, 2
 

@@ -101,6 +101,7 @@ __device__ __forceinline__ float unop_t(float a) {
   if constexpr (OP == FZ_EXP) return expf(a);
   else if constexpr (OP == FZ_LOG) return logf(a);
   else if constexpr (OP == FZ_SQRT) return __fsqrt_rn(a);
+  else if constexpr (OP == FZ_TF32_LO) return __fsub_rn(a, __uint_as_float(__float_as_uint(a) & 0xffffe000u));
   else return a;
 }
 

@@ -229,6 +229,7 @@ int dispatch_unary(int op, const EwPlan &p, float *out, const float *a, cudaStre
     case FZ_LOG: return launch_op<1, FZ_LOG>(p, out, a, nullptr, s);
     case FZ_SQRT: return launch_op<1, FZ_SQRT>(p, out, a, nullptr, s);
     case FZ_COPY: return launch_op<1, FZ_COPY>(p, out, a, nullptr, s);
+    case FZ_TF32_LO: return launch_op<1, FZ_TF32_LO>(p, out, a, nullptr, s);
   }
   return fz::fail(FZ_ERR_INVALID, "fz_ewise_unary: unknown op " + std::to_string(op));
 }

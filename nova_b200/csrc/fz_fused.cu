@@ -81,6 +81,7 @@ std::string unop_expr(int op, const std::string &a) {
     case FZ_LOG: return "logf(" + a + ")";
     case FZ_SQRT: return "__fsqrt_rn(" + a + ")";
     case FZ_COPY: return a;
+    case FZ_TF32_LO: return "__fsub_rn(" + a + ", __uint_as_float(__float_as_uint(" + a + ") & 0xffffe000u))";
   }
   return "";
 }
@@ -99,7 +100,7 @@ int validate(const fz_program &pg) {
       return fz::fail(FZ_ERR_INVALID, "fused program: bad node kind");
     if (n.kind == FZ_NODE_BINARY && (n.op < FZ_ADD || n.op > FZ_GE))
       return fz::fail(FZ_ERR_INVALID, "fused program: bad binary op");
-    if (n.kind == FZ_NODE_UNARY && (n.op < FZ_EXP || n.op > FZ_COPY))
+    if (n.kind == FZ_NODE_UNARY && (n.op < FZ_EXP || n.op > FZ_TF32_LO))
       return fz::fail(FZ_ERR_INVALID, "fused program: bad unary op");
     const int32_t srcs[2] = {n.src0, n.src1};
     for (int k = 0; k < nsrc; ++k) {

@@ -228,13 +228,16 @@ int collapse(std::vector<int64_t> &size, std::vector<std::vector<int64_t>> &st) 
 }
 }  // namespace
 
+// Launch a lowered program whose outputs (all of out_shape) go to `outs`.
 static void launch_program(const Lowering &L, const std::vector<size_t> &out_shape,
-                           float *out_ptr) {
-  const int nops = 1 + (int)L.leaves.size();
+                           const std::vector<float *> &outs) {
+  const int nout = (int)outs.size();
+  const int nops = nout + (int)L.leaves.size();
   std::vector<int64_t> size(out_shape.begin(), out_shape.end());
   std::vector<std::vector<int64_t>> st(nops, std::vector<int64_t>(out_shape.size()));
-  operand_strides(out_shape, out_shape, st[0].data());
-  for (size_t k = 0; k < L.leaves.size(); ++k) operand_strides(L.leaves[k]->shape, out_shape, st[k + 1].data());
+  for (int k = 0; k < nout; ++k) operand_strides(out_shape, out_shape, st[k].data());
+  for (size_t k = 0; k < L.leaves.size(); ++k)
+    operand_strides(L.leaves[k]->shape, out_shape, st[nout + k].data());
   if ((int)size.size() > FZ_MAX_DIMS) collapse(size, st);
   FB_CHECK((int)size.size() <= FZ_MAX_DIMS, "fused elementwise: too many non-mergeable dims");
   fz_ewise_plan plan{};
@@ -246,8 +249,7 @@ static void launch_program(const Lowering &L, const std::vector<size_t> &out_sha
   }
   std::vector<const float *> leaf_ptrs;
   for (auto *l : L.leaves) leaf_ptrs.push_back(l->buf->ptr);
-  float *outs[1] = {out_ptr};
-  fz_check(fz_fused_launch(&L.prog, &plan, outs, leaf_ptrs.data(), nullptr), "fz_fused_launch");
+  fz_check(fz_fused_launch(&L.prog, &plan, outs.data(), leaf_ptrs.data(), nullptr), "fz_fused_launch");
   ++g_fused_launches;
 }
 
@@ -307,7 +309,7 @@ static std::shared_ptr<DeviceBuffer> materialize_prefix(const ExprPtr &ep, size_
   L.prog.num_leaves = (int32_t)L.leaves.size();
   L.prog.num_outputs = 1;
   L.prog.out_node[0] = root;
-  launch_program(L, sub, out->ptr);
+  launch_program(L, sub, {out->ptr});
   return out;
 }
 
@@ -328,8 +330,46 @@ void materialize(const ExprPtr &ep) {
     L.prog.num_leaves = (int32_t)L.leaves.size();
     L.prog.num_outputs = 1;
     L.prog.out_node[0] = root;
-    launch_program(L, e->shape, out->ptr);
+    launch_program(L, e->shape, {out->ptr});
   }
+  e->kind = Expr::Leaf;
+  e->buf = std::move(out);
+  e->a.reset();
+  e->b.reset();
+  e->nodes_ub = 0;
+  e->leaves_ub = 1;
+}
+
+// Lower a pending node together with its TF32 remainder plane (the lo plane a 3xTF32
+// GEMM reads), as two outputs of one fused program: the plane costs one extra write
+// instead of a second pass over the value. The plane is kept with the new buffer.
+void materialize_with_lo(const ExprPtr &ep) {
+  Expr *e = ep.get();
+  if (e->kind == Expr::Leaf || e->kind == Expr::Const || e->numel() == 0) {
+    materialize(ep);
+    return;
+  }
+  Lowering L;
+  const int root = L.visit(e);
+  if (L.overflow || root < 0 || L.prog.num_nodes >= FZ_MAX_NODES) {
+    materialize(ep);
+    return;
+  }
+  fz_node &n = L.prog.nodes[L.prog.num_nodes];
+  n.kind = FZ_NODE_UNARY;
+  n.op = FZ_TF32_LO;
+  n.src0 = root;
+  n.src1 = 0;
+  n.imm = 0.0f;
+  const int lo_node = L.prog.num_nodes++;
+  L.prog.num_leaves = (int32_t)L.leaves.size();
+  L.prog.num_outputs = 2;
+  L.prog.out_node[0] = root;
+  L.prog.out_node[1] = lo_node;
+  auto out = std::make_shared<DeviceBuffer>(e->numel());
+  auto lo = std::make_shared<DeviceBuffer>(e->numel());
+  launch_program(L, e->shape, {out->ptr, lo->ptr});
+  out->tf32_lo = std::move(lo);
   e->kind = Expr::Leaf;
   e->buf = std::move(out);
   e->a.reset();
@@ -575,9 +615,12 @@ RawTensor reduce(int op, const RawTensor &x, size_t axis, bool keepdim) {
 // kept with its buffer; null (the GEMM splits it itself) when caching is off or the
 // GEMM could not read it directly (pitch or batch stride not a multiple of 4 floats,
 // broadcast batch).
+static bool split_plane_usable(int64_t ld, int64_t stride, size_t batch) {
+  return split_cache_enabled() && ld % 4 == 0 && stride % 4 == 0 && !(batch > 1 && stride == 0);
+}
+
 static const float *tf32_lo_plane(const RawTensor &t, int64_t ld, int64_t stride, size_t batch) {
-  if (!split_cache_enabled() || ld % 4 != 0 || stride % 4 != 0 || (batch > 1 && stride == 0))
-    return nullptr;
+  if (!split_plane_usable(ld, stride, batch)) return nullptr;
   ExprPtr e = t.expr();
   if (!e || e->kind != Expr::Leaf || !e->buf) return nullptr;
   DeviceBuffer &b = *e->buf;
@@ -615,12 +658,15 @@ RawTensor matmul(const RawTensor &A, const RawTensor &B, bool transA, bool trans
            "matmul: batch dims broadcast only as a whole");
   oshape.push_back(M);
   oshape.push_back(N);
-  const float *pa = A.data(), *pb = B.data();
-  size_t n = batch * M * N;
-  auto buf = std::make_shared<DeviceBuffer>(n);
   const int64_t lda = (int64_t)as[ar - 1], ldb = (int64_t)bs[br - 1];
   const int64_t sA = ba == 1 ? 0 : (int64_t)(as[ar - 1] * as[ar - 2]);
   const int64_t sB = bb == 1 ? 0 : (int64_t)(bs[br - 1] * bs[br - 2]);
+  // pending operands are lowered with their remainder planes in the same pass
+  if (A.pending() && split_plane_usable(lda, sA, batch)) materialize_with_lo(A.expr());
+  if (B.pending() && split_plane_usable(ldb, sB, batch)) materialize_with_lo(B.expr());
+  const float *pa = A.data(), *pb = B.data();
+  size_t n = batch * M * N;
+  auto buf = std::make_shared<DeviceBuffer>(n);
   const float *la = tf32_lo_plane(A, lda, sA, batch), *lb = tf32_lo_plane(B, ldb, sB, batch);
   fz_check(fz_gemm_f32_split((int64_t)batch, (int64_t)M, (int64_t)N, (int64_t)Ka, pa, la, lda, sA,
                              transA, pb, lb, ldb, sB, transB, buf->ptr, (int64_t)N,

@@ -105,6 +105,8 @@ void set_split_cache_enabled(bool on);
 bool split_cache_enabled();
 // Lower a pending node to one fused kernel (no-op for a Leaf).
 void materialize(const ExprPtr &e);
+// Lower a pending node and its TF32 remainder plane in one fused pass (GEMM operands).
+void materialize_with_lo(const ExprPtr &e);
 int64_t fused_launches();
 
 class RawTensor {

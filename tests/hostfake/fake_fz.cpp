@@ -41,11 +41,21 @@ float binop(int op, float a, float b) {
   return 0.0f;
 }
 
+static float tf32_lo1(float x) {
+  uint32_t u;
+  std::memcpy(&u, &x, 4);
+  u &= 0xffffe000u;
+  float h;
+  std::memcpy(&h, &u, 4);
+  return x - h;
+}
+
 float unop(int op, float a) {
   switch (op) {
     case FZ_EXP: return std::exp(a);
     case FZ_LOG: return std::log(a);
     case FZ_SQRT: return std::sqrt(a);
+    case FZ_TF32_LO: return tf32_lo1(a);
     default: return a;
   }
 }
@@ -211,14 +221,6 @@ int fz_gemm_f32(int64_t batch, int64_t M, int64_t N, int64_t K, const float *A, 
   return FZ_OK;
 }
 
-static float tf32_lo1(float x) {
-  uint32_t u;
-  std::memcpy(&u, &x, 4);
-  u &= 0xffffe000u;
-  float h;
-  std::memcpy(&h, &u, 4);
-  return x - h;
-}
 
 int fz_gemm_set_tiles(int mode) { return mode >= 0 && mode <= 2 ? FZ_OK : fail(FZ_ERR_INVALID, "fz_gemm_set_tiles: unknown mode"); }
 

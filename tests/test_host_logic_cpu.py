@@ -138,3 +138,21 @@ def test_inplace_update_does_not_grow_readers(fake_fusion):
         want = want - np.float32(0.5)
         assert not b.is_pending()
     np.testing.assert_array_equal(b.to_numpy(), want)
+
+
+def test_pending_gemm_operand_lowered_with_its_plane(fake_fusion):
+    """A pending operand of `@` is lowered together with its TF32 remainder plane (one
+    fused program with two outputs), so no separate split pass runs for it."""
+    F = fake_fusion
+    rng = np.random.default_rng(9)
+    x = api_cases.T(F, rng.standard_normal((16, 8)))
+    b = api_cases.T(F, rng.standard_normal(8))
+    W = api_cases.T(F, rng.standard_normal((8, 4)))
+    (x @ W).to_numpy()  # W gets its plane here
+    y = (x + b).maximum(0.0)
+    assert y.is_pending()
+    before = F.stats()["kernel_launches"]
+    z = y @ W
+    assert F.stats()["kernel_launches"] - before == 2  # the fused program and the GEMM
+    want = np.maximum(x.to_numpy() + b.to_numpy(), 0).astype(np.float64) @ W.to_numpy()
+    np.testing.assert_allclose(z.to_numpy(), want, rtol=1e-5, atol=1e-6)

@@ -325,6 +325,28 @@ def test_fused_bias_relu(capi, port):
     assert_bits_equal(do.numpy(), want, "fused relu(x+b)")
 
 
+def test_fused_value_and_tf32_remainder(capi):
+    """relu(x + b) and its TF32 remainder plane as two outputs of one program, the form
+    a pending GEMM operand is lowered in."""
+    A = capi
+    x = RNG.standard_normal((300, 2048)).astype(np.float32)
+    b = RNG.uniform(-0.1, 0.1, (2048,)).astype(np.float32)
+    prog = _program([(A.NODE_BINARY, A.BINOPS["add"], -1, -2, 0.0),
+                     (A.NODE_CONST, 0, 0, 0, 0.0),
+                     (A.NODE_BINARY, A.BINOPS["maximum"], 0, 1, 0.0),
+                     (A.NODE_UNARY, A.UNOPS["tf32_lo"], 2, 0, 0.0)], 2, [2, 3])
+    plan = A.make_plan(x.shape, [x.shape, x.shape, x.shape, b.shape])
+    dx, db = A.DeviceArray.from_numpy(x), A.DeviceArray.from_numpy(b)
+    dv, dl = A.DeviceArray(x.shape), A.DeviceArray(x.shape)
+    outs = (C.c_void_p * 2)(dv.ptr, dl.ptr)
+    leaves = (C.c_void_p * 2)(dx.ptr, db.ptr)
+    A.check(A.lib().fz_fused_launch(C.byref(prog), C.byref(plan), outs, leaves, None))
+    v = np.maximum((x + b).astype(np.float32), np.float32(0))
+    hi = (v.view(np.uint32) & np.uint32(0xFFFFE000)).view(np.float32)
+    assert_bits_equal(dv.numpy(), v, "value")
+    assert_bits_equal(dl.numpy(), v - hi, "remainder")
+
+
 def test_fused_divide_backward_two_outputs(capi, port):
     """gx = g/y and gy = ((0 - g) * x) / (y * y) in one pass (Divide backward)."""
     A = capi
