@@ -72,6 +72,14 @@ int fz_get_device(int *device);
 /* The calling thread's stream on the current device (created on first use). */
 void *fz_default_stream(void);
 int fz_stream_sync(void *stream);
+/* A second non-blocking stream on the current device (for collectives that overlap the
+ * thread's compute stream), and its release. */
+int fz_stream_create(void **stream);
+int fz_stream_destroy(void *stream);
+/* Work submitted to `waiter` after this call starts only once the work submitted to
+ * `signaler` before it has finished (an event recorded on `signaler`, waited on by
+ * `waiter`; NULL means the thread's stream). The host does not block. */
+int fz_stream_wait(void *waiter, void *signaler);
 int fz_device_sync(void);
 
 /* Stream-ordered device memory. fz_free puts the block on a free list of `stream`

@@ -197,6 +197,32 @@ int fz_stream_sync(void *stream) {
   return FZ_OK;
 }
 
+int fz_stream_create(void **stream) {
+  FZ_REQUIRE(stream, "fz_stream_create: null pointer");
+  cudaStream_t s = nullptr;
+  FZ_CUDA(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
+  *stream = (void *)s;
+  return FZ_OK;
+}
+
+int fz_stream_destroy(void *stream) {
+  if (!stream) return FZ_OK;
+  FZ_CUDA(cudaStreamDestroy((cudaStream_t)stream));
+  return FZ_OK;
+}
+
+int fz_stream_wait(void *waiter, void *signaler) {
+  cudaStream_t w = resolve(waiter), g = resolve(signaler);
+  if (w == g) return FZ_OK;
+  cudaEvent_t e = nullptr;
+  FZ_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+  cudaError_t rc = cudaEventRecord(e, g);
+  if (rc == cudaSuccess) rc = cudaStreamWaitEvent(w, e, 0);
+  cudaEventDestroy(e);  // released once the wait no longer needs it
+  if (rc != cudaSuccess) return cuda_fail(rc, "fz_stream_wait", __FILE__, __LINE__);
+  return FZ_OK;
+}
+
 int fz_device_sync(void) {
   FZ_CUDA(cudaDeviceSynchronize());
   return FZ_OK;

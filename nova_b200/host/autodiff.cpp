@@ -286,12 +286,23 @@ std::vector<NodeID> Engine::topo_order() const {
   return order;
 }
 
+static thread_local GradReadyHook t_grad_ready_hook;
+void set_grad_ready_hook(GradReadyHook hook) { t_grad_ready_hook = std::move(hook); }
+
 BackwardResult Engine::backward(ValueID seed) {
   grad_.resize(val_.size());
   for (auto &g : grad_)
     if (g.is_initialised()) g.clear();
   std::vector<NodeID> order = topo_order();
   grad_[seed] = ones_like(val_[seed]);
+  // readers left per value, to tell the hook when a leaf's gradient is complete
+  const GradReadyHook hook = t_grad_ready_hook;
+  std::vector<int> readers_left;
+  if (hook) {
+    readers_left.assign(val_.size(), 0);
+    for (const TapeNode &nd : nodes_)
+      for (ValueID v : nd.inputs) ++readers_left[v];
+  }
   for (auto it = order.rbegin(); it != order.rend(); ++it) {
     TapeNode &n = nodes_[*it];
     FB_CHECK(!n.outputs.empty(), "node has no outputs in backward()");
@@ -318,6 +329,11 @@ BackwardResult Engine::backward(ValueID seed) {
       if (!dst.is_initialised()) dst = gin[j];
       else dst = dst + gin[j];
     }
+    if (hook)
+      for (ValueID v : n.inputs)
+        if (--readers_left[v] == 0 && produced_by_[v] == -1 && requires_grad_set_.count(v) &&
+            grad_[v].is_initialised())
+          hook(v, grad_[v]);
   }
   BackwardResult r;
   for (int64_t v : requires_grad_set_) r.grads.try_emplace(v, grad_[v]);

@@ -22,6 +22,7 @@
 #pragma once
 
 #include <memory>
+#include <functional>
 #include <optional>
 #include <string>
 #include <unordered_map>
@@ -97,6 +98,13 @@ class Engine {
   ValueID new_intermediate_value();
   std::vector<NodeID> topo_order() const;
 };
+
+// Called during Engine::backward, on the engine's thread, as soon as the gradient of a
+// leaf value that requires grad is complete (every node reading it has contributed), so
+// a caller can start using it (an all-reduce on another stream) while the rest of the
+// backward is still being computed. Thread-local; an empty function removes it.
+using GradReadyHook = std::function<void(ValueID, const RawTensor &)>;
+void set_grad_ready_hook(GradReadyHook hook);
 
 // thread-local engine slot (EngineContext.hpp:10-25)
 Engine *engine_instance();

@@ -9,6 +9,7 @@
 #include <pybind11/stl.h>
 
 #include <numeric>
+#include <optional>
 #include <random>
 #include <sstream>
 
@@ -61,6 +62,15 @@ struct GradTape {
 struct Comm {
   void *c = nullptr;
   int world = 1, rank = 0;
+  void *side = nullptr;  // stream for all-reduces that overlap the backward
+  struct Watched {
+    ADTensor *param;
+    ValueID vid;
+    std::optional<RawTensor> avg;  // averaged gradient (what the update reads)
+    std::optional<RawTensor> sent;  // the reduced values, kept alive until collect()
+  };
+  std::vector<Watched> watched;
+  int overlapped = 0;  // gradients the last backward handed over while it ran
   Comm(int w, int r, py::bytes uid) : world(w), rank(r) {
     std::string id = uid;
     if (id.size() != FZ_UNIQUE_ID_BYTES) throw std::invalid_argument("Comm: unique id must be 128 bytes");
@@ -68,8 +78,60 @@ struct Comm {
   }
   ~Comm() { destroy(); }
   void destroy() {
+    if (!watched.empty()) set_grad_ready_hook({});
+    watched.clear();
     if (c) fz_comm_destroy(c);
     c = nullptr;
+    if (side) fz_stream_destroy(side);
+    side = nullptr;
+  }
+  // All-reduce (average) what `param -= grad * lr` reads from grad: all of it, or its
+  // first param.size values when the gradient is larger (a bias gradient that keeps the
+  // batch dimension), on the side stream after the work that produced it.
+  void reduce_into(Watched &w, const RawTensor &g) {
+    const size_t n = w.param->raw().size();
+    RawTensor src = g.size() > n ? math::flat_prefix(g, n, w.param->raw().shape()) : g;
+    const float *in = src.data();
+    auto out = std::make_shared<DeviceBuffer>(src.size());
+    fz_check(fz_stream_wait(side, nullptr), "fz_stream_wait");
+    fz_check(fz_comm_allreduce(c, in, out->ptr, (int64_t)src.size(), 1.0f / (float)world, side),
+             "fz_comm_allreduce");
+    w.avg = RawTensor::from_buffer(out, src.shape(), src.dtype(), src.device());
+    w.sent = std::move(src);
+  }
+  // Average the gradients of `params` over ranks while the backward runs: each one is
+  // all-reduced on a second stream as soon as the engine has completed it, so the
+  // transfers overlap the backward of the earlier layers. Call after the forward and
+  // before backward(); collect() returns the averaged gradients. Every rank issues the
+  // all-reduces in the engine's (deterministic) completion order.
+  void watch(const std::vector<ADTensor *> &params) {
+    if (!c) throw std::runtime_error("Comm: destroyed");
+    if (!side) fz_check(fz_stream_create(&side), "fz_stream_create");
+    watched.clear();
+    for (ADTensor *p : params) watched.push_back(Watched{p, p->has_vid() ? p->vid() : -1, {}, {}});
+    set_grad_ready_hook([this](ValueID v, const RawTensor &g) {
+      for (Watched &w : watched)
+        if (w.vid == v && w.vid >= 0 && !w.avg) reduce_into(w, g);
+    });
+  }
+  // The averaged gradients of the watched parameters (None where a parameter got no
+  // gradient). Gradients the backward did not announce are reduced here, in parameter
+  // order. The thread's stream then waits for the side stream.
+  std::vector<py::object> collect() {
+    set_grad_ready_hook({});
+    overlapped = 0;
+    for (Watched &w : watched) overlapped += w.avg ? 1 : 0;
+    for (Watched &w : watched)
+      if (!w.avg) {
+        std::optional<ADTensor> g = w.param->grad();
+        if (g) reduce_into(w, g->raw());
+      }
+    if (side) fz_check(fz_stream_wait(nullptr, side), "fz_stream_wait");
+    std::vector<py::object> out;
+    for (Watched &w : watched)
+      out.push_back(w.avg ? py::cast(ADTensor(*w.avg, false)) : py::none());
+    watched.clear();
+    return out;
   }
   // Average each tensor over ranks, out of place, then rebind the tensor's storage
   // to the result so pending readers of the old value keep it. All reductions are
@@ -321,6 +383,13 @@ PYBIND11_MODULE(fusion, m) {
       .def_readonly("rank", &Comm::rank)
       .def("allreduce_mean", &Comm::allreduce_mean, py::arg("tensors"),
            "Average tensors over all ranks (one NCCL group, out of place).")
+      .def("watch", &Comm::watch, py::arg("params"),
+           "Average these parameters' gradients over ranks as the backward completes them "
+           "(on a second stream, overlapping the rest of the backward).")
+      .def_readonly("overlapped", &Comm::overlapped,
+                    "How many of the last collect()'s gradients were reduced during the backward.")
+      .def("collect", &Comm::collect,
+           "The averaged gradients of the watched parameters, in order (None if none).")
       .def("broadcast", &Comm::broadcast, py::arg("tensors"), py::arg("root") = 0)
       .def("wait", &Comm::wait, py::arg("timeout_s"),
            "Wait for this rank's stream with a deadline; on expiry abort the communicator "

@@ -474,6 +474,14 @@ void RawTensor::set_values(const float *src, size_t n) {
   storage_->expr = make_leaf(std::move(buf), shape_);
 }
 
+RawTensor RawTensor::from_buffer(std::shared_ptr<DeviceBuffer> buf, std::vector<size_t> shape,
+                                 DType dtype, Device device) {
+  size_t n = 1;
+  for (size_t d : shape) n *= d;
+  FB_CHECK(buf && buf->numel == n, "from_buffer: size mismatch");
+  return RawTensor(make_leaf(std::move(buf), std::move(shape)), dtype, device);
+}
+
 void RawTensor::rebind_buffer(std::shared_ptr<DeviceBuffer> buf) {
   FB_CHECK(storage_, "uninitialised tensor");
   FB_CHECK(buf && buf->numel == size(), "rebind_buffer: size mismatch");

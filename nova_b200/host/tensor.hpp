@@ -121,6 +121,9 @@ class RawTensor {
   RawTensor(ExprPtr e, DType dtype, Device device);
 
   static RawTensor full(const std::vector<size_t> &shape, float value, DType dtype, Device device);
+  // A tensor over an existing device buffer (numel = product of shape).
+  static RawTensor from_buffer(std::shared_ptr<DeviceBuffer> buf, std::vector<size_t> shape,
+                               DType dtype, Device device);
   static RawTensor scalar(float v, DType dtype, Device device) { return full({1}, v, dtype, device); }
 
   DType dtype() const { return dtype_; }

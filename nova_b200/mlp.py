@@ -10,7 +10,10 @@ autodiff exactly as a Nova model does:
     (nova/src/losses/loss_fn.py:14-15, loss.py:34-37; argument order as in
     examples/simple_network/mlp.py:65);
   * SGD (momentum 0): ``p -= grad * lr`` (nova/src/optim/sgd.py:29-44).
-With data parallelism the gradients are averaged over ranks before the update.
+With data parallelism the gradients are averaged over ranks before the update; with
+the backend's ``Comm`` each one is all-reduced on a second stream as soon as the
+backward has completed it (``Comm.watch`` / ``Comm.collect``), overlapping the backward
+of the earlier layers.
 Fusion's in-place subtract reads only the parameter's count of values from the
 gradient (fusion/src/Fusion/ops/Ewise.hpp:69-83), so a bias, whose gradient keeps
 the batch dimension ([B, U]), moves by row 0 of it; the ranks average just those
@@ -61,17 +64,23 @@ class MLP:
     def step(self, x, y, lr: float, comm=None):
         """One training step; returns the loss tensor ([batch, out] elementwise MSE)."""
         F = self.F
+        flat = [p for pair in self.params for p in pair]
+        overlap = comm is not None and hasattr(comm, "watch")
         with F.grad_tape():
             pred = self.forward(x)
             loss = (pred - y) ** 2
             loss = loss / loss.size
+            if overlap:
+                comm.watch(flat)  # all-reduce each gradient as soon as the backward completes it
             loss.backward()
-        flat = [p for pair in self.params for p in pair]
-        grads = [p.get_grad() for p in flat]
-        if comm is not None:
-            grads = [g if g is None or g.size == p.size else self._prefix(g, p)
-                     for p, g in zip(flat, grads)]
-            comm.allreduce_mean([g for g in grads if g is not None])
+        if overlap:
+            grads = comm.collect()
+        else:
+            grads = [p.get_grad() for p in flat]
+            if comm is not None:
+                grads = [g if g is None or g.size == p.size else self._prefix(g, p)
+                         for p, g in zip(flat, grads)]
+                comm.allreduce_mean([g for g in grads if g is not None])
         for p, g in zip(flat, grads):
             if g is None:
                 continue

@@ -156,3 +156,25 @@ def test_pending_gemm_operand_lowered_with_its_plane(fake_fusion):
     assert F.stats()["kernel_launches"] - before == 2  # the fused program and the GEMM
     want = np.maximum(x.to_numpy() + b.to_numpy(), 0).astype(np.float64) @ W.to_numpy()
     np.testing.assert_allclose(z.to_numpy(), want, rtol=1e-5, atol=1e-6)
+
+
+def test_overlapped_gradient_average_matches_plain_step(fake_fusion):
+    """Comm.watch/collect (each gradient all-reduced as the backward completes it) gives
+    the same update as the plain step; with one rank the average is the gradient, and
+    a bias moves by row 0 of its [B, U] gradient either way."""
+    from nova_b200.mlp import MLP
+
+    F = fake_fusion
+    X, Y, Ws, bs = api_cases.mlp_inputs(5, [8, 16, 16, 4], 12)
+    bs = [np.linspace(-0.1, 0.1, b.size).astype(np.float32) for b in bs]
+    plain, over = MLP(F, Ws, bs), MLP(F, Ws, bs)
+    comm = F.Comm(1, 0, F.comm_unique_id())
+    for _ in range(2):
+        lp = plain.step(plain.tensor(X, True), plain.tensor(Y, True), 1e-2)
+        lo = over.step(over.tensor(X, True), over.tensor(Y, True), 1e-2, comm)
+        np.testing.assert_array_equal(lo.to_numpy(), lp.to_numpy())
+        assert comm.overlapped == 6  # every parameter's gradient went out during backward()
+    for (Wp, bp), (Wo, bo) in zip(plain.numpy_params(), over.numpy_params()):
+        np.testing.assert_array_equal(Wo, Wp)
+        np.testing.assert_array_equal(bo, bp)
+    comm.destroy()
