@@ -184,6 +184,18 @@ def time_launch(capi, fn, reps=10, warm=3):
     return t.stop_ms() / reps
 
 
+def fused_program(capi, nodes, nleaves, outs):
+    """An fz_program from (kind, op, src0, src1, imm) tuples (src < 0: leaf -1-src)."""
+    p = capi.Program()
+    p.num_nodes, p.num_leaves, p.num_outputs = len(nodes), nleaves, len(outs)
+    for i, node in enumerate(outs):
+        p.out_node[i] = node
+    for i, (kind, op, s0, s1, imm) in enumerate(nodes):
+        p.nodes[i].kind, p.nodes[i].op, p.nodes[i].src0, p.nodes[i].src1 = kind, op, s0, s1
+        p.nodes[i].imm = imm
+    return p
+
+
 def kernel_suite(capi, pk):
     """Elementwise / reduction / GEMM workloads of the hot-path sweep, one line each."""
     L, A = capi.lib(), capi
@@ -224,7 +236,44 @@ def kernel_suite(capi, pk):
     shp = (C.c_int64 * 2)(r, r)
     rec("swapaxes_16384^2", time_launch(A, lambda: A.check(L.fz_swapaxes(o.ptr, a.ptr, shp, 2, 0, 1, None))),
         8 * r * r)
-    for arr in (a, b, o):
+    # Backward formulas (the registry's, as the fusion IR lowers them: one fused program
+    # per op, sibling gradients of a binary op as two outputs of one program), upstream
+    # gradient g ~ U(-1,1), x ~ U(-1,1) (U(0.01,10) for log/sqrt), y ~ U(0.5,2); 2^28
+    # elements; algorithmic bytes as counted for the backward sweep.
+    rng = np.random.default_rng(SEED + 5)
+    m = n
+    def uni(lo, hi):
+        return A.DeviceArray.from_numpy(rng.random(m, dtype=np.float32) * np.float32(hi - lo)
+                                        + np.float32(lo))
+    ga, xa, xp, ya = uni(-1, 1), uni(-1, 1), uni(0.01, 10), uni(0.5, 2)
+    o2 = A.DeviceArray((m,))
+    BI, UN, CO = A.NODE_BINARY, A.NODE_UNARY, A.NODE_CONST
+    bo, uo = A.BINOPS, A.UNOPS
+    # name: (nodes with leaf i referenced as -1-i, leaves, output nodes, bytes per element)
+    progs = {
+        "add_bwd_accumulate": ([(BI, bo["add"], -1, -2, 0.0)], [ga, xa], [0], 12),
+        "sub_bwd": ([(CO, 0, 0, 0, 0.0), (BI, bo["sub"], 0, -1, 0.0)], [ga], [1], 8),
+        "mul_bwd": ([(BI, bo["mul"], -1, -3, 0.0), (BI, bo["mul"], -1, -2, 0.0)], [ga, xa, ya],
+                    [0, 1], 20),
+        "div_bwd": ([(BI, bo["div"], -1, -3, 0.0), (CO, 0, 0, 0, 0.0), (BI, bo["sub"], 1, -1, 0.0),
+                     (BI, bo["mul"], 2, -2, 0.0), (BI, bo["mul"], -3, -3, 0.0),
+                     (BI, bo["div"], 3, 4, 0.0)], [ga, xa, ya], [0, 5], 20),
+        "exp_bwd": ([(UN, uo["exp"], -2, 0, 0.0), (BI, bo["mul"], -1, 0, 0.0)], [ga, xa], [1], 12),
+        "log_bwd": ([(BI, bo["div"], -1, -2, 0.0)], [ga, xp], [0], 12),
+        "sqrt_bwd": ([(UN, uo["sqrt"], -2, 0, 0.0), (CO, 0, 0, 0, 2.0), (BI, bo["mul"], 0, 1, 0.0),
+                      (BI, bo["div"], -1, 2, 0.0)], [ga, xp], [3], 12),
+        "relu_bwd": ([(CO, 0, 0, 0, 0.0), (BI, bo["gt"], -2, 0, 0.0), (BI, bo["mul"], -1, 1, 0.0)],
+                     [ga, xa], [2], 12),
+    }
+    for name, (nodes, leaf_arrays, outs, per_elem) in progs.items():
+        prog = fused_program(A, nodes, len(leaf_arrays), outs)
+        plan = A.make_plan((m,), [(m,)] * (len(outs) + len(leaf_arrays)))
+        leaves = (C.c_void_p * len(leaf_arrays))(*[arr.ptr for arr in leaf_arrays])
+        optrs = (C.c_void_p * len(outs))(*[arr.ptr for arr in (o, o2)[:len(outs)]])
+        ms = time_launch(A, lambda: A.check(L.fz_fused_launch(C.byref(prog), C.byref(plan), optrs,
+                                                               leaves, None)))
+        rec(name + "_2^28", ms, per_elem * m)
+    for arr in (a, b, o, o2, ga, xa, xp, ya):
         arr.free()
     # GEMMs (N(0,1) operands), whole fz_gemm_f32 call including the remainder split:
     # square 8192^3 (A [M,K], B [K,N]) and the weight-gradient shape x^T @ g

@@ -323,6 +323,18 @@ BackwardResult Engine::backward(ValueID seed) {
                                ": " + e.what());
     }
     FB_CHECK(gin.size() == n.inputs.size(), "backward arity mismatch");
+    // Both operands are leaves that require grad (their gradients are final values):
+    // lower the two pending gradients together, one pass over the shared upstream
+    // gradient and operands (e.g. Multiply: g0*y and g0*x read g0, x, y once).
+    if (gin.size() == 2 && n.inputs[0] != n.inputs[1] && gin[0].is_initialised() &&
+        gin[1].is_initialised() && gin[0].pending() && gin[1].pending() &&
+        gin[0].shape() == gin[1].shape()) {
+      bool leaves = true;
+      for (ValueID v : n.inputs)
+        leaves = leaves && produced_by_[v] == -1 && requires_grad_set_.count(v) &&
+                 !grad_[v].is_initialised();
+      if (leaves) materialize_group({gin[0].expr(), gin[1].expr()});
+    }
     for (size_t j = 0; j < n.inputs.size(); ++j) {
       if (!gin[j].is_initialised()) continue;  // unobservable gradient, not computed
       RawTensor &dst = grad_[n.inputs[j]];

@@ -378,6 +378,48 @@ void materialize_with_lo(const ExprPtr &ep) {
   e->leaves_ub = 1;
 }
 
+// Lower several pending nodes of one shape as the outputs of one fused program
+// (sibling gradients of a binary op read the same upstream gradient and operands: one
+// pass instead of one per output). Falls back to lowering them one by one.
+void materialize_group(const std::vector<ExprPtr> &eps) {
+  std::vector<ExprPtr> todo;
+  for (const ExprPtr &e : eps)
+    if (e && e->kind != Expr::Leaf && e->kind != Expr::Const && e->numel() > 0 &&
+        std::find(todo.begin(), todo.end(), e) == todo.end())
+      todo.push_back(e);
+  bool grouped = todo.size() >= 2 && (int)todo.size() <= FZ_MAX_OUTPUTS;
+  for (const ExprPtr &e : todo) grouped = grouped && e->shape == todo[0]->shape;
+  if (grouped) {
+    Lowering L;
+    std::vector<int> roots;
+    for (const ExprPtr &e : todo) roots.push_back(L.visit(e.get()));
+    for (int r : roots) grouped = grouped && r >= 0;
+    if (grouped && !L.overflow) {
+      L.prog.num_leaves = (int32_t)L.leaves.size();
+      L.prog.num_outputs = (int32_t)todo.size();
+      std::vector<std::shared_ptr<DeviceBuffer>> bufs;
+      std::vector<float *> outs;
+      for (size_t k = 0; k < todo.size(); ++k) {
+        L.prog.out_node[k] = roots[k];
+        bufs.push_back(std::make_shared<DeviceBuffer>(todo[k]->numel()));
+        outs.push_back(bufs.back()->ptr);
+      }
+      launch_program(L, todo[0]->shape, outs);
+      for (size_t k = 0; k < todo.size(); ++k) {
+        Expr *e = todo[k].get();
+        e->kind = Expr::Leaf;
+        e->buf = bufs[k];
+        e->a.reset();
+        e->b.reset();
+        e->nodes_ub = 0;
+        e->leaves_ub = 1;
+      }
+      return;
+    }
+  }
+  for (const ExprPtr &e : todo) materialize(e);
+}
+
 static ExprPtr make_op(Expr::Kind kind, int op, ExprPtr a, ExprPtr b, std::vector<size_t> shape) {
   // size policy: keep every pending program within the fused-kernel limits
   auto nodes = [&]() { return 1 + a->nodes_ub + (b ? b->nodes_ub : 0); };

@@ -107,6 +107,8 @@ bool split_cache_enabled();
 void materialize(const ExprPtr &e);
 // Lower a pending node and its TF32 remainder plane in one fused pass (GEMM operands).
 void materialize_with_lo(const ExprPtr &e);
+// Lower several pending nodes of one shape as outputs of one fused program.
+void materialize_group(const std::vector<ExprPtr> &eps);
 int64_t fused_launches();
 
 class RawTensor {

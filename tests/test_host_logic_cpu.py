@@ -178,3 +178,22 @@ def test_overlapped_gradient_average_matches_plain_step(fake_fusion):
         np.testing.assert_array_equal(Wo, Wp)
         np.testing.assert_array_equal(bo, bp)
     comm.destroy()
+
+
+def test_sibling_gradients_lowered_together(fake_fusion):
+    """Multiply backward over two leaves: g0*y and g0*x come out of one fused program
+    (one pass over g0, x and y), with the same values as separate lowering."""
+    F = fake_fusion
+    rng = np.random.default_rng(4)
+    a, b, g = (rng.standard_normal((64, 32)).astype(np.float32) for _ in range(3))
+    x, y = api_cases.T(F, a, True), api_cases.T(F, b, True)
+    gt = api_cases.T(F, g)
+    with F.grad_tape():
+        z = x * y
+        w = z * gt
+        before = F.stats()["fused_launches"]
+        w.backward()
+        after = F.stats()["fused_launches"]
+    assert after - before == 1
+    np.testing.assert_array_equal(x.get_grad().to_numpy(), (np.ones_like(g) * g) * b)
+    np.testing.assert_array_equal(y.get_grad().to_numpy(), (np.ones_like(g) * g) * a)
