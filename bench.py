@@ -213,6 +213,10 @@ def kernel_suite(capi, pk):
     for op in ("add", "mul", "div"):
         rec(f"{op}_2^28", time_launch(A, lambda: A.check(L.fz_ewise_binary_contig(
             A.BINOPS[op], n, o.ptr, a.ptr, b.ptr, None))), 12 * n)
+    for e in (25, 26, 27):  # smaller sizes of the sweep (three operands still exceed L2)
+        k = 1 << e
+        rec(f"add_2^{e}", time_launch(A, lambda: A.check(L.fz_ewise_binary_contig(
+            0, k, o.ptr, a.ptr, b.ptr, None))), 12 * k)
     plan = A.make_plan((n,), [(n,), (n,)])
     for op in ("exp", "log", "sqrt"):
         rec(f"{op}_2^28", time_launch(A, lambda: A.check(L.fz_ewise_unary(
@@ -275,22 +279,48 @@ def kernel_suite(capi, pk):
         rec(name + "_2^28", ms, per_elem * m)
     for arr in (a, b, o, o2, ga, xa, xp, ya):
         arr.free()
-    # GEMMs (N(0,1) operands), whole fz_gemm_f32 call including the remainder split:
-    # square 8192^3 (A [M,K], B [K,N]) and the weight-gradient shape x^T @ g
-    # (K = 65536 batch rows, both operands MN-major)
-    for name, (M, N, K, tA, tB) in (("gemm_3xtf32_8192^3", (8192, 8192, 8192, 0, 0)),
-                                    ("gemm_3xtf32_wgrad_4096x4096x65536", (4096, 4096, 65536, 1, 0))):
-        x = _random_device(A, (K, M) if tA else (M, K), 21)
-        y = _random_device(A, (N, K) if tB else (K, N), 22)
-        c = A.DeviceArray((M, N))
+    # GEMM sweep (N(0,1)/sqrt(K) operands), whole fz_gemm_f32 call including the remainder
+    # split: square M=N=K (A [M,K], B [K,N]), the transpose-B variant (B given [N,K]), the
+    # batched [64,512,512]^2, the weight-gradient shape x^T @ g (K = 65536 batch rows, both
+    # operands MN-major) and the linear+ReLU forward of [512,1024] x [1024,512] (+ bias, ReLU)
+    gemms = [(f"gemm_3xtf32_{s}^3", (1, s, s, s, 0, 0)) for s in (1024, 2048, 4096, 8192, 16384)]
+    gemms += [("gemm_3xtf32_8192^3_transB", (1, 8192, 8192, 8192, 0, 1)),
+              ("gemm_3xtf32_batched_64x512^3", (64, 512, 512, 512, 0, 0)),
+              ("gemm_3xtf32_wgrad_4096x4096x65536", (1, 4096, 4096, 65536, 1, 0))]
+    for name, (bt, M, N, K, tA, tB) in gemms:
+        x = _random_device(A, (bt, K, M) if tA else (bt, M, K), 21)
+        y = _random_device(A, (bt, N, K) if tB else (bt, K, N), 22)
+        c = A.DeviceArray((bt, M, N))
         lda, ldb = (M if tA else K), (K if tB else N)
-        ms = time_launch(A, lambda: A.check(L.fz_gemm_f32(1, M, N, K, x.ptr, lda, 0, tA, y.ptr, ldb,
-                                                          0, tB, c.ptr, N, 0, None)), reps=5, warm=2)
-        tf = 2.0 * M * N * K / ms / 1e9
-        out[name] = {"ms": round(ms, 3), "TFLOP/s": round(tf, 1), "tensor_pipe_TFLOP/s": round(3 * tf, 1)}
+        reps = 3 if M * N * K >= 16384 ** 3 else 5
+        ms = time_launch(A, lambda: A.check(L.fz_gemm_f32(bt, M, N, K, x.ptr, lda, M * K, tA, y.ptr,
+                                                          ldb, N * K, tB, c.ptr, N, M * N, None)),
+                         reps=reps, warm=2)
+        tf = 2.0 * bt * M * N * K / ms / 1e9
+        out[name] = {"ms": round(ms, 3), "TFLOP/s": round(tf, 1), "tensor_pipe_TFLOP/s": round(3 * tf, 1),
+                     "frac_of_3xtf32_ceiling": round(tf / (pk["bf16_tflops"] / 6.0), 3)}
         for arr in (x, y, c):
             arr.free()
+    out["linear_relu_512x1024x512"] = linear_relu_case(capi)
     return out
+
+
+def linear_relu_case(capi):
+    """C = relu(A @ B + bias), A [512,1024], B [1024,512], bias [512], through the Python
+    API (GEMM, then the fused bias+ReLU program): device time per call."""
+    import nova_b200
+
+    F = nova_b200.fusion
+    rng = np.random.default_rng(SEED + 9)
+    dev = F.CppDevice(F.CppDeviceType.CPU, 0)
+
+    def t(a):
+        return F.Tensor(list(a.shape), a.ravel(), F.CppDType.FLOAT32, dev, False)
+    Am = t(rng.standard_normal((512, 1024), dtype=np.float32))
+    Bm = t(rng.standard_normal((1024, 512), dtype=np.float32))
+    bias = t(rng.uniform(-0.1, 0.1, 512).astype(np.float32))
+    ms = time_launch(capi, lambda: F.flush((Am @ Bm + bias).maximum(0.0)), reps=20, warm=3)
+    return {"ms": round(ms, 4), "TFLOP/s": round(2.0 * 512 * 1024 * 512 / ms / 1e9, 2)}
 
 
 def _random_device(capi, shape, seed):

@@ -901,9 +901,9 @@ int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
 std::atomic<int> g_tile_mode{FZ_GEMM_TILES_AUTO};
 
 // Number of K splits for a GEMM of `tiles` output tiles. A split turns one tile
-// into several units over K ranges (multiples of the 256-wide promotion chunk, at
-// least 1024 long) whose fp32 partials are summed afterwards; it pays when the
-// tiles fill the 148 SMs poorly (weight gradients: few tiles, K = batch rows).
+// into several units over K ranges (multiples of the 256-wide promotion chunk)
+// whose fp32 partials are summed afterwards; it pays when the tiles fill the 148
+// SMs poorly (weight gradients: few tiles, K = batch rows; small square products).
 // Cost model in units of one tile's time per k: waves * K_per_unit, plus the
 // partials' write and read at HBM speed.
 int choose_splits(int64_t tiles, int64_t M, int64_t N, int64_t K, int64_t batch, int64_t workers) {
@@ -914,7 +914,7 @@ int choose_splits(int64_t tiles, int64_t M, int64_t N, int64_t K, int64_t batch,
   const int cand[] = {1, 2, 3, 4, 6, 8, 12, 16, 24, 32};
   for (int sp : cand) {
     const int64_t kps = sp == 1 ? K : round_up((K + sp - 1) / sp, (int64_t)BK * KCHUNK);
-    if (sp > 1 && kps < 1024) break;
+    if (sp > 1 && kps < (int64_t)BK * KCHUNK) break;
     const int64_t real = (K + kps - 1) / kps;
     const int64_t waves = (tiles * real + sms - 1) / sms;
     double t = (double)waves * (double)kps;
