@@ -261,8 +261,9 @@ int fz_gemm_f32_split(int64_t batch, int64_t M, int64_t N, int64_t K,
  * (the plane fz_gemm_f32_split takes). */
 int fz_tf32_lo(float *lo, const float *x, int64_t n, void *stream);
 /* GEMM tile schedule for the calls that follow (process-wide): FZ_GEMM_TILES_AUTO picks
- * CTA pairs (256 x 256 tiles, tcgen05 cta_group::2) for products with at least 256 rows
- * and enough tiles to occupy every SM pair, single CTAs (128 x 256 tiles) otherwise;
+ * CTA pairs (256 x 256 tiles, tcgen05 cta_group::2) for products with at least 256 rows,
+ * more than 64 columns and enough tiles to occupy every SM pair, single CTAs otherwise
+ * (128 x 256 tiles, or 128 x 64 / 128 x 16 for outputs of at most 64 / 16 columns);
  * SINGLE and PAIR force one schedule (a pair schedule on fewer rows computes zero rows).
  * Both meet the same error bounds; with the same K split (none, or the same count) an
  * output element is accumulated from the same K chunks in the same order. */

@@ -323,8 +323,47 @@ __device__ __forceinline__ int unit_k_tiles(const GemmArgs &a, int ks, int &k_be
 // Persistent kernel: one CTA per SM walks tiles blockIdx.x, +gridDim.x, ...
 // K is cut into chunks of KCHUNK k-tiles accumulated alternately in two TMEM
 // buffers; warps 2-9 fold each finished chunk into fp32 registers.
-// A_MN / B_MN: the operand is MN-major in global and shared memory.
-template <bool A_MN, bool B_MN>
+// Per tile width TBN (output columns per tile): 256 for wide products, 64 or 16 for
+// narrow ones (a 16-wide output layer would otherwise compute 256 columns for 16).
+// Narrow tiles use more stages of smaller k-tiles, within the same ~192 KB.
+template <int TBN>
+struct TileCfg {
+  static constexpr int B_BYTES = TBN * BK * 4;
+  static constexpr int STAGE = 2 * TILE_A_BYTES + 2 * B_BYTES;
+  static constexpr int NSTAGE = TBN == BN ? STAGES : (192 * 1024) / STAGE;
+  static constexpr int TMEM = TBN < 32 ? 32 : TBN;  // TMEM columns per accumulator buffer
+  static constexpr int CPW = TBN / 2;               // columns per epilogue warp
+  static_assert(TBN == 256 || TBN == 64 || TBN == 16, "tile width");
+};
+
+// Add CPW accumulator columns of this warp's TMEM lanes, from `taddr`, into acc.
+template <int CPW>
+__device__ __forceinline__ void promote_cols(uint32_t taddr, float (&acc)[CPW]) {
+  if constexpr (CPW >= 32) {
+#pragma unroll
+    for (int c0 = 0; c0 < CPW; c0 += 32) {
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(taddr + (uint32_t)c0, r);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) acc[c0 + i] = __fadd_rn(acc[c0 + i], __uint_as_float(r[i]));
+    }
+  } else {
+    static_assert(CPW == 8, "columns per warp");
+    uint32_t r[8];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] = __fadd_rn(acc[i], __uint_as_float(r[i]));
+  }
+}
+
+// A_MN / B_MN: the operand is MN-major in global and shared memory (B is K-major
+// whenever TBN < 256).
+template <bool A_MN, bool B_MN, int TBN>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap mapAh,
                        const __grid_constant__ CUtensorMap mapAl,
@@ -333,6 +372,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  using T = TileCfg<TBN>;
+  constexpr int STAGES = T::NSTAGE;
+  constexpr int STAGE_BYTES = T::STAGE;
+  constexpr int TILE_B_BYTES = T::B_BYTES;
+  constexpr int TMEM_COLS = T::TMEM;
+  constexpr int CPW = T::CPW;
+  static_assert(TBN == BN || !B_MN, "narrow tiles read B K-major");
   __shared__ __align__(8) uint64_t full_bar[STAGES];
   __shared__ __align__(8) uint64_t empty_bar[STAGES];
   __shared__ __align__(8) uint64_t acc_full[2];
@@ -341,7 +387,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   __shared__ volatile int abort_flag;
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  constexpr uint32_t kIdesc = make_idesc(BM, BN, A_MN, B_MN);
+  constexpr uint32_t kIdesc = make_idesc(BM, TBN, A_MN, B_MN);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -401,8 +447,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const int k0 = kb + kt * BK;
           load_operand<A_MN, BM>(stage_ptr(s, 0), &mapAh, &full_bar[s], k0, mb * BM, bz, args.wide & 1);
           load_operand<A_MN, BM>(stage_ptr(s, 1), &mapAl, &full_bar[s], k0, mb * BM, bz, args.wide & 2);
-          load_operand<B_MN, BN>(stage_ptr(s, 2), &mapBh, &full_bar[s], k0, nb * BN, bz, args.wide & 4);
-          load_operand<B_MN, BN>(stage_ptr(s, 3), &mapBl, &full_bar[s], k0, nb * BN, bz, args.wide & 8);
+          load_operand<B_MN, TBN>(stage_ptr(s, 2), &mapBh, &full_bar[s], k0, nb * TBN, bz, args.wide & 4);
+          load_operand<B_MN, TBN>(stage_ptr(s, 3), &mapBl, &full_bar[s], k0, nb * TBN, bz, args.wide & 8);
         }
       }
       if (!ok) {
@@ -466,7 +512,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   } else {
     // ------------------------------------------------------ promotion + epilogue (warps 2..9)
     const int q = warp & 3;             // TMEM lane quarter this warp may access
-    const int half = (warp - 2) >> 2;   // which 128 of the 256 columns
+    const int half = (warp - 2) >> 2;   // which half of the tile's columns
     const bool vec = ((args.ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(args.C) & 15) == 0) &&
                      ((args.strideC & 3) == 0);
     int cc = 0;
@@ -475,9 +521,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       int mb, nb, bz, ks, kb;
       decode_tile(t, args, mb, nb, bz, ks);
       const int num_k = unit_k_tiles(args, ks, kb);
-      float acc[128];
+      float acc[CPW];
 #pragma unroll
-      for (int i = 0; i < 128; ++i) acc[i] = 0.0f;
+      for (int i = 0; i < CPW; ++i) acc[i] = 0.0f;
       for (int kt0 = 0; kt0 < num_k; kt0 += KCHUNK, ++cc) {
         const int b = cc & 1;
         if (!mbar_wait(&acc_full[b], (cc >> 1) & 1, &abort_flag)) {
@@ -487,31 +533,25 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           break;
         }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint32_t taddr = tmem_base + (uint32_t)(b * TMEM_COLS + half * 128) +
+        const uint32_t taddr = tmem_base + (uint32_t)(b * TMEM_COLS + half * CPW) +
                                ((uint32_t)(q * 32) << 16);
-#pragma unroll
-        for (int c0 = 0; c0 < 128; c0 += 32) {
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(taddr + (uint32_t)c0, r);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) acc[c0 + i] = __fadd_rn(acc[c0 + i], __uint_as_float(r[i]));
-        }
+        promote_cols<CPW>(taddr, acc);
         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
         mbar_arrive(&acc_empty[b]);
       }
       if (!ok) break;
       const int row = mb * BM + q * 32 + lane;
-      const int col0 = nb * BN + half * 128;
+      const int col0 = nb * TBN + half * CPW;
       if (row < args.M && col0 < args.N) {
         float *crow = args.C + (int64_t)ks * args.split_stride + (int64_t)bz * args.strideC +
                       (int64_t)row * args.ldc + col0;
-        if (vec && col0 + 128 <= args.N) {
+        if (vec && col0 + CPW <= args.N) {
 #pragma unroll
-          for (int i = 0; i < 128; i += 4)
+          for (int i = 0; i < CPW; i += 4)
             *reinterpret_cast<float4 *>(crow + i) = make_float4(acc[i], acc[i + 1], acc[i + 2], acc[i + 3]);
         } else {
 #pragma unroll
-          for (int i = 0; i < 128; ++i)
+          for (int i = 0; i < CPW; ++i)
             if (col0 + i < args.N) crow[i] = acc[i];
         }
       }
@@ -992,7 +1032,7 @@ int prepare(const float *src, int64_t ld, int64_t sb, const float *lo_given, int
   return FZ_OK;
 }
 
-template <bool A_MN, bool B_MN>
+template <bool A_MN, bool B_MN, int TBN>
 int launch_gemm(const CUtensorMap &mAh, const CUtensorMap &mAl, const CUtensorMap &mBh,
                 const CUtensorMap &mBl, const GemmArgs &ga, unsigned grid, bool pair,
                 cudaStream_t s) {
@@ -1000,24 +1040,40 @@ int launch_gemm(const CUtensorMap &mAh, const CUtensorMap &mAl, const CUtensorMa
   int dev = 0;
   cudaGetDevice(&dev);
   const size_t smem = pair ? (size_t)PAIR_STAGES * PAIR_STAGE_BYTES + 1024
-                           : (size_t)STAGES * STAGE_BYTES + 1024;
+                           : (size_t)TileCfg<TBN>::NSTAGE * TileCfg<TBN>::STAGE + 1024;
   if (dev < 64 && !attr_done[pair][dev]) {
     if (pair)
       cudaFuncSetAttribute(gemm_pair_kernel<A_MN, B_MN>,
                            cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     else
-      cudaFuncSetAttribute(gemm_3xtf32_kernel<A_MN, B_MN>,
+      cudaFuncSetAttribute(gemm_3xtf32_kernel<A_MN, B_MN, TBN>,
                            cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     attr_done[pair][dev] = true;
   }
   if (pair)
     gemm_pair_kernel<A_MN, B_MN><<<2 * grid, NUM_THREADS, smem, s>>>(mAh, mAl, mBh, mBl, ga);
   else
-    gemm_3xtf32_kernel<A_MN, B_MN><<<grid, NUM_THREADS, smem, s>>>(mAh, mAl, mBh, mBl, ga);
+    gemm_3xtf32_kernel<A_MN, B_MN, TBN><<<grid, NUM_THREADS, smem, s>>>(mAh, mAl, mBh, mBl, ga);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fz::cuda_fail(e, "gemm_3xtf32_kernel launch", __FILE__, __LINE__);
   fz::note_launch();
   return FZ_OK;
+}
+
+// Kernel for the operand layouts and tile width (narrow tiles read B K-major).
+int dispatch_gemm(bool a_mn, bool b_mn, int tbn, const CUtensorMap &mAh, const CUtensorMap &mAl,
+                  const CUtensorMap &mBh, const CUtensorMap &mBl, const GemmArgs &ga,
+                  unsigned grid, bool pair, cudaStream_t s) {
+  if (tbn == 16)
+    return a_mn ? launch_gemm<true, false, 16>(mAh, mAl, mBh, mBl, ga, grid, false, s)
+                : launch_gemm<false, false, 16>(mAh, mAl, mBh, mBl, ga, grid, false, s);
+  if (tbn == 64)
+    return a_mn ? launch_gemm<true, false, 64>(mAh, mAl, mBh, mBl, ga, grid, false, s)
+                : launch_gemm<false, false, 64>(mAh, mAl, mBh, mBl, ga, grid, false, s);
+  if (!a_mn && !b_mn) return launch_gemm<false, false, BN>(mAh, mAl, mBh, mBl, ga, grid, pair, s);
+  if (!a_mn && b_mn) return launch_gemm<false, true, BN>(mAh, mAl, mBh, mBl, ga, grid, pair, s);
+  if (a_mn && !b_mn) return launch_gemm<true, false, BN>(mAh, mAl, mBh, mBl, ga, grid, pair, s);
+  return launch_gemm<true, true, BN>(mAh, mAl, mBh, mBl, ga, grid, pair, s);
 }
 
 int gemm_impl(int64_t batch, int64_t M, int64_t N, int64_t K, const float *A, const float *A_lo,
@@ -1044,6 +1100,36 @@ int gemm_impl(int64_t batch, int64_t M, int64_t N, int64_t K, const float *A, co
   int rc = get_encoder();
   if (rc) return rc;
 
+  // CTA pairs (256 x 256 tiles, cta_group::2) when there are rows for both halves
+  // and enough tiles to keep the pairs busy; single CTAs otherwise, with 16- or
+  // 64-column tiles for narrow outputs
+  const int64_t pair_tiles = ((M + 2 * BM - 1) / (2 * BM)) * ((N + BN - 1) / BN) * batch;
+  const int mode = g_tile_mode.load(std::memory_order_relaxed);
+  const bool pair = mode == FZ_GEMM_TILES_PAIR ||
+                    (mode == FZ_GEMM_TILES_AUTO && M >= 2 * BM && N > 64 &&
+                     pair_tiles * 2 >= fz::num_sms());
+  int tbn = pair || N > 64 ? BN : N > 16 ? 64 : 16;
+  // narrow tiles read B K-major: a dense MN-major B ([K, N], N <= 64, a few MB) is
+  // transposed into a K-major copy first
+  float *bt = nullptr;
+  if (tbn < BN && transB == 0) {
+    if (ldb == N && (batch == 1 || strideB == K * N) && (((uintptr_t)B) & 15) == 0) {
+      rc = fz_malloc((void **)&bt, sizeof(float) * batch * N * K, s);
+      const int64_t shp[3] = {batch, K, N};
+      if (!rc) rc = fz_swapaxes(bt, B, shp, 3, 1, 2, s);
+      if (rc) {
+        fz_free(bt, s);
+        return rc;
+      }
+      B = bt;
+      B_lo = nullptr;
+      ldb = K;
+      strideB = N * K;
+      transB = 1;
+    } else {
+      tbn = BN;
+    }
+  }
   // A as stored: [M, K] (transA = 0, K-major) or [K, M] (MN-major); B: [N, K]
   // (transB != 0, K-major) or [K, N] (MN-major).
   Operand oa{transA != 0, transA ? K : M, transA ? M : K};
@@ -1053,18 +1139,15 @@ int gemm_impl(int64_t batch, int64_t M, int64_t N, int64_t K, const float *A, co
   float *ws = nullptr;
   if (a_need + b_need) {
     rc = fz_malloc((void **)&ws, sizeof(float) * (a_need + b_need), s);
-    if (rc) return rc;
+    if (rc) {
+      fz_free(bt, s);
+      return rc;
+    }
   }
   rc = prepare(A, lda, strideA, A_lo, batch, ws, &oa, s);
   if (!rc) rc = prepare(B, ldb, strideB, B_lo, batch, ws + a_need, &ob, s);
 
-  // CTA pairs (256 x 256 tiles, cta_group::2) when there are rows for both halves
-  // and enough tiles to keep the pairs busy; single CTAs (128 x 256) otherwise
-  const int64_t pair_tiles = ((M + 2 * BM - 1) / (2 * BM)) * ((N + BN - 1) / BN) * batch;
-  const int mode = g_tile_mode.load(std::memory_order_relaxed);
-  const bool pair = mode == FZ_GEMM_TILES_PAIR ||
-                    (mode == FZ_GEMM_TILES_AUTO && M >= 2 * BM && pair_tiles * 2 >= fz::num_sms());
-  const int tile_m = pair ? 2 * BM : BM, box_b = pair ? BM : BN;
+  const int tile_m = pair ? 2 * BM : BM, box_b = pair ? BM : tbn;
   const int64_t workers = pair ? fz::num_sms() / 2 : fz::num_sms();
   CUtensorMap mAh, mAl, mBh, mBl;
   bool wide[4] = {false, false, false, false};
@@ -1073,7 +1156,7 @@ int gemm_impl(int64_t batch, int64_t M, int64_t N, int64_t K, const float *A, co
   if (!rc) rc = make_map(&mBh, ob.hi, ob.mn, N, K, ob.hi_ld, ob.hi_sb, batch, box_b, ob.hi_padded, &wide[2]);
   if (!rc) rc = make_map(&mBl, ob.lo, ob.mn, N, K, ob.lo_ld, ob.lo_sb, batch, box_b, ob.lo_padded, &wide[3]);
   const int wide_mask = (int)wide[0] | (int)wide[1] << 1 | (int)wide[2] << 2 | (int)wide[3] << 3;
-  const int tiles_m = (int)((M + tile_m - 1) / tile_m), tiles_n = (int)((N + BN - 1) / BN);
+  const int tiles_m = (int)((M + tile_m - 1) / tile_m), tiles_n = (int)((N + tbn - 1) / tbn);
   const int64_t tiles = (int64_t)tiles_m * tiles_n * batch;
   const bool dense_c = ldc == N && (batch == 1 || strideC == M * N);
   const int splits = dense_c ? choose_splits(tiles, M, N, K, batch, workers) : 1;
@@ -1094,15 +1177,13 @@ int gemm_impl(int64_t batch, int64_t M, int64_t N, int64_t K, const float *A, co
                 real_splits, (int)kps, wide_mask, err};
     // persistent grid: one CTA (or CTA pair) per SM (pair of SMs)
     const unsigned grid = (unsigned)(num_units < workers ? num_units : workers);
-    if (!oa.mn && !ob.mn) rc = launch_gemm<false, false>(mAh, mAl, mBh, mBl, ga, grid, pair, s);
-    else if (!oa.mn && ob.mn) rc = launch_gemm<false, true>(mAh, mAl, mBh, mBl, ga, grid, pair, s);
-    else if (oa.mn && !ob.mn) rc = launch_gemm<true, false>(mAh, mAl, mBh, mBl, ga, grid, pair, s);
-    else rc = launch_gemm<true, true>(mAh, mAl, mBh, mBl, ga, grid, pair, s);
+    rc = dispatch_gemm(oa.mn, ob.mn, tbn, mAh, mAl, mBh, mBl, ga, grid, pair, s);
     // K-split partials: summed over the splits in a fixed order (deterministic)
     if (!rc && partial) rc = fz_reduce(FZ_RSUM, C, partial, 1, real_splits, batch * M * N, s);
   }
   if (partial) fz_free(partial, s);
   fz_free(ws, s);
+  fz_free(bt, s);
   return rc;
 }
 
