@@ -237,6 +237,18 @@ def kernel_suite(capi, pk):
         A.check(L.fz_reduce(0, b.ptr, o.ptr, 64 * 256, 64, 1, None))
         A.check(L.fz_reduce(0, o.ptr, b.ptr, 1, 64, 256, None))
     rec("sum_4d_axes023_chained", time_launch(A, chain4d), 4 * 64 * 256 * 64 * 64)
+    # the same through the Python API: x.sum(3, True).sum(2, True).sum(0, True), where the
+    # host joins the adjacent axes 2 and 3 into one pass (rows of 4096), then axis 0
+    import nova_b200
+
+    F = nova_b200.fusion
+    dev = F.CppDevice(F.CppDeviceType.CPU, 0)
+    x4 = np.random.default_rng(SEED + 3).standard_normal((64, 256, 64, 64), dtype=np.float32)
+    t4 = F.Tensor(list(x4.shape), x4.ravel(), F.CppDType.FLOAT32, dev, False)
+    del x4
+    rec("sum_4d_axes023_api", time_launch(A, lambda: F.flush(t4.sum(3, True).sum(2, True).sum(0, True))),
+        4 * 64 * 256 * 64 * 64)
+    del t4
     shp = (C.c_int64 * 2)(r, r)
     rec("swapaxes_16384^2", time_launch(A, lambda: A.check(L.fz_swapaxes(o.ptr, a.ptr, shp, 2, 0, 1, None))),
         8 * r * r)

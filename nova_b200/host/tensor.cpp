@@ -313,9 +313,34 @@ static std::shared_ptr<DeviceBuffer> materialize_prefix(const ExprPtr &ep, size_
   return out;
 }
 
+// [outer, len, inner] view of a Reduce node over its input's shape.
+static void reduce_view(const Expr &e, int64_t &outer, int64_t &len, int64_t &inner) {
+  const auto &s = e.a->shape;
+  outer = len = inner = 1;
+  for (int d = 0; d < (int)s.size(); ++d) {
+    if (d < e.red_lo) outer *= (int64_t)s[d];
+    else if (d <= e.red_hi) len *= (int64_t)s[d];
+    else inner *= (int64_t)s[d];
+  }
+}
+
 void materialize(const ExprPtr &ep) {
   Expr *e = ep.get();
   if (e->kind == Expr::Leaf) return;
+  if (e->kind == Expr::Reduce) {
+    if (e->a->kind != Expr::Leaf) materialize(e->a);
+    int64_t outer, len, inner;
+    reduce_view(*e, outer, len, inner);
+    auto out = std::make_shared<DeviceBuffer>(e->numel());
+    if (e->numel() > 0)
+      fz_check(fz_reduce(e->op, out->ptr, e->a->buf->ptr, outer, len, inner, nullptr), "fz_reduce");
+    e->kind = Expr::Leaf;
+    e->buf = std::move(out);
+    e->a.reset();
+    e->nodes_ub = 0;
+    e->leaves_ub = 1;
+    return;
+  }
   auto out = std::make_shared<DeviceBuffer>(e->numel());
   if (e->numel() > 0 && !try_single_op(e, out->ptr)) {
     Lowering L;
@@ -345,7 +370,8 @@ void materialize(const ExprPtr &ep) {
 // instead of a second pass over the value. The plane is kept with the new buffer.
 void materialize_with_lo(const ExprPtr &ep) {
   Expr *e = ep.get();
-  if (e->kind == Expr::Leaf || e->kind == Expr::Const || e->numel() == 0) {
+  if (e->kind == Expr::Leaf || e->kind == Expr::Const || e->kind == Expr::Reduce ||
+      e->numel() == 0) {
     materialize(ep);
     return;
   }
@@ -384,6 +410,8 @@ void materialize_with_lo(const ExprPtr &ep) {
 void materialize_group(const std::vector<ExprPtr> &eps) {
   std::vector<ExprPtr> todo;
   for (const ExprPtr &e : eps)
+    if (e && e->kind == Expr::Reduce) materialize(e);
+  for (const ExprPtr &e : eps)
     if (e && e->kind != Expr::Leaf && e->kind != Expr::Const && e->numel() > 0 &&
         std::find(todo.begin(), todo.end(), e) == todo.end())
       todo.push_back(e);
@@ -421,6 +449,9 @@ void materialize_group(const std::vector<ExprPtr> &eps) {
 }
 
 static ExprPtr make_op(Expr::Kind kind, int op, ExprPtr a, ExprPtr b, std::vector<size_t> shape) {
+  // reductions are lowered on their own, never inside an elementwise program
+  if (a && a->kind == Expr::Reduce) materialize(a);
+  if (b && b->kind == Expr::Reduce) materialize(b);
   // size policy: keep every pending program within the fused-kernel limits
   auto nodes = [&]() { return 1 + a->nodes_ub + (b ? b->nodes_ub : 0); };
   auto leaves = [&]() { return a->leaves_ub + (b ? b->leaves_ub : 0); };
@@ -631,19 +662,21 @@ RawTensor unary(int op, const RawTensor &x) {
 // fusion::math::sum/mean (ops/Reduce.hpp:18-36) via make_reduction_meta
 // (PlanMeta.hpp:148-182): axis == (size_t)-1 with keepdim == false is the global
 // reduction to shape [1]; otherwise one axis, removed or kept as 1.
+// fusion::math::sum/mean/max over one axis (ops/Reduce.hpp:18-36). The result is a
+// pending Reduce node; when x is itself a pending reduction of the same op and keepdim
+// over the axes next to `axis`, the two join into one reduction over the merged axes
+// of x's input (x.sum(3, True).sum(2, True) reads its input once, as rows of
+// shape[2]*shape[3]). mean joins as one sum divided by the merged length. Joined
+// sums add in a different order than the chained calls: the result stays within the
+// reductions' error bound, not bit for bit.
 RawTensor reduce(int op, const RawTensor &x, size_t axis, bool keepdim) {
   FB_CHECK(x.is_initialised(), "reduction: uninitialised tensor");
   const auto &s = x.shape();
   std::vector<size_t> oshape;
-  int64_t outer = 1, len, inner = 1;
   if (axis == kGlobalReduceAxis && !keepdim) {
     oshape = {1};
-    len = (int64_t)x.size();
   } else {
     if (axis >= s.size()) throw std::runtime_error("axis out of range");
-    for (size_t d = 0; d < axis; ++d) outer *= (int64_t)s[d];
-    len = (int64_t)s[axis];
-    for (size_t d = axis + 1; d < s.size(); ++d) inner *= (int64_t)s[d];
     for (size_t d = 0; d < s.size(); ++d) {
       if (d == axis) {
         if (keepdim) oshape.push_back(1);
@@ -653,12 +686,36 @@ RawTensor reduce(int op, const RawTensor &x, size_t axis, bool keepdim) {
     }
     if (oshape.empty()) oshape = {1};
   }
-  const float *in = x.data();
-  size_t n = 1;
-  for (auto v : oshape) n *= v;
-  auto buf = std::make_shared<DeviceBuffer>(n);
-  fz_check(fz_reduce(op, buf->ptr, in, outer, len, inner, nullptr), "fz_reduce");
-  return RawTensor(make_leaf(std::move(buf), oshape), x.dtype(), x.device());
+  ExprPtr xe = x.expr();
+  auto e = std::make_shared<Expr>();
+  e->kind = Expr::Reduce;
+  e->op = op;
+  e->shape = oshape;
+  e->red_keep = keepdim;
+  if (axis == kGlobalReduceAxis && !keepdim) {
+    if (xe->kind == Expr::Reduce) materialize(xe);
+    e->a = xe;
+    e->red_lo = 0;
+    e->red_hi = (int)s.size() - 1;
+    return RawTensor(e, x.dtype(), x.device());
+  }
+  // join a pending reduction of the same op and keepdim over the adjacent axes
+  if (xe->kind == Expr::Reduce && xe->op == op && xe->red_keep == keepdim &&
+      !(xe->red_lo == 0 && xe->red_hi + 1 == (int)xe->a->shape.size() && !keepdim)) {
+    // axis of xe's input that `axis` names
+    const int removed = keepdim ? 0 : xe->red_hi - xe->red_lo + 1;
+    const int ax = (int)axis < xe->red_lo ? (int)axis : (int)axis + removed;
+    if (ax == xe->red_lo - 1 || ax == xe->red_hi + 1) {
+      e->a = xe->a;
+      e->red_lo = ax < xe->red_lo ? ax : xe->red_lo;
+      e->red_hi = ax > xe->red_hi ? ax : xe->red_hi;
+      return RawTensor(e, x.dtype(), x.device());
+    }
+  }
+  if (xe->kind == Expr::Reduce) materialize(xe);
+  e->a = xe;
+  e->red_lo = e->red_hi = (int)axis;
+  return RawTensor(e, x.dtype(), x.device());
 }
 
 // The TF32 remainder plane of a materialised GEMM operand, split on first use and
@@ -751,7 +808,7 @@ RawTensor swapaxes(const RawTensor &x, int a1, int a2) {
 // dims (the [U] bias minus row 0 of a [B, U] gradient), lower just that slice into
 // a buffer instead of all of y; null otherwise (read y itself).
 static std::shared_ptr<DeviceBuffer> prefix_values(const RawTensor &y, size_t n) {
-  if (!y.pending() || y.size() <= n) return nullptr;
+  if (!y.pending() || y.size() <= n || y.expr()->kind == Expr::Reduce) return nullptr;
   const auto &ys = y.shape();
   size_t tail = 1;
   for (size_t k = ys.size(); k-- > 0;) {

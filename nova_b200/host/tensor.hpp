@@ -75,12 +75,17 @@ struct DeviceBuffer {
 
 // ---- fusion IR node --------------------------------------------------------------
 struct Expr {
-  enum Kind { Leaf, Const, Unary, Binary } kind;
-  int op = 0;  // fz_binop / fz_unop
+  // Reduce: a pending single- or multi-axis reduction of `a` (fz_redop in op), kept
+  // pending so a following reduction over an adjacent axis can join it (one pass over
+  // the merged axes); lowered by itself, never inside an elementwise program.
+  enum Kind { Leaf, Const, Unary, Binary, Reduce } kind;
+  int op = 0;  // fz_binop / fz_unop / fz_redop
   std::vector<size_t> shape;
   std::shared_ptr<Expr> a, b;
   std::shared_ptr<DeviceBuffer> buf;  // Leaf
   float imm = 0.0f;                   // Const
+  int red_lo = 0, red_hi = 0;         // Reduce: axes [red_lo, red_hi] of a's shape
+  bool red_keep = false;              // Reduce: reduced axes kept as extent 1
   int nodes_ub = 1;                   // upper bounds used by the fusion size policy
   int leaves_ub = 0;
   size_t numel() const;

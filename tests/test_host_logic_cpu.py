@@ -197,3 +197,33 @@ def test_sibling_gradients_lowered_together(fake_fusion):
     assert after - before == 1
     np.testing.assert_array_equal(x.get_grad().to_numpy(), (np.ones_like(g) * g) * b)
     np.testing.assert_array_equal(y.get_grad().to_numpy(), (np.ones_like(g) * g) * a)
+
+
+@pytest.mark.parametrize("op", ["sum", "mean", "max"])
+def test_reduction_chains_join_adjacent_axes(fake_fusion, op):
+    """x.op(3, True).op(2, True) joins into one reduction over the merged axes (one
+    launch), a non-adjacent axis starts a new one; values match numpy's."""
+    F = fake_fusion
+    rng = np.random.default_rng(11)
+    a = rng.standard_normal((4, 5, 6, 7)).astype(np.float32)
+    x = api_cases.T(F, a)
+    f = {"sum": np.sum, "mean": np.mean, "max": np.max}[op]
+    if op == "max" and not hasattr(F.Tensor, "max"):
+        pytest.skip("no max reduction in this module")
+    before = F.stats()["kernel_launches"]
+    y = getattr(getattr(getattr(x, op)(3, True), op)(2, True), op)(0, True)
+    got = y.to_numpy()
+    assert F.stats()["kernel_launches"] - before == 2  # axes (2, 3) joined, then axis 0
+    want = f(a.astype(np.float64), axis=(0, 2, 3), keepdims=True)
+    np.testing.assert_allclose(got, want, rtol=1e-5, atol=1e-5)
+    # keepdim=False chain over adjacent axes, and a non-adjacent pair
+    z = getattr(getattr(x, op)(3), op)(2)
+    np.testing.assert_allclose(z.to_numpy(), f(a.astype(np.float64), axis=(2, 3)), rtol=1e-5, atol=1e-5)
+    before = F.stats()["kernel_launches"]
+    w = getattr(getattr(x, op)(1, True), op)(3, True)
+    np.testing.assert_allclose(w.to_numpy(), f(a.astype(np.float64), axis=(1, 3), keepdims=True),
+                               rtol=1e-5, atol=1e-5)
+    assert F.stats()["kernel_launches"] - before == 2
+    # a pending reduction feeding an elementwise op is lowered first
+    v = (getattr(x, op)(3, True) + 1.0).to_numpy()
+    np.testing.assert_allclose(v, f(a.astype(np.float64), axis=3, keepdims=True) + 1, rtol=1e-5, atol=1e-5)
