@@ -72,6 +72,7 @@ __global__ void __launch_bounds__(256) rows_group_kernel(const float *__restrict
     float acc[R];
 #pragma unroll
     for (int i = 0; i < R; ++i) acc[i] = Red<OP>::init();
+#pragma unroll 4
     for (int64_t j = lane; j < nv; j += G) {
       float4 q[R];
 #pragma unroll
@@ -349,7 +350,10 @@ int take_scratch(const Scratch &sc, int64_t need, float **part, bool *own, cudaS
 template <int OP>
 int launch_rows(const float *in, float *out, int64_t rows, int64_t len, int64_t div_len,
                 const Scratch &sc, cudaStream_t s) {
-  if (len <= 2048) return launch_rows_group<OP>(in, out, rows, len, len, div_len, true, s);
+  // short rows, or rows of up to 4K floats when there are enough of them for every warp
+  // of a full GPU to own some: lane groups (a whole warp per row above 256 floats)
+  if (len <= 2048 || (len <= 4096 && rows >= (int64_t)fz::num_sms() * 8))
+    return launch_rows_group<OP>(in, out, rows, len, len, div_len, true, s);
   const int threads = 512;
   const int64_t target_ctas = (int64_t)fz::num_sms() * 4;
   int64_t splits = 1;
