@@ -1171,9 +1171,12 @@ int gemm_impl(int64_t batch, int64_t M, int64_t N, int64_t K, const float *A, co
   int *err = nullptr;
   if (!rc) rc = fz::device_error_word(&err);
   if (!rc) {
+    // raster bands of 16 row tiles walked column by column (a narrower band for the
+    // 256-row pair tiles re-reads B once more per band and measured slower)
+    const int band = 16;
     GemmArgs ga{partial ? partial : C, partial ? N : ldc, partial ? M * N : strideC,
                 batch * M * N, (int)M, (int)N, (int)K, (int)batch,
-                tiles_m, tiles_n, (int)num_units, tiles_m < 16 ? tiles_m : 16,
+                tiles_m, tiles_n, (int)num_units, tiles_m < band ? tiles_m : band,
                 real_splits, (int)kps, wide_mask, err};
     // persistent grid: one CTA (or CTA pair) per SM (pair of SMs)
     const unsigned grid = (unsigned)(num_units < workers ? num_units : workers);
