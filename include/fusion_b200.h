@@ -72,6 +72,11 @@ int fz_get_device(int *device);
 /* The calling thread's stream on the current device (created on first use). */
 void *fz_default_stream(void);
 int fz_stream_sync(void *stream);
+/* The calling thread's upload stream on the current device (created on first use):
+ * host-to-device copies issued on it run beside the compute stream's work; a block
+ * fz_malloc'd on it and freed on another stream is reused only after that stream has
+ * passed the free. */
+void *fz_upload_stream(void);
 /* A second non-blocking stream on the current device (for collectives that overlap the
  * thread's compute stream), and its release. */
 int fz_stream_create(void **stream);
@@ -82,10 +87,11 @@ int fz_stream_destroy(void *stream);
 int fz_stream_wait(void *waiter, void *signaler);
 int fz_device_sync(void);
 
-/* Stream-ordered device memory. fz_free puts the block on a free list of `stream`
- * (the block may be reused by work ordered after that point on `stream`); the next
- * fz_malloc of the same size class on that stream takes it back without a driver
- * call. Misses go to the device's pool (cudaMallocAsync, release threshold raised).
+/* Stream-ordered device memory. fz_free(ptr, stream) marks the block free after the
+ * work submitted to `stream` so far; it goes back to the free list of the stream it
+ * was allocated on, and the next fz_malloc of the same size class there takes it back
+ * without a driver call (waiting for `stream` first when that is another stream).
+ * Misses go to the device's pool (cudaMallocAsync, release threshold raised).
  * Replaces PoolAllocator::allocate/deallocate
  * (fusion/src/Fusion/alloc/BFCPoolAllocator.cpp:59-111) for tensor storage.
  * fz_free of a pointer fz_malloc did not return fails with FZ_ERR_INVALID. */

@@ -197,6 +197,17 @@ int fz_stream_sync(void *stream) {
   return FZ_OK;
 }
 
+static thread_local cudaStream_t t_upload[kMaxDevices] = {};
+
+void *fz_upload_stream(void) {
+  int d = current_device();
+  if (!t_upload[d]) {
+    setup_device(d);
+    cudaStreamCreateWithFlags(&t_upload[d], cudaStreamNonBlocking);
+  }
+  return (void *)t_upload[d];
+}
+
 int fz_stream_create(void **stream) {
   FZ_REQUIRE(stream, "fz_stream_create: null pointer");
   cudaStream_t s = nullptr;
@@ -230,21 +241,29 @@ int fz_device_sync(void) {
 
 // Block cache in front of the stream-ordered pool, in the role of Fusion's
 // PoolAllocator (fusion/src/Fusion/alloc/BFCPoolAllocator.cpp:59-111). A freed
-// block goes onto a free list keyed by (stream, size class); the next allocation
-// of that class on the same stream takes it back without calling the driver. Work
-// on one stream runs in order, so a block reused on the stream it was freed on
-// needs no event. A training step allocates the same sizes every step, so in the
+// block goes back onto the free list of the stream it was allocated on (its home),
+// keyed by size class; the next allocation of that class on that stream takes it
+// back without calling the driver. Work on one stream runs in order, so a block
+// freed on its home stream is reused with no event; a block freed on another stream
+// (an upload buffer allocated on the upload stream and last read by the compute
+// stream) carries an event recorded at the free, which the home stream waits on
+// before reusing it. A training step allocates the same sizes every step, so in the
 // steady state no allocation reaches cudaMallocAsync; that call can block the host
 // for tens to hundreds of milliseconds in the driver while it maps pool pages,
 // long enough to leave the GPU idle behind it.
 namespace {
+struct CachedBlock {
+  void *ptr;
+  cudaEvent_t ready;  // recorded where the block was freed, if not on its home stream
+};
 struct FreeLists {
   int device = 0;
-  std::unordered_map<size_t, std::vector<void *>> by_size;
+  std::unordered_map<size_t, std::vector<CachedBlock>> by_size;
 };
 struct LiveBlock {
   size_t size;
   int device;
+  cudaStream_t home;
 };
 std::mutex g_cache_mu;
 std::unordered_map<void *, LiveBlock> g_live;
@@ -264,6 +283,7 @@ size_t size_class(size_t bytes) {
 // The device is synchronised first, so the blocks can be freed on any stream.
 int release_cached(int device) {
   std::vector<void *> blocks;
+  std::vector<cudaEvent_t> events;
   {
     std::lock_guard<std::mutex> lk(g_cache_mu);
     for (auto it = g_free.begin(); it != g_free.end();) {
@@ -272,7 +292,10 @@ int release_cached(int device) {
         continue;
       }
       for (auto &kv : it->second.by_size)
-        for (void *p : kv.second) blocks.push_back(p);
+        for (const CachedBlock &c : kv.second) {
+          blocks.push_back(c.ptr);
+          if (c.ready) events.push_back(c.ready);
+        }
       it = g_free.erase(it);
     }
     g_cached_bytes[device] = 0;
@@ -282,6 +305,7 @@ int release_cached(int device) {
   FZ_CUDA(cudaSetDevice(device));
   cudaStream_t s = fz::resolve(nullptr);
   cudaError_t e = cudaDeviceSynchronize();
+  for (cudaEvent_t ev : events) cudaEventDestroy(ev);
   for (void *p : blocks)
     if (e == cudaSuccess) e = cudaFreeAsync(p, s);
   if (e == cudaSuccess) e = cudaStreamSynchronize(s);
@@ -308,12 +332,17 @@ int fz_malloc(void **ptr, size_t bytes, void *stream) {
     if (it != g_free.end()) {
       auto jt = it->second.by_size.find(sz);
       if (jt != it->second.by_size.end() && !jt->second.empty()) {
-        void *p = jt->second.back();
+        const CachedBlock c = jt->second.back();
         jt->second.pop_back();
+        if (c.ready) {  // last used on another stream: wait for that use to finish
+          cudaError_t e = cudaStreamWaitEvent(s, c.ready, 0);
+          cudaEventDestroy(c.ready);
+          if (e != cudaSuccess) return cuda_fail(e, "cudaStreamWaitEvent(cached block)", __FILE__, __LINE__);
+        }
         g_cached_bytes[d] -= sz;
-        g_live.emplace(p, LiveBlock{sz, d});
+        g_live.emplace(c.ptr, LiveBlock{sz, d, s});
         g_live_bytes[d] += sz;
-        *ptr = p;
+        *ptr = c.ptr;
         return FZ_OK;
       }
     }
@@ -333,7 +362,7 @@ int fz_malloc(void **ptr, size_t bytes, void *stream) {
                                 " bytes failed: " + cudaGetErrorString(e));
   }
   std::lock_guard<std::mutex> lk(g_cache_mu);
-  g_live.emplace(*ptr, LiveBlock{sz, d});
+  g_live.emplace(*ptr, LiveBlock{sz, d, s});
   g_live_bytes[d] += sz;
   return FZ_OK;
 }
@@ -345,11 +374,17 @@ int fz_free(void *ptr, void *stream) {
   auto it = g_live.find(ptr);
   FZ_REQUIRE(it != g_live.end(), "fz_free: pointer was not returned by fz_malloc or was freed already");
   const LiveBlock b = it->second;
+  cudaEvent_t ready = nullptr;
+  if (s != b.home) {  // freed where it was last used, not where it lives
+    cudaError_t e = cudaEventCreateWithFlags(&ready, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventRecord(ready, s);
+    if (e != cudaSuccess) return cuda_fail(e, "fz_free: recording the free point", __FILE__, __LINE__);
+  }
   g_live.erase(it);
   g_live_bytes[b.device] -= b.size;
-  FreeLists &fl = g_free[s];
+  FreeLists &fl = g_free[b.home];
   fl.device = b.device;
-  fl.by_size[b.size].push_back(ptr);
+  fl.by_size[b.size].push_back(CachedBlock{ptr, ready});
   g_cached_bytes[b.device] += b.size;
   return FZ_OK;
 }

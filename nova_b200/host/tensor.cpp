@@ -71,10 +71,12 @@ size_t dtype_size(DType d) {
 }
 
 // ---------------------------------------------------------------- memory
-DeviceBuffer::DeviceBuffer(size_t n) : numel(n) {
+DeviceBuffer::DeviceBuffer(size_t n) : DeviceBuffer(n, nullptr) {}
+
+DeviceBuffer::DeviceBuffer(size_t n, void *stream) : numel(n) {
   fz_get_device(&device);
   void *p = nullptr;
-  fz_check(fz_malloc(&p, n * sizeof(float), nullptr), "fz_malloc");
+  fz_check(fz_malloc(&p, n * sizeof(float), stream), "fz_malloc");
   ptr = static_cast<float *>(p);
 }
 
@@ -489,8 +491,17 @@ RawTensor::RawTensor(std::vector<size_t> shape, const float *data, DType dtype, 
   set_contiguous_strides();
   size_t n = 1;
   for (auto s : shape_) n *= s;
-  auto buf = std::make_shared<DeviceBuffer>(n);
-  if (n) fz_check(fz_memcpy_h2d(buf->ptr, data, n * sizeof(float), nullptr), "fz_memcpy_h2d");
+  // Uploaded on the thread's upload stream, beside whatever the compute stream is
+  // still running (the next step's inputs while the current step computes). The host
+  // waits for the copy itself, so `data` may be reused or freed on return as with a
+  // synchronous copy; compute work submitted afterwards is ordered after it.
+  void *up = fz_upload_stream();
+  auto buf = std::make_shared<DeviceBuffer>(n, up);
+  if (n) {
+    fz_check(fz_memcpy_h2d(buf->ptr, data, n * sizeof(float), up), "fz_memcpy_h2d");
+    fz_check(fz_stream_sync(up), "fz_stream_sync(upload)");
+    fz_check(fz_stream_wait(nullptr, up), "fz_stream_wait");
+  }
   storage_ = std::make_shared<Storage>(make_leaf(std::move(buf), shape_));
 }
 
@@ -531,7 +542,11 @@ void RawTensor::to_host(float *dst) const {
   size_t n = size();
   if (!n) return;
   float *p = data();
-  fz_check(fz_memcpy_d2h(dst, p, n * sizeof(float), nullptr), "fz_memcpy_d2h");
+  // read back on the upload stream once the compute stream has produced the value,
+  // so the copy does not wait for compute work submitted after it (the next step)
+  void *up = fz_upload_stream();
+  fz_check(fz_stream_wait(up, nullptr), "fz_stream_wait");
+  fz_check(fz_memcpy_d2h(dst, p, n * sizeof(float), up), "fz_memcpy_d2h");
 }
 
 std::vector<float> RawTensor::to_host() const {

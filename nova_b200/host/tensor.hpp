@@ -68,6 +68,7 @@ struct DeviceBuffer {
   int device = 0;
   std::shared_ptr<DeviceBuffer> tf32_lo;  // fz_tf32_lo(ptr), made by the first GEMM reading it
   explicit DeviceBuffer(size_t n);
+  DeviceBuffer(size_t n, void *stream);  // allocated for first use on `stream`
   ~DeviceBuffer();
   DeviceBuffer(const DeviceBuffer &) = delete;
   DeviceBuffer &operator=(const DeviceBuffer &) = delete;

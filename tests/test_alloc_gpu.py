@@ -105,3 +105,31 @@ def test_data_survives_reuse_in_stream_order(capi):
         z = capi.DeviceArray.from_numpy(np.zeros(n, np.float32))
         np.testing.assert_array_equal(y.numpy(), x)
         del y, z
+
+
+def test_block_freed_on_another_stream_returns_home_after_its_use(capi):
+    """A block allocated on the upload stream and freed on the compute stream goes back
+    to the upload stream's cache; reusing it there waits for the compute stream's use."""
+    import numpy as np
+
+    L = capi.lib()
+    L.fz_upload_stream.restype = C.c_void_p
+    up = C.c_void_p(L.fz_upload_stream())
+    n = 1 << 22
+    x = np.arange(n, dtype=np.float32)
+    p = C.c_void_p()
+    capi.check(L.fz_malloc(C.byref(p), n * 4, up))
+    capi.check(L.fz_memcpy_h2d(p, x.ctypes.data, n * 4, up))
+    capi.check(L.fz_stream_wait(None, up))
+    q = capi.DeviceArray((n,))
+    for _ in range(8):  # queue compute-stream reads of the block
+        capi.check(L.fz_memcpy_d2d(q.ptr, p, n * 4, None))
+    capi.check(L.fz_free(p, None))  # freed on the compute stream
+    p2 = C.c_void_p()
+    capi.check(L.fz_malloc(C.byref(p2), n * 4, up))
+    assert p2.value == p.value  # back in its home cache
+    z = np.zeros(n, np.float32)
+    capi.check(L.fz_memcpy_h2d(p2, z.ctypes.data, n * 4, up))  # must wait for the reads
+    capi.check(L.fz_stream_sync(up))
+    np.testing.assert_array_equal(q.numpy(), x)
+    capi.check(L.fz_free(p2, up))
