@@ -85,6 +85,11 @@ int fz_stream_destroy(void *stream);
  * `signaler` before it has finished (an event recorded on `signaler`, waited on by
  * `waiter`; NULL means the thread's stream). The host does not block. */
 int fz_stream_wait(void *waiter, void *signaler);
+/* An event marking the work submitted to `stream` so far (NULL: the thread's stream);
+ * fz_stream_wait_event makes `waiter` wait for it; fz_event_destroy releases it. */
+int fz_event_record(void **event, void *stream);
+int fz_stream_wait_event(void *waiter, void *event);
+int fz_event_destroy(void *event);
 int fz_device_sync(void);
 
 /* Stream-ordered device memory. fz_free(ptr, stream) marks the block free after the

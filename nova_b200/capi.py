@@ -85,6 +85,9 @@ def lib() -> C.CDLL:
         L.fz_stream_destroy.argtypes = [vp]
         L.fz_stream_wait.argtypes = [vp, vp]
         L.fz_upload_stream.restype = C.c_void_p
+        L.fz_event_record.argtypes = [C.POINTER(C.c_void_p), vp]
+        L.fz_stream_wait_event.argtypes = [vp, vp]
+        L.fz_event_destroy.argtypes = [vp]
         L.fz_ewise_binary.argtypes = [C.c_int, C.POINTER(EwisePlan), vp, vp, vp, vp]
         L.fz_ewise_binary_contig.argtypes = [C.c_int, i64, vp, vp, vp, vp]
         L.fz_ewise_unary.argtypes = [C.c_int, C.POINTER(EwisePlan), vp, vp, vp]

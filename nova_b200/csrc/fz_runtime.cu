@@ -197,6 +197,30 @@ int fz_stream_sync(void *stream) {
   return FZ_OK;
 }
 
+int fz_event_record(void **event, void *stream) {
+  FZ_REQUIRE(event, "fz_event_record: null pointer");
+  cudaEvent_t e = nullptr;
+  FZ_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+  cudaError_t rc = cudaEventRecord(e, resolve(stream));
+  if (rc != cudaSuccess) {
+    cudaEventDestroy(e);
+    return cuda_fail(rc, "fz_event_record", __FILE__, __LINE__);
+  }
+  *event = (void *)e;
+  return FZ_OK;
+}
+
+int fz_stream_wait_event(void *waiter, void *event) {
+  FZ_REQUIRE(event, "fz_stream_wait_event: null event");
+  FZ_CUDA(cudaStreamWaitEvent(resolve(waiter), (cudaEvent_t)event, 0));
+  return FZ_OK;
+}
+
+int fz_event_destroy(void *event) {
+  if (event) FZ_CUDA(cudaEventDestroy((cudaEvent_t)event));
+  return FZ_OK;
+}
+
 static thread_local cudaStream_t t_upload[kMaxDevices] = {};
 
 void *fz_upload_stream(void) {

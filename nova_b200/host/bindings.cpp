@@ -355,8 +355,12 @@ PYBIND11_MODULE(fusion, m) {
   m.def("split_cache_enabled", &split_cache_enabled);
   m.def("empty_cache", []() { fz_check(fz_pool_release(), "fz_pool_release"); },
         "Return this device's cached blocks to the driver (synchronises the device).");
-  m.def("flush", [](const T &t) { t.raw().data(); }, py::arg("tensor"),
-        "Lower a pending tensor to device memory now.");
+  m.def("flush", [](const T &t) {
+          t.raw().data();
+          t.raw().expr()->buf->mark_ready();
+        }, py::arg("tensor"),
+        "Lower a pending tensor to device memory now; a later to_numpy() then reads it back "
+        "as soon as it is ready, without waiting for work submitted after the flush.");
   m.def("stats", []() {
     py::dict d;
     d["kernel_launches"] = fz_launch_count();

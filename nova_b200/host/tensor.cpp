@@ -81,7 +81,14 @@ DeviceBuffer::DeviceBuffer(size_t n, void *stream) : numel(n) {
 }
 
 DeviceBuffer::~DeviceBuffer() {
+  if (ready) fz_event_destroy(ready);
   if (ptr) fz_free(ptr, nullptr);
+}
+
+void DeviceBuffer::mark_ready() {
+  if (ready) fz_event_destroy(ready);
+  ready = nullptr;
+  fz_check(fz_event_record(&ready, nullptr), "fz_event_record");
 }
 
 size_t Expr::numel() const {
@@ -542,10 +549,13 @@ void RawTensor::to_host(float *dst) const {
   size_t n = size();
   if (!n) return;
   float *p = data();
-  // read back on the upload stream once the compute stream has produced the value,
-  // so the copy does not wait for compute work submitted after it (the next step)
+  // read back on the upload stream once the compute stream has produced the value;
+  // for a value flushed earlier that point is its ready event, so the copy does not
+  // wait for compute work submitted since (the next step)
   void *up = fz_upload_stream();
-  fz_check(fz_stream_wait(up, nullptr), "fz_stream_wait");
+  const DeviceBuffer *b = expr()->buf.get();
+  if (b && b->ready) fz_check(fz_stream_wait_event(up, b->ready), "fz_stream_wait_event");
+  else fz_check(fz_stream_wait(up, nullptr), "fz_stream_wait");
   fz_check(fz_memcpy_d2h(dst, p, n * sizeof(float), up), "fz_memcpy_d2h");
 }
 

@@ -67,6 +67,8 @@ struct DeviceBuffer {
   size_t numel = 0;
   int device = 0;
   std::shared_ptr<DeviceBuffer> tf32_lo;  // fz_tf32_lo(ptr), made by the first GEMM reading it
+  void *ready = nullptr;  // event after the producing work, recorded by flush() for read-backs
+  void mark_ready();      // (re)record `ready` at the current point of the thread's stream
   explicit DeviceBuffer(size_t n);
   DeviceBuffer(size_t n, void *stream);  // allocated for first use on `stream`
   ~DeviceBuffer();
