@@ -227,3 +227,24 @@ def test_reduction_chains_join_adjacent_axes(fake_fusion, op):
     # a pending reduction feeding an elementwise op is lowered first
     v = (getattr(x, op)(3, True) + 1.0).to_numpy()
     np.testing.assert_allclose(v, f(a.astype(np.float64), axis=3, keepdims=True) + 1, rtol=1e-5, atol=1e-5)
+
+
+def test_reduction_chain_edge_cases(fake_fusion):
+    """Joined reductions stop where they must: a global reduction after an axis
+    reduction, mixed keepdim, different ops, and a chain read twice."""
+    F = fake_fusion
+    rng = np.random.default_rng(12)
+    a = rng.standard_normal((3, 4, 5)).astype(np.float32)
+    x = api_cases.T(F, a)
+    d = a.astype(np.float64)
+    np.testing.assert_allclose(x.sum(2).sum().to_numpy(), [d.sum()], rtol=1e-5)
+    np.testing.assert_allclose(x.sum(2, True).sum(1).to_numpy(), d.sum(axis=2, keepdims=True).sum(axis=1),
+                               rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(x.mean(2, True).sum(1, True).to_numpy(),
+                               d.mean(axis=2, keepdims=True).sum(axis=1, keepdims=True), rtol=1e-5, atol=1e-6)
+    y = x.sum(1, True)
+    z1 = y.sum(2, True).to_numpy()  # joined with y's pending reduction
+    z2 = y.to_numpy()               # y itself is still its own value
+    np.testing.assert_allclose(z1, d.sum(axis=(1, 2), keepdims=True), rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(z2, d.sum(axis=1, keepdims=True), rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(x.sum(0).sum(0).sum(0).to_numpy(), [d.sum()], rtol=1e-5)
