@@ -356,18 +356,32 @@ int fz_malloc(void **ptr, size_t bytes, void *stream) {
     if (it != g_free.end()) {
       auto jt = it->second.by_size.find(sz);
       if (jt != it->second.by_size.end() && !jt->second.empty()) {
-        const CachedBlock c = jt->second.back();
-        jt->second.pop_back();
-        if (c.ready) {  // last used on another stream: wait for that use to finish
-          cudaError_t e = cudaStreamWaitEvent(s, c.ready, 0);
-          cudaEventDestroy(c.ready);
-          if (e != cudaSuccess) return cuda_fail(e, "cudaStreamWaitEvent(cached block)", __FILE__, __LINE__);
+        // A block freed on its home stream is reusable at once; one freed on another
+        // stream only when that stream has passed the free. Waiting for a free point that
+        // lies ahead (the upload of step i+2 taking the buffer step i+1 is still reading)
+        // would serialise the streams, so such blocks are skipped and, if none is ready,
+        // new memory is taken: a rotation of buffers forms instead.
+        auto &v = jt->second;
+        for (size_t k = v.size(); k-- > 0;) {
+          const CachedBlock c = v[k];
+          if (c.ready) {
+            const cudaError_t q = cudaEventQuery(c.ready);
+            if (q == cudaErrorNotReady) {
+              // make sure the answer is not left as the thread's last error, where the
+              // next launch check would read it
+              if (cudaPeekAtLastError() == cudaErrorNotReady) cudaGetLastError();
+              continue;
+            }
+            if (q != cudaSuccess) return cuda_fail(q, "cudaEventQuery(cached block)", __FILE__, __LINE__);
+          }
+          v.erase(v.begin() + (long)k);
+          if (c.ready) cudaEventDestroy(c.ready);
+          g_cached_bytes[d] -= sz;
+          g_live.emplace(c.ptr, LiveBlock{sz, d, s});
+          g_live_bytes[d] += sz;
+          *ptr = c.ptr;
+          return FZ_OK;
         }
-        g_cached_bytes[d] -= sz;
-        g_live.emplace(c.ptr, LiveBlock{sz, d, s});
-        g_live_bytes[d] += sz;
-        *ptr = c.ptr;
-        return FZ_OK;
       }
     }
   }

@@ -109,7 +109,9 @@ def test_data_survives_reuse_in_stream_order(capi):
 
 def test_block_freed_on_another_stream_returns_home_after_its_use(capi):
     """A block allocated on the upload stream and freed on the compute stream goes back
-    to the upload stream's cache; reusing it there waits for the compute stream's use."""
+    to the upload stream's cache. It is handed out there again only once the compute
+    stream has passed the free; before that a request takes other memory, so a write on
+    the upload stream never lands under the queued reads."""
     import numpy as np
 
     L = capi.lib()
@@ -127,9 +129,15 @@ def test_block_freed_on_another_stream_returns_home_after_its_use(capi):
     capi.check(L.fz_free(p, None))  # freed on the compute stream
     p2 = C.c_void_p()
     capi.check(L.fz_malloc(C.byref(p2), n * 4, up))
-    assert p2.value == p.value  # back in its home cache
     z = np.zeros(n, np.float32)
-    capi.check(L.fz_memcpy_h2d(p2, z.ctypes.data, n * 4, up))  # must wait for the reads
+    capi.check(L.fz_memcpy_h2d(p2, z.ctypes.data, n * 4, up))
     capi.check(L.fz_stream_sync(up))
-    np.testing.assert_array_equal(q.numpy(), x)
+    np.testing.assert_array_equal(q.numpy(), x)  # the queued reads saw the old contents
     capi.check(L.fz_free(p2, up))
+    capi.check(L.fz_stream_sync(None))  # the compute stream is past the free now
+    p3, p4 = C.c_void_p(), C.c_void_p()
+    capi.check(L.fz_malloc(C.byref(p3), n * 4, up))
+    capi.check(L.fz_malloc(C.byref(p4), n * 4, up))
+    assert p.value in (p3.value, p4.value)  # back in its home cache
+    capi.check(L.fz_free(p3, up))
+    capi.check(L.fz_free(p4, up))
