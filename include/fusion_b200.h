@@ -268,6 +268,41 @@ int fz_gemm_f32_split(int64_t batch, int64_t M, int64_t N, int64_t K,
                       const float *A, const float *A_lo, int64_t lda, int64_t strideA, int transA,
                       const float *B, const float *B_lo, int64_t ldb, int64_t strideB, int transB,
                       float *C, int64_t ldc, int64_t strideC, void *stream);
+/* One input of a GEMM epilogue program (program leaf k >= 1 reads inputs[k-1];
+ * leaf 0 is the product). At output element (b, i, j) it reads
+ * ptr[b * batch_stride + i * row_stride + j * col_stride], col_stride 0 or 1: a
+ * bias row bias[j] has batch_stride = row_stride = 0 and col_stride = 1, a
+ * same-shape tensor row_stride = its row pitch, a per-row value col_stride = 0. */
+typedef struct fz_epi_input {
+  const float *ptr;
+  int64_t batch_stride, row_stride, col_stride;
+} fz_epi_input;
+
+/* GEMM with a fused elementwise epilogue. With P[b] = op(A[b]) @ op(B[b]) computed
+ * as by fz_gemm_f32_split, the program `epi` (declared below) is evaluated at every
+ * output element (b, i, j) with leaf 0 = P[b][i][j] and leaf k = inputs[k-1] at
+ * (b, i, j); output k is stored at outputs[k][b * strideC + i * ldc + j]. The results
+ * equal, bit for bit, fz_gemm_f32_split into a buffer followed by fz_fused_launch of
+ * `epi` over it; P itself is stored only if the program outputs it (an FZ_COPY node
+ * of leaf 0). The program is compiled into the epilogue of the GEMM kernel (NVRTC,
+ * cached per program structure, input classes and kernel variant), so P never goes
+ * through HBM; when the GEMM splits K (few output tiles) or K = 0, P is formed in a
+ * workspace and the program runs as one fused pass over it. At most FZ_MAX_LEAVES - 1
+ * inputs and FZ_MAX_OUTPUTS outputs. No reference counterpart: the reference runs
+ * the product and each following op as separate passes
+ * (fusion/src/Fusion/core/TensorIter.hpp:96-249, 299-323). */
+struct fz_program;
+int fz_gemm_f32_epilogue(int64_t batch, int64_t M, int64_t N, int64_t K,
+                         const float *A, const float *A_lo, int64_t lda, int64_t strideA, int transA,
+                         const float *B, const float *B_lo, int64_t ldb, int64_t strideB, int transB,
+                         const struct fz_program *epi, const fz_epi_input *inputs,
+                         float *const *outputs, int64_t ldc, int64_t strideC, void *stream);
+/* Compile (NVRTC only: no device is needed, nothing is loaded or cached) the GEMM
+ * kernel variant with `epi` as its epilogue: A / B MN-major (a_mn, b_mn), output
+ * tile width tile_n (16, 64 or 256; narrow tiles take a K-major B), CTA pair (tile_n
+ * 256). Returns FZ_ERR_JIT with the compiler log in fz_last_error on failure. */
+int fz_gemm_epilogue_compile(const struct fz_program *epi, const fz_epi_input *inputs,
+                             int a_mn, int b_mn, int tile_n, int pair);
 /* lo[i] = x[i] - tf32_hi(x[i]) for i < n, tf32_hi clearing the 13 low mantissa bits
  * (the plane fz_gemm_f32_split takes). */
 int fz_tf32_lo(float *lo, const float *x, int64_t n, void *stream);

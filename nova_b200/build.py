@@ -67,9 +67,24 @@ def _run(cmd, verbose):
         sys.stderr.write(r.stderr)
 
 
+def _embed_kernel_source() -> pathlib.Path:
+    """Write the GEMM kernels' device source as a C++ string literal, the text the
+    library hands NVRTC when it compiles a GEMM with a fused epilogue (rewritten only
+    when the header changed)."""
+    src = (CSRC / "fz_gemm_kernels.cuh").read_text()
+    delim = "FZSRC"
+    assert ")" + delim + '"' not in src
+    out = OBJ / "fz_gemm_kernels.inc"
+    text = 'R"' + delim + "(" + src + ")" + delim + '"\n'
+    if not out.exists() or out.read_text() != text:
+        out.write_text(text)
+    return out
+
+
 def build_lib(verbose: bool = False, jobs: int = 8) -> pathlib.Path:
     OBJ.mkdir(exist_ok=True)
-    headers = list(CSRC.glob("*.cuh")) + list(CSRC.glob("*.hpp")) + [INCLUDE / "fusion_b200.h"]
+    inc = _embed_kernel_source()
+    headers = list(CSRC.glob("*.cuh")) + list(CSRC.glob("*.hpp")) + [INCLUDE / "fusion_b200.h", inc]
     srcs = sorted(CSRC.glob("*.cu"))
     nccl_inc, nccl_lib = _nccl_dirs()
     jobs_list = []
@@ -78,7 +93,8 @@ def build_lib(verbose: bool = False, jobs: int = 8) -> pathlib.Path:
         obj = OBJ / (src.stem + ".o")
         objs.append(obj)
         if _stale(obj, [src, *headers]):
-            jobs_list.append([NVCC, *NVCC_FLAGS, "-I" + str(nccl_inc), "-c", str(src), "-o", str(obj)])
+            jobs_list.append([NVCC, *NVCC_FLAGS, "-I" + str(OBJ), "-I" + str(nccl_inc), "-c", str(src),
+                              "-o", str(obj)])
     with ThreadPoolExecutor(max_workers=jobs) as ex:
         list(ex.map(lambda c: _run(c, verbose), jobs_list))
     if jobs_list or _stale(LIB, objs):

@@ -53,6 +53,12 @@ class Program(C.Structure):
                 ("nodes", Node * FZ_MAX_NODES)]
 
 
+class EpiInput(C.Structure):
+    """fz_epi_input: one input of a GEMM epilogue program (leaf k >= 1)."""
+    _fields_ = [("ptr", C.c_void_p), ("batch_stride", C.c_int64), ("row_stride", C.c_int64),
+                ("col_stride", C.c_int64)]
+
+
 def header_symbols() -> list[str]:
     """Function names declared in include/fusion_b200.h."""
     text = HEADER.read_text()
@@ -102,6 +108,11 @@ def lib() -> C.CDLL:
                                         i64, i64, C.c_int, vp, i64, i64, vp]
         L.fz_tf32_lo.argtypes = [vp, vp, i64, vp]
         L.fz_gemm_set_tiles.argtypes = [C.c_int]
+        L.fz_gemm_f32_epilogue.argtypes = [i64, i64, i64, i64, vp, vp, i64, i64, C.c_int, vp, vp,
+                                           i64, i64, C.c_int, C.POINTER(Program),
+                                           C.POINTER(EpiInput), C.POINTER(C.c_void_p), i64, i64, vp]
+        L.fz_gemm_epilogue_compile.argtypes = [C.POINTER(Program), C.POINTER(EpiInput), C.c_int,
+                                               C.c_int, C.c_int, C.c_int]
         L.fz_timer_create.argtypes = [C.POINTER(C.c_void_p)]
         L.fz_timer_start.argtypes = [vp, vp]
         L.fz_timer_stop.argtypes = [vp, vp]

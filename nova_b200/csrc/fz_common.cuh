@@ -7,6 +7,7 @@
 #include <cstdint>
 #include <cstdio>
 #include <string>
+#include <vector>
 
 #include "fusion_b200.h"
 
@@ -26,6 +27,14 @@ cudaStream_t resolve(void *stream);
 // nonzero code when a wait expires; read and cleared by fz_kernel_status.
 int device_error_word(int **word);
 int num_sms();
+
+// Fused-program support shared by the elementwise and GEMM-epilogue compilers
+// (fz_fused.cu): validation, the CUDA C of a program's scalar evaluator fz_eval, and
+// NVRTC compilation for sm_100a (name_expr, when given, is lowered into *lowered).
+int validate_program(const fz_program &pg);
+std::string program_eval_source(const fz_program &pg);
+int nvrtc_cubin(const std::string &src, const char *name, const char *name_expr,
+                std::vector<char> *cubin, std::string *lowered);
 
 // Grid size for a streaming kernel: enough CTAs to cover `work_items` at
 // `per_cta` items each, capped at `waves` full waves of resident CTAs (148 SMs).

@@ -173,11 +173,10 @@ void generate_tiles(std::ostringstream &o, const fz_program &pg, const int *cls,
   o << "        }\n      }\n    }\n  }\n}\n";
 }
 
-std::string generate(const fz_program &pg, const int *cls, int vec, bool i64, int tiles_u) {
-  std::ostringstream o;
+// The prelude and the scalar evaluator fz_eval(l0.., &o0..) of a program.
+void generate_eval(std::ostringstream &o, const fz_program &pg) {
   o << kPrelude;
-  const int nout = pg.num_outputs, nleaf = pg.num_leaves, nops = nout + nleaf;
-  // scalar evaluator of the program
+  const int nout = pg.num_outputs, nleaf = pg.num_leaves;
   o << "__device__ __forceinline__ void fz_eval(";
   for (int k = 0; k < nleaf; ++k) o << "float l" << k << ", ";
   for (int k = 0; k < nout; ++k) o << "float &o" << k << (k + 1 < nout ? ", " : "");
@@ -196,6 +195,12 @@ std::string generate(const fz_program &pg, const int *cls, int vec, bool i64, in
   }
   for (int k = 0; k < nout; ++k) o << "  o" << k << " = t" << pg.out_node[k] << ";\n";
   o << "}\n";
+}
+
+std::string generate(const fz_program &pg, const int *cls, int vec, bool i64, int tiles_u) {
+  std::ostringstream o;
+  generate_eval(o, pg);
+  const int nout = pg.num_outputs, nleaf = pg.num_leaves, nops = nout + nleaf;
   if (tiles_u) {
     generate_tiles(o, pg, cls, tiles_u);
     return o.str();
@@ -272,24 +277,9 @@ Cache &cache() {
 }
 
 int compile(const std::string &src, cudaKernel_t *out) {
-  nvrtcProgram prog;
-  nvrtcResult r = nvrtcCreateProgram(&prog, src.c_str(), "fz_fused.cu", 0, nullptr, nullptr);
-  if (r != NVRTC_SUCCESS) return fz::fail(FZ_ERR_JIT, std::string("nvrtcCreateProgram: ") + nvrtcGetErrorString(r));
-  const char *opts[] = {"--gpu-architecture=sm_100a", "--fmad=false", "--std=c++17", "-lineinfo"};
-  r = nvrtcCompileProgram(prog, 4, opts);
-  if (r != NVRTC_SUCCESS) {
-    size_t n = 0;
-    nvrtcGetProgramLogSize(prog, &n);
-    std::string log(n, '\0');
-    nvrtcGetProgramLog(prog, log.data());
-    nvrtcDestroyProgram(&prog);
-    return fz::fail(FZ_ERR_JIT, "NVRTC compilation of a fused program failed: " + log);
-  }
-  size_t nbin = 0;
-  nvrtcGetCUBINSize(prog, &nbin);
-  std::vector<char> bin(nbin);
-  nvrtcGetCUBIN(prog, bin.data());
-  nvrtcDestroyProgram(&prog);
+  std::vector<char> bin;
+  int rc = fz::nvrtc_cubin(src, "fz_fused.cu", nullptr, &bin, nullptr);
+  if (rc) return rc;
   cudaLibrary_t lib;
   cudaError_t e = cudaLibraryLoadData(&lib, bin.data(), nullptr, nullptr, 0, nullptr, nullptr, 0);
   if (e != cudaSuccess) return fz::cuda_fail(e, "cudaLibraryLoadData(fused)", __FILE__, __LINE__);
@@ -299,6 +289,47 @@ int compile(const std::string &src, cudaKernel_t *out) {
 }
 
 }  // namespace
+
+namespace fz {
+
+int validate_program(const fz_program &pg) { return validate(pg); }
+
+std::string program_eval_source(const fz_program &pg) {
+  std::ostringstream o;
+  generate_eval(o, pg);
+  return o.str();
+}
+
+int nvrtc_cubin(const std::string &src, const char *name, const char *name_expr,
+                std::vector<char> *cubin, std::string *lowered) {
+  nvrtcProgram prog;
+  nvrtcResult r = nvrtcCreateProgram(&prog, src.c_str(), name, 0, nullptr, nullptr);
+  if (r != NVRTC_SUCCESS) return fail(FZ_ERR_JIT, std::string("nvrtcCreateProgram: ") + nvrtcGetErrorString(r));
+  if (name_expr) nvrtcAddNameExpression(prog, name_expr);
+  const char *opts[] = {"--gpu-architecture=sm_100a", "--fmad=false", "--std=c++17", "-lineinfo"};
+  r = nvrtcCompileProgram(prog, 4, opts);
+  if (r != NVRTC_SUCCESS) {
+    size_t n = 0;
+    nvrtcGetProgramLogSize(prog, &n);
+    std::string log(n, '\0');
+    nvrtcGetProgramLog(prog, log.data());
+    nvrtcDestroyProgram(&prog);
+    return fail(FZ_ERR_JIT, std::string("NVRTC compilation of ") + name + " failed: " + log);
+  }
+  if (name_expr && lowered) {
+    const char *ln = nullptr;
+    nvrtcGetLoweredName(prog, name_expr, &ln);
+    *lowered = ln ? ln : "";
+  }
+  size_t nbin = 0;
+  nvrtcGetCUBINSize(prog, &nbin);
+  cubin->resize(nbin);
+  nvrtcGetCUBIN(prog, cubin->data());
+  nvrtcDestroyProgram(&prog);
+  return FZ_OK;
+}
+
+}  // namespace fz
 
 extern "C" {
 

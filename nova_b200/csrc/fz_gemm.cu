@@ -36,36 +36,21 @@
 #include <cudaTypedefs.h>
 
 #include <atomic>
+#include <cstddef>
+#include <cstring>
 #include <mutex>
+#include <sstream>
+#include <string>
+#include <unordered_map>
+#include <vector>
 
 #include "fz_common.cuh"
 
+#include "fz_gemm_kernels.cuh"
+
 namespace {
 
-constexpr int BM = 128;
-constexpr int BN = 256;
-// k-tile: BK fp32 = one swizzle row (BK = 16 -> 64-byte swizzle, 4 stages of 48 KB;
-// BK = 32 -> 128-byte swizzle, 2 stages of 96 KB)
-#ifndef FZ_GEMM_BK
-#define FZ_GEMM_BK 16
-#endif
-constexpr int BK = FZ_GEMM_BK;
-constexpr int STAGES = BK == 16 ? 4 : 2;
-constexpr int SWIZZLE_BYTES = BK * 4;
-static_assert(BK == 16 || BK == 32, "BK must be 16 or 32");
-constexpr int UMMA_K = 8;  // K of one kind::tf32 MMA
-constexpr int MN_CHUNK = 32;              // MN-major tiles: M/N rows per 128-byte swizzle row
-constexpr int MN_CHUNK_BYTES = BK * 128;  // one such chunk of a stage tile (BK k-rows)
-constexpr int TILE_A_BYTES = BM * BK * 4;  // 16 KB
-constexpr int TILE_B_BYTES = BN * BK * 4;  // 32 KB
-constexpr int STAGE_BYTES = 2 * TILE_A_BYTES + 2 * TILE_B_BYTES;  // 96 KB
-constexpr int TMEM_COLS = 256;          // one accumulator buffer (BN fp32 columns)
-constexpr int KCHUNK = 16;              // k-tiles per promotion chunk (K = 256)
-constexpr int NUM_EPI_WARPS = 8;        // 2 per TMEM lane quarter
-constexpr int NUM_THREADS = 64 + 32 * NUM_EPI_WARPS;
-constexpr unsigned long long kWaitNs = 4000000000ull;  // 4 s per wait
-
-enum : int { kErrNone = 0, kErrTimeoutFull = 1, kErrTimeoutEmpty = 2, kErrTimeoutAcc = 3 };
+using namespace fz_gemm_dev;
 
 // ---------------------------------------------------------------- split pass
 __device__ __forceinline__ void split1(float x, float &hi, float &lo) {
@@ -114,764 +99,6 @@ __global__ void __launch_bounds__(256) lo_kernel(const float *__restrict__ src, 
   }
 }
 
-// ---------------------------------------------------------------- PTX helpers
-__device__ __forceinline__ uint32_t smem_u32(const void *p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ uint64_t globaltimer() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
-               "r"(bytes)
-               : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.b32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-// Bounded wait: true on success, false when the deadline passed or another role
-// already reported an error.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = globaltimer();
-  while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if (*abort_flag) return false;
-    if (globaltimer() - t0 > kWaitNs) return false;
-  }
-}
-
-__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, uint64_t *bar,
-                                            int c0, int c1, int c2) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
-      : "memory");
-}
-
-__device__ __forceinline__ void prefetch_map(const CUtensorMap *map) {
-  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
-}
-
-__device__ __forceinline__ void tma_load_4d(void *dst, const CUtensorMap *map, uint64_t *bar,
-                                            int c0, int c1, int c2, int c3) {
-  asm volatile(
-      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
-      : "memory");
-}
-
-// One operand's k-tile [row0, row0 + ROWS) x [k0, k0 + BK) into a stage tile.
-// K-major: one box {BK, ROWS}. MN-major: the tile is ROWS / 32 chunks of
-// MN_CHUNK_BYTES; a "wide" map (4D: 32 rows, K, chunk, batch) fetches all chunks in
-// one box, a narrow one (3D) one chunk per box. Rows past the operand's extent are
-// zero-filled by the TMA unit.
-template <bool MN, int ROWS>
-__device__ __forceinline__ void load_operand(uint8_t *dst, const CUtensorMap *map, uint64_t *bar,
-                                             int k0, int row0, int bz, bool wide) {
-  if constexpr (MN) {
-    if (wide) {
-      tma_load_4d(dst, map, bar, 0, k0, row0 / MN_CHUNK, bz);
-    } else {
-#pragma unroll
-      for (int j = 0; j < ROWS / MN_CHUNK; ++j)
-        tma_load_3d(dst + j * MN_CHUNK_BYTES, map, bar, row0 + j * MN_CHUNK, k0, bz);
-    }
-  } else {
-    tma_load_3d(dst, map, bar, k0, row0, bz);
-  }
-}
-
-// K-major shared-memory descriptor for rows of SWIZZLE_BYTES (one swizzle atom
-// row per tile row): 8-row groups 8*SWIZZLE_BYTES apart (SBO), LBO unused (1),
-// descriptor version 1 (bit 46), layout type at bits 61-63: 2 = SWIZZLE_128B,
-// 4 = SWIZZLE_64B.
-__device__ __forceinline__ uint64_t smem_desc_k(uint32_t addr) {
-  uint64_t d = 0;
-  d |= (uint64_t)((addr >> 4) & 0x3fff);
-  d |= (uint64_t)1 << 16;
-  d |= (uint64_t)((8 * SWIZZLE_BYTES) >> 4) << 32;
-  d |= (uint64_t)1 << 46;
-  d |= (uint64_t)(SWIZZLE_BYTES == 128 ? 2 : 4) << 61;
-  return d;
-}
-
-// MN-major shared-memory descriptor. For 32-bit (TF32) operands the MN-major layout
-// is the 128-byte swizzle with 32-byte atomicity (layout type 1): 32-byte units of a
-// 128-byte row are permuted by the row index mod 4, in atoms of 4 k-rows x 128 bytes
-// (512 B). The tile is stored as chunks of 32 M/N rows, each BK k-rows of 128 bytes;
-// LBO = distance between the 32-wide M/N chunks (BK * 128 bytes), SBO = distance
-// between 4-row k atoms (512 bytes). The TMA writes this image with
-// CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B.
-__device__ __forceinline__ uint64_t smem_desc_mn(uint32_t addr) {
-  uint64_t d = 0;
-  d |= (uint64_t)((addr >> 4) & 0x3fff);
-  d |= (uint64_t)(MN_CHUNK_BYTES >> 4) << 16;
-  d |= (uint64_t)(512 >> 4) << 32;
-  d |= (uint64_t)1 << 46;
-  d |= (uint64_t)1 << 61;
-  return d;
-}
-
-// Descriptor of k-step kk (UMMA_K wide) of a stage tile at `base`.
-template <bool MN>
-__device__ __forceinline__ uint64_t operand_desc(uint32_t base, int kk) {
-  if constexpr (MN) return smem_desc_mn(base + (uint32_t)kk * (UMMA_K * 128));  // 8 k-rows
-  else return smem_desc_k(base + (uint32_t)kk * (UMMA_K * 4));                  // 32 bytes
-}
-
-// kind::tf32 instruction descriptor: D = F32 (bits 4-5 = 1), A = B = TF32 (2),
-// A major at bit 15 and B major at bit 16 (0 = K-major, 1 = MN-major), N >> 3 at
-// bits 17-22, M >> 4 at bits 24-28.
-__host__ __device__ constexpr uint32_t make_idesc(int m, int n, bool a_mn, bool b_mn) {
-  return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)a_mn << 15) | ((uint32_t)b_mn << 16) |
-         ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
-}
-
-__device__ __forceinline__ void umma_tf32(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc,
-                                          uint32_t accum) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-      "l"(a), "l"(b), "r"(idesc), "r"(accum)
-      : "memory");
-}
-
-__device__ __forceinline__ void umma_commit(uint64_t *bar) {
-  asm volatile(
-      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-          smem_u32(bar))
-      : "memory");
-}
-
-__device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
-        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
-        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
-
-struct GemmArgs {
-  float *C;
-  int64_t ldc, strideC;
-  int64_t split_stride;  // floats between the partial outputs of consecutive K splits
-  int M, N, K, batch;
-  int tiles_m, tiles_n, num_tiles, group_m;  // num_tiles counts work units (tiles x K splits)
-  int splits, k_per_split;  // K is cut into `splits` ranges of k_per_split (multiple of BK)
-  int wide;                 // bits 0-3: map Ah, Al, Bh, Bl is a wide (4D) MN-major map
-  int *err;
-};
-
-__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-
-// Work unit t -> (K split, batch, m block, n block). Units of one K split are
-// consecutive; within a batch, bands of group_m row blocks are walked column by
-// column, so the units in flight on the 148 SMs share A rows and B columns in L2.
-__device__ __forceinline__ void decode_tile(int t, const GemmArgs &a, int &mb, int &nb, int &bz,
-                                            int &ks) {
-  const int per_batch = a.tiles_m * a.tiles_n;
-  const int per_split = per_batch * a.batch;  // units of one K split
-  ks = t / per_split;
-  t -= ks * per_split;
-  bz = t / per_batch;
-  const int r = t - bz * per_batch;
-  const int band = r / (a.group_m * a.tiles_n);
-  const int first_m = band * a.group_m;
-  const int rows = min(a.group_m, a.tiles_m - first_m);
-  const int in_band = r - band * a.group_m * a.tiles_n;
-  mb = first_m + in_band % rows;
-  nb = in_band / rows;
-}
-
-// k-tiles of unit `ks`: [ks * k_per_split, min(K, (ks + 1) * k_per_split)).
-__device__ __forceinline__ int unit_k_tiles(const GemmArgs &a, int ks, int &k_begin) {
-  k_begin = ks * a.k_per_split;
-  const int k_end = min(a.K, k_begin + a.k_per_split);
-  return (k_end - k_begin + BK - 1) / BK;
-}
-
-// Persistent kernel: one CTA per SM walks tiles blockIdx.x, +gridDim.x, ...
-// K is cut into chunks of KCHUNK k-tiles accumulated alternately in two TMEM
-// buffers; warps 2-9 fold each finished chunk into fp32 registers.
-// Per tile width TBN (output columns per tile): 256 for wide products, 64 or 16 for
-// narrow ones (a 16-wide output layer would otherwise compute 256 columns for 16).
-// Narrow tiles use more stages of smaller k-tiles, within the same ~192 KB.
-template <int TBN>
-struct TileCfg {
-  static constexpr int B_BYTES = TBN * BK * 4;
-  static constexpr int STAGE = 2 * TILE_A_BYTES + 2 * B_BYTES;
-  static constexpr int NSTAGE = TBN == BN ? STAGES : (192 * 1024) / STAGE;
-  static constexpr int TMEM = TBN < 32 ? 32 : TBN;  // TMEM columns per accumulator buffer
-  static constexpr int CPW = TBN / 2;               // columns per epilogue warp
-  static_assert(TBN == 256 || TBN == 64 || TBN == 16, "tile width");
-};
-
-// Add CPW accumulator columns of this warp's TMEM lanes, from `taddr`, into acc.
-template <int CPW>
-__device__ __forceinline__ void promote_cols(uint32_t taddr, float (&acc)[CPW]) {
-  if constexpr (CPW >= 32) {
-#pragma unroll
-    for (int c0 = 0; c0 < CPW; c0 += 32) {
-      uint32_t r[32];
-      tmem_ld_32x32b_x32(taddr + (uint32_t)c0, r);
-#pragma unroll
-      for (int i = 0; i < 32; ++i) acc[c0 + i] = __fadd_rn(acc[c0 + i], __uint_as_float(r[i]));
-    }
-  } else {
-    static_assert(CPW == 8, "columns per warp");
-    uint32_t r[8];
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-          "=r"(r[7])
-        : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-    for (int i = 0; i < 8; ++i) acc[i] = __fadd_rn(acc[i], __uint_as_float(r[i]));
-  }
-}
-
-// A_MN / B_MN: the operand is MN-major in global and shared memory (B is K-major
-// whenever TBN < 256).
-template <bool A_MN, bool B_MN, int TBN>
-__global__ void __launch_bounds__(NUM_THREADS, 1)
-    gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap mapAh,
-                       const __grid_constant__ CUtensorMap mapAl,
-                       const __grid_constant__ CUtensorMap mapBh,
-                       const __grid_constant__ CUtensorMap mapBl, GemmArgs args) {
-  extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t *smem = reinterpret_cast<uint8_t *>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-  using T = TileCfg<TBN>;
-  constexpr int STAGES = T::NSTAGE;
-  constexpr int STAGE_BYTES = T::STAGE;
-  constexpr int TILE_B_BYTES = T::B_BYTES;
-  constexpr int TMEM_COLS = T::TMEM;
-  constexpr int CPW = T::CPW;
-  static_assert(TBN == BN || !B_MN, "narrow tiles read B K-major");
-  __shared__ __align__(8) uint64_t full_bar[STAGES];
-  __shared__ __align__(8) uint64_t empty_bar[STAGES];
-  __shared__ __align__(8) uint64_t acc_full[2];
-  __shared__ __align__(8) uint64_t acc_empty[2];
-  __shared__ uint32_t tmem_base_slot;
-  __shared__ volatile int abort_flag;
-
-  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  constexpr uint32_t kIdesc = make_idesc(BM, TBN, A_MN, B_MN);
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&full_bar[s], 1);
-      mbar_init(&empty_bar[s], 1);
-    }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 32 * NUM_EPI_WARPS);  // every epilogue thread arrives
-    }
-    abort_flag = 0;
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    prefetch_map(&mapAh);
-    prefetch_map(&mapAl);
-    prefetch_map(&mapBh);
-    prefetch_map(&mapBl);
-  }
-  if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                     smem_u32(&tmem_base_slot)),
-                 "r"(2 * TMEM_COLS)
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-  }
-  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-  __syncthreads();
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-  const uint32_t tmem_base = tmem_base_slot;
-
-  auto stage_ptr = [&](int s, int which) -> uint8_t * {
-    uint8_t *base = smem + (size_t)s * STAGE_BYTES;
-    switch (which) {
-      case 0: return base;
-      case 1: return base + TILE_A_BYTES;
-      case 2: return base + 2 * TILE_A_BYTES;
-      default: return base + 2 * TILE_A_BYTES + TILE_B_BYTES;
-    }
-  };
-
-  if (warp == 0) {
-    if (lane == 0) {
-      // ------------------------------------------------------ TMA producer
-      int it = 0;
-      bool ok = true;
-      for (int t = blockIdx.x; ok && t < args.num_tiles; t += gridDim.x) {
-        int mb, nb, bz, ks, kb;
-        decode_tile(t, args, mb, nb, bz, ks);
-        const int nk = unit_k_tiles(args, ks, kb);
-        for (int kt = 0; kt < nk; ++kt, ++it) {
-          const int s = it % STAGES;
-          const uint32_t round = it / STAGES;
-          if (it >= STAGES && !mbar_wait(&empty_bar[s], (round - 1) & 1, &abort_flag)) {
-            ok = false;
-            break;
-          }
-          mbar_expect_tx(&full_bar[s], STAGE_BYTES);
-          const int k0 = kb + kt * BK;
-          load_operand<A_MN, BM>(stage_ptr(s, 0), &mapAh, &full_bar[s], k0, mb * BM, bz, args.wide & 1);
-          load_operand<A_MN, BM>(stage_ptr(s, 1), &mapAl, &full_bar[s], k0, mb * BM, bz, args.wide & 2);
-          load_operand<B_MN, TBN>(stage_ptr(s, 2), &mapBh, &full_bar[s], k0, nb * TBN, bz, args.wide & 4);
-          load_operand<B_MN, TBN>(stage_ptr(s, 3), &mapBl, &full_bar[s], k0, nb * TBN, bz, args.wide & 8);
-        }
-      }
-      if (!ok) {
-        atomicCAS(args.err, kErrNone, kErrTimeoutEmpty);
-        abort_flag = 1;
-        // drain: wait (bounded) for the loads of the last STAGES issued k-tiles
-        for (int i = (it > STAGES ? it - STAGES : 0); i < it; ++i) {
-          const int s = i % STAGES;
-          const uint64_t t0 = globaltimer();
-          while (!mbar_try_wait(&full_bar[s], (i / STAGES) & 1) && globaltimer() - t0 < kWaitNs) {
-          }
-        }
-      }
-    }
-  } else if (warp == 1) {
-    if (lane == 0) {
-      // ------------------------------------------------------ MMA issuer
-      int it = 0, cc = 0;  // k-tile and chunk counters, running across tiles
-      bool ok = true;
-      for (int t = blockIdx.x; ok && t < args.num_tiles; t += gridDim.x) {
-        int mb, nb, bz, ks, kb;
-        decode_tile(t, args, mb, nb, bz, ks);
-        const int num_k = unit_k_tiles(args, ks, kb);
-        for (int kt0 = 0; ok && kt0 < num_k; kt0 += KCHUNK, ++cc) {
-          const int b = cc & 1;
-          if (cc >= 2 && !mbar_wait(&acc_empty[b], ((cc >> 1) - 1) & 1, &abort_flag)) {
-            ok = false;
-            break;
-          }
-          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-          const uint32_t d_tmem = tmem_base + (uint32_t)(b * TMEM_COLS);
-          const int kend = kt0 + KCHUNK < num_k ? kt0 + KCHUNK : num_k;
-          for (int kt = kt0; kt < kend; ++kt, ++it) {
-            const int s = it % STAGES;
-            if (!mbar_wait(&full_bar[s], (it / STAGES) & 1, &abort_flag)) {
-              ok = false;
-              break;
-            }
-            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            const uint32_t a_hi = smem_u32(stage_ptr(s, 0)), a_lo = smem_u32(stage_ptr(s, 1));
-            const uint32_t b_hi = smem_u32(stage_ptr(s, 2)), b_lo = smem_u32(stage_ptr(s, 3));
-#pragma unroll
-            for (int kk = 0; kk < BK / UMMA_K; ++kk) {
-              const uint64_t dah = operand_desc<A_MN>(a_hi, kk), dal = operand_desc<A_MN>(a_lo, kk);
-              const uint64_t dbh = operand_desc<B_MN>(b_hi, kk), dbl = operand_desc<B_MN>(b_lo, kk);
-              const uint32_t first = (kt == kt0 && kk == 0) ? 0u : 1u;
-              umma_tf32(d_tmem, dal, dbh, kIdesc, first);  // lo * hi
-              umma_tf32(d_tmem, dah, dbl, kIdesc, 1u);     // hi * lo
-              umma_tf32(d_tmem, dah, dbh, kIdesc, 1u);     // hi * hi (largest term last)
-            }
-            umma_commit(&empty_bar[s]);
-          }
-          if (ok) umma_commit(&acc_full[b]);
-        }
-      }
-      if (!ok) {
-        atomicCAS(args.err, kErrNone, kErrTimeoutFull);
-        abort_flag = 1;
-      }
-    }
-  } else {
-    // ------------------------------------------------------ promotion + epilogue (warps 2..9)
-    const int q = warp & 3;             // TMEM lane quarter this warp may access
-    const int half = (warp - 2) >> 2;   // which half of the tile's columns
-    const bool vec = ((args.ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(args.C) & 15) == 0) &&
-                     ((args.strideC & 3) == 0);
-    int cc = 0;
-    bool ok = true;
-    for (int t = blockIdx.x; ok && t < args.num_tiles; t += gridDim.x) {
-      int mb, nb, bz, ks, kb;
-      decode_tile(t, args, mb, nb, bz, ks);
-      const int num_k = unit_k_tiles(args, ks, kb);
-      float acc[CPW];
-#pragma unroll
-      for (int i = 0; i < CPW; ++i) acc[i] = 0.0f;
-      for (int kt0 = 0; kt0 < num_k; kt0 += KCHUNK, ++cc) {
-        const int b = cc & 1;
-        if (!mbar_wait(&acc_full[b], (cc >> 1) & 1, &abort_flag)) {
-          if (lane == 0) atomicCAS(args.err, kErrNone, kErrTimeoutAcc);
-          abort_flag = 1;
-          ok = false;
-          break;
-        }
-        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint32_t taddr = tmem_base + (uint32_t)(b * TMEM_COLS + half * CPW) +
-                               ((uint32_t)(q * 32) << 16);
-        promote_cols<CPW>(taddr, acc);
-        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-        mbar_arrive(&acc_empty[b]);
-      }
-      if (!ok) break;
-      const int row = mb * BM + q * 32 + lane;
-      const int col0 = nb * TBN + half * CPW;
-      if (row < args.M && col0 < args.N) {
-        float *crow = args.C + (int64_t)ks * args.split_stride + (int64_t)bz * args.strideC +
-                      (int64_t)row * args.ldc + col0;
-        if (vec && col0 + CPW <= args.N) {
-#pragma unroll
-          for (int i = 0; i < CPW; i += 4)
-            *reinterpret_cast<float4 *>(crow + i) = make_float4(acc[i], acc[i + 1], acc[i + 2], acc[i + 3]);
-        } else {
-#pragma unroll
-          for (int i = 0; i < CPW; ++i)
-            if (col0 + i < args.N) crow[i] = acc[i];
-        }
-      }
-    }
-  }
-
-  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-  __syncthreads();
-  if (warp == 1) {
-    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
-                 "r"(2 * TMEM_COLS)
-                 : "memory");
-  }
-}
-
-// ---------------------------------------------------------------- 2-SM (CTA pair) variant
-//
-// A cluster of two CTAs computes a 256 x 256 output tile with
-// tcgen05.mma.cta_group::2: each CTA holds 128 rows of A and 128 rows (N) of B per
-// stage, the leader CTA (rank 0) issues the MMAs, the tensor cores read the peer's
-// half of each operand from its shared memory, and each CTA's TMEM receives its 128
-// rows x 256 columns. Per MMA a CTA reads half of B from its own shared memory
-// instead of all of it, and loads a third fewer bytes per k-tile: less shared-memory
-// and L2 traffic, and energy, per product. Protocol: both CTAs' TMA loads complete
-// their bytes on the leader's full barrier (which the leader's producer armed for the
-// pair's bytes); the leader's commits multicast to both CTAs' empty and acc_full
-// barriers; the peer's epilogue threads arrive on the leader's acc_empty barriers.
-// TMEM is allocated and freed with cta_group::2 by warp 1 of both CTAs. Every wait is
-// bounded as in the single-CTA kernel, and both CTAs meet at a cluster barrier before
-// freeing TMEM and exiting.
-constexpr int PAIR_STAGES = 6;
-constexpr int PAIR_TILE_BYTES = BM * BK * 4;             // 128 rows of A or B: 8 KB
-constexpr int PAIR_STAGE_BYTES = 4 * PAIR_TILE_BYTES;    // A_hi, A_lo, B_hi, B_lo: 32 KB
-
-__device__ __forceinline__ uint32_t cluster_rank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-
-__device__ __forceinline__ void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
-                   : "memory");
-}
-
-// Shared-memory address of the same variable in the cluster's CTA 0.
-__device__ __forceinline__ uint32_t in_leader(const void *p) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, 0;" : "=r"(r) : "r"(smem_u32(p)));
-  return r;
-}
-
-__device__ __forceinline__ void tma_load_3d_pair(void *dst, const CUtensorMap *map, uint32_t bar,
-                                                 int c0, int c1, int c2) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
-      : "memory");
-}
-
-__device__ __forceinline__ void tma_load_4d_pair(void *dst, const CUtensorMap *map, uint32_t bar,
-                                                 int c0, int c1, int c2, int c3) {
-  asm volatile(
-      "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
-      : "memory");
-}
-
-// load_operand for a CTA of a pair: 128 rows, bytes completed on the leader's barrier.
-template <bool MN>
-__device__ __forceinline__ void load_operand_pair(uint8_t *dst, const CUtensorMap *map, uint32_t bar,
-                                                  int k0, int row0, int bz, bool wide) {
-  if constexpr (MN) {
-    if (wide) {
-      tma_load_4d_pair(dst, map, bar, 0, k0, row0 / MN_CHUNK, bz);
-    } else {
-#pragma unroll
-      for (int j = 0; j < BM / MN_CHUNK; ++j)
-        tma_load_3d_pair(dst + j * MN_CHUNK_BYTES, map, bar, row0 + j * MN_CHUNK, k0, bz);
-    }
-  } else {
-    tma_load_3d_pair(dst, map, bar, k0, row0, bz);
-  }
-}
-
-__device__ __forceinline__ void umma_tf32_pair(uint32_t tmem_d, uint64_t a, uint64_t b,
-                                               uint32_t idesc, uint32_t accum) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-      "l"(a), "l"(b), "r"(idesc), "r"(accum)
-      : "memory");
-}
-
-// Arrive on the barrier at this offset in both CTAs of the pair when the MMAs issued
-// so far have completed.
-__device__ __forceinline__ void umma_commit_pair(uint64_t *bar) {
-  asm volatile(
-      "{\n\t.reg .b16 m;\n\tmov.b16 m, 3;\n\t"
-      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
-      " [%0], m;\n\t}" ::"r"(smem_u32(bar))
-      : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
-               : "memory");
-}
-
-template <bool A_MN, bool B_MN>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
-    gemm_pair_kernel(const __grid_constant__ CUtensorMap mapAh,
-                     const __grid_constant__ CUtensorMap mapAl,
-                     const __grid_constant__ CUtensorMap mapBh,
-                     const __grid_constant__ CUtensorMap mapBl, GemmArgs args) {
-  extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t *smem = reinterpret_cast<uint8_t *>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-  __shared__ __align__(8) uint64_t full_bar[PAIR_STAGES];
-  __shared__ __align__(8) uint64_t empty_bar[PAIR_STAGES];
-  __shared__ __align__(8) uint64_t acc_full[2];
-  __shared__ __align__(8) uint64_t acc_empty[2];
-  __shared__ uint32_t tmem_base_slot;
-  __shared__ volatile int abort_flag;
-
-  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const uint32_t rank = cluster_rank();
-  const bool leader = rank == 0;
-  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
-  constexpr uint32_t kIdesc = make_idesc(2 * BM, BN, A_MN, B_MN);
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < PAIR_STAGES; ++s) {
-      mbar_init(&full_bar[s], 1);
-      mbar_init(&empty_bar[s], 1);
-    }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 2 * 32 * NUM_EPI_WARPS);  // both CTAs' epilogue threads
-    }
-    abort_flag = 0;
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    prefetch_map(&mapAh);
-    prefetch_map(&mapAl);
-    prefetch_map(&mapBh);
-    prefetch_map(&mapBl);
-  }
-  if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                     smem_u32(&tmem_base_slot)),
-                 "r"(2 * TMEM_COLS)
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
-  }
-  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-  __syncthreads();
-  cluster_sync_all();  // both CTAs' barriers initialised and TMEM allocated
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-  const uint32_t tmem_base = tmem_base_slot;
-
-  auto stage_ptr = [&](int s, int which) -> uint8_t * {
-    return smem + (size_t)s * PAIR_STAGE_BYTES + (size_t)which * PAIR_TILE_BYTES;
-  };
-
-  if (warp == 0) {
-    if (lane == 0) {
-      // ------------------------------------------------------ TMA producer (both CTAs)
-      int it = 0;
-      bool ok = true;
-      for (int t = pair; ok && t < args.num_tiles; t += npairs) {
-        int mb, nb, bz, ks, kb;
-        decode_tile(t, args, mb, nb, bz, ks);
-        const int nk = unit_k_tiles(args, ks, kb);
-        const int row_a = mb * 2 * BM + (int)rank * BM, row_b = nb * BN + (int)rank * BM;
-        for (int kt = 0; kt < nk; ++kt, ++it) {
-          const int s = it % PAIR_STAGES;
-          const uint32_t round = it / PAIR_STAGES;
-          if (it >= PAIR_STAGES && !mbar_wait(&empty_bar[s], (round - 1) & 1, &abort_flag)) {
-            ok = false;
-            break;
-          }
-          if (leader) mbar_expect_tx(&full_bar[s], 2 * PAIR_STAGE_BYTES);
-          const uint32_t fb = in_leader(&full_bar[s]);
-          const int k0 = kb + kt * BK;
-          load_operand_pair<A_MN>(stage_ptr(s, 0), &mapAh, fb, k0, row_a, bz, args.wide & 1);
-          load_operand_pair<A_MN>(stage_ptr(s, 1), &mapAl, fb, k0, row_a, bz, args.wide & 2);
-          load_operand_pair<B_MN>(stage_ptr(s, 2), &mapBh, fb, k0, row_b, bz, args.wide & 4);
-          load_operand_pair<B_MN>(stage_ptr(s, 3), &mapBl, fb, k0, row_b, bz, args.wide & 8);
-        }
-      }
-      if (!ok) {
-        atomicCAS(args.err, kErrNone, kErrTimeoutEmpty);
-        abort_flag = 1;
-        if (leader) {  // drain (bounded): the last PAIR_STAGES k-tiles' loads of the pair
-          for (int i = (it > PAIR_STAGES ? it - PAIR_STAGES : 0); i < it; ++i) {
-            const int s = i % PAIR_STAGES;
-            const uint64_t t0 = globaltimer();
-            while (!mbar_try_wait(&full_bar[s], (i / PAIR_STAGES) & 1) && globaltimer() - t0 < kWaitNs) {
-            }
-          }
-        }
-      }
-    }
-  } else if (warp == 1) {
-    if (lane == 0 && leader) {
-      // ------------------------------------------------------ MMA issuer (leader only)
-      int it = 0, cc = 0;
-      bool ok = true;
-      for (int t = pair; ok && t < args.num_tiles; t += npairs) {
-        int mb, nb, bz, ks, kb;
-        decode_tile(t, args, mb, nb, bz, ks);
-        const int num_k = unit_k_tiles(args, ks, kb);
-        for (int kt0 = 0; ok && kt0 < num_k; kt0 += KCHUNK, ++cc) {
-          const int b = cc & 1;
-          if (cc >= 2 && !mbar_wait(&acc_empty[b], ((cc >> 1) - 1) & 1, &abort_flag)) {
-            ok = false;
-            break;
-          }
-          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-          const uint32_t d_tmem = tmem_base + (uint32_t)(b * TMEM_COLS);
-          const int kend = kt0 + KCHUNK < num_k ? kt0 + KCHUNK : num_k;
-          for (int kt = kt0; kt < kend; ++kt, ++it) {
-            const int s = it % PAIR_STAGES;
-            if (!mbar_wait(&full_bar[s], (it / PAIR_STAGES) & 1, &abort_flag)) {
-              ok = false;
-              break;
-            }
-            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            const uint32_t a_hi = smem_u32(stage_ptr(s, 0)), a_lo = smem_u32(stage_ptr(s, 1));
-            const uint32_t b_hi = smem_u32(stage_ptr(s, 2)), b_lo = smem_u32(stage_ptr(s, 3));
-#pragma unroll
-            for (int kk = 0; kk < BK / UMMA_K; ++kk) {
-              const uint64_t dah = operand_desc<A_MN>(a_hi, kk), dal = operand_desc<A_MN>(a_lo, kk);
-              const uint64_t dbh = operand_desc<B_MN>(b_hi, kk), dbl = operand_desc<B_MN>(b_lo, kk);
-              const uint32_t first = (kt == kt0 && kk == 0) ? 0u : 1u;
-              umma_tf32_pair(d_tmem, dal, dbh, kIdesc, first);  // lo * hi
-              umma_tf32_pair(d_tmem, dah, dbl, kIdesc, 1u);     // hi * lo
-              umma_tf32_pair(d_tmem, dah, dbh, kIdesc, 1u);     // hi * hi
-            }
-            umma_commit_pair(&empty_bar[s]);
-          }
-          if (ok) umma_commit_pair(&acc_full[b]);
-        }
-      }
-      if (!ok) {
-        atomicCAS(args.err, kErrNone, kErrTimeoutFull);
-        abort_flag = 1;
-      }
-    }
-  } else {
-    // ------------------------------------------------------ promotion + epilogue (warps 2..9)
-    const int q = warp & 3;
-    const int half = (warp - 2) >> 2;
-    const bool vec = ((args.ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(args.C) & 15) == 0) &&
-                     ((args.strideC & 3) == 0);
-    const uint32_t acc_empty_leader[2] = {in_leader(&acc_empty[0]), in_leader(&acc_empty[1])};
-    int cc = 0;
-    bool ok = true;
-    for (int t = pair; ok && t < args.num_tiles; t += npairs) {
-      int mb, nb, bz, ks, kb;
-      decode_tile(t, args, mb, nb, bz, ks);
-      const int num_k = unit_k_tiles(args, ks, kb);
-      float acc[128];
-#pragma unroll
-      for (int i = 0; i < 128; ++i) acc[i] = 0.0f;
-      for (int kt0 = 0; kt0 < num_k; kt0 += KCHUNK, ++cc) {
-        const int b = cc & 1;
-        if (!mbar_wait(&acc_full[b], (cc >> 1) & 1, &abort_flag)) {
-          if (lane == 0) atomicCAS(args.err, kErrNone, kErrTimeoutAcc);
-          abort_flag = 1;
-          ok = false;
-          break;
-        }
-        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint32_t taddr = tmem_base + (uint32_t)(b * TMEM_COLS + half * 128) +
-                               ((uint32_t)(q * 32) << 16);
-#pragma unroll
-        for (int c0 = 0; c0 < 128; c0 += 32) {
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(taddr + (uint32_t)c0, r);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) acc[c0 + i] = __fadd_rn(acc[c0 + i], __uint_as_float(r[i]));
-        }
-        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-        if (leader) mbar_arrive(&acc_empty[b]);
-        else mbar_arrive_remote(acc_empty_leader[b]);
-      }
-      if (!ok) break;
-      const int row = mb * 2 * BM + (int)rank * BM + q * 32 + lane;
-      const int col0 = nb * BN + half * 128;
-      if (row < args.M && col0 < args.N) {
-        float *crow = args.C + (int64_t)ks * args.split_stride + (int64_t)bz * args.strideC +
-                      (int64_t)row * args.ldc + col0;
-        if (vec && col0 + 128 <= args.N) {
-#pragma unroll
-          for (int i = 0; i < 128; i += 4)
-            *reinterpret_cast<float4 *>(crow + i) = make_float4(acc[i], acc[i + 1], acc[i + 2], acc[i + 3]);
-        } else {
-#pragma unroll
-          for (int i = 0; i < 128; ++i)
-            if (col0 + i < args.N) crow[i] = acc[i];
-        }
-      }
-    }
-  }
-
-  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-  __syncthreads();
-  cluster_sync_all();  // neither CTA frees TMEM or exits while the pair may still use it
-  if (warp == 1) {
-    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
-                 "r"(2 * TMEM_COLS)
-                 : "memory");
-  }
-}
 
 // ---------------------------------------------------------------- host side
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
@@ -1032,6 +259,14 @@ int prepare(const float *src, int64_t ld, int64_t sb, const float *lo_given, int
   return FZ_OK;
 }
 
+// Dynamic shared memory of a kernel variant (stage ring + alignment slack).
+size_t smem_bytes(bool pair, int tbn) {
+  if (pair) return (size_t)PAIR_STAGES * PAIR_STAGE_BYTES + 1024;
+  if (tbn == 16) return (size_t)TileCfg<16>::NSTAGE * TileCfg<16>::STAGE + 1024;
+  if (tbn == 64) return (size_t)TileCfg<64>::NSTAGE * TileCfg<64>::STAGE + 1024;
+  return (size_t)TileCfg<BN>::NSTAGE * TileCfg<BN>::STAGE + 1024;
+}
+
 template <bool A_MN, bool B_MN, int TBN>
 int launch_gemm(const CUtensorMap &mAh, const CUtensorMap &mAl, const CUtensorMap &mBh,
                 const CUtensorMap &mBl, const GemmArgs &ga, unsigned grid, bool pair,
@@ -1039,21 +274,21 @@ int launch_gemm(const CUtensorMap &mAh, const CUtensorMap &mAl, const CUtensorMa
   static bool attr_done[2][64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
-  const size_t smem = pair ? (size_t)PAIR_STAGES * PAIR_STAGE_BYTES + 1024
-                           : (size_t)TileCfg<TBN>::NSTAGE * TileCfg<TBN>::STAGE + 1024;
+  const size_t smem = smem_bytes(pair, TBN);
   if (dev < 64 && !attr_done[pair][dev]) {
     if (pair)
-      cudaFuncSetAttribute(gemm_pair_kernel<A_MN, B_MN>,
+      cudaFuncSetAttribute(gemm_pair_kernel<A_MN, B_MN, StoreEpi>,
                            cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     else
-      cudaFuncSetAttribute(gemm_3xtf32_kernel<A_MN, B_MN, TBN>,
+      cudaFuncSetAttribute(gemm_3xtf32_kernel<A_MN, B_MN, TBN, StoreEpi>,
                            cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     attr_done[pair][dev] = true;
   }
+  const EpiParams ep{};
   if (pair)
-    gemm_pair_kernel<A_MN, B_MN><<<2 * grid, NUM_THREADS, smem, s>>>(mAh, mAl, mBh, mBl, ga);
+    gemm_pair_kernel<A_MN, B_MN, StoreEpi><<<2 * grid, NUM_THREADS, smem, s>>>(mAh, mAl, mBh, mBl, ga, ep);
   else
-    gemm_3xtf32_kernel<A_MN, B_MN, TBN><<<grid, NUM_THREADS, smem, s>>>(mAh, mAl, mBh, mBl, ga);
+    gemm_3xtf32_kernel<A_MN, B_MN, TBN, StoreEpi><<<grid, NUM_THREADS, smem, s>>>(mAh, mAl, mBh, mBl, ga, ep);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fz::cuda_fail(e, "gemm_3xtf32_kernel launch", __FILE__, __LINE__);
   fz::note_launch();
@@ -1076,18 +311,218 @@ int dispatch_gemm(bool a_mn, bool b_mn, int tbn, const CUtensorMap &mAh, const C
   return launch_gemm<true, true, BN>(mAh, mAl, mBh, mBl, ga, grid, pair, s);
 }
 
+// ---------------------------------------------------------------- fused epilogues
+//
+// A fused elementwise program over the product (leaf 0) and inputs broadcast into
+// the [batch, M, N] output space is compiled into the GEMM kernel: the text of
+// fz_gemm_kernels.cuh, the program's scalar evaluator (the same fz_eval the fused
+// elementwise kernels use, so each output rounds exactly as there) and a generated
+// epilogue class GenEpi, instantiated for the kernel variant by NVRTC and cached per
+// (program, input classes, variant).
+const char *const kGemmKernelSource =
+#include "fz_gemm_kernels.inc"
+    ;
+
+static_assert(EPI_MAX_IN + 1 == FZ_MAX_LEAVES && EPI_MAX_OUT == FZ_MAX_OUTPUTS,
+              "epilogue operand limits follow the fused-program limits");
+
+struct Epilogue {
+  const fz_program *pg = nullptr;
+  const fz_epi_input *inputs = nullptr;
+  float *const *outputs = nullptr;
+};
+
+// cls[k]: 1 when input k varies along the columns (col_stride 1), else 0.
+std::string epilogue_class(const fz_program &pg, const int *cls) {
+  const int nin = pg.num_leaves - 1, nout = pg.num_outputs;
+  std::ostringstream o;
+  o << "struct GenEpi {\n"
+    << "  template <int CPW>\n"
+    << "  static __device__ __forceinline__ void store(const fz_gemm_dev::GemmArgs &a,\n"
+    << "      const fz_gemm_dev::EpiParams &p, int, int bz, int row, int col0,\n"
+    << "      const float (&acc)[CPW]) {\n"
+    << "    if (row >= a.M || col0 >= a.N) return;\n"
+    << "    const long long ob = (long long)bz * a.strideC + (long long)row * a.ldc + col0;\n";
+  for (int k = 0; k < nin; ++k) {
+    o << "    const float *b" << k << " = p.in[" << k << "] + (long long)bz * p.in_sb[" << k
+      << "] + (long long)row * p.in_sm[" << k << "]" << (cls[k] ? " + col0" : "") << ";\n";
+    if (!cls[k]) o << "    const float s" << k << " = b" << k << "[0];\n";
+  }
+  for (int j = 0; j < nout; ++j) o << "    float *o" << j << " = p.out[" << j << "] + ob;\n";
+  auto leaf_args = [&](const char *lane, bool vec) {
+    std::string r;
+    for (int k = 0; k < nin; ++k) {
+      if (!cls[k]) r += "s" + std::to_string(k) + ", ";
+      else if (vec) r += "v" + std::to_string(k) + "." + lane + ", ";
+      else r += "b" + std::to_string(k) + "[i], ";
+    }
+    return r;
+  };
+  o << "    if (p.vec && col0 + CPW <= a.N) {\n#pragma unroll\n"
+    << "      for (int i = 0; i < CPW; i += 4) {\n";
+  for (int k = 0; k < nin; ++k)
+    if (cls[k]) o << "        const float4 v" << k << " = *reinterpret_cast<const float4 *>(b" << k << " + i);\n";
+  for (int j = 0; j < nout; ++j) o << "        float4 q" << j << ";\n";
+  const char *lanes[4] = {"x", "y", "z", "w"};
+  for (int ln = 0; ln < 4; ++ln) {
+    o << "        fz_eval(acc[i + " << ln << "], " << leaf_args(lanes[ln], true);
+    for (int j = 0; j < nout; ++j) o << "q" << j << "." << lanes[ln] << (j + 1 < nout ? ", " : "");
+    o << ");\n";
+  }
+  for (int j = 0; j < nout; ++j) o << "        *reinterpret_cast<float4 *>(o" << j << " + i) = q" << j << ";\n";
+  o << "      }\n    } else {\n#pragma unroll\n"
+    << "      for (int i = 0; i < CPW; ++i) {\n"
+    << "        if (col0 + i < a.N) {\n";
+  for (int j = 0; j < nout; ++j) o << "          float r" << j << ";\n";
+  o << "          fz_eval(acc[i], " << leaf_args("", false);
+  for (int j = 0; j < nout; ++j) o << "r" << j << (j + 1 < nout ? ", " : "");
+  o << ");\n";
+  for (int j = 0; j < nout; ++j) o << "          o" << j << "[i] = r" << j << ";\n";
+  o << "        }\n      }\n    }\n  }\n};\n";
+  return o.str();
+}
+
+struct JitEntry {
+  cudaKernel_t kern = nullptr;
+  uint64_t attr_devices = 0;  // devices whose shared-memory limit was raised
+};
+std::mutex g_jit_mu;
+std::unordered_map<std::string, JitEntry> g_jit;
+
+std::string epilogue_source(const fz_program &pg, const int *cls) {
+  return "#define FZ_GEMM_BK " + std::to_string(BK) + "\n" + kGemmKernelSource + "\n" +
+         fz::program_eval_source(pg) + epilogue_class(pg, cls);
+}
+
+std::string epilogue_kernel_name(bool a_mn, bool b_mn, int tbn, bool pair) {
+  auto b = [](bool v) { return std::string(v ? "true" : "false"); };
+  if (pair) return "&fz_gemm_dev::gemm_pair_kernel<" + b(a_mn) + ", " + b(b_mn) + ", GenEpi>";
+  return "&fz_gemm_dev::gemm_3xtf32_kernel<" + b(a_mn) + ", " + b(b_mn) + ", " + std::to_string(tbn) +
+         ", GenEpi>";
+}
+
+int jit_kernel(const fz_program &pg, const int *cls, bool a_mn, bool b_mn, int tbn, bool pair,
+               size_t smem, cudaKernel_t *out) {
+  std::string key(reinterpret_cast<const char *>(&pg),
+                  offsetof(fz_program, nodes) + sizeof(fz_node) * pg.num_nodes);
+  for (int k = 0; k + 1 < pg.num_leaves; ++k) key.push_back((char)('0' + cls[k]));
+  key += pair ? "P" : "S";
+  key.push_back((char)('0' + a_mn));
+  key.push_back((char)('0' + b_mn));
+  key += std::to_string(tbn);
+  int dev = 0;
+  FZ_CUDA(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lk(g_jit_mu);
+  JitEntry &e = g_jit[key];
+  if (!e.kern) {
+    std::vector<char> bin;
+    std::string lowered;
+    const std::string name = epilogue_kernel_name(a_mn, b_mn, tbn, pair);
+    int rc = fz::nvrtc_cubin(epilogue_source(pg, cls), "fz_gemm_epilogue.cu", name.c_str(), &bin, &lowered);
+    if (rc) return rc;
+    cudaLibrary_t lib;
+    FZ_CUDA(cudaLibraryLoadData(&lib, bin.data(), nullptr, nullptr, 0, nullptr, nullptr, 0));
+    FZ_CUDA(cudaLibraryGetKernel(&e.kern, lib, lowered.c_str()));
+  }
+  if (dev >= 64 || !((e.attr_devices >> dev) & 1)) {
+    FZ_CUDA(cudaKernelSetAttributeForDevice(e.kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            (int)smem, dev));
+    if (dev < 64) e.attr_devices |= 1ull << dev;
+  }
+  *out = e.kern;
+  return FZ_OK;
+}
+
+int launch_epilogue_gemm(const Epilogue &E, const int *cls, const EpiParams &ep, bool a_mn,
+                         bool b_mn, int tbn, const CUtensorMap &mAh, const CUtensorMap &mAl,
+                         const CUtensorMap &mBh, const CUtensorMap &mBl, const GemmArgs &ga,
+                         unsigned grid, bool pair, cudaStream_t s) {
+  const size_t smem = smem_bytes(pair, tbn);
+  cudaKernel_t k = nullptr;
+  int rc = jit_kernel(*E.pg, cls, a_mn, b_mn, tbn, pair, smem, &k);
+  if (rc) return rc;
+  void *args[] = {const_cast<CUtensorMap *>(&mAh), const_cast<CUtensorMap *>(&mAl),
+                  const_cast<CUtensorMap *>(&mBh), const_cast<CUtensorMap *>(&mBl),
+                  const_cast<GemmArgs *>(&ga), const_cast<EpiParams *>(&ep)};
+  FZ_CUDA(cudaLaunchKernel((const void *)k, dim3(pair ? 2 * grid : grid), dim3(NUM_THREADS), args,
+                           smem, s));
+  fz::note_launch();
+  return FZ_OK;
+}
+
+// The epilogue program as one fused elementwise pass over a dense product P
+// ([batch, M, N]): the form taken when the GEMM splits K or K = 0.
+int epilogue_pass(const Epilogue &E, const float *P, int64_t batch, int64_t M, int64_t N,
+                  int64_t ldc, int64_t strideC, cudaStream_t s) {
+  const fz_program &pg = *E.pg;
+  const int nout = pg.num_outputs, nleaf = pg.num_leaves;
+  fz_ewise_plan plan{};
+  plan.ndim = 3;
+  plan.num_operands = nout + nleaf;
+  plan.size[0] = batch;
+  plan.size[1] = M;
+  plan.size[2] = N;
+  auto set = [&](int k, int64_t sb, int64_t sm, int64_t sn) {
+    plan.stride_bytes[k][0] = sb * 4;
+    plan.stride_bytes[k][1] = sm * 4;
+    plan.stride_bytes[k][2] = sn * 4;
+  };
+  for (int k = 0; k < nout; ++k) set(k, strideC, ldc, 1);
+  set(nout, M * N, N, 1);
+  std::vector<const float *> leaves(nleaf);
+  leaves[0] = P;
+  for (int k = 1; k < nleaf; ++k) {
+    const fz_epi_input &in = E.inputs[k - 1];
+    set(nout + k, in.batch_stride, in.row_stride, in.col_stride);
+    leaves[k] = in.ptr;
+  }
+  return fz_fused_launch(&pg, &plan, E.outputs, leaves.data(), s);
+}
+
+int check_epilogue(const Epilogue &E, int64_t N, int64_t ldc) {
+  FZ_REQUIRE(E.pg && E.outputs, "fz_gemm_f32_epilogue: null program or outputs");
+  int rc = fz::validate_program(*E.pg);
+  if (rc) return rc;
+  const fz_program &pg = *E.pg;
+  FZ_REQUIRE(pg.num_leaves >= 1 && pg.num_leaves <= 1 + EPI_MAX_IN,
+             "fz_gemm_f32_epilogue: the program needs leaf 0 (the product) and at most " +
+                 std::to_string(EPI_MAX_IN) + " inputs");
+  FZ_REQUIRE(pg.num_outputs <= EPI_MAX_OUT, "fz_gemm_f32_epilogue: too many outputs");
+  FZ_REQUIRE(pg.num_leaves == 1 || E.inputs, "fz_gemm_f32_epilogue: null inputs");
+  for (int k = 0; k < pg.num_outputs; ++k) FZ_REQUIRE(E.outputs[k], "fz_gemm_f32_epilogue: null output");
+  for (int k = 1; k < pg.num_leaves; ++k) {
+    FZ_REQUIRE(E.inputs[k - 1].ptr, "fz_gemm_f32_epilogue: null input");
+    FZ_REQUIRE(E.inputs[k - 1].col_stride == 0 || E.inputs[k - 1].col_stride == 1,
+               "fz_gemm_f32_epilogue: input column stride must be 0 or 1");
+  }
+  FZ_REQUIRE(ldc >= N, "fz_gemm_f32_epilogue: ldc < N");
+  return FZ_OK;
+}
+
 int gemm_impl(int64_t batch, int64_t M, int64_t N, int64_t K, const float *A, const float *A_lo,
               int64_t lda, int64_t strideA, int transA, const float *B, const float *B_lo,
               int64_t ldb, int64_t strideB, int transB, float *C, int64_t ldc, int64_t strideC,
-              void *stream) {
+              const Epilogue &E, void *stream) {
   FZ_REQUIRE(batch >= 0 && M >= 0 && N >= 0 && K >= 0, "fz_gemm_f32: negative extent");
+  if (E.pg) {
+    int rc = check_epilogue(E, N, ldc);
+    if (rc) return rc;
+  }
   if (batch == 0 || M == 0 || N == 0) return FZ_OK;
-  FZ_REQUIRE(C, "fz_gemm_f32: null C");
+  FZ_REQUIRE(C || E.pg, "fz_gemm_f32: null C");
   FZ_REQUIRE(M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31) && batch < 65536,
              "fz_gemm_f32: extent too large");
   FZ_REQUIRE(ldc >= N, "fz_gemm_f32: ldc < N");
   cudaStream_t s = fz::resolve(stream);
   if (K == 0) {
+    if (E.pg) {
+      float *P = nullptr;
+      int rc = fz_malloc((void **)&P, sizeof(float) * batch * M * N, s);
+      if (!rc) rc = fz_fill_f32(P, 0.0f, batch * M * N, s);
+      if (!rc) rc = epilogue_pass(E, P, batch, M, N, ldc, strideC, s);
+      fz_free(P, s);
+      return rc;
+    }
     for (int64_t b = 0; b < batch; ++b)
       for (int64_t r = 0; r < M; ++r) {
         int rc = fz_fill_f32(C + b * strideC + r * ldc, 0.0f, N, s);
@@ -1159,7 +594,7 @@ int gemm_impl(int64_t batch, int64_t M, int64_t N, int64_t K, const float *A, co
   const int tiles_m = (int)((M + tile_m - 1) / tile_m), tiles_n = (int)((N + tbn - 1) / tbn);
   const int64_t tiles = (int64_t)tiles_m * tiles_n * batch;
   const bool dense_c = ldc == N && (batch == 1 || strideC == M * N);
-  const int splits = dense_c ? choose_splits(tiles, M, N, K, batch, workers) : 1;
+  const int splits = dense_c || E.pg ? choose_splits(tiles, M, N, K, batch, workers) : 1;
   const int64_t kps = splits > 1 ? round_up((K + splits - 1) / splits, (int64_t)BK * KCHUNK) : K;
   const int real_splits = (int)((K + kps - 1) / kps);
   const int64_t num_units = tiles * real_splits;
@@ -1167,6 +602,31 @@ int gemm_impl(int64_t batch, int64_t M, int64_t N, int64_t K, const float *A, co
   float *partial = nullptr;
   if (!rc && real_splits > 1)
     rc = fz_malloc((void **)&partial, sizeof(float) * real_splits * batch * M * N, s);
+  // split K with an epilogue: the partials are summed into a dense product, which the
+  // program then reads in one fused pass
+  float *product = nullptr;
+  if (!rc && E.pg && real_splits > 1) rc = fz_malloc((void **)&product, sizeof(float) * batch * M * N, s);
+  // epilogue operands, and the column class of each input compiled into the kernel
+  EpiParams ep{};
+  int cls[EPI_MAX_IN] = {};
+  if (E.pg && !product) {
+    bool vec = ldc % 4 == 0 && (batch == 1 || strideC % 4 == 0);
+    for (int k = 0; k < E.pg->num_outputs; ++k) {
+      ep.out[k] = E.outputs[k];
+      vec = vec && ((uintptr_t)E.outputs[k] & 15) == 0;
+    }
+    for (int k = 0; k + 1 < E.pg->num_leaves; ++k) {
+      const fz_epi_input &in = E.inputs[k];
+      ep.in[k] = in.ptr;
+      ep.in_sb[k] = in.batch_stride;
+      ep.in_sm[k] = in.row_stride;
+      cls[k] = in.col_stride == 1;
+      if (cls[k])
+        vec = vec && ((uintptr_t)in.ptr & 15) == 0 && in.row_stride % 4 == 0 &&
+              (batch == 1 || in.batch_stride % 4 == 0);
+    }
+    ep.vec = vec;
+  }
 
   int *err = nullptr;
   if (!rc) rc = fz::device_error_word(&err);
@@ -1174,16 +634,22 @@ int gemm_impl(int64_t batch, int64_t M, int64_t N, int64_t K, const float *A, co
     // raster bands of 16 row tiles walked column by column (a narrower band for the
     // 256-row pair tiles re-reads B once more per band and measured slower)
     const int band = 16;
-    GemmArgs ga{partial ? partial : C, partial ? N : ldc, partial ? M * N : strideC,
-                batch * M * N, (int)M, (int)N, (int)K, (int)batch,
+    const bool in_kernel = E.pg && !product;
+    GemmArgs ga{partial ? partial : in_kernel ? nullptr : C, partial ? N : ldc,
+                partial ? M * N : strideC, batch * M * N, (int)M, (int)N, (int)K, (int)batch,
                 tiles_m, tiles_n, (int)num_units, tiles_m < band ? tiles_m : band,
                 real_splits, (int)kps, wide_mask, err};
     // persistent grid: one CTA (or CTA pair) per SM (pair of SMs)
     const unsigned grid = (unsigned)(num_units < workers ? num_units : workers);
-    rc = dispatch_gemm(oa.mn, ob.mn, tbn, mAh, mAl, mBh, mBl, ga, grid, pair, s);
+    if (in_kernel)
+      rc = launch_epilogue_gemm(E, cls, ep, oa.mn, ob.mn, tbn, mAh, mAl, mBh, mBl, ga, grid, pair, s);
+    else
+      rc = dispatch_gemm(oa.mn, ob.mn, tbn, mAh, mAl, mBh, mBl, ga, grid, pair, s);
     // K-split partials: summed over the splits in a fixed order (deterministic)
-    if (!rc && partial) rc = fz_reduce(FZ_RSUM, C, partial, 1, real_splits, batch * M * N, s);
+    if (!rc && partial) rc = fz_reduce(FZ_RSUM, product ? product : C, partial, 1, real_splits, batch * M * N, s);
+    if (!rc && product) rc = epilogue_pass(E, product, batch, M, N, ldc, strideC, s);
   }
+  if (product) fz_free(product, s);
   if (partial) fz_free(partial, s);
   fz_free(ws, s);
   fz_free(bt, s);
@@ -1197,7 +663,7 @@ extern "C" int fz_gemm_f32(int64_t batch, int64_t M, int64_t N, int64_t K, const
                            int64_t strideB, int transB, float *C, int64_t ldc, int64_t strideC,
                            void *stream) {
   return gemm_impl(batch, M, N, K, A, nullptr, lda, strideA, transA, B, nullptr, ldb, strideB,
-                   transB, C, ldc, strideC, stream);
+                   transB, C, ldc, strideC, Epilogue{}, stream);
 }
 
 extern "C" int fz_gemm_f32_split(int64_t batch, int64_t M, int64_t N, int64_t K, const float *A,
@@ -1205,7 +671,38 @@ extern "C" int fz_gemm_f32_split(int64_t batch, int64_t M, int64_t N, int64_t K,
                                  const float *B, const float *B_lo, int64_t ldb, int64_t strideB,
                                  int transB, float *C, int64_t ldc, int64_t strideC, void *stream) {
   return gemm_impl(batch, M, N, K, A, A_lo, lda, strideA, transA, B, B_lo, ldb, strideB, transB,
-                   C, ldc, strideC, stream);
+                   C, ldc, strideC, Epilogue{}, stream);
+}
+
+extern "C" int fz_gemm_f32_epilogue(int64_t batch, int64_t M, int64_t N, int64_t K, const float *A,
+                                    const float *A_lo, int64_t lda, int64_t strideA, int transA,
+                                    const float *B, const float *B_lo, int64_t ldb, int64_t strideB,
+                                    int transB, const fz_program *epi, const fz_epi_input *inputs,
+                                    float *const *outputs, int64_t ldc, int64_t strideC,
+                                    void *stream) {
+  FZ_REQUIRE(epi, "fz_gemm_f32_epilogue: null program");
+  Epilogue E{epi, inputs, outputs};
+  return gemm_impl(batch, M, N, K, A, A_lo, lda, strideA, transA, B, B_lo, ldb, strideB, transB,
+                   nullptr, ldc, strideC, E, stream);
+}
+
+extern "C" int fz_gemm_epilogue_compile(const fz_program *epi, const fz_epi_input *inputs,
+                                        int a_mn, int b_mn, int tile_n, int pair) {
+  FZ_REQUIRE(epi, "fz_gemm_epilogue_compile: null program");
+  int rc = fz::validate_program(*epi);
+  if (rc) return rc;
+  FZ_REQUIRE(epi->num_leaves >= 1 && epi->num_leaves <= 1 + EPI_MAX_IN &&
+                 epi->num_outputs <= EPI_MAX_OUT && (epi->num_leaves == 1 || inputs),
+             "fz_gemm_epilogue_compile: bad program");
+  FZ_REQUIRE(pair ? tile_n == BN : (tile_n == 16 || tile_n == 64 || tile_n == BN),
+             "fz_gemm_epilogue_compile: tile width must be 16, 64 or 256 (256 for pairs)");
+  FZ_REQUIRE(tile_n == BN || !b_mn, "fz_gemm_epilogue_compile: narrow tiles read B K-major");
+  int cls[EPI_MAX_IN] = {};
+  for (int k = 0; k + 1 < epi->num_leaves; ++k) cls[k] = inputs[k].col_stride == 1;
+  std::vector<char> bin;
+  std::string lowered;
+  const std::string name = epilogue_kernel_name(a_mn != 0, b_mn != 0, tile_n, pair != 0);
+  return fz::nvrtc_cubin(epilogue_source(*epi, cls), "fz_gemm_epilogue.cu", name.c_str(), &bin, &lowered);
 }
 
 extern "C" int fz_tf32_lo(float *lo, const float *x, int64_t n, void *stream) {

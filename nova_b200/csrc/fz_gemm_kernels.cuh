@@ -1,0 +1,826 @@
+// Device code of the 3xTF32 GEMM kernels (tcgen05 + TMEM + TMA, sm_100a), shared by
+// the ahead-of-time build and by runtime compilation with a fused epilogue.
+//
+// The kernels are templates over an epilogue class EPI whose
+//   template <int CPW> static void store(args, ep, ks, bz, row, col0, acc)
+// receives, per epilogue thread, one output row's CPW consecutive accumulator
+// columns [col0, col0 + CPW) in registers and writes them out. StoreEpi stores the
+// product (the library's ahead-of-time instances). A fused elementwise program over
+// the product is compiled by NVRTC into a generated epilogue class, with this file's
+// text (embedded in the library) as the kernel source, so the program's outputs are
+// written straight from the accumulators.
+#pragma once
+
+#ifdef __CUDACC_RTC__
+typedef unsigned char uint8_t;
+typedef unsigned int uint32_t;
+typedef int int32_t;
+typedef unsigned long long uint64_t;
+typedef long long int64_t;
+typedef unsigned long long uintptr_t;
+// layout of the driver's CUtensorMap (128 opaque bytes, 64-byte aligned)
+struct __align__(64) CUtensorMap {
+  unsigned long long opaque[16];
+};
+#else
+#include <cuda.h>
+
+#include <cstdint>
+#endif
+
+namespace fz_gemm_dev {
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+// k-tile: BK fp32 = one swizzle row (BK = 16 -> 64-byte swizzle, 4 stages of 48 KB;
+// BK = 32 -> 128-byte swizzle, 2 stages of 96 KB)
+#ifndef FZ_GEMM_BK
+#define FZ_GEMM_BK 16
+#endif
+constexpr int BK = FZ_GEMM_BK;
+constexpr int STAGES = BK == 16 ? 4 : 2;
+constexpr int SWIZZLE_BYTES = BK * 4;
+static_assert(BK == 16 || BK == 32, "BK must be 16 or 32");
+constexpr int UMMA_K = 8;  // K of one kind::tf32 MMA
+constexpr int MN_CHUNK = 32;              // MN-major tiles: M/N rows per 128-byte swizzle row
+constexpr int MN_CHUNK_BYTES = BK * 128;  // one such chunk of a stage tile (BK k-rows)
+constexpr int TILE_A_BYTES = BM * BK * 4;  // 16 KB
+constexpr int TILE_B_BYTES = BN * BK * 4;  // 32 KB
+constexpr int STAGE_BYTES = 2 * TILE_A_BYTES + 2 * TILE_B_BYTES;  // 96 KB
+constexpr int TMEM_COLS = 256;          // one accumulator buffer (BN fp32 columns)
+constexpr int KCHUNK = 16;              // k-tiles per promotion chunk (K = 256)
+constexpr int NUM_EPI_WARPS = 8;        // 2 per TMEM lane quarter
+constexpr int NUM_THREADS = 64 + 32 * NUM_EPI_WARPS;
+constexpr unsigned long long kWaitNs = 4000000000ull;  // 4 s per wait
+
+enum : int { kErrNone = 0, kErrTimeoutFull = 1, kErrTimeoutEmpty = 2, kErrTimeoutAcc = 3 };
+
+
+// ---------------------------------------------------------------- PTX helpers
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.b32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait: true on success, false when the deadline passed or another role
+// already reported an error.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (globaltimer() - t0 > kWaitNs) return false;
+  }
+}
+
+__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, uint64_t *bar,
+                                            int c0, int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
+__device__ __forceinline__ void prefetch_map(const CUtensorMap *map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+__device__ __forceinline__ void tma_load_4d(void *dst, const CUtensorMap *map, uint64_t *bar,
+                                            int c0, int c1, int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+
+// One operand's k-tile [row0, row0 + ROWS) x [k0, k0 + BK) into a stage tile.
+// K-major: one box {BK, ROWS}. MN-major: the tile is ROWS / 32 chunks of
+// MN_CHUNK_BYTES; a "wide" map (4D: 32 rows, K, chunk, batch) fetches all chunks in
+// one box, a narrow one (3D) one chunk per box. Rows past the operand's extent are
+// zero-filled by the TMA unit.
+template <bool MN, int ROWS>
+__device__ __forceinline__ void load_operand(uint8_t *dst, const CUtensorMap *map, uint64_t *bar,
+                                             int k0, int row0, int bz, bool wide) {
+  if constexpr (MN) {
+    if (wide) {
+      tma_load_4d(dst, map, bar, 0, k0, row0 / MN_CHUNK, bz);
+    } else {
+#pragma unroll
+      for (int j = 0; j < ROWS / MN_CHUNK; ++j)
+        tma_load_3d(dst + j * MN_CHUNK_BYTES, map, bar, row0 + j * MN_CHUNK, k0, bz);
+    }
+  } else {
+    tma_load_3d(dst, map, bar, k0, row0, bz);
+  }
+}
+
+// K-major shared-memory descriptor for rows of SWIZZLE_BYTES (one swizzle atom
+// row per tile row): 8-row groups 8*SWIZZLE_BYTES apart (SBO), LBO unused (1),
+// descriptor version 1 (bit 46), layout type at bits 61-63: 2 = SWIZZLE_128B,
+// 4 = SWIZZLE_64B.
+__device__ __forceinline__ uint64_t smem_desc_k(uint32_t addr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((addr >> 4) & 0x3fff);
+  d |= (uint64_t)1 << 16;
+  d |= (uint64_t)((8 * SWIZZLE_BYTES) >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)(SWIZZLE_BYTES == 128 ? 2 : 4) << 61;
+  return d;
+}
+
+// MN-major shared-memory descriptor. For 32-bit (TF32) operands the MN-major layout
+// is the 128-byte swizzle with 32-byte atomicity (layout type 1): 32-byte units of a
+// 128-byte row are permuted by the row index mod 4, in atoms of 4 k-rows x 128 bytes
+// (512 B). The tile is stored as chunks of 32 M/N rows, each BK k-rows of 128 bytes;
+// LBO = distance between the 32-wide M/N chunks (BK * 128 bytes), SBO = distance
+// between 4-row k atoms (512 bytes). The TMA writes this image with
+// CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B.
+__device__ __forceinline__ uint64_t smem_desc_mn(uint32_t addr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((addr >> 4) & 0x3fff);
+  d |= (uint64_t)(MN_CHUNK_BYTES >> 4) << 16;
+  d |= (uint64_t)(512 >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)1 << 61;
+  return d;
+}
+
+// Descriptor of k-step kk (UMMA_K wide) of a stage tile at `base`.
+template <bool MN>
+__device__ __forceinline__ uint64_t operand_desc(uint32_t base, int kk) {
+  if constexpr (MN) return smem_desc_mn(base + (uint32_t)kk * (UMMA_K * 128));  // 8 k-rows
+  else return smem_desc_k(base + (uint32_t)kk * (UMMA_K * 4));                  // 32 bytes
+}
+
+// kind::tf32 instruction descriptor: D = F32 (bits 4-5 = 1), A = B = TF32 (2),
+// A major at bit 15 and B major at bit 16 (0 = K-major, 1 = MN-major), N >> 3 at
+// bits 17-22, M >> 4 at bits 24-28.
+__host__ __device__ constexpr uint32_t make_idesc(int m, int n, bool a_mn, bool b_mn) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)a_mn << 15) | ((uint32_t)b_mn << 16) |
+         ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_tf32(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc,
+                                          uint32_t accum) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(a), "l"(b), "r"(idesc), "r"(accum)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t *bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+struct GemmArgs {
+  float *C;
+  int64_t ldc, strideC;
+  int64_t split_stride;  // floats between the partial outputs of consecutive K splits
+  int M, N, K, batch;
+  int tiles_m, tiles_n, num_tiles, group_m;  // num_tiles counts work units (tiles x K splits)
+  int splits, k_per_split;  // K is cut into `splits` ranges of k_per_split (multiple of BK)
+  int wide;                 // bits 0-3: map Ah, Al, Bh, Bl is a wide (4D) MN-major map
+  int *err;
+};
+
+// Operands of a fused epilogue program. Leaf 0 of the program is the product; leaf
+// k >= 1 reads in[k-1] at bz * in_sb + row * in_sm (+ col when the input varies
+// along the columns, a property compiled into the epilogue). Output k is written at
+// out[k] + bz * strideC + row * ldc + col. vec: every column-varying input and
+// every output allows 16-byte accesses at each row.
+constexpr int EPI_MAX_IN = 11;
+constexpr int EPI_MAX_OUT = 4;
+struct EpiParams {
+  const float *in[EPI_MAX_IN];
+  long long in_sb[EPI_MAX_IN], in_sm[EPI_MAX_IN];
+  float *out[EPI_MAX_OUT];
+  int vec;
+};
+
+// The plain epilogue: C = product (or this unit's K-split partial).
+struct StoreEpi {
+  template <int CPW>
+  static __device__ __forceinline__ void store(const GemmArgs &a, const EpiParams &, int ks, int bz,
+                                               int row, int col0, const float (&acc)[CPW]) {
+    if (row >= a.M || col0 >= a.N) return;
+    float *crow = a.C + (int64_t)ks * a.split_stride + (int64_t)bz * a.strideC +
+                  (int64_t)row * a.ldc + col0;
+    const bool vec = ((a.ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(a.C) & 15) == 0) &&
+                     ((a.strideC & 3) == 0);
+    if (vec && col0 + CPW <= a.N) {
+#pragma unroll
+      for (int i = 0; i < CPW; i += 4)
+        *reinterpret_cast<float4 *>(crow + i) = make_float4(acc[i], acc[i + 1], acc[i + 2], acc[i + 3]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < CPW; ++i)
+        if (col0 + i < a.N) crow[i] = acc[i];
+    }
+  }
+};
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Work unit t -> (K split, batch, m block, n block). Units of one K split are
+// consecutive; within a batch, bands of group_m row blocks are walked column by
+// column, so the units in flight on the 148 SMs share A rows and B columns in L2.
+__device__ __forceinline__ void decode_tile(int t, const GemmArgs &a, int &mb, int &nb, int &bz,
+                                            int &ks) {
+  const int per_batch = a.tiles_m * a.tiles_n;
+  const int per_split = per_batch * a.batch;  // units of one K split
+  ks = t / per_split;
+  t -= ks * per_split;
+  bz = t / per_batch;
+  const int r = t - bz * per_batch;
+  const int band = r / (a.group_m * a.tiles_n);
+  const int first_m = band * a.group_m;
+  const int rows = min(a.group_m, a.tiles_m - first_m);
+  const int in_band = r - band * a.group_m * a.tiles_n;
+  mb = first_m + in_band % rows;
+  nb = in_band / rows;
+}
+
+// k-tiles of unit `ks`: [ks * k_per_split, min(K, (ks + 1) * k_per_split)).
+__device__ __forceinline__ int unit_k_tiles(const GemmArgs &a, int ks, int &k_begin) {
+  k_begin = ks * a.k_per_split;
+  const int k_end = min(a.K, k_begin + a.k_per_split);
+  return (k_end - k_begin + BK - 1) / BK;
+}
+
+// Persistent kernel: one CTA per SM walks tiles blockIdx.x, +gridDim.x, ...
+// K is cut into chunks of KCHUNK k-tiles accumulated alternately in two TMEM
+// buffers; warps 2-9 fold each finished chunk into fp32 registers.
+// Per tile width TBN (output columns per tile): 256 for wide products, 64 or 16 for
+// narrow ones (a 16-wide output layer would otherwise compute 256 columns for 16).
+// Narrow tiles use more stages of smaller k-tiles, within the same ~192 KB.
+template <int TBN>
+struct TileCfg {
+  static constexpr int B_BYTES = TBN * BK * 4;
+  static constexpr int STAGE = 2 * TILE_A_BYTES + 2 * B_BYTES;
+  static constexpr int NSTAGE = TBN == BN ? STAGES : (192 * 1024) / STAGE;
+  static constexpr int TMEM = TBN < 32 ? 32 : TBN;  // TMEM columns per accumulator buffer
+  static constexpr int CPW = TBN / 2;               // columns per epilogue warp
+  static_assert(TBN == 256 || TBN == 64 || TBN == 16, "tile width");
+};
+
+// Add CPW accumulator columns of this warp's TMEM lanes, from `taddr`, into acc.
+template <int CPW>
+__device__ __forceinline__ void promote_cols(uint32_t taddr, float (&acc)[CPW]) {
+  if constexpr (CPW >= 32) {
+#pragma unroll
+    for (int c0 = 0; c0 < CPW; c0 += 32) {
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(taddr + (uint32_t)c0, r);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) acc[c0 + i] = __fadd_rn(acc[c0 + i], __uint_as_float(r[i]));
+    }
+  } else {
+    static_assert(CPW == 8, "columns per warp");
+    uint32_t r[8];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] = __fadd_rn(acc[i], __uint_as_float(r[i]));
+  }
+}
+
+// A_MN / B_MN: the operand is MN-major in global and shared memory (B is K-major
+// whenever TBN < 256).
+template <bool A_MN, bool B_MN, int TBN, class EPI>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap mapAh,
+                       const __grid_constant__ CUtensorMap mapAl,
+                       const __grid_constant__ CUtensorMap mapBh,
+                       const __grid_constant__ CUtensorMap mapBl, GemmArgs args,
+                       const __grid_constant__ EpiParams ep) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  using T = TileCfg<TBN>;
+  constexpr int STAGES = T::NSTAGE;
+  constexpr int STAGE_BYTES = T::STAGE;
+  constexpr int TILE_B_BYTES = T::B_BYTES;
+  constexpr int TMEM_COLS = T::TMEM;
+  constexpr int CPW = T::CPW;
+  static_assert(TBN == BN || !B_MN, "narrow tiles read B K-major");
+  __shared__ __align__(8) uint64_t full_bar[STAGES];
+  __shared__ __align__(8) uint64_t empty_bar[STAGES];
+  __shared__ __align__(8) uint64_t acc_full[2];
+  __shared__ __align__(8) uint64_t acc_empty[2];
+  __shared__ uint32_t tmem_base_slot;
+  __shared__ volatile int abort_flag;
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  constexpr uint32_t kIdesc = make_idesc(BM, TBN, A_MN, B_MN);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 32 * NUM_EPI_WARPS);  // every epilogue thread arrives
+    }
+    abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    prefetch_map(&mapAh);
+    prefetch_map(&mapAl);
+    prefetch_map(&mapBh);
+    prefetch_map(&mapBl);
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(&tmem_base_slot)),
+                 "r"(2 * TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem_base = tmem_base_slot;
+
+  auto stage_ptr = [&](int s, int which) -> uint8_t * {
+    uint8_t *base = smem + (size_t)s * STAGE_BYTES;
+    switch (which) {
+      case 0: return base;
+      case 1: return base + TILE_A_BYTES;
+      case 2: return base + 2 * TILE_A_BYTES;
+      default: return base + 2 * TILE_A_BYTES + TILE_B_BYTES;
+    }
+  };
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------ TMA producer
+      int it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < args.num_tiles; t += gridDim.x) {
+        int mb, nb, bz, ks, kb;
+        decode_tile(t, args, mb, nb, bz, ks);
+        const int nk = unit_k_tiles(args, ks, kb);
+        for (int kt = 0; kt < nk; ++kt, ++it) {
+          const int s = it % STAGES;
+          const uint32_t round = it / STAGES;
+          if (it >= STAGES && !mbar_wait(&empty_bar[s], (round - 1) & 1, &abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(&full_bar[s], STAGE_BYTES);
+          const int k0 = kb + kt * BK;
+          load_operand<A_MN, BM>(stage_ptr(s, 0), &mapAh, &full_bar[s], k0, mb * BM, bz, args.wide & 1);
+          load_operand<A_MN, BM>(stage_ptr(s, 1), &mapAl, &full_bar[s], k0, mb * BM, bz, args.wide & 2);
+          load_operand<B_MN, TBN>(stage_ptr(s, 2), &mapBh, &full_bar[s], k0, nb * TBN, bz, args.wide & 4);
+          load_operand<B_MN, TBN>(stage_ptr(s, 3), &mapBl, &full_bar[s], k0, nb * TBN, bz, args.wide & 8);
+        }
+      }
+      if (!ok) {
+        atomicCAS(args.err, kErrNone, kErrTimeoutEmpty);
+        abort_flag = 1;
+        // drain: wait (bounded) for the loads of the last STAGES issued k-tiles
+        for (int i = (it > STAGES ? it - STAGES : 0); i < it; ++i) {
+          const int s = i % STAGES;
+          const uint64_t t0 = globaltimer();
+          while (!mbar_try_wait(&full_bar[s], (i / STAGES) & 1) && globaltimer() - t0 < kWaitNs) {
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------------------------------ MMA issuer
+      int it = 0, cc = 0;  // k-tile and chunk counters, running across tiles
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < args.num_tiles; t += gridDim.x) {
+        int mb, nb, bz, ks, kb;
+        decode_tile(t, args, mb, nb, bz, ks);
+        const int num_k = unit_k_tiles(args, ks, kb);
+        for (int kt0 = 0; ok && kt0 < num_k; kt0 += KCHUNK, ++cc) {
+          const int b = cc & 1;
+          if (cc >= 2 && !mbar_wait(&acc_empty[b], ((cc >> 1) - 1) & 1, &abort_flag)) {
+            ok = false;
+            break;
+          }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const uint32_t d_tmem = tmem_base + (uint32_t)(b * TMEM_COLS);
+          const int kend = kt0 + KCHUNK < num_k ? kt0 + KCHUNK : num_k;
+          for (int kt = kt0; kt < kend; ++kt, ++it) {
+            const int s = it % STAGES;
+            if (!mbar_wait(&full_bar[s], (it / STAGES) & 1, &abort_flag)) {
+              ok = false;
+              break;
+            }
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const uint32_t a_hi = smem_u32(stage_ptr(s, 0)), a_lo = smem_u32(stage_ptr(s, 1));
+            const uint32_t b_hi = smem_u32(stage_ptr(s, 2)), b_lo = smem_u32(stage_ptr(s, 3));
+#pragma unroll
+            for (int kk = 0; kk < BK / UMMA_K; ++kk) {
+              const uint64_t dah = operand_desc<A_MN>(a_hi, kk), dal = operand_desc<A_MN>(a_lo, kk);
+              const uint64_t dbh = operand_desc<B_MN>(b_hi, kk), dbl = operand_desc<B_MN>(b_lo, kk);
+              const uint32_t first = (kt == kt0 && kk == 0) ? 0u : 1u;
+              umma_tf32(d_tmem, dal, dbh, kIdesc, first);  // lo * hi
+              umma_tf32(d_tmem, dah, dbl, kIdesc, 1u);     // hi * lo
+              umma_tf32(d_tmem, dah, dbh, kIdesc, 1u);     // hi * hi (largest term last)
+            }
+            umma_commit(&empty_bar[s]);
+          }
+          if (ok) umma_commit(&acc_full[b]);
+        }
+      }
+      if (!ok) {
+        atomicCAS(args.err, kErrNone, kErrTimeoutFull);
+        abort_flag = 1;
+      }
+    }
+  } else {
+    // ------------------------------------------------------ promotion + epilogue (warps 2..9)
+    const int q = warp & 3;             // TMEM lane quarter this warp may access
+    const int half = (warp - 2) >> 2;   // which half of the tile's columns
+    int cc = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; ok && t < args.num_tiles; t += gridDim.x) {
+      int mb, nb, bz, ks, kb;
+      decode_tile(t, args, mb, nb, bz, ks);
+      const int num_k = unit_k_tiles(args, ks, kb);
+      float acc[CPW];
+#pragma unroll
+      for (int i = 0; i < CPW; ++i) acc[i] = 0.0f;
+      for (int kt0 = 0; kt0 < num_k; kt0 += KCHUNK, ++cc) {
+        const int b = cc & 1;
+        if (!mbar_wait(&acc_full[b], (cc >> 1) & 1, &abort_flag)) {
+          if (lane == 0) atomicCAS(args.err, kErrNone, kErrTimeoutAcc);
+          abort_flag = 1;
+          ok = false;
+          break;
+        }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t taddr = tmem_base + (uint32_t)(b * TMEM_COLS + half * CPW) +
+                               ((uint32_t)(q * 32) << 16);
+        promote_cols<CPW>(taddr, acc);
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        mbar_arrive(&acc_empty[b]);
+      }
+      if (!ok) break;
+      EPI::template store<CPW>(args, ep, ks, bz, mb * BM + q * 32 + lane, nb * TBN + half * CPW, acc);
+    }
+  }
+
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 1) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                 "r"(2 * TMEM_COLS)
+                 : "memory");
+  }
+}
+
+// ---------------------------------------------------------------- 2-SM (CTA pair) variant
+//
+// A cluster of two CTAs computes a 256 x 256 output tile with
+// tcgen05.mma.cta_group::2: each CTA holds 128 rows of A and 128 rows (N) of B per
+// stage, the leader CTA (rank 0) issues the MMAs, the tensor cores read the peer's
+// half of each operand from its shared memory, and each CTA's TMEM receives its 128
+// rows x 256 columns. Per MMA a CTA reads half of B from its own shared memory
+// instead of all of it, and loads a third fewer bytes per k-tile: less shared-memory
+// and L2 traffic, and energy, per product. Protocol: both CTAs' TMA loads complete
+// their bytes on the leader's full barrier (which the leader's producer armed for the
+// pair's bytes); the leader's commits multicast to both CTAs' empty and acc_full
+// barriers; the peer's epilogue threads arrive on the leader's acc_empty barriers.
+// TMEM is allocated and freed with cta_group::2 by warp 1 of both CTAs. Every wait is
+// bounded as in the single-CTA kernel, and both CTAs meet at a cluster barrier before
+// freeing TMEM and exiting.
+constexpr int PAIR_STAGES = 6;
+constexpr int PAIR_TILE_BYTES = BM * BK * 4;             // 128 rows of A or B: 8 KB
+constexpr int PAIR_STAGE_BYTES = 4 * PAIR_TILE_BYTES;    // A_hi, A_lo, B_hi, B_lo: 32 KB
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                   : "memory");
+}
+
+// Shared-memory address of the same variable in the cluster's CTA 0.
+__device__ __forceinline__ uint32_t in_leader(const void *p) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, 0;" : "=r"(r) : "r"(smem_u32(p)));
+  return r;
+}
+
+__device__ __forceinline__ void tma_load_3d_pair(void *dst, const CUtensorMap *map, uint32_t bar,
+                                                 int c0, int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_4d_pair(void *dst, const CUtensorMap *map, uint32_t bar,
+                                                 int c0, int c1, int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+
+// load_operand for a CTA of a pair: 128 rows, bytes completed on the leader's barrier.
+template <bool MN>
+__device__ __forceinline__ void load_operand_pair(uint8_t *dst, const CUtensorMap *map, uint32_t bar,
+                                                  int k0, int row0, int bz, bool wide) {
+  if constexpr (MN) {
+    if (wide) {
+      tma_load_4d_pair(dst, map, bar, 0, k0, row0 / MN_CHUNK, bz);
+    } else {
+#pragma unroll
+      for (int j = 0; j < BM / MN_CHUNK; ++j)
+        tma_load_3d_pair(dst + j * MN_CHUNK_BYTES, map, bar, row0 + j * MN_CHUNK, k0, bz);
+    }
+  } else {
+    tma_load_3d_pair(dst, map, bar, k0, row0, bz);
+  }
+}
+
+__device__ __forceinline__ void umma_tf32_pair(uint32_t tmem_d, uint64_t a, uint64_t b,
+                                               uint32_t idesc, uint32_t accum) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(a), "l"(b), "r"(idesc), "r"(accum)
+      : "memory");
+}
+
+// Arrive on the barrier at this offset in both CTAs of the pair when the MMAs issued
+// so far have completed.
+__device__ __forceinline__ void umma_commit_pair(uint64_t *bar) {
+  asm volatile(
+      "{\n\t.reg .b16 m;\n\tmov.b16 m, 3;\n\t"
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], m;\n\t}" ::"r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+               : "memory");
+}
+
+template <bool A_MN, bool B_MN, class EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap mapAh,
+                     const __grid_constant__ CUtensorMap mapAl,
+                     const __grid_constant__ CUtensorMap mapBh,
+                     const __grid_constant__ CUtensorMap mapBl, GemmArgs args,
+                     const __grid_constant__ EpiParams ep) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  __shared__ __align__(8) uint64_t full_bar[PAIR_STAGES];
+  __shared__ __align__(8) uint64_t empty_bar[PAIR_STAGES];
+  __shared__ __align__(8) uint64_t acc_full[2];
+  __shared__ __align__(8) uint64_t acc_empty[2];
+  __shared__ uint32_t tmem_base_slot;
+  __shared__ volatile int abort_flag;
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  constexpr uint32_t kIdesc = make_idesc(2 * BM, BN, A_MN, B_MN);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < PAIR_STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 2 * 32 * NUM_EPI_WARPS);  // both CTAs' epilogue threads
+    }
+    abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    prefetch_map(&mapAh);
+    prefetch_map(&mapAl);
+    prefetch_map(&mapBh);
+    prefetch_map(&mapBl);
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(&tmem_base_slot)),
+                 "r"(2 * TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  cluster_sync_all();  // both CTAs' barriers initialised and TMEM allocated
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem_base = tmem_base_slot;
+
+  auto stage_ptr = [&](int s, int which) -> uint8_t * {
+    return smem + (size_t)s * PAIR_STAGE_BYTES + (size_t)which * PAIR_TILE_BYTES;
+  };
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------ TMA producer (both CTAs)
+      int it = 0;
+      bool ok = true;
+      for (int t = pair; ok && t < args.num_tiles; t += npairs) {
+        int mb, nb, bz, ks, kb;
+        decode_tile(t, args, mb, nb, bz, ks);
+        const int nk = unit_k_tiles(args, ks, kb);
+        const int row_a = mb * 2 * BM + (int)rank * BM, row_b = nb * BN + (int)rank * BM;
+        for (int kt = 0; kt < nk; ++kt, ++it) {
+          const int s = it % PAIR_STAGES;
+          const uint32_t round = it / PAIR_STAGES;
+          if (it >= PAIR_STAGES && !mbar_wait(&empty_bar[s], (round - 1) & 1, &abort_flag)) {
+            ok = false;
+            break;
+          }
+          if (leader) mbar_expect_tx(&full_bar[s], 2 * PAIR_STAGE_BYTES);
+          const uint32_t fb = in_leader(&full_bar[s]);
+          const int k0 = kb + kt * BK;
+          load_operand_pair<A_MN>(stage_ptr(s, 0), &mapAh, fb, k0, row_a, bz, args.wide & 1);
+          load_operand_pair<A_MN>(stage_ptr(s, 1), &mapAl, fb, k0, row_a, bz, args.wide & 2);
+          load_operand_pair<B_MN>(stage_ptr(s, 2), &mapBh, fb, k0, row_b, bz, args.wide & 4);
+          load_operand_pair<B_MN>(stage_ptr(s, 3), &mapBl, fb, k0, row_b, bz, args.wide & 8);
+        }
+      }
+      if (!ok) {
+        atomicCAS(args.err, kErrNone, kErrTimeoutEmpty);
+        abort_flag = 1;
+        if (leader) {  // drain (bounded): the last PAIR_STAGES k-tiles' loads of the pair
+          for (int i = (it > PAIR_STAGES ? it - PAIR_STAGES : 0); i < it; ++i) {
+            const int s = i % PAIR_STAGES;
+            const uint64_t t0 = globaltimer();
+            while (!mbar_try_wait(&full_bar[s], (i / PAIR_STAGES) & 1) && globaltimer() - t0 < kWaitNs) {
+            }
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      // ------------------------------------------------------ MMA issuer (leader only)
+      int it = 0, cc = 0;
+      bool ok = true;
+      for (int t = pair; ok && t < args.num_tiles; t += npairs) {
+        int mb, nb, bz, ks, kb;
+        decode_tile(t, args, mb, nb, bz, ks);
+        const int num_k = unit_k_tiles(args, ks, kb);
+        for (int kt0 = 0; ok && kt0 < num_k; kt0 += KCHUNK, ++cc) {
+          const int b = cc & 1;
+          if (cc >= 2 && !mbar_wait(&acc_empty[b], ((cc >> 1) - 1) & 1, &abort_flag)) {
+            ok = false;
+            break;
+          }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const uint32_t d_tmem = tmem_base + (uint32_t)(b * TMEM_COLS);
+          const int kend = kt0 + KCHUNK < num_k ? kt0 + KCHUNK : num_k;
+          for (int kt = kt0; kt < kend; ++kt, ++it) {
+            const int s = it % PAIR_STAGES;
+            if (!mbar_wait(&full_bar[s], (it / PAIR_STAGES) & 1, &abort_flag)) {
+              ok = false;
+              break;
+            }
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const uint32_t a_hi = smem_u32(stage_ptr(s, 0)), a_lo = smem_u32(stage_ptr(s, 1));
+            const uint32_t b_hi = smem_u32(stage_ptr(s, 2)), b_lo = smem_u32(stage_ptr(s, 3));
+#pragma unroll
+            for (int kk = 0; kk < BK / UMMA_K; ++kk) {
+              const uint64_t dah = operand_desc<A_MN>(a_hi, kk), dal = operand_desc<A_MN>(a_lo, kk);
+              const uint64_t dbh = operand_desc<B_MN>(b_hi, kk), dbl = operand_desc<B_MN>(b_lo, kk);
+              const uint32_t first = (kt == kt0 && kk == 0) ? 0u : 1u;
+              umma_tf32_pair(d_tmem, dal, dbh, kIdesc, first);  // lo * hi
+              umma_tf32_pair(d_tmem, dah, dbl, kIdesc, 1u);     // hi * lo
+              umma_tf32_pair(d_tmem, dah, dbh, kIdesc, 1u);     // hi * hi
+            }
+            umma_commit_pair(&empty_bar[s]);
+          }
+          if (ok) umma_commit_pair(&acc_full[b]);
+        }
+      }
+      if (!ok) {
+        atomicCAS(args.err, kErrNone, kErrTimeoutFull);
+        abort_flag = 1;
+      }
+    }
+  } else {
+    // ------------------------------------------------------ promotion + epilogue (warps 2..9)
+    const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const uint32_t acc_empty_leader[2] = {in_leader(&acc_empty[0]), in_leader(&acc_empty[1])};
+    int cc = 0;
+    bool ok = true;
+    for (int t = pair; ok && t < args.num_tiles; t += npairs) {
+      int mb, nb, bz, ks, kb;
+      decode_tile(t, args, mb, nb, bz, ks);
+      const int num_k = unit_k_tiles(args, ks, kb);
+      float acc[128];
+#pragma unroll
+      for (int i = 0; i < 128; ++i) acc[i] = 0.0f;
+      for (int kt0 = 0; kt0 < num_k; kt0 += KCHUNK, ++cc) {
+        const int b = cc & 1;
+        if (!mbar_wait(&acc_full[b], (cc >> 1) & 1, &abort_flag)) {
+          if (lane == 0) atomicCAS(args.err, kErrNone, kErrTimeoutAcc);
+          abort_flag = 1;
+          ok = false;
+          break;
+        }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t taddr = tmem_base + (uint32_t)(b * TMEM_COLS + half * 128) +
+                               ((uint32_t)(q * 32) << 16);
+#pragma unroll
+        for (int c0 = 0; c0 < 128; c0 += 32) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(taddr + (uint32_t)c0, r);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) acc[c0 + i] = __fadd_rn(acc[c0 + i], __uint_as_float(r[i]));
+        }
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        if (leader) mbar_arrive(&acc_empty[b]);
+        else mbar_arrive_remote(acc_empty_leader[b]);
+      }
+      if (!ok) break;
+      EPI::template store<128>(args, ep, ks, bz, mb * 2 * BM + (int)rank * BM + q * 32 + lane,
+                               nb * BN + half * 128, acc);
+    }
+  }
+
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  cluster_sync_all();  // neither CTA frees TMEM or exits while the pair may still use it
+  if (warp == 1) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                 "r"(2 * TMEM_COLS)
+                 : "memory");
+  }
+}
+
+
+}  // namespace fz_gemm_dev

@@ -323,6 +323,10 @@ BackwardResult Engine::backward(ValueID seed) {
                                ": " + e.what());
     }
     FB_CHECK(gin.size() == n.inputs.size(), "backward arity mismatch");
+    // An intermediate value's gradient is read by this node alone (its producer) and
+    // never returned: drop it, so a pending product inside it is not kept alive (and
+    // stored) only for this table.
+    if (out != seed && produced_by_[out] != -1 && !requires_grad_set_.count(out)) grad_[out] = RawTensor();
     // Both operands are leaves that require grad (their gradients are final values):
     // lower the two pending gradients together, one pass over the shared upstream
     // gradient and operands (e.g. Multiply: g0*y and g0*x read g0, x, y once).

@@ -70,6 +70,11 @@ struct Comm {
     std::optional<RawTensor> sent;  // the reduced values, kept alive until collect()
   };
   std::vector<Watched> watched;
+  // Gradients announced while still pending, reduced at the next announcement (or in
+  // collect()): by then the backward has usually lowered them as part of a larger
+  // program (a bias gradient is the operand of the next GEMMs), where reducing at once
+  // would force its pending product to be computed on its own first.
+  std::vector<std::pair<Watched *, RawTensor>> deferred;
   int overlapped = 0;  // gradients the last backward handed over while it ran
   Comm(int w, int r, py::bytes uid) : world(w), rank(r) {
     std::string id = uid;
@@ -79,6 +84,7 @@ struct Comm {
   ~Comm() { destroy(); }
   void destroy() {
     if (!watched.empty()) set_grad_ready_hook({});
+    deferred.clear();
     watched.clear();
     if (c) fz_comm_destroy(c);
     c = nullptr;
@@ -109,16 +115,27 @@ struct Comm {
     if (!side) fz_check(fz_stream_create(&side), "fz_stream_create");
     watched.clear();
     for (ADTensor *p : params) watched.push_back(Watched{p, p->has_vid() ? p->vid() : -1, {}, {}});
+    deferred.clear();
     set_grad_ready_hook([this](ValueID v, const RawTensor &g) {
+      flush_deferred();
       for (Watched &w : watched)
-        if (w.vid == v && w.vid >= 0 && !w.avg) reduce_into(w, g);
+        if (w.vid == v && w.vid >= 0 && !w.avg) {
+          if (g.pending()) deferred.emplace_back(&w, g);
+          else reduce_into(w, g);
+        }
     });
+  }
+  void flush_deferred() {
+    for (auto &d : deferred)
+      if (!d.first->avg) reduce_into(*d.first, d.second);
+    deferred.clear();
   }
   // The averaged gradients of the watched parameters (None where a parameter got no
   // gradient). Gradients the backward did not announce are reduced here, in parameter
   // order. The thread's stream then waits for the side stream.
   std::vector<py::object> collect() {
     set_grad_ready_hook({});
+    flush_deferred();
     overlapped = 0;
     for (Watched &w : watched) overlapped += w.avg ? 1 : 0;
     for (Watched &w : watched)
@@ -353,6 +370,10 @@ PYBIND11_MODULE(fusion, m) {
   m.def("set_split_cache", &set_split_cache_enabled, py::arg("enabled"),
         "Keep GEMM operands' TF32 remainder planes with their buffers (default on).");
   m.def("split_cache_enabled", &split_cache_enabled);
+  m.def("set_gemm_epilogue", &set_gemm_epilogue_enabled, py::arg("enabled"),
+        "Defer each GEMM so the elementwise program reading its product runs in the GEMM's "
+        "epilogue (default on); off launches every GEMM where it is called.");
+  m.def("gemm_epilogue_enabled", &gemm_epilogue_enabled);
   m.def("empty_cache", []() { fz_check(fz_pool_release(), "fz_pool_release"); },
         "Return this device's cached blocks to the driver (synchronises the device).");
   m.def("flush", [](const T &t) {
@@ -365,6 +386,7 @@ PYBIND11_MODULE(fusion, m) {
     py::dict d;
     d["kernel_launches"] = fz_launch_count();
     d["fused_launches"] = fused_launches();
+    d["epilogue_gemms"] = epilogue_gemms();
     d["fused_kernels_compiled"] = fz_fused_cache_size();
     size_t r = 0, u = 0;
     if (fz_pool_stats(&r, &u) == FZ_OK) {

@@ -6,6 +6,7 @@
 #include <numeric>
 #include <sstream>
 #include <unordered_map>
+#include <unordered_set>
 
 namespace fusion_b200 {
 
@@ -102,6 +103,11 @@ static bool g_fusion = true;
 static bool g_split_cache = true;
 void set_split_cache_enabled(bool on) { g_split_cache = on; }
 bool split_cache_enabled() { return g_split_cache; }
+static bool g_gemm_epilogue = true;
+void set_gemm_epilogue_enabled(bool on) { g_gemm_epilogue = on; }
+bool gemm_epilogue_enabled() { return g_gemm_epilogue; }
+static int64_t g_epilogue_gemms = 0;
+int64_t epilogue_gemms() { return g_epilogue_gemms; }
 static int64_t g_fused_launches = 0;
 constexpr int kNodeLimit = 40;   // below FZ_MAX_NODES, leaving room for dedupe slack
 constexpr int kLeafLimit = 10;   // below FZ_MAX_LEAVES
@@ -168,6 +174,8 @@ static void operand_strides(const std::vector<size_t> &s, const std::vector<size
   }
 }
 
+static void lower_gemm(Expr *e);
+
 namespace {
 struct Lowering {
   fz_program prog{};
@@ -175,6 +183,10 @@ struct Lowering {
   std::vector<const Expr *> leaves;
   std::unordered_map<const float *, int> leaf_of_buf;  // dedupe equal buffers of equal shape
   bool overflow = false;
+  const Expr *acc = nullptr;  // epilogue programs: the pending GEMM read as leaf 0
+
+  Lowering() = default;
+  explicit Lowering(const Expr *product) : acc(product) { leaves.push_back(product); }
 
   int leaf_index(const Expr *e) {
     auto it = leaf_of_buf.find(e->buf->ptr);
@@ -191,6 +203,9 @@ struct Lowering {
   // Returns an operand reference (>= 0 node, < 0 leaf).
   int visit(const Expr *e) {
     if (overflow) return 0;
+    if (e == acc) return -1;
+    // any other pending GEMM is a plain product read as a leaf
+    if (e->kind == Expr::Gemm) lower_gemm(const_cast<Expr *>(e));
     if (e->kind == Expr::Leaf) return -1 - leaf_index(e);
     auto it = node_of.find(e);
     if (it != node_of.end()) return it->second;
@@ -333,9 +348,218 @@ static void reduce_view(const Expr &e, int64_t &outer, int64_t &len, int64_t &in
   }
 }
 
+// A pending GEMM lowered by itself: the product into a buffer.
+static void lower_gemm(Expr *e) {
+  const GemmSpec &g = *e->gemm;
+  auto out = std::make_shared<DeviceBuffer>(e->numel());
+  fz_check(fz_gemm_f32_split(g.batch, g.M, g.N, g.K, g.pa, g.la, g.lda, g.sA, g.transA, g.pb,
+                             g.lb, g.ldb, g.sB, g.transB, out->ptr, g.N, g.M * g.N, nullptr),
+           "fz_gemm_f32_split");
+  e->kind = Expr::Leaf;
+  e->buf = std::move(out);
+  e->gemm.reset();
+  e->nodes_ub = 0;
+  e->leaves_ub = 1;
+}
+
+namespace {
+// The DAG under a set of roots, as the epilogue lowering needs it.
+struct EpiScan {
+  std::unordered_set<const Expr *> seen, roots;
+  std::unordered_map<const Expr *, int> in_edges;           // parent edges inside the DAG
+  std::unordered_map<const Expr *, const ExprPtr *> owner;  // a parent's pointer to the node
+  std::vector<const Expr *> ops;                            // Unary / Binary nodes
+  const Expr *gemm = nullptr;
+  int gemms = 0;
+  bool ok = true;
+
+  void scan(const Expr *e, const ExprPtr *from) {
+    if (from) {
+      ++in_edges[e];
+      owner.emplace(e, from);
+    }
+    if (!seen.insert(e).second) return;
+    switch (e->kind) {
+      case Expr::Leaf:
+      case Expr::Const: return;
+      case Expr::Reduce: ok = false; return;
+      case Expr::Gemm:
+        gemm = e;
+        ++gemms;
+        return;
+      case Expr::Unary:
+        ops.push_back(e);
+        scan(e->a.get(), &e->a);
+        return;
+      case Expr::Binary:
+        ops.push_back(e);
+        scan(e->a.get(), &e->a);
+        scan(e->b.get(), &e->b);
+        return;
+    }
+  }
+  // References to e from outside the DAG (tensors, saved contexts, other programs).
+  long external(const Expr *e) const {
+    auto it = owner.find(e);
+    if (it == owner.end()) return 1;
+    auto jt = in_edges.find(e);
+    return it->second->use_count() - (jt == in_edges.end() ? 0 : jt->second);
+  }
+};
+
+bool reaches(const Expr *e, const Expr *target, std::unordered_map<const Expr *, bool> &memo) {
+  if (e == target) return true;
+  if (e->kind != Expr::Unary && e->kind != Expr::Binary) return false;
+  auto it = memo.find(e);
+  if (it != memo.end()) return it->second;
+  bool r = reaches(e->a.get(), target, memo) || (e->kind == Expr::Binary && reaches(e->b.get(), target, memo));
+  memo[e] = r;
+  return r;
+}
+
+// How an input of shape `s` reads from the product's [batch..., M, N] index space:
+// strides along the (flattened) batch, the rows and the columns. False when the batch
+// dims do not flatten into one stride.
+bool epilogue_input(const std::vector<size_t> &s, const std::vector<size_t> &out, const float *ptr,
+                    fz_epi_input *in) {
+  const size_t nd = out.size();
+  if (s.size() > nd || nd < 2) return false;
+  int64_t st[64];
+  if (nd > 64) return false;
+  operand_strides(s, out, st);
+  in->ptr = ptr;
+  in->col_stride = st[nd - 1];
+  in->row_stride = st[nd - 2];
+  if (in->col_stride != 0 && in->col_stride != 1) return false;
+  // batch offset = bz * batch_stride for the flat batch index bz
+  int64_t sb = 0, inner = 1;
+  bool have = false;
+  for (long d = (long)nd - 3; d >= 0; --d) {
+    if (out[d] == 1) continue;
+    if (!have) {
+      sb = st[d];
+      have = true;
+    } else if (st[d] != sb * inner) {
+      return false;
+    }
+    inner *= (int64_t)out[d];
+  }
+  in->batch_stride = sb;
+  return true;
+}
+}  // namespace
+
+// Lower pending nodes that read exactly one pending GEMM (and leaves broadcast into its
+// product as rows, columns or batch slices) as the outputs of that GEMM's epilogue:
+// one kernel writes every root (and, for roots with want_lo, its TF32 remainder plane)
+// straight from the accumulators. The product is stored as well only when something
+// outside these roots still holds the GEMM node. Returns false, having done nothing,
+// when the roots do not qualify.
+static bool try_epilogue(const std::vector<ExprPtr> &roots, const std::vector<bool> &want_lo) {
+  if (!g_gemm_epilogue || !g_fusion || roots.empty()) return false;
+  EpiScan S;
+  for (const ExprPtr &r : roots) S.roots.insert(r.get());
+  for (const ExprPtr &r : roots) S.scan(r.get(), nullptr);
+  if (!S.ok || S.gemms != 1) return false;
+  Expr *G = const_cast<Expr *>(S.gemm);
+  const std::vector<size_t> &oshape = G->shape;
+  for (const ExprPtr &r : roots)
+    if (r->shape != oshape) return false;
+  const bool g_root = S.roots.count(G) > 0;
+  bool g_needed = false;
+  if (!g_root) {
+    g_needed = S.external(G) > 0;
+    std::unordered_map<const Expr *, bool> memo;
+    for (const Expr *x : S.ops)
+      if (!g_needed && !S.roots.count(x) && S.external(x) > 0 && reaches(x, G, memo)) g_needed = true;
+  }
+  Lowering L(G);
+  std::vector<int> refs;
+  for (const ExprPtr &r : roots) refs.push_back(L.visit(r.get()));
+  if (L.overflow) return false;
+  auto add_node = [&](int kind, int op, int src) {
+    if (L.prog.num_nodes >= FZ_MAX_NODES) return -1;
+    fz_node &n = L.prog.nodes[L.prog.num_nodes];
+    n.kind = kind;
+    n.op = op;
+    n.src0 = src;
+    n.src1 = 0;
+    n.imm = 0.0f;
+    return L.prog.num_nodes++;
+  };
+  std::vector<int> outs;
+  for (int &r : refs) {
+    if (r < 0) r = add_node(FZ_NODE_UNARY, FZ_COPY, r);  // a root that is the product itself
+    if (r < 0) return false;
+    outs.push_back(r);
+  }
+  int nlo = 0;
+  for (size_t k = 0; k < roots.size(); ++k)
+    if (want_lo[k]) {
+      const int n = add_node(FZ_NODE_UNARY, FZ_TF32_LO, refs[k]);
+      if (n < 0) return false;
+      outs.push_back(n);
+      ++nlo;
+    }
+  if (g_needed) {
+    const int n = add_node(FZ_NODE_UNARY, FZ_COPY, -1);
+    if (n < 0) return false;
+    outs.push_back(n);
+  }
+  if ((int)outs.size() > FZ_MAX_OUTPUTS) return false;
+  std::vector<fz_epi_input> inputs(L.leaves.size() - 1);
+  for (size_t k = 1; k < L.leaves.size(); ++k)
+    if (!epilogue_input(L.leaves[k]->shape, oshape, L.leaves[k]->buf->ptr, &inputs[k - 1])) return false;
+  L.prog.num_leaves = (int32_t)L.leaves.size();
+  L.prog.num_outputs = (int32_t)outs.size();
+  for (size_t k = 0; k < outs.size(); ++k) L.prog.out_node[k] = outs[k];
+
+  const GemmSpec &g = *G->gemm;
+  const size_t n = G->numel();
+  std::vector<std::shared_ptr<DeviceBuffer>> bufs;
+  std::vector<float *> ptrs;
+  for (size_t k = 0; k < outs.size(); ++k) {
+    bufs.push_back(std::make_shared<DeviceBuffer>(n));
+    ptrs.push_back(bufs.back()->ptr);
+  }
+  fz_check(fz_gemm_f32_epilogue(g.batch, g.M, g.N, g.K, g.pa, g.la, g.lda, g.sA, g.transA, g.pb,
+                                g.lb, g.ldb, g.sB, g.transB, &L.prog,
+                                inputs.empty() ? nullptr : inputs.data(), ptrs.data(), g.N,
+                                g.M * g.N, nullptr),
+           "fz_gemm_f32_epilogue");
+  ++g_epilogue_gemms;
+  size_t next_lo = roots.size();
+  for (size_t k = 0; k < roots.size(); ++k) {
+    Expr *e = roots[k].get();
+    if (want_lo[k]) bufs[k]->tf32_lo = bufs[next_lo++];
+    e->kind = Expr::Leaf;
+    e->buf = bufs[k];
+    e->a.reset();
+    e->b.reset();
+    e->gemm.reset();
+    e->nodes_ub = 0;
+    e->leaves_ub = 1;
+  }
+  if (g_needed) {
+    G->kind = Expr::Leaf;
+    G->buf = bufs.back();
+    G->gemm.reset();
+    G->nodes_ub = 0;
+    G->leaves_ub = 1;
+  }
+  return true;
+}
+
 void materialize(const ExprPtr &ep) {
   Expr *e = ep.get();
   if (e->kind == Expr::Leaf) return;
+  if (e->kind == Expr::Gemm) {
+    lower_gemm(e);
+    return;
+  }
+  if ((e->kind == Expr::Unary || e->kind == Expr::Binary) && e->numel() > 0 &&
+      try_epilogue({ep}, {false}))
+    return;
   if (e->kind == Expr::Reduce) {
     if (e->a->kind != Expr::Leaf) materialize(e->a);
     int64_t outer, len, inner;
@@ -384,6 +608,11 @@ void materialize_with_lo(const ExprPtr &ep) {
     materialize(ep);
     return;
   }
+  if (try_epilogue({ep}, {true})) return;
+  if (e->kind == Expr::Gemm) {
+    lower_gemm(e);
+    return;
+  }
   Lowering L;
   const int root = L.visit(e);
   if (L.overflow || root < 0 || L.prog.num_nodes >= FZ_MAX_NODES) {
@@ -426,6 +655,7 @@ void materialize_group(const std::vector<ExprPtr> &eps) {
       todo.push_back(e);
   bool grouped = todo.size() >= 2 && (int)todo.size() <= FZ_MAX_OUTPUTS;
   for (const ExprPtr &e : todo) grouped = grouped && e->shape == todo[0]->shape;
+  if (grouped && try_epilogue(todo, std::vector<bool>(todo.size(), false))) return;
   if (grouped) {
     Lowering L;
     std::vector<int> roots;
@@ -796,15 +1026,35 @@ RawTensor matmul(const RawTensor &A, const RawTensor &B, bool transA, bool trans
   // pending operands are lowered with their remainder planes in the same pass
   if (A.pending() && split_plane_usable(lda, sA, batch)) materialize_with_lo(A.expr());
   if (B.pending() && split_plane_usable(ldb, sB, batch)) materialize_with_lo(B.expr());
-  const float *pa = A.data(), *pb = B.data();
-  size_t n = batch * M * N;
-  auto buf = std::make_shared<DeviceBuffer>(n);
-  const float *la = tf32_lo_plane(A, lda, sA, batch), *lb = tf32_lo_plane(B, ldb, sB, batch);
-  fz_check(fz_gemm_f32_split((int64_t)batch, (int64_t)M, (int64_t)N, (int64_t)Ka, pa, la, lda, sA,
-                             transA, pb, lb, ldb, sB, transB, buf->ptr, (int64_t)N,
-                             (int64_t)(M * N), nullptr),
-           "fz_gemm_f32_split");
-  return RawTensor(make_leaf(std::move(buf), oshape), A.dtype(), A.device());
+  auto g = std::make_shared<GemmSpec>();
+  g->pa = A.data();
+  g->pb = B.data();
+  g->la = tf32_lo_plane(A, lda, sA, batch);
+  g->lb = tf32_lo_plane(B, ldb, sB, batch);
+  g->keep_a = A.expr()->buf;
+  g->keep_b = B.expr()->buf;
+  if (g->la) g->keep_la = A.expr()->buf->tf32_lo;
+  if (g->lb) g->keep_lb = B.expr()->buf->tf32_lo;
+  g->batch = (int64_t)batch;
+  g->M = (int64_t)M;
+  g->N = (int64_t)N;
+  g->K = (int64_t)Ka;
+  g->lda = lda;
+  g->sA = sA;
+  g->ldb = ldb;
+  g->sB = sB;
+  g->transA = transA;
+  g->transB = transB;
+  auto e = std::make_shared<Expr>();
+  e->kind = Expr::Gemm;
+  e->shape = oshape;
+  e->gemm = std::move(g);
+  e->nodes_ub = 0;
+  e->leaves_ub = 1;
+  // launched where its value is first needed: inside the epilogue of the program that
+  // reads it, or as a plain product
+  if (!g_gemm_epilogue || batch * M * N == 0) lower_gemm(e.get());
+  return RawTensor(std::move(e), A.dtype(), A.device());
 }
 
 // fusion::math::linalg::swapaxes (ops/Linalg.hpp:109-128): a materialised copy;

@@ -76,15 +76,30 @@ struct DeviceBuffer {
   DeviceBuffer &operator=(const DeviceBuffer &) = delete;
 };
 
+// A GEMM whose launch is deferred (Expr::Gemm): the operands as the GEMM reads them,
+// materialised, with their TF32 remainder planes, kept alive by the node.
+struct GemmSpec {
+  int64_t batch = 1, M = 0, N = 0, K = 0;
+  const float *pa = nullptr, *la = nullptr, *pb = nullptr, *lb = nullptr;
+  int64_t lda = 0, sA = 0, ldb = 0, sB = 0;
+  int transA = 0, transB = 0;
+  std::shared_ptr<DeviceBuffer> keep_a, keep_b, keep_la, keep_lb;
+};
+
 // ---- fusion IR node --------------------------------------------------------------
 struct Expr {
   // Reduce: a pending single- or multi-axis reduction of `a` (fz_redop in op), kept
   // pending so a following reduction over an adjacent axis can join it (one pass over
   // the merged axes); lowered by itself, never inside an elementwise program.
-  enum Kind { Leaf, Const, Unary, Binary, Reduce } kind;
+  // Gemm: a pending product [batch..., M, N] (`gemm`). The first elementwise program
+  // lowered over it runs in the GEMM's epilogue (fz_gemm_f32_epilogue), and the
+  // product itself is stored only if something else still holds the node; lowered by
+  // any other reader, it is a plain GEMM into a buffer.
+  enum Kind { Leaf, Const, Unary, Binary, Reduce, Gemm } kind;
   int op = 0;  // fz_binop / fz_unop / fz_redop
   std::vector<size_t> shape;
   std::shared_ptr<Expr> a, b;
+  std::shared_ptr<GemmSpec> gemm;     // Gemm
   std::shared_ptr<DeviceBuffer> buf;  // Leaf
   float imm = 0.0f;                   // Const
   int red_lo = 0, red_hi = 0;         // Reduce: axes [red_lo, red_hi] of a's shape
@@ -111,6 +126,12 @@ bool fusion_enabled();
 // for buffers made later).
 void set_split_cache_enabled(bool on);
 bool split_cache_enabled();
+// Defer GEMM launches so that the elementwise program reading a product runs in the
+// GEMM's epilogue (on by default; off launches every GEMM where it is called).
+void set_gemm_epilogue_enabled(bool on);
+bool gemm_epilogue_enabled();
+// GEMMs launched with a fused epilogue program so far in this process.
+int64_t epilogue_gemms();
 // Lower a pending node to one fused kernel (no-op for a Leaf).
 void materialize(const ExprPtr &e);
 // Lower a pending node and its TF32 remainder plane in one fused pass (GEMM operands).

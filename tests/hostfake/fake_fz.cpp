@@ -11,6 +11,7 @@
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
+#include <map>
 #include <set>
 #include <string>
 #include <vector>
@@ -92,15 +93,29 @@ int fz_get_device(int *d) { *d = 0; return FZ_OK; }
 void *fz_default_stream(void) { static int s; return &s; }
 int fz_stream_sync(void *) { return FZ_OK; }
 int fz_device_sync(void) { return FZ_OK; }
+// live allocations, so pool_used_bytes reports what the host keeps
+std::map<void *, size_t> g_live;
+size_t g_live_bytes = 0;
 int fz_malloc(void **p, size_t bytes, void *) {
   *p = nullptr;
   if (!bytes) return FZ_OK;
   *p = std::aligned_alloc(256, (bytes + 255) & ~(size_t)255);
-  return *p ? FZ_OK : fail(FZ_ERR_OOM, "host allocation failed");
+  if (!*p) return fail(FZ_ERR_OOM, "host allocation failed");
+  g_live[*p] = bytes;
+  g_live_bytes += bytes;
+  return FZ_OK;
 }
-int fz_free(void *p, void *) { std::free(p); return FZ_OK; }
+int fz_free(void *p, void *) {
+  auto it = g_live.find(p);
+  if (it != g_live.end()) {
+    g_live_bytes -= it->second;
+    g_live.erase(it);
+  }
+  std::free(p);
+  return FZ_OK;
+}
 int fz_pool_release(void) { return FZ_OK; }
-int fz_pool_stats(size_t *r, size_t *u) { if (r) *r = 0; if (u) *u = 0; return FZ_OK; }
+int fz_pool_stats(size_t *r, size_t *u) { if (r) *r = g_live_bytes; if (u) *u = g_live_bytes; return FZ_OK; }
 int fz_memcpy_h2d(void *d, const void *s, size_t n, void *) { if (n) std::memcpy(d, s, n); return FZ_OK; }
 int fz_memcpy_d2h(void *d, const void *s, size_t n, void *) { if (n) std::memcpy(d, s, n); return FZ_OK; }
 int fz_memcpy_d2d(void *d, const void *s, size_t n, void *) { if (n) std::memmove(d, s, n); return FZ_OK; }
@@ -221,6 +236,50 @@ int fz_gemm_f32(int64_t batch, int64_t M, int64_t N, int64_t K, const float *A, 
   return FZ_OK;
 }
 
+
+int64_t g_epilogue_launches = 0;
+int fz_gemm_f32_epilogue(int64_t batch, int64_t M, int64_t N, int64_t K, const float *A,
+                         const float *A_lo, int64_t lda, int64_t sA, int tA, const float *B,
+                         const float *B_lo, int64_t ldb, int64_t sB, int tB,
+                         const struct fz_program *pg, const fz_epi_input *inputs,
+                         float *const *outs, int64_t ldc, int64_t sC, void *st) {
+  if (!pg || pg->num_leaves < 1 || pg->num_leaves > FZ_MAX_LEAVES || pg->num_outputs > FZ_MAX_OUTPUTS)
+    return fail(FZ_ERR_INVALID, "fz_gemm_f32_epilogue: bad program");
+  std::vector<float> P((size_t)(batch * M * N));
+  int64_t before = g_launches;
+  int rc = fz_gemm_f32_split(batch, M, N, K, A, A_lo, lda, sA, tA, B, B_lo, ldb, sB, tB, P.data(), N,
+                             M * N, st);
+  if (rc) return rc;
+  fz_ewise_plan plan{};
+  plan.ndim = 3;
+  plan.num_operands = pg->num_outputs + pg->num_leaves;
+  plan.size[0] = batch;
+  plan.size[1] = M;
+  plan.size[2] = N;
+  auto set = [&](int k, int64_t b, int64_t m, int64_t n) {
+    plan.stride_bytes[k][0] = b * 4;
+    plan.stride_bytes[k][1] = m * 4;
+    plan.stride_bytes[k][2] = n * 4;
+  };
+  for (int k = 0; k < pg->num_outputs; ++k) set(k, sC, ldc, 1);
+  std::vector<const float *> leaves(pg->num_leaves);
+  leaves[0] = P.data();
+  set(pg->num_outputs, M * N, N, 1);
+  for (int k = 1; k < pg->num_leaves; ++k) {
+    const fz_epi_input &in = inputs[k - 1];
+    if (in.col_stride != 0 && in.col_stride != 1)
+      return fail(FZ_ERR_INVALID, "fz_gemm_f32_epilogue: input column stride must be 0 or 1");
+    leaves[k] = in.ptr;
+    set(pg->num_outputs + k, in.batch_stride, in.row_stride, in.col_stride);
+  }
+  rc = fz_fused_launch(pg, &plan, outs, leaves.data(), st);
+  g_launches = before + 1;  // one kernel on the device
+  ++g_epilogue_launches;
+  return rc;
+}
+int fz_gemm_epilogue_compile(const struct fz_program *, const fz_epi_input *, int, int, int, int) {
+  return FZ_OK;
+}
 
 int fz_stream_create(void **s) { static int token; *s = &token; return FZ_OK; }
 void *fz_upload_stream(void) { static int token; return &token; }

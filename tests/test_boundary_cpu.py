@@ -91,3 +91,46 @@ def test_device_validation_on_host():
     with pytest.raises(RuntimeError):
         F.CppDevice(F.CppDeviceType.CPU, 1)  # reference: CPU index must be <= 0
     F.CppDevice(F.CppDeviceType.CUDA, 3)  # CUDA ordinals are checked when used
+
+
+def _epi_program(capi, nodes, nleaves, outs):
+    p = capi.Program()
+    p.num_nodes, p.num_leaves, p.num_outputs = len(nodes), nleaves, len(outs)
+    for i, o in enumerate(outs):
+        p.out_node[i] = o
+    for i, (kind, op, s0, s1, imm) in enumerate(nodes):
+        n = p.nodes[i]
+        n.kind, n.op, n.src0, n.src1, n.imm = kind, op, s0, s1, imm
+    return p
+
+
+# (a_mn, b_mn, tile_n, pair): every variant the GEMM dispatch can pick
+GEMM_VARIANTS = [(a, b, 256, p) for p in (1, 0) for a in (0, 1) for b in (0, 1)] + \
+                [(a, 0, t, 0) for t in (16, 64) for a in (0, 1)]
+
+
+def test_gemm_epilogues_compile_for_every_kernel_variant():
+    """NVRTC (no device needed) compiles each GEMM variant with a generated epilogue:
+    relu(P + bias) with its TF32 remainder plane and P, and the ReLU-mask gradient."""
+    import ctypes as C
+
+    from nova_b200 import capi
+
+    L = capi.lib()
+    B, U, K = capi.NODE_BINARY, capi.NODE_UNARY, capi.NODE_CONST
+    fwd = _epi_program(capi, [(B, capi.BINOPS["add"], -1, -2, 0.0), (K, 0, 0, 0, 0.0),
+                              (B, capi.BINOPS["maximum"], 0, 1, 0.0), (U, capi.UNOPS["tf32_lo"], 2, 0, 0.0),
+                              (U, capi.UNOPS["copy"], -1, 0, 0.0)], 2, [2, 3, 4])
+    bwd = _epi_program(capi, [(B, capi.BINOPS["add"], -2, -3, 0.0), (K, 0, 0, 0, 0.0),
+                              (B, capi.BINOPS["gt"], 0, 1, 0.0), (B, capi.BINOPS["mul"], -1, 2, 0.0),
+                              (U, capi.UNOPS["tf32_lo"], 3, 0, 0.0)], 3, [3, 4])
+    row = (capi.EpiInput * 1)(capi.EpiInput(None, 0, 0, 1))
+    full_row = (capi.EpiInput * 2)(capi.EpiInput(None, 4096, 64, 1), capi.EpiInput(None, 0, 0, 1))
+    for v in GEMM_VARIANTS:
+        rc = L.fz_gemm_epilogue_compile(C.byref(fwd), row, *v)
+        assert rc == 0, (v, L.fz_last_error())
+    for v in [(0, 0, 256, 1), (0, 1, 256, 1), (0, 0, 16, 0)]:
+        rc = L.fz_gemm_epilogue_compile(C.byref(bwd), full_row, *v)
+        assert rc == 0, (v, L.fz_last_error())
+    # narrow tiles take a K-major B only
+    assert L.fz_gemm_epilogue_compile(C.byref(fwd), row, 0, 1, 16, 0) == 1

@@ -153,9 +153,11 @@ def test_pending_gemm_operand_lowered_with_its_plane(fake_fusion):
     assert y.is_pending()
     before = F.stats()["kernel_launches"]
     z = y @ W
-    assert F.stats()["kernel_launches"] - before == 2  # the fused program and the GEMM
+    assert F.stats()["kernel_launches"] - before == 1  # the fused program (value + plane)
+    assert z.is_pending()  # the GEMM itself waits for its first reader
     want = np.maximum(x.to_numpy() + b.to_numpy(), 0).astype(np.float64) @ W.to_numpy()
     np.testing.assert_allclose(z.to_numpy(), want, rtol=1e-5, atol=1e-6)
+    assert F.stats()["kernel_launches"] - before == 2
 
 
 def test_overlapped_gradient_average_matches_plain_step(fake_fusion):
@@ -248,3 +250,119 @@ def test_reduction_chain_edge_cases(fake_fusion):
     np.testing.assert_allclose(z1, d.sum(axis=(1, 2), keepdims=True), rtol=1e-5, atol=1e-6)
     np.testing.assert_allclose(z2, d.sum(axis=1, keepdims=True), rtol=1e-5, atol=1e-6)
     np.testing.assert_allclose(x.sum(0).sum(0).sum(0).to_numpy(), [d.sum()], rtol=1e-5)
+
+
+def _stat(F, k):
+    return F.stats()[k]
+
+
+def _plain(F, fn):
+    """fn() evaluated with every GEMM launched where it is called."""
+    F.set_gemm_epilogue(False)
+    try:
+        return fn()
+    finally:
+        F.set_gemm_epilogue(True)
+
+
+def _mlp_layer_inputs(F, seed):
+    rng = np.random.default_rng(seed)
+    arrs = [rng.standard_normal(s).astype(np.float32) for s in [(32, 8), (8, 16), (16,), (16, 4)]]
+    x, W, b, W2 = (api_cases.T(F, a) for a in arrs)
+    (x @ W).to_numpy()  # the operands' TF32 remainder planes are made here
+    (api_cases.T(F, np.ones((2, 16), np.float32)) @ W2).to_numpy()
+    return x, W, b, W2
+
+
+def test_bias_relu_runs_in_the_gemm_epilogue(fake_fusion):
+    """max(x @ W + b, 0) read by the next `@` is written, with its TF32 remainder plane,
+    by the epilogue of the x @ W GEMM: one kernel, the product itself not stored (no
+    tensor holds it), values equal to the unfused lowering bit for bit."""
+    F = fake_fusion
+    x, W, b, W2 = _mlp_layer_inputs(F, 11)
+    e0, k0, u0 = _stat(F, "epilogue_gemms"), _stat(F, "kernel_launches"), _stat(F, "pool_used_bytes")
+    y = ((x @ W) + b).maximum(0.0)
+    z = y @ W2
+    assert _stat(F, "epilogue_gemms") - e0 == 1
+    assert _stat(F, "kernel_launches") - k0 == 1
+    assert _stat(F, "pool_used_bytes") - u0 == 2 * y.size * 4  # y and its plane only
+    assert z.is_pending()
+    want_y, want_z = _plain(F, lambda: (((x @ W) + b).maximum(0.0).to_numpy(),
+                                        (((x @ W) + b).maximum(0.0) @ W2).to_numpy()))
+    np.testing.assert_array_equal(y.to_numpy(), want_y)
+    np.testing.assert_array_equal(z.to_numpy(), want_z)
+
+
+def test_gemm_epilogue_stores_a_product_still_held(fake_fusion):
+    """When a tensor still holds the product, the same epilogue stores it too."""
+    F = fake_fusion
+    x, W, b, W2 = _mlp_layer_inputs(F, 12)
+    e0, k0, u0 = _stat(F, "epilogue_gemms"), _stat(F, "kernel_launches"), _stat(F, "pool_used_bytes")
+    t = x @ W
+    y = (t + b).maximum(0.0)
+    y @ W2
+    assert _stat(F, "epilogue_gemms") - e0 == 1
+    assert _stat(F, "kernel_launches") - k0 == 1
+    assert not t.is_pending()
+    assert _stat(F, "pool_used_bytes") - u0 == 3 * y.size * 4  # y, its plane and t
+    np.testing.assert_array_equal(t.to_numpy(), _plain(F, lambda: (x @ W).to_numpy()))
+
+
+def test_pending_product_operand_gets_value_and_plane_from_its_epilogue(fake_fusion):
+    F = fake_fusion
+    x, W, b, W2 = _mlp_layer_inputs(F, 13)
+    e0, k0 = _stat(F, "epilogue_gemms"), _stat(F, "kernel_launches")
+    t = x @ W
+    z = t @ W2
+    assert _stat(F, "epilogue_gemms") - e0 == 1 and _stat(F, "kernel_launches") - k0 == 1
+    assert not t.is_pending() and z.is_pending()
+    np.testing.assert_array_equal(z.to_numpy(), _plain(F, lambda: ((x @ W) @ W2).to_numpy()))
+
+
+def test_program_over_two_products_lowers_them_plainly(fake_fusion):
+    F = fake_fusion
+    x, W, b, W2 = _mlp_layer_inputs(F, 14)
+    e0, k0 = _stat(F, "epilogue_gemms"), _stat(F, "kernel_launches")
+    y = ((x @ W) + (x @ W) * 2.0).to_numpy()
+    assert _stat(F, "epilogue_gemms") == e0
+    assert _stat(F, "kernel_launches") - k0 == 3  # two GEMMs and the fused program
+    np.testing.assert_array_equal(y, _plain(F, lambda: ((x @ W) + (x @ W) * 2.0).to_numpy()))
+
+
+@pytest.mark.parametrize("cshape,fused", [((2, 3, 1, 5), True), ((5,), True), ((4, 1), True),
+                                          ((2, 1, 4, 5), False), ((3, 4, 5), False)])
+def test_epilogue_inputs_broadcast_over_batched_products(fake_fusion, cshape, fused):
+    """Inputs whose batch dims flatten into one stride run in the epilogue; others (a
+    broadcast batch dim in front of a varying one) fall back to a plain GEMM and a fused
+    program; both give the unfused values."""
+    F = fake_fusion
+    rng = np.random.default_rng(15)
+    a = api_cases.T(F, rng.standard_normal((2, 3, 4, 8)))
+    w = api_cases.T(F, rng.standard_normal((2, 3, 8, 5)))
+    c = api_cases.T(F, rng.standard_normal(cshape))
+    e0 = _stat(F, "epilogue_gemms")
+    got = ((a @ w) * c - 1.0).to_numpy()
+    assert (_stat(F, "epilogue_gemms") - e0 == 1) == fused
+    np.testing.assert_array_equal(got, _plain(F, lambda: ((a @ w) * c - 1.0).to_numpy()))
+
+
+def test_mlp_step_with_gemm_epilogues_matches_plain(fake_fusion):
+    """A training step with deferred GEMMs gives the eager-GEMM step's values bit for bit;
+    each hidden layer's bias + ReLU and ReLU-mask gradient run in GEMM epilogues."""
+    from nova_b200.mlp import MLP
+
+    F = fake_fusion
+    X, Y, Ws, bs = api_cases.mlp_inputs(6, [8, 16, 16, 16, 4], 12)
+    bs = [np.linspace(-0.1, 0.1, b.size).astype(np.float32) for b in bs]
+    fused, plain = MLP(F, Ws, bs), MLP(F, Ws, bs)
+    for _ in range(2):
+        e0 = _stat(F, "epilogue_gemms")
+        lf = fused.step(fused.tensor(X, True), fused.tensor(Y, True), 1e-2).to_numpy()
+        # forward: 3 bias+ReLU layers and the output layer's loss gradient; backward: the
+        # ReLU-mask input gradients of the 3 hidden layers
+        assert _stat(F, "epilogue_gemms") - e0 == 7
+        lp = _plain(F, lambda: plain.step(plain.tensor(X, True), plain.tensor(Y, True), 1e-2).to_numpy())
+        np.testing.assert_array_equal(lf, lp)
+    for (Wf, bf), (Wp, bp) in zip(fused.numpy_params(), plain.numpy_params()):
+        np.testing.assert_array_equal(Wf, Wp)
+        np.testing.assert_array_equal(bf, bp)
