@@ -259,13 +259,21 @@ int prepare(const float *src, int64_t ld, int64_t sb, const float *lo_given, int
   return FZ_OK;
 }
 
-// Dynamic shared memory of a kernel variant (stage ring + alignment slack).
+// Dynamic shared memory of a kernel variant: stage ring, the epilogue warps' staging
+// tiles and alignment slack (at most 225 KB of the 227 KB a CTA may use).
 size_t smem_bytes(bool pair, int tbn) {
-  if (pair) return (size_t)PAIR_STAGES * PAIR_STAGE_BYTES + 1024;
-  if (tbn == 16) return (size_t)TileCfg<16>::NSTAGE * TileCfg<16>::STAGE + 1024;
-  if (tbn == 64) return (size_t)TileCfg<64>::NSTAGE * TileCfg<64>::STAGE + 1024;
-  return (size_t)TileCfg<BN>::NSTAGE * TileCfg<BN>::STAGE + 1024;
+  size_t ring;
+  if (pair) ring = (size_t)PAIR_STAGES * PAIR_STAGE_BYTES;
+  else if (tbn == 16) ring = (size_t)TileCfg<16>::NSTAGE * TileCfg<16>::STAGE;
+  else if (tbn == 64) ring = (size_t)TileCfg<64>::NSTAGE * TileCfg<64>::STAGE;
+  else ring = (size_t)TileCfg<BN>::NSTAGE * TileCfg<BN>::STAGE;
+  return ring + EPI_SMEM_BYTES + 1024;
 }
+static_assert((size_t)PAIR_STAGES * PAIR_STAGE_BYTES + EPI_SMEM_BYTES + 1024 <= 232448 &&
+                  (size_t)TileCfg<BN>::NSTAGE * TileCfg<BN>::STAGE + EPI_SMEM_BYTES + 1024 <= 232448 &&
+                  (size_t)TileCfg<64>::NSTAGE * TileCfg<64>::STAGE + EPI_SMEM_BYTES + 1024 <= 232448 &&
+                  (size_t)TileCfg<16>::NSTAGE * TileCfg<16>::STAGE + EPI_SMEM_BYTES + 1024 <= 232448,
+              "shared memory per CTA");
 
 template <bool A_MN, bool B_MN, int TBN>
 int launch_gemm(const CUtensorMap &mAh, const CUtensorMap &mAl, const CUtensorMap &mBh,
@@ -332,7 +340,10 @@ struct Epilogue {
   float *const *outputs = nullptr;
 };
 
-// cls[k]: 1 when input k varies along the columns (col_stride 1), else 0.
+// cls[k] of input k: 0 constant along a row (a per-row value or a scalar), 1 a row
+// vector (same for every row: a bias), 2 varying along rows and columns (a tensor of
+// the product's shape). Class-2 inputs are read through the warp's staging tile in
+// whole row segments; class-1 inputs are the same address for every lane.
 std::string epilogue_class(const fz_program &pg, const int *cls) {
   const int nin = pg.num_leaves - 1, nout = pg.num_outputs;
   std::ostringstream o;
@@ -340,46 +351,95 @@ std::string epilogue_class(const fz_program &pg, const int *cls) {
     << "  template <int CPW>\n"
     << "  static __device__ __forceinline__ void store(const fz_gemm_dev::GemmArgs &a,\n"
     << "      const fz_gemm_dev::EpiParams &p, int, int bz, int row, int col0,\n"
-    << "      const float (&acc)[CPW]) {\n"
-    << "    if (row >= a.M || col0 >= a.N) return;\n"
-    << "    const long long ob = (long long)bz * a.strideC + (long long)row * a.ldc + col0;\n";
+    << "      const float (&acc)[CPW], float4 *tile) {\n"
+    << "    using namespace fz_gemm_dev;\n"
+    << "    const int lane = threadIdx.x & 31;\n"
+    << "    const int row0 = row - lane;\n"
+    << "    const int rows = min(32, a.M - row0);\n"
+    << "    if (rows <= 0 || col0 >= a.N) return;\n"
+    << "    const unsigned mask = __activemask();\n"
+    << "    const bool live = lane < rows;\n"
+    << "    (void)live;\n"
+    << "    constexpr int BW = CPW < EPI_BW ? CPW : EPI_BW;\n"
+    << "    const long long ob = (long long)bz * a.strideC + (long long)row0 * a.ldc + col0;\n";
   for (int k = 0; k < nin; ++k) {
-    o << "    const float *b" << k << " = p.in[" << k << "] + (long long)bz * p.in_sb[" << k
-      << "] + (long long)row * p.in_sm[" << k << "]" << (cls[k] ? " + col0" : "") << ";\n";
-    if (!cls[k]) o << "    const float s" << k << " = b" << k << "[0];\n";
+    const std::string K = std::to_string(k);
+    if (cls[k] == 0)
+      o << "    const float s" << K << " = live ? p.in[" << K << "][(long long)bz * p.in_sb[" << K
+        << "] + (long long)row * p.in_sm[" << K << "]] : 0.0f;\n";
+    else if (cls[k] == 1)
+      o << "    const float *g" << K << " = p.in[" << K << "] + (long long)bz * p.in_sb[" << K
+        << "] + col0;\n";
+    else
+      o << "    const float *g" << K << " = p.in[" << K << "] + (long long)bz * p.in_sb[" << K
+        << "] + (long long)row0 * p.in_sm[" << K << "] + col0;\n";
   }
-  for (int j = 0; j < nout; ++j) o << "    float *o" << j << " = p.out[" << j << "] + ob;\n";
-  auto leaf_args = [&](const char *lane, bool vec) {
-    std::string r;
+  o << "#pragma unroll\n"
+    << "    for (int cb = 0; cb < CPW / BW; ++cb) {\n"
+    << "      const int cols = min(BW, a.N - col0 - cb * BW);\n"
+    << "      if (cols <= 0) break;\n";
+  // class-2 inputs: one block of this lane's row, through the tile
+  for (int k = 0; k < nin; ++k) {
+    if (cls[k] != 2) continue;
+    const std::string K = std::to_string(k);
+    o << "      float v" << K << "[BW];\n"
+      << "      tile_load<BW>(tile, g" << K << " + cb * BW, p.in_sm[" << K << "], rows, cols, p.vec, lane);\n"
+      << "      __syncwarp(mask);\n"
+      << "#pragma unroll\n"
+      << "      for (int c4 = 0; c4 < BW / 4; ++c4) {\n"
+      << "        const float4 t = tile_get(tile, lane, c4);\n"
+      << "        v" << K << "[c4 * 4] = t.x; v" << K << "[c4 * 4 + 1] = t.y; v" << K
+      << "[c4 * 4 + 2] = t.z; v" << K << "[c4 * 4 + 3] = t.w;\n"
+      << "      }\n"
+      << "      __syncwarp(mask);\n";
+  }
+  // each output: evaluate the block into the tile, then store it in row segments
+  for (int j = 0; j < nout; ++j) {
+    o << "#pragma unroll\n"
+      << "      for (int c4 = 0; c4 < BW / 4; ++c4) {\n"
+      << "        float r[4];\n";
+    // class-1 inputs: this group of 4 columns (zeros past N)
     for (int k = 0; k < nin; ++k) {
-      if (!cls[k]) r += "s" + std::to_string(k) + ", ";
-      else if (vec) r += "v" + std::to_string(k) + "." + lane + ", ";
-      else r += "b" + std::to_string(k) + "[i], ";
+      if (cls[k] != 1) continue;
+      const std::string K = std::to_string(k);
+      o << "        float4 w" << K << " = make_float4(0.0f, 0.0f, 0.0f, 0.0f);\n"
+        << "        {\n"
+        << "          const float *q = g" << K << " + cb * BW + c4 * 4;\n"
+        << "          if (p.vec && c4 * 4 + 4 <= cols) w" << K << " = *reinterpret_cast<const float4 *>(q);\n"
+        << "          else {\n"
+        << "            if (c4 * 4 + 0 < cols) w" << K << ".x = q[0];\n"
+        << "            if (c4 * 4 + 1 < cols) w" << K << ".y = q[1];\n"
+        << "            if (c4 * 4 + 2 < cols) w" << K << ".z = q[2];\n"
+        << "            if (c4 * 4 + 3 < cols) w" << K << ".w = q[3];\n"
+        << "          }\n"
+        << "        }\n"
+        << "        const float u" << K << "[4] = {w" << K << ".x, w" << K << ".y, w" << K << ".z, w" << K << ".w};\n";
     }
-    return r;
-  };
-  o << "    if (p.vec && col0 + CPW <= a.N) {\n#pragma unroll\n"
-    << "      for (int i = 0; i < CPW; i += 4) {\n";
-  for (int k = 0; k < nin; ++k)
-    if (cls[k]) o << "        const float4 v" << k << " = *reinterpret_cast<const float4 *>(b" << k << " + i);\n";
-  for (int j = 0; j < nout; ++j) o << "        float4 q" << j << ";\n";
-  const char *lanes[4] = {"x", "y", "z", "w"};
-  for (int ln = 0; ln < 4; ++ln) {
-    o << "        fz_eval(acc[i + " << ln << "], " << leaf_args(lanes[ln], true);
-    for (int j = 0; j < nout; ++j) o << "q" << j << "." << lanes[ln] << (j + 1 < nout ? ", " : "");
-    o << ");\n";
+    o << "#pragma unroll\n"
+      << "        for (int e = 0; e < 4; ++e) {\n"
+      << "          const int c = c4 * 4 + e;\n";
+    for (int k = 0; k < nout; ++k) o << "          float q" << k << ";\n";
+    o << "          fz_eval(acc[cb * BW + c], ";
+    for (int k = 0; k < nin; ++k)
+      o << (cls[k] == 0 ? "s" + std::to_string(k)
+                        : cls[k] == 1 ? "u" + std::to_string(k) + "[e]" : "v" + std::to_string(k) + "[c]")
+        << ", ";
+    for (int k = 0; k < nout; ++k) o << "q" << k << (k + 1 < nout ? ", " : "");
+    o << ");\n"
+      << "          r[e] = q" << j << ";\n"
+      << "        }\n"
+      << "        tile_put(tile, lane, c4, make_float4(r[0], r[1], r[2], r[3]));\n"
+      << "      }\n"
+      << "      __syncwarp(mask);\n"
+      << "      tile_store<BW>(tile, p.out[" << j << "] + ob + cb * BW, a.ldc, rows, cols, p.vec, lane);\n"
+      << "      __syncwarp(mask);\n";
   }
-  for (int j = 0; j < nout; ++j) o << "        *reinterpret_cast<float4 *>(o" << j << " + i) = q" << j << ";\n";
-  o << "      }\n    } else {\n#pragma unroll\n"
-    << "      for (int i = 0; i < CPW; ++i) {\n"
-    << "        if (col0 + i < a.N) {\n";
-  for (int j = 0; j < nout; ++j) o << "          float r" << j << ";\n";
-  o << "          fz_eval(acc[i], " << leaf_args("", false);
-  for (int j = 0; j < nout; ++j) o << "r" << j << (j + 1 < nout ? ", " : "");
-  o << ");\n";
-  for (int j = 0; j < nout; ++j) o << "          o" << j << "[i] = r" << j << ";\n";
-  o << "        }\n      }\n    }\n  }\n};\n";
+  o << "    }\n  }\n};\n";
   return o.str();
+}
+
+int input_class(const fz_epi_input &in) {
+  return in.col_stride == 0 ? 0 : in.row_stride == 0 ? 1 : 2;
 }
 
 struct JitEntry {
@@ -620,7 +680,7 @@ int gemm_impl(int64_t batch, int64_t M, int64_t N, int64_t K, const float *A, co
       ep.in[k] = in.ptr;
       ep.in_sb[k] = in.batch_stride;
       ep.in_sm[k] = in.row_stride;
-      cls[k] = in.col_stride == 1;
+      cls[k] = input_class(in);
       if (cls[k])
         vec = vec && ((uintptr_t)in.ptr & 15) == 0 && in.row_stride % 4 == 0 &&
               (batch == 1 || in.batch_stride % 4 == 0);
@@ -698,7 +758,7 @@ extern "C" int fz_gemm_epilogue_compile(const fz_program *epi, const fz_epi_inpu
              "fz_gemm_epilogue_compile: tile width must be 16, 64 or 256 (256 for pairs)");
   FZ_REQUIRE(tile_n == BN || !b_mn, "fz_gemm_epilogue_compile: narrow tiles read B K-major");
   int cls[EPI_MAX_IN] = {};
-  for (int k = 0; k + 1 < epi->num_leaves; ++k) cls[k] = inputs[k].col_stride == 1;
+  for (int k = 0; k + 1 < epi->num_leaves; ++k) cls[k] = input_class(inputs[k]);
   std::vector<char> bin;
   std::string lowered;
   const std::string name = epilogue_kernel_name(a_mn != 0, b_mn != 0, tile_n, pair != 0);

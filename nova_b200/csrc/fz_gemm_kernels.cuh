@@ -246,24 +246,102 @@ struct EpiParams {
   int vec;
 };
 
-// The plain epilogue: C = product (or this unit's K-split partial).
+// ---- warp-cooperative epilogue I/O
+//
+// The 32 lanes of an epilogue warp hold 32 consecutive output rows (lane = row), each
+// a run of CPW columns in registers. A lane storing its own row would make every warp
+// store touch 32 rows. Instead, per block of EPI_BW columns, the lanes exchange values
+// through the warp's private 32 x 32 fp32 staging tile in shared memory. Each row of
+// the tile is 8 float4 slots; slot c4 of row r lives at r * 8 + (c4 ^ (r & 7)), so both
+// the row-per-lane and the row-per-8-lanes access patterns are free of bank conflicts.
+// Global accesses then move whole row segments (EPI_BW / 4 lanes per row).
+constexpr int EPI_BW = 16;                   // columns per block (register pressure:
+                                             // the 128 accumulators stay live meanwhile)
+constexpr int EPI_TILE_BYTES = 32 * 32 * 4;  // per epilogue warp
+constexpr int EPI_SMEM_BYTES = NUM_EPI_WARPS * EPI_TILE_BYTES;
+
+__device__ __forceinline__ void tile_put(float4 *t, int r, int c4, float4 v) { t[r * 8 + (c4 ^ (r & 7))] = v; }
+__device__ __forceinline__ float4 tile_get(const float4 *t, int r, int c4) { return t[r * 8 + (c4 ^ (r & 7))]; }
+
+// tile rows [0, rows) x columns [0, cols) -> dst (row pitch ld); 16-byte stores when vec
+// (dst 16-byte aligned, ld a multiple of 4), else per element.
+template <int BW>
+__device__ __forceinline__ void tile_store(const float4 *t, float *dst, long long ld, int rows,
+                                           int cols, bool vec, int lane) {
+  constexpr int LPR = BW / 4, RPI = 32 / LPR;  // lanes per row, rows per instruction
+  const int c4 = lane % LPR;
+#pragma unroll
+  for (int r0 = 0; r0 < 32; r0 += RPI) {
+    const int r = r0 + lane / LPR;
+    if (r < rows) {
+      const float4 v = tile_get(t, r, c4);
+      float *d = dst + (long long)r * ld + c4 * 4;
+      if (vec && c4 * 4 + 4 <= cols) {
+        *reinterpret_cast<float4 *>(d) = v;
+      } else {
+        if (c4 * 4 + 0 < cols) d[0] = v.x;
+        if (c4 * 4 + 1 < cols) d[1] = v.y;
+        if (c4 * 4 + 2 < cols) d[2] = v.z;
+        if (c4 * 4 + 3 < cols) d[3] = v.w;
+      }
+    }
+  }
+}
+
+// src (row pitch ld) rows [0, rows) x columns [0, cols) -> tile, zeros elsewhere.
+template <int BW>
+__device__ __forceinline__ void tile_load(float4 *t, const float *src, long long ld, int rows,
+                                          int cols, bool vec, int lane) {
+  constexpr int LPR = BW / 4, RPI = 32 / LPR;
+  const int c4 = lane % LPR;
+#pragma unroll
+  for (int r0 = 0; r0 < 32; r0 += RPI) {
+    const int r = r0 + lane / LPR;
+    float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    if (r < rows) {
+      const float *s = src + (long long)r * ld + c4 * 4;
+      if (vec && c4 * 4 + 4 <= cols) {
+        v = *reinterpret_cast<const float4 *>(s);
+      } else {
+        if (c4 * 4 + 0 < cols) v.x = s[0];
+        if (c4 * 4 + 1 < cols) v.y = s[1];
+        if (c4 * 4 + 2 < cols) v.z = s[2];
+        if (c4 * 4 + 3 < cols) v.w = s[3];
+      }
+    }
+    tile_put(t, r, c4, v);
+  }
+}
+
+// The plain epilogue: C = product (or this unit's K-split partial), stored through
+// the staging tile. `row` is this lane's row; the warp's rows are row - lane + [0, 32).
 struct StoreEpi {
   template <int CPW>
   static __device__ __forceinline__ void store(const GemmArgs &a, const EpiParams &, int ks, int bz,
-                                               int row, int col0, const float (&acc)[CPW]) {
-    if (row >= a.M || col0 >= a.N) return;
-    float *crow = a.C + (int64_t)ks * a.split_stride + (int64_t)bz * a.strideC +
-                  (int64_t)row * a.ldc + col0;
+                                               int row, int col0, const float (&acc)[CPW],
+                                               float4 *tile) {
+    const int lane = threadIdx.x & 31;
+    const int row0 = row - lane;
+    const int rows = min(32, a.M - row0);
+    if (rows <= 0 || col0 >= a.N) return;  // uniform over the warp
+    const unsigned mask = __activemask();
+    constexpr int BW = CPW < EPI_BW ? CPW : EPI_BW;
+    float *base = a.C + (int64_t)ks * a.split_stride + (int64_t)bz * a.strideC +
+                  (int64_t)row0 * a.ldc + col0;
     const bool vec = ((a.ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(a.C) & 15) == 0) &&
-                     ((a.strideC & 3) == 0);
-    if (vec && col0 + CPW <= a.N) {
+                     ((a.strideC & 3) == 0) && ((a.split_stride & 3) == 0);
 #pragma unroll
-      for (int i = 0; i < CPW; i += 4)
-        *reinterpret_cast<float4 *>(crow + i) = make_float4(acc[i], acc[i + 1], acc[i + 2], acc[i + 3]);
-    } else {
+    for (int cb = 0; cb < CPW / BW; ++cb) {
+      const int cols = min(BW, a.N - col0 - cb * BW);
+      if (cols <= 0) break;
 #pragma unroll
-      for (int i = 0; i < CPW; ++i)
-        if (col0 + i < a.N) crow[i] = acc[i];
+      for (int c4 = 0; c4 < BW / 4; ++c4) {
+        const int i = cb * BW + c4 * 4;
+        tile_put(tile, lane, c4, make_float4(acc[i], acc[i + 1], acc[i + 2], acc[i + 3]));
+      }
+      __syncwarp(mask);
+      tile_store<BW>(tile, base + cb * BW, a.ldc, rows, cols, vec, lane);
+      __syncwarp(mask);
     }
   }
 };
@@ -492,6 +570,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     // ------------------------------------------------------ promotion + epilogue (warps 2..9)
     const int q = warp & 3;             // TMEM lane quarter this warp may access
     const int half = (warp - 2) >> 2;   // which half of the tile's columns
+    float4 *epi_tile = reinterpret_cast<float4 *>(smem + (size_t)STAGES * STAGE_BYTES +
+                                                  (size_t)(warp - 2) * EPI_TILE_BYTES);
     int cc = 0;
     bool ok = true;
     for (int t = blockIdx.x; ok && t < args.num_tiles; t += gridDim.x) {
@@ -517,7 +597,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         mbar_arrive(&acc_empty[b]);
       }
       if (!ok) break;
-      EPI::template store<CPW>(args, ep, ks, bz, mb * BM + q * 32 + lane, nb * TBN + half * CPW, acc);
+      EPI::template store<CPW>(args, ep, ks, bz, mb * BM + q * 32 + lane, nb * TBN + half * CPW, acc,
+                               epi_tile);
     }
   }
 
@@ -773,6 +854,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     // ------------------------------------------------------ promotion + epilogue (warps 2..9)
     const int q = warp & 3;
     const int half = (warp - 2) >> 2;
+    float4 *epi_tile = reinterpret_cast<float4 *>(smem + (size_t)PAIR_STAGES * PAIR_STAGE_BYTES +
+                                                  (size_t)(warp - 2) * EPI_TILE_BYTES);
     const uint32_t acc_empty_leader[2] = {in_leader(&acc_empty[0]), in_leader(&acc_empty[1])};
     int cc = 0;
     bool ok = true;
@@ -807,7 +890,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       }
       if (!ok) break;
       EPI::template store<128>(args, ep, ks, bz, mb * 2 * BM + (int)rank * BM + q * 32 + lane,
-                               nb * BN + half * 128, acc);
+                               nb * BN + half * 128, acc, epi_tile);
     }
   }
 
