@@ -81,7 +81,9 @@ def test_fusion_on_and_off_agree(capi):
 
 
 def test_fused_chain_is_one_kernel(capi):
-    """relu(x @ W.T + b) lowers the bias add and ReLU to one fused launch."""
+    """relu(x @ W.T + b) lowers the bias add and ReLU into the GEMM's epilogue (no
+    separate launch); with epilogue fusion off, into one fused launch after the GEMM.
+    Both give the same bits."""
     import nova_b200
 
     F = nova_b200.fusion
@@ -90,6 +92,18 @@ def test_fused_chain_is_one_kernel(capi):
     b = api_cases.T(F, np.random.default_rng(2).standard_normal((16,)))
     y = (x @ w.swapaxes(1, 0) + b).maximum(0.0)
     assert y.is_pending()
-    before = F.stats()["fused_launches"]
-    y.to_numpy()
-    assert F.stats()["fused_launches"] == before + 1
+    s0 = F.stats()
+    got_epi = y.to_numpy()
+    s1 = F.stats()
+    assert s1["fused_launches"] == s0["fused_launches"]
+    assert s1["epilogue_gemms"] == s0["epilogue_gemms"] + 1
+    F.set_gemm_epilogue(False)
+    try:
+        y = (x @ w.swapaxes(1, 0) + b).maximum(0.0)
+        got_plain = y.to_numpy()
+        s2 = F.stats()
+        assert s2["fused_launches"] == s1["fused_launches"] + 1
+        assert s2["epilogue_gemms"] == s1["epilogue_gemms"]
+    finally:
+        F.set_gemm_epilogue(True)
+    assert_bits_equal(got_epi, got_plain, "relu(x W^T + b)")
