@@ -54,7 +54,7 @@ def parse():
     ap.add_argument("--kernel", default=None,
                     help="run one hot-path kernel on a profiling-sized case instead of the step "
                          "(step, gemm, gemm_wgrad, tf32_lo, add, bcast_add, exp, log, sqrt, sum_ax0, "
-                         "sum_ax1, max_ax0, sum_rows64, swapaxes, bias_relu)")
+                         "sum_ax1, max_ax0, sum_rows64, swapaxes, bias_relu, linear_relu)")
     ap.add_argument("--reps", type=int, default=3)
     return ap.parse_args()
 
@@ -616,6 +616,19 @@ def run_kernel(args):
         a, o = _random_device(A, (n,), 3), A.DeviceArray((n,))
         fn = lambda: A.check(L.fz_tf32_lo(o.ptr, a.ptr, n, None))
         work = 8.0 * n
+    elif k == "linear_relu":  # relu(x @ W^T + b) through the API: the GEMM with its epilogue
+        rows, cols, kk = 8192, 4096, 4096
+        rng = np.random.default_rng(SEED + 5)
+        dev = F.CppDevice(F.CppDeviceType.CPU, 0)
+        mk = lambda shp: F.Tensor(list(shp), rng.standard_normal(shp, dtype=np.float32).ravel(),
+                                  F.CppDType.FLOAT32, dev, False)
+        xt, wt, bt = mk((rows, kk)), mk((cols, kk)), mk((cols,))
+        wT = wt.swapaxes(1, 0)
+        F.flush(wT)
+
+        def fn():
+            F.flush((xt @ wT + bt).maximum(0.0))
+        work = 2.0 * rows * cols * kk
     elif k == "bias_relu":  # fused relu(x + b) of the MLP forward through the fusion IR
         rows, cols = 16384, 4096
         dev = F.CppDevice(F.CppDeviceType.CPU, 0)
@@ -650,7 +663,7 @@ def run_kernel(args):
         }[k]
     ms = time_launch(A, fn, reps=args.reps, warm=1)
     F.synchronize()
-    gemm = k.startswith("gemm")
+    gemm = k.startswith("gemm") or k == "linear_relu"
     unit = "TFLOP/s" if gemm else "samples/s" if k == "step" else "GB/s"
     scale = 1e9 if gemm else 1e-3 if k == "step" else 1e6
     print(json.dumps({"kernel": k, "ms": round(ms, 4), unit: round(work / ms / scale, 1)}),

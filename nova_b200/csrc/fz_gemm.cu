@@ -349,6 +349,17 @@ std::string epilogue_class(const fz_program &pg, const int *cls) {
   std::ostringstream o;
   o << "struct GenEpi {\n"
     << "  template <int CPW>\n"
+    << "  static __device__ __forceinline__ void prefetch(const fz_gemm_dev::GemmArgs &a,\n"
+    << "      const fz_gemm_dev::EpiParams &p, int bz, int row, int col0) {\n"
+    << "    if (row >= a.M || col0 >= a.N) return;\n"
+    << "    const int n = min(CPW, a.N - col0);\n"
+    << "    (void)p; (void)bz; (void)n;\n";
+  for (int k = 0; k < nin; ++k)
+    if (cls[k] == 2)
+      o << "    fz_gemm_dev::prefetch_row_l2(p.in[" << k << "] + (long long)bz * p.in_sb[" << k
+        << "] + (long long)row * p.in_sm[" << k << "] + col0, n);\n";
+  o << "  }\n"
+    << "  template <int CPW>\n"
     << "  static __device__ __forceinline__ void store(const fz_gemm_dev::GemmArgs &a,\n"
     << "      const fz_gemm_dev::EpiParams &p, int, int bz, int row, int col0,\n"
     << "      const float (&acc)[CPW], float4 *tile) {\n"
@@ -383,7 +394,8 @@ std::string epilogue_class(const fz_program &pg, const int *cls) {
     if (cls[k] != 2) continue;
     const std::string K = std::to_string(k);
     o << "      float v" << K << "[BW];\n"
-      << "      tile_load<BW>(tile, g" << K << " + cb * BW, p.in_sm[" << K << "], rows, cols, p.vec, lane);\n"
+      << "      if (p.vec) tile_load_async<BW>(tile, g" << K << " + cb * BW, p.in_sm[" << K << "], rows, cols, lane);\n"
+      << "      else tile_load<BW>(tile, g" << K << " + cb * BW, p.in_sm[" << K << "], rows, cols, false, lane);\n"
       << "      __syncwarp(mask);\n"
       << "#pragma unroll\n"
       << "      for (int c4 = 0; c4 < BW / 4; ++c4) {\n"

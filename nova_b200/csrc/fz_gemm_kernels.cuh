@@ -2,6 +2,8 @@
 // the ahead-of-time build and by runtime compilation with a fused epilogue.
 //
 // The kernels are templates over an epilogue class EPI whose
+//   template <int CPW> static void prefetch(args, ep, bz, row, col0)
+// is called when a tile starts (before its MMAs complete) and whose
 //   template <int CPW> static void store(args, ep, ks, bz, row, col0, acc)
 // receives, per epilogue thread, one output row's CPW consecutive accumulator
 // columns [col0, col0 + CPW) in registers and writes them out. StoreEpi stores the
@@ -313,9 +315,49 @@ __device__ __forceinline__ void tile_load(float4 *t, const float *src, long long
   }
 }
 
+// Same as tile_load for 16-byte-aligned rows (dst pitch and src pointer multiples of
+// 16 bytes), but every lane's copies go global -> shared with cp.async, so all of a
+// block's loads are in flight at once and no registers hold them. Past `cols` or
+// `rows` the copy reads fewer (or no) bytes and zero-fills the slot; such a copy
+// points at src itself, which lies inside the tensor.
+template <int BW>
+__device__ __forceinline__ void tile_load_async(float4 *t, const float *src, long long ld,
+                                                int rows, int cols, int lane) {
+  constexpr int LPR = BW / 4, RPI = 32 / LPR;
+  const int c4 = lane % LPR;
+#pragma unroll
+  for (int r0 = 0; r0 < 32; r0 += RPI) {
+    const int r = r0 + lane / LPR;
+    const int left = cols - c4 * 4;
+    const uint32_t bytes = (r < rows && left > 0) ? 4u * (uint32_t)min(left, 4) : 0u;
+    const float *s = bytes ? src + (long long)r * ld + c4 * 4 : src;
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(
+                     smem_u32(t + r * 8 + (c4 ^ (r & 7)))),
+                 "l"(s), "r"(bytes)
+                 : "memory");
+  }
+  asm volatile("cp.async.wait_all;" ::: "memory");
+}
+
+// Pull this lane's row segment [col0, col0 + n) of a full-shape epilogue input into
+// L2 (one prefetch per 128-byte line), issued when a tile starts so that the loads
+// of its epilogue, after the tile's MMAs, hit L2. Only addresses inside the segment.
+__device__ __forceinline__ void prefetch_row_l2(const float *p, int n) {
+  if (n <= 0) return;
+  const uintptr_t first = reinterpret_cast<uintptr_t>(p) & ~(uintptr_t)127;
+  const uintptr_t last = reinterpret_cast<uintptr_t>(p + n - 1);
+  for (uintptr_t a = first; a <= last; a += 128) {
+    const uintptr_t q = a < reinterpret_cast<uintptr_t>(p) ? reinterpret_cast<uintptr_t>(p) : a;
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(q));
+  }
+}
+
 // The plain epilogue: C = product (or this unit's K-split partial), stored through
 // the staging tile. `row` is this lane's row; the warp's rows are row - lane + [0, 32).
 struct StoreEpi {
+  template <int CPW>
+  static __device__ __forceinline__ void prefetch(const GemmArgs &, const EpiParams &, int, int,
+                                                  int) {}
   template <int CPW>
   static __device__ __forceinline__ void store(const GemmArgs &a, const EpiParams &, int ks, int bz,
                                                int row, int col0, const float (&acc)[CPW],
@@ -578,6 +620,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       int mb, nb, bz, ks, kb;
       decode_tile(t, args, mb, nb, bz, ks);
       const int num_k = unit_k_tiles(args, ks, kb);
+      EPI::template prefetch<CPW>(args, ep, bz, mb * BM + q * 32 + lane, nb * TBN + half * CPW);
       float acc[CPW];
 #pragma unroll
       for (int i = 0; i < CPW; ++i) acc[i] = 0.0f;
@@ -863,6 +906,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       int mb, nb, bz, ks, kb;
       decode_tile(t, args, mb, nb, bz, ks);
       const int num_k = unit_k_tiles(args, ks, kb);
+      EPI::template prefetch<128>(args, ep, bz, mb * 2 * BM + (int)rank * BM + q * 32 + lane,
+                                  nb * BN + half * 128);
       float acc[128];
 #pragma unroll
       for (int i = 0; i < 128; ++i) acc[i] = 0.0f;
