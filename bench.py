@@ -54,7 +54,8 @@ def parse():
     ap.add_argument("--kernel", default=None,
                     help="run one hot-path kernel on a profiling-sized case instead of the step "
                          "(step, gemm, gemm_wgrad, tf32_lo, add, bcast_add, exp, log, sqrt, sum_ax0, "
-                         "sum_ax1, max_ax0, sum_rows64, swapaxes, bias_relu, linear_relu)")
+                         "sum_ax1, max_ax0, sum_rows64, swapaxes, bias_relu, linear_relu, gemm_epi_fwd, "
+                         "gemm_epi_bwd)")
     ap.add_argument("--reps", type=int, default=3)
     return ap.parse_args()
 
@@ -598,6 +599,32 @@ def run_kernel(args):
         A.check(L.fz_tf32_lo(wl.ptr, w.ptr, n * kk, None))
         fn = lambda: A.check(L.fz_gemm_f32_split(1, m, n, kk, x.ptr, xl.ptr, ash[1], 0, tA, w.ptr,
                                                   wl.ptr, bsh[1], 0, tB, c.ptr, n, 0, None))
+        work = 2.0 * m * n * kk
+    elif k in ("gemm_epi_fwd", "gemm_epi_bwd"):
+        # the "gemm" product with the MLP's fused epilogues: forward relu(P + b) with its
+        # remainder plane and P (three outputs), backward P * (T + b > 0) with its plane
+        m, n, kk = 8192, 4096, 4096
+        x, w = _random_device(A, (m, kk), 1), _random_device(A, (n, kk), 2)
+        xl, wl = A.DeviceArray((m, kk)), A.DeviceArray((n, kk))
+        A.check(L.fz_tf32_lo(xl.ptr, x.ptr, m * kk, None))
+        A.check(L.fz_tf32_lo(wl.ptr, w.ptr, n * kk, None))
+        Bn, Un, Kn = A.NODE_BINARY, A.NODE_UNARY, A.NODE_CONST
+        bo, uo = A.BINOPS, A.UNOPS
+        bias, full = _random_device(A, (n,), 3), _random_device(A, (m, n), 4)
+        if k == "gemm_epi_fwd":
+            prog = fused_program(A, [(Bn, bo["add"], -1, -2, 0.0), (Kn, 0, 0, 0, 0.0),
+                                     (Bn, bo["maximum"], 0, 1, 0.0), (Un, uo["tf32_lo"], 2, 0, 0.0),
+                                     (Un, uo["copy"], -1, 0, 0.0)], 2, [2, 3, 4])
+            ins = (A.EpiInput * 1)(A.EpiInput(bias.ptr, 0, 0, 1))
+        else:
+            prog = fused_program(A, [(Bn, bo["add"], -2, -3, 0.0), (Kn, 0, 0, 0, 0.0),
+                                     (Bn, bo["gt"], 0, 1, 0.0), (Bn, bo["mul"], -1, 2, 0.0),
+                                     (Un, uo["tf32_lo"], 3, 0, 0.0)], 3, [3, 4])
+            ins = (A.EpiInput * 2)(A.EpiInput(full.ptr, 0, n, 1), A.EpiInput(bias.ptr, 0, 0, 1))
+        outs = [A.DeviceArray((m, n)) for _ in range(prog.num_outputs)]
+        optr = (C.c_void_p * len(outs))(*[o.ptr for o in outs])
+        fn = lambda: A.check(L.fz_gemm_f32_epilogue(1, m, n, kk, x.ptr, xl.ptr, kk, 0, 0, w.ptr, wl.ptr,
+                                                     kk, 0, 1, C.byref(prog), ins, optr, n, 0, None))
         work = 2.0 * m * n * kk
     elif k == "step":  # the MLP training step alone (reps steps), for a launch list
         from nova_b200.mlp import MLP, init_params

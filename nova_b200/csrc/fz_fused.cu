@@ -19,6 +19,8 @@
 
 #include <cstring>
 #include <mutex>
+#include <cstdio>
+#include <cstdlib>
 #include <sstream>
 #include <string>
 #include <unordered_map>
@@ -306,8 +308,19 @@ int nvrtc_cubin(const std::string &src, const char *name, const char *name_expr,
   nvrtcResult r = nvrtcCreateProgram(&prog, src.c_str(), name, 0, nullptr, nullptr);
   if (r != NVRTC_SUCCESS) return fail(FZ_ERR_JIT, std::string("nvrtcCreateProgram: ") + nvrtcGetErrorString(r));
   if (name_expr) nvrtcAddNameExpression(prog, name_expr);
-  const char *opts[] = {"--gpu-architecture=sm_100a", "--fmad=false", "--std=c++17", "-lineinfo"};
-  r = nvrtcCompileProgram(prog, 4, opts);
+  // FZ_NVRTC_VERBOSE=1 prints ptxas' resource usage (registers, spills, shared
+  // memory) of every runtime-compiled kernel to stderr.
+  static const bool verbose = std::getenv("FZ_NVRTC_VERBOSE") != nullptr;
+  const char *opts[] = {"--gpu-architecture=sm_100a", "--fmad=false", "--std=c++17", "-lineinfo",
+                        "--ptxas-options=-v"};
+  r = nvrtcCompileProgram(prog, verbose ? 5 : 4, opts);
+  if (r == NVRTC_SUCCESS && verbose) {
+    size_t n = 0;
+    nvrtcGetProgramLogSize(prog, &n);
+    std::string log(n, '\0');
+    nvrtcGetProgramLog(prog, log.data());
+    std::fprintf(stderr, "[fz nvrtc] %s (%s):\n%s\n", name, name_expr ? name_expr : "", log.c_str());
+  }
   if (r != NVRTC_SUCCESS) {
     size_t n = 0;
     nvrtcGetProgramLogSize(prog, &n);

@@ -267,16 +267,18 @@ __device__ __forceinline__ float4 tile_get(const float4 *t, int r, int c4) { ret
 
 // tile rows [0, rows) x columns [0, cols) -> dst (row pitch ld); 16-byte stores when vec
 // (dst 16-byte aligned, ld a multiple of 4), else per element.
+// `slot`: the block's first float4 slot in each tile row (blocks narrower than the
+// tile row may share the tile: an epilogue's inputs and outputs side by side).
 template <int BW>
 __device__ __forceinline__ void tile_store(const float4 *t, float *dst, long long ld, int rows,
-                                           int cols, bool vec, int lane) {
+                                           int cols, bool vec, int lane, int slot = 0) {
   constexpr int LPR = BW / 4, RPI = 32 / LPR;  // lanes per row, rows per instruction
   const int c4 = lane % LPR;
 #pragma unroll
   for (int r0 = 0; r0 < 32; r0 += RPI) {
     const int r = r0 + lane / LPR;
     if (r < rows) {
-      const float4 v = tile_get(t, r, c4);
+      const float4 v = tile_get(t, r, slot + c4);
       float *d = dst + (long long)r * ld + c4 * 4;
       if (vec && c4 * 4 + 4 <= cols) {
         *reinterpret_cast<float4 *>(d) = v;
@@ -293,7 +295,7 @@ __device__ __forceinline__ void tile_store(const float4 *t, float *dst, long lon
 // src (row pitch ld) rows [0, rows) x columns [0, cols) -> tile, zeros elsewhere.
 template <int BW>
 __device__ __forceinline__ void tile_load(float4 *t, const float *src, long long ld, int rows,
-                                          int cols, bool vec, int lane) {
+                                          int cols, bool vec, int lane, int slot = 0) {
   constexpr int LPR = BW / 4, RPI = 32 / LPR;
   const int c4 = lane % LPR;
 #pragma unroll
@@ -311,7 +313,7 @@ __device__ __forceinline__ void tile_load(float4 *t, const float *src, long long
         if (c4 * 4 + 3 < cols) v.w = s[3];
       }
     }
-    tile_put(t, r, c4, v);
+    tile_put(t, r, slot + c4, v);
   }
 }
 
@@ -322,7 +324,7 @@ __device__ __forceinline__ void tile_load(float4 *t, const float *src, long long
 // points at src itself, which lies inside the tensor.
 template <int BW>
 __device__ __forceinline__ void tile_load_async(float4 *t, const float *src, long long ld,
-                                                int rows, int cols, int lane) {
+                                                int rows, int cols, int lane, int slot = 0) {
   constexpr int LPR = BW / 4, RPI = 32 / LPR;
   const int c4 = lane % LPR;
 #pragma unroll
@@ -332,7 +334,7 @@ __device__ __forceinline__ void tile_load_async(float4 *t, const float *src, lon
     const uint32_t bytes = (r < rows && left > 0) ? 4u * (uint32_t)min(left, 4) : 0u;
     const float *s = bytes ? src + (long long)r * ld + c4 * 4 : src;
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(
-                     smem_u32(t + r * 8 + (c4 ^ (r & 7)))),
+                     smem_u32(t + r * 8 + ((slot + c4) ^ (r & 7)))),
                  "l"(s), "r"(bytes)
                  : "memory");
   }

@@ -132,5 +132,16 @@ def test_gemm_epilogues_compile_for_every_kernel_variant():
     for v in [(0, 0, 256, 1), (0, 1, 256, 1), (0, 0, 16, 0)]:
         rc = L.fz_gemm_epilogue_compile(C.byref(bwd), full_row, *v)
         assert rc == 0, (v, L.fz_last_error())
+    # more full-shape inputs and outputs: 4-column side-by-side blocks, and the
+    # per-output passes when they do not fit the staging tile side by side
+    many = _epi_program(capi, [(B, capi.BINOPS["add"], -1, -2, 0.0), (B, capi.BINOPS["add"], 0, -3, 0.0),
+                               (B, capi.BINOPS["add"], 1, -4, 0.0), (B, capi.BINOPS["mul"], 2, -5, 0.0),
+                               (B, capi.BINOPS["sub"], 3, -6, 0.0)], 6, [1, 2, 3, 4])
+    five = (capi.EpiInput * 5)(*[capi.EpiInput(None, 4096, 64, 1)] * 5)
+    for v in [(0, 0, 256, 1), (0, 0, 16, 0), (1, 0, 64, 0)]:
+        assert L.fz_gemm_epilogue_compile(C.byref(many), five, *v) == 0, (v, L.fz_last_error())
+    two = (capi.EpiInput * 5)(*([capi.EpiInput(None, 4096, 64, 1)] * 2 + [capi.EpiInput(None, 0, 0, 1)] * 3))
+    for v in [(0, 0, 256, 1), (0, 0, 16, 0)]:
+        assert L.fz_gemm_epilogue_compile(C.byref(many), two, *v) == 0, (v, L.fz_last_error())
     # narrow tiles take a K-major B only
     assert L.fz_gemm_epilogue_compile(C.byref(fwd), row, 0, 1, 16, 0) == 1

@@ -42,6 +42,17 @@ def _programs(A):
         "relu_mask": ([(B, bo["add"], -2, -3, 0.0), (K, 0, 0, 0, 0.0), (B, bo["gt"], 0, 1, 0.0),
                        (B, bo["mul"], -1, 2, 0.0), (U, uo["tf32_lo"], 3, 0, 0.0)],
                       ["full", "row"], [3, 4]),
+        # two full-shape inputs and four outputs (inputs and outputs share the staging
+        # tile in 4-column blocks)
+        "two_full_four_out": ([(B, bo["mul"], -1, -2, 0.0), (B, bo["add"], -1, -3, 0.0),
+                               (B, bo["sub"], 0, 1, 0.0), (U, uo["copy"], -1, 0, 0.0)],
+                              ["full", "full"], [0, 1, 2, 3]),
+        # five full-shape inputs and four outputs (too many to share the tile: the
+        # inputs are read per output pass)
+        "five_full_four_out": ([(B, bo["add"], -1, -2, 0.0), (B, bo["add"], 0, -3, 0.0),
+                                (B, bo["add"], 1, -4, 0.0), (B, bo["mul"], 2, -5, 0.0),
+                                (B, bo["sub"], 3, -6, 0.0)],
+                               ["full"] * 5, [1, 2, 3, 4]),
         # a per-row and a scalar input: exp(P / c_i) - s
         "row_scale_exp": ([(B, bo["div"], -1, -2, 0.0), (U, uo["exp"], 0, 0, 0.0),
                            (B, bo["sub"], 1, -3, 0.0)],
@@ -123,7 +134,8 @@ CASES = [
 ]
 
 
-@pytest.mark.parametrize("name", ["bias_relu", "relu_mask", "row_scale_exp"])
+@pytest.mark.parametrize("name", ["bias_relu", "relu_mask", "row_scale_exp", "two_full_four_out",
+                                  "five_full_four_out"])
 @pytest.mark.parametrize("case", CASES, ids=lambda c: "x".join(map(str, c[:4])) + f"-{c[7]}")
 def test_epilogue_equals_gemm_then_program(capi, name, case):
     _run(capi, name, *case)
