@@ -315,6 +315,12 @@ int fz_tf32_lo(float *lo, const float *x, int64_t n, void *stream);
  * output element is accumulated from the same K chunks in the same order. */
 enum fz_gemm_tiles { FZ_GEMM_TILES_AUTO = 0, FZ_GEMM_TILES_SINGLE = 1, FZ_GEMM_TILES_PAIR = 2 };
 int fz_gemm_set_tiles(int mode);
+/* How GEMM kernels write their outputs, for the calls that follow (process-wide):
+ * on (default), through TMA bulk tensor stores from shared-memory staging tiles
+ * wherever every output is 16-byte aligned with a pitch of a multiple of 4 floats;
+ * off, by per-thread stores. Results are identical either way. Replaces no reference
+ * interface (the reference's cblas_sgemm writes C directly). */
+int fz_gemm_set_tma_stores(int on);
 
 /* ---- collectives (data-parallel MLP step) -------------------------------- */
 

@@ -163,9 +163,28 @@ int make_map(CUtensorMap *map, const float *base, bool mn, int64_t rows, int64_t
   return FZ_OK;
 }
 
+// Store map of an output: 3D {N, M, Z} over fp32 with row pitch ld and slice pitch sz,
+// box {bw, 32, 1}, no swizzle (the staging regions are row-major). false when the
+// layout is not one TMA can store (then the epilogue stores per thread).
+bool make_out_map(CUtensorMap *map, float *base, int64_t N, int64_t M, int64_t Z, int64_t ld,
+                  int64_t sz, int bw) {
+  if (Z == 1) sz = ld * M;
+  if (!base || ((uintptr_t)base & 15) || (ld * 4) % 16 || (sz * 4) % 16 || bw < 4) return false;
+  cuuint64_t dims[3] = {(cuuint64_t)N, (cuuint64_t)M, (cuuint64_t)Z};
+  cuuint64_t strides[2] = {(cuuint64_t)(ld * 4), (cuuint64_t)(sz * 4)};
+  cuuint32_t box[3] = {(cuuint32_t)bw, 32, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, (void *)base, dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
 
 std::atomic<int> g_tile_mode{FZ_GEMM_TILES_AUTO};
+// Epilogue outputs through TMA bulk tensor stores where the layout allows (default);
+// off: every output stored per thread (fz_gemm_set_tma_stores).
+std::atomic<bool> g_tma_stores{true};
 
 // Number of K splits for a GEMM of `tiles` output tiles. A split turns one tile
 // into several units over K ranges (multiples of the 256-wide promotion chunk)
@@ -277,8 +296,8 @@ static_assert((size_t)PAIR_STAGES * PAIR_STAGE_BYTES + EPI_SMEM_BYTES + 1024 <= 
 
 template <bool A_MN, bool B_MN, int TBN>
 int launch_gemm(const CUtensorMap &mAh, const CUtensorMap &mAl, const CUtensorMap &mBh,
-                const CUtensorMap &mBl, const GemmArgs &ga, unsigned grid, bool pair,
-                cudaStream_t s) {
+                const CUtensorMap &mBl, const GemmArgs &ga, const EpiParams &ep, unsigned grid,
+                bool pair, cudaStream_t s) {
   static bool attr_done[2][64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -292,7 +311,6 @@ int launch_gemm(const CUtensorMap &mAh, const CUtensorMap &mAl, const CUtensorMa
                            cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     attr_done[pair][dev] = true;
   }
-  const EpiParams ep{};
   if (pair)
     gemm_pair_kernel<A_MN, B_MN, StoreEpi><<<2 * grid, NUM_THREADS, smem, s>>>(mAh, mAl, mBh, mBl, ga, ep);
   else
@@ -306,17 +324,17 @@ int launch_gemm(const CUtensorMap &mAh, const CUtensorMap &mAl, const CUtensorMa
 // Kernel for the operand layouts and tile width (narrow tiles read B K-major).
 int dispatch_gemm(bool a_mn, bool b_mn, int tbn, const CUtensorMap &mAh, const CUtensorMap &mAl,
                   const CUtensorMap &mBh, const CUtensorMap &mBl, const GemmArgs &ga,
-                  unsigned grid, bool pair, cudaStream_t s) {
+                  const EpiParams &ep, unsigned grid, bool pair, cudaStream_t s) {
   if (tbn == 16)
-    return a_mn ? launch_gemm<true, false, 16>(mAh, mAl, mBh, mBl, ga, grid, false, s)
-                : launch_gemm<false, false, 16>(mAh, mAl, mBh, mBl, ga, grid, false, s);
+    return a_mn ? launch_gemm<true, false, 16>(mAh, mAl, mBh, mBl, ga, ep, grid, false, s)
+                : launch_gemm<false, false, 16>(mAh, mAl, mBh, mBl, ga, ep, grid, false, s);
   if (tbn == 64)
-    return a_mn ? launch_gemm<true, false, 64>(mAh, mAl, mBh, mBl, ga, grid, false, s)
-                : launch_gemm<false, false, 64>(mAh, mAl, mBh, mBl, ga, grid, false, s);
-  if (!a_mn && !b_mn) return launch_gemm<false, false, BN>(mAh, mAl, mBh, mBl, ga, grid, pair, s);
-  if (!a_mn && b_mn) return launch_gemm<false, true, BN>(mAh, mAl, mBh, mBl, ga, grid, pair, s);
-  if (a_mn && !b_mn) return launch_gemm<true, false, BN>(mAh, mAl, mBh, mBl, ga, grid, pair, s);
-  return launch_gemm<true, true, BN>(mAh, mAl, mBh, mBl, ga, grid, pair, s);
+    return a_mn ? launch_gemm<true, false, 64>(mAh, mAl, mBh, mBl, ga, ep, grid, false, s)
+                : launch_gemm<false, false, 64>(mAh, mAl, mBh, mBl, ga, ep, grid, false, s);
+  if (!a_mn && !b_mn) return launch_gemm<false, false, BN>(mAh, mAl, mBh, mBl, ga, ep, grid, pair, s);
+  if (!a_mn && b_mn) return launch_gemm<false, true, BN>(mAh, mAl, mBh, mBl, ga, ep, grid, pair, s);
+  if (a_mn && !b_mn) return launch_gemm<true, false, BN>(mAh, mAl, mBh, mBl, ga, ep, grid, pair, s);
+  return launch_gemm<true, true, BN>(mAh, mAl, mBh, mBl, ga, ep, grid, pair, s);
 }
 
 // ---------------------------------------------------------------- fused epilogues
@@ -433,11 +451,88 @@ void epilogue_side_by_side(std::ostringstream &o, const fz_program &pg, const in
     << "    }\n  }\n};\n";
 }
 
+// Regions a TMA-stored epilogue needs per block: its class-2 inputs are copied into
+// regions 0..n2-1 and output j is staged in region j (in place over input j: a lane
+// reads all inputs of a column group before writing that group's outputs, and only
+// its own row). The block width follows from how many fit in the 4 KB tile.
+int tma_regions(const fz_program &pg, const int *cls) {
+  int n2 = 0;
+  for (int k = 0; k + 1 < pg.num_leaves; ++k) n2 += cls[k] == 2;
+  return n2 > pg.num_outputs ? n2 : pg.num_outputs;
+}
+int tma_block_width(const fz_program &pg, const int *cls, int tbn) {
+  const int R = tma_regions(pg, cls);
+  const int bw = R <= 2 ? 16 : R <= 4 ? 8 : R <= 8 ? 4 : 0;
+  return bw < tbn / 2 ? bw : tbn / 2;  // at most the columns per epilogue warp
+}
+
+// The TMA form of the generated epilogue (outputs through omap[j]; see EpiParams).
+// With one region per block two sets alternate, so a block is staged while the
+// previous block's stores still read their region.
+void epilogue_tma(std::ostringstream &o, const fz_program &pg, const int *cls, int bw) {
+  const int nin = pg.num_leaves - 1, nout = pg.num_outputs, R = tma_regions(pg, cls);
+  o << "    constexpr int BW = CPW < " << bw << " ? CPW : " << bw << ";\n"
+    << "    constexpr int R = " << R << ";\n"
+    << "    constexpr int S = (32 / BW) / R >= 2 ? 2 : 1;\n";
+  epilogue_operands(o, nin, cls);
+  o << "#pragma unroll\n"
+    << "    for (int cb = 0; cb < CPW / BW; ++cb) {\n"
+    << "      const int cols = min(BW, a.N - col0 - cb * BW);\n"
+    << "      if (cols <= 0) break;\n"
+    << "      const int set = S == 2 ? (cb & 1) * R : 0;\n"
+    << "      if (S == 1 || cb == 0) store_reads_done<0>(lane, mask);\n"
+    << "      else store_reads_done<1>(lane, mask);\n";
+  std::vector<int> reg(nin, -1);
+  int n2 = 0;
+  for (int k = 0; k < nin; ++k) {
+    if (cls[k] != 2) continue;
+    const std::string K = std::to_string(k);
+    reg[k] = n2++;
+    o << "      region_load_async<BW>(region_ptr(tile, BW, set + " << reg[k] << "), g" << K
+      << " + cb * BW, p.in_sm[" << K << "], rows, cols, lane);\n";
+  }
+  if (n2) o << "      __syncwarp(mask);\n";
+  o << "#pragma unroll\n"
+    << "      for (int c4 = 0; c4 < BW / 4; ++c4) {\n";
+  for (int k = 0; k < nin; ++k) {
+    const std::string K = std::to_string(k);
+    if (cls[k] == 1) epilogue_row_vector(o, k);
+    if (cls[k] == 2)
+      o << "        const float4 x" << K << " = region_get(region_ptr(tile, BW, set + " << reg[k]
+        << "), BW, lane, c4);\n"
+        << "        const float v" << K << "[4] = {x" << K << ".x, x" << K << ".y, x" << K << ".z, x" << K
+        << ".w};\n";
+  }
+  for (int j = 0; j < nout; ++j) o << "        float r" << j << "[4];\n";
+  o << "#pragma unroll\n"
+    << "        for (int e = 0; e < 4; ++e) {\n";
+  for (int j = 0; j < nout; ++j) o << "          float q" << j << ";\n";
+  o << "          fz_eval(acc[cb * BW + c4 * 4 + e], ";
+  for (int k = 0; k < nin; ++k)
+    o << (cls[k] == 0 ? "s" : cls[k] == 1 ? "u" : "v") << k << (cls[k] == 0 ? "" : "[e]") << ", ";
+  for (int j = 0; j < nout; ++j) o << "q" << j << (j + 1 < nout ? ", " : "");
+  o << ");\n";
+  for (int j = 0; j < nout; ++j) o << "          r" << j << "[e] = q" << j << ";\n";
+  o << "        }\n";
+  for (int j = 0; j < nout; ++j)
+    o << "        region_put(region_ptr(tile, BW, set + " << j << "), BW, lane, c4, make_float4(r" << j
+      << "[0], r" << j << "[1], r" << j << "[2], r" << j << "[3]));\n";
+  o << "      }\n"
+    << "      staged_for_tma(mask);\n"
+    << "      if (lane == 0) {\n";
+  for (int j = 0; j < nout; ++j)
+    o << "        tma_store_3d(&p.omap[" << j << "], region_ptr(tile, BW, set + " << j
+      << "), col0 + cb * BW, row0, bz);\n";
+  o << "        tma_store_commit();\n"
+    << "      }\n"
+    << "    }\n  }\n};\n";
+}
+
 // cls[k] of input k: 0 constant along a row (a per-row value or a scalar), 1 a row
 // vector (same for every row: a bias), 2 varying along rows and columns (a tensor of
 // the product's shape). Class-2 inputs are read through the warp's staging tile in
 // whole row segments; class-1 inputs are the same address for every lane.
-std::string epilogue_class(const fz_program &pg, const int *cls) {
+std::string epilogue_class(const fz_program &pg, const int *cls, int tma_bw) {
   const int nin = pg.num_leaves - 1, nout = pg.num_outputs;
   std::ostringstream o;
   o << "struct GenEpi {\n"
@@ -475,6 +570,10 @@ std::string epilogue_class(const fz_program &pg, const int *cls) {
   // 1.123 -> 1.105 ms, the K = 16 one of the MLP 1.91 -> 1.60 ms. Without class-2
   // inputs the per-output passes at 16 columns are faster (bias + ReLU with three
   // outputs: 1.056 ms, against 1.085 side by side at 8 columns).
+  if (tma_bw) {
+    epilogue_tma(o, pg, cls, tma_bw);
+    return o.str();
+  }
   int n2 = 0;
   for (int k = 0; k < nin; ++k) n2 += cls[k] == 2;
   const int side = n2 + nout;
@@ -547,9 +646,9 @@ struct JitEntry {
 std::mutex g_jit_mu;
 std::unordered_map<std::string, JitEntry> g_jit;
 
-std::string epilogue_source(const fz_program &pg, const int *cls) {
+std::string epilogue_source(const fz_program &pg, const int *cls, int tma_bw) {
   return "#define FZ_GEMM_BK " + std::to_string(BK) + "\n" + kGemmKernelSource + "\n" +
-         fz::program_eval_source(pg) + epilogue_class(pg, cls);
+         fz::program_eval_source(pg) + epilogue_class(pg, cls, tma_bw);
 }
 
 std::string epilogue_kernel_name(bool a_mn, bool b_mn, int tbn, bool pair) {
@@ -560,7 +659,7 @@ std::string epilogue_kernel_name(bool a_mn, bool b_mn, int tbn, bool pair) {
 }
 
 int jit_kernel(const fz_program &pg, const int *cls, bool a_mn, bool b_mn, int tbn, bool pair,
-               size_t smem, cudaKernel_t *out) {
+               int tma_bw, size_t smem, cudaKernel_t *out) {
   std::string key(reinterpret_cast<const char *>(&pg),
                   offsetof(fz_program, nodes) + sizeof(fz_node) * pg.num_nodes);
   for (int k = 0; k + 1 < pg.num_leaves; ++k) key.push_back((char)('0' + cls[k]));
@@ -568,6 +667,7 @@ int jit_kernel(const fz_program &pg, const int *cls, bool a_mn, bool b_mn, int t
   key.push_back((char)('0' + a_mn));
   key.push_back((char)('0' + b_mn));
   key += std::to_string(tbn);
+  key += "T" + std::to_string(tma_bw);
   int dev = 0;
   FZ_CUDA(cudaGetDevice(&dev));
   std::lock_guard<std::mutex> lk(g_jit_mu);
@@ -576,7 +676,8 @@ int jit_kernel(const fz_program &pg, const int *cls, bool a_mn, bool b_mn, int t
     std::vector<char> bin;
     std::string lowered;
     const std::string name = epilogue_kernel_name(a_mn, b_mn, tbn, pair);
-    int rc = fz::nvrtc_cubin(epilogue_source(pg, cls), "fz_gemm_epilogue.cu", name.c_str(), &bin, &lowered);
+    int rc = fz::nvrtc_cubin(epilogue_source(pg, cls, tma_bw), "fz_gemm_epilogue.cu", name.c_str(), &bin,
+                             &lowered);
     if (rc) return rc;
     cudaLibrary_t lib;
     FZ_CUDA(cudaLibraryLoadData(&lib, bin.data(), nullptr, nullptr, 0, nullptr, nullptr, 0));
@@ -597,7 +698,8 @@ int launch_epilogue_gemm(const Epilogue &E, const int *cls, const EpiParams &ep,
                          unsigned grid, bool pair, cudaStream_t s) {
   const size_t smem = smem_bytes(pair, tbn);
   cudaKernel_t k = nullptr;
-  int rc = jit_kernel(*E.pg, cls, a_mn, b_mn, tbn, pair, smem, &k);
+  int rc = jit_kernel(*E.pg, cls, a_mn, b_mn, tbn, pair, ep.tma ? tma_block_width(*E.pg, cls, tbn) : 0,
+                      smem, &k);
   if (rc) return rc;
   void *args[] = {const_cast<CUtensorMap *>(&mAh), const_cast<CUtensorMap *>(&mAl),
                   const_cast<CUtensorMap *>(&mBh), const_cast<CUtensorMap *>(&mBl),
@@ -799,10 +901,23 @@ int gemm_impl(int64_t batch, int64_t M, int64_t N, int64_t K, const float *A, co
                 real_splits, (int)kps, wide_mask, err};
     // persistent grid: one CTA (or CTA pair) per SM (pair of SMs)
     const unsigned grid = (unsigned)(num_units < workers ? num_units : workers);
-    if (in_kernel)
+    // outputs stored by TMA when every output's layout allows it
+    if (in_kernel) {
+      const int bw = tma_block_width(*E.pg, cls, tbn);
+      bool tma = ep.vec && bw > 0 && g_tma_stores;
+      for (int k = 0; tma && k < E.pg->num_outputs; ++k)
+        tma = make_out_map(&ep.omap[k], E.outputs[k], N, M, batch, ldc, strideC, bw);
+      ep.tma = tma;
       rc = launch_epilogue_gemm(E, cls, ep, oa.mn, ob.mn, tbn, mAh, mAl, mBh, mBl, ga, grid, pair, s);
-    else
-      rc = dispatch_gemm(oa.mn, ob.mn, tbn, mAh, mAl, mBh, mBl, ga, grid, pair, s);
+    } else {
+      // C, or the K-split partials [split][batch][M][N] as Z = splits x batch slices
+      ep.tma = g_tma_stores && (partial ? make_out_map(&ep.omap[0], partial, N, M, real_splits * batch, N,
+                                                       M * N, tbn / 2 < EPI_BW ? tbn / 2 : EPI_BW)
+                                        : (batch == 1 || strideC % 4 == 0) &&
+                                              make_out_map(&ep.omap[0], C, N, M, batch, ldc, strideC,
+                                                           tbn / 2 < EPI_BW ? tbn / 2 : EPI_BW));
+      rc = dispatch_gemm(oa.mn, ob.mn, tbn, mAh, mAl, mBh, mBl, ga, ep, grid, pair, s);
+    }
     // K-split partials: summed over the splits in a fixed order (deterministic)
     if (!rc && partial) rc = fz_reduce(FZ_RSUM, product ? product : C, partial, 1, real_splits, batch * M * N, s);
     if (!rc && product) rc = epilogue_pass(E, product, batch, M, N, ldc, strideC, s);
@@ -860,7 +975,12 @@ extern "C" int fz_gemm_epilogue_compile(const fz_program *epi, const fz_epi_inpu
   std::vector<char> bin;
   std::string lowered;
   const std::string name = epilogue_kernel_name(a_mn != 0, b_mn != 0, tile_n, pair != 0);
-  return fz::nvrtc_cubin(epilogue_source(*epi, cls), "fz_gemm_epilogue.cu", name.c_str(), &bin, &lowered);
+  // both forms: per-thread stores, and bulk tensor stores from the staging tile
+  int rc2 = fz::nvrtc_cubin(epilogue_source(*epi, cls, 0), "fz_gemm_epilogue.cu", name.c_str(), &bin, &lowered);
+  const int bw = tma_block_width(*epi, cls, tile_n);
+  if (!rc2 && bw)
+    rc2 = fz::nvrtc_cubin(epilogue_source(*epi, cls, bw), "fz_gemm_epilogue.cu", name.c_str(), &bin, &lowered);
+  return rc2;
 }
 
 extern "C" int fz_tf32_lo(float *lo, const float *x, int64_t n, void *stream) {
@@ -871,6 +991,11 @@ extern "C" int fz_tf32_lo(float *lo, const float *x, int64_t n, void *stream) {
   unsigned grid = fz::grid_for(n / 4 + 1, 256, 8, 4);
   lo_kernel<<<grid, 256, 0, s>>>(x, n, n, 1, n, n, 1, lo, nullptr);
   FZ_CHECK_LAUNCH();
+  return FZ_OK;
+}
+
+extern "C" int fz_gemm_set_tma_stores(int on) {
+  g_tma_stores = on != 0;
   return FZ_OK;
 }
 

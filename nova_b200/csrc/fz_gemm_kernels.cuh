@@ -239,13 +239,23 @@ struct GemmArgs {
 // along the columns, a property compiled into the epilogue). Output k is written at
 // out[k] + bz * strideC + row * ldc + col. vec: every column-varying input and
 // every output allows 16-byte accesses at each row.
+//
+// tma: the outputs are written by TMA bulk tensor stores from the staging tile,
+// through omap[k] (output k; the plain epilogue's C or K-split partials in omap[0]):
+// 3D maps {N, M, Z} over fp32 with row pitch ldc, Z = batch (or K splits x batch for
+// partials), boxes of {BW, 32, 1}, no swizzle. The TMA unit clips boxes at N and M.
+// Plain per-thread stores drain at about 15 GB/s per SM while the mainloop's TMA
+// loads run (measured: 9 us per 128 KB output tile per CTA, whatever the access
+// pattern), longer than the MMAs can run ahead; bulk stores leave the SM at once.
 constexpr int EPI_MAX_IN = 11;
 constexpr int EPI_MAX_OUT = 4;
-struct EpiParams {
+struct __align__(64) EpiParams {
+  CUtensorMap omap[EPI_MAX_OUT];
   const float *in[EPI_MAX_IN];
   long long in_sb[EPI_MAX_IN], in_sm[EPI_MAX_IN];
   float *out[EPI_MAX_OUT];
   int vec;
+  int tma;
 };
 
 // ---- warp-cooperative epilogue I/O
@@ -354,6 +364,71 @@ __device__ __forceinline__ void prefetch_row_l2(const float *p, int n) {
   }
 }
 
+// ---- TMA output staging
+//
+// With TMA stores the warp's 4 KB tile is cut into 32 / BW regions of 32 rows x BW
+// floats, row-major (BW * 4 bytes per row), region i at byte i * BW * 128. A lane
+// writes its own row of a region; one lane then issues the region's bulk store.
+// A region is rewritten only after the stores that read it are done reading
+// (cp.async.bulk.wait_group.read by the issuing lane, then a warp barrier).
+__device__ __forceinline__ float4 *region_ptr(float4 *tile, int bw, int i) {
+  return tile + i * bw * 8;  // bw * 128 bytes = bw * 8 float4
+}
+__device__ __forceinline__ void region_put(float4 *reg, int bw, int r, int c4, float4 v) {
+  reg[r * (bw / 4) + c4] = v;
+}
+__device__ __forceinline__ float4 region_get(const float4 *reg, int bw, int r, int c4) {
+  return reg[r * (bw / 4) + c4];
+}
+// Wait (lane 0) until at most `pending` committed store groups still read shared
+// memory, then let the warp go on.
+template <int PENDING>
+__device__ __forceinline__ void store_reads_done(int lane, unsigned mask) {
+  if (lane == 0) asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(PENDING) : "memory");
+  __syncwarp(mask);
+}
+// The warp's generic-proxy writes to the staged regions become visible to the TMA
+// unit; then lane 0 may issue the stores.
+__device__ __forceinline__ void staged_for_tma(unsigned mask) {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  __syncwarp(mask);
+}
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap *map, const void *src, int x, int y,
+                                             int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+__device__ __forceinline__ void tma_store_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// End of an epilogue warp's work: its last bulk stores have completed.
+__device__ __forceinline__ void tma_stores_drain(const EpiParams &ep, int lane) {
+  if (ep.tma && lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+// Copy rows [0, rows) x columns [0, cols) of src (row pitch ld, 16-byte aligned rows)
+// into region `reg` (zeros elsewhere), every lane's copies in flight at once.
+template <int BW>
+__device__ __forceinline__ void region_load_async(float4 *reg, const float *src, long long ld,
+                                                  int rows, int cols, int lane) {
+  constexpr int LPR = BW / 4, RPI = 32 / LPR;
+  const int c4 = lane % LPR;
+#pragma unroll
+  for (int r0 = 0; r0 < 32; r0 += RPI) {
+    const int r = r0 + lane / LPR;
+    const int left = cols - c4 * 4;
+    const uint32_t bytes = (r < rows && left > 0) ? 4u * (uint32_t)min(left, 4) : 0u;
+    const float *s = bytes ? src + (long long)r * ld + c4 * 4 : src;
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(
+                     smem_u32(reg + r * LPR + c4)),
+                 "l"(s), "r"(bytes)
+                 : "memory");
+  }
+  asm volatile("cp.async.wait_all;" ::: "memory");
+}
+
 // The plain epilogue: C = product (or this unit's K-split partial), stored through
 // the staging tile. `row` is this lane's row; the warp's rows are row - lane + [0, 32).
 struct StoreEpi {
@@ -361,8 +436,8 @@ struct StoreEpi {
   static __device__ __forceinline__ void prefetch(const GemmArgs &, const EpiParams &, int, int,
                                                   int) {}
   template <int CPW>
-  static __device__ __forceinline__ void store(const GemmArgs &a, const EpiParams &, int ks, int bz,
-                                               int row, int col0, const float (&acc)[CPW],
+  static __device__ __forceinline__ void store(const GemmArgs &a, const EpiParams &ep, int ks,
+                                               int bz, int row, int col0, const float (&acc)[CPW],
                                                float4 *tile) {
     const int lane = threadIdx.x & 31;
     const int row0 = row - lane;
@@ -370,6 +445,31 @@ struct StoreEpi {
     if (rows <= 0 || col0 >= a.N) return;  // uniform over the warp
     const unsigned mask = __activemask();
     constexpr int BW = CPW < EPI_BW ? CPW : EPI_BW;
+    if (ep.tma) {
+      // two regions: block cb is staged in region cb & 1 while the previous block's
+      // store may still read the other
+      const int z = ks * a.batch + bz;
+#pragma unroll
+      for (int cb = 0; cb < CPW / BW; ++cb) {
+        if (col0 + cb * BW >= a.N) break;
+        float4 *reg = region_ptr(tile, BW, cb & 1);
+        // a tile's first block waits for every earlier store (the previous tile may
+        // have ended in either region)
+        if (cb == 0) store_reads_done<0>(lane, mask);
+        else store_reads_done<1>(lane, mask);
+#pragma unroll
+        for (int c4 = 0; c4 < BW / 4; ++c4) {
+          const int i = cb * BW + c4 * 4;
+          region_put(reg, BW, lane, c4, make_float4(acc[i], acc[i + 1], acc[i + 2], acc[i + 3]));
+        }
+        staged_for_tma(mask);
+        if (lane == 0) {
+          tma_store_3d(&ep.omap[0], reg, col0 + cb * BW, row0, z);
+          tma_store_commit();
+        }
+      }
+      return;
+    }
     float *base = a.C + (int64_t)ks * a.split_stride + (int64_t)bz * a.strideC +
                   (int64_t)row0 * a.ldc + col0;
     const bool vec = ((a.ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(a.C) & 15) == 0) &&
@@ -645,6 +745,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       EPI::template store<CPW>(args, ep, ks, bz, mb * BM + q * 32 + lane, nb * TBN + half * CPW, acc,
                                epi_tile);
     }
+    tma_stores_drain(ep, lane);
   }
 
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -939,6 +1040,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       EPI::template store<128>(args, ep, ks, bz, mb * 2 * BM + (int)rank * BM + q * 32 + lane,
                                nb * BN + half * 128, acc, epi_tile);
     }
+    tma_stores_drain(ep, lane);
   }
 
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");

@@ -288,6 +288,7 @@ int fz_stream_wait_event(void *, void *) { return FZ_OK; }
 int fz_event_destroy(void *) { return FZ_OK; }
 int fz_stream_destroy(void *) { return FZ_OK; }
 int fz_stream_wait(void *, void *) { return FZ_OK; }
+int fz_gemm_set_tma_stores(int) { return FZ_OK; }
 int fz_gemm_set_tiles(int mode) { return mode >= 0 && mode <= 2 ? FZ_OK : fail(FZ_ERR_INVALID, "fz_gemm_set_tiles: unknown mode"); }
 
 int fz_tf32_lo(float *lo, const float *x, int64_t n, void *) {

@@ -97,10 +97,14 @@ def _run(A, name, batch, M, N, K, tA, tB, ldc_pad=0, tiles="auto"):
         A.check(L.fz_gemm_f32_epilogue(batch, M, N, K, da.ptr, None, lda, sA, int(tA), db.ptr, None,
                                        ldb, sB, int(tB), C.byref(prog), epi_in, capi_outs(got), ldc, sC,
                                        None))
+        # the reference product with per-thread stores (the epilogue above uses TMA
+        # stores wherever the outputs allow)
+        A.check(L.fz_gemm_set_tma_stores(0))
         A.check(L.fz_gemm_f32_split(batch, M, N, K, da.ptr, None, lda, sA, int(tA), db.ptr, None, ldb,
                                     sB, int(tB), P.ptr, N, M * N, None))
     finally:
         L.fz_gemm_set_tiles(0)
+        L.fz_gemm_set_tma_stores(1)
     # reference: the program as a fused pass over P
     plan = A.EwisePlan()
     plan.ndim, plan.num_operands = 3, len(outs) + 1 + len(ins)
@@ -139,6 +143,18 @@ CASES = [
 @pytest.mark.parametrize("case", CASES, ids=lambda c: "x".join(map(str, c[:4])) + f"-{c[7]}")
 def test_epilogue_equals_gemm_then_program(capi, name, case):
     _run(capi, name, *case)
+
+
+@pytest.mark.parametrize("name", ["bias_relu", "relu_mask", "two_full_four_out"])
+def test_epilogue_thread_stores(capi, name):
+    """The per-thread-store form of the generated epilogues (TMA stores off)."""
+    L = capi.lib()
+    capi.check(L.fz_gemm_set_tma_stores(0))
+    try:
+        for case in CASES[:3]:
+            _run(capi, name, *case)
+    finally:
+        L.fz_gemm_set_tma_stores(1)
 
 
 def test_epilogue_at_a_hidden_layer_size(capi):

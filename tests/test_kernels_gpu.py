@@ -230,6 +230,50 @@ def test_gemm_3xtf32_cta_pairs(capi, batch, M, N, K, tA, tB):
     assert np.all(np.abs(got - want) <= 1e-5 * bound + 1e-30)
 
 
+def _gemm_into(capi, a, b, tA, tB, ldc, strideC):
+    """fz_gemm_f32 into an output of pitch ldc and slice pitch strideC (padding kept)."""
+    batch = a.shape[0]
+    M = a.shape[2] if tA else a.shape[1]
+    K = a.shape[1] if tA else a.shape[2]
+    N = b.shape[1] if tB else b.shape[2]
+    da, db = capi.DeviceArray.from_numpy(a), capi.DeviceArray.from_numpy(b)
+    dc = capi.DeviceArray.from_numpy(np.full((batch * strideC,), 7.0, np.float32))
+    capi.check(capi.lib().fz_gemm_f32(batch, M, N, K, da.ptr, a.shape[2], a.shape[1] * a.shape[2], int(tA),
+                                      db.ptr, b.shape[2], b.shape[1] * b.shape[2], int(tB), dc.ptr, ldc,
+                                      strideC, None))
+    capi.check(capi.lib().fz_kernel_status())
+    return dc.numpy()
+
+
+@pytest.mark.parametrize("batch,M,N,K,pad,tB", [
+    (1, 2560, 2048, 256, 0, True),    # CTA pairs
+    (1, 300, 200, 100, 0, False),     # single CTAs, ragged M and N
+    (2, 520, 264, 64, 4, True),       # batch, padded pitch
+    (1, 4096, 16, 512, 0, True),      # 16-column tiles
+    (1, 2048, 48, 300, 0, False),     # 64-column tiles
+    (1, 256, 256, 8192, 0, False),    # K split: partials stored by TMA
+    (1, 130, 260, 40, 1, True),       # odd pitch: per-thread stores either way
+])
+def test_gemm_tma_stores_match_thread_stores(capi, batch, M, N, K, pad, tB):
+    """Outputs written by TMA bulk tensor stores equal per-thread stores bit for bit,
+    and neither touches the padding past N."""
+    L = capi.lib()
+    rng = np.random.default_rng(M * 7 + N + K)
+    A = rng.standard_normal((batch, M, K)).astype(np.float32)
+    B = rng.standard_normal((batch, N, K) if tB else (batch, K, N)).astype(np.float32)
+    ldc = N + pad
+    outs = []
+    try:
+        for on in (1, 0):
+            capi.check(L.fz_gemm_set_tma_stores(on))
+            outs.append(_gemm_into(capi, A, B, False, tB, ldc, M * ldc))
+    finally:
+        capi.check(L.fz_gemm_set_tma_stores(1))
+    assert_bits_equal(outs[0], outs[1], "tma vs thread stores")
+    c = outs[0].reshape(batch, M, ldc)
+    assert np.all(c[..., N:] == 7.0)
+
+
 @pytest.mark.parametrize("tA,tB", [(False, True), (True, False)])
 def test_gemm_tile_schedules_agree(capi, tA, tB):
     """The single-CTA and CTA-pair schedules, forced through fz_gemm_set_tiles, give the
