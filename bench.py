@@ -342,10 +342,12 @@ def _random_device(capi, shape, seed):
 
 
 def gemm_roofline(capi, pk, m):
-    """Dominant kernel of the step: gemm_3xtf32_kernel on the [m,4096] x [4096,4096]^T
-    product of layers 2-3, timed live on the library stream with CUDA events. The
-    operands' TF32 remainder planes are split before the timed region (as the step's
-    split cache does), so the timed launches are the GEMM kernel alone."""
+    """Dominant kernel of the step: the 3xTF32 GEMM (gemm_pair_kernel, CTA pairs) on the
+    [m,4096] x [4096,4096]^T product of layers 2-3, timed live on the library stream
+    with CUDA events. The operands' TF32 remainder planes are split before the timed
+    region (as the step's split cache does), so the timed launches are the GEMM kernel
+    alone; in the step the same kernel body runs with fused epilogues (launch list in
+    profiles/mlp_step_launch_list.md)."""
     A, L = capi, capi.lib()
     k = n = 4096
     x, w, c = _random_device(A, (m, k), 11), _random_device(A, (n, k), 12), A.DeviceArray((m, n))
@@ -367,8 +369,8 @@ def gemm_roofline(capi, pk, m):
         for line in summary.read_text().splitlines():
             if line.startswith("dram_bytes_per_launch_full_size:"):
                 traffic = float(line.split(":", 1)[1])
-    return {"kernel": f"gemm_3xtf32_kernel [{m},{k}]x[{n},{k}]^T, N(0,1) operands, "
-                      f"remainder planes split beforehand",
+    return {"kernel": f"gemm_pair_kernel (3xTF32, tcgen05 cta_group::2) [{m},{k}]x[{n},{k}]^T, "
+                      f"N(0,1) operands, remainder planes split beforehand",
             "bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak, 1),
             "unit": "TFLOP/s", "frac": round(achieved / peak, 3), "traffic": traffic,
             "peak_basis": f"{pk['basis']} bf16 {pk['bf16_tflops']} TFLOP/s / 2 (TF32 rate) / 3 (3xTF32)",
