@@ -12,14 +12,15 @@
 // swizzle with 32-byte atoms), selected per operand by template and the MMA's major bits.
 //
 // Main kernel, persistent (one CTA per SM walking 128 x 256 output tiles in grouped
-// order), warp-specialised, 320 threads:
+// order), warp-specialised, 384 threads (registers rebalanced per warpgroup with
+// setmaxnreg: warps 0-3 at 56, the epilogue warpgroups at 224):
 //   warp 0     TMA producer: per k-tile of BK = 16 loads A_hi, A_lo (128 x 16) and
 //              B_hi, B_lo (256 x 16) into a 4-stage ring of 48 KB
 //   warp 1     allocates 2 x 256 TMEM columns; one lane issues, per 8-wide k-step,
 //              tcgen05.mma.kind::tf32 lo*hi, hi*lo, hi*hi, and tcgen05.commit frees
 //              each stage. The K range is cut into chunks of 256; each chunk
 //              accumulates from zero into one of the two TMEM buffers.
-//   warps 2-9  promotion and epilogue: two warps per TMEM lane quarter, each owning
+//   warps 4-11 promotion and epilogue: two warps per TMEM lane quarter, each owning
 //              128 of the 256 columns, tcgen05.ld every finished chunk and add it
 //              into an fp32 register accumulator (IEEE adds), then store C.
 // The tensor core's own fp32 accumulation is truncating, so its error grows with
@@ -294,6 +295,19 @@ static_assert((size_t)PAIR_STAGES * PAIR_STAGE_BYTES + EPI_SMEM_BYTES + 1024 <= 
                   (size_t)TileCfg<16>::NSTAGE * TileCfg<16>::STAGE + EPI_SMEM_BYTES + 1024 <= 232448,
               "shared memory per CTA");
 
+// The kernels split REG_LAUNCH registers per thread between their warpgroups with
+// setmaxnreg (warpgroup 0 gives up what the epilogue warpgroups take). A kernel
+// compiled to another count would make that split wrong, so it is refused here.
+int check_kernel_registers(const void *fn) {
+  cudaFuncAttributes fa{};
+  FZ_CUDA(cudaFuncGetAttributes(&fa, fn));
+  if (fa.numRegs != REG_LAUNCH)
+    return fz::fail(FZ_ERR_CUDA, "GEMM kernel compiled to " + std::to_string(fa.numRegs) +
+                                     " registers per thread; its warpgroup register split needs " +
+                                     std::to_string(REG_LAUNCH));
+  return FZ_OK;
+}
+
 template <bool A_MN, bool B_MN, int TBN>
 int launch_gemm(const CUtensorMap &mAh, const CUtensorMap &mAl, const CUtensorMap &mBh,
                 const CUtensorMap &mBl, const GemmArgs &ga, const EpiParams &ep, unsigned grid,
@@ -302,14 +316,13 @@ int launch_gemm(const CUtensorMap &mAh, const CUtensorMap &mAl, const CUtensorMa
   int dev = 0;
   cudaGetDevice(&dev);
   const size_t smem = smem_bytes(pair, TBN);
-  if (dev < 64 && !attr_done[pair][dev]) {
-    if (pair)
-      cudaFuncSetAttribute(gemm_pair_kernel<A_MN, B_MN, StoreEpi>,
-                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    else
-      cudaFuncSetAttribute(gemm_3xtf32_kernel<A_MN, B_MN, TBN, StoreEpi>,
-                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    attr_done[pair][dev] = true;
+  if (dev >= 64 || !attr_done[pair][dev]) {
+    const void *fn = pair ? (const void *)gemm_pair_kernel<A_MN, B_MN, StoreEpi>
+                          : (const void *)gemm_3xtf32_kernel<A_MN, B_MN, TBN, StoreEpi>;
+    int rc = check_kernel_registers(fn);
+    if (rc) return rc;
+    cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (dev < 64) attr_done[pair][dev] = true;
   }
   if (pair)
     gemm_pair_kernel<A_MN, B_MN, StoreEpi><<<2 * grid, NUM_THREADS, smem, s>>>(mAh, mAl, mBh, mBl, ga, ep);
@@ -681,7 +694,11 @@ int jit_kernel(const fz_program &pg, const int *cls, bool a_mn, bool b_mn, int t
     if (rc) return rc;
     cudaLibrary_t lib;
     FZ_CUDA(cudaLibraryLoadData(&lib, bin.data(), nullptr, nullptr, 0, nullptr, nullptr, 0));
-    FZ_CUDA(cudaLibraryGetKernel(&e.kern, lib, lowered.c_str()));
+    cudaKernel_t kern = nullptr;
+    FZ_CUDA(cudaLibraryGetKernel(&kern, lib, lowered.c_str()));
+    rc = check_kernel_registers((const void *)kern);
+    if (rc) return rc;
+    e.kern = kern;
   }
   if (dev >= 64 || !((e.attr_devices >> dev) & 1)) {
     FZ_CUDA(cudaKernelSetAttributeForDevice(e.kern, cudaFuncAttributeMaxDynamicSharedMemorySize,

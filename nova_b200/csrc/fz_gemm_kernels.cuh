@@ -52,7 +52,21 @@ constexpr int STAGE_BYTES = 2 * TILE_A_BYTES + 2 * TILE_B_BYTES;  // 96 KB
 constexpr int TMEM_COLS = 256;          // one accumulator buffer (BN fp32 columns)
 constexpr int KCHUNK = 16;              // k-tiles per promotion chunk (K = 256)
 constexpr int NUM_EPI_WARPS = 8;        // 2 per TMEM lane quarter
-constexpr int NUM_THREADS = 64 + 32 * NUM_EPI_WARPS;
+// Warp roles: 0 TMA producer, 1 MMA issuer (and TMEM owner), 2-3 idle, 4-11 promotion
+// and epilogue. Registers are rebalanced per warpgroup with setmaxnreg: the launch
+// gives every thread REG_LAUNCH (12 warps = 3 per SM sub-partition: 168 of the 65536);
+// warpgroup 0 (warps 0-3) drops to REG_CTRL and the epilogue warpgroups take what it
+// frees, so their 128 fp32 accumulators per thread leave room for the epilogue program.
+// The launch check in fz_gemm.cu refuses a kernel whose register count is not
+// REG_LAUNCH (the split would not add up: setmaxnreg.inc would wait for registers
+// that no warp frees).
+constexpr int EPI_WARP0 = 4;
+constexpr int NUM_THREADS = 32 * (EPI_WARP0 + NUM_EPI_WARPS);
+constexpr int REG_LAUNCH = 168, REG_CTRL = 56, REG_EPI = 224;
+static_assert(NUM_THREADS * REG_LAUNCH <= 65536, "registers at launch");
+static_assert(128 * REG_CTRL + 32 * NUM_EPI_WARPS * REG_EPI == NUM_THREADS * REG_LAUNCH,
+              "setmaxnreg split uses exactly the launch's registers");
+static_assert(NUM_EPI_WARPS == 8 && EPI_WARP0 == 4, "two epilogue warpgroups after warpgroup 0");
 constexpr unsigned long long kWaitNs = 4000000000ull;  // 4 s per wait
 
 enum : int { kErrNone = 0, kErrTimeoutFull = 1, kErrTimeoutEmpty = 2, kErrTimeoutAcc = 3 };
@@ -522,7 +536,7 @@ __device__ __forceinline__ int unit_k_tiles(const GemmArgs &a, int ks, int &k_be
 
 // Persistent kernel: one CTA per SM walks tiles blockIdx.x, +gridDim.x, ...
 // K is cut into chunks of KCHUNK k-tiles accumulated alternately in two TMEM
-// buffers; warps 2-9 fold each finished chunk into fp32 registers.
+// buffers; warps 4-11 fold each finished chunk into fp32 registers.
 // Per tile width TBN (output columns per tile): 256 for wide products, 64 or 16 for
 // narrow ones (a 16-wide output layer would otherwise compute 256 columns for 16).
 // Narrow tiles use more stages of smaller k-tiles, within the same ~192 KB.
@@ -628,94 +642,100 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
   };
 
-  if (warp == 0) {
-    if (lane == 0) {
-      // ------------------------------------------------------ TMA producer
-      int it = 0;
-      bool ok = true;
-      for (int t = blockIdx.x; ok && t < args.num_tiles; t += gridDim.x) {
-        int mb, nb, bz, ks, kb;
-        decode_tile(t, args, mb, nb, bz, ks);
-        const int nk = unit_k_tiles(args, ks, kb);
-        for (int kt = 0; kt < nk; ++kt, ++it) {
-          const int s = it % STAGES;
-          const uint32_t round = it / STAGES;
-          if (it >= STAGES && !mbar_wait(&empty_bar[s], (round - 1) & 1, &abort_flag)) {
-            ok = false;
-            break;
-          }
-          mbar_expect_tx(&full_bar[s], STAGE_BYTES);
-          const int k0 = kb + kt * BK;
-          load_operand<A_MN, BM>(stage_ptr(s, 0), &mapAh, &full_bar[s], k0, mb * BM, bz, args.wide & 1);
-          load_operand<A_MN, BM>(stage_ptr(s, 1), &mapAl, &full_bar[s], k0, mb * BM, bz, args.wide & 2);
-          load_operand<B_MN, TBN>(stage_ptr(s, 2), &mapBh, &full_bar[s], k0, nb * TBN, bz, args.wide & 4);
-          load_operand<B_MN, TBN>(stage_ptr(s, 3), &mapBl, &full_bar[s], k0, nb * TBN, bz, args.wide & 8);
-        }
-      }
-      if (!ok) {
-        atomicCAS(args.err, kErrNone, kErrTimeoutEmpty);
-        abort_flag = 1;
-        // drain: wait (bounded) for the loads of the last STAGES issued k-tiles
-        for (int i = (it > STAGES ? it - STAGES : 0); i < it; ++i) {
-          const int s = i % STAGES;
-          const uint64_t t0 = globaltimer();
-          while (!mbar_try_wait(&full_bar[s], (i / STAGES) & 1) && globaltimer() - t0 < kWaitNs) {
-          }
-        }
-      }
-    }
-  } else if (warp == 1) {
-    if (lane == 0) {
-      // ------------------------------------------------------ MMA issuer
-      int it = 0, cc = 0;  // k-tile and chunk counters, running across tiles
-      bool ok = true;
-      for (int t = blockIdx.x; ok && t < args.num_tiles; t += gridDim.x) {
-        int mb, nb, bz, ks, kb;
-        decode_tile(t, args, mb, nb, bz, ks);
-        const int num_k = unit_k_tiles(args, ks, kb);
-        for (int kt0 = 0; ok && kt0 < num_k; kt0 += KCHUNK, ++cc) {
-          const int b = cc & 1;
-          if (cc >= 2 && !mbar_wait(&acc_empty[b], ((cc >> 1) - 1) & 1, &abort_flag)) {
-            ok = false;
-            break;
-          }
-          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-          const uint32_t d_tmem = tmem_base + (uint32_t)(b * TMEM_COLS);
-          const int kend = kt0 + KCHUNK < num_k ? kt0 + KCHUNK : num_k;
-          for (int kt = kt0; kt < kend; ++kt, ++it) {
+  // registers rebalanced per warpgroup (setmaxnreg at the top of each warpgroup's
+  // branch, so the compiler allocates each role within its share)
+  if (warp < EPI_WARP0) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(REG_CTRL));
+    if (warp == 0) {
+      if (lane == 0) {
+        // ------------------------------------------------------ TMA producer
+        int it = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; ok && t < args.num_tiles; t += gridDim.x) {
+          int mb, nb, bz, ks, kb;
+          decode_tile(t, args, mb, nb, bz, ks);
+          const int nk = unit_k_tiles(args, ks, kb);
+          for (int kt = 0; kt < nk; ++kt, ++it) {
             const int s = it % STAGES;
-            if (!mbar_wait(&full_bar[s], (it / STAGES) & 1, &abort_flag)) {
+            const uint32_t round = it / STAGES;
+            if (it >= STAGES && !mbar_wait(&empty_bar[s], (round - 1) & 1, &abort_flag)) {
+              ok = false;
+              break;
+            }
+            mbar_expect_tx(&full_bar[s], STAGE_BYTES);
+            const int k0 = kb + kt * BK;
+            load_operand<A_MN, BM>(stage_ptr(s, 0), &mapAh, &full_bar[s], k0, mb * BM, bz, args.wide & 1);
+            load_operand<A_MN, BM>(stage_ptr(s, 1), &mapAl, &full_bar[s], k0, mb * BM, bz, args.wide & 2);
+            load_operand<B_MN, TBN>(stage_ptr(s, 2), &mapBh, &full_bar[s], k0, nb * TBN, bz, args.wide & 4);
+            load_operand<B_MN, TBN>(stage_ptr(s, 3), &mapBl, &full_bar[s], k0, nb * TBN, bz, args.wide & 8);
+          }
+        }
+        if (!ok) {
+          atomicCAS(args.err, kErrNone, kErrTimeoutEmpty);
+          abort_flag = 1;
+          // drain: wait (bounded) for the loads of the last STAGES issued k-tiles
+          for (int i = (it > STAGES ? it - STAGES : 0); i < it; ++i) {
+            const int s = i % STAGES;
+            const uint64_t t0 = globaltimer();
+            while (!mbar_try_wait(&full_bar[s], (i / STAGES) & 1) && globaltimer() - t0 < kWaitNs) {
+            }
+          }
+        }
+      }
+    } else if (warp == 1) {
+      if (lane == 0) {
+        // ------------------------------------------------------ MMA issuer
+        int it = 0, cc = 0;  // k-tile and chunk counters, running across tiles
+        bool ok = true;
+        for (int t = blockIdx.x; ok && t < args.num_tiles; t += gridDim.x) {
+          int mb, nb, bz, ks, kb;
+          decode_tile(t, args, mb, nb, bz, ks);
+          const int num_k = unit_k_tiles(args, ks, kb);
+          for (int kt0 = 0; ok && kt0 < num_k; kt0 += KCHUNK, ++cc) {
+            const int b = cc & 1;
+            if (cc >= 2 && !mbar_wait(&acc_empty[b], ((cc >> 1) - 1) & 1, &abort_flag)) {
               ok = false;
               break;
             }
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            const uint32_t a_hi = smem_u32(stage_ptr(s, 0)), a_lo = smem_u32(stage_ptr(s, 1));
-            const uint32_t b_hi = smem_u32(stage_ptr(s, 2)), b_lo = smem_u32(stage_ptr(s, 3));
-#pragma unroll
-            for (int kk = 0; kk < BK / UMMA_K; ++kk) {
-              const uint64_t dah = operand_desc<A_MN>(a_hi, kk), dal = operand_desc<A_MN>(a_lo, kk);
-              const uint64_t dbh = operand_desc<B_MN>(b_hi, kk), dbl = operand_desc<B_MN>(b_lo, kk);
-              const uint32_t first = (kt == kt0 && kk == 0) ? 0u : 1u;
-              umma_tf32(d_tmem, dal, dbh, kIdesc, first);  // lo * hi
-              umma_tf32(d_tmem, dah, dbl, kIdesc, 1u);     // hi * lo
-              umma_tf32(d_tmem, dah, dbh, kIdesc, 1u);     // hi * hi (largest term last)
+            const uint32_t d_tmem = tmem_base + (uint32_t)(b * TMEM_COLS);
+            const int kend = kt0 + KCHUNK < num_k ? kt0 + KCHUNK : num_k;
+            for (int kt = kt0; kt < kend; ++kt, ++it) {
+              const int s = it % STAGES;
+              if (!mbar_wait(&full_bar[s], (it / STAGES) & 1, &abort_flag)) {
+                ok = false;
+                break;
+              }
+              asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+              const uint32_t a_hi = smem_u32(stage_ptr(s, 0)), a_lo = smem_u32(stage_ptr(s, 1));
+              const uint32_t b_hi = smem_u32(stage_ptr(s, 2)), b_lo = smem_u32(stage_ptr(s, 3));
+  #pragma unroll
+              for (int kk = 0; kk < BK / UMMA_K; ++kk) {
+                const uint64_t dah = operand_desc<A_MN>(a_hi, kk), dal = operand_desc<A_MN>(a_lo, kk);
+                const uint64_t dbh = operand_desc<B_MN>(b_hi, kk), dbl = operand_desc<B_MN>(b_lo, kk);
+                const uint32_t first = (kt == kt0 && kk == 0) ? 0u : 1u;
+                umma_tf32(d_tmem, dal, dbh, kIdesc, first);  // lo * hi
+                umma_tf32(d_tmem, dah, dbl, kIdesc, 1u);     // hi * lo
+                umma_tf32(d_tmem, dah, dbh, kIdesc, 1u);     // hi * hi (largest term last)
+              }
+              umma_commit(&empty_bar[s]);
             }
-            umma_commit(&empty_bar[s]);
+            if (ok) umma_commit(&acc_full[b]);
           }
-          if (ok) umma_commit(&acc_full[b]);
         }
-      }
-      if (!ok) {
-        atomicCAS(args.err, kErrNone, kErrTimeoutFull);
-        abort_flag = 1;
+        if (!ok) {
+          atomicCAS(args.err, kErrNone, kErrTimeoutFull);
+          abort_flag = 1;
+        }
       }
     }
   } else {
-    // ------------------------------------------------------ promotion + epilogue (warps 2..9)
-    const int q = warp & 3;             // TMEM lane quarter this warp may access
-    const int half = (warp - 2) >> 2;   // which half of the tile's columns
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(REG_EPI));
+    // ------------------------------------------------------ promotion + epilogue (warps 4..11)
+    const int q = warp & 3;                     // TMEM lane quarter this warp may access
+    const int half = (warp - EPI_WARP0) >> 2;   // which half of the tile's columns
     float4 *epi_tile = reinterpret_cast<float4 *>(smem + (size_t)STAGES * STAGE_BYTES +
-                                                  (size_t)(warp - 2) * EPI_TILE_BYTES);
+                                                  (size_t)(warp - EPI_WARP0) * EPI_TILE_BYTES);
     int cc = 0;
     bool ok = true;
     for (int t = blockIdx.x; ok && t < args.num_tiles; t += gridDim.x) {
@@ -911,97 +931,103 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     return smem + (size_t)s * PAIR_STAGE_BYTES + (size_t)which * PAIR_TILE_BYTES;
   };
 
-  if (warp == 0) {
-    if (lane == 0) {
-      // ------------------------------------------------------ TMA producer (both CTAs)
-      int it = 0;
-      bool ok = true;
-      for (int t = pair; ok && t < args.num_tiles; t += npairs) {
-        int mb, nb, bz, ks, kb;
-        decode_tile(t, args, mb, nb, bz, ks);
-        const int nk = unit_k_tiles(args, ks, kb);
-        const int row_a = mb * 2 * BM + (int)rank * BM, row_b = nb * BN + (int)rank * BM;
-        for (int kt = 0; kt < nk; ++kt, ++it) {
-          const int s = it % PAIR_STAGES;
-          const uint32_t round = it / PAIR_STAGES;
-          if (it >= PAIR_STAGES && !mbar_wait(&empty_bar[s], (round - 1) & 1, &abort_flag)) {
-            ok = false;
-            break;
+  // registers rebalanced per warpgroup (setmaxnreg at the top of each warpgroup's
+  // branch, so the compiler allocates each role within its share)
+  if (warp < EPI_WARP0) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(REG_CTRL));
+    if (warp == 0) {
+      if (lane == 0) {
+        // ------------------------------------------------------ TMA producer (both CTAs)
+        int it = 0;
+        bool ok = true;
+        for (int t = pair; ok && t < args.num_tiles; t += npairs) {
+          int mb, nb, bz, ks, kb;
+          decode_tile(t, args, mb, nb, bz, ks);
+          const int nk = unit_k_tiles(args, ks, kb);
+          const int row_a = mb * 2 * BM + (int)rank * BM, row_b = nb * BN + (int)rank * BM;
+          for (int kt = 0; kt < nk; ++kt, ++it) {
+            const int s = it % PAIR_STAGES;
+            const uint32_t round = it / PAIR_STAGES;
+            if (it >= PAIR_STAGES && !mbar_wait(&empty_bar[s], (round - 1) & 1, &abort_flag)) {
+              ok = false;
+              break;
+            }
+            if (leader) mbar_expect_tx(&full_bar[s], 2 * PAIR_STAGE_BYTES);
+            const uint32_t fb = in_leader(&full_bar[s]);
+            const int k0 = kb + kt * BK;
+            load_operand_pair<A_MN>(stage_ptr(s, 0), &mapAh, fb, k0, row_a, bz, args.wide & 1);
+            load_operand_pair<A_MN>(stage_ptr(s, 1), &mapAl, fb, k0, row_a, bz, args.wide & 2);
+            load_operand_pair<B_MN>(stage_ptr(s, 2), &mapBh, fb, k0, row_b, bz, args.wide & 4);
+            load_operand_pair<B_MN>(stage_ptr(s, 3), &mapBl, fb, k0, row_b, bz, args.wide & 8);
           }
-          if (leader) mbar_expect_tx(&full_bar[s], 2 * PAIR_STAGE_BYTES);
-          const uint32_t fb = in_leader(&full_bar[s]);
-          const int k0 = kb + kt * BK;
-          load_operand_pair<A_MN>(stage_ptr(s, 0), &mapAh, fb, k0, row_a, bz, args.wide & 1);
-          load_operand_pair<A_MN>(stage_ptr(s, 1), &mapAl, fb, k0, row_a, bz, args.wide & 2);
-          load_operand_pair<B_MN>(stage_ptr(s, 2), &mapBh, fb, k0, row_b, bz, args.wide & 4);
-          load_operand_pair<B_MN>(stage_ptr(s, 3), &mapBl, fb, k0, row_b, bz, args.wide & 8);
         }
-      }
-      if (!ok) {
-        atomicCAS(args.err, kErrNone, kErrTimeoutEmpty);
-        abort_flag = 1;
-        if (leader) {  // drain (bounded): the last PAIR_STAGES k-tiles' loads of the pair
-          for (int i = (it > PAIR_STAGES ? it - PAIR_STAGES : 0); i < it; ++i) {
-            const int s = i % PAIR_STAGES;
-            const uint64_t t0 = globaltimer();
-            while (!mbar_try_wait(&full_bar[s], (i / PAIR_STAGES) & 1) && globaltimer() - t0 < kWaitNs) {
+        if (!ok) {
+          atomicCAS(args.err, kErrNone, kErrTimeoutEmpty);
+          abort_flag = 1;
+          if (leader) {  // drain (bounded): the last PAIR_STAGES k-tiles' loads of the pair
+            for (int i = (it > PAIR_STAGES ? it - PAIR_STAGES : 0); i < it; ++i) {
+              const int s = i % PAIR_STAGES;
+              const uint64_t t0 = globaltimer();
+              while (!mbar_try_wait(&full_bar[s], (i / PAIR_STAGES) & 1) && globaltimer() - t0 < kWaitNs) {
+              }
             }
           }
         }
       }
-    }
-  } else if (warp == 1) {
-    if (lane == 0 && leader) {
-      // ------------------------------------------------------ MMA issuer (leader only)
-      int it = 0, cc = 0;
-      bool ok = true;
-      for (int t = pair; ok && t < args.num_tiles; t += npairs) {
-        int mb, nb, bz, ks, kb;
-        decode_tile(t, args, mb, nb, bz, ks);
-        const int num_k = unit_k_tiles(args, ks, kb);
-        for (int kt0 = 0; ok && kt0 < num_k; kt0 += KCHUNK, ++cc) {
-          const int b = cc & 1;
-          if (cc >= 2 && !mbar_wait(&acc_empty[b], ((cc >> 1) - 1) & 1, &abort_flag)) {
-            ok = false;
-            break;
-          }
-          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-          const uint32_t d_tmem = tmem_base + (uint32_t)(b * TMEM_COLS);
-          const int kend = kt0 + KCHUNK < num_k ? kt0 + KCHUNK : num_k;
-          for (int kt = kt0; kt < kend; ++kt, ++it) {
-            const int s = it % PAIR_STAGES;
-            if (!mbar_wait(&full_bar[s], (it / PAIR_STAGES) & 1, &abort_flag)) {
+    } else if (warp == 1) {
+      if (lane == 0 && leader) {
+        // ------------------------------------------------------ MMA issuer (leader only)
+        int it = 0, cc = 0;
+        bool ok = true;
+        for (int t = pair; ok && t < args.num_tiles; t += npairs) {
+          int mb, nb, bz, ks, kb;
+          decode_tile(t, args, mb, nb, bz, ks);
+          const int num_k = unit_k_tiles(args, ks, kb);
+          for (int kt0 = 0; ok && kt0 < num_k; kt0 += KCHUNK, ++cc) {
+            const int b = cc & 1;
+            if (cc >= 2 && !mbar_wait(&acc_empty[b], ((cc >> 1) - 1) & 1, &abort_flag)) {
               ok = false;
               break;
             }
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            const uint32_t a_hi = smem_u32(stage_ptr(s, 0)), a_lo = smem_u32(stage_ptr(s, 1));
-            const uint32_t b_hi = smem_u32(stage_ptr(s, 2)), b_lo = smem_u32(stage_ptr(s, 3));
-#pragma unroll
-            for (int kk = 0; kk < BK / UMMA_K; ++kk) {
-              const uint64_t dah = operand_desc<A_MN>(a_hi, kk), dal = operand_desc<A_MN>(a_lo, kk);
-              const uint64_t dbh = operand_desc<B_MN>(b_hi, kk), dbl = operand_desc<B_MN>(b_lo, kk);
-              const uint32_t first = (kt == kt0 && kk == 0) ? 0u : 1u;
-              umma_tf32_pair(d_tmem, dal, dbh, kIdesc, first);  // lo * hi
-              umma_tf32_pair(d_tmem, dah, dbl, kIdesc, 1u);     // hi * lo
-              umma_tf32_pair(d_tmem, dah, dbh, kIdesc, 1u);     // hi * hi
+            const uint32_t d_tmem = tmem_base + (uint32_t)(b * TMEM_COLS);
+            const int kend = kt0 + KCHUNK < num_k ? kt0 + KCHUNK : num_k;
+            for (int kt = kt0; kt < kend; ++kt, ++it) {
+              const int s = it % PAIR_STAGES;
+              if (!mbar_wait(&full_bar[s], (it / PAIR_STAGES) & 1, &abort_flag)) {
+                ok = false;
+                break;
+              }
+              asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+              const uint32_t a_hi = smem_u32(stage_ptr(s, 0)), a_lo = smem_u32(stage_ptr(s, 1));
+              const uint32_t b_hi = smem_u32(stage_ptr(s, 2)), b_lo = smem_u32(stage_ptr(s, 3));
+  #pragma unroll
+              for (int kk = 0; kk < BK / UMMA_K; ++kk) {
+                const uint64_t dah = operand_desc<A_MN>(a_hi, kk), dal = operand_desc<A_MN>(a_lo, kk);
+                const uint64_t dbh = operand_desc<B_MN>(b_hi, kk), dbl = operand_desc<B_MN>(b_lo, kk);
+                const uint32_t first = (kt == kt0 && kk == 0) ? 0u : 1u;
+                umma_tf32_pair(d_tmem, dal, dbh, kIdesc, first);  // lo * hi
+                umma_tf32_pair(d_tmem, dah, dbl, kIdesc, 1u);     // hi * lo
+                umma_tf32_pair(d_tmem, dah, dbh, kIdesc, 1u);     // hi * hi
+              }
+              umma_commit_pair(&empty_bar[s]);
             }
-            umma_commit_pair(&empty_bar[s]);
+            if (ok) umma_commit_pair(&acc_full[b]);
           }
-          if (ok) umma_commit_pair(&acc_full[b]);
         }
-      }
-      if (!ok) {
-        atomicCAS(args.err, kErrNone, kErrTimeoutFull);
-        abort_flag = 1;
+        if (!ok) {
+          atomicCAS(args.err, kErrNone, kErrTimeoutFull);
+          abort_flag = 1;
+        }
       }
     }
   } else {
-    // ------------------------------------------------------ promotion + epilogue (warps 2..9)
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(REG_EPI));
+    // ------------------------------------------------------ promotion + epilogue (warps 4..11)
     const int q = warp & 3;
-    const int half = (warp - 2) >> 2;
+    const int half = (warp - EPI_WARP0) >> 2;
     float4 *epi_tile = reinterpret_cast<float4 *>(smem + (size_t)PAIR_STAGES * PAIR_STAGE_BYTES +
-                                                  (size_t)(warp - 2) * EPI_TILE_BYTES);
+                                                  (size_t)(warp - EPI_WARP0) * EPI_TILE_BYTES);
     const uint32_t acc_empty_leader[2] = {in_leader(&acc_empty[0]), in_leader(&acc_empty[1])};
     int cc = 0;
     bool ok = true;
