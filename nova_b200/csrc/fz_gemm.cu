@@ -165,7 +165,8 @@ int make_map(CUtensorMap *map, const float *base, bool mn, int64_t rows, int64_t
 }
 
 // Store map of an output: 3D {N, M, Z} over fp32 with row pitch ld and slice pitch sz,
-// box {bw, 32, 1}, no swizzle (the staging regions are row-major). false when the
+// box {bw, 32, 1}: for bw = 32 the 128-byte swizzle of the staging tile's full-width
+// layout (tile_put), else no swizzle (row-major staging regions). false when the
 // layout is not one TMA can store (then the epilogue stores per thread).
 bool make_out_map(CUtensorMap *map, float *base, int64_t N, int64_t M, int64_t Z, int64_t ld,
                   int64_t sz, int bw) {
@@ -176,7 +177,8 @@ bool make_out_map(CUtensorMap *map, float *base, int64_t N, int64_t M, int64_t Z
   cuuint32_t box[3] = {(cuuint32_t)bw, 32, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   return g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, (void *)base, dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  bw == 32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
                   CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -474,6 +476,9 @@ int tma_regions(const fz_program &pg, const int *cls) {
   return n2 > pg.num_outputs ? n2 : pg.num_outputs;
 }
 int tma_block_width(const fz_program &pg, const int *cls, int tbn) {
+  int n2 = 0;
+  for (int k = 0; k + 1 < pg.num_leaves; ++k) n2 += cls[k] == 2;
+  if (tbn / 2 >= 32 && n2 == 0) return 32;  // the per-output form (epilogue_tma_wide)
   const int R = tma_regions(pg, cls);
   const int bw = R <= 2 ? 16 : R <= 4 ? 8 : R <= 8 ? 4 : 0;
   return bw < tbn / 2 ? bw : tbn / 2;  // at most the columns per epilogue warp
@@ -541,6 +546,56 @@ void epilogue_tma(std::ostringstream &o, const fz_program &pg, const int *cls, i
     << "    }\n  }\n};\n";
 }
 
+// The wide TMA form, for warps owning at least 32 columns and programs without
+// class-2 inputs: per 32-column block, for each output the program is evaluated over
+// the block, staged in the whole tile (128-byte-swizzled tile_put layout) and written
+// by one 32 x 32 TMA store. Outputs are stored one at a time, so a block costs nout
+// stores of 4 KB (a store has a fixed cost of about 0.5 us: staging, proxy fence and
+// issue, timed with %globaltimer). Same box, [8192,4096]x[4096,4096]^T: bias+ReLU with
+// three outputs 1.044 -> 1.031 ms against the 8-column region form. With a class-2
+// input (loaded per lane into registers) the ReLU-mask gradient measured 1.049 ->
+// 1.063 ms, so class-2 inputs keep the region form, whose cp.async copies coalesce.
+void epilogue_tma_wide(std::ostringstream &o, const fz_program &pg, const int *cls) {
+  const int nin = pg.num_leaves - 1, nout = pg.num_outputs;
+  o << "    constexpr int BW = 32;\n";
+  epilogue_operands(o, nin, cls);
+  o << "#pragma unroll\n"
+    << "    for (int cb = 0; cb < CPW / BW; ++cb) {\n"
+    << "      const int cols = min(BW, a.N - col0 - cb * BW);\n"
+    << "      if (cols <= 0) break;\n";
+  for (int j = 0; j < nout; ++j) {
+    o << "      {\n"
+      << "        float r[BW];\n"
+      << "#pragma unroll\n"
+      << "        for (int c4 = 0; c4 < BW / 4; ++c4) {\n";
+    for (int k = 0; k < nin; ++k)
+      if (cls[k] == 1) epilogue_row_vector(o, k);
+    o << "#pragma unroll\n"
+      << "          for (int e = 0; e < 4; ++e) {\n"
+      << "            const int c = c4 * 4 + e;\n";
+    for (int q = 0; q < nout; ++q) o << "            float q" << q << ";\n";
+    o << "            fz_eval(acc[cb * BW + c], ";
+    for (int k = 0; k < nin; ++k)
+      o << (cls[k] == 0 ? "s" + std::to_string(k) : "u" + std::to_string(k) + "[e]") << ", ";
+    for (int q = 0; q < nout; ++q) o << "q" << q << (q + 1 < nout ? ", " : "");
+    o << ");\n"
+      << "            r[c] = q" << j << ";\n"
+      << "          }\n"
+      << "        }\n"
+      << "        store_reads_done<0>(lane, mask);\n"
+      << "#pragma unroll\n"
+      << "        for (int c4 = 0; c4 < BW / 4; ++c4)\n"
+      << "          tile_put(tile, lane, c4, make_float4(r[c4 * 4], r[c4 * 4 + 1], r[c4 * 4 + 2], r[c4 * 4 + 3]));\n"
+      << "        staged_for_tma(mask);\n"
+      << "        if (lane == 0) {\n"
+      << "          tma_store_3d(&p.omap[" << j << "], tile, col0 + cb * BW, row0, bz);\n"
+      << "          tma_store_commit();\n"
+      << "        }\n"
+      << "      }\n";
+  }
+  o << "    }\n  }\n};\n";
+}
+
 // cls[k] of input k: 0 constant along a row (a per-row value or a scalar), 1 a row
 // vector (same for every row: a bias), 2 varying along rows and columns (a tensor of
 // the product's shape). Class-2 inputs are read through the warp's staging tile in
@@ -583,6 +638,10 @@ std::string epilogue_class(const fz_program &pg, const int *cls, int tma_bw) {
   // 1.123 -> 1.105 ms, the K = 16 one of the MLP 1.91 -> 1.60 ms. Without class-2
   // inputs the per-output passes at 16 columns are faster (bias + ReLU with three
   // outputs: 1.056 ms, against 1.085 side by side at 8 columns).
+  if (tma_bw == 32) {
+    epilogue_tma_wide(o, pg, cls);
+    return o.str();
+  }
   if (tma_bw) {
     epilogue_tma(o, pg, cls, tma_bw);
     return o.str();
@@ -928,11 +987,12 @@ int gemm_impl(int64_t batch, int64_t M, int64_t N, int64_t K, const float *A, co
       rc = launch_epilogue_gemm(E, cls, ep, oa.mn, ob.mn, tbn, mAh, mAl, mBh, mBl, ga, grid, pair, s);
     } else {
       // C, or the K-split partials [split][batch][M][N] as Z = splits x batch slices
+      // (32-column swizzled boxes when a warp owns at least 32 columns; see StoreEpi)
+      const int sbw = tbn / 2 >= 32 ? 32 : tbn / 2 < EPI_BW ? tbn / 2 : EPI_BW;
       ep.tma = g_tma_stores && (partial ? make_out_map(&ep.omap[0], partial, N, M, real_splits * batch, N,
-                                                       M * N, tbn / 2 < EPI_BW ? tbn / 2 : EPI_BW)
+                                                       M * N, sbw)
                                         : (batch == 1 || strideC % 4 == 0) &&
-                                              make_out_map(&ep.omap[0], C, N, M, batch, ldc, strideC,
-                                                           tbn / 2 < EPI_BW ? tbn / 2 : EPI_BW));
+                                              make_out_map(&ep.omap[0], C, N, M, batch, ldc, strideC, sbw));
       rc = dispatch_gemm(oa.mn, ob.mn, tbn, mAh, mAl, mBh, mBl, ga, ep, grid, pair, s);
     }
     // K-split partials: summed over the splits in a fixed order (deterministic)

@@ -459,6 +459,30 @@ struct StoreEpi {
     if (rows <= 0 || col0 >= a.N) return;  // uniform over the warp
     const unsigned mask = __activemask();
     constexpr int BW = CPW < EPI_BW ? CPW : EPI_BW;
+    if (ep.tma && CPW >= 32) {
+      // 32-column blocks: the whole 4 KB tile in the 128-byte-swizzled layout of
+      // tile_put, one 32 x 32 box per store (the map swizzles the same way). A block
+      // is staged once the previous block's store has read the tile (a short wait; a
+      // store's fixed cost, about 0.5 us of staging, proxy fence and issue, is what
+      // the wider blocks halve).
+      const int z = ks * a.batch + bz;
+#pragma unroll
+      for (int cb = 0; cb < CPW / 32; ++cb) {
+        if (col0 + cb * 32 >= a.N) break;
+        store_reads_done<0>(lane, mask);
+#pragma unroll
+        for (int c4 = 0; c4 < 8; ++c4) {
+          const int i = cb * 32 + c4 * 4;
+          tile_put(tile, lane, c4, make_float4(acc[i], acc[i + 1], acc[i + 2], acc[i + 3]));
+        }
+        staged_for_tma(mask);
+        if (lane == 0) {
+          tma_store_3d(&ep.omap[0], tile, col0 + cb * 32, row0, z);
+          tma_store_commit();
+        }
+      }
+      return;
+    }
     if (ep.tma) {
       // two regions: block cb is staged in region cb & 1 while the previous block's
       // store may still read the other
