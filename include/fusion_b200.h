@@ -75,7 +75,7 @@ int fz_stream_sync(void *stream);
 /* The calling thread's upload stream on the current device (created on first use):
  * host-to-device copies issued on it run beside the compute stream's work; a block
  * fz_malloc'd on it and freed on another stream is reused only after that stream has
- * passed the free. */
+ * passed the free. Null if the stream could not be created (fz_last_error says why). */
 void *fz_upload_stream(void);
 /* A second non-blocking stream on the current device (for collectives that overlap the
  * thread's compute stream), and its release. */
@@ -108,6 +108,9 @@ int fz_pool_release(void);
 /* reserved: bytes the current device's pool holds (in use, cached or pool-internal);
  * used: bytes handed out by fz_malloc and not freed yet. */
 int fz_pool_stats(size_t *reserved, size_t *used);
+/* bytes: freed blocks the current device's block cache holds for reuse (not yet
+ * returned to the driver pool). */
+int fz_pool_cached(size_t *bytes);
 
 /* Copies. d2h waits for the stream so the host buffer is valid on return.
  * Replaces the host std::copy of tensor_to_numpy / set_values
@@ -321,6 +324,26 @@ int fz_gemm_set_tiles(int mode);
  * off, by per-thread stores. Results are identical either way. Replaces no reference
  * interface (the reference's cblas_sgemm writes C directly). */
 int fz_gemm_set_tma_stores(int on);
+/* Launches of the GEMM kernels so far in this process, by schedule: counts[0] CTA-pair
+ * launches, [1] single-CTA launches, [2] launches split over K, [3] launches with a
+ * fused epilogue program. Instrumentation for tests and measurement; replaces no
+ * reference interface. */
+int fz_gemm_stats(int64_t counts[4]);
+/* Device time of each GEMM main-kernel launch (instrumentation; no reference
+ * counterpart). fz_gemm_timing(1) clears the records and starts recording a CUDA
+ * event pair around every launch on its own stream, up to FZ_GEMM_TIMING_MAX
+ * launches; fz_gemm_timing(0) clears and stops. fz_gemm_timing_read waits for the
+ * recorded launches and copies up to `max` records, in launch order. */
+#define FZ_GEMM_TIMING_MAX 4096
+typedef struct fz_gemm_timing_rec {
+  int64_t batch, M, N, K;
+  int32_t pair;      /* CTA-pair kernel */
+  int32_t epilogue;  /* fused epilogue program compiled in */
+  int32_t splits;    /* K splits (partials summed by a separate launch, not timed here) */
+  float ms;          /* event-timed duration of the launch */
+} fz_gemm_timing_rec;
+int fz_gemm_timing(int on);
+int fz_gemm_timing_read(fz_gemm_timing_rec *out, int max, int *count);
 
 /* ---- collectives (data-parallel MLP step) -------------------------------- */
 

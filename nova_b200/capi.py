@@ -59,6 +59,12 @@ class EpiInput(C.Structure):
                 ("col_stride", C.c_int64)]
 
 
+class GemmTimingRec(C.Structure):
+    _fields_ = [("batch", C.c_int64), ("M", C.c_int64), ("N", C.c_int64), ("K", C.c_int64),
+                ("pair", C.c_int32), ("epilogue", C.c_int32), ("splits", C.c_int32),
+                ("ms", C.c_float)]
+
+
 def header_symbols() -> list[str]:
     """Function names declared in include/fusion_b200.h."""
     text = HEADER.read_text()
@@ -121,6 +127,9 @@ def lib() -> C.CDLL:
         L.fz_timer_destroy.argtypes = [vp]
         L.fz_host_alloc.argtypes = [C.POINTER(C.c_void_p), C.c_size_t]
         L.fz_host_free.argtypes = [vp]
+        L.fz_gemm_stats.argtypes = [C.POINTER(C.c_int64)]
+        L.fz_gemm_timing.argtypes = [C.c_int]
+        L.fz_gemm_timing_read.argtypes = [C.POINTER(GemmTimingRec), C.c_int, C.POINTER(C.c_int)]
         L.fz_comm_init.argtypes = [C.POINTER(C.c_void_p), C.c_int, C.c_int, C.c_char_p]
         L.fz_comm_allreduce.argtypes = [vp, vp, vp, i64, f, vp]
         L.fz_comm_broadcast.argtypes = [vp, vp, i64, C.c_int, vp]
@@ -202,3 +211,11 @@ def make_plan(out_shape, operand_shapes) -> EwisePlan:
         for d in range(nd):
             p.stride_bytes[k][d] = st[d]
     return p
+
+
+def gemm_timing_read(max_records: int = 4096) -> list:
+    """The GEMM launches recorded since fz_gemm_timing(1), with their device times."""
+    recs = (GemmTimingRec * max_records)()
+    n = C.c_int()
+    check(lib().fz_gemm_timing_read(recs, max_records, C.byref(n)))
+    return list(recs[:n.value])

@@ -184,6 +184,59 @@ bool make_out_map(CUtensorMap *map, float *base, int64_t N, int64_t M, int64_t Z
 
 int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
 
+// Launch counters by schedule (fz_gemm_stats): CTA-pair launches, single-CTA launches,
+// launches split over K, launches with a fused epilogue program compiled in.
+std::atomic<int64_t> g_stat_pair{0}, g_stat_single{0}, g_stat_ksplit{0}, g_stat_epilogue{0};
+
+// Per-launch device timing of the main GEMM kernel (fz_gemm_timing): an event pair
+// recorded around the launch on its stream. Events are pooled and reused.
+struct TimedLaunch {
+  fz_gemm_timing_rec rec;
+  cudaEvent_t start, stop;
+};
+std::mutex g_timing_mu;
+bool g_timing_on = false;
+std::vector<TimedLaunch> g_timed;
+std::vector<cudaEvent_t> g_event_pool;
+
+cudaEvent_t pooled_event() {
+  if (!g_event_pool.empty()) {
+    cudaEvent_t e = g_event_pool.back();
+    g_event_pool.pop_back();
+    return e;
+  }
+  cudaEvent_t e = nullptr;
+  if (cudaEventCreate(&e) != cudaSuccess) return nullptr;
+  return e;
+}
+
+// Brackets one main-kernel launch with an event pair while timing is on.
+struct LaunchTimer {
+  TimedLaunch t{};
+  bool on = false;
+  cudaStream_t s;
+  LaunchTimer(int64_t batch, int64_t M, int64_t N, int64_t K, bool pair, bool epi, int splits,
+              cudaStream_t stream)
+      : s(stream) {
+    std::lock_guard<std::mutex> lk(g_timing_mu);
+    if (!g_timing_on || g_timed.size() >= FZ_GEMM_TIMING_MAX) return;
+    t.rec = fz_gemm_timing_rec{batch, M, N, K, pair ? 1 : 0, epi ? 1 : 0, splits, 0.0f};
+    t.start = pooled_event();
+    t.stop = pooled_event();
+    on = t.start && t.stop && cudaEventRecord(t.start, s) == cudaSuccess;
+  }
+  void done(int rc) {
+    if (!on) return;
+    std::lock_guard<std::mutex> lk(g_timing_mu);
+    if (rc == FZ_OK && cudaEventRecord(t.stop, s) == cudaSuccess) {
+      g_timed.push_back(t);
+    } else {
+      g_event_pool.push_back(t.start);
+      g_event_pool.push_back(t.stop);
+    }
+  }
+};
+
 std::atomic<int> g_tile_mode{FZ_GEMM_TILES_AUTO};
 // Epilogue outputs through TMA bulk tensor stores where the layout allows (default);
 // off: every output stored per thread (fz_gemm_set_tma_stores).
@@ -977,6 +1030,10 @@ int gemm_impl(int64_t batch, int64_t M, int64_t N, int64_t K, const float *A, co
                 real_splits, (int)kps, wide_mask, err};
     // persistent grid: one CTA (or CTA pair) per SM (pair of SMs)
     const unsigned grid = (unsigned)(num_units < workers ? num_units : workers);
+    (pair ? g_stat_pair : g_stat_single).fetch_add(1, std::memory_order_relaxed);
+    if (real_splits > 1) g_stat_ksplit.fetch_add(1, std::memory_order_relaxed);
+    if (in_kernel) g_stat_epilogue.fetch_add(1, std::memory_order_relaxed);
+    LaunchTimer timer(batch, M, N, K, pair, in_kernel, real_splits, s);
     // outputs stored by TMA when every output's layout allows it
     if (in_kernel) {
       const int bw = tma_block_width(*E.pg, cls, tbn);
@@ -995,6 +1052,7 @@ int gemm_impl(int64_t batch, int64_t M, int64_t N, int64_t K, const float *A, co
                                               make_out_map(&ep.omap[0], C, N, M, batch, ldc, strideC, sbw));
       rc = dispatch_gemm(oa.mn, ob.mn, tbn, mAh, mAl, mBh, mBl, ga, ep, grid, pair, s);
     }
+    timer.done(rc);
     // K-split partials: summed over the splits in a fixed order (deterministic)
     if (!rc && partial) rc = fz_reduce(FZ_RSUM, product ? product : C, partial, 1, real_splits, batch * M * N, s);
     if (!rc && product) rc = epilogue_pass(E, product, batch, M, N, ldc, strideC, s);
@@ -1080,5 +1138,42 @@ extern "C" int fz_gemm_set_tiles(int mode) {
   FZ_REQUIRE(mode == FZ_GEMM_TILES_AUTO || mode == FZ_GEMM_TILES_SINGLE || mode == FZ_GEMM_TILES_PAIR,
              "fz_gemm_set_tiles: unknown mode " + std::to_string(mode));
   g_tile_mode.store(mode, std::memory_order_relaxed);
+  return FZ_OK;
+}
+
+extern "C" int fz_gemm_stats(int64_t counts[4]) {
+  FZ_REQUIRE(counts, "fz_gemm_stats: null pointer");
+  counts[0] = g_stat_pair.load();
+  counts[1] = g_stat_single.load();
+  counts[2] = g_stat_ksplit.load();
+  counts[3] = g_stat_epilogue.load();
+  return FZ_OK;
+}
+
+extern "C" int fz_gemm_timing(int on) {
+  std::lock_guard<std::mutex> lk(g_timing_mu);
+  for (TimedLaunch &t : g_timed) {
+    g_event_pool.push_back(t.start);
+    g_event_pool.push_back(t.stop);
+  }
+  g_timed.clear();
+  g_timing_on = on != 0;
+  return FZ_OK;
+}
+
+extern "C" int fz_gemm_timing_read(fz_gemm_timing_rec *out, int max, int *count) {
+  FZ_REQUIRE(count && (out || max == 0) && max >= 0, "fz_gemm_timing_read: bad arguments");
+  std::lock_guard<std::mutex> lk(g_timing_mu);
+  int n = 0;
+  for (TimedLaunch &t : g_timed) {
+    if (n >= max) break;
+    FZ_CUDA(cudaEventSynchronize(t.stop));
+    float ms = 0.0f;
+    FZ_CUDA(cudaEventElapsedTime(&ms, t.start, t.stop));
+    out[n] = t.rec;
+    out[n].ms = ms;
+    ++n;
+  }
+  *count = n;
   return FZ_OK;
 }

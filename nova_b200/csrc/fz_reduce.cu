@@ -488,7 +488,14 @@ extern "C" int fz_reduce(int op, float *out, const float *in, int64_t outer, int
 // device) race on it and must be serialised by the caller.
 namespace {
 
+// Size of the fixed array. The split plans above bound the partials a reduction
+// needs by the SM count: the row path splits only when rows < 4 * SMs, so it writes
+// rows * splits < 8 * SMs partials; the column path splits only when its column
+// groups (base) number fewer than 1024 * SMs and writes splits * outer * inner <
+// 4 * (1024 * SMs + base) < 8 * 1024 * SMs. 2^21 floats covers every plan on GPUs of
+// up to 256 SMs (B200: 148); a GPU with more is refused on first use.
 constexpr int64_t kNoAllocScratchFloats = int64_t(1) << 21;
+constexpr int64_t kNoAllocPartialsPerSm = 8 * 1024;
 static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchFloats];
 
 std::mutex g_noalloc_mu;
@@ -500,6 +507,10 @@ int noalloc_scratch(float **p) {
   FZ_REQUIRE(dev >= 0 && dev < 64, "fz_reduce_noalloc: device ordinal out of range");
   std::lock_guard<std::mutex> lk(g_noalloc_mu);
   if (!g_noalloc_ptr[dev]) {
+    if (kNoAllocPartialsPerSm * fz::num_sms() > kNoAllocScratchFloats)
+      return fz::fail(FZ_ERR_INVALID, "fz_reduce_noalloc: this GPU has " + std::to_string(fz::num_sms()) +
+                                          " SMs; the fixed scratch covers the split plans of at most " +
+                                          std::to_string(kNoAllocScratchFloats / kNoAllocPartialsPerSm));
     void *q = nullptr;
     cudaError_t e = cudaGetSymbolAddress(&q, g_noalloc_scratch);
     if (e != cudaSuccess) return fz::cuda_fail(e, "cudaGetSymbolAddress(scratch)", __FILE__, __LINE__);

@@ -221,13 +221,22 @@ int fz_event_destroy(void *event) {
   return FZ_OK;
 }
 
+int release_stream_blocks(cudaStream_t s);  // block cache, below
+
 static thread_local cudaStream_t t_upload[kMaxDevices] = {};
 
 void *fz_upload_stream(void) {
   int d = current_device();
   if (!t_upload[d]) {
     setup_device(d);
-    cudaStreamCreateWithFlags(&t_upload[d], cudaStreamNonBlocking);
+    cudaStream_t s = nullptr;
+    cudaError_t e = cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking);
+    if (e != cudaSuccess) {
+      // reported through fz_last_error; the caller gets null and must not copy
+      cuda_fail(e, "creating the upload stream", __FILE__, __LINE__);
+      return nullptr;
+    }
+    t_upload[d] = s;
   }
   return (void *)t_upload[d];
 }
@@ -242,7 +251,15 @@ int fz_stream_create(void **stream) {
 
 int fz_stream_destroy(void *stream) {
   if (!stream) return FZ_OK;
-  FZ_CUDA(cudaStreamDestroy((cudaStream_t)stream));
+  cudaStream_t s = (cudaStream_t)stream;
+  // The block cache keys free lists by stream handle, and a later fz_stream_create
+  // may return the same handle: hand this stream's cached blocks back to the pool now
+  // (each free ordered after the stream's work, and after its free point when it was
+  // freed elsewhere), and re-home its live blocks to the thread's compute stream, so
+  // their eventual free does not file them under a handle that no longer exists.
+  int rc = release_stream_blocks(s);
+  if (rc) return rc;
+  FZ_CUDA(cudaStreamDestroy(s));
   return FZ_OK;
 }
 
@@ -342,6 +359,37 @@ int release_cached(int device) {
 }
 }  // namespace
 
+// The block cache's part of fz_stream_destroy (see there).
+int release_stream_blocks(cudaStream_t s) {
+  std::vector<CachedBlock> blocks;
+  {
+    std::lock_guard<std::mutex> lk(g_cache_mu);
+    auto it = g_free.find(s);
+    if (it != g_free.end()) {
+      for (auto &kv : it->second.by_size) {
+        for (const CachedBlock &c : kv.second) blocks.push_back(c);
+        g_cached_bytes[it->second.device] -= kv.first * kv.second.size();
+      }
+      g_free.erase(it);
+    }
+    bool have = false;
+    for (const auto &kv : g_live) have = have || kv.second.home == s;
+    if (have) {
+      const cudaStream_t home = resolve(nullptr);
+      for (auto &kv : g_live)
+        if (kv.second.home == s) kv.second.home = home;
+    }
+  }
+  cudaError_t e = cudaSuccess;
+  for (const CachedBlock &c : blocks) {
+    if (c.ready && e == cudaSuccess) e = cudaStreamWaitEvent(s, c.ready, 0);
+    if (e == cudaSuccess) e = cudaFreeAsync(c.ptr, s);
+    if (c.ready) cudaEventDestroy(c.ready);
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "fz_stream_destroy: returning cached blocks", __FILE__, __LINE__);
+  return FZ_OK;
+}
+
 int fz_malloc(void **ptr, size_t bytes, void *stream) {
   FZ_REQUIRE(ptr, "fz_malloc: null pointer");
   *ptr = nullptr;
@@ -432,6 +480,15 @@ int fz_pool_release(void) {
   FZ_CUDA(cudaGetDevice(&d));
   FZ_REQUIRE(d < kMaxDevices, "fz_pool_release: device index out of range");
   return release_cached(d);
+}
+
+int fz_pool_cached(size_t *bytes) {
+  FZ_REQUIRE(bytes, "fz_pool_cached: null pointer");
+  int d = 0;
+  FZ_CUDA(cudaGetDevice(&d));
+  std::lock_guard<std::mutex> lk(g_cache_mu);
+  *bytes = d < kMaxDevices ? g_cached_bytes[d] : 0;
+  return FZ_OK;
 }
 
 int fz_pool_stats(size_t *reserved, size_t *used) {

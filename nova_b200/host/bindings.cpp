@@ -370,6 +370,10 @@ PYBIND11_MODULE(fusion, m) {
   m.def("set_split_cache", &set_split_cache_enabled, py::arg("enabled"),
         "Keep GEMM operands' TF32 remainder planes with their buffers (default on).");
   m.def("split_cache_enabled", &split_cache_enabled);
+  m.def("set_swap_views", &set_swap_views_enabled, py::arg("enabled"),
+        "Keep swapaxes of the last two axes (Nova's .T) as a view that GEMMs read in place "
+        "(default on); off materialises every swapaxes where it is called.");
+  m.def("swap_views_enabled", &swap_views_enabled);
   m.def("set_gemm_epilogue", &set_gemm_epilogue_enabled, py::arg("enabled"),
         "Defer each GEMM so the elementwise program reading its product runs in the GEMM's "
         "epilogue (default on); off launches every GEMM where it is called.");
@@ -387,6 +391,8 @@ PYBIND11_MODULE(fusion, m) {
     d["kernel_launches"] = fz_launch_count();
     d["fused_launches"] = fused_launches();
     d["epilogue_gemms"] = epilogue_gemms();
+    d["swap_materializations"] = swap_materializations();
+    d["lo_splits"] = lo_splits();
     d["fused_kernels_compiled"] = fz_fused_cache_size();
     size_t r = 0, u = 0;
     if (fz_pool_stats(&r, &u) == FZ_OK) {

@@ -112,6 +112,14 @@ static int64_t g_fused_launches = 0;
 constexpr int kNodeLimit = 40;   // below FZ_MAX_NODES, leaving room for dedupe slack
 constexpr int kLeafLimit = 10;   // below FZ_MAX_LEAVES
 
+static int64_t g_lo_splits = 0;  // separate split passes (planes not made by a producer)
+int64_t lo_splits() { return g_lo_splits; }
+static bool g_swap_views = true;
+static int64_t g_swap_materializations = 0;
+void set_swap_views_enabled(bool on) { g_swap_views = on; }
+bool swap_views_enabled() { return g_swap_views; }
+int64_t swap_materializations() { return g_swap_materializations; }
+
 void set_fusion_enabled(bool on) { g_fusion = on; }
 bool fusion_enabled() { return g_fusion; }
 int64_t fused_launches() { return g_fused_launches; }
@@ -175,6 +183,7 @@ static void operand_strides(const std::vector<size_t> &s, const std::vector<size
 }
 
 static void lower_gemm(Expr *e);
+static void lower_swap(Expr *e);
 
 namespace {
 struct Lowering {
@@ -204,8 +213,10 @@ struct Lowering {
   int visit(const Expr *e) {
     if (overflow) return 0;
     if (e == acc) return -1;
-    // any other pending GEMM is a plain product read as a leaf
+    // any other pending GEMM is a plain product read as a leaf, and a pending
+    // swapaxes view is materialised and read as a leaf
     if (e->kind == Expr::Gemm) lower_gemm(const_cast<Expr *>(e));
+    if (e->kind == Expr::Swap) lower_swap(const_cast<Expr *>(e));
     if (e->kind == Expr::Leaf) return -1 - leaf_index(e);
     auto it = node_of.find(e);
     if (it != node_of.end()) return it->second;
@@ -348,6 +359,24 @@ static void reduce_view(const Expr &e, int64_t &outer, int64_t &len, int64_t &in
   }
 }
 
+// A swapaxes(-1, -2) view read by something other than a GEMM or a swapaxes: the
+// source (lowered first if pending) transposed into a buffer by the transpose kernel.
+static void lower_swap(Expr *e) {
+  if (e->a->kind != Expr::Leaf) materialize(e->a);
+  const std::vector<size_t> &src = e->a->shape;
+  std::vector<int64_t> shp(src.begin(), src.end());
+  const int nd = (int)shp.size();
+  auto out = std::make_shared<DeviceBuffer>(e->numel());
+  if (e->numel() > 0)
+    fz_check(fz_swapaxes(out->ptr, e->a->buf->ptr, shp.data(), nd, nd - 2, nd - 1, nullptr), "fz_swapaxes");
+  ++g_swap_materializations;
+  e->kind = Expr::Leaf;
+  e->buf = std::move(out);
+  e->a.reset();
+  e->nodes_ub = 0;
+  e->leaves_ub = 1;
+}
+
 // A pending GEMM lowered by itself: the product into a buffer.
 static void lower_gemm(Expr *e) {
   const GemmSpec &g = *e->gemm;
@@ -382,7 +411,8 @@ struct EpiScan {
     switch (e->kind) {
       case Expr::Leaf:
       case Expr::Const: return;
-      case Expr::Reduce: ok = false; return;
+      case Expr::Reduce:
+      case Expr::Swap: ok = false; return;
       case Expr::Gemm:
         gemm = e;
         ++gemms;
@@ -553,6 +583,10 @@ static bool try_epilogue(const std::vector<ExprPtr> &roots, const std::vector<bo
 void materialize(const ExprPtr &ep) {
   Expr *e = ep.get();
   if (e->kind == Expr::Leaf) return;
+  if (e->kind == Expr::Swap) {
+    lower_swap(e);
+    return;
+  }
   if (e->kind == Expr::Gemm) {
     lower_gemm(e);
     return;
@@ -604,7 +638,7 @@ void materialize(const ExprPtr &ep) {
 void materialize_with_lo(const ExprPtr &ep) {
   Expr *e = ep.get();
   if (e->kind == Expr::Leaf || e->kind == Expr::Const || e->kind == Expr::Reduce ||
-      e->numel() == 0) {
+      e->kind == Expr::Swap || e->numel() == 0) {
     materialize(ep);
     return;
   }
@@ -688,9 +722,10 @@ void materialize_group(const std::vector<ExprPtr> &eps) {
 }
 
 static ExprPtr make_op(Expr::Kind kind, int op, ExprPtr a, ExprPtr b, std::vector<size_t> shape) {
-  // reductions are lowered on their own, never inside an elementwise program
-  if (a && a->kind == Expr::Reduce) materialize(a);
-  if (b && b->kind == Expr::Reduce) materialize(b);
+  // reductions are lowered on their own, never inside an elementwise program, and an
+  // elementwise op reads a swapaxes view materialised
+  if (a && (a->kind == Expr::Reduce || a->kind == Expr::Swap)) materialize(a);
+  if (b && (b->kind == Expr::Reduce || b->kind == Expr::Swap)) materialize(b);
   // size policy: keep every pending program within the fused-kernel limits
   auto nodes = [&]() { return 1 + a->nodes_ub + (b ? b->nodes_ub : 0); };
   auto leaves = [&]() { return a->leaves_ub + (b ? b->leaves_ub : 0); };
@@ -712,6 +747,14 @@ static ExprPtr make_op(Expr::Kind kind, int op, ExprPtr a, ExprPtr b, std::vecto
 }
 
 // ---------------------------------------------------------------- RawTensor
+// The calling thread's upload stream; null from the library means it could not be
+// created, and the copy must not fall back to another stream silently.
+static void *upload_stream() {
+  void *up = fz_upload_stream();
+  if (!up) fz_check(FZ_ERR_CUDA, "fz_upload_stream");
+  return up;
+}
+
 void RawTensor::set_contiguous_strides() {
   strides_.assign(shape_.size(), 0);
   int64_t r = 1;
@@ -732,7 +775,7 @@ RawTensor::RawTensor(std::vector<size_t> shape, const float *data, DType dtype, 
   // still running (the next step's inputs while the current step computes). The host
   // waits for the copy itself, so `data` may be reused or freed on return as with a
   // synchronous copy; compute work submitted afterwards is ordered after it.
-  void *up = fz_upload_stream();
+  void *up = upload_stream();
   auto buf = std::make_shared<DeviceBuffer>(n, up);
   if (n) {
     fz_check(fz_memcpy_h2d(buf->ptr, data, n * sizeof(float), up), "fz_memcpy_h2d");
@@ -782,7 +825,7 @@ void RawTensor::to_host(float *dst) const {
   // read back on the upload stream once the compute stream has produced the value;
   // for a value flushed earlier that point is its ready event, so the copy does not
   // wait for compute work submitted since (the next step)
-  void *up = fz_upload_stream();
+  void *up = upload_stream();
   const DeviceBuffer *b = expr()->buf.get();
   if (b && b->ready) fz_check(fz_stream_wait_event(up, b->ready), "fz_stream_wait_event");
   else fz_check(fz_stream_wait(up, nullptr), "fz_stream_wait");
@@ -990,15 +1033,27 @@ static const float *tf32_lo_plane(const RawTensor &t, int64_t ld, int64_t stride
     auto lo = std::make_shared<DeviceBuffer>(b.numel);
     fz_check(fz_tf32_lo(lo->ptr, b.ptr, (int64_t)b.numel, nullptr), "fz_tf32_lo");
     b.tf32_lo = std::move(lo);
+    ++g_lo_splits;
   }
   return b.tf32_lo->ptr;
 }
 
-RawTensor matmul(const RawTensor &A, const RawTensor &B, bool transA, bool transB) {
-  FB_CHECK(A.is_initialised(), "matmul: A uninitialised");
-  FB_CHECK(B.is_initialised(), "matmul: B uninitialised");
-  FB_CHECK(A.dtype() == B.dtype(), "matmul: dtype mismatch");
-  FB_CHECK(A.device() == B.device(), "matmul: device mismatch");
+// An operand that is a swapaxes(-1, -2) view is read as its source in the other
+// layout (K-major <-> MN-major): W.T in `x @ W.T` is W read K-major, and the
+// backward's `g @ swapaxes(W.T)` is W read MN-major; nothing is transposed.
+static RawTensor gemm_operand(const RawTensor &T, bool &trans) {
+  const ExprPtr &e = T.expr();
+  if (e->kind != Expr::Swap) return T;
+  trans = !trans;
+  return RawTensor(e->a, T.dtype(), T.device());
+}
+
+RawTensor matmul(const RawTensor &A0, const RawTensor &B0, bool transA, bool transB) {
+  FB_CHECK(A0.is_initialised(), "matmul: A uninitialised");
+  FB_CHECK(B0.is_initialised(), "matmul: B uninitialised");
+  FB_CHECK(A0.dtype() == B0.dtype(), "matmul: dtype mismatch");
+  FB_CHECK(A0.device() == B0.device(), "matmul: device mismatch");
+  const RawTensor A = gemm_operand(A0, transA), B = gemm_operand(B0, transB);
   const auto &as = A.shape(), &bs = B.shape();
   if (as.size() < 2 || bs.size() < 2) throw std::runtime_error("matmul: expected rank >= 2");
   const size_t ar = as.size(), br = bs.size();
@@ -1057,8 +1112,47 @@ RawTensor matmul(const RawTensor &A, const RawTensor &B, bool transA, bool trans
   return RawTensor(std::move(e), A.dtype(), A.device());
 }
 
-// fusion::math::linalg::swapaxes (ops/Linalg.hpp:109-128): a materialised copy;
-// rank < 2 or equal axes give an unchanged copy.
+// The pending product (A B)^T as the pending product B^T A^T: the operands trade
+// places and layouts, nothing is transposed. The swapaxes of a weight gradient
+// (SwapAxes backward of `W.T`) so lands in W's layout straight from the GEMM.
+static ExprPtr transposed_gemm(const Expr &g) {
+  const GemmSpec &s = *g.gemm;
+  auto t = std::make_shared<GemmSpec>();
+  t->batch = s.batch;
+  t->M = s.N;
+  t->N = s.M;
+  t->K = s.K;
+  t->pa = s.pb;
+  t->la = s.lb;
+  t->lda = s.ldb;
+  t->sA = s.sB;
+  t->transA = !s.transB;
+  t->pb = s.pa;
+  t->lb = s.la;
+  t->ldb = s.lda;
+  t->sB = s.sA;
+  t->transB = !s.transA;
+  t->keep_a = s.keep_b;
+  t->keep_la = s.keep_lb;
+  t->keep_b = s.keep_a;
+  t->keep_lb = s.keep_la;
+  auto e = std::make_shared<Expr>();
+  e->kind = Expr::Gemm;
+  e->shape = g.shape;
+  std::swap(e->shape[e->shape.size() - 1], e->shape[e->shape.size() - 2]);
+  e->gemm = std::move(t);
+  e->nodes_ub = 0;
+  e->leaves_ub = 1;
+  return e;
+}
+
+// fusion::math::linalg::swapaxes (ops/Linalg.hpp:109-128) has copy semantics: rank < 2
+// or equal axes give an unchanged copy, other axes a transposed copy. A swap of the
+// last two axes (Nova's `.T`, _tensor.py:91-98) is kept as a view (Expr::Swap) that
+// the consumer resolves: a GEMM reads the source in the other layout, a swapaxes of a
+// view gives back the source, a pending product becomes the transposed product, and
+// any other reader materialises it. Values are never shared with later in-place
+// writes: those rebind the source's Storage to a new Expr, and the view keeps the old.
 RawTensor swapaxes(const RawTensor &x, int a1, int a2) {
   FB_CHECK(x.is_initialised(), "swapaxes: uninitialised tensor");
   const int nd = (int)x.rank();
@@ -1072,6 +1166,18 @@ RawTensor swapaxes(const RawTensor &x, int a1, int a2) {
   if (n1 == n2) return RawTensor(x.expr(), x.dtype(), x.device());
   std::vector<size_t> oshape = x.shape();
   std::swap(oshape[n1], oshape[n2]);
+  const ExprPtr &xe = x.expr();
+  if (g_swap_views && std::min(n1, n2) == nd - 2 && std::max(n1, n2) == nd - 1) {
+    if (xe->kind == Expr::Swap) return RawTensor(xe->a, x.dtype(), x.device());
+    if (xe->kind == Expr::Gemm) return RawTensor(transposed_gemm(*xe), x.dtype(), x.device());
+    auto e = std::make_shared<Expr>();
+    e->kind = Expr::Swap;
+    e->shape = oshape;
+    e->a = xe;
+    e->nodes_ub = 0;
+    e->leaves_ub = 1;
+    return RawTensor(std::move(e), x.dtype(), x.device());
+  }
   std::vector<int64_t> shp(x.shape().begin(), x.shape().end());
   const float *in = x.data();
   auto buf = std::make_shared<DeviceBuffer>(x.size());
@@ -1102,9 +1208,14 @@ void sub_inplace(RawTensor &x, const RawTensor &y) {
   if (x.shape() == y.shape()) {
     // lowered now, as one fused program with y's pending ops: an updated value (a
     // parameter) is read again and again, and left pending it would be inlined into
-    // every reader, growing by one term with every update
+    // every reader, growing by one term with every update. A value whose previous
+    // one was split for a GEMM (a weight) gets its TF32 remainder plane from the same
+    // program, so the next GEMM reading it needs no split pass.
+    const ExprPtr &old = x.expr();
+    const bool split = split_cache_enabled() && old->kind == Expr::Leaf && old->buf && old->buf->tf32_lo;
     x.storage()->expr = make_op(Expr::Binary, FZ_SUB, x.expr(), y.expr(), x.shape());
-    materialize(x.storage()->expr);
+    if (split) materialize_with_lo(x.storage()->expr);
+    else materialize(x.storage()->expr);
     return;
   }
   const size_t n = x.size();

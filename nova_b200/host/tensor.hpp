@@ -95,7 +95,11 @@ struct Expr {
   // lowered over it runs in the GEMM's epilogue (fz_gemm_f32_epilogue), and the
   // product itself is stored only if something else still holds the node; lowered by
   // any other reader, it is a plain GEMM into a buffer.
-  enum Kind { Leaf, Const, Unary, Binary, Reduce, Gemm } kind;
+  // Swap: `a` with its last two axes exchanged (swapaxes(-1, -2), Nova's `.T`), kept as
+  // a view: a GEMM reads the source in the other operand layout, a swapaxes of it
+  // gives the source back, and any other reader gets it materialised by the
+  // transpose kernel.
+  enum Kind { Leaf, Const, Unary, Binary, Reduce, Gemm, Swap } kind;
   int op = 0;  // fz_binop / fz_unop / fz_redop
   std::vector<size_t> shape;
   std::shared_ptr<Expr> a, b;
@@ -134,6 +138,14 @@ bool gemm_epilogue_enabled();
 int64_t epilogue_gemms();
 // Lower a pending node to one fused kernel (no-op for a Leaf).
 void materialize(const ExprPtr &e);
+// Keep `swapaxes(-1, -2)` pending as a view (on by default; off materialises every
+// swapaxes where it is called, as the reference does).
+void set_swap_views_enabled(bool on);
+bool swap_views_enabled();
+int64_t swap_materializations();
+// TF32 remainder planes split by a separate pass (fz_tf32_lo) so far: operands whose
+// plane no producing kernel wrote (host uploads, values lowered without a plane).
+int64_t lo_splits();
 // Lower a pending node and its TF32 remainder plane in one fused pass (GEMM operands).
 void materialize_with_lo(const ExprPtr &e);
 // Lower several pending nodes of one shape as outputs of one fused program.

@@ -168,6 +168,9 @@ class Ref:
                                    C.POINTER(C.c_void_p)]
         L.ref_mlp_step.argtypes = [C.c_void_p, C.c_void_p, C.POINTER(C.c_void_p),
                                    C.POINTER(C.c_void_p), C.c_int, C.c_float, _f32p]
+        L.ref_mlp_step_grads.argtypes = [C.c_void_p, C.c_void_p, C.POINTER(C.c_void_p),
+                                         C.POINTER(C.c_void_p), C.c_int, C.c_float, _f32p,
+                                         C.POINTER(C.c_void_p)]
         L.ref_last_error.restype = C.c_char_p
 
     def _check(self, h):
@@ -217,8 +220,9 @@ class Ref:
             raise RuntimeError(self.lib.ref_last_error().decode())
         return [_RefTensor(self.lib, out[i]).numpy() for i in range(n)]
 
-    def mlp_step(self, X, Y, Ws, bs, lr):
-        """One reference MLP training step; returns (new Ws, new bs, loss)."""
+    def mlp_step(self, X, Y, Ws, bs, lr, grads=False):
+        """One reference MLP training step; returns (new Ws, new bs, loss), and with
+        grads=True also the gradients [(gW_i, gb_i)] the engine computed."""
         tX, tY = self.tensor(X), self.tensor(Y)
         tW = [self.tensor(w) for w in Ws]
         tb = [self.tensor(b) for b in bs]
@@ -226,10 +230,19 @@ class Ref:
         Wa = (C.c_void_p * n)(*[t.h for t in tW])
         ba = (C.c_void_p * n)(*[t.h for t in tb])
         loss = np.empty((X.shape[0], Ws[-1].shape[0]), dtype=np.float32)
-        rc = self.lib.ref_mlp_step(tX.h, tY.h, Wa, ba, n, C.c_float(lr), _fp(loss))
+        if not grads:
+            rc = self.lib.ref_mlp_step(tX.h, tY.h, Wa, ba, n, C.c_float(lr), _fp(loss))
+            if rc:
+                raise RuntimeError(self.lib.ref_last_error().decode())
+            return [t.numpy() for t in tW], [t.numpy() for t in tb], loss
+        ga = (C.c_void_p * (2 * n))()
+        rc = self.lib.ref_mlp_step_grads(tX.h, tY.h, Wa, ba, n, C.c_float(lr), _fp(loss), ga)
+        hs = [_RefTensor(self.lib, ga[i]) if ga[i] else None for i in range(2 * n)]
         if rc:
             raise RuntimeError(self.lib.ref_last_error().decode())
-        return [t.numpy() for t in tW], [t.numpy() for t in tb], loss
+        gr = [(hs[2 * i].numpy() if hs[2 * i] else None, hs[2 * i + 1].numpy() if hs[2 * i + 1] else None)
+              for i in range(n)]
+        return [t.numpy() for t in tW], [t.numpy() for t in tb], loss, gr
 
 
 def have_ref() -> bool:

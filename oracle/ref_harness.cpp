@@ -218,8 +218,10 @@ int ref_backward(const char *name, void *x, void *y, void *g0, void **out) {
 //
 // W[i] / b[i] are handles updated in place. loss_out receives the loss tensor
 // ([B, out_dim]) when non-null.
-int ref_mlp_step(void *X, void *Y, void **W, void **b, int nlayers, float lr,
-                 float *loss_out) {
+// One step as ref_mlp_step; grads_out (2 * nlayers handles, nullable) receives each
+// kernel's and bias's gradient as the engine left it (gW_i at 2i, gb_i at 2i + 1).
+int ref_mlp_step_grads(void *X, void *Y, void **W, void **b, int nlayers, float lr,
+                       float *loss_out, void **grads_out) {
    return guard([&]() -> int {
       std::vector<AT> Ws, bs;
       Ws.reserve(nlayers);
@@ -249,8 +251,11 @@ int ref_mlp_step(void *X, void *Y, void **W, void **b, int nlayers, float lr,
          scope.exit();
       }
       for (int i = 0; i < nlayers; ++i) {
+         int slot = 0;
          for (AT *p : {&Ws[i], &bs[i]}) {
             auto g = p->grad();
+            if (grads_out) grads_out[2 * i + slot] = g ? wrap(RT(g->raw())) : nullptr;
+            ++slot;
             if (!g) continue;
             AT step = *g * lr;
             p->raw() -= step.raw();
@@ -258,6 +263,11 @@ int ref_mlp_step(void *X, void *Y, void **W, void **b, int nlayers, float lr,
       }
       return 1;
    }) ? 0 : -1;
+}
+
+int ref_mlp_step(void *X, void *Y, void **W, void **b, int nlayers, float lr,
+                 float *loss_out) {
+   return ref_mlp_step_grads(X, Y, W, b, nlayers, lr, loss_out, nullptr);
 }
 
 } // extern "C"

@@ -141,3 +141,40 @@ def test_block_freed_on_another_stream_returns_home_after_its_use(capi):
     assert p.value in (p3.value, p4.value)  # back in its home cache
     capi.check(L.fz_free(p3, up))
     capi.check(L.fz_free(p4, up))
+
+
+def test_stream_destroy_returns_its_cached_blocks(capi):
+    """Blocks cached for a stream leave the cache when the stream is destroyed (a new
+    stream may get the same handle), and a block still live on it is re-homed: freeing
+    it afterwards caches it for the thread's compute stream, where it is reused."""
+    L = capi.lib()
+    L.fz_pool_cached.argtypes = [C.POINTER(C.c_size_t)]
+
+    def cached():
+        v = C.c_size_t()
+        capi.check(L.fz_pool_cached(C.byref(v)))
+        return v.value
+
+    s = C.c_void_p()
+    capi.check(L.fz_stream_create(C.byref(s)))
+    p, keep = C.c_void_p(), C.c_void_p()
+    capi.check(L.fz_malloc(C.byref(p), 3 << 20, s))
+    capi.check(L.fz_malloc(C.byref(keep), 5 << 20, s))
+    c0 = cached()
+    capi.check(L.fz_free(p, s))
+    assert cached() == c0 + (4 << 20)  # 2 MiB size classes above 1 MiB
+    capi.check(L.fz_stream_destroy(s))
+    assert cached() == c0
+    capi.check(L.fz_stream_sync(None))
+    capi.check(L.fz_free(keep, None))  # live block of the destroyed stream
+    assert cached() == c0 + (6 << 20)
+    q = C.c_void_p()
+    capi.check(L.fz_malloc(C.byref(q), 5 << 20, None))
+    assert q.value == keep.value  # reused from the compute stream's cache
+    capi.check(L.fz_free(q, None))
+    s2 = C.c_void_p()
+    capi.check(L.fz_stream_create(C.byref(s2)))
+    r = C.c_void_p()
+    capi.check(L.fz_malloc(C.byref(r), 3 << 20, s2))  # nothing stale cached for s2
+    capi.check(L.fz_free(r, s2))
+    capi.check(L.fz_stream_destroy(s2))

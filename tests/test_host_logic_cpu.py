@@ -359,10 +359,105 @@ def test_mlp_step_with_gemm_epilogues_matches_plain(fake_fusion):
         e0 = _stat(F, "epilogue_gemms")
         lf = fused.step(fused.tensor(X, True), fused.tensor(Y, True), 1e-2).to_numpy()
         # forward: 3 bias+ReLU layers and the output layer's loss gradient; backward: the
-        # ReLU-mask input gradients of the 3 hidden layers
-        assert _stat(F, "epilogue_gemms") - e0 == 7
+        # ReLU-mask input gradients of the 3 hidden layers; update: the 4 weights' SGD
+        # steps, run in the epilogues of the weight-gradient GEMMs (W.T is a view, so
+        # its gradient's swapaxes is the transposed product, in W's layout)
+        assert _stat(F, "epilogue_gemms") - e0 == 11
         lp = _plain(F, lambda: plain.step(plain.tensor(X, True), plain.tensor(Y, True), 1e-2).to_numpy())
         np.testing.assert_array_equal(lf, lp)
     for (Wf, bf), (Wp, bp) in zip(fused.numpy_params(), plain.numpy_params()):
         np.testing.assert_array_equal(Wf, Wp)
         np.testing.assert_array_equal(bf, bp)
+
+
+def test_swapaxes_view_is_read_in_place_by_gemms(fake_fusion):
+    """x @ W.T reads W in the other operand layout and the backward reads it back in
+    its own: a training step of a Linear layer transposes nothing, and the weight's
+    gradient lands in W's layout straight from the GEMM."""
+    F = fake_fusion
+    rng = np.random.default_rng(31)
+    X, W, b = rng.standard_normal((12, 8)), rng.standard_normal((6, 8)), rng.standard_normal((6,))
+    x, w, bt = api_cases.T(F, X, True), api_cases.T(F, W, True), api_cases.T(F, b, True)
+    s0 = _stat(F, "swap_materializations")
+    with F.grad_tape():
+        y = (x @ w.swapaxes(1, 0) + bt).maximum(0.0)
+        loss = y * y
+        loss.backward()
+    gw, gx = w.get_grad().to_numpy(), x.get_grad().to_numpy()
+    out = y.to_numpy()
+    assert _stat(F, "swap_materializations") == s0
+    pre = X.astype(np.float32) @ W.astype(np.float32).T + b.astype(np.float32)
+    g = 2 * np.maximum(pre, 0) * (pre > 0)
+    np.testing.assert_allclose(out, np.maximum(pre, 0), rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(gw, g.T @ X, rtol=1e-4, atol=1e-5)
+    np.testing.assert_allclose(gx, g @ W, rtol=1e-4, atol=1e-5)
+
+
+def test_swapaxes_view_values_and_copy_semantics(fake_fusion):
+    """A view equals the transposed copy wherever it is read; a swapaxes of a view is
+    the source; an in-place write to the source later leaves the view's values as they
+    were (swapaxes has copy semantics); other axes are transposed at once."""
+    F = fake_fusion
+    rng = np.random.default_rng(32)
+    A = rng.standard_normal((2, 5, 3)).astype(np.float32)
+    a = api_cases.T(F, A)
+    v = a.swapaxes(2, 1)
+    assert v.shape == [2, 3, 5]
+    s0 = _stat(F, "swap_materializations")
+    back = v.swapaxes(1, 2)
+    np.testing.assert_array_equal(back.to_numpy(), A)
+    assert _stat(F, "swap_materializations") == s0
+    a -= api_cases.T(F, np.ones_like(A))  # rebinds a's storage; v keeps the old value
+    np.testing.assert_array_equal((v + 0.0).to_numpy(), A.transpose(0, 2, 1))
+    assert _stat(F, "swap_materializations") == s0 + 1  # the elementwise read materialised it
+    np.testing.assert_array_equal(v.to_numpy(), A.transpose(0, 2, 1))
+    assert _stat(F, "swap_materializations") == s0 + 1  # once
+    np.testing.assert_array_equal(a.swapaxes(0, 2).to_numpy(), (A - 1).transpose(2, 1, 0))
+    np.testing.assert_array_equal(v.sum(2, False).to_numpy(), A.transpose(0, 2, 1).sum(2))
+
+
+def test_swapaxes_of_a_pending_product_is_the_transposed_product(fake_fusion):
+    F = fake_fusion
+    rng = np.random.default_rng(33)
+    A, B = rng.standard_normal((7, 4)), rng.standard_normal((4, 9))
+    a, b = api_cases.T(F, A), api_cases.T(F, B)
+    s0 = _stat(F, "swap_materializations")
+    p = a @ b
+    assert p.is_pending()
+    t = p.swapaxes(0, 1)
+    assert t.shape == [9, 7] and t.is_pending()
+    got = (t * 2.0).to_numpy()
+    assert _stat(F, "swap_materializations") == s0
+    want = (A.astype(np.float32) @ B.astype(np.float32)).T * 2
+    np.testing.assert_allclose(got, want, rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(p.to_numpy(), want.T / 2, rtol=1e-5, atol=1e-6)
+
+
+def test_swap_views_off_materialises_like_the_reference(fake_fusion):
+    F = fake_fusion
+    X = np.arange(12, dtype=np.float32).reshape(3, 4)
+    F.set_swap_views(False)
+    try:
+        s0 = _stat(F, "swap_materializations")
+        t = api_cases.T(F, X).swapaxes(1, 0)
+        assert not t.is_pending()
+        np.testing.assert_array_equal(t.to_numpy(), X.T)
+        assert _stat(F, "swap_materializations") == s0
+    finally:
+        F.set_swap_views(True)
+
+
+def test_weight_update_keeps_its_remainder_plane(fake_fusion):
+    """After a training step the weights' new values carry their TF32 remainder planes
+    (written by the update program), so the next forward splits no weight."""
+    from nova_b200.mlp import MLP
+
+    F = fake_fusion
+    X, Y, Ws, bs = api_cases.mlp_inputs(8, [8, 16, 4], 10)
+    m = MLP(F, Ws, bs)
+    m.step(m.tensor(X, True), m.tensor(Y, True), 1e-2).to_numpy()
+    m.step(m.tensor(X, True), m.tensor(Y, True), 1e-2).to_numpy()
+    t0 = _stat(F, "lo_splits")
+    m.step(m.tensor(X, True), m.tensor(Y, True), 1e-2).to_numpy()
+    # the input batch X is split once (it arrives from the host); no weight is
+    assert _stat(F, "lo_splits") - t0 == 1
