@@ -47,8 +47,9 @@ enum fz_binop {
 };
 
 /* Unary ops: SimdTags.hpp:55-71 (exp/log/sqrt) plus identity (copy). */
-/* FZ_TF32_LO: x minus x with its 13 low mantissa bits cleared (the remainder plane a
- * 3xTF32 GEMM reads; fz_tf32_lo); not an op of Fusion's API. */
+/* FZ_TF32_LO: x minus x with its 13 low mantissa bits cleared, rounded to the nearest
+ * TF32 value (ties to even): the remainder plane a 3xTF32 GEMM reads (fz_tf32_lo);
+ * not an op of Fusion's API. */
 enum fz_unop { FZ_EXP = 0, FZ_LOG = 1, FZ_SQRT = 2, FZ_COPY = 3, FZ_TF32_LO = 4 };
 
 /* Reductions: SumSIMD via reduction_tag (fusion/src/Fusion/core/TensorIter.hpp:251-297);
@@ -91,6 +92,11 @@ int fz_event_record(void **event, void *stream);
 int fz_stream_wait_event(void *waiter, void *event);
 int fz_event_destroy(void *event);
 int fz_device_sync(void);
+/* Queue a host-side pause of `seconds` (0..60) on `stream`: work queued after it starts
+ * that much later; nothing runs on the GPU meanwhile. For exercising the host-side
+ * watchdog (fz_comm_wait) with a stream that is late, without any device fault.
+ * Replaces no reference interface. */
+int fz_stream_delay(void *stream, double seconds);
 
 /* Stream-ordered device memory. fz_free(ptr, stream) marks the block free after the
  * work submitted to `stream` so far; it goes back to the free list of the stream it
@@ -306,8 +312,9 @@ int fz_gemm_f32_epilogue(int64_t batch, int64_t M, int64_t N, int64_t K,
  * 256). Returns FZ_ERR_JIT with the compiler log in fz_last_error on failure. */
 int fz_gemm_epilogue_compile(const struct fz_program *epi, const fz_epi_input *inputs,
                              int a_mn, int b_mn, int tile_n, int pair);
-/* lo[i] = x[i] - tf32_hi(x[i]) for i < n, tf32_hi clearing the 13 low mantissa bits
- * (the plane fz_gemm_f32_split takes). */
+/* lo[i] = tf32_rn(x[i] - tf32_hi(x[i])) for i < n: tf32_hi clears the 13 low mantissa
+ * bits (what the MMA reads for x), the difference is exact, and tf32_rn rounds it to the
+ * nearest TF32 value, ties to even (the plane fz_gemm_f32_split takes). */
 int fz_tf32_lo(float *lo, const float *x, int64_t n, void *stream);
 /* GEMM tile schedule for the calls that follow (process-wide): FZ_GEMM_TILES_AUTO picks
  * CTA pairs (256 x 256 tiles, tcgen05 cta_group::2) for products with at least 256 rows,
@@ -344,6 +351,22 @@ typedef struct fz_gemm_timing_rec {
 } fz_gemm_timing_rec;
 int fz_gemm_timing(int on);
 int fz_gemm_timing_read(fz_gemm_timing_rec *out, int max, int *count);
+
+/* ---- device-side random numbers (Philox-4x32-10) ------------------------- */
+
+/* Counter-based generator, a device-side alternative to Random::uniform_base
+ * (fusion/src/Fusion/Random.hpp:20-36, std::mt19937 on the host, whose stream it does
+ * not reproduce). Element i of the stream (seed, offset) is lane (offset + i) % 4 of
+ * Philox-4x32-10 at counter (offset + i) / 4 under key seed; u = (bits >> 8) * 2^-24.
+ * offset must be a multiple of 4; out 16-byte aligned. */
+int fz_philox_uniform(float *out, int64_t n, uint64_t seed, uint64_t offset, float lo, float hi,
+                      void *stream);
+/* Nova's Dropout (nova/src/blocks/regularisation/dropout.py:17-23) in one pass with
+ * the mask drawn in the kernel: out[i] = (x[i] * (u_i > rate ? 1 : 0)) / keep, u_i the
+ * stream's uniform in [0, 1), keep = fp32(1 - rate) as Nova passes it (Fusion's `>=`
+ * is `>`). No mask tensor is written. */
+int fz_philox_dropout(float *out, const float *x, int64_t n, float rate, float keep, uint64_t seed,
+                      uint64_t offset, void *stream);
 
 /* ---- collectives (data-parallel MLP step) -------------------------------- */
 

@@ -105,12 +105,23 @@ __device__ __forceinline__ float binop_t(float a, float b) {
   else return a >= b ? 1.0f : 0.0f;
 }
 
+// TF32 remainder plane of x: x - hi (hi = x with its 13 low mantissa bits cleared,
+// the value a kind::tf32 MMA reads for x; the difference is exact in fp32), rounded
+// to the nearest TF32 value, ties to even. The MMA reads the plane exactly, so
+// hi + lo represents x to 2^-22 relative with an unbiased error (truncating the
+// remainder to TF32 inside the MMA would bias every product toward zero).
+__device__ __forceinline__ float tf32_lo(float a) {
+  uint32_t u = __float_as_uint(__fsub_rn(a, __uint_as_float(__float_as_uint(a) & 0xffffe000u)));
+  if ((u & 0x7f800000u) != 0x7f800000u) u = (u + 0xfffu + ((u >> 13) & 1u)) & 0xffffe000u;
+  return __uint_as_float(u);
+}
+
 template <int OP>
 __device__ __forceinline__ float unop_t(float a) {
   if constexpr (OP == FZ_EXP) return expf(a);
   else if constexpr (OP == FZ_LOG) return logf(a);
   else if constexpr (OP == FZ_SQRT) return __fsqrt_rn(a);
-  else if constexpr (OP == FZ_TF32_LO) return __fsub_rn(a, __uint_as_float(__float_as_uint(a) & 0xffffe000u));
+  else if constexpr (OP == FZ_TF32_LO) return tf32_lo(a);
   else return a;
 }
 

@@ -61,6 +61,11 @@ __device__ __forceinline__ float fz_pow(float a, float b) {
 __device__ __forceinline__ float fz_max(float a, float b) { return a > b ? a : b; }
 __device__ __forceinline__ float fz_gt(float a, float b) { return a > b ? 1.0f : 0.0f; }
 __device__ __forceinline__ float fz_ge(float a, float b) { return a >= b ? 1.0f : 0.0f; }
+__device__ __forceinline__ float fz_tf32_lo(float a) {
+  unsigned u = __float_as_uint(__fsub_rn(a, __uint_as_float(__float_as_uint(a) & 0xffffe000u)));
+  if ((u & 0x7f800000u) != 0x7f800000u) u = (u + 0xfffu + ((u >> 13) & 1u)) & 0xffffe000u;
+  return __uint_as_float(u);
+}
 )";
 
 std::string binop_expr(int op, const std::string &a, const std::string &b) {
@@ -83,7 +88,7 @@ std::string unop_expr(int op, const std::string &a) {
     case FZ_LOG: return "logf(" + a + ")";
     case FZ_SQRT: return "__fsqrt_rn(" + a + ")";
     case FZ_COPY: return a;
-    case FZ_TF32_LO: return "__fsub_rn(" + a + ", __uint_as_float(__float_as_uint(" + a + ") & 0xffffe000u))";
+    case FZ_TF32_LO: return "fz_tf32_lo(" + a + ")";
   }
   return "";
 }

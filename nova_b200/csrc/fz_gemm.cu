@@ -18,16 +18,19 @@
 //              B_hi, B_lo (256 x 16) into a 4-stage ring of 48 KB
 //   warp 1     allocates 2 x 256 TMEM columns; one lane issues, per 8-wide k-step,
 //              tcgen05.mma.kind::tf32 lo*hi, hi*lo, hi*hi, and tcgen05.commit frees
-//              each stage. The K range is cut into chunks of 256; each chunk
+//              each stage. The K range is cut into chunks of 128; each chunk
 //              accumulates from zero into one of the two TMEM buffers.
 //   warps 4-11 promotion and epilogue: two warps per TMEM lane quarter, each owning
-//              128 of the 256 columns, tcgen05.ld every finished chunk and add it
-//              into an fp32 register accumulator (IEEE adds), then store C.
-// The tensor core's own fp32 accumulation is truncating, so its error grows with
-// the number of MMAs folded into one accumulator (about 3e-5 relative at K = 4096
-// when a whole tile accumulates in TMEM); promoting every 256 of K bounds it to the
-// error of a 256-long chunk and keeps long-K products (weight gradients, K = batch)
-// within 1e-5. Double-buffered chunks let the MMAs run on while a chunk is promoted.
+//              128 of the 256 columns, tcgen05.ld every finished chunk (two loads in
+//              flight per wait) and add it into an fp32 register accumulator (IEEE
+//              adds), then store C; one arrival per warp frees the buffer.
+// The tensor core's own fp32 accumulation truncates, so its error grows with the
+// number of MMAs folded into one accumulator, always toward zero (about 3e-5
+// relative at K = 4096 when a whole tile accumulates in TMEM). Promoting every 128 of
+// K bounds the bias to that of a 128-long chunk (about 1e-6; 2e-6 with chunks of 256,
+// a bias that adds up over the layers of a network), and the TF32 remainder planes
+// are rounded to nearest rather than truncated by the MMA. Double-buffered chunks let
+// the MMAs run on while a chunk is promoted.
 //
 // Every mbarrier wait is bounded by a %globaltimer deadline; on expiry the kernel
 // records an error code in the device's error word (read by fz_kernel_status),
@@ -56,7 +59,7 @@ using namespace fz_gemm_dev;
 // ---------------------------------------------------------------- split pass
 __device__ __forceinline__ void split1(float x, float &hi, float &lo) {
   hi = __uint_as_float(__float_as_uint(x) & 0xffffe000u);
-  lo = __fsub_rn(x, hi);
+  lo = fzd::tf32_lo(x);
 }
 
 // src[b][r][k] at b*sb + r*ld + k (k the contiguous index: K for a K-major operand,
@@ -255,8 +258,8 @@ int choose_splits(int64_t tiles, int64_t M, int64_t N, int64_t K, int64_t batch,
   double best_t = 1e300;
   const int cand[] = {1, 2, 3, 4, 6, 8, 12, 16, 24, 32};
   for (int sp : cand) {
-    const int64_t kps = sp == 1 ? K : round_up((K + sp - 1) / sp, (int64_t)BK * KCHUNK);
-    if (sp > 1 && kps < (int64_t)BK * KCHUNK) break;
+    const int64_t kps = sp == 1 ? K : round_up((K + sp - 1) / sp, (int64_t)BK * KSPLIT_GRAN);
+    if (sp > 1 && kps < (int64_t)BK * KSPLIT_GRAN) break;
     const int64_t real = (K + kps - 1) / kps;
     const int64_t waves = (tiles * real + sms - 1) / sms;
     double t = (double)waves * (double)kps;
@@ -984,7 +987,7 @@ int gemm_impl(int64_t batch, int64_t M, int64_t N, int64_t K, const float *A, co
   const int64_t tiles = (int64_t)tiles_m * tiles_n * batch;
   const bool dense_c = ldc == N && (batch == 1 || strideC == M * N);
   const int splits = dense_c || E.pg ? choose_splits(tiles, M, N, K, batch, workers) : 1;
-  const int64_t kps = splits > 1 ? round_up((K + splits - 1) / splits, (int64_t)BK * KCHUNK) : K;
+  const int64_t kps = splits > 1 ? round_up((K + splits - 1) / splits, (int64_t)BK * KSPLIT_GRAN) : K;
   const int real_splits = (int)((K + kps - 1) / kps);
   const int64_t num_units = tiles * real_splits;
   if (!rc && num_units >= (1ll << 31)) rc = fz::fail(FZ_ERR_INVALID, "fz_gemm_f32: too many tiles");

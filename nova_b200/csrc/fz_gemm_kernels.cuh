@@ -50,7 +50,17 @@ constexpr int TILE_A_BYTES = BM * BK * 4;  // 16 KB
 constexpr int TILE_B_BYTES = BN * BK * 4;  // 32 KB
 constexpr int STAGE_BYTES = 2 * TILE_A_BYTES + 2 * TILE_B_BYTES;  // 96 KB
 constexpr int TMEM_COLS = 256;          // one accumulator buffer (BN fp32 columns)
-constexpr int KCHUNK = 16;              // k-tiles per promotion chunk (K = 256)
+// k-tiles per promotion chunk (K = 128). The tensor core's accumulation truncates: each
+// MMA added into a TMEM accumulator shifts the sum toward zero by about 0.3 ulp, so the
+// relative bias of a chunk grows with its 3 * K / 8 MMAs (about 1.9e-8 per MMA,
+// measured); chunks of 128 keep it near 1e-6 per product, against 2e-6 for chunks of
+// 256, at about 2 % of the GEMM's time (more handoffs between MMA issuer and promoting
+// warps, and less run-ahead of the MMAs while the epilogue stores).
+#ifndef FZ_GEMM_KCHUNK
+#define FZ_GEMM_KCHUNK 8
+#endif
+constexpr int KCHUNK = FZ_GEMM_KCHUNK;
+constexpr int KSPLIT_GRAN = 16;         // K splits are multiples of this many k-tiles
 constexpr int NUM_EPI_WARPS = 8;        // 2 per TMEM lane quarter
 // Warp roles: 0 TMA producer, 1 MMA issuer (and TMEM owner), 2-3 idle, 4-11 promotion
 // and epilogue. Registers are rebalanced per warpgroup with setmaxnreg: the launch
@@ -222,6 +232,23 @@ __device__ __forceinline__ void umma_commit(uint64_t *bar) {
           smem_u32(bar))
       : "memory");
 }
+
+// 32 columns of this warp's 32 TMEM lanes into r, without waiting for them
+// (tmem_wait_ld), so several loads can be in flight.
+__device__ __forceinline__ void tmem_ld_32x32b_x32_async(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile(
@@ -577,7 +604,20 @@ struct TileCfg {
 // Add CPW accumulator columns of this warp's TMEM lanes, from `taddr`, into acc.
 template <int CPW>
 __device__ __forceinline__ void promote_cols(uint32_t taddr, float (&acc)[CPW]) {
-  if constexpr (CPW >= 32) {
+  if constexpr (CPW >= 64) {
+    // two 32-column loads in flight per wait
+#pragma unroll
+    for (int c0 = 0; c0 < CPW; c0 += 64) {
+      uint32_t r0[32], r1[32];
+      tmem_ld_32x32b_x32_async(taddr + (uint32_t)c0, r0);
+      tmem_ld_32x32b_x32_async(taddr + (uint32_t)(c0 + 32), r1);
+      tmem_wait_ld();
+#pragma unroll
+      for (int i = 0; i < 32; ++i) acc[c0 + i] = __fadd_rn(acc[c0 + i], __uint_as_float(r0[i]));
+#pragma unroll
+      for (int i = 0; i < 32; ++i) acc[c0 + 32 + i] = __fadd_rn(acc[c0 + 32 + i], __uint_as_float(r1[i]));
+    }
+  } else if constexpr (CPW >= 32) {
 #pragma unroll
     for (int c0 = 0; c0 < CPW; c0 += 32) {
       uint32_t r[32];
@@ -635,7 +675,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 32 * NUM_EPI_WARPS);  // every epilogue thread arrives
+      mbar_init(&acc_empty[b], NUM_EPI_WARPS);  // one arrival per epilogue warp
     }
     abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -783,7 +823,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                                ((uint32_t)(q * 32) << 16);
         promote_cols<CPW>(taddr, acc);
         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-        mbar_arrive(&acc_empty[b]);
+        __syncwarp();  // the whole warp has read the buffer: one arrival for it
+        if (lane == 0) mbar_arrive(&acc_empty[b]);
       }
       if (!ok) break;
       EPI::template store<CPW>(args, ep, ks, bz, mb * BM + q * 32 + lane, nb * TBN + half * CPW, acc,
@@ -929,7 +970,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 2 * 32 * NUM_EPI_WARPS);  // both CTAs' epilogue threads
+      mbar_init(&acc_empty[b], 2 * NUM_EPI_WARPS);  // one arrival per epilogue warp of both CTAs
     }
     abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -1075,16 +1116,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const uint32_t taddr = tmem_base + (uint32_t)(b * TMEM_COLS + half * 128) +
                                ((uint32_t)(q * 32) << 16);
-#pragma unroll
-        for (int c0 = 0; c0 < 128; c0 += 32) {
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(taddr + (uint32_t)c0, r);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) acc[c0 + i] = __fadd_rn(acc[c0 + i], __uint_as_float(r[i]));
-        }
+        promote_cols<128>(taddr, acc);
         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-        if (leader) mbar_arrive(&acc_empty[b]);
-        else mbar_arrive_remote(acc_empty_leader[b]);
+        __syncwarp();  // the whole warp has read the buffer: one arrival for it
+        if (lane == 0) {
+          if (leader) mbar_arrive(&acc_empty[b]);
+          else mbar_arrive_remote(acc_empty_leader[b]);
+        }
       }
       if (!ok) break;
       EPI::template store<128>(args, ep, ks, bz, mb * 2 * BM + (int)rank * BM + q * 32 + lane,

@@ -3,6 +3,8 @@
 #include <atomic>
 #include <cstring>
 #include <mutex>
+#include <thread>
+#include <chrono>
 #include <string>
 #include <unordered_map>
 #include <vector>
@@ -272,6 +274,25 @@ int fz_stream_wait(void *waiter, void *signaler) {
   if (rc == cudaSuccess) rc = cudaStreamWaitEvent(w, e, 0);
   cudaEventDestroy(e);  // released once the wait no longer needs it
   if (rc != cudaSuccess) return cuda_fail(rc, "fz_stream_wait", __FILE__, __LINE__);
+  return FZ_OK;
+}
+
+namespace {
+void CUDART_CB host_pause(void *arg) {
+  double *secs = static_cast<double *>(arg);
+  std::this_thread::sleep_for(std::chrono::duration<double>(*secs));
+  delete secs;
+}
+}  // namespace
+
+int fz_stream_delay(void *stream, double seconds) {
+  FZ_REQUIRE(seconds >= 0.0 && seconds <= 60.0, "fz_stream_delay: seconds must be in [0, 60]");
+  double *arg = new double(seconds);
+  cudaError_t e = cudaLaunchHostFunc(resolve(stream), host_pause, arg);
+  if (e != cudaSuccess) {
+    delete arg;
+    return cuda_fail(e, "fz_stream_delay", __FILE__, __LINE__);
+  }
   return FZ_OK;
 }
 

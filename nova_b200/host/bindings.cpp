@@ -393,6 +393,8 @@ PYBIND11_MODULE(fusion, m) {
     d["epilogue_gemms"] = epilogue_gemms();
     d["swap_materializations"] = swap_materializations();
     d["lo_splits"] = lo_splits();
+    d["plan_cache_hits"] = plan_cache_hits();
+    d["plan_cache_misses"] = plan_cache_misses();
     d["fused_kernels_compiled"] = fz_fused_cache_size();
     size_t r = 0, u = 0;
     if (fz_pool_stats(&r, &u) == FZ_OK) {

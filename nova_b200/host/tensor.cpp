@@ -263,16 +263,46 @@ int collapse(std::vector<int64_t> &size, std::vector<std::vector<int64_t>> &st) 
 }
 }  // namespace
 
-// Launch a lowered program whose outputs (all of out_shape) go to `outs`.
-static void launch_program(const Lowering &L, const std::vector<size_t> &out_shape,
-                           const std::vector<float *> &outs) {
-  const int nout = (int)outs.size();
-  const int nops = nout + (int)L.leaves.size();
-  std::vector<int64_t> size(out_shape.begin(), out_shape.end());
-  std::vector<std::vector<int64_t>> st(nops, std::vector<int64_t>(out_shape.size()));
-  for (int k = 0; k < nout; ++k) operand_strides(out_shape, out_shape, st[k].data());
-  for (size_t k = 0; k < L.leaves.size(); ++k)
-    operand_strides(L.leaves[k]->shape, out_shape, st[nout + k].data());
+// ---- launch-plan cache (the shape caching fusion/src/Fusion/core/PlanMeta.hpp:10-13
+// leaves as a TODO): the plan of `nout` outputs of shape `out` and operands of the
+// given shapes depends on the shapes only, so it is built once per shape set.
+namespace {
+struct PlanKeyHash {
+  size_t operator()(const std::vector<int64_t> &k) const {
+    size_t h = 1469598103934665603ull;
+    for (int64_t v : k) h = (h ^ (size_t)v) * 1099511628211ull;
+    return h;
+  }
+};
+thread_local std::unordered_map<std::vector<int64_t>, fz_ewise_plan, PlanKeyHash> t_plans;
+int64_t g_plan_hits = 0, g_plan_misses = 0;
+constexpr size_t kPlanCacheMax = 4096;
+}  // namespace
+int64_t plan_cache_hits() { return g_plan_hits; }
+int64_t plan_cache_misses() { return g_plan_misses; }
+
+static const fz_ewise_plan &cached_plan(const std::vector<size_t> &out, int nout,
+                                        const std::vector<const std::vector<size_t> *> &ins) {
+  std::vector<int64_t> key;
+  key.reserve(2 + out.size() + 4 * ins.size());
+  key.push_back(nout);
+  key.push_back((int64_t)out.size());
+  for (size_t d : out) key.push_back((int64_t)d);
+  for (const auto *s : ins) {
+    key.push_back(-1 - (int64_t)s->size());
+    for (size_t d : *s) key.push_back((int64_t)d);
+  }
+  auto it = t_plans.find(key);
+  if (it != t_plans.end()) {
+    ++g_plan_hits;
+    return it->second;
+  }
+  ++g_plan_misses;
+  const int nops = nout + (int)ins.size();
+  std::vector<int64_t> size(out.begin(), out.end());
+  std::vector<std::vector<int64_t>> st(nops, std::vector<int64_t>(out.size()));
+  for (int k = 0; k < nout; ++k) operand_strides(out, out, st[k].data());
+  for (size_t k = 0; k < ins.size(); ++k) operand_strides(*ins[k], out, st[nout + k].data());
   if ((int)size.size() > FZ_MAX_DIMS) collapse(size, st);
   FB_CHECK((int)size.size() <= FZ_MAX_DIMS, "fused elementwise: too many non-mergeable dims");
   fz_ewise_plan plan{};
@@ -282,6 +312,17 @@ static void launch_program(const Lowering &L, const std::vector<size_t> &out_sha
     plan.size[d] = size[d];
     for (int k = 0; k < nops; ++k) plan.stride_bytes[k][d] = st[k][d] * 4;
   }
+  if (t_plans.size() >= kPlanCacheMax) t_plans.clear();
+  return t_plans.emplace(std::move(key), plan).first->second;
+}
+
+// Launch a lowered program whose outputs (all of out_shape) go to `outs`.
+static void launch_program(const Lowering &L, const std::vector<size_t> &out_shape,
+                           const std::vector<float *> &outs) {
+  std::vector<const std::vector<size_t> *> ins;
+  ins.reserve(L.leaves.size());
+  for (const Expr *l : L.leaves) ins.push_back(&l->shape);
+  const fz_ewise_plan plan = cached_plan(out_shape, (int)outs.size(), ins);
   std::vector<const float *> leaf_ptrs;
   for (auto *l : L.leaves) leaf_ptrs.push_back(l->buf->ptr);
   fz_check(fz_fused_launch(&L.prog, &plan, outs.data(), leaf_ptrs.data(), nullptr), "fz_fused_launch");
@@ -298,17 +339,7 @@ static bool try_single_op(Expr *e, float *out_ptr) {
       return true;
     }
     if (os.size() <= FZ_MAX_DIMS) {
-      fz_ewise_plan plan{};
-      plan.ndim = (int32_t)os.size();
-      plan.num_operands = 3;
-      int64_t st[3][FZ_MAX_DIMS];
-      operand_strides(os, os, st[0]);
-      operand_strides(e->a->shape, os, st[1]);
-      operand_strides(e->b->shape, os, st[2]);
-      for (int d = 0; d < plan.ndim; ++d) {
-        plan.size[d] = os[d];
-        for (int k = 0; k < 3; ++k) plan.stride_bytes[k][d] = st[k][d] * 4;
-      }
+      const fz_ewise_plan &plan = cached_plan(os, 1, {&e->a->shape, &e->b->shape});
       fz_check(fz_ewise_binary(e->op, &plan, out_ptr, e->a->buf->ptr, e->b->buf->ptr, nullptr),
                "fz_ewise_binary");
       return true;
@@ -487,6 +518,9 @@ bool epilogue_input(const std::vector<size_t> &s, const std::vector<size_t> &out
 // when the roots do not qualify.
 static bool try_epilogue(const std::vector<ExprPtr> &roots, const std::vector<bool> &want_lo) {
   if (!g_gemm_epilogue || !g_fusion || roots.empty()) return false;
+  bool any = false;  // no pending GEMM under any root: nothing to scan
+  for (const ExprPtr &r : roots) any = any || r->gemm_below;
+  if (!any) return false;
   EpiScan S;
   for (const ExprPtr &r : roots) S.roots.insert(r.get());
   for (const ExprPtr &r : roots) S.scan(r.get(), nullptr);
@@ -739,6 +773,7 @@ static ExprPtr make_op(Expr::Kind kind, int op, ExprPtr a, ExprPtr b, std::vecto
   e->op = op;
   e->nodes_ub = nodes();
   e->leaves_ub = leaves();
+  e->gemm_below = a->gemm_below || (b && b->gemm_below);
   e->a = std::move(a);
   e->b = std::move(b);
   e->shape = std::move(shape);
@@ -1106,6 +1141,7 @@ RawTensor matmul(const RawTensor &A0, const RawTensor &B0, bool transA, bool tra
   e->gemm = std::move(g);
   e->nodes_ub = 0;
   e->leaves_ub = 1;
+  e->gemm_below = true;
   // launched where its value is first needed: inside the epilogue of the program that
   // reads it, or as a plain product
   if (!g_gemm_epilogue || batch * M * N == 0) lower_gemm(e.get());
@@ -1143,6 +1179,7 @@ static ExprPtr transposed_gemm(const Expr &g) {
   e->gemm = std::move(t);
   e->nodes_ub = 0;
   e->leaves_ub = 1;
+  e->gemm_below = true;
   return e;
 }
 

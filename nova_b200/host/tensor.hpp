@@ -110,6 +110,7 @@ struct Expr {
   bool red_keep = false;              // Reduce: reduced axes kept as extent 1
   int nodes_ub = 1;                   // upper bounds used by the fusion size policy
   int leaves_ub = 0;
+  bool gemm_below = false;            // a pending GEMM may sit in this DAG (never false if one does)
   size_t numel() const;
 };
 using ExprPtr = std::shared_ptr<Expr>;
@@ -146,6 +147,10 @@ int64_t swap_materializations();
 // TF32 remainder planes split by a separate pass (fz_tf32_lo) so far: operands whose
 // plane no producing kernel wrote (host uploads, values lowered without a plane).
 int64_t lo_splits();
+// Launch plans (per-operand broadcast strides over the output, chained dims merged)
+// are cached by the shapes they are built from: hits and misses so far.
+int64_t plan_cache_hits();
+int64_t plan_cache_misses();
 // Lower a pending node and its TF32 remainder plane in one fused pass (GEMM operands).
 void materialize_with_lo(const ExprPtr &e);
 // Lower several pending nodes of one shape as outputs of one fused program.

@@ -190,3 +190,70 @@ void orc_swapaxes(float *out, const float *in, const int64_t *shape, int nd, int
   }
   (void)ist;
 }
+
+/* Philox-4x32-10 (Salmon, Moraes, Dror, Shaw, SC'11; no reference counterpart: the
+ * reference draws from std::mt19937, fusion/src/Fusion/Random.hpp:20-36). Restated
+ * from the paper: ten rounds on a 128-bit counter with multipliers 0xD2511F53 and
+ * 0xCD9E8D57 and a 64-bit key bumped by 0x9E3779B9 / 0xBB67AE85 between rounds.
+ * Stream layout of the device generator: element i of (seed, offset) is lane
+ * (offset + i) % 4 of the block at counter (offset + i) / 4; u = (bits >> 8) * 2^-24. */
+static void orc_philox(uint64_t ctr, uint64_t key, uint32_t out[4]) {
+  uint32_t c[4] = {(uint32_t)ctr, (uint32_t)(ctr >> 32), 0u, 0u};
+  uint32_t k0 = (uint32_t)key, k1 = (uint32_t)(key >> 32);
+  for (int r = 0; r < 10; ++r) {
+    uint64_t p0 = (uint64_t)0xD2511F53u * c[0], p1 = (uint64_t)0xCD9E8D57u * c[2];
+    uint32_t hi0 = (uint32_t)(p0 >> 32), lo0 = (uint32_t)p0;
+    uint32_t hi1 = (uint32_t)(p1 >> 32), lo1 = (uint32_t)p1;
+    uint32_t n0 = hi1 ^ c[1] ^ k0, n2 = hi0 ^ c[3] ^ k1;
+    c[0] = n0;
+    c[1] = lo1;
+    c[2] = n2;
+    c[3] = lo0;
+    k0 += 0x9E3779B9u;
+    k1 += 0xBB67AE85u;
+  }
+  memcpy(out, c, sizeof(c));
+}
+
+static float orc_unit(uint32_t bits) { return (float)(bits >> 8) * 5.9604644775390625e-08f; }
+
+/* Raw Philox-4x32-10 block for counter/key (for the published known-answer vectors). */
+void orc_philox4x32_10(uint64_t ctr_lo, uint64_t ctr_hi, uint64_t key, uint32_t out[4]) {
+  uint32_t c[4] = {(uint32_t)ctr_lo, (uint32_t)(ctr_lo >> 32), (uint32_t)ctr_hi, (uint32_t)(ctr_hi >> 32)};
+  uint32_t k0 = (uint32_t)key, k1 = (uint32_t)(key >> 32);
+  for (int r = 0; r < 10; ++r) {
+    uint64_t p0 = (uint64_t)0xD2511F53u * c[0], p1 = (uint64_t)0xCD9E8D57u * c[2];
+    uint32_t n0 = (uint32_t)(p1 >> 32) ^ c[1] ^ k0, n2 = (uint32_t)(p0 >> 32) ^ c[3] ^ k1;
+    c[1] = (uint32_t)p1;
+    c[3] = (uint32_t)p0;
+    c[0] = n0;
+    c[2] = n2;
+    k0 += 0x9E3779B9u;
+    k1 += 0xBB67AE85u;
+  }
+  memcpy(out, c, sizeof(c));
+}
+
+void orc_philox_uniform(float *out, int64_t n, uint64_t seed, uint64_t offset, float lo, float hi) {
+  const float span = hi - lo;
+  for (int64_t i = 0; i < n; ++i) {
+    uint32_t r[4];
+    orc_philox((offset + (uint64_t)i) / 4, seed, r);
+    float v = fmaf(span, orc_unit(r[(offset + (uint64_t)i) % 4]), lo);
+    if (v >= hi) v = nextafterf(hi, lo);
+    out[i] = v;
+  }
+}
+
+/* Nova's Dropout, nova/src/blocks/regularisation/dropout.py:17-23: inputs * (u >= rate)
+ * / (1 - rate), where Fusion's >= is > (core/RawTensor.hpp:207-209) and the mask is a
+ * 1.0 / 0.0 tensor multiplied in. */
+void orc_philox_dropout(float *out, const float *x, int64_t n, float rate, float keep, uint64_t seed,
+                        uint64_t offset) {
+  for (int64_t i = 0; i < n; ++i) {
+    uint32_t r[4];
+    orc_philox((offset + (uint64_t)i) / 4, seed, r);
+    float m = orc_unit(r[(offset + (uint64_t)i) % 4]) > rate ? 1.0f : 0.0f;
+    out[i] = (x[i] * m) / keep;
+  }
+}

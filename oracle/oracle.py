@@ -251,3 +251,38 @@ def have_ref() -> bool:
 
 def have_port() -> bool:
     return (REF_DIR / "libfusion_oracle.so").exists()
+
+
+def mlp_step_f64(X, Y, Ws, bs, masks=None):
+    """Float64 restatement of the reference MLP step's forward and backward (Nova's
+    Linear/ReLU/MSE sequence as the registry differentiates it): pre-activations
+    t_l = h_{l-1} W_l^T + b_l (nova/src/blocks/core/linear.py:42-48), h_l = relu(t_l)
+    for hidden layers (activations.py:9-10), loss = (out - Y)^2 / size elementwise
+    (losses/loss.py:34-37); backward g_L = 2 (out - Y) / size (Pow.hpp:34-51 with the
+    Divide backward), gW_l = g_l^T h_{l-1} (MatMul.hpp:55-58 through SwapAxes), gb_l = g_l
+    unreduced ([B, U], Add.hpp:41-45), g_{l-1} = (g_l W_l) * (t_{l-1} > 0) (Maximum.hpp:
+    34-51; `>=` is `>`). `masks` (one boolean array per hidden layer) replaces the
+    ReLU decisions t > 0, so a float32 implementation's own decisions can be replayed
+    exactly. Returns loss, [(gW_l, gb_l)], [t_l] (float64) and the masks used."""
+    X = np.asarray(X, np.float64)
+    Y = np.asarray(Y, np.float64)
+    Ws = [np.asarray(w, np.float64) for w in Ws]
+    bs = [np.asarray(b, np.float64) for b in bs]
+    L = len(Ws)
+    hs, ts, used = [X], [], []
+    for i in range(L):
+        t = hs[-1] @ Ws[i].T + bs[i]
+        ts.append(t)
+        if i + 1 < L:
+            m = (t > 0) if masks is None else np.asarray(masks[i], bool)
+            used.append(m)
+            hs.append(t * m)
+    out = ts[-1]
+    loss = (out - Y) ** 2 / out.size
+    g = 2.0 * (out - Y) / out.size
+    grads = [None] * L
+    for i in range(L - 1, -1, -1):
+        grads[i] = (g.T @ hs[i], g)
+        if i > 0:
+            g = (g @ Ws[i]) * used[i - 1]
+    return loss, grads, ts, used

@@ -48,7 +48,11 @@ static float tf32_lo1(float x) {
   u &= 0xffffe000u;
   float h;
   std::memcpy(&h, &u, 4);
-  return x - h;
+  float r = x - h;
+  std::memcpy(&u, &r, 4);
+  if ((u & 0x7f800000u) != 0x7f800000u) u = (u + 0xfffu + ((u >> 13) & 1u)) & 0xffffe000u;
+  std::memcpy(&r, &u, 4);
+  return r;
 }
 
 float unop(int op, float a) {
@@ -323,20 +327,54 @@ int fz_gemm_f32_split(int64_t batch, int64_t M, int64_t N, int64_t K, const floa
   return fz_gemm_f32(batch, M, N, K, A, lda, sA, tA, B, ldb, sB, tB, C, ldc, sC, st);
 }
 
-int fz_comm_unique_id(unsigned char id[FZ_UNIQUE_ID_BYTES]) { std::memset(id, 0, FZ_UNIQUE_ID_BYTES); return FZ_OK; }
-int fz_comm_init(void **c, int world, int, const unsigned char *) {
-  if (world != 1) return fail(FZ_ERR_UNSUPPORTED, "host test double: world must be 1");
-  *c = std::malloc(1);
+// Collectives. With a transport set (fake_comm_set_transport: a host callback that sums
+// a buffer over the ranks of a host process group, e.g. gloo), communicators of more
+// than one rank work and fz_comm_allreduce sums through it; otherwise world must be 1.
+// Stream time is emulated for the watchdog: fz_stream_delay marks the streams busy for
+// that long, and fz_comm_wait with a shorter timeout then aborts the communicator and
+// fails as the real one does.
+typedef int (*fake_allreduce_fn)(float *buf, int64_t n);
+static fake_allreduce_fn g_transport = nullptr;
+static double g_busy_s = 0.0;
+struct FakeComm {
+  int world;
+  bool aborted;
+};
+void fake_comm_set_transport(fake_allreduce_fn fn) { g_transport = fn; }
+
+int fz_stream_delay(void *, double seconds) {
+  if (!(seconds >= 0.0 && seconds <= 60.0)) return fail(FZ_ERR_INVALID, "fz_stream_delay: seconds must be in [0, 60]");
+  g_busy_s += seconds;
   return FZ_OK;
 }
-int fz_comm_allreduce(void *, const float *s, float *r, int64_t n, float scale, void *) {
-  for (int64_t i = 0; i < n; ++i) r[i] = s[i] * scale;
+int fz_comm_unique_id(unsigned char id[FZ_UNIQUE_ID_BYTES]) { std::memset(id, 0, FZ_UNIQUE_ID_BYTES); return FZ_OK; }
+int fz_comm_init(void **c, int world, int, const unsigned char *) {
+  if (world != 1 && !g_transport) return fail(FZ_ERR_UNSUPPORTED, "host test double: world must be 1");
+  *c = new FakeComm{world, false};
+  return FZ_OK;
+}
+int fz_comm_allreduce(void *comm, const float *s, float *r, int64_t n, float scale, void *) {
+  FakeComm *c = static_cast<FakeComm *>(comm);
+  if (c->aborted) return fail(FZ_ERR_INVALID, "fz_comm_allreduce: communicator was aborted");
+  if (r != s) std::memmove(r, s, sizeof(float) * (size_t)n);
+  if (c->world > 1 && g_transport(r, n) != 0) return fail(FZ_ERR_NCCL, "host transport failed");
+  for (int64_t i = 0; i < n; ++i) r[i] = r[i] * scale;
   return FZ_OK;
 }
 int fz_comm_group_start(void) { return FZ_OK; }
 int fz_comm_group_end(void) { return FZ_OK; }
 int fz_comm_broadcast(void *, float *, int64_t, int, void *) { return FZ_OK; }
-int fz_comm_wait(void *, void *, double) { return FZ_OK; }
-int fz_comm_destroy(void *c) { std::free(c); return FZ_OK; }
+int fz_comm_wait(void *comm, void *, double timeout_s) {
+  FakeComm *c = static_cast<FakeComm *>(comm);
+  const bool late = g_busy_s > timeout_s;
+  g_busy_s = 0.0;
+  if (late) {
+    c->aborted = true;
+    return fail(FZ_ERR_TIMEOUT, "collective did not complete within " + std::to_string(timeout_s) +
+                                    " s; communicator aborted");
+  }
+  return FZ_OK;
+}
+int fz_comm_destroy(void *c) { delete static_cast<FakeComm *>(c); return FZ_OK; }
 
 }  // extern "C"

@@ -461,3 +461,21 @@ def test_weight_update_keeps_its_remainder_plane(fake_fusion):
     m.step(m.tensor(X, True), m.tensor(Y, True), 1e-2).to_numpy()
     # the input batch X is split once (it arrives from the host); no weight is
     assert _stat(F, "lo_splits") - t0 == 1
+
+
+def test_launch_plans_are_cached_by_shape(fake_fusion):
+    """The broadcast plan of a launch is built once per shape set (the plan caching the
+    reference leaves as a TODO, PlanMeta.hpp:10-13) and results are unchanged."""
+    F = fake_fusion
+    rng = np.random.default_rng(40)
+    X, B = rng.standard_normal((5, 7)).astype(np.float32), rng.standard_normal((7,)).astype(np.float32)
+    x, b = api_cases.T(F, X), api_cases.T(F, B)
+    first = (x * b + 1.0).maximum(0.0).to_numpy()
+    h0, m0 = _stat(F, "plan_cache_hits"), _stat(F, "plan_cache_misses")
+    for _ in range(3):
+        np.testing.assert_array_equal((x * b + 1.0).maximum(0.0).to_numpy(), first)
+    assert _stat(F, "plan_cache_misses") == m0
+    assert _stat(F, "plan_cache_hits") >= h0 + 3
+    y = api_cases.T(F, rng.standard_normal((3, 5, 7)))
+    (y * b).to_numpy()  # a new shape set: one more plan
+    assert _stat(F, "plan_cache_misses") == m0 + 1

@@ -307,14 +307,40 @@ def test_gemm_3xtf32_long_k(capi, port, M, N, K):
     assert err <= 1e-5, err
 
 
+def tf32_lo_reference(x):
+    """x - hi (hi: x with its 13 low mantissa bits cleared; exact in fp32), rounded to
+    the nearest TF32 value, ties to even; non-finite remainders kept."""
+    x = np.asarray(x, np.float32)
+    hi = (x.view(np.uint32) & np.uint32(0xFFFFE000)).view(np.float32)
+    with np.errstate(invalid="ignore"):
+        r = (x - hi).astype(np.float32)
+    u = r.view(np.uint32).astype(np.uint64)
+    finite = (u & 0x7F800000) != 0x7F800000
+    rn = ((u + 0xFFF + ((u >> 13) & 1)) & 0xFFFFE000) & 0xFFFFFFFF
+    return np.where(finite, rn, u).astype(np.uint32).view(np.float32)
+
+
 def test_tf32_lo_plane_bits(capi):
-    """fz_tf32_lo: x - (x with its 13 low mantissa bits cleared), exact, any length."""
+    """fz_tf32_lo: the remainder x - hi rounded to the nearest TF32 value (ties to even,
+    including carries into the exponent), any length. The remainder is below 2^(e-10)
+    for x in [2^e, 2^(e+1)), so rounding it to 11 significant bits errs by at most
+    2^(e-22): hi + lo is within 2^-22 of x, relatively."""
     for n in [1, 3, 4, 1027, (1 << 20) + 5]:
         x = (RNG.standard_normal(n) * 10.0 ** RNG.integers(-30, 30, n)).astype(np.float32)
-        hi = (x.view(np.uint32) & np.uint32(0xFFFFE000)).view(np.float32)
+        if n > 8:
+            # x in [2048, 4096) has hi = x rounded down to a multiple of 2, so these
+            # remainders are 1 + 2^-11 (a tie, to even: 1), 1 + 3 * 2^-11 (a tie, to
+            # even: 1 + 2^-9), 1 + 2^-12 (below a tie), its negative, and 2 - 2^-11
+            # (rounds up into the next binade: 2)
+            x[:5] = np.array([2049 + 2.0 ** -11, 2049 + 3 * 2.0 ** -11, 2049 + 2.0 ** -12,
+                              -(2049 + 3 * 2.0 ** -11), 2050 - 2.0 ** -11], np.float32)
         dx, dl = capi.DeviceArray.from_numpy(x), capi.DeviceArray((n,))
         capi.check(capi.lib().fz_tf32_lo(dl.ptr, dx.ptr, n, None))
-        assert_bits_equal(dl.numpy(), x - hi, f"tf32 lo n={n}")
+        lo = dl.numpy()
+        assert_bits_equal(lo, tf32_lo_reference(x), f"tf32 lo n={n}")
+        hi = (x.view(np.uint32) & np.uint32(0xFFFFE000)).view(np.float32)
+        err = np.abs(hi.astype(np.float64) + lo - x.astype(np.float64))
+        assert np.all(err <= np.abs(x.astype(np.float64)) * 2.0 ** -22)
 
 
 @pytest.mark.parametrize("tA,tB", [(False, False), (False, True), (True, False), (True, True)])
@@ -386,9 +412,8 @@ def test_fused_value_and_tf32_remainder(capi):
     leaves = (C.c_void_p * 2)(dx.ptr, db.ptr)
     A.check(A.lib().fz_fused_launch(C.byref(prog), C.byref(plan), outs, leaves, None))
     v = np.maximum((x + b).astype(np.float32), np.float32(0))
-    hi = (v.view(np.uint32) & np.uint32(0xFFFFE000)).view(np.float32)
     assert_bits_equal(dv.numpy(), v, "value")
-    assert_bits_equal(dl.numpy(), v - hi, "remainder")
+    assert_bits_equal(dl.numpy(), tf32_lo_reference(v), "remainder")
 
 
 def test_fused_divide_backward_two_outputs(capi, port):
