@@ -7,6 +7,7 @@
 #include <cstdint>
 #include <cstdio>
 #include <string>
+#include <utility>
 #include <vector>
 
 #include "fusion_b200.h"
@@ -46,7 +47,32 @@ inline unsigned grid_for(int64_t work_items, int64_t per_cta, int ctas_per_sm, i
   return (unsigned)need;
 }
 
+// Programmatic dependent launch (PDL): `kernel` is launched on `s` with programmatic
+// stream serialization, so its launch and scheduling overlap the tail of the kernel
+// before it in the stream instead of starting after it has drained. The kernel must
+// execute pdl_wait() before it reads or writes global memory: that returns once the
+// preceding grid has completed and its memory operations are visible.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                              Args &&...args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 }  // namespace fz
+
+// First statement of a kernel launched with fz::launch_pdl: wait for the preceding
+// grid in the stream (a no-op when the launch had no programmatic dependency).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 #define FZ_CUDA(call)                                                        \
   do {                                                                       \

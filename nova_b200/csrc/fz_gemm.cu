@@ -39,6 +39,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <atomic>
 #include <cstddef>
 #include <cstring>
@@ -186,6 +187,19 @@ bool make_out_map(CUtensorMap *map, float *base, int64_t N, int64_t M, int64_t Z
 }
 
 int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
+
+// Bytes of B planes a column band of the raster may hold (kept in the 126 MB L2
+// beside A's streaming rows and the output's write-back).
+#ifndef FZ_GEMM_RASTER_MB
+#define FZ_GEMM_RASTER_MB 64
+#endif
+constexpr int64_t kRasterBandBytes = (int64_t)FZ_GEMM_RASTER_MB << 20;
+// With column bands, B's TMA loads carry an evict_last L2 policy and A's evict_first,
+// so the band's B planes outlive the activations streaming past them.
+#ifndef FZ_GEMM_L2_HINTS
+#define FZ_GEMM_L2_HINTS 1
+#endif
+constexpr bool g_l2_hints = FZ_GEMM_L2_HINTS != 0;
 
 // Launch counters by schedule (fz_gemm_stats): CTA-pair launches, single-CTA launches,
 // launches split over K, launches with a fused epilogue program compiled in.
@@ -1023,14 +1037,22 @@ int gemm_impl(int64_t batch, int64_t M, int64_t N, int64_t K, const float *A, co
   int *err = nullptr;
   if (!rc) rc = fz::device_error_word(&err);
   if (!rc) {
-    // raster bands of 16 row tiles walked column by column (a narrower band for the
-    // 256-row pair tiles re-reads B once more per band and measured slower)
+    // raster: bands of 16 row tiles walked column by column; or, when A is the much
+    // larger operand (activations against a weight), bands of column tiles walked row
+    // by row, as many as keep the band's B planes (hi and lo) within kRasterBandBytes,
+    // so B stays in L2 and A streams from DRAM once per band
     const int band = 16;
+    int group_n = 0;
+    if (kRasterBandBytes > 0 && tiles_m >= 4 * tiles_n && tiles_n > 1) {
+      const int64_t col_bytes = (int64_t)tbn * kps * 8;
+      group_n = (int)std::max<int64_t>(1, std::min<int64_t>(tiles_n, kRasterBandBytes / col_bytes));
+      if (group_n >= tiles_n) group_n = 0;  // one band: the row order is the same walk
+    }
     const bool in_kernel = E.pg && !product;
     GemmArgs ga{partial ? partial : in_kernel ? nullptr : C, partial ? N : ldc,
                 partial ? M * N : strideC, batch * M * N, (int)M, (int)N, (int)K, (int)batch,
-                tiles_m, tiles_n, (int)num_units, tiles_m < band ? tiles_m : band,
-                real_splits, (int)kps, wide_mask, err};
+                tiles_m, tiles_n, (int)num_units, tiles_m < band ? tiles_m : band, group_n,
+                group_n > 0 && g_l2_hints ? 1 : 0, real_splits, (int)kps, wide_mask, err};
     // persistent grid: one CTA (or CTA pair) per SM (pair of SMs)
     const unsigned grid = (unsigned)(num_units < workers ? num_units : workers);
     (pair ? g_stat_pair : g_stat_single).fetch_add(1, std::memory_order_relaxed);

@@ -64,6 +64,7 @@ __global__ void __launch_bounds__(256) rows_group_kernel(const float *__restrict
                                                          float *__restrict__ out, int64_t rows,
                                                          int64_t len, int64_t ld,
                                                          int64_t div_len, int final, int vec) {
+  pdl_wait();
   const int lane = threadIdx.x % G;
   const int64_t groups_total = (int64_t)gridDim.x * (blockDim.x / G);
   const int64_t nv = vec ? len >> 2 : 0;
@@ -108,6 +109,7 @@ __global__ void __launch_bounds__(512) rows_block_kernel(const float *__restrict
                                                          int64_t len, int64_t ld, int64_t splits,
                                                          int64_t chunk, int64_t div_len,
                                                          int final, int vec) {
+  pdl_wait();
   __shared__ float warp_part[32];
   const int64_t items = rows * splits;
   for (int64_t it = blockIdx.x; it < items; it += gridDim.x) {
@@ -160,6 +162,7 @@ __global__ void __launch_bounds__(256) cols_kernel(const float *__restrict__ in,
                                                    float *__restrict__ out, int64_t outer,
                                                    int64_t len, int64_t inner, int64_t splits,
                                                    int64_t chunk, int64_t div_len) {
+  pdl_wait();
   const int64_t cgroups = (inner + V - 1) / V;
   const int64_t items = splits * outer * cgroups;
   const bool split = splits > 1;
@@ -226,6 +229,7 @@ __global__ void __launch_bounds__(256, 4) cols_cluster_kernel(const float *__res
                                                            float *__restrict__ out, int64_t outer,
                                                            int64_t len, int64_t inner,
                                                            int64_t rows_per_cta, int64_t div_len) {
+  pdl_wait();
   namespace cg = cooperative_groups;
   cg::cluster_group cluster = cg::this_cluster();
   __shared__ float4 warp_part[8][32];
@@ -285,13 +289,15 @@ int launch_cols_cluster(const float *in, float *out, int64_t outer, int64_t len,
   cfg.gridDim = dim3((unsigned)(outer * cblocks), (unsigned)cs, 1);
   cfg.blockDim = dim3(256, 1, 1);
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 1;
   attr[0].val.clusterDim.y = (unsigned)cs;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // PDL: see fz::launch_pdl
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   FZ_CUDA(cudaLaunchKernelEx(&cfg, cols_cluster_kernel<OP>, in, out, outer, len, inner,
                              rows_per_cta, len));
   fz::note_launch();
@@ -310,8 +316,8 @@ int launch_rows_group(const float *in, float *out, int64_t rows, int64_t len, in
   unsigned grid = fz::grid_for(rows, per_cta, 8, 4);
 #define FZ_RG(g, r)                                                                          \
   if (G == g && R == r) {                                                                    \
-    rows_group_kernel<OP, g, r><<<grid, 256, 0, s>>>(in, out, rows, len, ld, div_len, final, \
-                                                      vec);                                  \
+    FZ_CUDA(fz::launch_pdl(rows_group_kernel<OP, g, r>, dim3(grid), dim3(256), 0, s, in, out, rows, \
+                           len, ld, div_len, (int)final, vec));                              \
   } else
   FZ_RG(1, 4) FZ_RG(2, 4) FZ_RG(4, 4) FZ_RG(8, 4) FZ_RG(16, 4) FZ_RG(32, 4)
   FZ_RG(32, 2) FZ_RG(32, 1) {
@@ -370,8 +376,8 @@ int launch_rows(const float *in, float *out, int64_t rows, int64_t len, int64_t 
   int64_t items = rows * splits;
   unsigned grid = (unsigned)(items < target_ctas * 2 ? items : target_ctas * 2);
   if (splits == 1) {
-    rows_block_kernel<OP><<<grid, threads, 0, s>>>(in, out, rows, len, len, 1, chunk, div_len,
-                                                   true, vec);
+    FZ_CUDA(fz::launch_pdl(rows_block_kernel<OP>, dim3(grid), dim3(threads), 0, s, in, out, rows, len, len,
+                           (int64_t)1, chunk, div_len, 1, vec));
     FZ_CHECK_LAUNCH();
     return FZ_OK;
   }
@@ -379,8 +385,9 @@ int launch_rows(const float *in, float *out, int64_t rows, int64_t len, int64_t 
   bool own = false;
   int rc = take_scratch(sc, items, &part, &own, s);
   if (rc) return rc;
-  rows_block_kernel<OP><<<grid, threads, 0, s>>>(in, part, rows, len, len, splits, chunk, 0,
-                                                 false, vec);
+  const cudaError_t e = fz::launch_pdl(rows_block_kernel<OP>, dim3(grid), dim3(threads), 0, s, in, part, rows,
+                                       len, len, splits, chunk, (int64_t)0, 0, vec);
+  if (e != cudaSuccess) return fz::cuda_fail(e, "rows_block_kernel launch", __FILE__, __LINE__);
   FZ_CHECK_LAUNCH();
   // splits <= 4 * SMs, so the second pass is a short-row group reduction
   rc = launch_rows_group<OP>(part, out, rows, splits, splits, div_len, true, s);
@@ -422,9 +429,11 @@ int launch_cols(const float *in, float *out, int64_t outer, int64_t len, int64_t
     if (rc) return rc;
   }
   if (V == 4)
-    cols_kernel<OP, 4><<<grid, 256, 0, s>>>(in, dst, outer, len, inner, splits, chunk, len);
+    FZ_CUDA(fz::launch_pdl(cols_kernel<OP, 4>, dim3(grid), dim3(256), 0, s, in, dst, outer, len, inner, splits,
+                           chunk, len));
   else
-    cols_kernel<OP, 1><<<grid, 256, 0, s>>>(in, dst, outer, len, inner, splits, chunk, len);
+    FZ_CUDA(fz::launch_pdl(cols_kernel<OP, 1>, dim3(grid), dim3(256), 0, s, in, dst, outer, len, inner, splits,
+                           chunk, len));
   FZ_CHECK_LAUNCH();
   if (splits == 1) return FZ_OK;
   // second pass: every output column's `splits` partials are contiguous

@@ -54,6 +54,7 @@ const char *op_name(OpKind k) {
     case OpKind::Sum: return "Sum";
     case OpKind::Mean: return "Mean";
     case OpKind::SwapAxes: return "SwapAxes";
+    case OpKind::Dropout: return "Dropout";
   }
   return "?";
 }
@@ -131,6 +132,9 @@ std::vector<RawTensor> op_forward(OpKind k, OpContext &ctx, const std::vector<Ra
       (void)unused;
       return {x};
     }
+    case OpKind::Dropout:
+      ctx.param = p;
+      return {math::dropout(x, p.rate, p.keep, p.rng_seed, p.rng_offset)};
     case OpKind::SwapAxes:
       FB_CHECK(p.axis1 != p.axis2, "SwapAxes: axes must be different");
       ctx.ints["axis1"] = p.axis1;
@@ -192,6 +196,13 @@ std::vector<RawTensor> op_backward(OpKind k, OpContext &ctx, const RawTensor &g0
     }
     case OpKind::SwapAxes:
       return {g0.swapaxes(ctx.ints.at("axis1"), ctx.ints.at("axis2"))};
+    case OpKind::Dropout: {
+      // the composition's backward, Divide (g0 / keep) then Multiply (* mask), gives
+      // (g0 / keep) * m, which equals (g0 * m) / keep for m in {0, 1} bit for bit
+      // (signed zeros and NaNs included): the same kernel redraws the same mask
+      const OpParam &q = ctx.param;
+      return {math::dropout(g0, q.rate, q.keep, q.rng_seed, q.rng_offset)};
+    }
   }
   throw std::runtime_error("unknown op");
 }
@@ -452,6 +463,7 @@ ADTensor ADTensor::unary_op(OpKind k, const OpParam &p) const {
       case OpKind::Sum: out = raw_.sum(p.axis, p.keepdim); break;
       case OpKind::Mean: out = raw_.mean(p.axis, p.keepdim); break;
       case OpKind::SwapAxes: out = raw_.swapaxes(p.axis1, p.axis2); break;
+      case OpKind::Dropout: out = math::dropout(raw_, p.rate, p.keep, p.rng_seed, p.rng_offset); break;
       default: throw std::runtime_error("not a unary op");
     }
     return ADTensor(out, requires_grad_);

@@ -40,17 +40,23 @@ struct OpParam {
   size_t axis = kGlobalReduceAxis;
   bool keepdim = false;
   int axis1 = 0, axis2 = 0;
+  // Dropout: the Philox stream (seed, offset) its mask is drawn from, the rate and
+  // the divisor keep = fp32(1 - rate)
+  uint64_t rng_seed = 0, rng_offset = 0;
+  float rate = 0.0f, keep = 1.0f;
 };
 
 struct OpContext {
   std::unordered_map<std::string, RawTensor> saved;
   std::unordered_map<std::string, int> ints;
+  OpParam param;  // the op's parameters, for backward formulas that need them
   const RawTensor &load(const std::string &k) const;
 };
 
 enum class OpKind {
   Add, Subtract, Multiply, Divide, Pow, Maximum, GreaterThan, GreaterThanEqual,
-  MatMul, Exp, Log, Sqrt, Sum, Mean, SwapAxes
+  MatMul, Exp, Log, Sqrt, Sum, Mean, SwapAxes,
+  Dropout  // no reference op: Nova's Dropout composition with a device-drawn mask
 };
 const char *op_name(OpKind k);
 

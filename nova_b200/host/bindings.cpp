@@ -26,9 +26,14 @@ size_t prod(const std::vector<size_t> &s) {
 
 // Random<T>::uniform_base (fusion/src/Fusion/Random.hpp:20-36): mt19937 with
 // uniform_real_distribution<float>, generated on the host, then uploaded.
+// The same seed also keys a device-side Philox-4x32-10 stream (fz_philox_*), for draws
+// made on the GPU: uniform_device and dropout. Its position advances by each draw's
+// size (rounded up to 4), so consecutive draws differ and a replayed sequence of draws
+// repeats. It does not reproduce the mt19937 stream of uniform_cpp.
 struct Random {
   std::mt19937 engine;
-  explicit Random(uint32_t seed) : engine(seed) {}
+  uint64_t seed = 0, offset = 0;
+  explicit Random(uint32_t s) : engine(s), seed(s) {}
   ADTensor uniform(const std::vector<size_t> &shape, float lo, float hi, Device dev) {
     std::vector<float> data;
     size_t n = prod(shape);
@@ -36,6 +41,27 @@ struct Random {
     std::uniform_real_distribution<float> dist(lo, hi);
     for (size_t i = 0; i < n; ++i) data.push_back(dist(engine));
     return ADTensor(RawTensor(shape, data, DType::FLOAT32, dev), false);
+  }
+  uint64_t advance(size_t n) {
+    const uint64_t at = offset;
+    offset += (n + 3) / 4 * 4;
+    return at;
+  }
+  ADTensor uniform_device(const std::vector<size_t> &shape, float lo, float hi, Device dev) {
+    const uint64_t at = advance(prod(shape));
+    return ADTensor(math::philox_uniform(shape, lo, hi, seed, at, DType::FLOAT32, dev), false);
+  }
+  // Nova's Dropout (nova/src/blocks/regularisation/dropout.py:17-23):
+  // inputs * (uniform >= rate) / (1 - rate), with `>=` computing `>` as Fusion's does,
+  // in one kernel and traced as one op whose backward redraws the mask.
+  ADTensor dropout(const ADTensor &x, double rate) {
+    if (!(rate >= 0.0 && rate < 1.0)) throw std::invalid_argument("dropout: rate must be in [0, 1)");
+    OpParam p;
+    p.rng_seed = seed;
+    p.rng_offset = advance(x.raw().size());
+    p.rate = (float)rate;
+    p.keep = (float)(1.0 - rate);
+    return x.unary_op(OpKind::Dropout, p);
   }
 };
 
@@ -319,6 +345,14 @@ PYBIND11_MODULE(fusion, m) {
 
   py::class_<Random>(m, "Random", py::module_local())
       .def(py::init<uint32_t>(), py::arg("seed") = std::random_device{}())
+      .def("uniform_device", &Random::uniform_device, py::arg("shape"), py::arg("min"), py::arg("max"),
+           py::arg("device"),
+           "Uniform values in [min, max) drawn on the GPU from this seed's Philox-4x32-10 stream "
+           "(not the mt19937 stream of uniform_cpp).")
+      .def("dropout", &Random::dropout, py::arg("x"), py::arg("rate"),
+           "Nova's Dropout, x * (u >= rate) / (1 - rate) with u drawn on the GPU, in one kernel; "
+           "traced by autodiff (the backward redraws the mask).")
+      .def_readonly("philox_offset", &Random::offset)
       .def("uniform_cpp", &Random::uniform, py::arg("shape"), py::arg("min"), py::arg("max"),
            py::arg("device"));
 

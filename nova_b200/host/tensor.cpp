@@ -1267,6 +1267,27 @@ void sub_inplace(RawTensor &x, const RawTensor &y) {
   x.storage()->expr = make_leaf(std::move(buf), x.shape());
 }
 
+RawTensor dropout(const RawTensor &x, float rate, float keep, uint64_t seed, uint64_t offset) {
+  FB_CHECK(x.is_initialised(), "dropout: uninitialised tensor");
+  FB_CHECK(rate >= 0.0f && rate < 1.0f, "dropout: rate must be in [0, 1)");
+  const float *px = x.data();
+  auto buf = std::make_shared<DeviceBuffer>(x.size());
+  fz_check(fz_philox_dropout(buf->ptr, px, (int64_t)x.size(), rate, keep, seed, offset, nullptr),
+           "fz_philox_dropout");
+  return RawTensor(make_leaf(std::move(buf), x.shape()), x.dtype(), x.device());
+}
+
+RawTensor philox_uniform(const std::vector<size_t> &shape, float lo, float hi, uint64_t seed,
+                         uint64_t offset, DType dtype, Device device) {
+  FB_CHECK(!shape.empty(), "Tensor: empty shape");
+  bind_device(device);
+  size_t n = 1;
+  for (size_t d : shape) n *= d;
+  auto buf = std::make_shared<DeviceBuffer>(n);
+  fz_check(fz_philox_uniform(buf->ptr, (int64_t)n, seed, offset, lo, hi, nullptr), "fz_philox_uniform");
+  return RawTensor(make_leaf(std::move(buf), shape), dtype, device);
+}
+
 // The first n values of x (flat order) as a tensor of `shape` (n elements).
 RawTensor flat_prefix(const RawTensor &x, size_t n, const std::vector<size_t> &shape) {
   FB_CHECK(x.is_initialised(), "flat_prefix: uninitialised tensor");

@@ -250,6 +250,12 @@ RawTensor reduce(int op, const RawTensor &x, size_t axis, bool keepdim);
 RawTensor matmul(const RawTensor &A, const RawTensor &B, bool transA = false, bool transB = false);
 RawTensor swapaxes(const RawTensor &x, int a1, int a2);
 void sub_inplace(RawTensor &x, const RawTensor &y);
+// (x * (u > rate)) / keep with u the Philox stream (seed, offset) in [0, 1): Nova's
+// Dropout composition in one pass (fz_philox_dropout), the mask never stored.
+RawTensor dropout(const RawTensor &x, float rate, float keep, uint64_t seed, uint64_t offset);
+// n values of the Philox stream (seed, offset) in [lo, hi) (fz_philox_uniform).
+RawTensor philox_uniform(const std::vector<size_t> &shape, float lo, float hi, uint64_t seed,
+                         uint64_t offset, DType dtype, Device device);
 RawTensor flat_prefix(const RawTensor &x, size_t n, const std::vector<size_t> &shape);
 }  // namespace math
 

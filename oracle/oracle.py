@@ -53,6 +53,10 @@ class Port:
         L.orc_reduce.restype = None
         L.orc_matmul.restype = None
         L.orc_swapaxes.restype = None
+        L.orc_philox4x32_10.argtypes = [C.c_uint64, C.c_uint64, C.c_uint64, C.POINTER(C.c_uint32)]
+        L.orc_philox4x32_10.restype = None
+        L.orc_philox_uniform.restype = None
+        L.orc_philox_dropout.restype = None
 
     def broadcast_shape(self, sa, sb):
         a, ap = _shape(sa)
@@ -110,6 +114,24 @@ class Port:
         out = np.empty(a.shape[:-2] + (m, n), dtype=np.float32)
         self.lib.orc_matmul(_fp(out), _fp(a), _fp(b), C.c_int64(batch), C.c_int64(m),
                             C.c_int64(n), C.c_int64(k))
+        return out
+
+    def philox_block(self, ctr_lo: int, ctr_hi: int, key: int) -> list:
+        out = (C.c_uint32 * 4)()
+        self.lib.orc_philox4x32_10(C.c_uint64(ctr_lo), C.c_uint64(ctr_hi), C.c_uint64(key), out)
+        return list(out)
+
+    def philox_uniform(self, n: int, seed: int, offset: int, lo: float, hi: float) -> np.ndarray:
+        out = np.empty(n, np.float32)
+        self.lib.orc_philox_uniform(_fp(out), C.c_int64(n), C.c_uint64(seed), C.c_uint64(offset),
+                                    C.c_float(lo), C.c_float(hi))
+        return out
+
+    def philox_dropout(self, x: np.ndarray, rate: float, keep: float, seed: int, offset: int) -> np.ndarray:
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        out = np.empty_like(x)
+        self.lib.orc_philox_dropout(_fp(out), _fp(x), C.c_int64(x.size), C.c_float(rate), C.c_float(keep),
+                                    C.c_uint64(seed), C.c_uint64(offset))
         return out
 
     def swapaxes(self, a: np.ndarray, a1: int, a2: int) -> np.ndarray:

@@ -347,6 +347,42 @@ int fz_stream_delay(void *, double seconds) {
   g_busy_s += seconds;
   return FZ_OK;
 }
+// Philox-4x32-10 (Salmon et al., SC'11), the device generator's stream layout.
+static void philox(uint64_t ctr, uint64_t key, uint32_t c[4]) {
+  c[0] = (uint32_t)ctr; c[1] = (uint32_t)(ctr >> 32); c[2] = 0; c[3] = 0;
+  uint32_t k0 = (uint32_t)key, k1 = (uint32_t)(key >> 32);
+  for (int r = 0; r < 10; ++r) {
+    const uint64_t p0 = (uint64_t)0xD2511F53u * c[0], p1 = (uint64_t)0xCD9E8D57u * c[2];
+    const uint32_t n0 = (uint32_t)(p1 >> 32) ^ c[1] ^ k0, n2 = (uint32_t)(p0 >> 32) ^ c[3] ^ k1;
+    c[1] = (uint32_t)p1; c[3] = (uint32_t)p0; c[0] = n0; c[2] = n2;
+    k0 += 0x9E3779B9u; k1 += 0xBB67AE85u;
+  }
+}
+static float philox_unit(uint64_t seed, uint64_t i) {
+  uint32_t c[4];
+  philox(i / 4, seed, c);
+  return (float)(c[i % 4] >> 8) * 5.9604644775390625e-08f;
+}
+int fz_philox_uniform(float *out, int64_t n, uint64_t seed, uint64_t offset, float lo, float hi, void *) {
+  if (offset % 4 || !(lo < hi)) return fail(FZ_ERR_INVALID, "fz_philox_uniform: bad arguments");
+  for (int64_t i = 0; i < n; ++i) {
+    float v = std::fmaf(hi - lo, philox_unit(seed, offset + (uint64_t)i), lo);
+    out[i] = v >= hi ? std::nextafterf(hi, lo) : v;
+  }
+  ++g_launches;
+  return FZ_OK;
+}
+int fz_philox_dropout(float *out, const float *x, int64_t n, float rate, float keep, uint64_t seed,
+                      uint64_t offset, void *) {
+  if (offset % 4 || !(rate >= 0.0f && rate < 1.0f)) return fail(FZ_ERR_INVALID, "fz_philox_dropout: bad arguments");
+  for (int64_t i = 0; i < n; ++i) {
+    const float m = philox_unit(seed, offset + (uint64_t)i) > rate ? 1.0f : 0.0f;
+    out[i] = (x[i] * m) / keep;
+  }
+  ++g_launches;
+  return FZ_OK;
+}
+
 int fz_comm_unique_id(unsigned char id[FZ_UNIQUE_ID_BYTES]) { std::memset(id, 0, FZ_UNIQUE_ID_BYTES); return FZ_OK; }
 int fz_comm_init(void **c, int world, int, const unsigned char *) {
   if (world != 1 && !g_transport) return fail(FZ_ERR_UNSUPPORTED, "host test double: world must be 1");

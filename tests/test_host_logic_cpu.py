@@ -13,6 +13,7 @@ import numpy as np
 import pytest
 
 import api_cases
+from conftest import assert_bits_equal
 from test_api_gpu import GOLDEN, _compare, _kinds
 
 HERE = pathlib.Path(__file__).resolve().parent
@@ -479,3 +480,31 @@ def test_launch_plans_are_cached_by_shape(fake_fusion):
     y = api_cases.T(F, rng.standard_normal((3, 5, 7)))
     (y * b).to_numpy()  # a new shape set: one more plan
     assert _stat(F, "plan_cache_misses") == m0 + 1
+
+
+def test_device_dropout_is_novas_composition(fake_fusion):
+    """Random.dropout equals Nova's Dropout composition, x * (u >= rate) / (1 - rate), over
+    the same seed's device stream (u from uniform_device), forward and backward, bit for
+    bit; consecutive draws advance the stream."""
+    F = fake_fusion
+    rng = np.random.default_rng(50)
+    X = rng.standard_normal((6, 10)).astype(np.float32)
+    X[0, :3] = [0.0, -0.0, np.inf]
+    rate = 0.3
+    r1, r2 = F.Random(77), F.Random(77)
+    x1, x2 = api_cases.T(F, X, True), api_cases.T(F, X, True)
+    with F.grad_tape():
+        y1 = r1.dropout(x1, rate)
+        (y1 * 3.0).backward()
+    with F.grad_tape():
+        u = r2.uniform_device([6, 10], 0.0, 1.0, F.CppDevice(F.CppDeviceType.CPU, 0))
+        y2 = x2 * (u >= rate) / (1 - rate)
+        (y2 * 3.0).backward()
+    with np.errstate(invalid="ignore"):
+        assert_bits_equal(y1.to_numpy(), y2.to_numpy(), "forward")
+        assert_bits_equal(x1.get_grad().to_numpy(), x2.get_grad().to_numpy(), "backward")
+    assert r1.philox_offset == r2.philox_offset == 60
+    d = F.CppDevice(F.CppDeviceType.CPU, 0)
+    a, b = F.Random(5).uniform_device([7], -2.0, 3.0, d).to_numpy(), F.Random(5).uniform_device([7], -2.0, 3.0, d)
+    np.testing.assert_array_equal(a, b.to_numpy())
+    assert np.all((a >= -2.0) & (a < 3.0))

@@ -136,3 +136,17 @@ def test_reference_mlp_step_matches_golden(golden, ref):
     for i in range(3):
         assert_bits_equal(W2[i], golden[f"case_mlp_step.W{i}"])
         assert_bits_equal(b2[i], golden[f"case_mlp_step.b{i}"])
+
+
+def test_philox_restatement_matches_published_vectors(port):
+    """The oracle's Philox-4x32-10 (Salmon et al., SC'11) reproduces the published
+    known-answer vectors of the algorithm (counter, key -> output)."""
+    kat = [((0, 0, 0, 0), (0, 0), (0x6627E8D5, 0xE169C58D, 0xBC57AC4C, 0x9B00DBD8)),
+           ((0xFFFFFFFF,) * 4, (0xFFFFFFFF,) * 2, (0x408F276D, 0x41C83B0E, 0xA20BC7C6, 0x6D5451FD)),
+           ((0x243F6A88, 0x85A308D3, 0x13198A2E, 0x03707344), (0xA4093822, 0x299F31D0),
+            (0xD16CFE09, 0x94FDCCEB, 0x5001E420, 0x24126EA1))]
+    for c, k, want in kat:
+        got = port.philox_block(c[0] | c[1] << 32, c[2] | c[3] << 32, k[0] | k[1] << 32)
+        assert tuple(got) == want
+    u = port.philox_uniform(1 << 16, 9, 0, 0.0, 1.0)
+    assert 0.0 <= u.min() and u.max() < 1.0 and abs(u.mean() - 0.5) < 0.01
