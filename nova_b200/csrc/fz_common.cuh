@@ -68,6 +68,22 @@ inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
+// The same for a kernel handle (runtime-compiled kernels) and its argument array.
+inline cudaError_t launch_pdl_handle(const void *kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                                     void **args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelExC(&cfg, kernel, args);
+}
+
 }  // namespace fz
 
 // First statement of a kernel launched with fz::launch_pdl: wait for the preceding

@@ -51,6 +51,7 @@ template <int NIN, int OP, int VEC, typename IDX>
 __global__ void __launch_bounds__(256) ewise_kernel(EwPlan p, float *__restrict__ out,
                                                     const float *__restrict__ a,
                                                     const float *__restrict__ b) {
+  pdl_wait();
   const int64_t inner = p.ndim ? p.size[p.ndim - 1] : 1;
   const IDX groups_per_row = (IDX)((inner + VEC - 1) / VEC);
   const IDX total = (IDX)p.rows * groups_per_row;
@@ -114,6 +115,7 @@ template <int NIN, int OP, int U>
 __global__ void __launch_bounds__(256) ewise_tiles_kernel(EwPlan p, float *__restrict__ out,
                                                           const float *__restrict__ a,
                                                           const float *__restrict__ b) {
+  pdl_wait();
   constexpr int64_t TW = 1024 * U;
   const int64_t inner = p.size[p.ndim - 1];
   const int64_t ctiles = (inner + TW - 1) / TW;
@@ -186,10 +188,12 @@ int launch_op(const EwPlan &p, float *out, const float *a, const float *b, cudaS
     const int U = (NIN == 1 && inner >= 8192) ? 8 : inner >= 4096 ? 4 : inner >= 2048 ? 2 : 1;
     const int64_t tiles = p.rows * ((inner + 1024 * U - 1) / (1024 * U));
     const unsigned grid = (unsigned)(tiles < (int64_t)fz::num_sms() * 8 ? tiles : fz::num_sms() * 8);
-    if (U == 8) ewise_tiles_kernel<NIN, OP, (NIN == 1 ? 8 : 4)><<<grid, 256, 0, s>>>(p, out, a, b);
-    else if (U == 4) ewise_tiles_kernel<NIN, OP, 4><<<grid, 256, 0, s>>>(p, out, a, b);
-    else if (U == 2) ewise_tiles_kernel<NIN, OP, 2><<<grid, 256, 0, s>>>(p, out, a, b);
-    else ewise_tiles_kernel<NIN, OP, 1><<<grid, 256, 0, s>>>(p, out, a, b);
+    cudaError_t e;
+    if (U == 8) e = fz::launch_pdl(ewise_tiles_kernel<NIN, OP, (NIN == 1 ? 8 : 4)>, dim3(grid), dim3(256), 0, s, p, out, a, b);
+    else if (U == 4) e = fz::launch_pdl(ewise_tiles_kernel<NIN, OP, 4>, dim3(grid), dim3(256), 0, s, p, out, a, b);
+    else if (U == 2) e = fz::launch_pdl(ewise_tiles_kernel<NIN, OP, 2>, dim3(grid), dim3(256), 0, s, p, out, a, b);
+    else e = fz::launch_pdl(ewise_tiles_kernel<NIN, OP, 1>, dim3(grid), dim3(256), 0, s, p, out, a, b);
+    if (e != cudaSuccess) return fz::cuda_fail(e, "ewise_tiles_kernel launch", __FILE__, __LINE__);
     FZ_CHECK_LAUNCH();
     return FZ_OK;
   }
@@ -197,13 +201,15 @@ int launch_op(const EwPlan &p, float *out, const float *a, const float *b, cudaS
   int64_t groups = p.rows * ((inner + V - 1) / V);
   bool i64 = groups > (int64_t)0x7fffffff - (int64_t)fz::num_sms() * 2048;
   unsigned grid = fz::grid_for(groups, 256 * 2, 8);
+  cudaError_t e;
   if (vec) {
-    if (i64) ewise_kernel<NIN, OP, 4, int64_t><<<grid, 256, 0, s>>>(p, out, a, b);
-    else ewise_kernel<NIN, OP, 4, int32_t><<<grid, 256, 0, s>>>(p, out, a, b);
+    if (i64) e = fz::launch_pdl(ewise_kernel<NIN, OP, 4, int64_t>, dim3(grid), dim3(256), 0, s, p, out, a, b);
+    else e = fz::launch_pdl(ewise_kernel<NIN, OP, 4, int32_t>, dim3(grid), dim3(256), 0, s, p, out, a, b);
   } else {
-    if (i64) ewise_kernel<NIN, OP, 1, int64_t><<<grid, 256, 0, s>>>(p, out, a, b);
-    else ewise_kernel<NIN, OP, 1, int32_t><<<grid, 256, 0, s>>>(p, out, a, b);
+    if (i64) e = fz::launch_pdl(ewise_kernel<NIN, OP, 1, int64_t>, dim3(grid), dim3(256), 0, s, p, out, a, b);
+    else e = fz::launch_pdl(ewise_kernel<NIN, OP, 1, int32_t>, dim3(grid), dim3(256), 0, s, p, out, a, b);
   }
+  if (e != cudaSuccess) return fz::cuda_fail(e, "ewise_kernel launch", __FILE__, __LINE__);
   FZ_CHECK_LAUNCH();
   return FZ_OK;
 }

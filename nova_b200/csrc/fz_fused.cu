@@ -131,6 +131,7 @@ std::string ref_name(int s) { return s >= 0 ? "t" + std::to_string(s) : "l" + st
 void generate_tiles(std::ostringstream &o, const fz_program &pg, const int *cls, int U) {
   const int nout = pg.num_outputs, nleaf = pg.num_leaves, nops = nout + nleaf;
   o << "extern \"C\" __global__ void __launch_bounds__(256) fz_fused(const FusedParams p) {\n"
+    << "  asm volatile(\"griddepcontrol.wait;\" ::: \"memory\");\n"
     << "  const long long inner = p.size[p.ndim - 1];\n"
     << "  const long long TW = " << 1024 * U << ";\n"
     << "  const long long ctiles = (inner + TW - 1) / TW;\n"
@@ -214,6 +215,7 @@ std::string generate(const fz_program &pg, const int *cls, int vec, bool i64, in
   }
   const char *IDX = i64 ? "long long" : "int";
   o << "extern \"C\" __global__ void __launch_bounds__(256) fz_fused(const FusedParams p) {\n"
+    << "  asm volatile(\"griddepcontrol.wait;\" ::: \"memory\");\n"
     << "  typedef " << IDX << " IDX;\n"
     << "  const long long inner = p.size[p.ndim - 1];\n"
     << "  const IDX gpr = (IDX)((inner + " << vec - 1 << ") / " << vec << ");\n"
@@ -432,7 +434,7 @@ int fz_fused_launch(const fz_program *prog, const fz_ewise_plan *plan, float *co
     grid = fz::grid_for(groups, 256 * 2, 8);
   }
   void *args[] = {&fp};
-  FZ_CUDA(cudaLaunchKernel((const void *)kern, dim3(grid), dim3(256), args, 0, fz::resolve(stream)));
+  FZ_CUDA(fz::launch_pdl_handle((const void *)kern, dim3(grid), dim3(256), 0, fz::resolve(stream), args));
   fz::note_launch();
   return FZ_OK;
 }

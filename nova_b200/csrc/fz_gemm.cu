@@ -72,6 +72,7 @@ __global__ void __launch_bounds__(256) lo_kernel(const float *__restrict__ src, 
                                                  int64_t sb, int64_t rows, int64_t K, int64_t kp,
                                                  int64_t batch, float *__restrict__ lo,
                                                  float *__restrict__ hi) {
+  pdl_wait();
   const int64_t step = (int64_t)gridDim.x * blockDim.x;
   const int64_t t0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (!hi && ld == kp && K == kp && kp % 4 == 0 && (batch == 1 || sb == rows * kp) &&
@@ -188,18 +189,6 @@ bool make_out_map(CUtensorMap *map, float *base, int64_t N, int64_t M, int64_t Z
 
 int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
 
-// Bytes of B planes a column band of the raster may hold (kept in the 126 MB L2
-// beside A's streaming rows and the output's write-back).
-#ifndef FZ_GEMM_RASTER_MB
-#define FZ_GEMM_RASTER_MB 64
-#endif
-constexpr int64_t kRasterBandBytes = (int64_t)FZ_GEMM_RASTER_MB << 20;
-// With column bands, B's TMA loads carry an evict_last L2 policy and A's evict_first,
-// so the band's B planes outlive the activations streaming past them.
-#ifndef FZ_GEMM_L2_HINTS
-#define FZ_GEMM_L2_HINTS 1
-#endif
-constexpr bool g_l2_hints = FZ_GEMM_L2_HINTS != 0;
 
 // Launch counters by schedule (fz_gemm_stats): CTA-pair launches, single-CTA launches,
 // launches split over K, launches with a fused epilogue program compiled in.
@@ -332,7 +321,7 @@ int prepare(const float *src, int64_t ld, int64_t sb, const float *lo_given, int
   const int64_t plane = batch * op->rows * pitch;
   float *lo = ws, *hi = direct ? nullptr : ws + plane;
   unsigned grid = fz::grid_for(plane / 4 + 1, 256, 8, 4);
-  lo_kernel<<<grid, 256, 0, s>>>(src, ld, sb, op->rows, op->inner, pitch, batch, lo, hi);
+  FZ_CUDA(fz::launch_pdl(lo_kernel, dim3(grid), dim3(256), 0, s, src, ld, sb, op->rows, op->inner, pitch, batch, lo, hi));
   FZ_CHECK_LAUNCH();
   op->lo = lo;
   op->lo_ld = pitch;
@@ -397,9 +386,9 @@ int launch_gemm(const CUtensorMap &mAh, const CUtensorMap &mAl, const CUtensorMa
     if (dev < 64) attr_done[pair][dev] = true;
   }
   if (pair)
-    gemm_pair_kernel<A_MN, B_MN, StoreEpi><<<2 * grid, NUM_THREADS, smem, s>>>(mAh, mAl, mBh, mBl, ga, ep);
+    FZ_CUDA(fz::launch_pdl(gemm_pair_kernel<A_MN, B_MN, StoreEpi>, dim3(2 * grid), dim3(NUM_THREADS), smem, s, mAh, mAl, mBh, mBl, ga, ep));
   else
-    gemm_3xtf32_kernel<A_MN, B_MN, TBN, StoreEpi><<<grid, NUM_THREADS, smem, s>>>(mAh, mAl, mBh, mBl, ga, ep);
+    FZ_CUDA(fz::launch_pdl(gemm_3xtf32_kernel<A_MN, B_MN, TBN, StoreEpi>, dim3(grid), dim3(NUM_THREADS), smem, s, mAh, mAl, mBh, mBl, ga, ep));
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fz::cuda_fail(e, "gemm_3xtf32_kernel launch", __FILE__, __LINE__);
   fz::note_launch();
@@ -850,8 +839,7 @@ int launch_epilogue_gemm(const Epilogue &E, const int *cls, const EpiParams &ep,
   void *args[] = {const_cast<CUtensorMap *>(&mAh), const_cast<CUtensorMap *>(&mAl),
                   const_cast<CUtensorMap *>(&mBh), const_cast<CUtensorMap *>(&mBl),
                   const_cast<GemmArgs *>(&ga), const_cast<EpiParams *>(&ep)};
-  FZ_CUDA(cudaLaunchKernel((const void *)k, dim3(pair ? 2 * grid : grid), dim3(NUM_THREADS), args,
-                           smem, s));
+  FZ_CUDA(fz::launch_pdl_handle((const void *)k, dim3(pair ? 2 * grid : grid), dim3(NUM_THREADS), smem, s, args));
   fz::note_launch();
   return FZ_OK;
 }
@@ -1037,22 +1025,15 @@ int gemm_impl(int64_t batch, int64_t M, int64_t N, int64_t K, const float *A, co
   int *err = nullptr;
   if (!rc) rc = fz::device_error_word(&err);
   if (!rc) {
-    // raster: bands of 16 row tiles walked column by column; or, when A is the much
-    // larger operand (activations against a weight), bands of column tiles walked row
-    // by row, as many as keep the band's B planes (hi and lo) within kRasterBandBytes,
-    // so B stays in L2 and A streams from DRAM once per band
+    // raster bands of 16 row tiles walked column by column (narrower bands, and bands of
+    // B columns walked row by row with L2 eviction hints keeping B, were measured slower:
+    // DRAM is not what bounds these kernels)
     const int band = 16;
-    int group_n = 0;
-    if (kRasterBandBytes > 0 && tiles_m >= 4 * tiles_n && tiles_n > 1) {
-      const int64_t col_bytes = (int64_t)tbn * kps * 8;
-      group_n = (int)std::max<int64_t>(1, std::min<int64_t>(tiles_n, kRasterBandBytes / col_bytes));
-      if (group_n >= tiles_n) group_n = 0;  // one band: the row order is the same walk
-    }
     const bool in_kernel = E.pg && !product;
     GemmArgs ga{partial ? partial : in_kernel ? nullptr : C, partial ? N : ldc,
                 partial ? M * N : strideC, batch * M * N, (int)M, (int)N, (int)K, (int)batch,
-                tiles_m, tiles_n, (int)num_units, tiles_m < band ? tiles_m : band, group_n,
-                group_n > 0 && g_l2_hints ? 1 : 0, real_splits, (int)kps, wide_mask, err};
+                tiles_m, tiles_n, (int)num_units, tiles_m < band ? tiles_m : band,
+                real_splits, (int)kps, wide_mask, err};
     // persistent grid: one CTA (or CTA pair) per SM (pair of SMs)
     const unsigned grid = (unsigned)(num_units < workers ? num_units : workers);
     (pair ? g_stat_pair : g_stat_single).fetch_add(1, std::memory_order_relaxed);
@@ -1149,7 +1130,7 @@ extern "C" int fz_tf32_lo(float *lo, const float *x, int64_t n, void *stream) {
   FZ_REQUIRE(lo && x, "fz_tf32_lo: null pointer");
   cudaStream_t s = fz::resolve(stream);
   unsigned grid = fz::grid_for(n / 4 + 1, 256, 8, 4);
-  lo_kernel<<<grid, 256, 0, s>>>(x, n, n, 1, n, n, 1, lo, nullptr);
+  FZ_CUDA(fz::launch_pdl(lo_kernel, dim3(grid), dim3(256), 0, s, x, n, n, 1, n, n, 1, lo, nullptr));
   FZ_CHECK_LAUNCH();
   return FZ_OK;
 }

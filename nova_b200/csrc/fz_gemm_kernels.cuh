@@ -127,36 +127,29 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volati
   }
 }
 
-// L2 eviction priority of a TMA load (createpolicy): the operand a raster keeps for
-// reuse across tiles goes in with evict_last, the one streamed past with evict_first.
-__device__ __forceinline__ uint64_t l2_policy(int kind) {
-  uint64_t p;
-  if (kind == 2) asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
-  else if (kind == 1) asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
-  else asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(p));
-  return p;
-}
-
 __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, uint64_t *bar,
-                                            int c0, int c1, int c2, uint64_t pol) {
+                                            int c0, int c1, int c2) {
   asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
-      " [%0], [%1, {%3, %4, %5}], [%2], %6;" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "l"(pol)
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
       : "memory");
 }
+
+// Kernels are launched with programmatic stream serialization (PDL): wait for the grid
+// before in the stream to complete before touching global memory.
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 __device__ __forceinline__ void prefetch_map(const CUtensorMap *map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
 __device__ __forceinline__ void tma_load_4d(void *dst, const CUtensorMap *map, uint64_t *bar,
-                                            int c0, int c1, int c2, int c3, uint64_t pol) {
+                                            int c0, int c1, int c2, int c3) {
   asm volatile(
-      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
-      " [%0], [%1, {%3, %4, %5, %6}], [%2], %7;" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3),
-      "l"(pol)
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
       : "memory");
 }
 
@@ -167,17 +160,17 @@ __device__ __forceinline__ void tma_load_4d(void *dst, const CUtensorMap *map, u
 // zero-filled by the TMA unit.
 template <bool MN, int ROWS>
 __device__ __forceinline__ void load_operand(uint8_t *dst, const CUtensorMap *map, uint64_t *bar,
-                                             int k0, int row0, int bz, bool wide, uint64_t pol) {
+                                             int k0, int row0, int bz, bool wide) {
   if constexpr (MN) {
     if (wide) {
-      tma_load_4d(dst, map, bar, 0, k0, row0 / MN_CHUNK, bz, pol);
+      tma_load_4d(dst, map, bar, 0, k0, row0 / MN_CHUNK, bz);
     } else {
 #pragma unroll
       for (int j = 0; j < ROWS / MN_CHUNK; ++j)
-        tma_load_3d(dst + j * MN_CHUNK_BYTES, map, bar, row0 + j * MN_CHUNK, k0, bz, pol);
+        tma_load_3d(dst + j * MN_CHUNK_BYTES, map, bar, row0 + j * MN_CHUNK, k0, bz);
     }
   } else {
-    tma_load_3d(dst, map, bar, k0, row0, bz, pol);
+    tma_load_3d(dst, map, bar, k0, row0, bz);
   }
 }
 
@@ -281,8 +274,6 @@ struct GemmArgs {
   int64_t split_stride;  // floats between the partial outputs of consecutive K splits
   int M, N, K, batch;
   int tiles_m, tiles_n, num_tiles, group_m;  // num_tiles counts work units (tiles x K splits)
-  int group_n;  // > 0: bands of group_n column blocks walked row by row (instead of group_m)
-  int l2_keep_b;  // load B with evict_last and A with evict_first (column bands), else normal
   int splits, k_per_split;  // K is cut into `splits` ranges of k_per_split (multiple of BK)
   int wide;                 // bits 0-3: map Ah, Al, Bh, Bl is a wide (4D) MN-major map
   int *err;
@@ -574,8 +565,7 @@ __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
 
 // Work unit t -> (K split, batch, m block, n block). Units of one K split are
 // consecutive; within a batch, bands of group_m row blocks are walked column by
-// column (or, with group_n, bands of group_n column blocks row by row), so the units
-// in flight on the 148 SMs share A rows and B columns in L2.
+// column, so the units in flight on the 148 SMs share A rows and B columns in L2.
 __device__ __forceinline__ void decode_tile(int t, const GemmArgs &a, int &mb, int &nb, int &bz,
                                             int &ks) {
   const int per_batch = a.tiles_m * a.tiles_n;
@@ -584,16 +574,6 @@ __device__ __forceinline__ void decode_tile(int t, const GemmArgs &a, int &mb, i
   t -= ks * per_split;
   bz = t / per_batch;
   const int r = t - bz * per_batch;
-  if (a.group_n > 0) {
-    // column bands: the band's B columns stay in L2 while A's rows stream past once
-    const int band = r / (a.group_n * a.tiles_m);
-    const int first_n = band * a.group_n;
-    const int cols = min(a.group_n, a.tiles_n - first_n);
-    const int in_band = r - band * a.group_n * a.tiles_m;
-    nb = first_n + in_band % cols;
-    mb = in_band / cols;
-    return;
-  }
   const int band = r / (a.group_m * a.tiles_n);
   const int first_m = band * a.group_m;
   const int rows = min(a.group_m, a.tiles_m - first_m);
@@ -672,6 +652,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                        const __grid_constant__ CUtensorMap mapBh,
                        const __grid_constant__ CUtensorMap mapBl, GemmArgs args,
                        const __grid_constant__ EpiParams ep) {
+  grid_dependency_wait();
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -737,7 +718,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if (warp == 0) {
       if (lane == 0) {
         // ------------------------------------------------------ TMA producer
-        const uint64_t pol_a = l2_policy(args.l2_keep_b ? 1 : 0), pol_b = l2_policy(args.l2_keep_b ? 2 : 0);
         int it = 0;
         bool ok = true;
         for (int t = blockIdx.x; ok && t < args.num_tiles; t += gridDim.x) {
@@ -753,10 +733,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             }
             mbar_expect_tx(&full_bar[s], STAGE_BYTES);
             const int k0 = kb + kt * BK;
-            load_operand<A_MN, BM>(stage_ptr(s, 0), &mapAh, &full_bar[s], k0, mb * BM, bz, args.wide & 1, pol_a);
-            load_operand<A_MN, BM>(stage_ptr(s, 1), &mapAl, &full_bar[s], k0, mb * BM, bz, args.wide & 2, pol_a);
-            load_operand<B_MN, TBN>(stage_ptr(s, 2), &mapBh, &full_bar[s], k0, nb * TBN, bz, args.wide & 4, pol_b);
-            load_operand<B_MN, TBN>(stage_ptr(s, 3), &mapBl, &full_bar[s], k0, nb * TBN, bz, args.wide & 8, pol_b);
+            load_operand<A_MN, BM>(stage_ptr(s, 0), &mapAh, &full_bar[s], k0, mb * BM, bz, args.wide & 1);
+            load_operand<A_MN, BM>(stage_ptr(s, 1), &mapAl, &full_bar[s], k0, mb * BM, bz, args.wide & 2);
+            load_operand<B_MN, TBN>(stage_ptr(s, 2), &mapBh, &full_bar[s], k0, nb * TBN, bz, args.wide & 4);
+            load_operand<B_MN, TBN>(stage_ptr(s, 3), &mapBl, &full_bar[s], k0, nb * TBN, bz, args.wide & 8);
           }
         }
         if (!ok) {
@@ -906,37 +886,37 @@ __device__ __forceinline__ uint32_t in_leader(const void *p) {
 }
 
 __device__ __forceinline__ void tma_load_3d_pair(void *dst, const CUtensorMap *map, uint32_t bar,
-                                                 int c0, int c1, int c2, uint64_t pol) {
+                                                 int c0, int c1, int c2) {
   asm volatile(
-      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
-      " [%0], [%1, {%3, %4, %5}], [%2], %6;" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2), "l"(pol)
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
       : "memory");
 }
 
 __device__ __forceinline__ void tma_load_4d_pair(void *dst, const CUtensorMap *map, uint32_t bar,
-                                                 int c0, int c1, int c2, int c3, uint64_t pol) {
+                                                 int c0, int c1, int c2, int c3) {
   asm volatile(
-      "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
-      " [%0], [%1, {%3, %4, %5, %6}], [%2], %7;" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "l"(pol)
+      "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
       : "memory");
 }
 
 // load_operand for a CTA of a pair: 128 rows, bytes completed on the leader's barrier.
 template <bool MN>
 __device__ __forceinline__ void load_operand_pair(uint8_t *dst, const CUtensorMap *map, uint32_t bar,
-                                                  int k0, int row0, int bz, bool wide, uint64_t pol) {
+                                                  int k0, int row0, int bz, bool wide) {
   if constexpr (MN) {
     if (wide) {
-      tma_load_4d_pair(dst, map, bar, 0, k0, row0 / MN_CHUNK, bz, pol);
+      tma_load_4d_pair(dst, map, bar, 0, k0, row0 / MN_CHUNK, bz);
     } else {
 #pragma unroll
       for (int j = 0; j < BM / MN_CHUNK; ++j)
-        tma_load_3d_pair(dst + j * MN_CHUNK_BYTES, map, bar, row0 + j * MN_CHUNK, k0, bz, pol);
+        tma_load_3d_pair(dst + j * MN_CHUNK_BYTES, map, bar, row0 + j * MN_CHUNK, k0, bz);
     }
   } else {
-    tma_load_3d_pair(dst, map, bar, k0, row0, bz, pol);
+    tma_load_3d_pair(dst, map, bar, k0, row0, bz);
   }
 }
 
@@ -972,6 +952,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
                      const __grid_constant__ CUtensorMap mapBh,
                      const __grid_constant__ CUtensorMap mapBl, GemmArgs args,
                      const __grid_constant__ EpiParams ep) {
+  grid_dependency_wait();
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -1028,7 +1009,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     if (warp == 0) {
       if (lane == 0) {
         // ------------------------------------------------------ TMA producer (both CTAs)
-        const uint64_t pol_a = l2_policy(args.l2_keep_b ? 1 : 0), pol_b = l2_policy(args.l2_keep_b ? 2 : 0);
         int it = 0;
         bool ok = true;
         for (int t = pair; ok && t < args.num_tiles; t += npairs) {
@@ -1046,10 +1026,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
             if (leader) mbar_expect_tx(&full_bar[s], 2 * PAIR_STAGE_BYTES);
             const uint32_t fb = in_leader(&full_bar[s]);
             const int k0 = kb + kt * BK;
-            load_operand_pair<A_MN>(stage_ptr(s, 0), &mapAh, fb, k0, row_a, bz, args.wide & 1, pol_a);
-            load_operand_pair<A_MN>(stage_ptr(s, 1), &mapAl, fb, k0, row_a, bz, args.wide & 2, pol_a);
-            load_operand_pair<B_MN>(stage_ptr(s, 2), &mapBh, fb, k0, row_b, bz, args.wide & 4, pol_b);
-            load_operand_pair<B_MN>(stage_ptr(s, 3), &mapBl, fb, k0, row_b, bz, args.wide & 8, pol_b);
+            load_operand_pair<A_MN>(stage_ptr(s, 0), &mapAh, fb, k0, row_a, bz, args.wide & 1);
+            load_operand_pair<A_MN>(stage_ptr(s, 1), &mapAl, fb, k0, row_a, bz, args.wide & 2);
+            load_operand_pair<B_MN>(stage_ptr(s, 2), &mapBh, fb, k0, row_b, bz, args.wide & 4);
+            load_operand_pair<B_MN>(stage_ptr(s, 3), &mapBl, fb, k0, row_b, bz, args.wide & 8);
           }
         }
         if (!ok) {

@@ -61,6 +61,7 @@ __device__ __forceinline__ uint32_t lane(const U4 &r, int k) {
 // so element i's block is offset/4 + i/4 and its lane i % 4.
 __global__ void __launch_bounds__(256) uniform_kernel(float *__restrict__ out, int64_t n, uint64_t seed,
                                                       uint64_t base, float lo, float hi) {
+  pdl_wait();
   const float span = hi - lo;
   const int64_t blocks = (n + 3) / 4;
   for (int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; b < blocks;
@@ -83,6 +84,7 @@ __global__ void __launch_bounds__(256) uniform_kernel(float *__restrict__ out, i
 __global__ void __launch_bounds__(256) dropout_kernel(float *__restrict__ out, const float *__restrict__ x,
                                                       int64_t n, float rate, float keep, uint64_t seed,
                                                       uint64_t base) {
+  pdl_wait();
   const int64_t blocks = (n + 3) / 4;
   for (int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; b < blocks;
        b += (int64_t)gridDim.x * blockDim.x) {
@@ -113,10 +115,9 @@ extern "C" int fz_philox_uniform(float *out, int64_t n, uint64_t seed, uint64_t 
   FZ_REQUIRE(offset % 4 == 0, "fz_philox_uniform: offset must be a multiple of 4");
   FZ_REQUIRE(lo < hi, "fz_philox_uniform: need min < max");
   const int64_t blocks = (n + 3) / 4;
-  uniform_kernel<<<fz::grid_for(blocks, 256 * 4, 8), 256, 0, fz::resolve(stream)>>>(out, n, seed, offset / 4,
-                                                                                     lo, hi);
+  FZ_CUDA(fz::launch_pdl(uniform_kernel, dim3(fz::grid_for(blocks, 256 * 4, 8)), dim3(256), 0, fz::resolve(stream),
+                         out, n, seed, offset / 4, lo, hi));
   FZ_CHECK_LAUNCH();
-  fz::note_launch();
   return FZ_OK;
 }
 
@@ -129,9 +130,8 @@ extern "C" int fz_philox_dropout(float *out, const float *x, int64_t n, float ra
   FZ_REQUIRE(offset % 4 == 0, "fz_philox_dropout: offset must be a multiple of 4");
   FZ_REQUIRE(rate >= 0.0f && rate < 1.0f && keep > 0.0f, "fz_philox_dropout: rate must be in [0, 1)");
   const int64_t blocks = (n + 3) / 4;
-  dropout_kernel<<<fz::grid_for(blocks, 256 * 4, 8), 256, 0, fz::resolve(stream)>>>(out, x, n, rate, keep, seed,
-                                                                                     offset / 4);
+  FZ_CUDA(fz::launch_pdl(dropout_kernel, dim3(fz::grid_for(blocks, 256 * 4, 8)), dim3(256), 0, fz::resolve(stream),
+                         out, x, n, rate, keep, seed, offset / 4));
   FZ_CHECK_LAUNCH();
-  fz::note_launch();
   return FZ_OK;
 }

@@ -120,6 +120,7 @@ using namespace fz;
 
 namespace {
 __global__ void fill_kernel(float *__restrict__ dst, float v, int64_t n) {
+  pdl_wait();
   int64_t nv = n >> 2;
   float4 q = make_float4(v, v, v, v);
   int64_t stride = (int64_t)gridDim.x * blockDim.x;
@@ -130,6 +131,7 @@ __global__ void fill_kernel(float *__restrict__ dst, float v, int64_t n) {
 }
 
 __global__ void sub_inplace_kernel(float *__restrict__ x, const float *__restrict__ y, int64_t n) {
+  pdl_wait();
   int64_t nv = n >> 2;
   int64_t stride = (int64_t)gridDim.x * blockDim.x;
   int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -555,7 +557,7 @@ int fz_fill_f32(float *dst, float value, int64_t n, void *stream) {
   FZ_REQUIRE(dst, "fz_fill_f32: null pointer");
   FZ_REQUIRE(((uintptr_t)dst & 15) == 0, "fz_fill_f32: destination must be 16-byte aligned");
   unsigned grid = grid_for((n + 3) / 4, 256 * 4, 8);
-  fill_kernel<<<grid, 256, 0, resolve(stream)>>>(dst, value, n);
+  FZ_CUDA(fz::launch_pdl(fill_kernel, dim3(grid), dim3(256), 0, resolve(stream), dst, value, n));
   FZ_CHECK_LAUNCH();
   return FZ_OK;
 }
@@ -566,7 +568,7 @@ int fz_sub_inplace(float *x, const float *y, int64_t n, void *stream) {
   FZ_REQUIRE((((uintptr_t)x | (uintptr_t)y) & 15) == 0,
              "fz_sub_inplace: operands must be 16-byte aligned");
   unsigned grid = grid_for((n + 3) / 4, 256 * 2, 8);
-  sub_inplace_kernel<<<grid, 256, 0, resolve(stream)>>>(x, y, n);
+  FZ_CUDA(fz::launch_pdl(sub_inplace_kernel, dim3(grid), dim3(256), 0, resolve(stream), x, y, n));
   FZ_CHECK_LAUNCH();
   return FZ_OK;
 }

@@ -21,6 +21,7 @@ constexpr int kRows = 8;
 __global__ void __launch_bounds__(kTile *kRows) transpose_tiles(const float *__restrict__ in,
                                                                float *__restrict__ out, int64_t P,
                                                                int64_t Q, int64_t A, int64_t B) {
+  pdl_wait();
   __shared__ float tile[kTile][kTile + 1];
   const int64_t ta = (A + kTile - 1) / kTile, tb = (B + kTile - 1) / kTile;
   const int tx = threadIdx.x % kTile, ty = threadIdx.x / kTile;
@@ -81,6 +82,7 @@ template <typename IDX>
 __global__ void __launch_bounds__(256, 4) transpose64_kernel(const float *__restrict__ in,
                                                           float *__restrict__ out, int64_t P,
                                                           int64_t Q, int64_t A, int64_t B) {
+  pdl_wait();
   __shared__ float tile[kBig][kBig + 1];
   const IDX ta = (IDX)((A + kBig - 1) / kBig), tb = (IDX)((B + kBig - 1) / kBig);
   const IDX per_plane = ta * tb;
@@ -139,6 +141,7 @@ template <int V>
 __global__ void __launch_bounds__(256) transpose_runs(const float *__restrict__ in,
                                                      float *__restrict__ out, int64_t P, int64_t A,
                                                      int64_t Q, int64_t B, int64_t R) {
+  pdl_wait();
   const int64_t rv = R / V;
   const int64_t total = P * B * Q * A * rv;
   for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total;
@@ -197,20 +200,20 @@ extern "C" int fz_swapaxes(float *out, const float *in, const int64_t *shape, in
     // one wave of persistent CTAs (four fit on an SM at this kernel's register count)
     const unsigned grid = (unsigned)(tiles < (int64_t)fz::num_sms() * 4 ? tiles : fz::num_sms() * 4);
     if (tiles < ((int64_t)1 << 31) && P * Q < ((int64_t)1 << 31))
-      transpose64_kernel<uint32_t><<<grid, 256, 0, s>>>(in, out, P, Q, A, B);
+      FZ_CUDA(fz::launch_pdl(transpose64_kernel<uint32_t>, dim3(grid), dim3(256), 0, s, in, out, P, Q, A, B));
     else
-      transpose64_kernel<int64_t><<<grid, 256, 0, s>>>(in, out, P, Q, A, B);
+      FZ_CUDA(fz::launch_pdl(transpose64_kernel<int64_t>, dim3(grid), dim3(256), 0, s, in, out, P, Q, A, B));
   } else if (R == 1) {
     const int64_t ta = (A + kTile - 1) / kTile, tb = (B + kTile - 1) / kTile;
     dim3 grid((unsigned)(tb < 0x7fffffff ? tb : 0x7fffffff), (unsigned)(ta < 65535 ? ta : 65535),
               (unsigned)(P * Q < 65535 ? P * Q : 65535));
-    transpose_tiles<<<grid, kTile * kRows, 0, s>>>(in, out, P, Q, A, B);
+    FZ_CUDA(fz::launch_pdl(transpose_tiles, grid, dim3(kTile * kRows), 0, s, in, out, P, Q, A, B));
   } else {
     bool v4 = R % 4 == 0 && (((uintptr_t)in | (uintptr_t)out) & 15) == 0;
     int64_t items = total / (v4 ? 4 : 1);
     unsigned grid = fz::grid_for(items, 256, 8, 4);
-    if (v4) transpose_runs<4><<<grid, 256, 0, s>>>(in, out, P, A, Q, B, R);
-    else transpose_runs<1><<<grid, 256, 0, s>>>(in, out, P, A, Q, B, R);
+    if (v4) FZ_CUDA(fz::launch_pdl(transpose_runs<4>, dim3(grid), dim3(256), 0, s, in, out, P, A, Q, B, R));
+    else FZ_CUDA(fz::launch_pdl(transpose_runs<1>, dim3(grid), dim3(256), 0, s, in, out, P, A, Q, B, R));
   }
   FZ_CHECK_LAUNCH();
   return FZ_OK;
