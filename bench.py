@@ -54,7 +54,7 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--kernel", default=None,
                     help="run one hot-path kernel on a profiling-sized case instead of the step "
-                         "(step, gemm, gemm_wgrad, tf32_lo, add, bcast_add, exp, log, sqrt, sum_ax0, "
+                         "(step, gemm, gemm_full, gemm_wgrad, tf32_lo, add, bcast_add, exp, log, sqrt, sum_ax0, "
                          "sum_ax1, max_ax0, sum_rows64, swapaxes, bias_relu, linear_relu, gemm_epi_fwd, "
                          "gemm_epi_bwd)")
     ap.add_argument("--reps", type=int, default=3)
@@ -477,7 +477,9 @@ def run_ours(args):
     d.barrier()
     F.synchronize()
     launches0 = L.fz_launch_count()
-    capi.check(L.fz_gemm_timing(1))  # event pairs around each GEMM launch (roofline)
+    roofline_timing = d.world == 1 and d.rank == 0
+    if roofline_timing:  # event pairs around each GEMM launch (the N=1 line's roofline)
+        capi.check(L.fz_gemm_timing(1))
     timer.start()
     for _ in range(args.steps):
         loss = model.step(X, Y, LR, comm)
@@ -486,7 +488,7 @@ def run_ours(args):
     if comm:
         comm.wait(120.0)
     launches = L.fz_launch_count() - launches0
-    gemm_recs = capi.gemm_timing_read()
+    gemm_recs = capi.gemm_timing_read() if roofline_timing else []
     capi.check(L.fz_gemm_timing(0))
     d.barrier()
     ms = d.max(ms_local) / args.steps
@@ -627,11 +629,13 @@ def run_kernel(args):
     F.set_device(0)
     A, L = capi, capi.lib()
     k = args.kernel
-    if k in ("gemm", "gemm_wgrad"):
+    if k in ("gemm", "gemm_full", "gemm_wgrad"):
         # gemm: the MLP's dominant forward shape x @ W^T at 1/8 of the batch (both operands
-        # K-major); gemm_wgrad: the weight gradient x^T @ g at 1/4 of the batch (both
-        # MN-major). Remainder planes split beforehand: the loop is the GEMM kernel alone.
-        m, n, kk, tA, tB = (8192, 4096, 4096, 0, 1) if k == "gemm" else (4096, 4096, 16384, 1, 0)
+        # K-major); gemm_full: the same at the full 65536 rows (the roofline's product);
+        # gemm_wgrad: the weight gradient x^T @ g at 1/4 of the batch (both MN-major).
+        # Remainder planes split beforehand: the loop is the GEMM kernel alone.
+        m, n, kk, tA, tB = {"gemm": (8192, 4096, 4096, 0, 1), "gemm_full": (65536, 4096, 4096, 0, 1),
+                            "gemm_wgrad": (4096, 4096, 16384, 1, 0)}[k]
         ash, bsh = ((kk, m) if tA else (m, kk)), ((n, kk) if tB else (kk, n))
         x, w, c = _random_device(A, ash, 1), _random_device(A, bsh, 2), A.DeviceArray((m, n))
         xl, wl = A.DeviceArray(ash), A.DeviceArray(bsh)
