@@ -568,7 +568,7 @@ def run_reference(args):
     A step at 65536 rows costs minutes on the host (serial transposes of 1 GiB
     activations dominate), and the first one about twice the next (the reference's
     pool allocator grows), so: one full-size warm-up step, then full-size timed steps
-    until `--steps` are done or REFERENCE_BUDGET_S has passed (at least one);
+    until `--steps` are done or the next would end after REFERENCE_BUDGET_S (at least one);
     `steps` reports the steps timed and `steps_requested` the flag."""
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
@@ -598,7 +598,8 @@ def run_reference(args):
     while done < args.steps:
         Ws, bs, _ = R.mlp_step(X, Y, Ws, bs, LR)
         done += 1
-        if time.perf_counter() - t0 > REFERENCE_BUDGET_S:
+        spent = time.perf_counter() - t0
+        if spent + spent / done > REFERENCE_BUDGET_S:  # the next step would overrun
             break
     dt = (time.perf_counter() - t0) / done
     v = round(rows / dt, 2)
