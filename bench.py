@@ -54,7 +54,7 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--kernel", default=None,
                     help="run one hot-path kernel on a profiling-sized case instead of the step "
-                         "(step, gemm, gemm_full, gemm_wgrad, tf32_lo, add, bcast_add, exp, log, sqrt, sum_ax0, "
+                         "(step, gemm, gemm_full, gemm_wgrad, gemm_16384q, tf32_lo, add, bcast_add, exp, log, sqrt, sum_ax0, "
                          "sum_ax1, max_ax0, sum_rows64, swapaxes, bias_relu, linear_relu, gemm_epi_fwd, "
                          "gemm_epi_bwd)")
     ap.add_argument("--reps", type=int, default=3)
@@ -630,13 +630,16 @@ def run_kernel(args):
     F.set_device(0)
     A, L = capi, capi.lib()
     k = args.kernel
-    if k in ("gemm", "gemm_full", "gemm_wgrad"):
+    if k in ("gemm", "gemm_full", "gemm_wgrad", "gemm_16384q"):
         # gemm: the MLP's dominant forward shape x @ W^T at 1/8 of the batch (both operands
         # K-major); gemm_full: the same at the full 65536 rows (the roofline's product);
         # gemm_wgrad: the weight gradient x^T @ g at 1/4 of the batch (both MN-major).
         # Remainder planes split beforehand: the loop is the GEMM kernel alone.
+        # gemm_16384q: the 16384^3 sweep product at a quarter of its rows (A [4096,16384],
+        # B [16384,16384] read MN-major as in the sweep).
         m, n, kk, tA, tB = {"gemm": (8192, 4096, 4096, 0, 1), "gemm_full": (65536, 4096, 4096, 0, 1),
-                            "gemm_wgrad": (4096, 4096, 16384, 1, 0)}[k]
+                            "gemm_wgrad": (4096, 4096, 16384, 1, 0),
+                            "gemm_16384q": (4096, 16384, 16384, 0, 0)}[k]
         ash, bsh = ((kk, m) if tA else (m, kk)), ((n, kk) if tB else (kk, n))
         x, w, c = _random_device(A, ash, 1), _random_device(A, bsh, 2), A.DeviceArray((m, n))
         xl, wl = A.DeviceArray(ash), A.DeviceArray(bsh)
