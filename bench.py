@@ -225,10 +225,12 @@ def kernel_suite(capi, pk):
     for op in ("add", "mul", "div"):
         rec(f"{op}_2^28", time_launch(A, lambda: A.check(L.fz_ewise_binary_contig(
             A.BINOPS[op], n, o.ptr, a.ptr, b.ptr, None))), 12 * n)
-    for e in (25, 26, 27):  # smaller sizes of the sweep (three operands still exceed L2)
+    for e in (20, 22, 24, 25, 26, 27):  # the sweep's smaller sizes
         k = 1 << e
         rec(f"add_2^{e}", time_launch(A, lambda: A.check(L.fz_ewise_binary_contig(
             0, k, o.ptr, a.ptr, b.ptr, None))), 12 * k)
+        if 12 * k <= 126 << 20:  # the three operands fit the 126 MB L2: an L2 rate, not HBM
+            out[f"add_2^{e}"]["l2_resident"] = True
     plan = A.make_plan((n,), [(n,), (n,)])
     for op in ("exp", "log", "sqrt"):
         rec(f"{op}_2^28", time_launch(A, lambda: A.check(L.fz_ewise_unary(
@@ -239,8 +241,9 @@ def kernel_suite(capi, pk):
         0, C.byref(bplan), o.ptr, a.ptr, b.ptr, None))), 8 * r * r + 4 * r)
     s = 8192
     for name, (outer, ln, inner) in (("sum_ax1_8192^2", (s, s, 1)), ("sum_ax0_8192^2", (1, s, s)),
-                                     ("max_ax0_8192^2", (1, s, s))):
-        op = 2 if name.startswith("max") else 0
+                                     ("mean_ax1_8192^2", (s, s, 1)), ("mean_ax0_8192^2", (1, s, s)),
+                                     ("max_ax1_8192^2", (s, s, 1)), ("max_ax0_8192^2", (1, s, s))):
+        op = 2 if name.startswith("max") else 1 if name.startswith("mean") else 0
         rec(name, time_launch(A, lambda: A.check(L.fz_reduce(op, o.ptr, a.ptr, outer, ln, inner, None))),
             4 * s * s + 4 * (outer * inner))
     # [64,256,64,64] over (0,2,3), keepdims: the reference reduces one axis per call
