@@ -32,10 +32,10 @@
 // are rounded to nearest rather than truncated by the MMA. Double-buffered chunks let
 // the MMAs run on while a chunk is promoted.
 //
-// Every mbarrier wait is bounded by a %globaltimer deadline; on expiry the kernel
-// records an error code in the device's error word (read by fz_kernel_status),
-// drains its own TMA loads (bounded), frees TMEM and returns, so a bad launch
-// surfaces as an error instead of a hang.
+// Every mbarrier wait is bounded by a %globaltimer deadline (4 s); on expiry the kernel
+// records an error code in the device's error word (read by fz_kernel_status), lets
+// the MMAs and TMA loads it already issued complete (bounded), frees TMEM and
+// returns, so a bad launch surfaces as an error instead of a hang.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 

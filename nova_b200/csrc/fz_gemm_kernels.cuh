@@ -127,6 +127,13 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volati
   }
 }
 
+// Wait for a phase without the abort shortcut (draining work already issued), bounded.
+__device__ __forceinline__ void mbar_drain(uint64_t *bar, uint32_t parity) {
+  const uint64_t t0 = globaltimer();
+  while (!mbar_try_wait(bar, parity) && globaltimer() - t0 < kWaitNs) {
+  }
+}
+
 __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, uint64_t *bar,
                                             int c0, int c1, int c2) {
   asm volatile(
@@ -667,6 +674,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   __shared__ __align__(8) uint64_t empty_bar[STAGES];
   __shared__ __align__(8) uint64_t acc_full[2];
   __shared__ __align__(8) uint64_t acc_empty[2];
+  __shared__ __align__(8) uint64_t drain_bar;  // MMAs issued before an abort, completed
   __shared__ uint32_t tmem_base_slot;
   __shared__ volatile int abort_flag;
 
@@ -682,6 +690,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       mbar_init(&acc_full[b], 1);
       mbar_init(&acc_empty[b], NUM_EPI_WARPS);  // one arrival per epilogue warp
     }
+    mbar_init(&drain_bar, 1);
     abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     prefetch_map(&mapAh);
@@ -743,12 +752,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           atomicCAS(args.err, kErrNone, kErrTimeoutEmpty);
           abort_flag = 1;
           // drain: wait (bounded) for the loads of the last STAGES issued k-tiles
-          for (int i = (it > STAGES ? it - STAGES : 0); i < it; ++i) {
-            const int s = i % STAGES;
-            const uint64_t t0 = globaltimer();
-            while (!mbar_try_wait(&full_bar[s], (i / STAGES) & 1) && globaltimer() - t0 < kWaitNs) {
-            }
-          }
+          for (int i = (it > STAGES ? it - STAGES : 0); i < it; ++i)
+            mbar_drain(&full_bar[i % STAGES], (i / STAGES) & 1);
         }
       }
     } else if (warp == 1) {
@@ -795,6 +800,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (!ok) {
           atomicCAS(args.err, kErrNone, kErrTimeoutFull);
           abort_flag = 1;
+          // the MMAs already issued complete before TMEM is freed (bounded)
+          umma_commit(&drain_bar);
+          mbar_drain(&drain_bar, 0);
         }
       }
     }
@@ -940,6 +948,15 @@ __device__ __forceinline__ void umma_commit_pair(uint64_t *bar) {
       : "memory");
 }
 
+// Arrive on the leader's barrier at this offset when the MMAs issued so far have completed.
+__device__ __forceinline__ void umma_commit_leader(uint64_t *bar) {
+  asm volatile(
+      "{\n\t.reg .b16 m;\n\tmov.b16 m, 1;\n\t"
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], m;\n\t}" ::"r"(smem_u32(bar))
+      : "memory");
+}
+
 __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
                : "memory");
@@ -960,6 +977,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   __shared__ __align__(8) uint64_t empty_bar[PAIR_STAGES];
   __shared__ __align__(8) uint64_t acc_full[2];
   __shared__ __align__(8) uint64_t acc_empty[2];
+  __shared__ __align__(8) uint64_t drain_bar;  // MMAs issued before an abort, completed
   __shared__ uint32_t tmem_base_slot;
   __shared__ volatile int abort_flag;
 
@@ -978,6 +996,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       mbar_init(&acc_full[b], 1);
       mbar_init(&acc_empty[b], 2 * NUM_EPI_WARPS);  // one arrival per epilogue warp of both CTAs
     }
+    mbar_init(&drain_bar, 1);
     abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     prefetch_map(&mapAh);
@@ -1036,12 +1055,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
           atomicCAS(args.err, kErrNone, kErrTimeoutEmpty);
           abort_flag = 1;
           if (leader) {  // drain (bounded): the last PAIR_STAGES k-tiles' loads of the pair
-            for (int i = (it > PAIR_STAGES ? it - PAIR_STAGES : 0); i < it; ++i) {
-              const int s = i % PAIR_STAGES;
-              const uint64_t t0 = globaltimer();
-              while (!mbar_try_wait(&full_bar[s], (i / PAIR_STAGES) & 1) && globaltimer() - t0 < kWaitNs) {
-              }
-            }
+            for (int i = (it > PAIR_STAGES ? it - PAIR_STAGES : 0); i < it; ++i)
+              mbar_drain(&full_bar[i % PAIR_STAGES], (i / PAIR_STAGES) & 1);
           }
         }
       }
@@ -1089,6 +1104,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         if (!ok) {
           atomicCAS(args.err, kErrNone, kErrTimeoutFull);
           abort_flag = 1;
+          // the MMAs already issued (writing both CTAs' TMEM) complete before the pair
+          // meets to free TMEM (bounded)
+          umma_commit_leader(&drain_bar);
+          mbar_drain(&drain_bar, 0);
         }
       }
     }
