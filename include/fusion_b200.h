@@ -331,6 +331,18 @@ int fz_gemm_set_tiles(int mode);
  * off, by per-thread stores. Results are identical either way. Replaces no reference
  * interface (the reference's cblas_sgemm writes C directly). */
 int fz_gemm_set_tma_stores(int on);
+/* Where the TF32 remainder planes that a GEMM call is not given come from, for the calls
+ * that follow (process-wide): FZ_GEMM_SPLIT_PASS and FZ_GEMM_SPLIT_AUTO (default), a
+ * separate pass writes each into a workspace before the GEMM; FZ_GEMM_SPLIT_IN_KERNEL,
+ * the GEMM kernel derives them in shared memory from the raw operand tiles and needs no
+ * workspace (full-width tiles, plain output, operands TMA can address; other calls use
+ * the pass). The in-kernel split is slower on B200 (1.2x for small products, about 2.5x
+ * for large ones), hence not the default. Results are identical bit for bit. Replaces
+ * no reference interface. fz_gemm_split_launches: how many launches so far derived
+ * them in shared memory. */
+enum fz_gemm_split { FZ_GEMM_SPLIT_AUTO = 0, FZ_GEMM_SPLIT_PASS = 1, FZ_GEMM_SPLIT_IN_KERNEL = 2 };
+int fz_gemm_set_split(int mode);
+int fz_gemm_split_launches(int64_t *count);
 /* Launches of the GEMM kernels so far in this process, by schedule: counts[0] CTA-pair
  * launches, [1] single-CTA launches, [2] launches split over K, [3] launches with a
  * fused epilogue program. Instrumentation for tests and measurement; replaces no

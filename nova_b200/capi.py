@@ -115,6 +115,8 @@ def lib() -> C.CDLL:
         L.fz_tf32_lo.argtypes = [vp, vp, i64, vp]
         L.fz_gemm_set_tiles.argtypes = [C.c_int]
         L.fz_gemm_set_tma_stores.argtypes = [C.c_int]
+        L.fz_gemm_set_split.argtypes = [C.c_int]
+        L.fz_gemm_split_launches.argtypes = [C.POINTER(C.c_int64)]
         L.fz_gemm_f32_epilogue.argtypes = [i64, i64, i64, i64, vp, vp, i64, i64, C.c_int, vp, vp,
                                            i64, i64, C.c_int, C.POINTER(Program),
                                            C.POINTER(EpiInput), C.POINTER(C.c_void_p), i64, i64, vp]

@@ -193,6 +193,7 @@ int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
 // Launch counters by schedule (fz_gemm_stats): CTA-pair launches, single-CTA launches,
 // launches split over K, launches with a fused epilogue program compiled in.
 std::atomic<int64_t> g_stat_pair{0}, g_stat_single{0}, g_stat_ksplit{0}, g_stat_epilogue{0};
+std::atomic<int64_t> g_stat_split_here{0};  // launches deriving remainder tiles in shared memory
 
 // Per-launch device timing of the main GEMM kernel (fz_gemm_timing): an event pair
 // recorded around the launch on its stream. Events are pooled and reused.
@@ -244,6 +245,14 @@ struct LaunchTimer {
 };
 
 std::atomic<int> g_tile_mode{FZ_GEMM_TILES_AUTO};
+// Where missing remainder planes come from (fz_gemm_set_split). AUTO takes the separate
+// pass: deriving them in shared memory (the SPLIT kernels) measured slower on every
+// product of the sweep, 1.2x for 1024^3 and batched 64x512^3 and 2.4-2.7x for large
+// products, with the remainders of a k-tile (4096 per SM per k-tile, about ten
+// instructions each) more than the two splitter warps issue in the ~860 cycles the
+// MMAs spend on it. The SPLIT kernels need no workspace, which callers short of memory
+// can choose them for.
+std::atomic<int> g_split_mode{FZ_GEMM_SPLIT_AUTO};
 // Epilogue outputs through TMA bulk tensor stores where the layout allows (default);
 // off: every output stored per thread (fz_gemm_set_tma_stores).
 std::atomic<bool> g_tma_stores{true};
@@ -369,7 +378,7 @@ int check_kernel_registers(const void *fn) {
   return FZ_OK;
 }
 
-template <bool A_MN, bool B_MN, int TBN>
+template <bool A_MN, bool B_MN, int TBN, bool SPLIT = false>
 int launch_gemm(const CUtensorMap &mAh, const CUtensorMap &mAl, const CUtensorMap &mBh,
                 const CUtensorMap &mBl, const GemmArgs &ga, const EpiParams &ep, unsigned grid,
                 bool pair, cudaStream_t s) {
@@ -378,27 +387,34 @@ int launch_gemm(const CUtensorMap &mAh, const CUtensorMap &mAl, const CUtensorMa
   cudaGetDevice(&dev);
   const size_t smem = smem_bytes(pair, TBN);
   if (dev >= 64 || !attr_done[pair][dev]) {
-    const void *fn = pair ? (const void *)gemm_pair_kernel<A_MN, B_MN, StoreEpi>
-                          : (const void *)gemm_3xtf32_kernel<A_MN, B_MN, TBN, StoreEpi>;
+    const void *fn = pair ? (const void *)gemm_pair_kernel<A_MN, B_MN, StoreEpi, SPLIT>
+                          : (const void *)gemm_3xtf32_kernel<A_MN, B_MN, TBN, StoreEpi, SPLIT>;
     int rc = check_kernel_registers(fn);
     if (rc) return rc;
     cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (dev < 64) attr_done[pair][dev] = true;
   }
   if (pair)
-    FZ_CUDA(fz::launch_pdl(gemm_pair_kernel<A_MN, B_MN, StoreEpi>, dim3(2 * grid), dim3(NUM_THREADS), smem, s, mAh, mAl, mBh, mBl, ga, ep));
+    FZ_CUDA(fz::launch_pdl(gemm_pair_kernel<A_MN, B_MN, StoreEpi, SPLIT>, dim3(2 * grid), dim3(NUM_THREADS), smem, s, mAh, mAl, mBh, mBl, ga, ep));
   else
-    FZ_CUDA(fz::launch_pdl(gemm_3xtf32_kernel<A_MN, B_MN, TBN, StoreEpi>, dim3(grid), dim3(NUM_THREADS), smem, s, mAh, mAl, mBh, mBl, ga, ep));
+    FZ_CUDA(fz::launch_pdl(gemm_3xtf32_kernel<A_MN, B_MN, TBN, StoreEpi, SPLIT>, dim3(grid), dim3(NUM_THREADS), smem, s, mAh, mAl, mBh, mBl, ga, ep));
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fz::cuda_fail(e, "gemm_3xtf32_kernel launch", __FILE__, __LINE__);
   fz::note_launch();
   return FZ_OK;
 }
 
-// Kernel for the operand layouts and tile width (narrow tiles read B K-major).
+// Kernel for the operand layouts and tile width (narrow tiles read B K-major); `split`:
+// the variant that derives the remainder tiles in shared memory (full-width tiles).
 int dispatch_gemm(bool a_mn, bool b_mn, int tbn, const CUtensorMap &mAh, const CUtensorMap &mAl,
                   const CUtensorMap &mBh, const CUtensorMap &mBl, const GemmArgs &ga,
-                  const EpiParams &ep, unsigned grid, bool pair, cudaStream_t s) {
+                  const EpiParams &ep, unsigned grid, bool pair, bool split, cudaStream_t s) {
+  if (split) {
+    if (!a_mn && !b_mn) return launch_gemm<false, false, BN, true>(mAh, mAl, mBh, mBl, ga, ep, grid, pair, s);
+    if (!a_mn && b_mn) return launch_gemm<false, true, BN, true>(mAh, mAl, mBh, mBl, ga, ep, grid, pair, s);
+    if (a_mn && !b_mn) return launch_gemm<true, false, BN, true>(mAh, mAl, mBh, mBl, ga, ep, grid, pair, s);
+    return launch_gemm<true, true, BN, true>(mAh, mAl, mBh, mBl, ga, ep, grid, pair, s);
+  }
   if (tbn == 16)
     return a_mn ? launch_gemm<true, false, 16>(mAh, mAl, mBh, mBl, ga, ep, grid, false, s)
                 : launch_gemm<false, false, 16>(mAh, mAl, mBh, mBl, ga, ep, grid, false, s);
@@ -963,18 +979,34 @@ int gemm_impl(int64_t batch, int64_t M, int64_t N, int64_t K, const float *A, co
   // (transB != 0, K-major) or [K, N] (MN-major).
   Operand oa{transA != 0, transA ? K : M, transA ? M : K};
   Operand ob{transB == 0, transB ? N : K, transB ? K : N};
-  const int64_t a_need = workspace_floats(oa, A, lda, strideA, A_lo, batch);
-  const int64_t b_need = workspace_floats(ob, B, ldb, strideB, B_lo, batch);
+  // Remainder planes the caller did not supply: written by a separate pass, or, when
+  // asked for (FZ_GEMM_SPLIT_IN_KERNEL), derived in shared memory by the kernel (full-
+  // width tiles, plain output, operands TMA can address as they are; a supplied plane
+  // is then not read, the values being the same)
+  const bool split_here = g_split_mode.load(std::memory_order_relaxed) == FZ_GEMM_SPLIT_IN_KERNEL && !E.pg &&
+                          tbn == BN && (!A_lo || !B_lo) && direct_hi(A, lda, strideA, batch) &&
+                          direct_hi(B, ldb, strideB, batch);
   float *ws = nullptr;
-  if (a_need + b_need) {
-    rc = fz_malloc((void **)&ws, sizeof(float) * (a_need + b_need), s);
-    if (rc) {
-      fz_free(bt, s);
-      return rc;
+  if (split_here) {
+    for (Operand *op : {&oa, &ob}) {
+      const bool is_a = op == &oa;
+      op->hi = op->lo = is_a ? A : B;
+      op->hi_ld = op->lo_ld = is_a ? lda : ldb;
+      op->hi_sb = op->lo_sb = batch == 1 ? op->hi_ld * op->rows : (is_a ? strideA : strideB);
     }
+  } else {
+    const int64_t a_need = workspace_floats(oa, A, lda, strideA, A_lo, batch);
+    const int64_t b_need = workspace_floats(ob, B, ldb, strideB, B_lo, batch);
+    if (a_need + b_need) {
+      rc = fz_malloc((void **)&ws, sizeof(float) * (a_need + b_need), s);
+      if (rc) {
+        fz_free(bt, s);
+        return rc;
+      }
+    }
+    rc = prepare(A, lda, strideA, A_lo, batch, ws, &oa, s);
+    if (!rc) rc = prepare(B, ldb, strideB, B_lo, batch, ws + a_need, &ob, s);
   }
-  rc = prepare(A, lda, strideA, A_lo, batch, ws, &oa, s);
-  if (!rc) rc = prepare(B, ldb, strideB, B_lo, batch, ws + a_need, &ob, s);
 
   const int tile_m = pair ? 2 * BM : BM, box_b = pair ? BM : tbn;
   const int64_t workers = pair ? fz::num_sms() / 2 : fz::num_sms();
@@ -1039,6 +1071,7 @@ int gemm_impl(int64_t batch, int64_t M, int64_t N, int64_t K, const float *A, co
     (pair ? g_stat_pair : g_stat_single).fetch_add(1, std::memory_order_relaxed);
     if (real_splits > 1) g_stat_ksplit.fetch_add(1, std::memory_order_relaxed);
     if (in_kernel) g_stat_epilogue.fetch_add(1, std::memory_order_relaxed);
+    if (split_here) g_stat_split_here.fetch_add(1, std::memory_order_relaxed);
     LaunchTimer timer(batch, M, N, K, pair, in_kernel, real_splits, s);
     // outputs stored by TMA when every output's layout allows it
     if (in_kernel) {
@@ -1056,7 +1089,7 @@ int gemm_impl(int64_t batch, int64_t M, int64_t N, int64_t K, const float *A, co
                                                        M * N, sbw)
                                         : (batch == 1 || strideC % 4 == 0) &&
                                               make_out_map(&ep.omap[0], C, N, M, batch, ldc, strideC, sbw));
-      rc = dispatch_gemm(oa.mn, ob.mn, tbn, mAh, mAl, mBh, mBl, ga, ep, grid, pair, s);
+      rc = dispatch_gemm(oa.mn, ob.mn, tbn, mAh, mAl, mBh, mBl, ga, ep, grid, pair, split_here, s);
     }
     timer.done(rc);
     // K-split partials: summed over the splits in a fixed order (deterministic)
@@ -1144,6 +1177,19 @@ extern "C" int fz_gemm_set_tiles(int mode) {
   FZ_REQUIRE(mode == FZ_GEMM_TILES_AUTO || mode == FZ_GEMM_TILES_SINGLE || mode == FZ_GEMM_TILES_PAIR,
              "fz_gemm_set_tiles: unknown mode " + std::to_string(mode));
   g_tile_mode.store(mode, std::memory_order_relaxed);
+  return FZ_OK;
+}
+
+extern "C" int fz_gemm_set_split(int mode) {
+  FZ_REQUIRE(mode == FZ_GEMM_SPLIT_AUTO || mode == FZ_GEMM_SPLIT_PASS || mode == FZ_GEMM_SPLIT_IN_KERNEL,
+             "fz_gemm_set_split: unknown mode");
+  g_split_mode.store(mode);
+  return FZ_OK;
+}
+
+extern "C" int fz_gemm_split_launches(int64_t *count) {
+  FZ_REQUIRE(count, "fz_gemm_split_launches: null pointer");
+  *count = g_stat_split_here.load();
   return FZ_OK;
 }
 

@@ -79,7 +79,11 @@ static_assert(128 * REG_CTRL + 32 * NUM_EPI_WARPS * REG_EPI == NUM_THREADS * REG
 static_assert(NUM_EPI_WARPS == 8 && EPI_WARP0 == 4, "two epilogue warpgroups after warpgroup 0");
 constexpr unsigned long long kWaitNs = 4000000000ull;  // 4 s per wait
 
-enum : int { kErrNone = 0, kErrTimeoutFull = 1, kErrTimeoutEmpty = 2, kErrTimeoutAcc = 3 };
+enum : int { kErrNone = 0, kErrTimeoutFull = 1, kErrTimeoutEmpty = 2, kErrTimeoutAcc = 3, kErrTimeoutSplit = 4 };
+// Kernels instantiated with SPLIT derive the remainder tiles in shared memory: the TMA
+// producer loads the raw operand tiles only and warps 2-3 (otherwise idle) write each
+// k-tile's remainder tiles beside them before the MMA issuer may use the stage.
+constexpr int NUM_SPLIT_WARPS = 2;
 
 
 // ---------------------------------------------------------------- PTX helpers
@@ -122,6 +126,30 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volati
   const uint64_t t0 = globaltimer();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (globaltimer() - t0 > kWaitNs) return false;
+  }
+}
+
+// mbar_wait with cluster-scope acquire: for a barrier that threads of the other CTA of
+// a pair release (their shared-memory writes must be visible to this CTA's MMAs).
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.b32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t *bar, uint32_t parity, volatile int *abort_flag) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  while (true) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
     if (*abort_flag) return false;
     if (globaltimer() - t0 > kWaitNs) return false;
   }
@@ -570,6 +598,53 @@ __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// The TF32 remainder of x, the arithmetic of the remainder pass (lo_kernel): x minus x
+// with its 13 low mantissa bits cleared (exact), rounded to the nearest TF32 value,
+// ties to even; an Inf or NaN difference passes through. An operand split here
+// therefore multiplies bit for bit as one whose remainder plane was written there.
+__device__ __forceinline__ float tf32_remainder(float a) {
+  uint32_t u = __float_as_uint(__fsub_rn(a, __uint_as_float(__float_as_uint(a) & 0xffffe000u)));
+  if ((u & 0x7f800000u) != 0x7f800000u) u = (u + 0xfffu + ((u >> 13) & 1u)) & 0xffffe000u;
+  return __uint_as_float(u);
+}
+
+__device__ __forceinline__ float4 lds_f4(uint32_t a) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(a)
+               : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void sts_f4(uint32_t a, float4 v) {
+  asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(a), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
+               : "memory");
+}
+
+// Remainder tile of a raw operand tile in shared memory, element for element at the
+// same offsets (TMA would have written the remainder plane in the same swizzled
+// layout), by the 64 splitter threads (index t): N4 float4s, N4 / 64 per thread, a
+// warp's 32 consecutive float4s per access, 8 loads in flight.
+template <int N4>
+__device__ __forceinline__ void split_tile(const uint8_t *hi, uint8_t *lo, int t) {
+  static_assert(N4 % 64 == 0, "whole rounds of float4s per thread");
+  constexpr int PER = N4 / 64, BATCH = PER < 8 ? PER : 8;
+  static_assert(PER % BATCH == 0, "whole batches");
+  const uint32_t h = smem_u32(hi), l = smem_u32(lo);
+#pragma unroll
+  for (int j0 = 0; j0 < PER; j0 += BATCH) {
+    float4 v[BATCH];
+#pragma unroll
+    for (int j = 0; j < BATCH; ++j) v[j] = lds_f4(h + (uint32_t)(((j0 + j) * 64 + t) * 16));
+#pragma unroll
+    for (int j = 0; j < BATCH; ++j)
+      sts_f4(l + (uint32_t)(((j0 + j) * 64 + t) * 16),
+             make_float4(tf32_remainder(v[j].x), tf32_remainder(v[j].y), tf32_remainder(v[j].z),
+                         tf32_remainder(v[j].w)));
+  }
+}
+
 // Work unit t -> (K split, batch, m block, n block). Units of one K split are
 // consecutive; within a batch, bands of group_m row blocks are walked column by
 // column, so the units in flight on the 148 SMs share A rows and B columns in L2.
@@ -652,7 +727,7 @@ __device__ __forceinline__ void promote_cols(uint32_t taddr, float (&acc)[CPW]) 
 
 // A_MN / B_MN: the operand is MN-major in global and shared memory (B is K-major
 // whenever TBN < 256).
-template <bool A_MN, bool B_MN, int TBN, class EPI>
+template <bool A_MN, bool B_MN, int TBN, class EPI, bool SPLIT = false>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap mapAh,
                        const __grid_constant__ CUtensorMap mapAl,
@@ -670,8 +745,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   constexpr int TMEM_COLS = T::TMEM;
   constexpr int CPW = T::CPW;
   static_assert(TBN == BN || !B_MN, "narrow tiles read B K-major");
-  __shared__ __align__(8) uint64_t full_bar[STAGES];
+  static_assert(!SPLIT || TBN == BN, "remainder tiles in shared memory: full-width tiles only");
+  __shared__ __align__(8) uint64_t full_bar[STAGES];   // stage ready for the MMAs
   __shared__ __align__(8) uint64_t empty_bar[STAGES];
+  __shared__ __align__(8) uint64_t raw_full[SPLIT ? STAGES : 1];  // SPLIT: raw tiles landed
   __shared__ __align__(8) uint64_t acc_full[2];
   __shared__ __align__(8) uint64_t acc_empty[2];
   __shared__ __align__(8) uint64_t drain_bar;  // MMAs issued before an abort, completed
@@ -683,8 +760,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&full_bar[s], 1);
+      mbar_init(&full_bar[s], SPLIT ? NUM_SPLIT_WARPS : 1);
       mbar_init(&empty_bar[s], 1);
+      if constexpr (SPLIT) mbar_init(&raw_full[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
@@ -740,12 +818,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
               ok = false;
               break;
             }
-            mbar_expect_tx(&full_bar[s], STAGE_BYTES);
             const int k0 = kb + kt * BK;
-            load_operand<A_MN, BM>(stage_ptr(s, 0), &mapAh, &full_bar[s], k0, mb * BM, bz, args.wide & 1);
-            load_operand<A_MN, BM>(stage_ptr(s, 1), &mapAl, &full_bar[s], k0, mb * BM, bz, args.wide & 2);
-            load_operand<B_MN, TBN>(stage_ptr(s, 2), &mapBh, &full_bar[s], k0, nb * TBN, bz, args.wide & 4);
-            load_operand<B_MN, TBN>(stage_ptr(s, 3), &mapBl, &full_bar[s], k0, nb * TBN, bz, args.wide & 8);
+            if constexpr (SPLIT) {  // the raw tiles only; the splitter warps add the remainders
+              mbar_expect_tx(&raw_full[s], TILE_A_BYTES + TILE_B_BYTES);
+              load_operand<A_MN, BM>(stage_ptr(s, 0), &mapAh, &raw_full[s], k0, mb * BM, bz, args.wide & 1);
+              load_operand<B_MN, TBN>(stage_ptr(s, 2), &mapBh, &raw_full[s], k0, nb * TBN, bz, args.wide & 4);
+            } else {
+              mbar_expect_tx(&full_bar[s], STAGE_BYTES);
+              load_operand<A_MN, BM>(stage_ptr(s, 0), &mapAh, &full_bar[s], k0, mb * BM, bz, args.wide & 1);
+              load_operand<A_MN, BM>(stage_ptr(s, 1), &mapAl, &full_bar[s], k0, mb * BM, bz, args.wide & 2);
+              load_operand<B_MN, TBN>(stage_ptr(s, 2), &mapBh, &full_bar[s], k0, nb * TBN, bz, args.wide & 4);
+              load_operand<B_MN, TBN>(stage_ptr(s, 3), &mapBl, &full_bar[s], k0, nb * TBN, bz, args.wide & 8);
+            }
           }
         }
         if (!ok) {
@@ -753,7 +837,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           abort_flag = 1;
           // drain: wait (bounded) for the loads of the last STAGES issued k-tiles
           for (int i = (it > STAGES ? it - STAGES : 0); i < it; ++i)
-            mbar_drain(&full_bar[i % STAGES], (i / STAGES) & 1);
+            mbar_drain(SPLIT ? &raw_full[i % STAGES] : &full_bar[i % STAGES], (i / STAGES) & 1);
         }
       }
     } else if (warp == 1) {
@@ -804,6 +888,35 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           umma_commit(&drain_bar);
           mbar_drain(&drain_bar, 0);
         }
+      }
+    } else if constexpr (SPLIT) {
+      // ------------------------------------------------------ remainder tiles (warps 2-3)
+      const int t64 = (int)threadIdx.x - 64;
+      int it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < args.num_tiles; t += gridDim.x) {
+        int mb, nb, bz, ks, kb;
+        decode_tile(t, args, mb, nb, bz, ks);
+        const int nk = unit_k_tiles(args, ks, kb);
+        for (int kt = 0; kt < nk; ++kt, ++it) {
+          const int s = it % STAGES;
+          // every lane waits (bounded) and the warp leaves together if any lane gave up
+          if (!__all_sync(0xffffffffu, mbar_wait(&raw_full[s], (it / STAGES) & 1, &abort_flag))) {
+            ok = false;
+            break;
+          }
+          split_tile<TILE_A_BYTES / 16>(stage_ptr(s, 0), stage_ptr(s, 1), t64);
+          split_tile<TILE_B_BYTES / 16>(stage_ptr(s, 2), stage_ptr(s, 3), t64);
+          // the remainder tiles, written through the generic proxy, are made visible to
+          // the tensor cores' reads before the stage is handed over
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&full_bar[s]);
+        }
+      }
+      if (!ok) {
+        if (lane == 0) atomicCAS(args.err, kErrNone, kErrTimeoutSplit);
+        abort_flag = 1;
       }
     }
   } else {
@@ -962,7 +1075,7 @@ __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
                : "memory");
 }
 
-template <bool A_MN, bool B_MN, class EPI>
+template <bool A_MN, bool B_MN, class EPI, bool SPLIT = false>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap mapAh,
                      const __grid_constant__ CUtensorMap mapAl,
@@ -975,6 +1088,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   __shared__ __align__(8) uint64_t full_bar[PAIR_STAGES];
   __shared__ __align__(8) uint64_t empty_bar[PAIR_STAGES];
+  __shared__ __align__(8) uint64_t raw_full[SPLIT ? PAIR_STAGES : 1];  // SPLIT: this CTA's raw tiles landed
   __shared__ __align__(8) uint64_t acc_full[2];
   __shared__ __align__(8) uint64_t acc_empty[2];
   __shared__ __align__(8) uint64_t drain_bar;  // MMAs issued before an abort, completed
@@ -989,8 +1103,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < PAIR_STAGES; ++s) {
-      mbar_init(&full_bar[s], 1);
+      // SPLIT: one arrival per splitter warp of both CTAs (in the leader's barrier)
+      mbar_init(&full_bar[s], SPLIT ? 2 * NUM_SPLIT_WARPS : 1);
       mbar_init(&empty_bar[s], 1);
+      if constexpr (SPLIT) mbar_init(&raw_full[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
@@ -1042,21 +1158,29 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
               ok = false;
               break;
             }
-            if (leader) mbar_expect_tx(&full_bar[s], 2 * PAIR_STAGE_BYTES);
-            const uint32_t fb = in_leader(&full_bar[s]);
             const int k0 = kb + kt * BK;
-            load_operand_pair<A_MN>(stage_ptr(s, 0), &mapAh, fb, k0, row_a, bz, args.wide & 1);
-            load_operand_pair<A_MN>(stage_ptr(s, 1), &mapAl, fb, k0, row_a, bz, args.wide & 2);
-            load_operand_pair<B_MN>(stage_ptr(s, 2), &mapBh, fb, k0, row_b, bz, args.wide & 4);
-            load_operand_pair<B_MN>(stage_ptr(s, 3), &mapBl, fb, k0, row_b, bz, args.wide & 8);
+            if constexpr (SPLIT) {
+              // this CTA's raw tiles, completed on its own barrier; its splitter warps add
+              // the remainders and report to the leader
+              mbar_expect_tx(&raw_full[s], 2 * PAIR_TILE_BYTES);
+              load_operand<A_MN, BM>(stage_ptr(s, 0), &mapAh, &raw_full[s], k0, row_a, bz, args.wide & 1);
+              load_operand<B_MN, BM>(stage_ptr(s, 2), &mapBh, &raw_full[s], k0, row_b, bz, args.wide & 4);
+            } else {
+              if (leader) mbar_expect_tx(&full_bar[s], 2 * PAIR_STAGE_BYTES);
+              const uint32_t fb = in_leader(&full_bar[s]);
+              load_operand_pair<A_MN>(stage_ptr(s, 0), &mapAh, fb, k0, row_a, bz, args.wide & 1);
+              load_operand_pair<A_MN>(stage_ptr(s, 1), &mapAl, fb, k0, row_a, bz, args.wide & 2);
+              load_operand_pair<B_MN>(stage_ptr(s, 2), &mapBh, fb, k0, row_b, bz, args.wide & 4);
+              load_operand_pair<B_MN>(stage_ptr(s, 3), &mapBl, fb, k0, row_b, bz, args.wide & 8);
+            }
           }
         }
         if (!ok) {
           atomicCAS(args.err, kErrNone, kErrTimeoutEmpty);
           abort_flag = 1;
-          if (leader) {  // drain (bounded): the last PAIR_STAGES k-tiles' loads of the pair
+          if (SPLIT || leader) {  // drain (bounded): the last PAIR_STAGES k-tiles' loads
             for (int i = (it > PAIR_STAGES ? it - PAIR_STAGES : 0); i < it; ++i)
-              mbar_drain(&full_bar[i % PAIR_STAGES], (i / PAIR_STAGES) & 1);
+              mbar_drain(SPLIT ? &raw_full[i % PAIR_STAGES] : &full_bar[i % PAIR_STAGES], (i / PAIR_STAGES) & 1);
           }
         }
       }
@@ -1080,7 +1204,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
             const int kend = kt0 + KCHUNK < num_k ? kt0 + KCHUNK : num_k;
             for (int kt = kt0; kt < kend; ++kt, ++it) {
               const int s = it % PAIR_STAGES;
-              if (!mbar_wait(&full_bar[s], (it / PAIR_STAGES) & 1, &abort_flag)) {
+              if (!(SPLIT ? mbar_wait_cluster(&full_bar[s], (it / PAIR_STAGES) & 1, &abort_flag)
+                          : mbar_wait(&full_bar[s], (it / PAIR_STAGES) & 1, &abort_flag))) {
                 ok = false;
                 break;
               }
@@ -1109,6 +1234,35 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
           umma_commit_leader(&drain_bar);
           mbar_drain(&drain_bar, 0);
         }
+      }
+    } else if constexpr (SPLIT) {
+      // ------------------------------------------------------ remainder tiles (warps 2-3, both CTAs)
+      const int t64 = (int)threadIdx.x - 64;
+      int it = 0;
+      bool ok = true;
+      for (int t = pair; ok && t < args.num_tiles; t += npairs) {
+        int mb, nb, bz, ks, kb;
+        decode_tile(t, args, mb, nb, bz, ks);
+        const int nk = unit_k_tiles(args, ks, kb);
+        for (int kt = 0; kt < nk; ++kt, ++it) {
+          const int s = it % PAIR_STAGES;
+          if (!__all_sync(0xffffffffu, mbar_wait(&raw_full[s], (it / PAIR_STAGES) & 1, &abort_flag))) {
+            ok = false;
+            break;
+          }
+          split_tile<PAIR_TILE_BYTES / 16>(stage_ptr(s, 0), stage_ptr(s, 1), t64);
+          split_tile<PAIR_TILE_BYTES / 16>(stage_ptr(s, 2), stage_ptr(s, 3), t64);
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          __syncwarp();
+          if (lane == 0) {
+            if (leader) mbar_arrive(&full_bar[s]);
+            else mbar_arrive_remote(in_leader(&full_bar[s]));
+          }
+        }
+      }
+      if (!ok) {
+        if (lane == 0) atomicCAS(args.err, kErrNone, kErrTimeoutSplit);
+        abort_flag = 1;
       }
     }
   } else {
