@@ -336,8 +336,9 @@ int fz_gemm_set_tma_stores(int on);
  * separate pass writes each into a workspace before the GEMM; FZ_GEMM_SPLIT_IN_KERNEL,
  * the GEMM kernel derives them in shared memory from the raw operand tiles and needs no
  * workspace (full-width tiles, plain output, operands TMA can address; other calls use
- * the pass). The in-kernel split is slower on B200 (1.2x for small products, about 2.5x
- * for large ones), hence not the default. Results are identical bit for bit. Replaces
+ * the pass). The in-kernel split is slower on B200 for all but single-wave products
+ * (1024^3: 0.87x the time; batched 64x512^3 1.3x; large products 1.5-1.9x), hence
+ * not the default. Results are identical bit for bit. Replaces
  * no reference interface. fz_gemm_split_launches: how many launches so far derived
  * them in shared memory. */
 enum fz_gemm_split { FZ_GEMM_SPLIT_AUTO = 0, FZ_GEMM_SPLIT_PASS = 1, FZ_GEMM_SPLIT_IN_KERNEL = 2 };

@@ -246,12 +246,11 @@ struct LaunchTimer {
 
 std::atomic<int> g_tile_mode{FZ_GEMM_TILES_AUTO};
 // Where missing remainder planes come from (fz_gemm_set_split). AUTO takes the separate
-// pass: deriving them in shared memory (the SPLIT kernels) measured slower on every
-// product of the sweep, 1.2x for 1024^3 and batched 64x512^3 and 2.4-2.7x for large
-// products, with the remainders of a k-tile (4096 per SM per k-tile, about ten
-// instructions each) more than the two splitter warps issue in the ~860 cycles the
-// MMAs spend on it. The SPLIT kernels need no workspace, which callers short of memory
-// can choose them for.
+// pass: deriving them in shared memory (the SPLIT kernels) measured slower on the sweep's
+// products except 1024^3 (0.87x the time; batched 64x512^3 1.3x, 2048^3 1.25x, large
+// products 1.5-1.9x), the main loop being bound by shared-memory traffic to which the
+// split adds its reads and writes. The SPLIT kernels need no workspace, which callers
+// short of memory can choose them for.
 std::atomic<int> g_split_mode{FZ_GEMM_SPLIT_AUTO};
 // Epilogue outputs through TMA bulk tensor stores where the layout allows (default);
 // off: every output stored per thread (fz_gemm_set_tma_stores).

@@ -81,9 +81,11 @@ constexpr unsigned long long kWaitNs = 4000000000ull;  // 4 s per wait
 
 enum : int { kErrNone = 0, kErrTimeoutFull = 1, kErrTimeoutEmpty = 2, kErrTimeoutAcc = 3, kErrTimeoutSplit = 4 };
 // Kernels instantiated with SPLIT derive the remainder tiles in shared memory: the TMA
-// producer loads the raw operand tiles only and warps 2-3 (otherwise idle) write each
-// k-tile's remainder tiles beside them before the MMA issuer may use the stage.
-constexpr int NUM_SPLIT_WARPS = 2;
+// producer loads the raw operand tiles only, and warps 2-3 (otherwise idle) and the
+// eight epilogue warps (between promotions) each write a share of every k-tile's
+// remainder tiles beside them; the MMA issuer takes the stage once all ten have.
+constexpr int NUM_SPLIT_WARPS = 2 + NUM_EPI_WARPS;
+constexpr int SPLIT_SHARE_CTRL = 128;  // float4s of a stage per splitter warp 2 or 3
 
 
 // ---------------------------------------------------------------- PTX helpers
@@ -622,27 +624,26 @@ __device__ __forceinline__ void sts_f4(uint32_t a, float4 v) {
                : "memory");
 }
 
-// Remainder tile of a raw operand tile in shared memory, element for element at the
-// same offsets (TMA would have written the remainder plane in the same swizzled
-// layout), by the 64 splitter threads (index t): N4 float4s, N4 / 64 per thread, a
-// warp's 32 consecutive float4s per access, 8 loads in flight.
-template <int N4>
-__device__ __forceinline__ void split_tile(const uint8_t *hi, uint8_t *lo, int t) {
-  static_assert(N4 % 64 == 0, "whole rounds of float4s per thread");
-  constexpr int PER = N4 / 64, BATCH = PER < 8 ? PER : 8;
-  static_assert(PER % BATCH == 0, "whole batches");
-  const uint32_t h = smem_u32(hi), l = smem_u32(lo);
+// One warp's share of a stage's remainders: float4s [f0, f0 + 32 * PER) of the stage's
+// raw tiles taken as one run (A's A_N4 float4s, then B's, B_OFF bytes into the stage),
+// PER per lane and 32 consecutive float4s per access; each remainder goes to the same
+// offset in its tile's remainder slot (A_LO or B_LO bytes after the raw tile), the
+// swizzled layout in which TMA would have written the remainder plane.
+template <int PER, int A_N4, int B_OFF, int A_LO, int B_LO>
+__device__ __forceinline__ void split_share(uint32_t stage, int f0, int lane) {
+  float4 v[PER];
+  uint32_t dst[PER];
 #pragma unroll
-  for (int j0 = 0; j0 < PER; j0 += BATCH) {
-    float4 v[BATCH];
-#pragma unroll
-    for (int j = 0; j < BATCH; ++j) v[j] = lds_f4(h + (uint32_t)(((j0 + j) * 64 + t) * 16));
-#pragma unroll
-    for (int j = 0; j < BATCH; ++j)
-      sts_f4(l + (uint32_t)(((j0 + j) * 64 + t) * 16),
-             make_float4(tf32_remainder(v[j].x), tf32_remainder(v[j].y), tf32_remainder(v[j].z),
-                         tf32_remainder(v[j].w)));
+  for (int j = 0; j < PER; ++j) {
+    const int f = f0 + j * 32 + lane;
+    const uint32_t src = f < A_N4 ? stage + (uint32_t)f * 16u : stage + (uint32_t)B_OFF + (uint32_t)(f - A_N4) * 16u;
+    dst[j] = src + (f < A_N4 ? (uint32_t)A_LO : (uint32_t)B_LO);
+    v[j] = lds_f4(src);
   }
+#pragma unroll
+  for (int j = 0; j < PER; ++j)
+    sts_f4(dst[j], make_float4(tf32_remainder(v[j].x), tf32_remainder(v[j].y), tf32_remainder(v[j].z),
+                               tf32_remainder(v[j].w)));
 }
 
 // Work unit t -> (K split, batch, m block, n block). Units of one K split are
@@ -744,6 +745,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   constexpr int TILE_B_BYTES = T::B_BYTES;
   constexpr int TMEM_COLS = T::TMEM;
   constexpr int CPW = T::CPW;
+  // SPLIT shares of a stage's float4s: warps 2-3 SPLIT_SHARE_CTRL each, then each
+  // epilogue warp SPLIT_SHARE_EPI
+  constexpr int SPLIT_A_N4 = TILE_A_BYTES / 16;
+  constexpr int SPLIT_SHARE_EPI = (SPLIT_A_N4 + TILE_B_BYTES / 16 - 2 * SPLIT_SHARE_CTRL) / NUM_EPI_WARPS;
+  static_assert(!SPLIT || (SPLIT_SHARE_EPI % 32 == 0 && 2 * SPLIT_SHARE_CTRL + NUM_EPI_WARPS * SPLIT_SHARE_EPI ==
+                                                            SPLIT_A_N4 + TILE_B_BYTES / 16),
+                "the shares cover the stage");
   static_assert(TBN == BN || !B_MN, "narrow tiles read B K-major");
   static_assert(!SPLIT || TBN == BN, "remainder tiles in shared memory: full-width tiles only");
   __shared__ __align__(8) uint64_t full_bar[STAGES];   // stage ready for the MMAs
@@ -891,7 +899,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
     } else if constexpr (SPLIT) {
       // ------------------------------------------------------ remainder tiles (warps 2-3)
-      const int t64 = (int)threadIdx.x - 64;
       int it = 0;
       bool ok = true;
       for (int t = blockIdx.x; ok && t < args.num_tiles; t += gridDim.x) {
@@ -905,8 +912,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             ok = false;
             break;
           }
-          split_tile<TILE_A_BYTES / 16>(stage_ptr(s, 0), stage_ptr(s, 1), t64);
-          split_tile<TILE_B_BYTES / 16>(stage_ptr(s, 2), stage_ptr(s, 3), t64);
+          split_share<SPLIT_SHARE_CTRL / 32, SPLIT_A_N4, 2 * TILE_A_BYTES, TILE_A_BYTES, TILE_B_BYTES>(
+              smem_u32(stage_ptr(s, 0)), (warp - 2) * SPLIT_SHARE_CTRL, lane);
           // the remainder tiles, written through the generic proxy, are made visible to
           // the tensor cores' reads before the stage is handed over
           asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -928,16 +935,45 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                                                   (size_t)(warp - EPI_WARP0) * EPI_TILE_BYTES);
     int cc = 0;
     bool ok = true;
+    // SPLIT: this warp's share of the remainders, k-tile by k-tile (global index sit),
+    // kept up to the end of the chunk after the one it promotes next
+    int sit = 0, it_base = 0;
     for (int t = blockIdx.x; ok && t < args.num_tiles; t += gridDim.x) {
       int mb, nb, bz, ks, kb;
       decode_tile(t, args, mb, nb, bz, ks);
       const int num_k = unit_k_tiles(args, ks, kb);
+      int next_first = 0;  // SPLIT: k-tiles in the first chunk of this CTA's next tile
+      if (SPLIT && t + (int)gridDim.x < args.num_tiles) {
+        int mb2, nb2, bz2, ks2, kb2;
+        decode_tile(t + (int)gridDim.x, args, mb2, nb2, bz2, ks2);
+        const int nk2 = unit_k_tiles(args, ks2, kb2);
+        next_first = nk2 < KCHUNK ? nk2 : KCHUNK;
+      }
       EPI::template prefetch<CPW>(args, ep, bz, mb * BM + q * 32 + lane, nb * TBN + half * CPW);
       float acc[CPW];
 #pragma unroll
       for (int i = 0; i < CPW; ++i) acc[i] = 0.0f;
       for (int kt0 = 0; kt0 < num_k; kt0 += KCHUNK, ++cc) {
         const int b = cc & 1;
+        if constexpr (SPLIT) {
+          const int target = it_base + (kt0 + KCHUNK < num_k ? (kt0 + 2 * KCHUNK < num_k ? kt0 + 2 * KCHUNK : num_k)
+                                                              : num_k + next_first);
+          for (; ok && sit < target; ++sit) {
+            const int s = sit % STAGES;
+            if (!__all_sync(0xffffffffu, mbar_wait(&raw_full[s], (sit / STAGES) & 1, &abort_flag))) {
+              if (lane == 0) atomicCAS(args.err, kErrNone, kErrTimeoutSplit);
+              abort_flag = 1;
+              ok = false;
+              break;
+            }
+            split_share<SPLIT_SHARE_EPI / 32, SPLIT_A_N4, 2 * TILE_A_BYTES, TILE_A_BYTES, TILE_B_BYTES>(
+                smem_u32(stage_ptr(s, 0)), 2 * SPLIT_SHARE_CTRL + (warp - EPI_WARP0) * SPLIT_SHARE_EPI, lane);
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&full_bar[s]);
+          }
+          if (!ok) break;
+        }
         if (!mbar_wait(&acc_full[b], (cc >> 1) & 1, &abort_flag)) {
           if (lane == 0) atomicCAS(args.err, kErrNone, kErrTimeoutAcc);
           abort_flag = 1;
@@ -955,6 +991,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if (!ok) break;
       EPI::template store<CPW>(args, ep, ks, bz, mb * BM + q * 32 + lane, nb * TBN + half * CPW, acc,
                                epi_tile);
+      it_base += num_k;
     }
     tma_stores_drain(ep, lane);
   }
@@ -1237,7 +1274,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       }
     } else if constexpr (SPLIT) {
       // ------------------------------------------------------ remainder tiles (warps 2-3, both CTAs)
-      const int t64 = (int)threadIdx.x - 64;
       int it = 0;
       bool ok = true;
       for (int t = pair; ok && t < args.num_tiles; t += npairs) {
@@ -1250,8 +1286,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
             ok = false;
             break;
           }
-          split_tile<PAIR_TILE_BYTES / 16>(stage_ptr(s, 0), stage_ptr(s, 1), t64);
-          split_tile<PAIR_TILE_BYTES / 16>(stage_ptr(s, 2), stage_ptr(s, 3), t64);
+          split_share<SPLIT_SHARE_CTRL / 32, PAIR_TILE_BYTES / 16, 2 * PAIR_TILE_BYTES, PAIR_TILE_BYTES,
+                      PAIR_TILE_BYTES>(smem_u32(stage_ptr(s, 0)), (warp - 2) * SPLIT_SHARE_CTRL, lane);
           asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
           __syncwarp();
           if (lane == 0) {
@@ -1275,10 +1311,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     const uint32_t acc_empty_leader0 = in_leader(&acc_empty[0]), acc_empty_leader1 = in_leader(&acc_empty[1]);
     int cc = 0;
     bool ok = true;
+    // SPLIT: this warp's share of the remainders, as in the single-CTA kernel; the
+    // leader's full barrier counts the ten warps of both CTAs
+    constexpr int SPLIT_SHARE_EPI = (2 * (PAIR_TILE_BYTES / 16) - 2 * SPLIT_SHARE_CTRL) / NUM_EPI_WARPS;
+    static_assert(SPLIT_SHARE_EPI % 32 == 0, "whole float4s per lane");
+    int sit = 0, it_base = 0;
     for (int t = pair; ok && t < args.num_tiles; t += npairs) {
       int mb, nb, bz, ks, kb;
       decode_tile(t, args, mb, nb, bz, ks);
       const int num_k = unit_k_tiles(args, ks, kb);
+      int next_first = 0;
+      if (SPLIT && t + npairs < args.num_tiles) {
+        int mb2, nb2, bz2, ks2, kb2;
+        decode_tile(t + npairs, args, mb2, nb2, bz2, ks2);
+        const int nk2 = unit_k_tiles(args, ks2, kb2);
+        next_first = nk2 < KCHUNK ? nk2 : KCHUNK;
+      }
       EPI::template prefetch<128>(args, ep, bz, mb * 2 * BM + (int)rank * BM + q * 32 + lane,
                                   nb * BN + half * 128);
       float acc[128];
@@ -1286,6 +1334,29 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       for (int i = 0; i < 128; ++i) acc[i] = 0.0f;
       for (int kt0 = 0; kt0 < num_k; kt0 += KCHUNK, ++cc) {
         const int b = cc & 1;
+        if constexpr (SPLIT) {
+          const int target = it_base + (kt0 + KCHUNK < num_k ? (kt0 + 2 * KCHUNK < num_k ? kt0 + 2 * KCHUNK : num_k)
+                                                              : num_k + next_first);
+          for (; ok && sit < target; ++sit) {
+            const int s = sit % PAIR_STAGES;
+            if (!__all_sync(0xffffffffu, mbar_wait(&raw_full[s], (sit / PAIR_STAGES) & 1, &abort_flag))) {
+              if (lane == 0) atomicCAS(args.err, kErrNone, kErrTimeoutSplit);
+              abort_flag = 1;
+              ok = false;
+              break;
+            }
+            split_share<SPLIT_SHARE_EPI / 32, PAIR_TILE_BYTES / 16, 2 * PAIR_TILE_BYTES, PAIR_TILE_BYTES,
+                        PAIR_TILE_BYTES>(smem_u32(stage_ptr(s, 0)),
+                                         2 * SPLIT_SHARE_CTRL + (warp - EPI_WARP0) * SPLIT_SHARE_EPI, lane);
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) {
+              if (leader) mbar_arrive(&full_bar[s]);
+              else mbar_arrive_remote(in_leader(&full_bar[s]));
+            }
+          }
+          if (!ok) break;
+        }
         if (!mbar_wait(&acc_full[b], (cc >> 1) & 1, &abort_flag)) {
           if (lane == 0) atomicCAS(args.err, kErrNone, kErrTimeoutAcc);
           abort_flag = 1;
@@ -1306,6 +1377,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       if (!ok) break;
       EPI::template store<128>(args, ep, ks, bz, mb * 2 * BM + (int)rank * BM + q * 32 + lane,
                                nb * BN + half * 128, acc, epi_tile);
+      it_base += num_k;
     }
     tma_stores_drain(ep, lane);
   }
