@@ -670,13 +670,109 @@ void epilogue_tma_wide(std::ostringstream &o, const fz_program &pg, const int *c
   o << "    }\n  }\n};\n";
 }
 
+// The wide TMA form with one full-shape input (class 2): per 32-column block the input's
+// 32 x 32 box comes into the warp's staging tile by a TMA load (epi_load_box: 128-byte
+// swizzle, zeros past the edges), each lane takes its row into registers, and each
+// output is evaluated over the block into the tile and leaves in one 32 x 32 store, as
+// in epilogue_tma_wide. Four blocks of one load and nout stores per 128 columns replace
+// the region form's eight blocks of 16 columns, each of which waited for a cp.async
+// copy of the input and for its stores to read the tile.
+void epilogue_tma_wide_in(std::ostringstream &o, const fz_program &pg, const int *cls) {
+  const int nin = pg.num_leaves - 1, nout = pg.num_outputs;
+  int kin = -1;
+  for (int k = 0; k < nin; ++k)
+    if (cls[k] == 2) kin = k;
+  const std::string KI = std::to_string(kin);
+  o << "    constexpr int BW = 32;\n";
+  epilogue_operands(o, nin, cls);
+  o << "    (void)g" << KI << ";\n"
+    << "#pragma unroll\n"
+    << "    for (int cb = 0; cb < CPW / BW; ++cb) {\n"
+    << "      const int cols = min(BW, a.N - col0 - cb * BW);\n"
+    << "      if (cols <= 0) break;\n"
+    << "      // block 0's load was started by prefetch, before the tile's last chunk\n"
+    << "      if (cb > 0) epi_issue_box(&p.imap, tile, sync, col0 + cb * BW, row0, bz, lane, mask);\n"
+    << "      if (!epi_wait_box(sync, lane, mask, a.err)) return;\n"
+    << "      float v" << KI << "[BW];\n"
+    << "#pragma unroll\n"
+    << "      for (int c4 = 0; c4 < BW / 4; ++c4) {\n"
+    << "        const float4 t = tile_get(tile, lane, c4);\n"
+    << "        v" << KI << "[c4 * 4] = t.x; v" << KI << "[c4 * 4 + 1] = t.y; v" << KI << "[c4 * 4 + 2] = t.z; v" << KI
+    << "[c4 * 4 + 3] = t.w;\n"
+    << "      }\n"
+    << "      __syncwarp(mask);  // every lane has its row before the tile is overwritten\n";
+  for (int j = 0; j < nout; ++j) {
+    o << "      {\n";
+    if (j > 0) o << "        store_reads_done<0>(lane, mask);\n";
+    o << "#pragma unroll\n"
+      << "        for (int c4 = 0; c4 < BW / 4; ++c4) {\n";
+    for (int k = 0; k < nin; ++k)
+      if (cls[k] == 1) epilogue_row_vector(o, k);
+    o << "          float r[4];\n"
+      << "#pragma unroll\n"
+      << "          for (int e = 0; e < 4; ++e) {\n"
+      << "            const int c = c4 * 4 + e;\n";
+    for (int q = 0; q < nout; ++q) o << "            float q" << q << ";\n";
+    o << "            fz_eval(acc[cb * BW + c], ";
+    for (int k = 0; k < nin; ++k)
+      o << (cls[k] == 0 ? "s" + std::to_string(k)
+                        : cls[k] == 1 ? "u" + std::to_string(k) + "[e]" : "v" + std::to_string(k) + "[c]")
+        << ", ";
+    for (int q = 0; q < nout; ++q) o << "q" << q << (q + 1 < nout ? ", " : "");
+    o << ");\n"
+      << "            r[e] = q" << j << ";\n"
+      << "          }\n"
+      << "          tile_put(tile, lane, c4, make_float4(r[0], r[1], r[2], r[3]));\n"
+      << "        }\n"
+      << "        staged_for_tma(mask);\n"
+      << "        if (lane == 0) {\n"
+      << "          tma_store_3d(&p.omap[" << j << "], tile, col0 + cb * BW, row0, bz);\n"
+      << "          tma_store_commit();\n"
+      << "        }\n"
+      << "      }\n";
+  }
+  o << "    }\n  }\n};\n";
+}
+
+// The one full-shape input of a program, or -1 (none, or more than one).
+int single_full_input(const fz_program &pg, const int *cls) {
+  int kin = -1;
+  for (int k = 0; k + 1 < pg.num_leaves; ++k)
+    if (cls[k] == 2) {
+      if (kin >= 0) return -1;
+      kin = k;
+    }
+  return kin;
+}
+
+// Load map of a full-shape epilogue input: 3D {N, M, Z}, its row and batch pitches,
+// 32 x 32 boxes in the staging tile's 128-byte swizzle. false when TMA cannot read
+// it (then the region form copies it with cp.async).
+bool make_in_map(CUtensorMap *map, const fz_epi_input &in, int64_t N, int64_t M, int64_t Z) {
+  const int64_t sm = in.row_stride, sb = Z == 1 ? in.row_stride * M : in.batch_stride;
+  if (!in.ptr || ((uintptr_t)in.ptr & 15) || sm < N || (sm * 4) % 16 || sb <= 0 || (sb * 4) % 16) return false;
+  cuuint64_t dims[3] = {(cuuint64_t)N, (cuuint64_t)M, (cuuint64_t)Z};
+  cuuint64_t strides[2] = {(cuuint64_t)(sm * 4), (cuuint64_t)(sb * 4)};
+  cuuint32_t box[3] = {32, 32, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(in.ptr), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // cls[k] of input k: 0 constant along a row (a per-row value or a scalar), 1 a row
 // vector (same for every row: a bias), 2 varying along rows and columns (a tensor of
 // the product's shape). Class-2 inputs are read through the warp's staging tile in
 // whole row segments; class-1 inputs are the same address for every lane.
-std::string epilogue_class(const fz_program &pg, const int *cls, int tma_bw) {
+std::string epilogue_class(const fz_program &pg, const int *cls, int tma_bw, bool wide_in) {
   const int nin = pg.num_leaves - 1, nout = pg.num_outputs;
   std::ostringstream o;
+  // prefetch: called when a tile starts, L2 prefetches of the full-shape inputs' rows
+  // lane by lane. before_last: called before the tile's last chunk is promoted; the
+  // TMA-input form starts its first block's load into the staging tile there (it lands
+  // while the chunk is promoted) and has the TMA unit prefetch the other blocks into L2
+  // (a prefetch at the start of the tile would be evicted by the main loop's operand
+  // traffic, which turns L2 over every ~15 us).
   o << "struct GenEpi {\n"
     << "  template <int CPW>\n"
     << "  static __device__ __forceinline__ void prefetch(const fz_gemm_dev::GemmArgs &a,\n"
@@ -684,16 +780,33 @@ std::string epilogue_class(const fz_program &pg, const int *cls, int tma_bw) {
     << "    if (row >= a.M || col0 >= a.N) return;\n"
     << "    const int n = min(CPW, a.N - col0);\n"
     << "    (void)p; (void)bz; (void)n;\n";
-  for (int k = 0; k < nin; ++k)
-    if (cls[k] == 2)
-      o << "    fz_gemm_dev::prefetch_row_l2(p.in[" << k << "] + (long long)bz * p.in_sb[" << k
-        << "] + (long long)row * p.in_sm[" << k << "] + col0, n);\n";
+  if (!wide_in)
+    for (int k = 0; k < nin; ++k)
+      if (cls[k] == 2)
+        o << "    fz_gemm_dev::prefetch_row_l2(p.in[" << k << "] + (long long)bz * p.in_sb[" << k
+          << "] + (long long)row * p.in_sm[" << k << "] + col0, n);\n";
+  o << "  }\n"
+    << "  template <int CPW>\n"
+    << "  static __device__ __forceinline__ void before_last(const fz_gemm_dev::GemmArgs &a,\n"
+    << "      const fz_gemm_dev::EpiParams &p, int bz, int row, int col0, float4 *tile,\n"
+    << "      fz_gemm_dev::EpiSync &sync) {\n"
+    << "    using namespace fz_gemm_dev;\n"
+    << "    (void)a; (void)p; (void)bz; (void)row; (void)col0; (void)tile; (void)sync;\n";
+  if (wide_in)
+    o << "    const int lane = threadIdx.x & 31;\n"
+      << "    const int row0 = row - lane;\n"
+      << "    if (row0 >= a.M || col0 >= a.N) return;  // uniform over the warp\n"
+      << "    const unsigned mask = __activemask();\n"
+      << "    epi_issue_box(&p.imap, tile, sync, col0, row0, bz, lane, mask);\n"
+      << "    if (lane == 0)\n"
+      << "      for (int cb = 1; cb < CPW / 32 && col0 + cb * 32 < a.N; ++cb) tma_prefetch_box(&p.imap, col0 + cb * 32, row0, bz);\n";
   o << "  }\n"
     << "  template <int CPW>\n"
     << "  static __device__ __forceinline__ void store(const fz_gemm_dev::GemmArgs &a,\n"
     << "      const fz_gemm_dev::EpiParams &p, int, int bz, int row, int col0,\n"
-    << "      const float (&acc)[CPW], float4 *tile) {\n"
+    << "      const float (&acc)[CPW], float4 *tile, fz_gemm_dev::EpiSync &sync) {\n"
     << "    using namespace fz_gemm_dev;\n"
+    << "    (void)sync;\n"
     << "    const int lane = threadIdx.x & 31;\n"
     << "    const int row0 = row - lane;\n"
     << "    const int rows = min(32, a.M - row0);\n"
@@ -712,6 +825,10 @@ std::string epilogue_class(const fz_program &pg, const int *cls, int tma_bw) {
   // 1.123 -> 1.105 ms, the K = 16 one of the MLP 1.91 -> 1.60 ms. Without class-2
   // inputs the per-output passes at 16 columns are faster (bias + ReLU with three
   // outputs: 1.056 ms, against 1.085 side by side at 8 columns).
+  if (wide_in) {
+    epilogue_tma_wide_in(o, pg, cls);
+    return o.str();
+  }
   if (tma_bw == 32) {
     epilogue_tma_wide(o, pg, cls);
     return o.str();
@@ -792,9 +909,9 @@ struct JitEntry {
 std::mutex g_jit_mu;
 std::unordered_map<std::string, JitEntry> g_jit;
 
-std::string epilogue_source(const fz_program &pg, const int *cls, int tma_bw) {
+std::string epilogue_source(const fz_program &pg, const int *cls, int tma_bw, bool wide_in) {
   return "#define FZ_GEMM_BK " + std::to_string(BK) + "\n" + kGemmKernelSource + "\n" +
-         fz::program_eval_source(pg) + epilogue_class(pg, cls, tma_bw);
+         fz::program_eval_source(pg) + epilogue_class(pg, cls, tma_bw, wide_in);
 }
 
 std::string epilogue_kernel_name(bool a_mn, bool b_mn, int tbn, bool pair) {
@@ -805,7 +922,7 @@ std::string epilogue_kernel_name(bool a_mn, bool b_mn, int tbn, bool pair) {
 }
 
 int jit_kernel(const fz_program &pg, const int *cls, bool a_mn, bool b_mn, int tbn, bool pair,
-               int tma_bw, size_t smem, cudaKernel_t *out) {
+               int tma_bw, bool wide_in, size_t smem, cudaKernel_t *out) {
   std::string key(reinterpret_cast<const char *>(&pg),
                   offsetof(fz_program, nodes) + sizeof(fz_node) * pg.num_nodes);
   for (int k = 0; k + 1 < pg.num_leaves; ++k) key.push_back((char)('0' + cls[k]));
@@ -813,7 +930,7 @@ int jit_kernel(const fz_program &pg, const int *cls, bool a_mn, bool b_mn, int t
   key.push_back((char)('0' + a_mn));
   key.push_back((char)('0' + b_mn));
   key += std::to_string(tbn);
-  key += "T" + std::to_string(tma_bw);
+  key += "T" + std::to_string(tma_bw) + (wide_in ? "I" : "");
   int dev = 0;
   FZ_CUDA(cudaGetDevice(&dev));
   std::lock_guard<std::mutex> lk(g_jit_mu);
@@ -822,7 +939,7 @@ int jit_kernel(const fz_program &pg, const int *cls, bool a_mn, bool b_mn, int t
     std::vector<char> bin;
     std::string lowered;
     const std::string name = epilogue_kernel_name(a_mn, b_mn, tbn, pair);
-    int rc = fz::nvrtc_cubin(epilogue_source(pg, cls, tma_bw), "fz_gemm_epilogue.cu", name.c_str(), &bin,
+    int rc = fz::nvrtc_cubin(epilogue_source(pg, cls, tma_bw, wide_in), "fz_gemm_epilogue.cu", name.c_str(), &bin,
                              &lowered);
     if (rc) return rc;
     cudaLibrary_t lib;
@@ -845,11 +962,10 @@ int jit_kernel(const fz_program &pg, const int *cls, bool a_mn, bool b_mn, int t
 int launch_epilogue_gemm(const Epilogue &E, const int *cls, const EpiParams &ep, bool a_mn,
                          bool b_mn, int tbn, const CUtensorMap &mAh, const CUtensorMap &mAl,
                          const CUtensorMap &mBh, const CUtensorMap &mBl, const GemmArgs &ga,
-                         unsigned grid, bool pair, cudaStream_t s) {
+                         unsigned grid, bool pair, int tma_bw, bool wide_in, cudaStream_t s) {
   const size_t smem = smem_bytes(pair, tbn);
   cudaKernel_t k = nullptr;
-  int rc = jit_kernel(*E.pg, cls, a_mn, b_mn, tbn, pair, ep.tma ? tma_block_width(*E.pg, cls, tbn) : 0,
-                      smem, &k);
+  int rc = jit_kernel(*E.pg, cls, a_mn, b_mn, tbn, pair, tma_bw, wide_in, smem, &k);
   if (rc) return rc;
   void *args[] = {const_cast<CUtensorMap *>(&mAh), const_cast<CUtensorMap *>(&mAl),
                   const_cast<CUtensorMap *>(&mBh), const_cast<CUtensorMap *>(&mBl),
@@ -1074,12 +1190,18 @@ int gemm_impl(int64_t batch, int64_t M, int64_t N, int64_t K, const float *A, co
     LaunchTimer timer(batch, M, N, K, pair, in_kernel, real_splits, s);
     // outputs stored by TMA when every output's layout allows it
     if (in_kernel) {
-      const int bw = tma_block_width(*E.pg, cls, tbn);
+      int bw = tma_block_width(*E.pg, cls, tbn);
       bool tma = ep.vec && bw > 0 && g_tma_stores;
+      // one full-shape input and warps owning 32 columns or more: the input comes into
+      // the staging tile by TMA as well, and the outputs leave in 32-column boxes
+      const int kin = single_full_input(*E.pg, cls);
+      const bool wide_in = tma && tbn / 2 >= 32 && kin >= 0 && make_in_map(&ep.imap, E.inputs[kin], N, M, batch);
+      if (wide_in) bw = 32;
       for (int k = 0; tma && k < E.pg->num_outputs; ++k)
         tma = make_out_map(&ep.omap[k], E.outputs[k], N, M, batch, ldc, strideC, bw);
       ep.tma = tma;
-      rc = launch_epilogue_gemm(E, cls, ep, oa.mn, ob.mn, tbn, mAh, mAl, mBh, mBl, ga, grid, pair, s);
+      rc = launch_epilogue_gemm(E, cls, ep, oa.mn, ob.mn, tbn, mAh, mAl, mBh, mBl, ga, grid, pair,
+                                tma ? bw : 0, wide_in && tma, s);
     } else {
       // C, or the K-split partials [split][batch][M][N] as Z = splits x batch slices
       // (32-column swizzled boxes when a warp owns at least 32 columns; see StoreEpi)
@@ -1148,11 +1270,18 @@ extern "C" int fz_gemm_epilogue_compile(const fz_program *epi, const fz_epi_inpu
   std::vector<char> bin;
   std::string lowered;
   const std::string name = epilogue_kernel_name(a_mn != 0, b_mn != 0, tile_n, pair != 0);
-  // both forms: per-thread stores, and bulk tensor stores from the staging tile
-  int rc2 = fz::nvrtc_cubin(epilogue_source(*epi, cls, 0), "fz_gemm_epilogue.cu", name.c_str(), &bin, &lowered);
+  // every form the launch may pick: per-thread stores, bulk tensor stores from the
+  // staging tile, and (one full-shape input, 32 columns or more per warp) the input
+  // loaded into the tile by TMA
+  int rc2 = fz::nvrtc_cubin(epilogue_source(*epi, cls, 0, false), "fz_gemm_epilogue.cu", name.c_str(), &bin,
+                            &lowered);
   const int bw = tma_block_width(*epi, cls, tile_n);
   if (!rc2 && bw)
-    rc2 = fz::nvrtc_cubin(epilogue_source(*epi, cls, bw), "fz_gemm_epilogue.cu", name.c_str(), &bin, &lowered);
+    rc2 = fz::nvrtc_cubin(epilogue_source(*epi, cls, bw, false), "fz_gemm_epilogue.cu", name.c_str(), &bin,
+                          &lowered);
+  if (!rc2 && tile_n / 2 >= 32 && single_full_input(*epi, cls) >= 0)
+    rc2 = fz::nvrtc_cubin(epilogue_source(*epi, cls, 32, true), "fz_gemm_epilogue.cu", name.c_str(), &bin,
+                          &lowered);
   return rc2;
 }
 

@@ -79,7 +79,10 @@ static_assert(128 * REG_CTRL + 32 * NUM_EPI_WARPS * REG_EPI == NUM_THREADS * REG
 static_assert(NUM_EPI_WARPS == 8 && EPI_WARP0 == 4, "two epilogue warpgroups after warpgroup 0");
 constexpr unsigned long long kWaitNs = 4000000000ull;  // 4 s per wait
 
-enum : int { kErrNone = 0, kErrTimeoutFull = 1, kErrTimeoutEmpty = 2, kErrTimeoutAcc = 3, kErrTimeoutSplit = 4 };
+enum : int {
+  kErrNone = 0, kErrTimeoutFull = 1, kErrTimeoutEmpty = 2, kErrTimeoutAcc = 3, kErrTimeoutSplit = 4,
+  kErrTimeoutEpiLoad = 5
+};
 // Kernels instantiated with SPLIT derive the remainder tiles in shared memory: the TMA
 // producer loads the raw operand tiles only, and warps 2-3 (otherwise idle) and the
 // eight epilogue warps (between promotions) each write a share of every k-tile's
@@ -329,10 +332,14 @@ struct GemmArgs {
 // Plain per-thread stores drain at about 15 GB/s per SM while the mainloop's TMA
 // loads run (measured: 9 us per 128 KB output tile per CTA, whatever the access
 // pattern), longer than the MMAs can run ahead; bulk stores leave the SM at once.
+// imap: with one full-shape input, its load map (the same {N, M, Z} layout and 32 x 32
+// boxes in the 128-byte swizzle of tile_put), used by the generated epilogue that
+// brings the input into the staging tile by TMA, 32 columns at a time.
 constexpr int EPI_MAX_IN = 11;
 constexpr int EPI_MAX_OUT = 4;
 struct __align__(64) EpiParams {
   CUtensorMap omap[EPI_MAX_OUT];
+  CUtensorMap imap;
   const float *in[EPI_MAX_IN];
   long long in_sb[EPI_MAX_IN], in_sm[EPI_MAX_IN];
   float *out[EPI_MAX_OUT];
@@ -434,8 +441,8 @@ __device__ __forceinline__ void tile_load_async(float4 *t, const float *src, lon
 }
 
 // Pull this lane's row segment [col0, col0 + n) of a full-shape epilogue input into
-// L2 (one prefetch per 128-byte line), issued when a tile starts so that the loads
-// of its epilogue, after the tile's MMAs, hit L2. Only addresses inside the segment.
+// L2 (one prefetch per 128-byte line), issued when a tile starts. Only addresses
+// inside the segment.
 __device__ __forceinline__ void prefetch_row_l2(const float *p, int n) {
   if (n <= 0) return;
   const uintptr_t first = reinterpret_cast<uintptr_t>(p) & ~(uintptr_t)127;
@@ -490,6 +497,60 @@ __device__ __forceinline__ void tma_store_commit() {
 __device__ __forceinline__ void tma_stores_drain(const EpiParams &ep, int lane) {
   if (ep.tma && lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
+
+// An epilogue warp's barrier for TMA loads into its staging tile, the parity of its
+// next phase, whether a load is in flight, and the CTA's abort flag (bounded waits as
+// in the main loop).
+struct EpiSync {
+  uint64_t *bar;
+  uint32_t phase;
+  int pending;
+  volatile int *abort;
+};
+
+// Start loading the 32 x 32 box of `map` at (x, y, z) into the warp's staging tile
+// (128-byte swizzle, zeros past the tensor's edges), once the tile's earlier stores
+// have read it.
+__device__ __forceinline__ void epi_issue_box(const CUtensorMap *map, float4 *tile, EpiSync &sync, int x, int y,
+                                              int z, int lane, unsigned mask) {
+  store_reads_done<0>(lane, mask);
+  if (lane == 0) {
+    mbar_expect_tx(sync.bar, 32 * 32 * 4);
+    tma_load_3d(tile, map, sync.bar, x, y, z);
+  }
+  sync.pending = 1;
+}
+
+// Wait for the box in flight. False (after recording the error and letting the load
+// land) if the wait ran out.
+__device__ __forceinline__ bool epi_wait_box(EpiSync &sync, int lane, unsigned mask, int *err) {
+  const bool ok = __all_sync(mask, mbar_wait(sync.bar, sync.phase, sync.abort));
+  if (!ok) {
+    if (lane == 0) atomicCAS(err, kErrNone, kErrTimeoutEpiLoad);
+    *sync.abort = 1;
+    mbar_drain(sync.bar, sync.phase);
+  }
+  sync.phase ^= 1u;
+  sync.pending = 0;
+  return ok;
+}
+
+// A load left in flight (a tile abandoned after an abort) lands before the CTA goes on.
+__device__ __forceinline__ void epi_settle(EpiSync &sync) {
+  if (sync.pending) {
+    mbar_drain(sync.bar, sync.phase);
+    sync.phase ^= 1u;
+    sync.pending = 0;
+  }
+}
+
+// L2 prefetch of a 32 x 32 box of `map` by the TMA unit.
+__device__ __forceinline__ void tma_prefetch_box(const CUtensorMap *map, int x, int y, int z) {
+  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y), "r"(z)
+               : "memory");
+}
 // Copy rows [0, rows) x columns [0, cols) of src (row pitch ld, 16-byte aligned rows)
 // into region `reg` (zeros elsewhere), every lane's copies in flight at once.
 template <int BW>
@@ -515,12 +576,14 @@ __device__ __forceinline__ void region_load_async(float4 *reg, const float *src,
 // the staging tile. `row` is this lane's row; the warp's rows are row - lane + [0, 32).
 struct StoreEpi {
   template <int CPW>
-  static __device__ __forceinline__ void prefetch(const GemmArgs &, const EpiParams &, int, int,
-                                                  int) {}
+  static __device__ __forceinline__ void prefetch(const GemmArgs &, const EpiParams &, int, int, int) {}
+  template <int CPW>
+  static __device__ __forceinline__ void before_last(const GemmArgs &, const EpiParams &, int, int, int,
+                                                     float4 *, EpiSync &) {}
   template <int CPW>
   static __device__ __forceinline__ void store(const GemmArgs &a, const EpiParams &ep, int ks,
                                                int bz, int row, int col0, const float (&acc)[CPW],
-                                               float4 *tile) {
+                                               float4 *tile, EpiSync &) {
     const int lane = threadIdx.x & 31;
     const int row0 = row - lane;
     const int rows = min(32, a.M - row0);
@@ -760,6 +823,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   __shared__ __align__(8) uint64_t acc_full[2];
   __shared__ __align__(8) uint64_t acc_empty[2];
   __shared__ __align__(8) uint64_t drain_bar;  // MMAs issued before an abort, completed
+  __shared__ __align__(8) uint64_t epi_bar[NUM_EPI_WARPS];  // epilogue loads into the staging tiles
   __shared__ uint32_t tmem_base_slot;
   __shared__ volatile int abort_flag;
 
@@ -777,6 +841,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       mbar_init(&acc_empty[b], NUM_EPI_WARPS);  // one arrival per epilogue warp
     }
     mbar_init(&drain_bar, 1);
+    for (int w = 0; w < NUM_EPI_WARPS; ++w) mbar_init(&epi_bar[w], 1);
     abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     prefetch_map(&mapAh);
@@ -933,6 +998,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int half = (warp - EPI_WARP0) >> 2;   // which half of the tile's columns
     float4 *epi_tile = reinterpret_cast<float4 *>(smem + (size_t)STAGES * STAGE_BYTES +
                                                   (size_t)(warp - EPI_WARP0) * EPI_TILE_BYTES);
+    EpiSync epi_sync{&epi_bar[warp - EPI_WARP0], 0u, 0, &abort_flag};
     int cc = 0;
     bool ok = true;
     // SPLIT: this warp's share of the remainders, k-tile by k-tile (global index sit),
@@ -974,6 +1040,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           }
           if (!ok) break;
         }
+        // the epilogue's first input block, requested while the tile's last chunk is
+        // still computed
+        if (kt0 + KCHUNK >= num_k)
+          EPI::template before_last<CPW>(args, ep, bz, mb * BM + q * 32 + lane, nb * TBN + half * CPW, epi_tile,
+                                         epi_sync);
         if (!mbar_wait(&acc_full[b], (cc >> 1) & 1, &abort_flag)) {
           if (lane == 0) atomicCAS(args.err, kErrNone, kErrTimeoutAcc);
           abort_flag = 1;
@@ -990,9 +1061,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
       if (!ok) break;
       EPI::template store<CPW>(args, ep, ks, bz, mb * BM + q * 32 + lane, nb * TBN + half * CPW, acc,
-                               epi_tile);
+                               epi_tile, epi_sync);
       it_base += num_k;
     }
+    epi_settle(epi_sync);
     tma_stores_drain(ep, lane);
   }
 
@@ -1129,6 +1201,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   __shared__ __align__(8) uint64_t acc_full[2];
   __shared__ __align__(8) uint64_t acc_empty[2];
   __shared__ __align__(8) uint64_t drain_bar;  // MMAs issued before an abort, completed
+  __shared__ __align__(8) uint64_t epi_bar[NUM_EPI_WARPS];  // epilogue loads into the staging tiles
   __shared__ uint32_t tmem_base_slot;
   __shared__ volatile int abort_flag;
 
@@ -1150,6 +1223,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       mbar_init(&acc_empty[b], 2 * NUM_EPI_WARPS);  // one arrival per epilogue warp of both CTAs
     }
     mbar_init(&drain_bar, 1);
+    for (int w = 0; w < NUM_EPI_WARPS; ++w) mbar_init(&epi_bar[w], 1);
     abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     prefetch_map(&mapAh);
@@ -1308,6 +1382,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     const int half = (warp - EPI_WARP0) >> 2;
     float4 *epi_tile = reinterpret_cast<float4 *>(smem + (size_t)PAIR_STAGES * PAIR_STAGE_BYTES +
                                                   (size_t)(warp - EPI_WARP0) * EPI_TILE_BYTES);
+    EpiSync epi_sync{&epi_bar[warp - EPI_WARP0], 0u, 0, &abort_flag};
     const uint32_t acc_empty_leader0 = in_leader(&acc_empty[0]), acc_empty_leader1 = in_leader(&acc_empty[1]);
     int cc = 0;
     bool ok = true;
@@ -1357,6 +1432,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
           }
           if (!ok) break;
         }
+        if (kt0 + KCHUNK >= num_k)
+          EPI::template before_last<128>(args, ep, bz, mb * 2 * BM + (int)rank * BM + q * 32 + lane,
+                                         nb * BN + half * 128, epi_tile, epi_sync);
         if (!mbar_wait(&acc_full[b], (cc >> 1) & 1, &abort_flag)) {
           if (lane == 0) atomicCAS(args.err, kErrNone, kErrTimeoutAcc);
           abort_flag = 1;
@@ -1376,9 +1454,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       }
       if (!ok) break;
       EPI::template store<128>(args, ep, ks, bz, mb * 2 * BM + (int)rank * BM + q * 32 + lane,
-                               nb * BN + half * 128, acc, epi_tile);
+                               nb * BN + half * 128, acc, epi_tile, epi_sync);
       it_base += num_k;
     }
+    epi_settle(epi_sync);
     tma_stores_drain(ep, lane);
   }
 
