@@ -96,11 +96,19 @@ std::vector<RawTensor> op_forward(OpKind k, OpContext &ctx, const std::vector<Ra
       ctx.saved["x"] = x;
       ctx.saved["y"] = in.at(1);
       return {x.pow(in.at(1))};
-    case OpKind::Maximum:
-      ctx.saved["x"] = x;
-      ctx.saved["y"] = in.at(1);
+    case OpKind::Maximum: {
       allow_scalar_binary(x, in.at(1), "Maximum");
-      return {x.maximum(in.at(1))};
+      RawTensor out = x.maximum(in.at(1));
+      ctx.saved["y"] = in.at(1);
+      // x's gradient mask (x > y) equals (max(x, y) > y) for every pair of values (x > y:
+      // the max is x; otherwise it is y, and y > y is false, NaN included), so when the
+      // engine marked the node (y needs no gradient and x is the engine's own value) the
+      // backward reads the output, which later ops keep anyway, instead of x: a ReLU
+      // after a GEMM then does not keep (and store) the product for its backward
+      if (ctx.ints.count("mask_from_out")) ctx.saved["out"] = out;
+      else ctx.saved["x"] = x;
+      return {out};
+    }
     case OpKind::GreaterThan:
     case OpKind::GreaterThanEqual: {
       const RawTensor &y = in.at(1);
@@ -167,7 +175,12 @@ std::vector<RawTensor> op_backward(OpKind k, OpContext &ctx, const RawTensor &g0
               want(1) ? (x.pow(y) * x.log()) * g0 : RawTensor()};
     }
     case OpKind::Maximum: {
-      const RawTensor &x = ctx.load("x"), &y = ctx.load("y");
+      const RawTensor &y = ctx.load("y");
+      if (ctx.saved.count("out")) {
+        FB_CHECK(!want(1), "Maximum::backward: the second operand's gradient needs the first operand");
+        return {want(0) ? g0 * (ctx.load("out") >= y) : RawTensor(), RawTensor()};
+      }
+      const RawTensor &x = ctx.load("x");
       return {want(0) ? g0 * (x >= y) : RawTensor(), want(1) ? g0 * (y > x) : RawTensor()};
     }
     case OpKind::GreaterThan:
@@ -253,6 +266,15 @@ ValueID Engine::apply(OpKind k, const std::vector<RawTensor> &ins,
     nodes_[nid].inputs.push_back(v);
     if ((int64_t)consumed_by_.size() <= v) consumed_by_.resize(v + 1);
     consumed_by_[v].push_back(nid);
+  }
+  // Maximum whose second operand needs no gradient (neither produced by a node nor a
+  // leaf that requires grad; the same test the backward applies) and whose first
+  // operand is a value the engine produced (no caller holds it to write in place):
+  // its backward may take the mask from the output (see op_forward)
+  if (k == OpKind::Maximum && vids.size() == 2) {
+    const ValueID vx = vids[0], vy = vids[1];
+    const bool y_needs = produced_by_[vy] != -1 || requires_grad_set_.count(vy);
+    if (!y_needs && produced_by_[vx] != -1) nodes_[nid].ctx.ints["mask_from_out"] = 1;
   }
   std::vector<RawTensor> out;
   {
