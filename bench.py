@@ -434,6 +434,10 @@ def cpu_baseline_ref(batch=4096, steps=1):
 
 # ---------------------------------------------------------------- our arm
 def run_ours(args):
+    # NCCL writes its log (with NCCL_DEBUG set, a version banner at least) to stdout, where
+    # the one JSON line goes: send it to stderr unless a log file was chosen
+    if os.environ.get("NCCL_DEBUG") and not os.environ.get("NCCL_DEBUG_FILE"):
+        os.environ["NCCL_DEBUG_FILE"] = "/dev/stderr"
     d = Dist()
     import nova_b200
     from nova_b200 import capi
