@@ -171,6 +171,31 @@ def case_binary_random_grads(F):
     return out
 
 
+def case_maximum_of_computed_value(F):
+    """Maximum whose first operand is computed in the trace: with a second operand that
+    needs no gradient (a scalar, a tensor) its backward may read the output for the mask,
+    which must give the reference's gradient, NaN, signed zeros and ties included; with a
+    second operand that requires grad both gradients come from the operands."""
+    out = {}
+    xv = np.array([-1.0, -0.0, 0.0, np.nan, 2.0, 1e-30, -1e-30, 0.5, 3.0, -2.0], np.float32)
+    gv = np.array([0.5, -0.25, 1.0, 2.0, -1.5, 3.0, 0.75, -1.0, 0.125, 4.0], np.float32)
+    yv = np.array([0.5, 0.0, -0.0, 1.0, 2.0, 0.0, 0.0, 0.5, np.nan, -3.0], np.float32)
+    with F.grad_tape():
+        x = T(F, xv, True)
+        (((x * 1.0).maximum(0.0)) * T(F, gv)).sum().backward()
+        out["scalar_gx"] = x.get_grad().to_numpy()
+    with F.grad_tape():
+        x = T(F, xv, True)
+        h = (x * 1.0).maximum(T(F, yv))
+        (h * T(F, gv)).sum().backward()
+        out["tensor"], out["tensor_gx"] = h.to_numpy(), x.get_grad().to_numpy()
+    with F.grad_tape():
+        x, y = T(F, xv, True), T(F, yv, True)
+        ((x * 1.0).maximum(y) * T(F, gv)).sum().backward()
+        out["both_gx"], out["both_gy"] = x.get_grad().to_numpy(), y.get_grad().to_numpy()
+    return out
+
+
 def case_reduction_random(F):
     r = _rng(13)
     x = r.standard_normal((7, 33, 9)).astype(np.float32)
@@ -305,7 +330,8 @@ def _neg_ok(F, x):
 
 CASES = [case_kat_forward, case_quirk_scalar_lhs, case_relu_special, case_reductions_kat,
          case_matmul_kat, case_backward_kat, case_unary_random, case_binary_random_grads,
-         case_reduction_random, case_traced_mean_returns_input, case_swapaxes, case_mlp_step,
+         case_maximum_of_computed_value, case_reduction_random, case_traced_mean_returns_input,
+         case_swapaxes, case_mlp_step,
          case_sub_inplace_bias_row0, case_errors, case_factory_random]
 
 
