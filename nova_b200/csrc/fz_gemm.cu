@@ -1060,14 +1060,19 @@ int gemm_impl(int64_t batch, int64_t M, int64_t N, int64_t K, const float *A, co
   int rc = get_encoder();
   if (rc) return rc;
 
-  // CTA pairs (256 x 256 tiles, cta_group::2) when there are rows for both halves
-  // and enough tiles to keep the pairs busy; single CTAs otherwise, with 16- or
-  // 64-column tiles for narrow outputs
+  // CTA pairs (256 x 256 tiles, cta_group::2) when there are rows for both halves and
+  // enough tiles to keep the pairs busy, or (with at least 1024 rows, so that the
+  // 256-row tiles waste little) a product of 8 GFLOP or more, whose K-split units keep
+  // them busy: per SM the pair kernel is the faster one (measured with planes supplied:
+  // 4096x1024x65536 2.05 against 2.12 ms, 3072x1024x4096 117 against 122 us, 2048^3
+  // 68 against 70 us; only 1024^3, 2 GFLOP, ran faster on single CTAs, 19 against 20 us).
+  // Single CTAs otherwise, with 16- or 64-column tiles for narrow outputs.
   const int64_t pair_tiles = ((M + 2 * BM - 1) / (2 * BM)) * ((N + BN - 1) / BN) * batch;
   const int mode = g_tile_mode.load(std::memory_order_relaxed);
+  const double flops = 2.0 * (double)batch * (double)M * (double)N * (double)K;
   const bool pair = mode == FZ_GEMM_TILES_PAIR ||
                     (mode == FZ_GEMM_TILES_AUTO && M >= 2 * BM && N > 64 &&
-                     pair_tiles * 2 >= fz::num_sms());
+                     (pair_tiles * 2 >= fz::num_sms() || (M >= 1024 && flops >= 8.0e9)));
   int tbn = pair || N > 64 ? BN : N > 16 ? 64 : 16;
   // narrow tiles read B K-major: a dense MN-major B ([K, N], N <= 64, a few MB) is
   // transposed into a K-major copy first
