@@ -1177,10 +1177,12 @@ int gemm_impl(int64_t batch, int64_t M, int64_t N, int64_t K, const float *A, co
   int *err = nullptr;
   if (!rc) rc = fz::device_error_word(&err);
   if (!rc) {
-    // raster bands of 16 row tiles walked column by column (narrower bands, and bands of
-    // B columns walked row by row with L2 eviction hints keeping B, were measured slower:
-    // DRAM is not what bounds these kernels)
-    const int band = 16;
+    // raster bands of 12 row tiles walked column by column. On [65536,4096]x[4096,4096]^T,
+    // bands of 16 / 12 / 8 read 14.3 / 12.6 / 12.9 GB from DRAM per launch in the same
+    // time (8.0 ms): the re-reads come mostly from CTA pairs drifting apart in K, not from
+    // the band; bands of B columns walked row by row with L2 eviction hints keeping B
+    // were measured slower (DRAM is not what bounds these kernels)
+    const int band = 12;
     const bool in_kernel = E.pg && !product;
     GemmArgs ga{partial ? partial : in_kernel ? nullptr : C, partial ? N : ldc,
                 partial ? M * N : strideC, batch * M * N, (int)M, (int)N, (int)K, (int)batch,
