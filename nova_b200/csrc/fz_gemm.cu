@@ -245,6 +245,31 @@ struct LaunchTimer {
 };
 
 std::atomic<int> g_tile_mode{FZ_GEMM_TILES_AUTO};
+
+// Counters for the producers' tile-boundary meetings (GemmArgs::tile_sync): per stream a
+// ring of kSyncSlots zeroed words, one per launch in turn; the ring is zeroed again, in
+// stream order behind every launch that used it, each time it wraps.
+constexpr int kSyncSlots = 1024;
+struct SyncRing {
+  unsigned int *words = nullptr;
+  int next = 0;
+};
+std::mutex g_sync_mu;
+std::unordered_map<cudaStream_t, SyncRing> g_sync_rings;
+
+int tile_sync_slot(cudaStream_t s, unsigned int **slot) {
+  std::lock_guard<std::mutex> lk(g_sync_mu);
+  SyncRing &r = g_sync_rings[s];
+  if (!r.words) {
+    FZ_CUDA(cudaMalloc((void **)&r.words, sizeof(unsigned int) * kSyncSlots));
+    FZ_CUDA(cudaMemsetAsync(r.words, 0, sizeof(unsigned int) * kSyncSlots, s));
+  } else if (r.next == kSyncSlots) {
+    FZ_CUDA(cudaMemsetAsync(r.words, 0, sizeof(unsigned int) * kSyncSlots, s));
+    r.next = 0;
+  }
+  *slot = r.words + r.next++;
+  return FZ_OK;
+}
 // Where missing remainder planes come from (fz_gemm_set_split). AUTO takes the separate
 // pass: deriving them in shared memory (the SPLIT kernels) measured slower on the sweep's
 // products except 1024^3 (0.87x the time; batched 64x512^3 1.3x, 2048^3 1.25x, large
@@ -1187,7 +1212,10 @@ int gemm_impl(int64_t batch, int64_t M, int64_t N, int64_t K, const float *A, co
     GemmArgs ga{partial ? partial : in_kernel ? nullptr : C, partial ? N : ldc,
                 partial ? M * N : strideC, batch * M * N, (int)M, (int)N, (int)K, (int)batch,
                 tiles_m, tiles_n, (int)num_units, tiles_m < band ? tiles_m : band,
-                real_splits, (int)kps, wide_mask, err};
+                real_splits, (int)kps, wide_mask, err, nullptr};
+    // CTA pairs' producers in lockstep for launches of four waves or more (fewer, short
+    // tiles measured slower: batched 64x512^3, 3.5 waves, 88 against 84 us)
+    if (!rc && pair && num_units >= 4 * workers) rc = tile_sync_slot(s, &ga.tile_sync);
     // persistent grid: one CTA (or CTA pair) per SM (pair of SMs)
     const unsigned grid = (unsigned)(num_units < workers ? num_units : workers);
     (pair ? g_stat_pair : g_stat_single).fetch_add(1, std::memory_order_relaxed);
